@@ -1,0 +1,59 @@
+// Python bindings of the nano_train_b200 CUDA extension (module `_C`).
+#include <torch/extension.h>
+
+#include "host_utils.h"
+
+namespace ntb {
+// gemm.cu
+void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+               bool a_mn, bool b_mn, bool accumulate, double alpha);
+// ops.cu
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
+                                    const at::Tensor& w, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& h, const at::Tensor& w,
+                                    const at::Tensor& rstd, const c10::optional<at::Tensor>& dres);
+std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& b,
+                                      double eps);
+std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                      const at::Tensor& mean, const at::Tensor& rstd);
+void rope_(at::Tensor& x, const c10::optional<at::Tensor>& positions, int64_t off, int64_t R, int64_t seq_len,
+           double theta, int64_t mode, bool inverse);
+at::Tensor swiglu_fwd(const at::Tensor& gu);
+at::Tensor swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu);
+at::Tensor gelu_fwd(const at::Tensor& x);
+at::Tensor gelu_bwd(const at::Tensor& dy, const at::Tensor& x);
+std::vector<at::Tensor> ce_stats(const at::Tensor& logits, const at::Tensor& labels, int64_t vstart,
+                                 int64_t ignore_index);
+void ce_bwd(const at::Tensor& logits, const at::Tensor& labels, const at::Tensor& lse, const at::Tensor& scale,
+            int64_t vstart, int64_t ignore_index, at::Tensor& grad);
+at::Tensor embedding_fwd(const at::Tensor& ids, const at::Tensor& W, int64_t vstart);
+void embedding_bwd_(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& dW, int64_t vstart);
+void adamw_flat_(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& g,
+                 const c10::optional<at::Tensor>& p_bf16, double lr, double b1, double b2, double eps, double wd,
+                 int64_t step, const c10::optional<at::Tensor>& grad_scale, const c10::optional<at::Tensor>& skip);
+void grad_stats_(at::Tensor& g, const c10::optional<at::Tensor>& inv_scale, at::Tensor& out);
+}  // namespace ntb
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "nano_train_b200 sm_100a kernels";
+  m.def("gemm_bf16", &ntb::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("out"),
+        py::arg("bias") = py::none(), py::arg("a_mn") = false, py::arg("b_mn") = false, py::arg("accumulate") = false,
+        py::arg("alpha") = 1.0);
+  m.def("rmsnorm_fwd", &ntb::rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &ntb::rmsnorm_bwd);
+  m.def("layernorm_fwd", &ntb::layernorm_fwd);
+  m.def("layernorm_bwd", &ntb::layernorm_bwd);
+  m.def("rope_", &ntb::rope_);
+  m.def("swiglu_fwd", &ntb::swiglu_fwd);
+  m.def("swiglu_bwd", &ntb::swiglu_bwd);
+  m.def("gelu_fwd", &ntb::gelu_fwd);
+  m.def("gelu_bwd", &ntb::gelu_bwd);
+  m.def("ce_stats", &ntb::ce_stats);
+  m.def("ce_bwd", &ntb::ce_bwd);
+  m.def("embedding_fwd", &ntb::embedding_fwd);
+  m.def("embedding_bwd_", &ntb::embedding_bwd_);
+  m.def("adamw_flat_", &ntb::adamw_flat_);
+  m.def("grad_stats_", &ntb::grad_stats_);
+  m.def("num_sms", &ntb::num_sms);
+  m.def("read_and_clear_status", &ntb::read_and_clear_status);
+}

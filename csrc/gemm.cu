@@ -1,0 +1,378 @@
+// Persistent warp-specialised bf16 GEMM for sm_100a on the 5th-gen tensor cores.
+//
+//   C[M,N] = alpha * op(A)[M,K] . op(B)[N,K]^T  (+ bias[N]) (+ C)
+//
+// op(A) is either A stored [M,K] (K-major) or A stored [K,M] (M-major); op(B)
+// is B stored [N,K] (K-major) or [K,N] (N-major). The three linear-layer
+// GEMMs map onto it without any transpose copy:
+//   forward  Y  = X . W^T   : A=X  [T,in]  K-major, B=W [out,in] K-major
+//   dgrad    dX = dY . W    : A=dY [T,out] K-major, B=W [out,in] N-major
+//   wgrad    dW = dY^T . X  : A=dY [T,out] M-major, B=X [T,in]  N-major
+//
+// Design (one CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128B-swizzled tiles into a STAGES-deep SMEM ring
+//   warp 1      MMA issuer: one elected thread issues tcgen05.mma 128xBNx16
+//               into a TMEM accumulator; owns the TMEM allocation
+//   warps 2..5  epilogue: tcgen05.ld TMEM -> registers -> fused bias /
+//               accumulate / cast -> global
+// The accumulator is double-buffered in TMEM (2 x BN fp32 columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1. Tiles are walked in
+// M-grouped order so one wave of CTAs shares A and B panels in the 126 MB L2.
+// Every wait is bounded (see common.cuh) and reports into a status word.
+//
+// Reference parity: replaces the F.linear / autograd matmuls of
+// src/layers.py:628-632, 1358-1360, 1484 (eager cuBLAS in the reference).
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace ntb {
+
+struct GemmParams {
+  int M, N, K;
+  void* C;
+  long ldc;
+  const __nv_bfloat16* bias;
+  float alpha;
+  int accumulate;  // 1: C = result + C (C read in its own dtype)
+  int c_f32;       // 1: C is fp32, else bf16
+  int* status;
+};
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 256 /*barriers*/;
+};
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
+  constexpr int GROUP = 16;
+  const int per_group = GROUP * num_n;
+  const int g = tile / per_group;
+  const int first_m = g * GROUP;
+  const int gm = min(GROUP, num_m - first_m);
+  const int r = tile - g * per_group;
+  mb = first_m + r % gm;
+  nb = r / gm;
+}
+
+template <int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                     GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
+  constexpr uint32_t IDESC = make_idesc_f16(BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 128);
+    }
+    mbar_init(drain, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled_mask = 0;
+      uint32_t last_phase[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_phase[s] = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        int mb, nb;
+        tile_coords(tile, num_m, num_n, mb, nb);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d(a_dst, &tmA, &full[stage], kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], mb * BM + j * 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], nb * BN + j * 64, kb * BK);
+          }
+          filled_mask |= 1u << stage;
+          last_phase[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // Never leave the CTA with a TMA write still landing in shared memory.
+      for (int s = 0; s < STAGES; ++s)
+        if (filled_mask & (1u << s)) mbar_wait(&full[s], last_phase[s], nullptr, 0) || true;
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // K-major: advance 16 elements (32 B) inside the 128 B swizzle row.
+            // MN-major: advance 16 K-rows (16 x 128 B) = two 8-row swizzle atoms.
+            const uint64_t adesc = A_MN ? make_smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                        : make_smem_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                        : make_smem_desc_sw128(b_base + k * 32, 16, 1024);
+            umma_f16_ss(d_tmem, adesc, bdesc, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // Make sure every MMA this thread issued has retired before TMEM is freed.
+      umma_commit(drain);
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    // Epilogue: warps 2..5 -> TMEM lane quarter (warp % 4).
+    const int q = warp & 3;
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+      int mb, nb;
+      tile_coords(tile, num_m, num_n, mb, nb);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const long m = static_cast<long>(mb) * BM + row;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 32) {
+        uint32_t r[32];
+        tmem_ld32(t_row + c, r);
+        tmem_wait_ld();
+        const int n0 = nb * BN + c;
+        if (m >= p.M || n0 >= p.N) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
+        if (p.bias) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j)
+            if (n0 + j < p.N) v[j] += __bfloat162float(p.bias[n0 + j]);
+        }
+        const bool full_chunk = vec_ok && (n0 + 32 <= p.N);
+        if (p.c_f32) {
+          float* crow = reinterpret_cast<float*>(p.C) + m * p.ldc + n0;
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 4) {
+              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+              if (p.accumulate) {
+                const float4 old = *reinterpret_cast<const float4*>(crow + j);
+                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
+              }
+              *reinterpret_cast<float4*>(crow + j) = o;
+            }
+          } else {
+            for (int j = 0; j < 32 && n0 + j < p.N; ++j) crow[j] = v[j] + (p.accumulate ? crow[j] : 0.f);
+          }
+        } else {
+          __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.C) + m * p.ldc + n0;
+          if (full_chunk) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              if (p.accumulate) {
+                const uint4 old = *reinterpret_cast<const uint4*>(crow + j);
+                v[j + 0] += bf16_lo(old.x); v[j + 1] += bf16_hi(old.x);
+                v[j + 2] += bf16_lo(old.y); v[j + 3] += bf16_hi(old.y);
+                v[j + 4] += bf16_lo(old.z); v[j + 5] += bf16_hi(old.z);
+                v[j + 6] += bf16_lo(old.w); v[j + 7] += bf16_hi(old.w);
+              }
+              uint4 o;
+              o.x = pack_bf16x2(v[j + 0], v[j + 1]);
+              o.y = pack_bf16x2(v[j + 2], v[j + 3]);
+              o.z = pack_bf16x2(v[j + 4], v[j + 5]);
+              o.w = pack_bf16x2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4*>(crow + j) = o;
+            }
+          } else {
+            for (int j = 0; j < 32 && n0 + j < p.N; ++j) {
+              float o = v[j] + (p.accumulate ? __bfloat162float(crow[j]) : 0.f);
+              crow[j] = __float2bfloat16(o);
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+template <int BN, bool A_MN, bool B_MN>
+static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN>;
+  static bool attr_set[16] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 15]) {
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    attr_set[dev & 15] = true;
+  }
+  const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN);
+  const int grid = std::min(num_tiles, num_sms(dev));
+  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  NTB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Builds the TMA descriptor of one operand. K-major operands are read as
+// [rows, K] boxes of 64 x rows_box; MN-major operands as [K, MN] boxes of
+// 64 x 64 (the swizzled K-row is the 64-element MN strip).
+static CUtensorMap operand_map(const at::Tensor& t, bool mn_major, int rows_box) {
+  const int64_t d0 = t.size(1), d1 = t.size(0);
+  const int64_t ld = t.stride(0);
+  if (mn_major) return make_tma_2d_bf16(t.data_ptr(), d0, d1, ld, 64, 64);
+  return make_tma_2d_bf16(t.data_ptr(), d0, d1, ld, 64, rows_box);
+}
+
+// out = alpha * op(a) . op(b)^T (+ bias) (+ out if accumulate).
+//   a: [M,K] (a_mn=false) or [K,M] (a_mn=true), bf16, unit inner stride
+//   b: [N,K] (b_mn=false) or [K,N] (b_mn=true), bf16, unit inner stride
+//   out: [M,N] bf16 or fp32 with unit inner stride
+void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+               bool a_mn, bool b_mn, bool accumulate, double alpha) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm_bf16: CUDA tensors required");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm_bf16: 2-D tensors");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && out.stride(1) == 1, "gemm_bf16: inner stride must be 1");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat, "gemm_bf16: bf16/fp32 out");
+  const int64_t M = a_mn ? a.size(1) : a.size(0);
+  const int64_t K = a_mn ? a.size(0) : a.size(1);
+  const int64_t N = b_mn ? b.size(1) : b.size(0);
+  const int64_t Kb = b_mn ? b.size(0) : b.size(1);
+  TORCH_CHECK(K == Kb, "gemm_bf16: K mismatch ", K, " vs ", Kb);
+  TORCH_CHECK(out.size(0) == M && out.size(1) == N, "gemm_bf16: bad out shape");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_bf16: row stride must be 16B aligned");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0,
+              "gemm_bf16: operands must be 16B aligned");
+  if (M == 0 || N == 0) return;
+  if (K == 0) {
+    if (!accumulate) out.zero_();
+    if (bias.has_value()) out.add_(bias.value());
+    return;
+  }
+  GemmParams p;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.C = out.data_ptr();
+  p.ldc = out.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias.value().data_ptr()) : nullptr;
+  if (bias.has_value()) TORCH_CHECK(bias.value().scalar_type() == at::kBFloat16 && bias.value().numel() == N, "gemm_bf16: bias");
+  p.alpha = static_cast<float>(alpha);
+  p.accumulate = accumulate ? 1 : 0;
+  p.c_f32 = out.scalar_type() == at::kFloat ? 1 : 0;
+  p.status = device_status(a.get_device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
+  // Narrow problems waste half of a 256-wide tile: use 128.
+  const bool wide = N > 128;
+  const CUtensorMap ta = operand_map(a, a_mn, 128);
+  const CUtensorMap tb = operand_map(b, b_mn, wide ? 256 : 128);
+#define NTB_GEMM_CASE(BN_, AM, BM_)                     \
+  if (a_mn == AM && b_mn == BM_) {                      \
+    launch_gemm<BN_, AM, BM_>(ta, tb, p, stream);       \
+    return;                                             \
+  }
+  if (wide) {
+    NTB_GEMM_CASE(256, false, false) NTB_GEMM_CASE(256, false, true) NTB_GEMM_CASE(256, true, false)
+    NTB_GEMM_CASE(256, true, true)
+  } else {
+    NTB_GEMM_CASE(128, false, false) NTB_GEMM_CASE(128, false, true) NTB_GEMM_CASE(128, true, false)
+    NTB_GEMM_CASE(128, true, true)
+  }
+#undef NTB_GEMM_CASE
+}
+
+}  // namespace ntb

@@ -1,0 +1,91 @@
+#include "host_utils.h"
+
+#include <mutex>
+
+namespace ntb {
+
+namespace {
+constexpr int kMaxDevices = 64;
+int g_sms[kMaxDevices] = {0};
+int* g_status[kMaxDevices] = {nullptr};
+std::mutex g_mu;
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    NTB_CUDA_CHECK(cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && ptr, "cuTensorMapEncodeTiled not available");
+    fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+}  // namespace
+
+int num_sms(int device) {
+  if (device < 0 || device >= kMaxDevices) device = 0;
+  if (!g_sms[device]) {
+    int v = 0;
+    NTB_CUDA_CHECK(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device));
+    g_sms[device] = v;
+  }
+  return g_sms[device];
+}
+
+int* device_status(int device) {
+  TORCH_CHECK(device >= 0 && device < kMaxDevices, "bad device");
+  if (!g_status[device]) {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_status[device]) {
+      int prev;
+      NTB_CUDA_CHECK(cudaGetDevice(&prev));
+      NTB_CUDA_CHECK(cudaSetDevice(device));
+      int* p = nullptr;
+      NTB_CUDA_CHECK(cudaMalloc(&p, sizeof(int) * 4));
+      NTB_CUDA_CHECK(cudaMemset(p, 0, sizeof(int) * 4));
+      NTB_CUDA_CHECK(cudaDeviceSynchronize());
+      NTB_CUDA_CHECK(cudaSetDevice(prev));
+      g_status[device] = p;
+    }
+  }
+  return g_status[device];
+}
+
+int read_and_clear_status(int device) {
+  int* p = device_status(device);
+  int prev;
+  NTB_CUDA_CHECK(cudaGetDevice(&prev));
+  NTB_CUDA_CHECK(cudaSetDevice(device));
+  NTB_CUDA_CHECK(cudaDeviceSynchronize());
+  int v = 0;
+  NTB_CUDA_CHECK(cudaMemcpy(&v, p, sizeof(int), cudaMemcpyDeviceToHost));
+  if (v) NTB_CUDA_CHECK(cudaMemset(p, 0, sizeof(int)));
+  NTB_CUDA_CHECK(cudaSetDevice(prev));
+  return v;
+}
+
+CUtensorMap make_tma_2d(void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1, int64_t ld,
+                        int box0, int box1, CUtensorMapSwizzle swz) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1)};
+  cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1)};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode_fn()(&m, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", static_cast<int>(r), ") dims=", d0, "x", d1,
+              " ld=", ld, " box=", box0, "x", box1);
+  return m;
+}
+
+CUtensorMap make_tma_2d_bf16(void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1) {
+  return make_tma_2d(base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d0, d1, ld, box0, box1,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+}  // namespace ntb

@@ -1,0 +1,38 @@
+// Host-side helpers shared by the extension's translation units.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <cstdint>
+
+#define NTB_CUDA_CHECK(expr)                                                                 \
+  do {                                                                                       \
+    cudaError_t _e = (expr);                                                                 \
+    TORCH_CHECK(_e == cudaSuccess, "CUDA error ", cudaGetErrorString(_e), " at ", __FILE__, \
+                ":", __LINE__, " in ", #expr);                                               \
+  } while (0)
+
+namespace ntb {
+
+// Number of SMs of a device (cached).
+int num_sms(int device);
+
+// Per-device status word that kernels raise on a bounded-wait timeout or a
+// rejected shape (see StatusCode in common.cuh). Allocated once per device.
+int* device_status(int device);
+
+// Reads and clears the status word of a device (synchronises the device).
+int read_and_clear_status(int device);
+
+// 2-D TMA descriptor for a bf16 matrix with inner extent d0 (contiguous),
+// outer extent d1, row pitch ld (elements), box box0 x box1, 128-byte swizzle.
+CUtensorMap make_tma_2d_bf16(void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1);
+
+// Same for an arbitrary element size in bytes with a chosen swizzle
+// (0 none, 3 = 128B).
+CUtensorMap make_tma_2d(void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1, int64_t ld,
+                        int box0, int box1, CUtensorMapSwizzle swz);
+
+}  // namespace ntb

@@ -1,0 +1,964 @@
+// Memory-bound sm_100a kernels: norms, RoPE, activations, cross-entropy,
+// embedding, fused AdamW and gradient unscale/finite/norm.
+//
+// All are row- or element-parallel with 16-byte vector access where the
+// shape allows; fp32 math internally, bf16 or fp32 storage.
+//
+// Reference parity (behaviour, not code):
+//   RMSNorm          src/models/deepseek.py:386-438
+//   LayerNorm        src/layers.py:639-781
+//   RoPE (both)      src/models/deepseek.py:517-543 (interleaved rotate, half-split cache)
+//   SwiGLU / GELU    src/models/moe.py:146-193, src/layers.py:1017-1095
+//   cross-entropy    src/losses.py:95-133, examples/train_4d.py:725-730
+//   embedding        src/layers.py:788-900
+//   AdamW            src/runtime/optimizer_runtime.py:68-116, src/distributed/zero.py:451-474
+//   unscale/finite   src/runtime/mixed_precision.py:813-854
+#include <ATen/cuda/CUDAContext.h>
+#include <torch/extension.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace ntb {
+
+using bf16 = __nv_bfloat16;
+
+// Typed raw pointer of a tensor (bf16 tensors are viewed as __nv_bfloat16).
+template <typename T>
+static inline T* P(const at::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+template <typename T>
+__device__ __forceinline__ float to_f(T v);
+template <>
+__device__ __forceinline__ float to_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ float to_f<bf16>(bf16 v) { return __bfloat162float(v); }
+
+template <typename T>
+__device__ __forceinline__ T from_f(float v);
+template <>
+__device__ __forceinline__ float from_f<float>(float v) { return v; }
+template <>
+__device__ __forceinline__ bf16 from_f<bf16>(float v) { return __float2bfloat16(v); }
+
+// Vector of 8 elements <-> 8 floats.
+template <typename T>
+__device__ __forceinline__ void ld8(const T* p, float (&v)[8]);
+template <>
+__device__ __forceinline__ void ld8<bf16>(const bf16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+  v[4] = bf16_lo(u.z); v[5] = bf16_hi(u.z); v[6] = bf16_lo(u.w); v[7] = bf16_hi(u.w);
+}
+template <>
+__device__ __forceinline__ void ld8<float>(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p);
+  const float4 b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+template <typename T>
+__device__ __forceinline__ void st8(T* p, const float (&v)[8]);
+template <>
+__device__ __forceinline__ void st8<bf16>(bf16* p, const float (&v)[8]) {
+  uint4 u;
+  u.x = pack_bf16x2(v[0], v[1]); u.y = pack_bf16x2(v[2], v[3]);
+  u.z = pack_bf16x2(v[4], v[5]); u.w = pack_bf16x2(v[6], v[7]);
+  *reinterpret_cast<uint4*>(p) = u;
+}
+template <>
+__device__ __forceinline__ void st8<float>(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// Block-wide sum over up to 1024 threads (result broadcast to every thread).
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.f;
+  if (w == 0) t = warp_sum(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  const int nw = (blockDim.x + 31) >> 5;
+  float t = (threadIdx.x < nw) ? red[threadIdx.x] : -INFINITY;
+  if (w == 0) t = warp_max(t);
+  if (threadIdx.x == 0) red[0] = t;
+  __syncthreads();
+  return red[0];
+}
+
+static int row_threads(int64_t H) {
+  int t = 32;
+  while (t < 1024 && t * 8 < H) t *= 2;
+  return t;
+}
+
+#define NTB_DISPATCH_FLOAT(T_, NAME, ...)                                   \
+  [&] {                                                                     \
+    if ((T_) == at::kBFloat16) {                                            \
+      using scalar_t = bf16;                                                \
+      return __VA_ARGS__();                                                 \
+    } else if ((T_) == at::kFloat) {                                        \
+      using scalar_t = float;                                               \
+      return __VA_ARGS__();                                                 \
+    } else {                                                                \
+      TORCH_CHECK(false, NAME, ": unsupported dtype ", (T_));              \
+    }                                                                       \
+  }()
+
+// =========================================================== RMSNorm
+// h = x (+ residual); y = h * rsqrt(mean(h^2) + eps) * w.
+template <typename T, bool VEC>
+__global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ res, const T* __restrict__ w,
+                                   T* __restrict__ y, T* __restrict__ h_out, float* __restrict__ rstd_out, int H,
+                                   float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * H;
+  const T* rr = res ? res + row * H : nullptr;
+  float ss = 0.f;
+  if (VEC) {
+    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+      float v[8];
+      ld8(xr + i, v);
+      if (rr) {
+        float r[8];
+        ld8(rr + i, r);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[j] += r[j];
+        st8(h_out + row * H + i, v);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[j] * v[j];
+    }
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      float v = to_f(xr[i]);
+      if (rr) {
+        v += to_f(rr[i]);
+        h_out[row * H + i] = from_f<T>(v);
+      }
+      ss += v * v;
+    }
+  }
+  ss = block_sum(ss, red);
+  const float rstd = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0) rstd_out[row] = rstd;
+  const T* hr = rr ? h_out + row * H : xr;
+  if (VEC) {
+    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+      float v[8], g[8];
+      ld8(hr + i, v);
+      ld8(w + i, g);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = v[j] * rstd * g[j];
+      st8(y + row * H + i, v);
+    }
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) y[row * H + i] = from_f<T>(to_f(hr[i]) * rstd * to_f(w[i]));
+  }
+}
+
+// dx = rstd * (g - n * mean(g * n)), g = dy * w, n = h * rstd; dw partials per block.
+template <typename T, bool VEC>
+__global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ h, const T* __restrict__ w,
+                                   const float* __restrict__ rstd, const T* __restrict__ dres, T* __restrict__ dx,
+                                   float* __restrict__ dw_part, int64_t rows, int H, int rows_per_block) {
+  __shared__ float red[32];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  float* dwp = dw_part + static_cast<int64_t>(blockIdx.x) * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) dwp[i] = 0.f;
+  for (int64_t row = r0; row < r0 + rows_per_block && row < rows; ++row) {
+    const float rs = rstd[row];
+    const T* dyr = dy + row * H;
+    const T* hr = h + row * H;
+    float dot = 0.f;
+    if (VEC) {
+      for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+        float a[8], b[8], c[8];
+        ld8(dyr + i, a);
+        ld8(hr + i, b);
+        ld8(w + i, c);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dot += a[j] * c[j] * b[j];
+      }
+    } else {
+      for (int i = threadIdx.x; i < H; i += blockDim.x) dot += to_f(dyr[i]) * to_f(w[i]) * to_f(hr[i]);
+    }
+    dot = block_sum(dot, red);
+    const float mean_gn = dot * rs / H;  // mean(g * n)
+    if (VEC) {
+      for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+        float a[8], b[8], c[8], o[8];
+        ld8(dyr + i, a);
+        ld8(hr + i, b);
+        ld8(w + i, c);
+        float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (dres) ld8(dres + row * H + i, d);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          const float n = b[j] * rs;
+          o[j] = rs * (a[j] * c[j] - n * mean_gn) + d[j];
+          dwp[i + j] += a[j] * n;
+        }
+        st8(dx + row * H + i, o);
+      }
+    } else {
+      for (int i = threadIdx.x; i < H; i += blockDim.x) {
+        const float a = to_f(dyr[i]), n = to_f(hr[i]) * rs;
+        float o = rs * (a * to_f(w[i]) - n * mean_gn);
+        if (dres) o += to_f(dres[row * H + i]);
+        dx[row * H + i] = from_f<T>(o);
+        dwp[i] += a * n;
+      }
+    }
+  }
+}
+
+__global__ void colsum_kernel(const float* __restrict__ part, int nparts, int H, float* __restrict__ out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= H) return;
+  float s = 0.f;
+  for (int p = 0; p < nparts; ++p) s += part[static_cast<int64_t>(p) * H + i];
+  out[i] = s;
+}
+
+static bool vec8_ok(const at::Tensor& t, int64_t H) {
+  return H % 8 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0;
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
+                                    const at::Tensor& w, double eps) {
+  TORCH_CHECK(x.is_cuda() && x.is_contiguous() && w.is_contiguous(), "rmsnorm_fwd: contiguous CUDA tensors");
+  const int64_t H = x.size(-1);
+  const int64_t rows = x.numel() / H;
+  TORCH_CHECK(w.numel() == H && w.scalar_type() == x.scalar_type(), "rmsnorm_fwd: weight");
+  auto y = at::empty_like(x);
+  at::Tensor h;
+  const bool has_res = residual.has_value();
+  if (has_res) {
+    TORCH_CHECK(residual->is_contiguous() && residual->sizes() == x.sizes(), "rmsnorm_fwd: residual");
+    h = at::empty_like(x);
+  }
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, h.defined() ? h : x, rstd};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int threads = row_threads(H);
+  bool vec = vec8_ok(x, H) && vec8_ok(w, H) && vec8_ok(y, H);
+  if (has_res) vec = vec && vec8_ok(*residual, H) && vec8_ok(h, H);
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "rmsnorm_fwd", [&] {
+    const scalar_t* rp = has_res ? P<scalar_t>(*residual) : nullptr;
+    scalar_t* hp = has_res ? P<scalar_t>(h) : nullptr;
+    if (vec)
+      rmsnorm_fwd_kernel<scalar_t, true><<<rows, threads, 0, stream>>>(P<scalar_t>(x), rp, P<scalar_t>(w),
+                                                                       P<scalar_t>(y), hp, rstd.data_ptr<float>(), H, eps);
+    else
+      rmsnorm_fwd_kernel<scalar_t, false><<<rows, threads, 0, stream>>>(P<scalar_t>(x), rp, P<scalar_t>(w),
+                                                                        P<scalar_t>(y), hp, rstd.data_ptr<float>(), H, eps);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return {y, has_res ? h : x, rstd};
+}
+
+// Returns (dx, dw). dres (optional) is added into dx (gradient flowing along the residual stream).
+std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& h, const at::Tensor& w,
+                                    const at::Tensor& rstd, const c10::optional<at::Tensor>& dres) {
+  TORCH_CHECK(dy.is_contiguous() && h.is_contiguous(), "rmsnorm_bwd: contiguous");
+  const int64_t H = h.size(-1);
+  const int64_t rows = h.numel() / H;
+  auto dx = at::empty_like(h);
+  auto dw = at::zeros({H}, h.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dw.to(w.scalar_type())};
+  const int nsm = num_sms(h.get_device());
+  const int blocks = static_cast<int>(std::min<int64_t>(rows, nsm * 4));
+  const int rpb = static_cast<int>((rows + blocks - 1) / blocks);
+  auto part = at::empty({blocks, H}, h.options().dtype(at::kFloat));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int threads = row_threads(H);
+  bool vec = vec8_ok(dy, H) && vec8_ok(h, H) && vec8_ok(w, H) && vec8_ok(dx, H);
+  if (dres.has_value()) vec = vec && vec8_ok(*dres, H);
+  NTB_DISPATCH_FLOAT(h.scalar_type(), "rmsnorm_bwd", [&] {
+    const scalar_t* dr = dres.has_value() ? P<scalar_t>(*dres) : nullptr;
+    if (vec)
+      rmsnorm_bwd_kernel<scalar_t, true><<<blocks, threads, 0, stream>>>(
+          P<scalar_t>(dy), P<scalar_t>(h), P<scalar_t>(w), rstd.data_ptr<float>(), dr,
+          P<scalar_t>(dx), part.data_ptr<float>(), rows, H, rpb);
+    else
+      rmsnorm_bwd_kernel<scalar_t, false><<<blocks, threads, 0, stream>>>(
+          P<scalar_t>(dy), P<scalar_t>(h), P<scalar_t>(w), rstd.data_ptr<float>(), dr,
+          P<scalar_t>(dx), part.data_ptr<float>(), rows, H, rpb);
+  });
+  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(part.data_ptr<float>(), blocks, H, dw.data_ptr<float>());
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return {dx, dw.to(w.scalar_type())};
+}
+
+// =========================================================== LayerNorm
+template <typename T>
+__global__ void layernorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w, const T* __restrict__ b,
+                                     T* __restrict__ y, float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                     int H, float eps) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* xr = x + row * H;
+  float s = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) s += to_f(xr[i]);
+  const float mean = block_sum(s, red) / H;
+  float v = 0.f;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    const float d = to_f(xr[i]) - mean;
+    v += d * d;
+  }
+  const float var = block_sum(v, red) / H;
+  const float rstd = rsqrtf(var + eps);
+  if (threadIdx.x == 0) {
+    mean_out[row] = mean;
+    rstd_out[row] = rstd;
+  }
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    float o = (to_f(xr[i]) - mean) * rstd * to_f(w[i]);
+    if (b) o += to_f(b[i]);
+    y[row * H + i] = from_f<T>(o);
+  }
+}
+
+template <typename T>
+__global__ void layernorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,
+                                     const float* __restrict__ mean, const float* __restrict__ rstd,
+                                     T* __restrict__ dx, float* __restrict__ dw_part, float* __restrict__ db_part,
+                                     int64_t rows, int H, int rows_per_block) {
+  __shared__ float red[32];
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  float* dwp = dw_part + static_cast<int64_t>(blockIdx.x) * H;
+  float* dbp = db_part + static_cast<int64_t>(blockIdx.x) * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) {
+    dwp[i] = 0.f;
+    dbp[i] = 0.f;
+  }
+  for (int64_t row = r0; row < r0 + rows_per_block && row < rows; ++row) {
+    const float mu = mean[row], rs = rstd[row];
+    float a = 0.f, bsum = 0.f;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float g = to_f(dy[row * H + i]) * to_f(w[i]);
+      const float xh = (to_f(x[row * H + i]) - mu) * rs;
+      a += g;
+      bsum += g * xh;
+    }
+    a = block_sum(a, red) / H;
+    bsum = block_sum(bsum, red) / H;
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float d = to_f(dy[row * H + i]);
+      const float g = d * to_f(w[i]);
+      const float xh = (to_f(x[row * H + i]) - mu) * rs;
+      dx[row * H + i] = from_f<T>(rs * (g - a - xh * bsum));
+      dwp[i] += d * xh;
+      dbp[i] += d;
+    }
+  }
+}
+
+std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& b,
+                                      double eps) {
+  TORCH_CHECK(x.is_contiguous(), "layernorm_fwd: contiguous");
+  const int64_t H = x.size(-1), rows = x.numel() / H;
+  auto y = at::empty_like(x);
+  auto mean = at::empty({rows}, x.options().dtype(at::kFloat));
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, mean, rstd};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "layernorm_fwd", [&] {
+    layernorm_fwd_kernel<scalar_t><<<rows, row_threads(H), 0, stream>>>(
+        P<scalar_t>(x), P<scalar_t>(w), b.has_value() ? P<scalar_t>(*b) : nullptr,
+        P<scalar_t>(y), mean.data_ptr<float>(), rstd.data_ptr<float>(), H, eps);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return {y, mean, rstd};
+}
+
+std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
+                                      const at::Tensor& mean, const at::Tensor& rstd) {
+  const int64_t H = x.size(-1), rows = x.numel() / H;
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({H}, x.options().dtype(at::kFloat));
+  auto db = at::zeros({H}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dw.to(w.scalar_type()), db.to(w.scalar_type())};
+  const int blocks = static_cast<int>(std::min<int64_t>(rows, num_sms(x.get_device()) * 4));
+  const int rpb = static_cast<int>((rows + blocks - 1) / blocks);
+  auto pw = at::empty({blocks, H}, x.options().dtype(at::kFloat));
+  auto pb = at::empty({blocks, H}, x.options().dtype(at::kFloat));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  auto dyc = dy.contiguous();
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "layernorm_bwd", [&] {
+    layernorm_bwd_kernel<scalar_t><<<blocks, row_threads(H), 0, stream>>>(
+        P<scalar_t>(dyc), P<scalar_t>(x), P<scalar_t>(w), mean.data_ptr<float>(),
+        rstd.data_ptr<float>(), P<scalar_t>(dx), pw.data_ptr<float>(), pb.data_ptr<float>(), rows, H, rpb);
+  });
+  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(pw.data_ptr<float>(), blocks, H, dw.data_ptr<float>());
+  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(pb.data_ptr<float>(), blocks, H, db.data_ptr<float>());
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return {dx, dw.to(w.scalar_type()), db.to(w.scalar_type())};
+}
+
+// =========================================================== RoPE
+// x: [T, heads, D] view with row stride (elements) `sx` between tokens and
+// `sh` between heads; rotary part occupies columns [off, off + R).
+// mode 0 (half-split, Llama/NeoX): pairs (i, i + R/2), angle pos * f[i].
+// mode 1 (interleaved pairs with half-split cache): element j of the pair
+//   (2i, 2i+1) uses angle pos * f[j mod R/2]; out[2i] = x[2i] c[2i] - x[2i+1] s[2i],
+//   out[2i+1] = x[2i+1] c[2i+1] + x[2i] s[2i+1] (matches the reference's
+//   rotate_half over interleaved elements combined with cat(freqs, freqs)).
+// inverse=true applies the transpose (backward).
+template <typename T>
+__global__ void rope_kernel(T* __restrict__ x, const int64_t* __restrict__ pos, int T_, int heads, int64_t sx,
+                            int64_t sh, int off, int R, int seq_len, float theta, int mode, bool inverse) {
+  const int half = R / 2;
+  const int64_t total = static_cast<int64_t>(T_) * heads * half;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int i = idx % half;
+    const int64_t th = idx / half;
+    const int hd = th % heads;
+    const int t = th / heads;
+    const float p = pos ? static_cast<float>(pos[t]) : static_cast<float>(t % seq_len);
+    T* base = x + t * sx + hd * sh + off;
+    if (mode == 0) {
+      const float f = powf(theta, -2.f * i / R);
+      float s, c;
+      sincosf(p * f, &s, &c);
+      if (inverse) s = -s;
+      const float a = to_f(base[i]), b = to_f(base[i + half]);
+      base[i] = from_f<T>(a * c - b * s);
+      base[i + half] = from_f<T>(b * c + a * s);
+    } else {
+      const int j0 = 2 * i, j1 = 2 * i + 1;
+      const float f0 = powf(theta, -2.f * (j0 % half) / R);
+      const float f1 = powf(theta, -2.f * (j1 % half) / R);
+      float s0, c0, s1, c1;
+      sincosf(p * f0, &s0, &c0);
+      sincosf(p * f1, &s1, &c1);
+      const float a = to_f(base[j0]), b = to_f(base[j1]);
+      if (!inverse) {
+        base[j0] = from_f<T>(a * c0 - b * s0);
+        base[j1] = from_f<T>(b * c1 + a * s1);
+      } else {
+        base[j0] = from_f<T>(a * c0 + b * s1);
+        base[j1] = from_f<T>(b * c1 - a * s0);
+      }
+    }
+  }
+}
+
+// In-place RoPE on x[..., heads, D] (last dim contiguous). positions: optional int64 [T].
+void rope_(at::Tensor& x, const c10::optional<at::Tensor>& positions, int64_t off, int64_t R, int64_t seq_len,
+           double theta, int64_t mode, bool inverse) {
+  TORCH_CHECK(x.stride(-1) == 1, "rope_: last dim must be contiguous");
+  TORCH_CHECK(R % 2 == 0 && off + R <= x.size(-1), "rope_: bad rotary range");
+  const int heads = static_cast<int>(x.size(-2));
+  const int64_t sh = x.stride(-2);
+  const int64_t sx = x.stride(-3);
+  const int64_t T_ = x.numel() / (x.size(-1) * heads);
+  TORCH_CHECK(x.dim() == 3 || x.is_contiguous() || x.stride(0) == x.size(1) * sx, "rope_: unsupported layout");
+  if (T_ == 0) return;
+  const int64_t total = T_ * heads * (R / 2);
+  const int threads = 256;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, 148 * 16));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "rope_", [&] {
+    rope_kernel<scalar_t><<<blocks, threads, 0, stream>>>(
+        P<scalar_t>(x), positions.has_value() ? positions->data_ptr<int64_t>() : nullptr,
+        static_cast<int>(T_), heads, sx, sh, static_cast<int>(off), static_cast<int>(R), static_cast<int>(seq_len),
+        static_cast<float>(theta), static_cast<int>(mode), inverse);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+}
+
+// =========================================================== activations
+// SwiGLU over a packed [rows, 2I] tensor: gate = cols [0, I), up = cols [I, 2I).
+template <typename T>
+__global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows, int I) {
+  const int64_t total = rows * I;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / I;
+    const int c = idx % I;
+    const float g = to_f(gu[r * 2 * I + c]), u = to_f(gu[r * 2 * I + I + c]);
+    const float sg = g / (1.f + __expf(-g));
+    out[idx] = from_f<T>(sg * u);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_fwd_vec_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows, int I) {
+  const int64_t total = rows * I / 8;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = idx * 8;
+    const int64_t r = e / I;
+    const int c = e % I;
+    float g[8], u[8], o[8];
+    ld8(gu + r * 2 * I + c, g);
+    ld8(gu + r * 2 * I + I + c, u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
+    st8(out + e, o);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_vec_kernel(const T* __restrict__ dout, const T* __restrict__ gu, T* __restrict__ dgu,
+                                      int64_t rows, int I) {
+  const int64_t total = rows * I / 8;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = idx * 8;
+    const int64_t r = e / I;
+    const int c = e % I;
+    float g[8], u[8], d[8], dg[8], du[8];
+    ld8(gu + r * 2 * I + c, g);
+    ld8(gu + r * 2 * I + I + c, u);
+    ld8(dout + e, d);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float s = 1.f / (1.f + __expf(-g[j]));
+      const float sg = g[j] * s;
+      du[j] = d[j] * sg;
+      dg[j] = d[j] * u[j] * (s + sg * (1.f - s));
+    }
+    st8(dgu + r * 2 * I + c, dg);
+    st8(dgu + r * 2 * I + I + c, du);
+  }
+}
+
+template <typename T>
+__global__ void swiglu_bwd_kernel(const T* __restrict__ dout, const T* __restrict__ gu, T* __restrict__ dgu,
+                                  int64_t rows, int I) {
+  const int64_t total = rows * I;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t r = idx / I;
+    const int c = idx % I;
+    const float g = to_f(gu[r * 2 * I + c]), u = to_f(gu[r * 2 * I + I + c]);
+    const float d = to_f(dout[idx]);
+    const float s = 1.f / (1.f + __expf(-g));
+    const float sg = g * s;
+    dgu[r * 2 * I + I + c] = from_f<T>(d * sg);
+    dgu[r * 2 * I + c] = from_f<T>(d * u * (s + sg * (1.f - s)));
+  }
+}
+
+static int ew_blocks(int64_t n) { return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, 148 * 32))); }
+
+at::Tensor swiglu_fwd(const at::Tensor& gu) {
+  TORCH_CHECK(gu.is_contiguous() && gu.size(-1) % 2 == 0, "swiglu_fwd: packed [.., 2I] contiguous");
+  const int I = static_cast<int>(gu.size(-1) / 2);
+  const int64_t rows = gu.numel() / (2 * I);
+  auto sizes = gu.sizes().vec();
+  sizes.back() = I;
+  auto out = at::empty(sizes, gu.options());
+  if (rows == 0) return out;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const bool vec = I % 8 == 0;
+  NTB_DISPATCH_FLOAT(gu.scalar_type(), "swiglu_fwd", [&] {
+    if (vec)
+      swiglu_fwd_vec_kernel<scalar_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(P<scalar_t>(gu), P<scalar_t>(out), rows, I);
+    else
+      swiglu_fwd_kernel<scalar_t><<<ew_blocks(rows * I), 256, 0, stream>>>(P<scalar_t>(gu), P<scalar_t>(out), rows, I);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return out;
+}
+
+at::Tensor swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu) {
+  const int I = static_cast<int>(gu.size(-1) / 2);
+  const int64_t rows = gu.numel() / (2 * I);
+  auto dgu = at::empty_like(gu);
+  if (rows == 0) return dgu;
+  auto d = dout.contiguous();
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const bool vec = I % 8 == 0;
+  NTB_DISPATCH_FLOAT(gu.scalar_type(), "swiglu_bwd", [&] {
+    if (vec)
+      swiglu_bwd_vec_kernel<scalar_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(gu),
+                                                                                P<scalar_t>(dgu), rows, I);
+    else
+      swiglu_bwd_kernel<scalar_t><<<ew_blocks(rows * I), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(gu),
+                                                                          P<scalar_t>(dgu), rows, I);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return dgu;
+}
+
+// Exact GELU x * Phi(x) using CUDA's erff.
+template <typename T>
+__global__ void gelu_fwd_kernel(const T* __restrict__ x, T* __restrict__ y, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float v = to_f(x[i]);
+    y[i] = from_f<T>(0.5f * v * (1.f + erff(v * 0.70710678118654752f)));
+  }
+}
+template <typename T>
+__global__ void gelu_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, T* __restrict__ dx, int64_t n) {
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float v = to_f(x[i]);
+    const float cdf = 0.5f * (1.f + erff(v * 0.70710678118654752f));
+    const float pdf = 0.3989422804014327f * __expf(-0.5f * v * v);
+    dx[i] = from_f<T>(to_f(dy[i]) * (cdf + v * pdf));
+  }
+}
+
+at::Tensor gelu_fwd(const at::Tensor& x) {
+  auto xc = x.contiguous();
+  auto y = at::empty_like(xc);
+  const int64_t n = xc.numel();
+  if (n == 0) return y;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "gelu_fwd", [&] {
+    gelu_fwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream>>>(P<scalar_t>(xc), P<scalar_t>(y), n);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return y;
+}
+
+at::Tensor gelu_bwd(const at::Tensor& dy, const at::Tensor& x) {
+  auto xc = x.contiguous();
+  auto d = dy.contiguous();
+  auto dx = at::empty_like(xc);
+  const int64_t n = xc.numel();
+  if (n == 0) return dx;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "gelu_bwd", [&] {
+    gelu_bwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(xc),
+                                                              P<scalar_t>(dx), n);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return dx;
+}
+
+// =========================================================== cross-entropy
+// Per-row statistics of a (possibly vocab-sharded) logits block [rows, V]:
+//   row_max, row_sumexp (relative to row_max), target logit (0 if the label
+//   is outside [vstart, vstart + V) or equals ignore_index).
+template <typename T>
+__global__ void ce_stats_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ labels,
+                                int64_t V, int64_t vstart, int64_t ignore_index, float* __restrict__ out_max,
+                                float* __restrict__ out_sum, float* __restrict__ out_tgt) {
+  __shared__ float red[32];
+  const int64_t row = blockIdx.x;
+  const T* lr = logits + row * ld;
+  float m = -INFINITY, s = 0.f;
+  const bool vec = (V % 8 == 0) && (ld % 8 == 0) && ((reinterpret_cast<uintptr_t>(logits) & 15) == 0);
+  if (vec) {
+    for (int64_t i = threadIdx.x * 8; i < V; i += blockDim.x * 8) {
+      float v[8];
+      ld8(lr + i, v);
+      float lm = v[0];
+#pragma unroll
+      for (int j = 1; j < 8; ++j) lm = fmaxf(lm, v[j]);
+      const float nm = fmaxf(m, lm);
+      float acc = s * __expf(m - nm);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc += __expf(v[j] - nm);
+      s = acc;
+      m = nm;
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+      const float v = to_f(lr[i]);
+      const float nm = fmaxf(m, v);
+      s = s * __expf(m - nm) + __expf(v - nm);
+      m = nm;
+    }
+  }
+  const float gm = block_max(m, red);
+  float sc = (m == -INFINITY) ? 0.f : s * __expf(m - gm);
+  sc = block_sum(sc, red);
+  if (threadIdx.x == 0) {
+    out_max[row] = gm;
+    out_sum[row] = sc;
+    const int64_t lab = labels[row];
+    float t = 0.f;
+    if (lab != ignore_index && lab >= vstart && lab < vstart + V) t = to_f(lr[lab - vstart]);
+    out_tgt[row] = t;
+  }
+}
+
+// grad[row, j] = (exp(x - lse[row]) - [j + vstart == label]) * scale[row or 0], 0 for ignored rows.
+template <typename T, typename G>
+__global__ void ce_bwd_kernel(const T* __restrict__ logits, int64_t ld, const int64_t* __restrict__ labels,
+                              const float* __restrict__ lse, const float* __restrict__ scale, int scale_per_row,
+                              int64_t V, int64_t vstart, int64_t ignore_index, G* __restrict__ grad, int64_t ldg) {
+  const int64_t row = blockIdx.x;
+  const int64_t lab = labels[row];
+  const T* lr = logits + row * ld;
+  G* gr = grad + row * ldg;
+  const float sc = scale[scale_per_row ? row : 0];
+  const float l = lse[row];
+  const bool ign = (lab == ignore_index);
+  const bool vec = (V % 8 == 0) && (ld % 8 == 0) && (ldg % 8 == 0) &&
+                   ((reinterpret_cast<uintptr_t>(logits) & 15) == 0) && ((reinterpret_cast<uintptr_t>(grad) & 15) == 0);
+  if (vec) {
+    for (int64_t i = threadIdx.x * 8; i < V; i += blockDim.x * 8) {
+      float v[8];
+      ld8(lr + i, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        float g = ign ? 0.f : __expf(v[j] - l);
+        if (!ign && i + j + vstart == lab) g -= 1.f;
+        v[j] = g * sc;
+      }
+      st8(gr + i, v);
+    }
+  } else {
+    for (int64_t i = threadIdx.x; i < V; i += blockDim.x) {
+      float g = ign ? 0.f : __expf(to_f(lr[i]) - l);
+      if (!ign && i + vstart == lab) g -= 1.f;
+      gr[i] = from_f<G>(g * sc);
+    }
+  }
+}
+
+std::vector<at::Tensor> ce_stats(const at::Tensor& logits, const at::Tensor& labels, int64_t vstart,
+                                 int64_t ignore_index) {
+  TORCH_CHECK(logits.dim() == 2 && logits.stride(1) == 1, "ce_stats: 2-D logits with unit inner stride");
+  TORCH_CHECK(labels.scalar_type() == at::kLong && labels.is_contiguous(), "ce_stats: int64 labels");
+  const int64_t rows = logits.size(0), V = logits.size(1);
+  auto opts = logits.options().dtype(at::kFloat);
+  auto mx = at::empty({rows}, opts), sm = at::empty({rows}, opts), tg = at::empty({rows}, opts);
+  if (rows == 0) return {mx, sm, tg};
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(logits.scalar_type(), "ce_stats", [&] {
+    ce_stats_kernel<scalar_t><<<rows, 1024, 0, stream>>>(P<scalar_t>(logits), logits.stride(0),
+                                                         labels.data_ptr<int64_t>(), V, vstart, ignore_index,
+                                                         mx.data_ptr<float>(), sm.data_ptr<float>(), tg.data_ptr<float>());
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return {mx, sm, tg};
+}
+
+// Writes the CE gradient into `grad` (may alias `logits`).
+void ce_bwd(const at::Tensor& logits, const at::Tensor& labels, const at::Tensor& lse, const at::Tensor& scale,
+            int64_t vstart, int64_t ignore_index, at::Tensor& grad) {
+  const int64_t rows = logits.size(0), V = logits.size(1);
+  if (rows == 0) return;
+  TORCH_CHECK(scale.scalar_type() == at::kFloat && (scale.numel() == 1 || scale.numel() == rows), "ce_bwd: scale");
+  TORCH_CHECK(grad.scalar_type() == logits.scalar_type() && grad.stride(1) == 1, "ce_bwd: grad");
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(logits.scalar_type(), "ce_bwd", [&] {
+    ce_bwd_kernel<scalar_t, scalar_t><<<rows, 1024, 0, stream>>>(
+        P<scalar_t>(logits), logits.stride(0), labels.data_ptr<int64_t>(), lse.data_ptr<float>(),
+        scale.data_ptr<float>(), scale.numel() == rows ? 1 : 0, V, vstart, ignore_index, P<scalar_t>(grad),
+        grad.stride(0));
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+}
+
+// =========================================================== embedding
+template <typename T>
+__global__ void embedding_fwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ W, T* __restrict__ out,
+                                     int64_t n, int H, int64_t vstart, int64_t vcount, int* status) {
+  const int64_t t = blockIdx.x;
+  const int64_t id = ids[t] - vstart;
+  T* o = out + t * H;
+  if (id < 0 || id >= vcount) {
+    // Outside this shard (vocab-parallel) -> zeros.
+    for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = from_f<T>(0.f);
+    return;
+  }
+  const T* w = W + id * H;
+  if ((H % 8 == 0) && sizeof(T) == 2) {
+    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8)
+      *reinterpret_cast<uint4*>(o + i) = *reinterpret_cast<const uint4*>(w + i);
+  } else {
+    for (int i = threadIdx.x; i < H; i += blockDim.x) o[i] = w[i];
+  }
+}
+
+template <typename T>
+__global__ void embedding_bwd_kernel(const int64_t* __restrict__ ids, const T* __restrict__ dout,
+                                     float* __restrict__ dW, int64_t n, int H, int64_t vstart, int64_t vcount) {
+  const int64_t t = blockIdx.x;
+  const int64_t id = ids[t] - vstart;
+  if (id < 0 || id >= vcount) return;
+  const T* d = dout + t * H;
+  float* g = dW + id * H;
+  for (int i = threadIdx.x; i < H; i += blockDim.x) atomicAdd(g + i, to_f(d[i]));
+}
+
+at::Tensor embedding_fwd(const at::Tensor& ids, const at::Tensor& W, int64_t vstart) {
+  TORCH_CHECK(ids.scalar_type() == at::kLong && W.is_contiguous(), "embedding_fwd: int64 ids, contiguous weight");
+  auto idc = ids.contiguous();
+  const int64_t n = idc.numel(), H = W.size(1);
+  auto sizes = ids.sizes().vec();
+  sizes.push_back(H);
+  auto out = at::empty(sizes, W.options());
+  if (n == 0) return out;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(W.scalar_type(), "embedding_fwd", [&] {
+    embedding_fwd_kernel<scalar_t><<<n, 128, 0, stream>>>(idc.data_ptr<int64_t>(), P<scalar_t>(W),
+                                                          P<scalar_t>(out), n, H, vstart, W.size(0), nullptr);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+  return out;
+}
+
+// Accumulates the embedding gradient into an fp32 buffer dW [V, H].
+void embedding_bwd_(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& dW, int64_t vstart) {
+  TORCH_CHECK(dW.scalar_type() == at::kFloat && dW.is_contiguous(), "embedding_bwd_: fp32 contiguous dW");
+  auto idc = ids.contiguous();
+  auto d = dout.contiguous();
+  const int64_t n = idc.numel(), H = dW.size(1);
+  if (n == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  NTB_DISPATCH_FLOAT(d.scalar_type(), "embedding_bwd_", [&] {
+    embedding_bwd_kernel<scalar_t><<<n, 256, 0, stream>>>(idc.data_ptr<int64_t>(), P<scalar_t>(d),
+                                                          dW.data_ptr<float>(), n, H, vstart, dW.size(0));
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+}
+
+// =========================================================== AdamW (flat)
+// torch.optim.AdamW semantics on flat fp32 state:
+//   p *= 1 - lr*wd ; m = b1 m + (1-b1) g ; v = b2 v + (1-b2) g^2
+//   p -= (lr / bc1) * m / (sqrt(v) / sqrt(bc2) + eps)
+// grad is read as fp32 or bf16 and multiplied by grad_scale[0] (unscale /
+// averaging folded in); an optional bf16 copy of the new parameter is written.
+template <typename G>
+__global__ void adamw_kernel(float* __restrict__ p, float* __restrict__ m, float* __restrict__ v,
+                             const G* __restrict__ g, bf16* __restrict__ p_bf16, int64_t n, float lr, float b1,
+                             float b2, float eps, float wd, float bc1, float sqrt_bc2,
+                             const float* __restrict__ grad_scale, const int* __restrict__ skip) {
+  if (skip && *skip) return;
+  const float gs = grad_scale ? *grad_scale : 1.f;
+  const float step = lr / bc1;
+  const float decay = 1.f - lr * wd;
+  const int64_t n4 = n / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n4;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float4 pp = reinterpret_cast<float4*>(p)[i];
+    float4 mm = reinterpret_cast<float4*>(m)[i];
+    float4 vv = reinterpret_cast<float4*>(v)[i];
+    float gg[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) gg[j] = to_f(g[i * 4 + j]) * gs;
+    float* P = &pp.x;
+    float* M = &mm.x;
+    float* Vv = &vv.x;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      P[j] *= decay;
+      M[j] = b1 * M[j] + (1.f - b1) * gg[j];
+      Vv[j] = b2 * Vv[j] + (1.f - b2) * gg[j] * gg[j];
+      P[j] -= step * M[j] / (sqrtf(Vv[j]) / sqrt_bc2 + eps);
+    }
+    reinterpret_cast<float4*>(p)[i] = pp;
+    reinterpret_cast<float4*>(m)[i] = mm;
+    reinterpret_cast<float4*>(v)[i] = vv;
+    if (p_bf16) {
+      uint2 o;
+      o.x = pack_bf16x2(pp.x, pp.y);
+      o.y = pack_bf16x2(pp.z, pp.w);
+      reinterpret_cast<uint2*>(p_bf16)[i] = o;
+    }
+  }
+  for (int64_t i = n4 * 4 + blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const float gg = to_f(g[i]) * gs;
+    float pp = p[i] * decay;
+    const float mm = b1 * m[i] + (1.f - b1) * gg;
+    const float vv = b2 * v[i] + (1.f - b2) * gg * gg;
+    pp -= step * mm / (sqrtf(vv) / sqrt_bc2 + eps);
+    p[i] = pp;
+    m[i] = mm;
+    v[i] = vv;
+    if (p_bf16) p_bf16[i] = __float2bfloat16(pp);
+  }
+}
+
+void adamw_flat_(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& g,
+                 const c10::optional<at::Tensor>& p_bf16, double lr, double b1, double b2, double eps, double wd,
+                 int64_t step, const c10::optional<at::Tensor>& grad_scale, const c10::optional<at::Tensor>& skip) {
+  TORCH_CHECK(p.scalar_type() == at::kFloat && m.scalar_type() == at::kFloat && v.scalar_type() == at::kFloat,
+              "adamw_flat_: fp32 state");
+  TORCH_CHECK(p.is_contiguous() && m.is_contiguous() && v.is_contiguous() && g.is_contiguous(), "adamw_flat_: contiguous");
+  const int64_t n = p.numel();
+  TORCH_CHECK(m.numel() == n && v.numel() == n && g.numel() == n, "adamw_flat_: sizes");
+  if (p_bf16.has_value()) TORCH_CHECK(p_bf16->numel() == n && p_bf16->scalar_type() == at::kBFloat16 && p_bf16->is_contiguous(), "adamw_flat_: p_bf16");
+  if (n == 0) return;
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(p.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(m.data_ptr()) & 15) == 0 &&
+                  (reinterpret_cast<uintptr_t>(v.data_ptr()) & 15) == 0,
+              "adamw_flat_: 16B alignment");
+  if (p_bf16.has_value()) TORCH_CHECK((reinterpret_cast<uintptr_t>(p_bf16->data_ptr()) & 7) == 0, "adamw_flat_: p_bf16 8B alignment");
+  const float bc1 = 1.f - static_cast<float>(std::pow(b1, static_cast<double>(step)));
+  const float bc2 = 1.f - static_cast<float>(std::pow(b2, static_cast<double>(step)));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n / 4 + 255) / 256, num_sms(p.get_device()) * 8)));
+  const float* gs = grad_scale.has_value() ? grad_scale->data_ptr<float>() : nullptr;
+  const int* sk = skip.has_value() ? skip->data_ptr<int>() : nullptr;
+  bf16* pb = p_bf16.has_value() ? reinterpret_cast<bf16*>(p_bf16->data_ptr()) : nullptr;
+  NTB_DISPATCH_FLOAT(g.scalar_type(), "adamw_flat_", [&] {
+    adamw_kernel<scalar_t><<<blocks, 256, 0, stream>>>(p.data_ptr<float>(), m.data_ptr<float>(), v.data_ptr<float>(),
+                                                       P<scalar_t>(g), pb, n, lr, b1, b2, eps, wd, bc1,
+                                                       std::sqrt(bc2), gs, sk);
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+}
+
+// =========================================================== unscale / finite / sum of squares
+// g *= inv_scale (in place, optional) ; out[0] += sum(g^2) ; out[1] = 1 if any non-finite.
+template <typename T>
+__global__ void grad_stats_kernel(T* __restrict__ g, int64_t n, const float* __restrict__ inv_scale,
+                                  float* __restrict__ out) {
+  __shared__ float red[32];
+  const float s = inv_scale ? *inv_scale : 1.f;
+  float ss = 0.f;
+  int bad = 0;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    float v = to_f(g[i]);
+    if (inv_scale) {
+      v *= s;
+      g[i] = from_f<T>(v);
+    }
+    if (!isfinite(v)) bad = 1;
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const int anybad = __syncthreads_or(bad);
+  if (threadIdx.x == 0) {
+    atomicAdd(out, ss);
+    if (anybad) out[1] = 1.f;
+  }
+}
+
+// Returns nothing; accumulates into out (fp32 [2]: sumsq, nonfinite flag).
+void grad_stats_(at::Tensor& g, const c10::optional<at::Tensor>& inv_scale, at::Tensor& out) {
+  TORCH_CHECK(g.is_contiguous() && out.scalar_type() == at::kFloat && out.numel() >= 2, "grad_stats_");
+  const int64_t n = g.numel();
+  if (n == 0) return;
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((n + 255) / 256, num_sms(g.get_device()) * 4)));
+  NTB_DISPATCH_FLOAT(g.scalar_type(), "grad_stats_", [&] {
+    grad_stats_kernel<scalar_t><<<blocks, 256, 0, stream>>>(P<scalar_t>(g), n,
+                                                            inv_scale.has_value() ? inv_scale->data_ptr<float>() : nullptr,
+                                                            out.data_ptr<float>());
+  });
+  NTB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace ntb

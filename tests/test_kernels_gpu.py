@@ -1,0 +1,221 @@
+"""Numerics of every sm_100a kernel against a plain PyTorch fp32 reference."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def rel_err(a, b):
+    a = a.float()
+    b = b.float()
+    return ((a - b).norm() / b.norm().clamp_min(1e-12)).item()
+
+
+@pytest.fixture(scope="module")
+def C():
+    from nano_train_b200.ops._ext import ext
+    return ext()
+
+
+SHAPES = [(128, 128, 64), (256, 512, 256), (304, 200, 136), (1000, 777 * 8, 520), (2048, 4096, 1024)]
+
+
+@pytest.mark.parametrize("a_mn", [False, True])
+@pytest.mark.parametrize("b_mn", [False, True])
+@pytest.mark.parametrize("shape", SHAPES)
+def test_gemm_bf16(C, a_mn, b_mn, shape):
+    M, N, K = shape
+    torch.manual_seed(0)
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    a = A.t().contiguous() if a_mn else A
+    b = B.t().contiguous() if b_mn else B
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    C.gemm_bf16(a, b, out, None, a_mn, b_mn, False, 1.0)
+    torch.cuda.synchronize()
+    ref = A.float() @ B.float().t()
+    assert rel_err(out, ref) < 1e-2, rel_err(out, ref)
+    from nano_train_b200.ops._ext import check_status
+    check_status(0)
+
+
+def test_gemm_fp32_accumulate_bias(C):
+    M, N, K = 384, 640, 192
+    A = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    B = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+    bias = torch.randn(N, device="cuda", dtype=torch.bfloat16)
+    out = torch.randn(M, N, device="cuda", dtype=torch.float32)
+    ref = out + 0.5 * (A.float() @ B.float().t()) + bias.float()
+    C.gemm_bf16(A, B, out, bias, False, False, True, 0.5)
+    torch.cuda.synchronize()
+    assert rel_err(out, ref) < 1e-5
+
+
+def test_linear_autograd_matches_reference():
+    from nano_train_b200.ops.linear import linear
+    torch.manual_seed(0)
+    x = torch.randn(4, 64, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.randn(384, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    b = torch.randn(384, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    y = linear(x, w, b)
+    gy = torch.randn_like(y)
+    y.backward(gy)
+    xr, wr, br = (t.detach().float().requires_grad_() for t in (x, w, b))
+    yr = F.linear(xr, wr, br)
+    yr.backward(gy.float())
+    assert rel_err(y, yr) < 1e-2
+    assert rel_err(x.grad, xr.grad) < 1e-2
+    assert rel_err(w.grad, wr.grad) < 1e-2
+    assert rel_err(b.grad, br.grad) < 1e-2
+
+
+def test_linear_main_grad_accumulation():
+    from nano_train_b200.ops.linear import linear
+    x = torch.randn(512, 256, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(128, 256, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w.main_grad = torch.ones(128, 256, device="cuda", dtype=torch.float32)
+    gy = torch.randn(512, 128, device="cuda", dtype=torch.bfloat16)
+    linear(x, w).backward(gy)
+    ref = 1.0 + gy.float().t() @ x.float()
+    assert w.grad is None
+    assert rel_err(w.main_grad, ref) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("H", [128, 4096, 100])
+def test_rmsnorm(dtype, H):
+    from nano_train_b200.ops.norm import add_rms_norm, rms_norm
+    x = torch.randn(64, H, device="cuda", dtype=dtype, requires_grad=True)
+    r = torch.randn(64, H, device="cuda", dtype=dtype, requires_grad=True)
+    w = (1 + 0.1 * torch.randn(H, device="cuda", dtype=dtype)).requires_grad_()
+    y, h = add_rms_norm(x, r, w, 1e-5)
+    gy = torch.randn_like(y)
+    gh = torch.randn_like(h)
+    (y * gy).sum().backward(retain_graph=True)
+    (h * gh).sum().backward()
+    xr, rr, wr = (t.detach().float().requires_grad_() for t in (x, r, w))
+    hr = xr + rr
+    yr = hr * torch.rsqrt(hr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr
+    ((yr * gy.float()).sum() + (hr * gh.float()).sum()).backward()
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-5
+    assert rel_err(y, yr) < tol
+    assert rel_err(x.grad, xr.grad) < tol
+    assert rel_err(w.grad, wr.grad) < tol
+    y2 = rms_norm(x.detach(), w.detach(), 1e-5)
+    assert rel_err(y2, xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr) < tol
+
+
+def test_layernorm():
+    from nano_train_b200.ops.norm import layer_norm
+    x = torch.randn(32, 192, device="cuda", requires_grad=True)
+    w = torch.randn(192, device="cuda", requires_grad=True)
+    b = torch.randn(192, device="cuda", requires_grad=True)
+    y = layer_norm(x, w, b, 1e-5)
+    g = torch.randn_like(y)
+    y.backward(g)
+    xr, wr, br = (t.detach().clone().requires_grad_() for t in (x, w, b))
+    yr = F.layer_norm(xr, (192,), wr, br, 1e-5)
+    yr.backward(g)
+    assert rel_err(y, yr) < 1e-5
+    assert rel_err(x.grad, xr.grad) < 1e-4
+    assert rel_err(w.grad, wr.grad) < 1e-4
+    assert rel_err(b.grad, br.grad) < 1e-4
+
+
+@pytest.mark.parametrize("mode", ["half", "deepseek"])
+def test_rope(mode):
+    from nano_train_b200.ops.rope import apply_rope, rope_reference
+    x = torch.randn(2, 48, 4, 64, device="cuda", requires_grad=True)
+    y = apply_rope(x, 10000.0, mode)
+    pos = torch.arange(48, device="cuda")
+    xr = x.detach().clone().requires_grad_()
+    yr = rope_reference(xr, pos, 10000.0, mode)
+    g = torch.randn_like(y)
+    y.backward(g)
+    yr.backward(g)
+    assert rel_err(y, yr) < 1e-5
+    assert rel_err(x.grad, xr.grad) < 1e-5
+
+
+def test_swiglu_gelu():
+    from nano_train_b200.ops.activation import gelu, swiglu
+    gu = torch.randn(40, 2 * 96, device="cuda", requires_grad=True)
+    y = swiglu(gu)
+    g = torch.randn_like(y)
+    y.backward(g)
+    gr = gu.detach().clone().requires_grad_()
+    a, b = gr.chunk(2, -1)
+    (F.silu(a) * b).backward(g)
+    assert rel_err(y, F.silu(a) * b) < 1e-5
+    assert rel_err(gu.grad, gr.grad) < 1e-5
+    x = torch.randn(1000, device="cuda", requires_grad=True)
+    y = gelu(x)
+    y.backward(torch.ones_like(y))
+    xr = x.detach().clone().requires_grad_()
+    F.gelu(xr).backward(torch.ones_like(y))
+    assert rel_err(y, F.gelu(xr)) < 1e-5
+    assert rel_err(x.grad, xr.grad) < 1e-4
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_cross_entropy(dtype):
+    from nano_train_b200.ops.loss import cross_entropy
+    logits = torch.randn(37, 1000, device="cuda", dtype=dtype, requires_grad=True)
+    labels = torch.randint(0, 1000, (37,), device="cuda")
+    labels[3] = -100
+    loss = cross_entropy(logits, labels)
+    loss.backward()
+    lr = logits.detach().float().requires_grad_()
+    ref = F.cross_entropy(lr, labels)
+    ref.backward()
+    assert abs(loss.item() - ref.item()) < (1e-4 if dtype == torch.float32 else 1e-2)
+    assert rel_err(logits.grad, lr.grad) < (1e-4 if dtype == torch.float32 else 2e-2)
+
+
+def test_embedding():
+    from nano_train_b200.ops.embedding import embedding
+    W = torch.randn(100, 64, device="cuda", requires_grad=True)
+    ids = torch.randint(0, 100, (4, 16), device="cuda")
+    y = embedding(ids, W)
+    g = torch.randn_like(y)
+    y.backward(g)
+    Wr = W.detach().clone().requires_grad_()
+    F.embedding(ids, Wr).backward(g)
+    assert torch.equal(y, F.embedding(ids, W.detach()))
+    assert rel_err(W.grad, Wr.grad) < 1e-6
+
+
+def test_adamw_flat_matches_torch():
+    from nano_train_b200.ops.optim import adamw_flat_
+    torch.manual_seed(0)
+    n = 1001
+    p = torch.randn(n, device="cuda")
+    m = torch.zeros(n, device="cuda")
+    v = torch.zeros(n, device="cuda")
+    ref = torch.nn.Parameter(p.clone())
+    opt = torch.optim.AdamW([ref], lr=1e-2, betas=(0.9, 0.95), eps=1e-8, weight_decay=0.1)
+    pb = torch.empty(n, device="cuda", dtype=torch.bfloat16)
+    for step in range(1, 7):
+        g = torch.randn(n, device="cuda")
+        ref.grad = g.clone()
+        opt.step()
+        adamw_flat_(p, m, v, g, lr=1e-2, beta1=0.9, beta2=0.95, eps=1e-8, weight_decay=0.1, step=step, param_bf16=pb)
+    torch.testing.assert_close(p, ref.detach(), rtol=1e-5, atol=1e-6)
+    torch.testing.assert_close(pb.float(), ref.detach(), rtol=1e-2, atol=1e-2)
+
+
+def test_grad_stats():
+    from nano_train_b200.ops.optim import grad_stats_
+    g = torch.randn(5000, device="cuda")
+    out = torch.zeros(2, device="cuda")
+    inv = torch.tensor([0.5], device="cuda")
+    ref = (g * 0.5).pow(2).sum()
+    grad_stats_(g, out, inv)
+    assert abs(out[0].item() - ref.item()) / ref.item() < 1e-5
+    assert out[1].item() == 0
+    g[7] = float("inf")
+    grad_stats_(g, out)
+    assert out[1].item() == 1
