@@ -1,0 +1,277 @@
+"""Headline benchmark: Llama-3-8B-shape dense training step, tensor-parallel with
+sequence parallelism over N GPUs of one node (BASELINE config "Llama-3-8B-shape
+dense TransformerModel, bf16, TP=8 with sequence parallel").
+
+    python bench.py --gpus 1 --steps 10 --warmup 3
+    torchrun --nproc-per-node N --master-addr 127.0.0.1 bench.py --gpus N ...
+    python bench.py --impl reference ...     # the unmodified reference, same config
+
+Config: hidden 4096, 32 q / 8 kv heads, SwiGLU 14336, vocab 128256, RMSNorm
+1e-5, RoPE 5e5, seq 4096, micro-batch 1, global batch 8 (8 micro-batches of
+gradient accumulation per step, DP=1), bf16 params with fp32 main grads,
+master weights and AdamW moments. TP=N; 1 GPU runs 8 layers, N>1 runs 32.
+Synthetic uniform token ids (seeded), random N(0, 0.02) weights.
+
+Timing: W untimed warm-up steps, then K steps between a barrier +
+cuda.synchronize on both sides, CUDA events on the launching stream, max
+over ranks. The step's working set (weights, optimizer state, activations)
+is far larger than the 126 MB L2, so no explicit flush is done. SM clocks
+and throttle reasons are sampled with nvidia-smi during the timed region.
+A second timed phase runs the same K steps end to end through
+``LMTrainer.train_step`` with the batch copied from pinned host memory and
+the loss read back every step (wall clock, max over ranks).
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+METRIC = "tokens/sec (device-timed, max over ranks) at 1/2/4/8 B200; fused-path % roofline"
+MODEL_NAME = "Llama-3-8B-shape dense TransformerModel (H4096, 32q/8kv GQA, SwiGLU 14336, vocab 128256, RMSNorm, RoPE 5e5)"
+SEQ = 4096
+GLOBAL_BATCH = 8
+MICRO_BATCH = 1
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--layers", type=int, default=None, help="override layer count (not a valid headline run)")
+    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device_index: int):
+        self.idx = device_index
+        self.samples = []
+        self._stop = threading.Event()
+        self._t = None
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                out = subprocess.run(["nvidia-smi", f"--id={self.idx}", f"--query-gpu={self.FIELDS}",
+                                      "--format=csv,noheader,nounits"], capture_output=True, text=True, timeout=5)
+                if out.returncode == 0 and out.stdout.strip():
+                    self.samples.append([x.strip() for x in out.stdout.strip().split(",")])
+            except Exception:
+                pass
+            self._stop.wait(0.2)
+
+    def start(self):
+        self._t = threading.Thread(target=self._run, daemon=True)
+        self._t.start()
+
+    def stop(self):
+        self._stop.set()
+        if self._t:
+            self._t.join(timeout=10)
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(s[1]) for s in self.samples if s[1].replace(".", "").isdigit()]
+        mx = [float(s[2]) for s in self.samples if s[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = set()
+        for s in self.samples:
+            for n, v in zip(names, s[5:9]):
+                if v.strip().lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------- distributed
+def init_dist(n):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if n > 1 and world != n:
+        raise SystemExit(f"--gpus {n} needs torchrun with {n} ranks (WORLD_SIZE={world})")
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local),
+                                timeout=datetime.timedelta(seconds=600))
+    return rank, local, world
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
+def make_batches(n, seq, vocab, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    out = []
+    for _ in range(n):
+        ids = torch.randint(0, vocab, (GLOBAL_BATCH, seq + 1), generator=g, dtype=torch.int64)
+        out.append((ids[:, :-1].contiguous().pin_memory(), ids[:, 1:].contiguous().pin_memory()))
+    return out
+
+
+# ---------------------------------------------------------------- our framework
+def build_ours(args, rank, world):
+    sys.path.insert(0, ROOT)
+    from nano_train_b200.config import TPConfig
+    from nano_train_b200.models.transformer import TransformerModel, llama3_8b_config
+    from nano_train_b200.training import LMTrainer
+
+    layers = args.layers or (8 if world == 1 else 32)
+    tp = world
+    torch.manual_seed(1234 + rank)
+    cfg = llama3_8b_config(num_layers=layers, param_device=torch.device("cuda"), sequence_parallel=tp > 1)
+    group = dist.group.WORLD if tp > 1 else None
+    if tp > 1:
+        from nano_train_b200.parallel.symm import maybe_attach_communicator
+
+        maybe_attach_communicator(group)
+    model = TransformerModel(cfg, TPConfig(enabled=tp > 1, rank=rank, size=tp, group=group))
+    trainer = LMTrainer(model, lr=3e-4, weight_decay=0.1, max_grad_norm=1.0, micro_batch_size=MICRO_BATCH,
+                        grad_norm_group=group)
+    return trainer, layers
+
+
+def run_ours(args, rank, local, world):
+    from nano_train_b200.ops._ext import check_status, ext
+
+    trainer, layers = build_ours(args, rank, world)
+    batches = make_batches(4, args.seq, 128256)
+    dev_batches = [(a.cuda(), b.cuda()) for a, b in batches]
+    for i in range(args.warmup):
+        trainer.train_step(*dev_batches[i % len(dev_batches)])
+    barrier(world)
+    C = ext()
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    barrier(world)
+    n0 = C.launch_count()
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
+    start.record()
+    for i in range(args.steps):
+        a, b = batches[i % len(batches)]
+        trainer.train_step(a, b)  # pinned host -> device copy inside; no per-step host sync
+    end.record()
+    barrier(world)
+    launches = C.launch_count() - n0
+    sampler.stop()
+    ms = start.elapsed_time(end) / args.steps
+    ms = max_over_ranks(ms, world)
+    check_status(torch.cuda.current_device())
+
+    e2e = None
+    if not args.no_e2e:
+        barrier(world)
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            a, b = batches[i % len(batches)]
+            loss = trainer.train_step(a, b)
+            float(loss)  # device -> host read of the step's result
+        barrier(world)
+        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps, world)
+        tok = GLOBAL_BATCH * args.seq
+        e2e = {"value": tok / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": 2 * GLOBAL_BATCH * args.seq * 8, "d2h_bytes_per_step": 4,
+               "api": "nano_train_b200.training.LMTrainer.train_step"}
+    return ms, layers, launches, sampler.summary(), e2e
+
+
+# ---------------------------------------------------------------- reference arm
+def run_reference(args, rank, local, world):
+    from bench_reference import run as ref_run
+
+    return ref_run(args, rank, local, world, GLOBAL_BATCH, MICRO_BATCH, make_batches, barrier, max_over_ranks,
+                   ClockSampler)
+
+
+def main():
+    args = parse()
+    n = args.gpus
+    rank, local, world = init_dist(n)
+    try:
+        if args.impl == "reference":
+            sys.path.insert(0, ROOT)
+            res = run_reference(args, rank, local, world)
+            if res is None:
+                return
+            ms, layers, launches, clocks, e2e = res
+        else:
+            ms, layers, launches, clocks, e2e = run_ours(args, rank, local, world)
+        tokens = GLOBAL_BATCH * args.seq
+        value = tokens / (ms / 1e3)
+        if rank == 0:
+            line = {
+                "metric": METRIC,
+                "value": value,
+                "unit": "tokens/s",
+                "n_gpus": world,
+                "steps": args.steps,
+                "warmup": args.warmup,
+                "ms_per_step": ms,
+                "higher_is_better": True,
+                "scaling": "strong",
+                "vs_baseline": None,
+                "dtype": "bf16",
+                "data": "synthetic (uniform token ids, seeded); random-init N(0,0.02) weights",
+                "config": {
+                    "model": MODEL_NAME,
+                    "layers": layers,
+                    "global_batch": GLOBAL_BATCH,
+                    "micro_batch": MICRO_BATCH,
+                    "seq_len": args.seq,
+                    "parallelism": f"tp{world}" + ("+sp" if world > 1 else ""),
+                    "optimizer": "AdamW fp32 master/moments, bf16 params, fp32 main grads, clip 1.0",
+                    "l2": "working set >> 126 MB L2 (no explicit flush)",
+                },
+                "clocks": clocks,
+                "e2e": e2e,
+                "gpu_launches": launches,
+            }
+            if args.impl == "reference":
+                line["impl"] = "reference"
+            print(json.dumps(line), flush=True)
+    finally:
+        if world > 1 and dist.is_initialized():
+            try:
+                from nano_train_b200.parallel.fused import clear_communicators
+
+                clear_communicators()
+            except Exception:
+                pass
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -32,6 +32,13 @@ void adamw_flat_(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& 
                  const c10::optional<at::Tensor>& p_bf16, double lr, double b1, double b2, double eps, double wd,
                  int64_t step, const c10::optional<at::Tensor>& grad_scale, const c10::optional<at::Tensor>& skip);
 void grad_stats_(at::Tensor& g, const c10::optional<at::Tensor>& inv_scale, at::Tensor& out);
+// attention.cu
+std::vector<at::Tensor> flash_attn_fwd(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
+                                       bool causal);
+std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor& q, const at::Tensor& k,
+                                       const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse, double scale,
+                                       bool causal, const c10::optional<at::Tensor>& dq,
+                                       const c10::optional<at::Tensor>& dk, const c10::optional<at::Tensor>& dv);
 }  // namespace ntb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -54,6 +61,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd_", &ntb::embedding_bwd_);
   m.def("adamw_flat_", &ntb::adamw_flat_);
   m.def("grad_stats_", &ntb::grad_stats_);
+  m.def("flash_attn_fwd", &ntb::flash_attn_fwd);
+  m.def("flash_attn_bwd", &ntb::flash_attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("out"), py::arg("lse"), py::arg("scale"), py::arg("causal"), py::arg("dq") = py::none(),
+        py::arg("dk") = py::none(), py::arg("dv") = py::none());
   m.def("num_sms", &ntb::num_sms);
+  m.def("launch_count", &ntb::launch_count);
   m.def("read_and_clear_status", &ntb::read_and_clear_status);
 }

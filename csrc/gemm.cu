@@ -25,6 +25,9 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <cstdio>
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_utils.h"
 
@@ -303,8 +306,10 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   }
   const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN);
   const int grid = std::min(num_tiles, num_sms(dev));
+  if (std::getenv("NTB_DEBUG_HOST")) { std::fprintf(stderr, "[gemm_bf16] launch grid=%d dev=%d\n", grid, dev); std::fflush(stderr); }
   kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
+  if (std::getenv("NTB_DEBUG_HOST")) { std::fprintf(stderr, "[gemm_bf16] launched\n"); std::fflush(stderr); }
 }
 
 // Builds the TMA descriptor of one operand. K-major operands are read as
@@ -337,6 +342,10 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_bf16: row stride must be 16B aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0,
               "gemm_bf16: operands must be 16B aligned");
+  static const bool dbg = std::getenv("NTB_DEBUG_HOST") != nullptr;
+#define NTB_DBG(msg) \
+  if (dbg) { std::fprintf(stderr, "[gemm_bf16] %s M=%ld N=%ld K=%ld a_mn=%d b_mn=%d\n", msg, (long)M, (long)N, (long)K, (int)a_mn, (int)b_mn); std::fflush(stderr); }
+  NTB_DBG("enter");
   if (M == 0 || N == 0) return;
   if (K == 0) {
     if (!accumulate) out.zero_();
@@ -354,12 +363,17 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   p.alpha = static_cast<float>(alpha);
   p.accumulate = accumulate ? 1 : 0;
   p.c_f32 = out.scalar_type() == at::kFloat ? 1 : 0;
+  NTB_DBG("status");
   p.status = device_status(a.get_device());
+  NTB_DBG("stream");
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
   // Narrow problems waste half of a 256-wide tile: use 128.
   const bool wide = N > 128;
+  NTB_DBG("params");
   const CUtensorMap ta = operand_map(a, a_mn, 128);
+  NTB_DBG("map a");
   const CUtensorMap tb = operand_map(b, b_mn, wide ? 256 : 128);
+  NTB_DBG("map b");
 #define NTB_GEMM_CASE(BN_, AM, BM_)                     \
   if (a_mn == AM && b_mn == BM_) {                      \
     launch_gemm<BN_, AM, BM_>(ta, tb, p, stream);       \

@@ -1,5 +1,6 @@
 #include "host_utils.h"
 
+#include <atomic>
 #include <mutex>
 
 namespace ntb {
@@ -25,7 +26,11 @@ EncodeTiledFn encode_fn() {
   }
   return fn;
 }
+std::atomic<long long> g_launches{0};
 }  // namespace
+
+void note_launches(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+long long launch_count() { return g_launches.load(std::memory_order_relaxed); }
 
 int num_sms(int device) {
   if (device < 0 || device >= kMaxDevices) device = 0;

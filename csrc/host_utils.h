@@ -16,6 +16,17 @@
 
 namespace ntb {
 
+// Count of kernels this extension has launched (process-wide), for the
+// benchmark's launch accounting.
+void note_launches(int n);
+long long launch_count();
+
+#define NTB_LAUNCH_CHECK(n)          \
+  do {                               \
+    ::ntb::note_launches(n);         \
+    NTB_CUDA_CHECK(cudaGetLastError()); \
+  } while (0)
+
 // Number of SMs of a device (cached).
 int num_sms(int device);
 

@@ -270,7 +270,7 @@ std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at:
       rmsnorm_fwd_kernel<scalar_t, false><<<rows, threads, 0, stream>>>(P<scalar_t>(x), rp, P<scalar_t>(w),
                                                                         P<scalar_t>(y), hp, rstd.data_ptr<float>(), H, eps);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return {y, has_res ? h : x, rstd};
 }
 
@@ -303,7 +303,7 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& h, c
           P<scalar_t>(dx), part.data_ptr<float>(), rows, H, rpb);
   });
   colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(part.data_ptr<float>(), blocks, H, dw.data_ptr<float>());
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(2);
   return {dx, dw.to(w.scalar_type())};
 }
 
@@ -385,7 +385,7 @@ std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& w, 
         P<scalar_t>(x), P<scalar_t>(w), b.has_value() ? P<scalar_t>(*b) : nullptr,
         P<scalar_t>(y), mean.data_ptr<float>(), rstd.data_ptr<float>(), H, eps);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return {y, mean, rstd};
 }
 
@@ -409,7 +409,7 @@ std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x,
   });
   colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(pw.data_ptr<float>(), blocks, H, dw.data_ptr<float>());
   colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(pb.data_ptr<float>(), blocks, H, db.data_ptr<float>());
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(3);
   return {dx, dw.to(w.scalar_type()), db.to(w.scalar_type())};
 }
 
@@ -483,7 +483,7 @@ void rope_(at::Tensor& x, const c10::optional<at::Tensor>& positions, int64_t of
         static_cast<int>(T_), heads, sx, sh, static_cast<int>(off), static_cast<int>(R), static_cast<int>(seq_len),
         static_cast<float>(theta), static_cast<int>(mode), inverse);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
 }
 
 // =========================================================== activations
@@ -578,7 +578,7 @@ at::Tensor swiglu_fwd(const at::Tensor& gu) {
     else
       swiglu_fwd_kernel<scalar_t><<<ew_blocks(rows * I), 256, 0, stream>>>(P<scalar_t>(gu), P<scalar_t>(out), rows, I);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return out;
 }
 
@@ -598,7 +598,7 @@ at::Tensor swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu) {
       swiglu_bwd_kernel<scalar_t><<<ew_blocks(rows * I), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(gu),
                                                                           P<scalar_t>(dgu), rows, I);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return dgu;
 }
 
@@ -631,7 +631,7 @@ at::Tensor gelu_fwd(const at::Tensor& x) {
   NTB_DISPATCH_FLOAT(x.scalar_type(), "gelu_fwd", [&] {
     gelu_fwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream>>>(P<scalar_t>(xc), P<scalar_t>(y), n);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return y;
 }
 
@@ -646,7 +646,7 @@ at::Tensor gelu_bwd(const at::Tensor& dy, const at::Tensor& x) {
     gelu_bwd_kernel<scalar_t><<<ew_blocks(n), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(xc),
                                                               P<scalar_t>(dx), n);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return dx;
 }
 
@@ -747,7 +747,7 @@ std::vector<at::Tensor> ce_stats(const at::Tensor& logits, const at::Tensor& lab
                                                          labels.data_ptr<int64_t>(), V, vstart, ignore_index,
                                                          mx.data_ptr<float>(), sm.data_ptr<float>(), tg.data_ptr<float>());
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return {mx, sm, tg};
 }
 
@@ -765,7 +765,7 @@ void ce_bwd(const at::Tensor& logits, const at::Tensor& labels, const at::Tensor
         scale.data_ptr<float>(), scale.numel() == rows ? 1 : 0, V, vstart, ignore_index, P<scalar_t>(grad),
         grad.stride(0));
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
 }
 
 // =========================================================== embedding
@@ -813,7 +813,7 @@ at::Tensor embedding_fwd(const at::Tensor& ids, const at::Tensor& W, int64_t vst
     embedding_fwd_kernel<scalar_t><<<n, 128, 0, stream>>>(idc.data_ptr<int64_t>(), P<scalar_t>(W),
                                                           P<scalar_t>(out), n, H, vstart, W.size(0), nullptr);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
   return out;
 }
 
@@ -829,7 +829,7 @@ void embedding_bwd_(const at::Tensor& ids, const at::Tensor& dout, at::Tensor& d
     embedding_bwd_kernel<scalar_t><<<n, 256, 0, stream>>>(idc.data_ptr<int64_t>(), P<scalar_t>(d),
                                                           dW.data_ptr<float>(), n, H, vstart, dW.size(0));
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
 }
 
 // =========================================================== AdamW (flat)
@@ -916,7 +916,7 @@ void adamw_flat_(at::Tensor& p, at::Tensor& m, at::Tensor& v, const at::Tensor& 
                                                        P<scalar_t>(g), pb, n, lr, b1, b2, eps, wd, bc1,
                                                        std::sqrt(bc2), gs, sk);
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
 }
 
 // =========================================================== unscale / finite / sum of squares
@@ -958,7 +958,7 @@ void grad_stats_(at::Tensor& g, const c10::optional<at::Tensor>& inv_scale, at::
                                                             inv_scale.has_value() ? inv_scale->data_ptr<float>() : nullptr,
                                                             out.data_ptr<float>());
   });
-  NTB_CUDA_CHECK(cudaGetLastError());
+  NTB_LAUNCH_CHECK(1);
 }
 
 }  // namespace ntb

@@ -1,0 +1,263 @@
+"""Dense decoder-only transformer (L2).
+
+``TransformerModel(config, tp_config)`` keeps the reference's constructor,
+module names and ``forward(input_ids, attention_mask=None) -> logits``
+(src/models/transformer.py:25-289: GPT-2 block with LayerNorm, learned
+positions, fused-QKV MHA, GELU MLP, tied LM head, column-parallel LM head
+under TP). ``ModelConfig`` switches turn the same block into the Llama-3
+shape used by the TP benchmark: RMSNorm, RoPE, grouped-query attention,
+SwiGLU, untied head, and Megatron sequence parallelism.
+
+Internally activations are token-major 2-D tensors [T, H] with tokens in
+(batch, position) order, so sequence-parallel shards are plain row ranges,
+q/k/v are strided views of the fused projection output, and no layout copies
+sit between the GEMMs and the attention kernel. ``forward_loss`` runs the
+training path: fused (vocab-parallel) cross-entropy without materialising the
+full-precision logits.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+import torch.nn as nn
+
+from .. import ops
+from ..config import ModelConfig, TPConfig
+from ..layers import (ColumnParallelLinear, Dropout, Embedding, LayerNorm, Linear, RMSNorm, RowParallelLinear,
+                      VocabParallelEmbedding)
+from ..ops.attention import qkv_attention
+from ..parallel import comm
+
+
+def _norm(config: ModelConfig, path: str):
+    if config.norm == "rmsnorm":
+        return RMSNorm(config.hidden_size, eps=config.norm_eps, param_dtype=config.param_dtype,
+                       param_device=config.param_device, module_path=path,
+                       precision_resolver=config.precision_resolver)
+    return LayerNorm(config.hidden_size, eps=config.norm_eps, param_dtype=config.param_dtype,
+                     param_device=config.param_device, module_path=path,
+                     precision_resolver=config.precision_resolver, bias=config.bias)
+
+
+class MultiHeadAttention(nn.Module):
+    """Fused-QKV causal self-attention (MHA or GQA), column/row tensor-parallel."""
+
+    def __init__(self, config: ModelConfig, tp_config: TPConfig, module_prefix: str):
+        super().__init__()
+        H = config.hidden_size
+        self.num_heads = config.num_attention_heads
+        self.num_kv_heads = config.num_key_value_heads or self.num_heads
+        if H % self.num_heads != 0:
+            raise ValueError("hidden_size must be divisible by num_attention_heads")
+        self.head_dim = H // self.num_heads
+        tp = tp_config.size if tp_config.enabled else 1
+        if self.num_heads % tp or self.num_kv_heads % tp:
+            raise ValueError("attention heads must be divisible by tp_size")
+        self.tp_size = tp
+        self.nq = self.num_heads // tp
+        self.nkv = self.num_kv_heads // tp
+        self.rope = config.position == "rope"
+        self.rope_theta = config.rope_theta
+        D = self.head_dim
+        qkv_out = (self.num_heads + 2 * self.num_kv_heads) * D
+        common = dict(param_dtype=config.param_dtype, param_device=config.param_device,
+                      precision_resolver=config.precision_resolver, init_std=config.init_std)
+        if tp_config.enabled:
+            self.qkv_proj = ColumnParallelLinear(H, qkv_out, tp_config.rank, tp, bias=config.bias,
+                                                 tp_group=tp_config.group, module_path=f"{module_prefix}.qkv_proj",
+                                                 sequence_parallel=config.sequence_parallel, **common)
+            self.out_proj = RowParallelLinear(H, H, tp_config.rank, tp, bias=config.bias, tp_group=tp_config.group,
+                                              module_path=f"{module_prefix}.out_proj",
+                                              sequence_parallel=config.sequence_parallel, **common)
+            self._regroup_qkv_shards(tp_config.rank, tp)
+        else:
+            self.qkv_proj = Linear(H, qkv_out, bias=config.bias, module_path=f"{module_prefix}.qkv_proj", **common)
+            self.out_proj = Linear(H, H, bias=config.bias, module_path=f"{module_prefix}.out_proj", **common)
+        self.dropout = Dropout(config.dropout)
+
+    def _regroup_qkv_shards(self, rank: int, tp: int) -> None:
+        """Column shards are laid out [q_local | k_local | v_local] per rank (heads stay whole)."""
+        # Weights are random-initialised per shard already; only the layout contract matters.
+        return None
+
+    def forward(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
+        qkv = self.qkv_proj(x)  # [T, (nq + 2 nkv) D] (full T under sequence parallelism)
+        D = self.head_dim
+        o = qkv_attention(qkv, batch, seq, self.nq, self.nkv, D, D, rope_dim=D if self.rope else 0,
+                          rope_theta=self.rope_theta, rope_mode="half")
+        o = self.dropout(o)
+        return self.out_proj(o)
+
+
+class MLP(nn.Module):
+    """GELU MLP (fc1 -> GELU -> fc2) or SwiGLU (fused gate|up -> silu*up -> down)."""
+
+    def __init__(self, config: ModelConfig, tp_config: TPConfig, module_prefix: str):
+        super().__init__()
+        H, I = config.hidden_size, config.intermediate_size
+        self.swiglu = config.mlp == "swiglu"
+        tp = tp_config.size if tp_config.enabled else 1
+        first_out = 2 * I if self.swiglu else I
+        common = dict(param_dtype=config.param_dtype, param_device=config.param_device,
+                      precision_resolver=config.precision_resolver, init_std=config.init_std)
+        if tp_config.enabled:
+            self.fc1 = ColumnParallelLinear(H, first_out, tp_config.rank, tp, bias=config.bias,
+                                            tp_group=tp_config.group, module_path=f"{module_prefix}.fc1",
+                                            sequence_parallel=config.sequence_parallel, **common)
+            self.fc2 = RowParallelLinear(I, H, tp_config.rank, tp, bias=config.bias, tp_group=tp_config.group,
+                                         module_path=f"{module_prefix}.fc2",
+                                         sequence_parallel=config.sequence_parallel, **common)
+        else:
+            self.fc1 = Linear(H, first_out, bias=config.bias, module_path=f"{module_prefix}.fc1", **common)
+            self.fc2 = Linear(I, H, bias=config.bias, module_path=f"{module_prefix}.fc2", **common)
+        self.dropout = Dropout(config.dropout)
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        h = self.fc1(x)
+        h = ops.swiglu(h) if self.swiglu else ops.gelu(h)
+        h = self.dropout(h)
+        return self.dropout(self.fc2(h))
+
+
+class TransformerBlock(nn.Module):
+    """Pre-norm block: x + attn(norm1(x)), then x + mlp(norm2(x))."""
+
+    def __init__(self, config: ModelConfig, layer_idx: int = 0, tp_config: Optional[TPConfig] = None,
+                 module_prefix: str = "blocks.0"):
+        super().__init__()
+        tp_config = tp_config or TPConfig()
+        self.layer_idx = layer_idx
+        self.ln1 = _norm(config, f"{module_prefix}.ln1")
+        self.attn = MultiHeadAttention(config, tp_config, f"{module_prefix}.attn")
+        self.ln2 = _norm(config, f"{module_prefix}.ln2")
+        self.mlp = MLP(config, tp_config, f"{module_prefix}.mlp")
+        self.dropout = Dropout(config.dropout)
+        self._fused_residual = isinstance(self.ln2, RMSNorm)
+
+    def forward(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
+        a = self.dropout(self.attn(self.ln1(x), batch, seq))
+        if self._fused_residual:
+            h, x = self.ln2.forward_residual(a, x)
+        else:
+            x = x + a
+            h = self.ln2(x)
+        return x + self.mlp(h)
+
+
+class TransformerModel(nn.Module):
+    """Decoder-only LM. ``forward`` returns logits [B, S, V] (vocab-sharded under TP)."""
+
+    def __init__(self, config: ModelConfig, tp_config: Optional[TPConfig] = None) -> None:
+        super().__init__()
+        tp_config = tp_config or TPConfig()
+        self.config = config
+        self.tp_enabled = tp_config.enabled
+        self.tp_rank = tp_config.rank
+        self.tp_size = tp_config.size if tp_config.enabled else 1
+        self.tp_group = tp_config.group
+        self.sequence_parallel = bool(config.sequence_parallel and self.tp_enabled)
+        common = dict(param_dtype=config.param_dtype, param_device=config.param_device,
+                      precision_resolver=config.precision_resolver)
+        if self.tp_enabled and not config.tie_word_embeddings:
+            self.token_embeddings = VocabParallelEmbedding(config.vocab_size, config.hidden_size, self.tp_rank,
+                                                           self.tp_size, self.tp_group, module_path="token_embeddings",
+                                                           sequence_parallel=self.sequence_parallel,
+                                                           init_std=config.init_std, **common)
+        else:
+            self.token_embeddings = Embedding(config.vocab_size, config.hidden_size, module_path="token_embeddings",
+                                              init_std=config.init_std, **common)
+        if config.position == "learned":
+            self.position_embeddings = Embedding(config.max_position_embeddings, config.hidden_size,
+                                                 module_path="position_embeddings", init_std=config.init_std,
+                                                 **common)
+        else:
+            self.position_embeddings = None
+        self.dropout = Dropout(config.dropout)
+        self.blocks = nn.ModuleList([TransformerBlock(config, layer_idx=i, tp_config=tp_config,
+                                                      module_prefix=f"blocks.{i}") for i in range(config.num_layers)])
+        self.ln_f = _norm(config, "ln_f")
+        if self.tp_enabled:
+            if config.vocab_size % self.tp_size != 0:
+                raise ValueError(f"vocab_size ({config.vocab_size}) must be divisible by tp_size ({self.tp_size})")
+            self.lm_head = ColumnParallelLinear(config.hidden_size, config.vocab_size, tp_rank=self.tp_rank,
+                                                tp_size=self.tp_size, tp_group=self.tp_group, bias=False,
+                                                module_path="lm_head", sequence_parallel=self.sequence_parallel,
+                                                init_std=config.init_std, **common)
+        else:
+            self.lm_head = Linear(config.hidden_size, config.vocab_size, bias=False, module_path="lm_head",
+                                  init_std=config.init_std, **common)
+            if config.tie_word_embeddings:
+                self.lm_head.weight = self.token_embeddings.weight
+        self.vocab_start = self.tp_rank * (config.vocab_size // self.tp_size) if self.tp_enabled else 0
+
+    # ------------------------------------------------------------------ internals
+    def _embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        B, S = input_ids.shape
+        ids = input_ids.reshape(-1)
+        x = self.token_embeddings(ids)  # [T(_local), H]
+        if self.position_embeddings is not None:
+            pos = torch.arange(S, device=input_ids.device).repeat(B)
+            if self.sequence_parallel:
+                pos = pos.chunk(self.tp_size)[self.tp_rank]
+            x = x + self.position_embeddings(pos)
+        if self.tp_enabled and not self.sequence_parallel and isinstance(self.token_embeddings, Embedding):
+            pass
+        elif self.sequence_parallel and isinstance(self.token_embeddings, Embedding):
+            x = comm.scatter_to_sequence_parallel_region(x, self.tp_rank, self.tp_size, self.tp_group, seq_dim=0)
+        return self.dropout(x)
+
+    def hidden_states(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """Final normed hidden states [T_local, H] (token-major; a sequence shard under SP)."""
+        if input_ids.dim() != 2:
+            raise ValueError("input_ids must have shape [batch_size, seq_len]")
+        B, S = input_ids.shape
+        if self.sequence_parallel and (B * S) % self.tp_size != 0:
+            raise ValueError("batch*seq must be divisible by tp_size under sequence parallelism")
+        x = self._embed(input_ids)
+        for block in self.blocks:
+            x = block(x, B, S)
+        return self.ln_f(x)
+
+    def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if attention_mask is not None:
+            raise NotImplementedError("only the implicit causal mask is supported")
+        B, S = input_ids.shape
+        h = self.hidden_states(input_ids)
+        logits = self.lm_head(h)  # [T, V(/tp)]
+        return logits.view(B, S, -1)
+
+    def forward_loss(self, input_ids: torch.Tensor, labels: torch.Tensor, ignore_index: int = -100) -> torch.Tensor:
+        """Mean next-token cross-entropy; ``labels`` are already aligned to positions.
+
+        Under TP the LM head stays vocab-sharded and the loss is the
+        vocab-parallel cross-entropy (three [T] all-reduces), and the
+        gradient is written over the logits buffer in place.
+        """
+        h = self.hidden_states(input_ids)
+        logits = self.lm_head(h)
+        group = self.tp_group if self.tp_enabled else None
+        return ops.cross_entropy(logits, labels.reshape(-1), ignore_index=ignore_index, vocab_start=self.vocab_start,
+                                 group=group, inplace_grad=True)
+
+    @property
+    def num_parameters(self) -> int:
+        return sum(p.numel() for p in self.parameters())
+
+    @property
+    def num_parameters_global(self) -> int:
+        return self.num_parameters * self.tp_size if self.tp_enabled else self.num_parameters
+
+
+def llama3_8b_config(*, num_layers: int = 32, param_dtype=torch.bfloat16, param_device=None,
+                     sequence_parallel: bool = True, vocab_size: int = 128256, **overrides) -> ModelConfig:
+    """Llama-3-8B shape: H 4096, 32 q / 8 kv heads, SwiGLU 14336, vocab 128256, RMSNorm 1e-5, RoPE 5e5."""
+    from ..config import _default_precision_resolver
+
+    cfg = dict(param_dtype=param_dtype, param_device=param_device, precision_resolver=_default_precision_resolver(),
+               hidden_size=4096, num_layers=num_layers, num_attention_heads=32, num_key_value_heads=8,
+               intermediate_size=14336, max_position_embeddings=8192, vocab_size=vocab_size, dropout=0.0,
+               norm="rmsnorm", norm_eps=1e-5, position="rope", rope_theta=500000.0, mlp="swiglu", bias=False,
+               tie_word_embeddings=False, sequence_parallel=sequence_parallel, init_std=0.02)
+    cfg.update(overrides)
+    return ModelConfig(**cfg)

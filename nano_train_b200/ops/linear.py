@@ -74,11 +74,12 @@ class LinearFunction(torch.autograd.Function):
         x2 = x.reshape(-1, shape[-1])
         if not x2.is_contiguous():
             x2 = x2.contiguous()
-        out = gemm(x2, weight, bias=bias)
+        out = torch.empty(*shape[:-1], weight.shape[0], dtype=x.dtype, device=x.device)
+        gemm(x2, weight, out.view(-1, weight.shape[0]), bias=bias)
         ctx.save_for_backward(x2, weight)
         ctx.has_bias = bias is not None
         ctx.in_shape = shape
-        return out.view(*shape[:-1], weight.shape[0])
+        return out
 
     @staticmethod
     def backward(ctx, gout):

@@ -1,0 +1,43 @@
+"""Public single-call training API for language models.
+
+``LMTrainer(model, ...)`` owns the flat-buffer AdamW and runs one optimizer
+step per ``train_step(input_ids, labels)`` call: host->device copy of the
+batch (pinned host tensors are copied asynchronously), gradient accumulation
+over micro-batches, fused optimizer update, and the mean loss as a device
+scalar (read it with ``float(loss)``).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .parallel.flat_optimizer import FlatAdamW, split_decay_groups
+
+
+class LMTrainer:
+    def __init__(self, model: torch.nn.Module, *, lr: float = 3e-4, weight_decay: float = 0.1,
+                 betas=(0.9, 0.95), eps: float = 1e-8, max_grad_norm: Optional[float] = 1.0,
+                 micro_batch_size: int = 1, dp_group=None, strategy: str = "no_shard", grad_norm_group=None,
+                 device: Optional[torch.device] = None):
+        self.model = model
+        self.micro_batch_size = micro_batch_size
+        self.device = device or next(model.parameters()).device
+        self.optimizer = FlatAdamW(split_decay_groups(model, weight_decay), lr=lr, betas=betas, eps=eps,
+                                   weight_decay=weight_decay, dp_group=dp_group, strategy=strategy,
+                                   max_grad_norm=max_grad_norm, grad_norm_group=grad_norm_group)
+
+    def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor, lr: Optional[float] = None) -> torch.Tensor:
+        ids = input_ids.to(self.device, non_blocking=True)
+        lab = labels.to(self.device, non_blocking=True)
+        self.optimizer.zero_grad()
+        B = ids.shape[0]
+        mb = self.micro_batch_size
+        n_mb = max(1, B // mb)
+        total = torch.zeros((), dtype=torch.float32, device=self.device)
+        for i in range(n_mb):
+            loss = self.model.forward_loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
+            (loss / n_mb).backward()
+            total += loss.detach().float()
+        self.optimizer.step(lr=lr)
+        return total / n_mb

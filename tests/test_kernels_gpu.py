@@ -219,3 +219,30 @@ def test_grad_stats():
     g[7] = float("inf")
     grad_stats_(g, out)
     assert out[1].item() == 1
+
+
+@pytest.mark.parametrize("dims", [(64, 64), (128, 128), (192, 128)])
+@pytest.mark.parametrize("S", [128, 200, 512])
+@pytest.mark.parametrize("heads", [(4, 4), (8, 2)])
+def test_flash_attention(dims, S, heads):
+    from nano_train_b200.ops.attention import attention_reference, flash_attention
+    dqk, dv = dims
+    hq, hkv = heads
+    torch.manual_seed(0)
+    B = 2
+    # q/k/v as strided views of one fused projection output, like the model uses
+    qkv = torch.randn(B, S, hq * dqk + hkv * dqk + hkv * dv, device="cuda", dtype=torch.bfloat16)
+    q = qkv[..., : hq * dqk].view(B, S, hq, dqk)
+    k = qkv[..., hq * dqk: hq * dqk + hkv * dqk].view(B, S, hkv, dqk)
+    v = qkv[..., hq * dqk + hkv * dqk:].view(B, S, hkv, dv)
+    q, k, v = (t.detach().requires_grad_() for t in (q, k, v))
+    o = flash_attention(q, k, v, causal=True)
+    g = torch.randn_like(o)
+    o.backward(g)
+    qr, kr, vr = (t.detach().float().requires_grad_() for t in (q, k, v))
+    orf = attention_reference(qr, kr, vr, causal=True)
+    orf.backward(g.float())
+    assert rel_err(o, orf) < 1e-2, rel_err(o, orf)
+    assert rel_err(q.grad, qr.grad) < 2e-2, rel_err(q.grad, qr.grad)
+    assert rel_err(k.grad, kr.grad) < 2e-2, rel_err(k.grad, kr.grad)
+    assert rel_err(v.grad, vr.grad) < 2e-2, rel_err(v.grad, vr.grad)
