@@ -1,7 +1,27 @@
 // Python bindings of the nano_train_b200 CUDA extension (module `_C`).
+#include <execinfo.h>
+#include <signal.h>
+#include <unistd.h>
+
+#include <cstdlib>
+
 #include <torch/extension.h>
 
 #include "host_utils.h"
+
+namespace {
+// Debug aid (NTB_DEBUG_HOST=1): print the native backtrace of a SIGSEGV before dying.
+void segv_backtrace(int sig) {
+  void* frames[64];
+  const int n = backtrace(frames, 64);
+  const char msg[] = "[ntb] native backtrace:\n";
+  ssize_t w = write(2, msg, sizeof(msg) - 1);
+  (void)w;
+  backtrace_symbols_fd(frames, n, 2);
+  signal(sig, SIG_DFL);
+  raise(sig);
+}
+}  // namespace
 
 namespace ntb {
 // gemm.cu
@@ -39,10 +59,15 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse, double scale,
                                        bool causal, const c10::optional<at::Tensor>& dq,
                                        const c10::optional<at::Tensor>& dk, const c10::optional<at::Tensor>& dv);
+// quant.cu
+std::vector<at::Tensor> fp8_quantize(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
+at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
+at::Tensor fp8_dequantize(const at::Tensor& q, const at::Tensor& scales, int64_t block_rows, at::ScalarType dtype);
 }  // namespace ntb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "nano_train_b200 sm_100a kernels";
+  if (std::getenv("NTB_DEBUG_HOST")) signal(SIGSEGV, segv_backtrace);
   m.def("gemm_bf16", &ntb::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("out"),
         py::arg("bias") = py::none(), py::arg("a_mn") = false, py::arg("b_mn") = false, py::arg("accumulate") = false,
         py::arg("alpha") = 1.0);
@@ -65,6 +90,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd", &ntb::flash_attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("out"), py::arg("lse"), py::arg("scale"), py::arg("causal"), py::arg("dq") = py::none(),
         py::arg("dk") = py::none(), py::arg("dv") = py::none());
+  m.def("fp8_quantize", &ntb::fp8_quantize);
+  m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
+  m.def("fp8_dequantize", &ntb::fp8_dequantize);
   m.def("num_sms", &ntb::num_sms);
   m.def("launch_count", &ntb::launch_count);
   m.def("read_and_clear_status", &ntb::read_and_clear_status);

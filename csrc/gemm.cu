@@ -294,7 +294,7 @@ __global__ void __launch_bounds__(192, 1)
 // ------------------------------------------------------------------ host side
 
 template <int BN, bool A_MN, bool B_MN>
-static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+static void launch_gemm(const CUtensorMap* ta, const CUtensorMap* tb, GemmParams p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_bf16_kernel<BN, A_MN, B_MN>;
   static bool attr_set[16] = {false};
@@ -306,20 +306,19 @@ static void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const Gemm
   }
   const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN);
   const int grid = std::min(num_tiles, num_sms(dev));
-  if (std::getenv("NTB_DEBUG_HOST")) { std::fprintf(stderr, "[gemm_bf16] launch grid=%d dev=%d\n", grid, dev); std::fflush(stderr); }
-  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  void* args[3] = {const_cast<CUtensorMap*>(ta), const_cast<CUtensorMap*>(tb), &p};
+  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(192), args,
+                                  Cfg::SMEM_BYTES, stream));
   NTB_LAUNCH_CHECK(1);
-  if (std::getenv("NTB_DEBUG_HOST")) { std::fprintf(stderr, "[gemm_bf16] launched\n"); std::fflush(stderr); }
 }
 
 // Builds the TMA descriptor of one operand. K-major operands are read as
 // [rows, K] boxes of 64 x rows_box; MN-major operands as [K, MN] boxes of
 // 64 x 64 (the swizzled K-row is the 64-element MN strip).
-static CUtensorMap operand_map(const at::Tensor& t, bool mn_major, int rows_box) {
+static void operand_map(CUtensorMap* out, const at::Tensor& t, bool mn_major, int rows_box) {
   const int64_t d0 = t.size(1), d1 = t.size(0);
   const int64_t ld = t.stride(0);
-  if (mn_major) return make_tma_2d_bf16(t.data_ptr(), d0, d1, ld, 64, 64);
-  return make_tma_2d_bf16(t.data_ptr(), d0, d1, ld, 64, rows_box);
+  make_tma_2d_bf16(out, t.data_ptr(), d0, d1, ld, 64, mn_major ? 64 : rows_box);
 }
 
 // out = alpha * op(a) . op(b)^T (+ bias) (+ out if accumulate).
@@ -342,10 +341,6 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_bf16: row stride must be 16B aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0,
               "gemm_bf16: operands must be 16B aligned");
-  static const bool dbg = std::getenv("NTB_DEBUG_HOST") != nullptr;
-#define NTB_DBG(msg) \
-  if (dbg) { std::fprintf(stderr, "[gemm_bf16] %s M=%ld N=%ld K=%ld a_mn=%d b_mn=%d\n", msg, (long)M, (long)N, (long)K, (int)a_mn, (int)b_mn); std::fflush(stderr); }
-  NTB_DBG("enter");
   if (M == 0 || N == 0) return;
   if (K == 0) {
     if (!accumulate) out.zero_();
@@ -363,17 +358,15 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   p.alpha = static_cast<float>(alpha);
   p.accumulate = accumulate ? 1 : 0;
   p.c_f32 = out.scalar_type() == at::kFloat ? 1 : 0;
-  NTB_DBG("status");
   p.status = device_status(a.get_device());
-  NTB_DBG("stream");
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
   // Narrow problems waste half of a 256-wide tile: use 128.
   const bool wide = N > 128;
-  NTB_DBG("params");
-  const CUtensorMap ta = operand_map(a, a_mn, 128);
-  NTB_DBG("map a");
-  const CUtensorMap tb = operand_map(b, b_mn, wide ? 256 : 128);
-  NTB_DBG("map b");
+  TmaSlots& slots = tls_tma_slots();
+  CUtensorMap* ta = &slots.m[0];
+  CUtensorMap* tb = &slots.m[1];
+  operand_map(ta, a, a_mn, 128);
+  operand_map(tb, b, b_mn, wide ? 256 : 128);
 #define NTB_GEMM_CASE(BN_, AM, BM_)                     \
   if (a_mn == AM && b_mn == BM_) {                      \
     launch_gemm<BN_, AM, BM_>(ta, tb, p, stream);       \

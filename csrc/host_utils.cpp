@@ -1,6 +1,8 @@
 #include "host_utils.h"
 
 #include <atomic>
+#include <cstdio>
+#include <cstdlib>
 #include <mutex>
 
 namespace ntb {
@@ -74,23 +76,39 @@ int read_and_clear_status(int device) {
   return v;
 }
 
-CUtensorMap make_tma_2d(void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1, int64_t ld,
-                        int box0, int box1, CUtensorMapSwizzle swz) {
-  CUtensorMap m;
+void bind_current_context() {
+  static thread_local int bound_device = -1;
+  int dev = 0;
+  NTB_CUDA_CHECK(cudaGetDevice(&dev));
+  if (bound_device != dev) {
+    NTB_CUDA_CHECK(cudaSetDevice(dev));
+    bound_device = dev;
+  }
+}
+
+TmaSlots& tls_tma_slots() {
+  static thread_local TmaSlots slots;
+  return slots;
+}
+
+void make_tma_2d(CUtensorMap* out, void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1,
+                 int64_t ld, int box0, int box1, CUtensorMapSwizzle swz) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(out) & 63) == 0, "tensor map storage must be 64-byte aligned");
   cuuint64_t dims[2] = {static_cast<cuuint64_t>(d0), static_cast<cuuint64_t>(d1)};
   cuuint64_t strides[1] = {static_cast<cuuint64_t>(ld * elem_bytes)};
   cuuint32_t box[2] = {static_cast<cuuint32_t>(box0), static_cast<cuuint32_t>(box1)};
   cuuint32_t estr[2] = {1, 1};
-  CUresult r = encode_fn()(&m, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+  // The driver call needs a current context; a thread that has not made a
+  // runtime call yet (e.g. autograd's device thread) has none.
+  bind_current_context();
+  CUresult r = encode_fn()(out, dtype, 2, base, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled failed (", static_cast<int>(r), ") dims=", d0, "x", d1,
               " ld=", ld, " box=", box0, "x", box1);
-  return m;
 }
 
-CUtensorMap make_tma_2d_bf16(void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1) {
-  return make_tma_2d(base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d0, d1, ld, box0, box1,
-                     CU_TENSOR_MAP_SWIZZLE_128B);
+void make_tma_2d_bf16(CUtensorMap* out, void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1) {
+  make_tma_2d(out, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d0, d1, ld, box0, box1, CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
 }  // namespace ntb

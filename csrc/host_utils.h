@@ -37,13 +37,25 @@ int* device_status(int device);
 // Reads and clears the status word of a device (synchronises the device).
 int read_and_clear_status(int device);
 
+// Tensor maps are written into caller-provided storage that must be 64-byte
+// aligned (the driver stores them with aligned vector writes). Host code
+// keeps them in thread-local aligned slots (TmaSlots) and launches kernels
+// with cudaLaunchKernel by pointer, never copying a CUtensorMap through an
+// ordinary stack frame whose alignment is not guaranteed.
+struct alignas(128) TmaSlots {
+  CUtensorMap m[4];
+};
+TmaSlots& tls_tma_slots();
+
+// Makes the current device's primary context current on this thread.
+void bind_current_context();
+
 // 2-D TMA descriptor for a bf16 matrix with inner extent d0 (contiguous),
 // outer extent d1, row pitch ld (elements), box box0 x box1, 128-byte swizzle.
-CUtensorMap make_tma_2d_bf16(void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1);
+void make_tma_2d_bf16(CUtensorMap* out, void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1);
 
-// Same for an arbitrary element size in bytes with a chosen swizzle
-// (0 none, 3 = 128B).
-CUtensorMap make_tma_2d(void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1, int64_t ld,
-                        int box0, int box1, CUtensorMapSwizzle swz);
+// Same for an arbitrary element size in bytes with a chosen swizzle.
+void make_tma_2d(CUtensorMap* out, void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1,
+                 int64_t ld, int box0, int box1, CUtensorMapSwizzle swz);
 
 }  // namespace ntb

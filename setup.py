@@ -8,6 +8,14 @@ library travels with the source tree.
 import glob
 import os
 
+# Use the system toolchain: a compiler wrapper whose private libstdc++.so
+# symlink does not resolve makes the linker fall back to the static archive,
+# and a second (static) libstdc++ inside the extension breaks iostreams.
+for _var, _path in (("CC", "/usr/bin/gcc"), ("CXX", "/usr/bin/g++")):
+    if os.path.exists(_path):
+        os.environ[_var] = _path
+os.environ.setdefault("CUDAHOSTCXX", os.environ.get("CXX", "g++"))
+
 from setuptools import find_packages, setup
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
