@@ -155,7 +155,7 @@ def build_ours(args, rank, world):
     if tp > 1:
         from nano_train_b200.parallel.symm import maybe_attach_communicator
 
-        maybe_attach_communicator(group)
+        maybe_attach_communicator(group, max_local_rows=MICRO_BATCH * args.seq // tp, max_k=4096, max_rs_n=4096)
     model = TransformerModel(cfg, TPConfig(enabled=tp > 1, rank=rank, size=tp, group=group))
     trainer = LMTrainer(model, lr=3e-4, weight_decay=0.1, max_grad_norm=1.0, micro_batch_size=MICRO_BATCH,
                         grad_norm_group=group)

@@ -63,6 +63,20 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
 std::vector<at::Tensor> fp8_quantize(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
 at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
 at::Tensor fp8_dequantize(const at::Tensor& q, const at::Tensor& scales, int64_t block_rows, at::ScalarType dtype);
+// tp_fused.cu
+void ag_gemm(const at::Tensor& x_local, at::Tensor& x_full_out, const at::Tensor& w, at::Tensor& y,
+             const c10::optional<at::Tensor>& bias, bool b_mn, std::vector<int64_t> slots, std::vector<int64_t> ready,
+             at::Tensor& chunk_flags, at::Tensor& tile_ctr, int64_t rank, int64_t epoch, int64_t copy_ctas);
+void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+             bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> counters, at::Tensor& tile_ctr, int64_t rank,
+             int64_t epoch);
+// symm.cpp
+std::tuple<int64_t, py::bytes> symm_alloc(int64_t bytes);
+int64_t symm_open(py::bytes handle);
+void symm_close(int64_t peer_ptr);
+void symm_free(int64_t ptr);
+at::Tensor symm_local_view(int64_t ptr, int64_t offset_bytes, std::vector<int64_t> sizes, at::ScalarType dtype,
+                           int64_t device);
 }  // namespace ntb
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -93,6 +107,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize", &ntb::fp8_quantize);
   m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
   m.def("fp8_dequantize", &ntb::fp8_dequantize);
+  m.def("ag_gemm", &ntb::ag_gemm);
+  m.def("gemm_rs", &ntb::gemm_rs);
+  m.def("symm_alloc", &ntb::symm_alloc);
+  m.def("symm_open", &ntb::symm_open);
+  m.def("symm_close", &ntb::symm_close);
+  m.def("symm_free", &ntb::symm_free);
+  m.def("symm_local_view", &ntb::symm_local_view);
   m.def("num_sms", &ntb::num_sms);
   m.def("launch_count", &ntb::launch_count);
   m.def("read_and_clear_status", &ntb::read_and_clear_status);

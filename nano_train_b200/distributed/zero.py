@@ -1,0 +1,488 @@
+"""Megatron-style ZeRO-1 / ZeRO-2 distributed optimizer with checkpoint format v2.
+
+Sharding semantics (and therefore the checkpoint format) are the reference's
+(src/distributed/zero.py:119-759): every parameter is split into
+``ceil(numel / g)`` chunks over its data-parallel domain (DP for dense,
+EDP for expert parameters); each rank owns fp32 master / exp_avg / exp_avg_sq
+for its chunk; ZeRO-1 (``optim``) all-reduces gradients, ZeRO-2
+(``optim_grads``) reduce-scatters them; updated shards are all-gathered back
+into the parameters. The v2 files are ``optimizer_nonparam.pt``,
+``optimizer_shard_rank{r}.pt`` and ``optimizer_manifest.json`` with the same
+keys, the same SHA-256 parameter-signature recipe (JSON of
+[{name, shape, dtype, is_expert_param}], sorted keys) and the same checks
+(format version 2, recipe metadata, signature hash, shard sizes, world size).
+
+Execution (B200 build): per domain, all local shards live in ONE flat buffer
+(rank-major: rank r's chunks of every parameter are contiguous), so a step
+is one permutation gather of the gradients into rank-major order, one
+reduce-scatter (or all-reduce), one fused AdamW kernel over the flat shard,
+and one all-gather + inverse permutation - instead of one collective and one
+optimizer loop iteration per parameter.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import logging
+import math
+import os
+from dataclasses import asdict, dataclass
+from typing import Dict, Literal, Optional, Set
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+
+from .. import ops
+
+LOGGER = logging.getLogger(__name__)
+ZERO_CHECKPOINT_FORMAT_VERSION = 2
+DataParallelShardingStrategy = Literal["no_shard", "optim", "optim_grads"]
+OptimizerStateDType = Literal["fp32", "bf16", "fp16"]
+
+
+@dataclass
+class DistributedOptimizerConfig:
+    use_distributed_optimizer: bool
+    data_parallel_sharding_strategy: DataParallelShardingStrategy
+    num_distributed_optimizer_instances: int = 1
+    learning_rate: float = 1e-3
+    weight_decay: float = 0.0
+    betas: tuple[float, float] = (0.9, 0.999)
+    eps: float = 1e-8
+    use_reduce_scatter: bool = True
+    main_params_dtype: OptimizerStateDType = "fp32"
+    main_grads_dtype: OptimizerStateDType = "fp32"
+    exp_avg_dtype: OptimizerStateDType = "fp32"
+    exp_avg_sq_dtype: OptimizerStateDType = "fp32"
+    precision_recipe_name: str = "default"
+    fp8_rounding: str = "nearest"
+    fp8_activation_quant_granularity: str = "tensor"
+    fp8_weight_quant_granularity: str = "tensor"
+    fp8_comm_quant_enabled: bool = False
+    fp8_comm_quant_granularity: str = "tensor"
+    debug: bool = False
+    debug_max_steps: int = 1
+    debug_max_params: int = 8
+
+
+@dataclass
+class _ShardMeta:
+    name: str
+    numel: int
+    shape: tuple[int, ...]
+    dtype: str
+    is_expert_param: bool
+    group_size: int
+    group_rank: int
+    shard_start: int
+    shard_end: int
+    chunk_size: int
+
+
+def _dist() -> bool:
+    return dist.is_available() and dist.is_initialized()
+
+
+def _world_size(group) -> int:
+    return int(dist.get_world_size(group=group)) if (group is not None and _dist()) else 1
+
+
+def _group_rank(group) -> int:
+    return int(dist.get_rank(group=group)) if (group is not None and _dist()) else 0
+
+
+def _dist_rank() -> int:
+    return int(dist.get_rank()) if _dist() else 0
+
+
+def _resolve_dtype_alias(alias: str) -> torch.dtype:
+    m = {"fp32": torch.float32, "bf16": torch.bfloat16, "fp16": torch.float16}
+    if alias not in m:
+        raise ValueError(f"Unsupported optimizer dtype alias: {alias}")
+    return m[alias]
+
+
+def _compute_shard(numel: int, rank: int, size: int) -> tuple[int, int, int]:
+    chunk = -(-numel // size)
+    start = min(rank * chunk, numel)
+    end = min(start + chunk, numel)
+    return start, end, chunk
+
+
+class _Domain:
+    """All parameters of one sharding domain (dense/DP or expert/EDP) as flat buffers.
+
+    Rank-major layout of size g * S, S = sum_p chunk_p: the block of rank r
+    holds [p0 chunk r | p1 chunk r | ...]; slot s of parameter p inside a block
+    starts at off_p. ``perm[i]`` is the natural flat index (into the padded
+    concatenation of all parameters) of rank-major element i, or -1 for
+    padding past the end of a parameter.
+    """
+
+    def __init__(self, items, group, device, dtypes):
+        self.items = items  # list of (name, param, meta)
+        self.group = group
+        self.g = _world_size(group)
+        self.r = _group_rank(group)
+        self.offs = []
+        S = 0
+        for _, _, m in items:
+            self.offs.append(S)
+            S += m.chunk_size
+        self.S = S
+        self.nat_offs = []
+        n = 0
+        for _, p, _ in items:
+            self.nat_offs.append(n)
+            n += p.numel()
+        self.N = n
+        perm = torch.full((self.g * S,), -1, dtype=torch.int64)
+        for (name, p, m), off, noff in zip(items, self.offs, self.nat_offs):
+            for rr in range(self.g):
+                s, e, _ = _compute_shard(m.numel, rr, self.g)
+                if e > s:
+                    perm[rr * S + off: rr * S + off + (e - s)] = torch.arange(noff + s, noff + e)
+        self.valid = (perm >= 0).to(device)
+        self.perm = perm.clamp_min(0).to(device)
+        self.inv_index = perm[perm >= 0].to(device)           # natural positions
+        self.inv_src = torch.nonzero(perm >= 0).flatten().to(device)  # rank-major positions
+        mp_dt, ea_dt, es_dt = dtypes
+        self.master = torch.zeros(S, dtype=mp_dt, device=device)
+        self.exp_avg = torch.zeros(S, dtype=ea_dt, device=device)
+        self.exp_avg_sq = torch.zeros(S, dtype=es_dt, device=device)
+        with torch.no_grad():
+            nat = self.natural_params(device, mp_dt)
+            self.master.copy_(self.to_rank_major(nat)[self.r * S:(self.r + 1) * S])
+
+    def natural_params(self, device, dtype) -> torch.Tensor:
+        return torch.cat([p.detach().reshape(-1).to(device=device, dtype=dtype) for _, p, _ in self.items]) \
+            if self.items else torch.zeros(0, dtype=dtype, device=device)
+
+    def natural_grads(self, device, dtype) -> torch.Tensor:
+        parts = []
+        for _, p, _ in self.items:
+            g = getattr(p, "main_grad", None)
+            if g is None:
+                g = p.grad
+            parts.append(torch.zeros(p.numel(), dtype=dtype, device=device) if g is None
+                         else g.detach().reshape(-1).to(device=device, dtype=dtype))
+        return torch.cat(parts) if parts else torch.zeros(0, dtype=dtype, device=device)
+
+    def to_rank_major(self, nat: torch.Tensor) -> torch.Tensor:
+        return torch.where(self.valid, nat[self.perm], torch.zeros((), dtype=nat.dtype, device=nat.device))
+
+    def scatter_natural(self, rank_major: torch.Tensor) -> torch.Tensor:
+        out = torch.empty(self.N, dtype=rank_major.dtype, device=rank_major.device)
+        out[self.inv_index] = rank_major[self.inv_src]
+        return out
+
+    def local_view(self, buf: torch.Tensor, idx: int) -> torch.Tensor:
+        _, _, m = self.items[idx]
+        n = max(0, m.shard_end - m.shard_start)
+        return buf[self.offs[idx]: self.offs[idx] + n]
+
+
+class MegatronZeroOptimizer:
+    """ZeRO-1/2 AdamW over DP (dense) and EDP (expert) domains."""
+
+    def __init__(self, model: nn.Module, config: DistributedOptimizerConfig, data_parallel_group,
+                 expert_data_parallel_group, expert_param_ids: Set[int]) -> None:
+        if not config.use_distributed_optimizer:
+            raise ValueError("MegatronZeroOptimizer requires use_distributed_optimizer=True")
+        if config.data_parallel_sharding_strategy not in ("optim", "optim_grads"):
+            raise ValueError("MegatronZeroOptimizer supports only sharded strategies: 'optim' or 'optim_grads'")
+        if config.num_distributed_optimizer_instances != 1:
+            raise ValueError("v1 supports only num_distributed_optimizer_instances=1")
+        if config.learning_rate <= 0:
+            raise ValueError("learning_rate must be positive")
+        if config.weight_decay < 0:
+            raise ValueError("weight_decay must be non-negative")
+        if config.debug_max_steps < 1:
+            raise ValueError("debug_max_steps must be >= 1")
+        if config.debug_max_params < 1:
+            raise ValueError("debug_max_params must be >= 1")
+        for a in (config.main_params_dtype, config.main_grads_dtype, config.exp_avg_dtype, config.exp_avg_sq_dtype):
+            _resolve_dtype_alias(a)
+        self.model = model
+        self.config = config
+        self.data_parallel_group = data_parallel_group
+        self.expert_data_parallel_group = expert_data_parallel_group
+        self.expert_param_ids = set(expert_param_ids)
+        self._reduce_scatter_fallback = False
+        self._main_params_dtype = _resolve_dtype_alias(config.main_params_dtype)
+        self._main_grads_dtype = _resolve_dtype_alias(config.main_grads_dtype)
+        self._exp_avg_dtype = _resolve_dtype_alias(config.exp_avg_dtype)
+        self._exp_avg_sq_dtype = _resolve_dtype_alias(config.exp_avg_sq_dtype)
+        self._named_params = [(n, p) for n, p in model.named_parameters() if p.requires_grad]
+        self._params = [p for _, p in self._named_params]
+        self._meta_by_param: Dict[int, _ShardMeta] = {}
+        self._meta_by_name: Dict[str, _ShardMeta] = {}
+        self.param_groups = [{"params": self._params, "lr": config.learning_rate, "weight_decay": config.weight_decay,
+                              "betas": config.betas, "eps": config.eps}]
+        self.state: Dict[nn.Parameter, dict] = {}
+        self._global_step = 0
+        self._debug_steps = 0
+        self._initialize_states()
+
+    # ------------------------------------------------------------------ init
+    def _initialize_states(self) -> None:
+        dense, expert = [], []
+        for name, p in self._named_params:
+            is_expert = id(p) in self.expert_param_ids
+            group = self.expert_data_parallel_group if is_expert else self.data_parallel_group
+            gs, gr = _world_size(group), _group_rank(group)
+            s, e, chunk = _compute_shard(int(p.numel()), gr, gs)
+            m = _ShardMeta(name=name, numel=int(p.numel()), shape=tuple(p.shape), dtype=str(p.dtype),
+                           is_expert_param=is_expert, group_size=gs, group_rank=gr, shard_start=s, shard_end=e,
+                           chunk_size=chunk)
+            self._meta_by_param[id(p)] = m
+            self._meta_by_name[name] = m
+            (expert if is_expert else dense).append((name, p, m))
+        device = self._params[0].device if self._params else torch.device("cpu")
+        dts = (self._main_params_dtype, self._exp_avg_dtype, self._exp_avg_sq_dtype)
+        self._domains = []
+        for items, group in ((dense, self.data_parallel_group), (expert, self.expert_data_parallel_group)):
+            if items:
+                self._domains.append(_Domain(items, group, device, dts))
+        for d in self._domains:
+            for i, (name, p, m) in enumerate(d.items):
+                self.state[p] = {"step": 0, "master_param": d.local_view(d.master, i),
+                                 "exp_avg": d.local_view(d.exp_avg, i), "exp_avg_sq": d.local_view(d.exp_avg_sq, i)}
+        if self.config.debug:
+            self._log_debug_initial_state()
+
+    def _log_debug_initial_state(self) -> None:
+        for i, (name, p) in enumerate(self._named_params[: self.config.debug_max_params]):
+            m = self._meta_by_param[id(p)]
+            LOGGER.info("[ZeRO Debug][rank=%d] param[%d] name=%s domain=%s numel=%d shard=[%d:%d) group_size=%d "
+                        "group_rank=%d", _dist_rank(), i, name, "EDP(expert)" if m.is_expert_param else "DP(dense)",
+                        m.numel, m.shard_start, m.shard_end, m.group_size, m.group_rank)
+
+    def _strategy(self) -> str:
+        return self.config.data_parallel_sharding_strategy
+
+    # ------------------------------------------------------------------ step
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        for p in self._params:
+            if p.grad is not None:
+                if set_to_none:
+                    p.grad = None
+                else:
+                    p.grad.zero_()
+            mg = getattr(p, "main_grad", None)
+            if mg is not None:
+                mg.zero_()
+
+    def _reduce(self, d: _Domain, rm_grad: torch.Tensor) -> torch.Tensor:
+        """Returns this rank's summed-and-averaged gradient shard [S]."""
+        S, g = d.S, d.g
+        if g == 1:
+            return rm_grad
+        if self._strategy() == "optim_grads" and self.config.use_reduce_scatter and not self._reduce_scatter_fallback:
+            try:
+                out = torch.empty(S, dtype=rm_grad.dtype, device=rm_grad.device)
+                dist.reduce_scatter_tensor(out, rm_grad, group=d.group)
+                return out.div_(g)
+            except Exception:  # sticky fallback, as in the reference
+                self._reduce_scatter_fallback = True
+        dist.all_reduce(rm_grad, group=d.group)
+        return rm_grad[d.r * S:(d.r + 1) * S].div_(g)
+
+    @torch.no_grad()
+    def step_with_ready_grads(self) -> bool:
+        lr = float(self.param_groups[0]["lr"])
+        b1, b2 = (float(x) for x in self.param_groups[0]["betas"])
+        eps = float(self.param_groups[0]["eps"])
+        wd = float(self.param_groups[0]["weight_decay"])
+        self._global_step += 1
+        for d in self._domains:
+            dev = d.master.device
+            nat = d.natural_grads(dev, self._main_grads_dtype)
+            shard_g = self._reduce(d, d.to_rank_major(nat))
+            step = None
+            for _, p, _ in d.items:
+                self.state[p]["step"] = int(self.state[p]["step"]) + 1
+                step = self.state[p]["step"]
+            if all(t.dtype == torch.float32 for t in (d.master, d.exp_avg, d.exp_avg_sq)) and d.S > 0:
+                ops.adamw_flat_(d.master, d.exp_avg, d.exp_avg_sq, shard_g.float().contiguous(), lr=lr, beta1=b1,
+                                beta2=b2, eps=eps, weight_decay=wd, step=step)
+            elif d.S > 0:
+                m, v, w = d.exp_avg.float(), d.exp_avg_sq.float(), d.master.float()
+                ops.adamw_flat_(w, m, v, shard_g.float(), lr=lr, beta1=b1, beta2=b2, eps=eps, weight_decay=wd,
+                                step=step)
+                d.master.copy_(w)
+                d.exp_avg.copy_(m)
+                d.exp_avg_sq.copy_(v)
+            full = torch.empty(d.g * d.S, dtype=d.master.dtype, device=dev)
+            if d.g > 1:
+                dist.all_gather_into_tensor(full, d.master.contiguous(), group=d.group)
+            else:
+                full.copy_(d.master)
+            nat_p = d.scatter_natural(full)
+            for (_, p, _), noff in zip(d.items, d.nat_offs):
+                p.data.copy_(nat_p[noff: noff + p.numel()].view_as(p).to(p.dtype))
+        if self.config.debug and self._debug_steps < self.config.debug_max_steps:
+            self._debug_steps += 1
+            LOGGER.info("[ZeRO Debug][rank=%d] step=%d strategy=%s rs_fallback=%s", _dist_rank(), self._global_step,
+                        self._strategy(), self._reduce_scatter_fallback)
+        return True
+
+    def step(self) -> bool:
+        return self.step_with_ready_grads()
+
+    # ------------------------------------------------------------------ checkpoint format v2
+    def _recipe(self) -> dict:
+        c = self.config
+        return {"name": c.precision_recipe_name, "fp8_rounding": c.fp8_rounding,
+                "fp8_activation_quant_granularity": c.fp8_activation_quant_granularity,
+                "fp8_weight_quant_granularity": c.fp8_weight_quant_granularity,
+                "fp8_comm_quant_enabled": c.fp8_comm_quant_enabled,
+                "fp8_comm_quant_granularity": c.fp8_comm_quant_granularity}
+
+    def _dtypes(self) -> dict:
+        c = self.config
+        return {"main_params_dtype": c.main_params_dtype, "main_grads_dtype": c.main_grads_dtype,
+                "exp_avg_dtype": c.exp_avg_dtype, "exp_avg_sq_dtype": c.exp_avg_sq_dtype}
+
+    def _param_signature_items(self) -> list[dict]:
+        return [{"name": n, "shape": list(p.shape), "dtype": str(p.dtype),
+                 "is_expert_param": self._meta_by_name[n].is_expert_param} for n, p in self._named_params]
+
+    def parameter_signature_hash(self) -> str:
+        payload = json.dumps(self._param_signature_items(), sort_keys=True).encode("utf-8")
+        return hashlib.sha256(payload).hexdigest()
+
+    def state_dict(self) -> dict:
+        return {"format_version": ZERO_CHECKPOINT_FORMAT_VERSION, "global_step": self._global_step,
+                "config": asdict(self.config), "precision_recipe": self._recipe(),
+                "param_groups": [{"lr": float(g["lr"]), "weight_decay": float(g["weight_decay"]),
+                                  "betas": tuple(g["betas"]), "eps": float(g["eps"])} for g in self.param_groups],
+                "parameter_signature_hash": self.parameter_signature_hash(),
+                "parameter_signature_items": self._param_signature_items()}
+
+    def load_state_dict(self, state: dict) -> None:
+        fv = int(state.get("format_version", -1))
+        if fv != ZERO_CHECKPOINT_FORMAT_VERSION:
+            raise ValueError(f"Unsupported ZeRO nonparam checkpoint format version: {fv}. "
+                             f"Expected {ZERO_CHECKPOINT_FORMAT_VERSION}.")
+        rec = state.get("precision_recipe")
+        if rec is not None and rec != self._recipe():
+            raise ValueError("ZeRO precision recipe metadata mismatch between checkpoint and optimizer config")
+        self._global_step = int(state.get("global_step", 0))
+        for cur, loaded in zip(self.param_groups, state.get("param_groups", []) or []):
+            cur["lr"] = float(loaded.get("lr", cur["lr"]))
+            cur["weight_decay"] = float(loaded.get("weight_decay", cur["weight_decay"]))
+            cur["betas"] = tuple(loaded.get("betas", cur["betas"]))
+            cur["eps"] = float(loaded.get("eps", cur["eps"]))
+
+    def get_parameter_state_dp_zero(self, include_tensors: bool = True) -> dict:
+        payload = {"format_version": ZERO_CHECKPOINT_FORMAT_VERSION, "global_step": self._global_step,
+                   "strategy": self._strategy(), "parameter_signature_hash": self.parameter_signature_hash(),
+                   "precision_recipe": self._recipe(), "optimizer_state_dtypes": self._dtypes(), "parameters": {}}
+        for name, p in self._named_params:
+            m = self._meta_by_name[name]
+            st = self.state[p]
+            rec = {"name": name, "shape": list(m.shape), "dtype": m.dtype, "numel": m.numel,
+                   "is_expert_param": m.is_expert_param, "group_size": m.group_size, "group_rank": m.group_rank,
+                   "shard_start": m.shard_start, "shard_end": m.shard_end, "chunk_size": m.chunk_size,
+                   "step": int(st["step"])}
+            if include_tensors:
+                for k in ("master_param", "exp_avg", "exp_avg_sq"):
+                    rec[k] = st[k].detach().cpu().clone()
+            payload["parameters"][name] = rec
+        return payload
+
+    def load_parameter_state_from_dp_zero(self, state_dict: dict, strict: bool = True) -> None:
+        fv = int(state_dict.get("format_version", -1))
+        if fv != ZERO_CHECKPOINT_FORMAT_VERSION:
+            raise ValueError(f"Unsupported ZeRO shard checkpoint format version: {fv}. "
+                             f"Expected {ZERO_CHECKPOINT_FORMAT_VERSION}.")
+        rec = state_dict.get("precision_recipe")
+        if rec is not None and rec != self._recipe():
+            raise ValueError("ZeRO shard precision recipe metadata mismatch between checkpoint and optimizer config")
+        exp, found = self.parameter_signature_hash(), state_dict.get("parameter_signature_hash")
+        if found != exp:
+            raise ValueError(f"Optimizer parameter signature mismatch. expected={exp}, found={found}")
+        params = state_dict.get("parameters")
+        if not isinstance(params, dict):
+            raise ValueError("Invalid parameter state payload: missing 'parameters' dict")
+        missing = []
+        for name, p in self._named_params:
+            r = params.get(name)
+            if r is None:
+                missing.append(name)
+                continue
+            st = self.state[p]
+            n = st["master_param"].numel()
+            for k in ("master_param", "exp_avg", "exp_avg_sq"):
+                t = r.get(k)
+                if not torch.is_tensor(t):
+                    raise ValueError(f"Missing tensor '{k}' for parameter '{name}'")
+                if t.numel() != n:
+                    raise ValueError(f"Shard shape mismatch for {name}:{k} (expected {n}, got {t.numel()})")
+                st[k].copy_(t.to(device=st[k].device, dtype=st[k].dtype).view_as(st[k]))
+            st["step"] = int(r.get("step", st["step"]))
+        if strict and missing:
+            raise ValueError(f"Missing parameter shards in optimizer state: {missing[:5]}")
+
+    def save_parameter_state(self, checkpoint_dir: str, rank: int, world_size: int) -> None:
+        if world_size < 1:
+            raise ValueError("world_size must be >= 1")
+        os.makedirs(checkpoint_dir, exist_ok=True)
+        payload = self.get_parameter_state_dp_zero(include_tensors=True)
+        payload["rank"] = rank
+        payload["world_size"] = world_size
+        torch.save(payload, os.path.join(checkpoint_dir, f"optimizer_shard_rank{rank}.pt"))
+
+    def load_parameter_state(self, checkpoint_dir: str, rank: int, world_size: int) -> None:
+        path = os.path.join(checkpoint_dir, f"optimizer_shard_rank{rank}.pt")
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"Missing optimizer shard file: {path}")
+        payload = torch.load(path, map_location="cpu", weights_only=False)
+        sws = int(payload.get("world_size", world_size))
+        if sws != world_size:
+            raise ValueError(f"Checkpoint world_size mismatch for optimizer shard: {sws} vs {world_size}")
+        self.load_parameter_state_from_dp_zero(payload, strict=True)
+
+    def build_checkpoint_manifest(self, rank: int, world_size: int) -> dict:
+        return {"format_version": ZERO_CHECKPOINT_FORMAT_VERSION, "optimizer_type": "MegatronZeroOptimizer",
+                "rank": rank, "world_size": world_size, "strategy": self._strategy(),
+                "num_distributed_optimizer_instances": self.config.num_distributed_optimizer_instances,
+                "parameter_signature_hash": self.parameter_signature_hash(), "precision_recipe": self._recipe(),
+                "optimizer_state_dtypes": self._dtypes(),
+                "files": {"nonparam": "optimizer_nonparam.pt", "shard": f"optimizer_shard_rank{rank}.pt"}}
+
+    # Convenience: whole v2 checkpoint of this rank in one directory.
+    def save_checkpoint_files(self, checkpoint_dir: str) -> None:
+        rank = _dist_rank()
+        world = dist.get_world_size() if _dist() else 1
+        os.makedirs(checkpoint_dir, exist_ok=True)
+        if rank == 0:
+            torch.save(self.state_dict(), os.path.join(checkpoint_dir, "optimizer_nonparam.pt"))
+        self.save_parameter_state(checkpoint_dir, rank, world)
+        with open(os.path.join(checkpoint_dir, f"optimizer_manifest_rank{rank}.json" if rank else
+                               "optimizer_manifest.json"), "w") as f:
+            json.dump(self.build_checkpoint_manifest(rank, world), f, indent=2, sort_keys=True)
+
+    def load_checkpoint_files(self, checkpoint_dir: str) -> None:
+        rank = _dist_rank()
+        world = dist.get_world_size() if _dist() else 1
+        self.load_state_dict(torch.load(os.path.join(checkpoint_dir, "optimizer_nonparam.pt"), map_location="cpu",
+                                        weights_only=False))
+        self.load_parameter_state(checkpoint_dir, rank, world)
+        # Re-materialise the full parameters from the restored shards.
+        with torch.no_grad():
+            for d in self._domains:
+                full = torch.empty(d.g * d.S, dtype=d.master.dtype, device=d.master.device)
+                if d.g > 1:
+                    dist.all_gather_into_tensor(full, d.master.contiguous(), group=d.group)
+                else:
+                    full.copy_(d.master)
+                nat = d.scatter_natural(full)
+                for (_, p, _), noff in zip(d.items, d.nat_offs):
+                    p.data.copy_(nat[noff: noff + p.numel()].view_as(p).to(p.dtype))
+
+
+def is_zero_optimizer(optimizer: object) -> bool:
+    return all(hasattr(optimizer, a) for a in ("step_with_ready_grads", "save_parameter_state", "load_parameter_state"))

@@ -31,15 +31,15 @@ def clear_communicators() -> None:
     _COMMUNICATORS.clear()
 
 
-def all_gather_gemm(x_shard: torch.Tensor, weight: torch.Tensor, group, bias=None):
-    """Returns (AG(x_shard) . W^T (+ bias), AG(x_shard))."""
+def all_gather_gemm(x_shard: torch.Tensor, weight: torch.Tensor, group, bias=None, *, b_mn: bool = False):
+    """Returns (AG(x_shard) . op(W)^T (+ bias), AG(x_shard)); op(W) = W^T when b_mn (dgrad form)."""
     if comm.group_size(group) == 1:
-        return gemm(x_shard, weight, bias=bias), x_shard
+        return gemm(x_shard, weight, bias=bias, b_mn=b_mn), x_shard
     c = get_communicator(group)
     if c is not None and c.supports(x_shard, weight):
-        return c.all_gather_gemm(x_shard, weight, bias)
+        return c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn)
     x_full = comm.all_gather_dim0(x_shard, group)
-    return gemm(x_full, weight, bias=bias), x_full
+    return gemm(x_full, weight, bias=bias, b_mn=b_mn), x_full
 
 
 def gemm_reduce_scatter(x: torch.Tensor, weight: torch.Tensor, group, *, b_mn: bool = False):

@@ -1,11 +1,171 @@
-"""Symmetric-memory communicator attachment for fused TP kernels.
+"""Symmetric-memory communicator for the fused tensor-parallel kernels.
 
-``maybe_attach_communicator(group)`` registers a peer-memory communicator on
-a process group when every rank of the group is a GPU of this node with
-peer access; until then the fused paths fall back to NCCL + GEMM.
+Each rank of a tensor-parallel group allocates one device buffer of the same
+layout (``cudaMalloc`` + CUDA IPC handle, exchanged once through the process
+group) and opens every peer's buffer, so the fused kernels address peer
+memory directly over NVLink:
+
+    [0, 4 KiB)          control words: AG ready epoch (u64 @0),
+                        RS arrival counters: parity 0 pair (u32 x2 @64),
+                        parity 1 pair (u32 x2 @128)
+    AG slots  x2        this rank's activation shard [T_local, K] per epoch parity
+    RS recv   x2        partial tiles from every source rank [n][T_local][N]
+
+Only this rank's own buffer is ever viewed as a torch tensor; peer pointers
+are handed to the fused kernels only.
 """
 from __future__ import annotations
 
+import os
 
-def maybe_attach_communicator(group):
-    return None
+import torch
+import torch.distributed as dist
+
+from ..ops._ext import ext
+from . import comm
+from .fused import register_communicator
+
+_CTRL = 4096
+
+
+class TPCommunicator:
+    def __init__(self, group, *, max_local_rows: int, max_k: int, max_rs_n: int, device=None):
+        self.group = group
+        self.n = comm.group_size(group)
+        self.rank = comm.group_rank(group)
+        if self.n > 8:
+            raise ValueError("TPCommunicator supports up to 8 ranks (one node)")
+        self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self.max_local_rows = max_local_rows
+        self.max_k = max_k
+        self.max_rs_n = max_rs_n
+        self.ag_slot_bytes = max_local_rows * max_k * 2
+        self.rs_slot_bytes = self.n * max_local_rows * max_rs_n * 2
+        self.ag_off = _CTRL
+        self.rs_off = self.ag_off + 2 * self.ag_slot_bytes
+        total = self.rs_off + 2 * self.rs_slot_bytes
+        C = ext()
+        self.local_ptr, handle = C.symm_alloc(total)
+        handles = [None] * self.n
+        dist.all_gather_object(handles, handle, group=group)
+        self.ptrs = []
+        self._opened = []
+        for i, h in enumerate(handles):
+            if i == self.rank:
+                self.ptrs.append(self.local_ptr)
+            else:
+                p = C.symm_open(h)
+                self.ptrs.append(p)
+                self._opened.append(p)
+        self.chunk_flags = torch.zeros(self.n, dtype=torch.int32, device=self.device)
+        self.tile_ctr = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.copy_ctas = int(os.environ.get("NTB_AG_COPY_CTAS", "8"))
+        self.ag_epoch = 0
+        self.rs_epoch = 0
+        self.closed = False
+        dist.barrier(group=group)
+
+    # ------------------------------------------------------------------ layout helpers
+    def _ready_ptrs(self):
+        return [p + 0 for p in self.ptrs]
+
+    def _ag_slot_ptrs(self, parity: int):
+        return [p + self.ag_off + parity * self.ag_slot_bytes for p in self.ptrs]
+
+    def _rs_recv_ptrs(self, parity: int):
+        return [p + self.rs_off + parity * self.rs_slot_bytes for p in self.ptrs]
+
+    def _rs_counter_ptrs(self, parity: int):
+        return [p + 64 + 64 * parity for p in self.ptrs]
+
+    def supports(self, x: torch.Tensor, w: torch.Tensor) -> bool:
+        return (not self.closed and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+                and x.dim() == 2 and x.shape[-1] % 8 == 0)
+
+    # ------------------------------------------------------------------ fused ops
+    def all_gather_gemm(self, x_shard: torch.Tensor, weight: torch.Tensor, bias=None, b_mn: bool = False):
+        T_local, K = x_shard.shape
+        N = weight.shape[1] if b_mn else weight.shape[0]
+        if T_local > self.max_local_rows or K > self.max_k or T_local % 128 != 0:
+            return None
+        self.ag_epoch += 1
+        parity = self.ag_epoch & 1
+        x_shard = x_shard.contiguous()
+        full = torch.empty(self.n * T_local, K, dtype=torch.bfloat16, device=x_shard.device)
+        y = torch.empty(self.n * T_local, N, dtype=torch.bfloat16, device=x_shard.device)
+        ext().ag_gemm(x_shard, full, weight, y, bias, b_mn, self._ag_slot_ptrs(parity), self._ready_ptrs(),
+                      self.chunk_flags, self.tile_ctr, self.rank, self.ag_epoch, self.copy_ctas)
+        return y, full
+
+    def gemm_reduce_scatter(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False, bias=None):
+        T, K = x.shape
+        N = weight.shape[1] if b_mn else weight.shape[0]
+        T_local = T // self.n
+        if T % self.n or T_local > self.max_local_rows or N > self.max_rs_n or T_local % 128 != 0:
+            return None
+        self.rs_epoch += 1
+        parity = self.rs_epoch & 1
+        out = torch.empty(T_local, N, dtype=torch.bfloat16, device=x.device)
+        ext().gemm_rs(x, weight, out, bias, b_mn, self._rs_recv_ptrs(parity), self._rs_counter_ptrs(parity),
+                      self.tile_ctr, self.rank, self.rs_epoch)
+        return out
+
+    def close(self):
+        if self.closed:
+            return
+        self.closed = True
+        torch.cuda.synchronize()
+        C = ext()
+        for p in self._opened:
+            C.symm_close(p)
+        C.symm_free(self.local_ptr)
+
+
+class _FusedAdapter:
+    """Adapts TPCommunicator to the fused-dispatch interface (falls back when a shape is out of range)."""
+
+    def __init__(self, c: TPCommunicator):
+        self.c = c
+
+    def supports(self, x, w):
+        return self.c.supports(x, w)
+
+    def all_gather_gemm(self, x_shard, weight, bias, b_mn=False):
+        r = self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn)
+        if r is None:
+            from ..ops.linear import gemm
+
+            full = comm.all_gather_dim0(x_shard, self.c.group)
+            return gemm(full, weight, bias=bias, b_mn=b_mn), full
+        return r
+
+    def gemm_reduce_scatter(self, x, weight, b_mn=False):
+        r = self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn)
+        if r is None:
+            from ..ops.linear import gemm
+
+            return comm.reduce_scatter_dim0(gemm(x, weight, b_mn=b_mn), self.c.group)
+        return r
+
+    def all_gather(self, x_shard):
+        return comm.all_gather_dim0(x_shard, self.c.group)
+
+    def close(self):
+        self.c.close()
+
+
+def maybe_attach_communicator(group, *, max_local_rows: int = 4096, max_k: int = 4096, max_rs_n: int = 4096):
+    """Register a fused-kernel communicator on a single-node NCCL group of CUDA ranks.
+
+    Disabled with NTB_FUSED_TP=0 (the NCCL + GEMM baseline then runs).
+    """
+    if os.environ.get("NTB_FUSED_TP", "1") == "0":
+        return None
+    if not (torch.cuda.is_available() and dist.is_initialized() and comm.group_size(group) > 1):
+        return None
+    if dist.get_backend(group) != "nccl":
+        return None
+    c = TPCommunicator(group, max_local_rows=max_local_rows, max_k=max_k, max_rs_n=max_rs_n)
+    a = _FusedAdapter(c)
+    register_communicator(group, a)
+    return a

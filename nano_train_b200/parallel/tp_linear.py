@@ -18,7 +18,7 @@ from __future__ import annotations
 
 import torch
 
-from ..ops.linear import accumulate_weight_grad, gemm
+from ..ops.linear import accumulate_weight_grad
 from . import comm
 from . import fused
 
@@ -69,8 +69,11 @@ class RowParallelSPFn(torch.autograd.Function):
     def backward(ctx, gy):
         x2, weight = ctx.saved_tensors
         g_shard = _flat(gy)
-        g_full = comm.all_gather_dim0(g_shard, ctx.group)
-        dx = gemm(g_full, weight, b_mn=True).view(ctx.in_shape) if ctx.needs_input_grad[0] else None
+        if ctx.needs_input_grad[0]:
+            dx, g_full = fused.all_gather_gemm(g_shard, weight, ctx.group, b_mn=True)
+            dx = dx.view(ctx.in_shape)
+        else:
+            dx, g_full = None, comm.all_gather_dim0(g_shard, ctx.group)
         dw = accumulate_weight_grad(weight, g_full, x2) if ctx.needs_input_grad[1] else None
         db = g_shard.float().sum(0).to(gy.dtype) if (ctx.has_bias and ctx.needs_input_grad[2]) else None
         return dx, dw, db, None
