@@ -60,11 +60,41 @@ def timeit(fn, iters, warm=3):
     return float(t.item())
 
 
+EVENTS = ["start", "copy_done", "first_tile", "first_remote_ready", "producer_done", "last_store",
+          "reduce_wait_done", "end"]
+
+
+def trace_report(c, fn, name, rank, n):
+    """Runs fn once with per-CTA globaltimer stamps; prints min/median/max (us since the earliest start)."""
+    sms = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    c.trace = torch.zeros(sms, 8, dtype=torch.int64, device="cuda")
+    torch.cuda.synchronize()
+    dist.barrier()
+    fn()
+    torch.cuda.synchronize()
+    tr = c.trace.cpu()
+    c.trace = None
+    t0 = int(tr[:, 0][tr[:, 0] > 0].min())
+    out = {"op": name, "rank": rank}
+    for e, ev in enumerate(EVENTS):
+        col = tr[:, e]
+        col = col[col > 0]
+        if col.numel() == 0:
+            continue
+        us = (col - t0).double() / 1e3
+        out[ev] = [round(float(us.min()), 1), round(float(us.median()), 1), round(float(us.max()), 1)]
+    for r in range(n):
+        dist.barrier()
+        if r == rank:
+            print("TRACE", json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--seq", type=int, default=4096)
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--trace", action="store_true", help="print per-CTA timeline of one fused call per op")
     args = ap.parse_args()
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
@@ -106,7 +136,16 @@ def main():
             alone = lambda: gemm(x, w, b_mn=b_mn)
             flops = 2.0 * T * N * K
             nvl_bytes = (n - 1) * Tl * N * 2
+        fused()
+        torch.cuda.synchronize()
+        st0 = ext().read_and_clear_status(local)
         tf = timeit(fused, args.iters)
+        torch.cuda.synchronize()
+        st1 = ext().read_and_clear_status(local)
+        if st0 or st1:
+            print(f"rank {rank} op {name}: kernel status after first call {st0}, after timing {st1}", flush=True)
+        if args.trace:
+            trace_report(c, fused, name, rank, n)
         tn = timeit(nccl, args.iters)
         ta = timeit(alone, args.iters)
         roof = max(flops / (peak * 1e12), nvl_bytes / (NVLINK_GBS * 1e9)) * 1e3

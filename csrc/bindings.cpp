@@ -66,10 +66,10 @@ at::Tensor fp8_dequantize(const at::Tensor& q, const at::Tensor& scales, int64_t
 // tp_fused.cu
 void ag_gemm(const at::Tensor& x_local, at::Tensor& x_full_out, const at::Tensor& w, at::Tensor& y,
              const c10::optional<at::Tensor>& bias, bool b_mn, std::vector<int64_t> slots, std::vector<int64_t> ready,
-             at::Tensor& chunk_flags, at::Tensor& tile_ctr, int64_t rank, int64_t epoch, int64_t copy_ctas);
+             at::Tensor& ctrs, int64_t rank, int64_t epoch, const c10::optional<at::Tensor>& trace);
 void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
-             bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> counters, at::Tensor& tile_ctr, int64_t rank,
-             int64_t epoch);
+             bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> tctrs, at::Tensor& ctrs, int64_t rank,
+             int64_t epoch, const c10::optional<at::Tensor>& trace);
 // symm.cpp
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t bytes);
 int64_t symm_open(py::bytes handle);
@@ -107,8 +107,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize", &ntb::fp8_quantize);
   m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
   m.def("fp8_dequantize", &ntb::fp8_dequantize);
-  m.def("ag_gemm", &ntb::ag_gemm);
-  m.def("gemm_rs", &ntb::gemm_rs);
+  m.def("ag_gemm", &ntb::ag_gemm, py::arg("x_local"), py::arg("x_full_out"), py::arg("w"), py::arg("y"),
+        py::arg("bias"), py::arg("b_mn"), py::arg("slots"), py::arg("ready"), py::arg("ctrs"), py::arg("rank"),
+        py::arg("epoch"), py::arg("trace") = py::none());
+  m.def("gemm_rs", &ntb::gemm_rs, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("b_mn"),
+        py::arg("recv"), py::arg("tctrs"), py::arg("ctrs"), py::arg("rank"), py::arg("epoch"),
+        py::arg("trace") = py::none());
   m.def("symm_alloc", &ntb::symm_alloc);
   m.def("symm_open", &ntb::symm_open);
   m.def("symm_close", &ntb::symm_close);

@@ -5,9 +5,9 @@ layout (``cudaMalloc`` + CUDA IPC handle, exchanged once through the process
 group) and opens every peer's buffer, so the fused kernels address peer
 memory directly over NVLink:
 
-    [0, 4 KiB)          control words: AG ready epoch (u64 @0),
-                        RS arrival counters: parity 0 pair (u32 x2 @64),
-                        parity 1 pair (u32 x2 @128)
+    [0, 4 KiB)          control words: AG ready epoch (u64 @0)
+    RS tile counters x2 per-tile arrival counters (u32, one per 128 x 128 output
+                        tile of this rank's chunk) per epoch parity; zero at rest
     AG slots  x2        this rank's activation shard [T_local, K] per epoch parity
     RS recv   x2        partial tiles from every source rank [n][T_local][N]
 
@@ -41,7 +41,10 @@ class TPCommunicator:
         self.max_rs_n = max_rs_n
         self.ag_slot_bytes = max_local_rows * max_k * 2
         self.rs_slot_bytes = self.n * max_local_rows * max_rs_n * 2
-        self.ag_off = _CTRL
+        n_tiles = (max_local_rows // 128) * ((max_rs_n + 127) // 128)
+        self.tctr_bytes = (n_tiles * 4 + 4095) // 4096 * 4096
+        self.tctr_off = _CTRL
+        self.ag_off = self.tctr_off + 2 * self.tctr_bytes
         self.rs_off = self.ag_off + 2 * self.ag_slot_bytes
         total = self.rs_off + 2 * self.rs_slot_bytes
         C = ext()
@@ -57,12 +60,13 @@ class TPCommunicator:
                 p = C.symm_open(h)
                 self.ptrs.append(p)
                 self._opened.append(p)
-        self.chunk_flags = torch.zeros(self.n, dtype=torch.int32, device=self.device)
-        self.tile_ctr = torch.zeros(4, dtype=torch.int32, device=self.device)
-        self.copy_ctas = int(os.environ.get("NTB_AG_COPY_CTAS", "8"))
+        # Local scratch of the fused kernels (tile/piece counters, per-chunk copy counts); zeroed per call.
+        self.ctrs = torch.zeros(1 + self.n, dtype=torch.int64, device=self.device)
         self.ag_epoch = 0
         self.rs_epoch = 0
         self.closed = False
+        # Optional int64 [num_sms, 8] tensor: per-CTA %globaltimer stamps of the last fused call.
+        self.trace = None
         dist.barrier(group=group)
 
     # ------------------------------------------------------------------ layout helpers
@@ -75,8 +79,8 @@ class TPCommunicator:
     def _rs_recv_ptrs(self, parity: int):
         return [p + self.rs_off + parity * self.rs_slot_bytes for p in self.ptrs]
 
-    def _rs_counter_ptrs(self, parity: int):
-        return [p + 64 + 64 * parity for p in self.ptrs]
+    def _rs_tctr_ptrs(self, parity: int):
+        return [p + self.tctr_off + parity * self.tctr_bytes for p in self.ptrs]
 
     def supports(self, x: torch.Tensor, w: torch.Tensor) -> bool:
         return (not self.closed and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
@@ -94,7 +98,7 @@ class TPCommunicator:
         full = torch.empty(self.n * T_local, K, dtype=torch.bfloat16, device=x_shard.device)
         y = torch.empty(self.n * T_local, N, dtype=torch.bfloat16, device=x_shard.device)
         ext().ag_gemm(x_shard, full, weight, y, bias, b_mn, self._ag_slot_ptrs(parity), self._ready_ptrs(),
-                      self.chunk_flags, self.tile_ctr, self.rank, self.ag_epoch, self.copy_ctas)
+                      self.ctrs, self.rank, self.ag_epoch, trace=self.trace)
         return y, full
 
     def gemm_reduce_scatter(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False, bias=None):
@@ -106,8 +110,8 @@ class TPCommunicator:
         self.rs_epoch += 1
         parity = self.rs_epoch & 1
         out = torch.empty(T_local, N, dtype=torch.bfloat16, device=x.device)
-        ext().gemm_rs(x, weight, out, bias, b_mn, self._rs_recv_ptrs(parity), self._rs_counter_ptrs(parity),
-                      self.tile_ctr, self.rank, self.rs_epoch)
+        ext().gemm_rs(x, weight, out, bias, b_mn, self._rs_recv_ptrs(parity), self._rs_tctr_ptrs(parity),
+                      self.ctrs, self.rank, self.rs_epoch, trace=self.trace)
         return out
 
     def close(self):
