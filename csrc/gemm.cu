@@ -52,7 +52,9 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = 1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + 256 /*barriers*/;
+  static constexpr int STAGE_BYTES = 4 * 8192;  // epilogue staging: 32 rows x 64 fp32 per epilogue warp
+  static constexpr int SMEM_BYTES =
+      1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256 /*barriers*/;
 };
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
@@ -64,6 +66,96 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   const int r = tile - g * per_group;
   mb = first_m + r % gm;
   nb = r / gm;
+}
+
+// Epilogue of one warp's 32 accumulator rows (TMEM lanes) of a 128 x BN tile.
+// Each 64-column group is read from TMEM (the lane's row), scaled and biased in
+// fp32, staged through the warp's 8 KB of shared memory (16-byte chunks
+// XOR-swizzled by row) and written row-contiguously: a warp instruction stores
+// 4 rows x 128 B (bf16) or 2 rows x 256 B (fp32) instead of 32 scattered
+// 16-byte pieces. `accumulate` adds the previous C in fp32 before the single
+// final rounding. m0: first row of the warp; n0: first column of the tile.
+template <int BN>
+__device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, const GemmParams& p, long m0, int n0,
+                                              bool vec_ok) {
+  const int lane = threadIdx.x & 31;
+#pragma unroll 1
+  for (int g = 0; g < BN; g += 64) {
+    const int cg = n0 + g;
+    if (cg >= p.N) break;  // warp-uniform
+    uint32_t r0[32], r1[32];
+    tmem_ld32(t_row + g, r0);
+    tmem_ld32(t_row + g + 32, r1);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      float4 v;
+      float* w = &v.x;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = j * 4 + u;
+        const uint32_t bits = c < 32 ? r0[c] : r1[c - 32];
+        float x = __uint_as_float(bits) * p.alpha;
+        if (p.bias != nullptr && cg + c < p.N) x += __bfloat162float(p.bias[cg + c]);
+        w[u] = x;
+      }
+      *reinterpret_cast<float4*>(stage + lane * 64 + ((j ^ (lane & 15)) * 4)) = v;
+    }
+    __syncwarp();
+    if (p.c_f32) {
+      float* C = reinterpret_cast<float*>(p.C);
+#pragma unroll 4
+      for (int it = 0; it < 16; ++it) {
+        const int row = it * 2 + (lane >> 4), ch = lane & 15;
+        const long m = m0 + row;
+        const int col = cg + ch * 4;
+        if (m >= p.M || col >= p.N) continue;
+        float4 v = *reinterpret_cast<const float4*>(stage + row * 64 + ((ch ^ (row & 15)) * 4));
+        float* dst = C + m * p.ldc + col;
+        if (vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0) {
+          if (p.accumulate) {
+            const float4 old = *reinterpret_cast<const float4*>(dst);
+            v.x += old.x; v.y += old.y; v.z += old.z; v.w += old.w;
+          }
+          *reinterpret_cast<float4*>(dst) = v;
+        } else {
+          const float* vv = &v.x;
+          for (int u = 0; u < 4 && col + u < p.N; ++u) dst[u] = vv[u] + (p.accumulate ? dst[u] : 0.f);
+        }
+      }
+    } else {
+      __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
+#pragma unroll 4
+      for (int it = 0; it < 8; ++it) {
+        const int row = it * 4 + (lane >> 3), c8 = lane & 7;
+        const long m = m0 + row;
+        const int col = cg + c8 * 8;
+        if (m >= p.M || col >= p.N) continue;
+        const float4 a = *reinterpret_cast<const float4*>(stage + row * 64 + (((2 * c8) ^ (row & 15)) * 4));
+        const float4 b = *reinterpret_cast<const float4*>(stage + row * 64 + (((2 * c8 + 1) ^ (row & 15)) * 4));
+        float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+        __nv_bfloat16* dst = C + m * p.ldc + col;
+        if (vec_ok && col + 8 <= p.N) {
+          if (p.accumulate) {
+            const uint4 old = *reinterpret_cast<const uint4*>(dst);
+            v[0] += bf16_lo(old.x); v[1] += bf16_hi(old.x);
+            v[2] += bf16_lo(old.y); v[3] += bf16_hi(old.y);
+            v[4] += bf16_lo(old.z); v[5] += bf16_hi(old.z);
+            v[6] += bf16_lo(old.w); v[7] += bf16_hi(old.w);
+          }
+          uint4 o;
+          o.x = pack_bf16x2(v[0], v[1]);
+          o.y = pack_bf16x2(v[2], v[3]);
+          o.z = pack_bf16x2(v[4], v[5]);
+          o.w = pack_bf16x2(v[6], v[7]);
+          *reinterpret_cast<uint4*>(dst) = o;
+        } else {
+          for (int u = 0; u < 8 && col + u < p.N; ++u)
+            dst[u] = __float2bfloat16(v[u] + (p.accumulate ? __bfloat162float(dst[u]) : 0.f));
+        }
+      }
+    }
+    __syncwarp();
+  }
 }
 
 template <int BN, bool A_MN, bool B_MN>
@@ -79,7 +171,8 @@ __global__ void __launch_bounds__(192, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_BYTES;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * B_BYTES);
+  uint8_t* stage_base = sB + STAGES * B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_base + Cfg::STAGE_BYTES);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -211,71 +304,15 @@ __global__ void __launch_bounds__(192, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+    float* stage = reinterpret_cast<float*>(stage_base + q * 8192);
+    (void)row;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       int mb, nb;
       tile_coords(tile, num_m, num_n, mb, nb);
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
-      const long m = static_cast<long>(mb) * BM + row;
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-#pragma unroll 1
-      for (int c = 0; c < BN; c += 32) {
-        uint32_t r[32];
-        tmem_ld32(t_row + c, r);
-        tmem_wait_ld();
-        const int n0 = nb * BN + c;
-        if (m >= p.M || n0 >= p.N) continue;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]) * p.alpha;
-        if (p.bias) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j)
-            if (n0 + j < p.N) v[j] += __bfloat162float(p.bias[n0 + j]);
-        }
-        const bool full_chunk = vec_ok && (n0 + 32 <= p.N);
-        if (p.c_f32) {
-          float* crow = reinterpret_cast<float*>(p.C) + m * p.ldc + n0;
-          if (full_chunk) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 4) {
-              float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-              if (p.accumulate) {
-                const float4 old = *reinterpret_cast<const float4*>(crow + j);
-                o.x += old.x; o.y += old.y; o.z += old.z; o.w += old.w;
-              }
-              *reinterpret_cast<float4*>(crow + j) = o;
-            }
-          } else {
-            for (int j = 0; j < 32 && n0 + j < p.N; ++j) crow[j] = v[j] + (p.accumulate ? crow[j] : 0.f);
-          }
-        } else {
-          __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.C) + m * p.ldc + n0;
-          if (full_chunk) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              if (p.accumulate) {
-                const uint4 old = *reinterpret_cast<const uint4*>(crow + j);
-                v[j + 0] += bf16_lo(old.x); v[j + 1] += bf16_hi(old.x);
-                v[j + 2] += bf16_lo(old.y); v[j + 3] += bf16_hi(old.y);
-                v[j + 4] += bf16_lo(old.z); v[j + 5] += bf16_hi(old.z);
-                v[j + 6] += bf16_lo(old.w); v[j + 7] += bf16_hi(old.w);
-              }
-              uint4 o;
-              o.x = pack_bf16x2(v[j + 0], v[j + 1]);
-              o.y = pack_bf16x2(v[j + 2], v[j + 3]);
-              o.z = pack_bf16x2(v[j + 4], v[j + 5]);
-              o.w = pack_bf16x2(v[j + 6], v[j + 7]);
-              *reinterpret_cast<uint4*>(crow + j) = o;
-            }
-          } else {
-            for (int j = 0; j < 32 && n0 + j < p.N; ++j) {
-              float o = v[j] + (p.accumulate ? __bfloat162float(crow[j]) : 0.f);
-              crow[j] = __float2bfloat16(o);
-            }
-          }
-        }
-      }
+      epilogue_tile<BN>(t_row, stage, p, static_cast<long>(mb) * BM + q * 32, nb * BN, vec_ok);
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
