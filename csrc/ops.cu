@@ -18,6 +18,10 @@
 
 #include "common.cuh"
 #include "host_utils.h"
+#include "no_alloc.h"
+
+#include <cstdio>
+#include <mutex>
 
 namespace ntb {
 
@@ -306,6 +310,86 @@ std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& h, c
   NTB_LAUNCH_CHECK(2);
   return {dx, dw.to(w.scalar_type())};
 }
+
+// ----------------------------------------------------------- allocation-free RMSNorm backward
+// Variant of rmsnorm_bwd for callers that cannot allocate (see no_alloc.h): the same two
+// kernels, with the per-block dW partials in a file-scope device array instead of a
+// per-call tensor. Each block overwrites its own partial row before accumulating into it,
+// so the array needs no initialisation.
+constexpr int kNoAllocBlocks = 128;
+static __device__ __align__(256) float g_rmsnorm_bwd_scratch[kNoAllocBlocks * NTB_NOALLOC_RMSNORM_MAX_H];
+
+constexpr int kNoAllocMaxDevices = 64;
+static float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+static std::mutex g_noalloc_mu;
+static thread_local char g_noalloc_err[256] = "";
+
+static int noalloc_fail(int code, const char* what, cudaError_t e) {
+  if (e != cudaSuccess)
+    std::snprintf(g_noalloc_err, sizeof(g_noalloc_err), "%s: %s", what, cudaGetErrorString(e));
+  else
+    std::snprintf(g_noalloc_err, sizeof(g_noalloc_err), "%s", what);
+  return code;
+}
+
+}  // namespace ntb
+
+extern "C" __attribute__((visibility("default"))) const char* ntb_noalloc_last_error(void) {
+  return ntb::g_noalloc_err;
+}
+
+extern "C" __attribute__((visibility("default"))) int ntb_rmsnorm_bwd_bf16_noalloc(
+    const void* dy, const void* h, const void* w, const float* rstd, const void* dres, void* dx, float* dw,
+    int64_t rows, int H, cudaStream_t stream) {
+  using namespace ntb;
+  using T = __nv_bfloat16;
+  if (H < 1 || H > NTB_NOALLOC_RMSNORM_MAX_H || rows < 0) {
+    std::snprintf(g_noalloc_err, sizeof(g_noalloc_err),
+                  "ntb_rmsnorm_bwd_bf16_noalloc: H=%d rows=%lld outside H in [1, %d], rows >= 0", H,
+                  static_cast<long long>(rows), NTB_NOALLOC_RMSNORM_MAX_H);
+    return 1;
+  }
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(2, "cudaGetDevice", e);
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return noalloc_fail(2, "device index beyond the set-up table", cudaSuccess);
+  float* scratch = nullptr;
+  {
+    // One-time set-up per device, with that device current: resolve the scratch array's address.
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+      void* ptr = nullptr;
+      e = cudaGetSymbolAddress(&ptr, g_rmsnorm_bwd_scratch);
+      if (e != cudaSuccess) return noalloc_fail(2, "cudaGetSymbolAddress(scratch)", e);
+      g_noalloc_scratch_ptr[dev] = static_cast<float*>(ptr);
+    }
+    scratch = g_noalloc_scratch_ptr[dev];
+  }
+  g_noalloc_err[0] = '\0';
+  if (rows == 0) return 0;
+  const int blocks = static_cast<int>(rows < kNoAllocBlocks ? rows : kNoAllocBlocks);
+  const int rpb = static_cast<int>((rows + blocks - 1) / blocks);
+  const int threads = row_threads(H);
+  const bool vec = (H % 8 == 0) && ((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(h) |
+                                     reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dx) |
+                                     (dres ? reinterpret_cast<uintptr_t>(dres) : 0)) &
+                                    15) == 0;
+  const T* dr = static_cast<const T*>(dres);
+  if (vec)
+    rmsnorm_bwd_kernel<T, true><<<blocks, threads, 0, stream>>>(
+        static_cast<const T*>(dy), static_cast<const T*>(h), static_cast<const T*>(w), rstd, dr, static_cast<T*>(dx),
+        scratch, rows, H, rpb);
+  else
+    rmsnorm_bwd_kernel<T, false><<<blocks, threads, 0, stream>>>(
+        static_cast<const T*>(dy), static_cast<const T*>(h), static_cast<const T*>(w), rstd, dr, static_cast<T*>(dx),
+        scratch, rows, H, rpb);
+  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(scratch, blocks, H, dw);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc_fail(2, "kernel launch", e);
+  return 0;
+}
+
+namespace ntb {
 
 // =========================================================== LayerNorm
 template <typename T>
