@@ -240,6 +240,45 @@ class TransformerModel(nn.Module):
         return ops.cross_entropy(logits, labels.reshape(-1), ignore_index=ignore_index, vocab_start=self.vocab_start,
                                  group=group, inplace_grad=True)
 
+    # ------------------------------------------------------------------ full <-> TP-shard state
+    def shard_full_state_dict(self, full: dict) -> dict:
+        """Slice an unsharded (TP=1) state dict into this rank's TP shards.
+
+        Column-parallel weights split their output rows: the fused QKV rows go
+        to each rank as [q heads | k heads | v heads] of that rank, the fused
+        SwiGLU gate|up rows as [gate rows | up rows]; row-parallel weights
+        split their input columns; the vocab-parallel embedding and LM head
+        split the vocabulary. Replicated tensors are copied.
+        """
+        if not self.tp_enabled:
+            return dict(full)
+        r, tp = self.tp_rank, self.tp_size
+        out = {}
+        for name, t in full.items():
+            if name.endswith("attn.qkv_proj.weight") or name.endswith("attn.qkv_proj.bias"):
+                attn = self.blocks[0].attn
+                D = attn.head_dim
+                nq, nkv = attn.num_heads * D, attn.num_kv_heads * D
+                q, k, v = t[:nq], t[nq:nq + nkv], t[nq + nkv:]
+                out[name] = torch.cat([q.chunk(tp)[r], k.chunk(tp)[r], v.chunk(tp)[r]], 0).contiguous()
+            elif self.config.mlp == "swiglu" and (name.endswith("mlp.fc1.weight") or name.endswith("mlp.fc1.bias")):
+                g, u = t.chunk(2, 0)
+                out[name] = torch.cat([g.chunk(tp)[r], u.chunk(tp)[r]], 0).contiguous()
+            elif name.endswith("mlp.fc1.weight") or name.endswith("mlp.fc1.bias"):
+                out[name] = t.chunk(tp, 0)[r].contiguous()
+            elif name.endswith(("attn.out_proj.weight", "mlp.fc2.weight")):
+                out[name] = t.chunk(tp, 1)[r].contiguous()
+            elif name in ("lm_head.weight",) or (name == "token_embeddings.weight"
+                                                 and not isinstance(self.token_embeddings, Embedding)):
+                out[name] = t.chunk(tp, 0)[r].contiguous()
+            else:
+                out[name] = t
+        return out
+
+    def load_full_state_dict(self, full: dict, strict: bool = True):
+        """Load an unsharded state dict (e.g. from a TP=1 run) into this (possibly TP-sharded) model."""
+        return self.load_state_dict(self.shard_full_state_dict(full), strict=strict)
+
     @property
     def num_parameters(self) -> int:
         return sum(p.numel() for p in self.parameters())

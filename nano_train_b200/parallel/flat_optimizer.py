@@ -16,6 +16,13 @@ scalar that the AdamW kernel multiplies into the gradient, so a step has no
 host synchronisation. fp32 master weights and moments exist only for the
 local shard.
 
+Tensor parallelism: groups flagged ``tp_replicated`` hold parameters that
+every TP rank keeps whole (norm weights, row-parallel biases, positions).
+Under sequence parallelism each TP rank only sees its sequence shard, so
+their gradients are partial and are summed over ``tp_group`` before the
+update. For the clipping norm, the squared sums of TP-sharded groups are
+summed over ``tp_group`` while replicated groups count once.
+
 Reference parity: src/runtime/optimizer_runtime.py:15-162 (PrecisionAdamW,
 full-size master), src/distributed/zero.py:119-503 (per-parameter ZeRO-1/2
 with one collective per parameter); here one collective and one kernel per
@@ -104,7 +111,8 @@ class FlatAdamW:
 
     def __init__(self, param_groups: list[dict], *, lr: float = 1e-3, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, dp_group=None, strategy: str = "no_shard",
-                 max_grad_norm: Optional[float] = None, grad_norm_group=None):
+                 max_grad_norm: Optional[float] = None, grad_norm_group=None, tp_group=None,
+                 sequence_parallel: bool = False):
         if strategy not in ("no_shard", "optim", "optim_grads"):
             raise ValueError(f"unknown sharding strategy {strategy}")
         self.lr = lr
@@ -115,10 +123,13 @@ class FlatAdamW:
         self.dp_rank = comm.group_rank(dp_group)
         self.strategy = strategy if self.dp_size > 1 else "no_shard"
         self.max_grad_norm = max_grad_norm
-        self.grad_norm_group = grad_norm_group
+        self.grad_norm_group = grad_norm_group if grad_norm_group is not None else tp_group
+        self.tp_group = tp_group
+        self.sequence_parallel = bool(sequence_parallel) and comm.group_size(tp_group) > 1
         self.step_count = 0
         self.buffers: list[FlatParamBuffer] = []
         self.group_wd: list[float] = []
+        self.group_replicated: list[bool] = []
         self.shards: list[dict] = []
         dp_for_pad = self.dp_size if self.strategy != "no_shard" else 1
         all_params = []
@@ -129,6 +140,7 @@ class FlatAdamW:
             buf = FlatParamBuffer(params, dp_size=dp_for_pad, name=g.get("name", f"group{i}"))
             self.buffers.append(buf)
             self.group_wd.append(g.get("weight_decay", weight_decay))
+            self.group_replicated.append(bool(g.get("tp_replicated", False)))
             all_params.extend(params)
             if self.strategy == "no_shard":
                 lo, hi = 0, buf.numel
@@ -141,6 +153,7 @@ class FlatAdamW:
         self._hooks = _install_grad_hooks(all_params)
         dev = self.buffers[0].param_data.device if self.buffers else torch.device("cpu")
         self._stats = torch.zeros(2, dtype=torch.float32, device=dev)
+        self._stats_rep = torch.zeros(2, dtype=torch.float32, device=dev)
         self._scale = torch.ones(1, dtype=torch.float32, device=dev)
         self.last_grad_norm: Optional[torch.Tensor] = None
 
@@ -155,8 +168,10 @@ class FlatAdamW:
     def _reduce_grads(self) -> list[torch.Tensor]:
         """Returns, per buffer, the (summed over DP) gradient of this rank's shard."""
         out = []
-        for buf, sh in zip(self.buffers, self.shards):
+        for buf, sh, rep in zip(self.buffers, self.shards, self.group_replicated):
             g = buf.grad_data
+            if rep and self.sequence_parallel:
+                dist.all_reduce(g, group=self.tp_group)
             if self.dp_size > 1:
                 if self.strategy == "optim_grads":
                     shard = torch.empty(sh["hi"] - sh["lo"], dtype=g.dtype, device=g.device)
@@ -175,12 +190,18 @@ class FlatAdamW:
         inv_dp = 1.0 / self.dp_size
         if self.max_grad_norm is not None and self.max_grad_norm > 0:
             self._stats.zero_()
-            for g in grads:
-                ops.grad_stats_(g.contiguous() if not g.is_contiguous() else g, self._stats)
+            self._stats_rep.zero_()
+            for g, rep in zip(grads, self.group_replicated):
+                ops.grad_stats_(g.contiguous() if not g.is_contiguous() else g,
+                                self._stats_rep if rep else self._stats)
             if self.strategy != "no_shard" and self.dp_size > 1:
-                dist.all_reduce(self._stats, group=self.dp_group)
+                both = torch.cat([self._stats, self._stats_rep])
+                dist.all_reduce(both, group=self.dp_group)
+                self._stats.copy_(both[:2])
+                self._stats_rep.copy_(both[2:])
             if self.grad_norm_group is not None and comm.group_size(self.grad_norm_group) > 1:
                 dist.all_reduce(self._stats, group=self.grad_norm_group)
+            self._stats.add_(self._stats_rep)
             norm = torch.sqrt(self._stats[0:1]) * inv_dp
             self.last_grad_norm = norm
             coef = torch.clamp(self.max_grad_norm / (norm + 1e-6), max=1.0)
@@ -202,17 +223,24 @@ class FlatAdamW:
         return self.shards
 
 
-def split_decay_groups(model: torch.nn.Module, weight_decay: float) -> list[dict]:
-    """Matrices decay; biases, norm weights and 1-D params do not (reference: src/optimizer.py:12-55)."""
-    decay, no_decay = [], []
+def split_decay_groups(model: torch.nn.Module, weight_decay: float, *, split_tp_replicated: bool = False) -> list[dict]:
+    """Matrices decay; biases, norm weights and 1-D params do not (reference: src/optimizer.py:12-55).
+
+    With ``split_tp_replicated`` the groups are further split into TP-sharded
+    parameters (marked ``tensor_model_parallel``) and TP-replicated ones
+    (flagged ``tp_replicated`` for the optimizer).
+    """
+    groups: dict[tuple[bool, bool], list] = {}
     seen = set()
     for name, p in model.named_parameters():
         if not p.requires_grad or id(p) in seen:
             continue
         seen.add(id(p))
-        if p.dim() < 2 or name.endswith(".bias") or "norm" in name or ".ln" in name or name.startswith("ln"):
-            no_decay.append(p)
-        else:
-            decay.append(p)
-    return [dict(params=decay, weight_decay=weight_decay, name="decay"),
-            dict(params=no_decay, weight_decay=0.0, name="no_decay")]
+        nd = p.dim() < 2 or name.endswith(".bias") or "norm" in name or ".ln" in name or name.startswith("ln")
+        rep = split_tp_replicated and not getattr(p, "tensor_model_parallel", False)
+        groups.setdefault((nd, rep), []).append(p)
+    out = []
+    for (nd, rep), params in sorted(groups.items()):
+        out.append(dict(params=params, weight_decay=0.0 if nd else weight_decay, tp_replicated=rep,
+                        name=("no_decay" if nd else "decay") + ("_tp_replicated" if rep else "")))
+    return out

@@ -4,7 +4,10 @@
 step per ``train_step(input_ids, labels)`` call: host->device copy of the
 batch (pinned host tensors are copied asynchronously), gradient accumulation
 over micro-batches, fused optimizer update, and the mean loss as a device
-scalar (read it with ``float(loss)``).
+scalar (read it with ``float(loss)``). For a tensor-parallel model the TP
+group and sequence-parallel flag are read from the model, so replicated
+parameters get their gradients summed over TP and count once in the
+clipping norm.
 """
 from __future__ import annotations
 
@@ -23,9 +26,14 @@ class LMTrainer:
         self.model = model
         self.micro_batch_size = micro_batch_size
         self.device = device or next(model.parameters()).device
-        self.optimizer = FlatAdamW(split_decay_groups(model, weight_decay), lr=lr, betas=betas, eps=eps,
-                                   weight_decay=weight_decay, dp_group=dp_group, strategy=strategy,
-                                   max_grad_norm=max_grad_norm, grad_norm_group=grad_norm_group)
+        tp_enabled = bool(getattr(model, "tp_enabled", False))
+        tp_group = getattr(model, "tp_group", None) if tp_enabled else None
+        self.optimizer = FlatAdamW(split_decay_groups(model, weight_decay, split_tp_replicated=tp_enabled), lr=lr,
+                                   betas=betas, eps=eps, weight_decay=weight_decay, dp_group=dp_group,
+                                   strategy=strategy, max_grad_norm=max_grad_norm,
+                                   grad_norm_group=grad_norm_group if grad_norm_group is not None else tp_group,
+                                   tp_group=tp_group,
+                                   sequence_parallel=bool(getattr(model, "sequence_parallel", False)))
 
     def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor, lr: Optional[float] = None) -> torch.Tensor:
         ids = input_ids.to(self.device, non_blocking=True)
