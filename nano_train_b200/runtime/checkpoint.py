@@ -49,7 +49,9 @@ class DirectoryCheckpointManager:
     """Save/restore to ``root/step_{N}/`` (one model + optimizer file per rank).
 
     A checkpoint directory is complete when its ``COMPLETE`` marker exists;
-    incomplete directories (a rank died mid-save) are ignored on load.
+    incomplete directories (a rank died mid-save) are ignored on load. A
+    checkpoint records ``next_step``, the number of completed steps, which is
+    where a resumed run starts.
     """
 
     def __init__(self, root: str, save_every: int = 0, keep_last: int = 2):
@@ -67,10 +69,15 @@ class DirectoryCheckpointManager:
                        and os.path.exists(os.path.join(self.root, d, "COMPLETE")))
         return os.path.join(self.root, cands[-1]) if cands else None
 
-    def save(self, *, model, optimizer_state: OptimizerState, state: TrainState, ctx: RuntimeContext) -> str:
+    def save(self, *, model, optimizer_state: OptimizerState, state: TrainState, ctx: RuntimeContext,
+             next_step: Optional[int] = None) -> str:
+        """Save after ``next_step`` completed steps (default: the step ``state.global_step`` just finished)."""
         rank = ctx.parallel.rank
         world = ctx.parallel.world_size
-        d = self._dir(state.global_step)
+        next_step = state.global_step + 1 if next_step is None else next_step
+        d = self._dir(next_step)
+        if os.path.exists(os.path.join(d, "COMPLETE")):
+            return d  # already saved at this point (step-end save followed by the run-end save)
         os.makedirs(d, exist_ok=True)
         torch.save(model.state_dict(), os.path.join(d, f"model_rank{rank}.pt"))
         opt = optimizer_state.optimizer
@@ -78,12 +85,13 @@ class DirectoryCheckpointManager:
             opt.save_checkpoint_files(d)
         elif hasattr(opt, "state_dict"):
             torch.save(opt.state_dict(), os.path.join(d, f"optimizer_rank{rank}.pt"))
-        torch.save({"train_state": vars(state).copy(), "rng": _rng_state()}, os.path.join(d, f"meta_rank{rank}.pt"))
+        torch.save({"train_state": vars(state).copy(), "next_step": next_step, "rng": _rng_state()},
+                   os.path.join(d, f"meta_rank{rank}.pt"))
         if world > 1 and torch.distributed.is_initialized():
             torch.distributed.barrier()
         if rank == 0:
             with open(os.path.join(d, "COMPLETE"), "w") as f:
-                json.dump({"global_step": state.global_step, "world_size": world}, f)
+                json.dump({"next_step": next_step, "world_size": world}, f)
             self._prune()
         if world > 1 and torch.distributed.is_initialized():
             torch.distributed.barrier()
@@ -113,7 +121,7 @@ class DirectoryCheckpointManager:
         meta = torch.load(os.path.join(d, f"meta_rank{rank}.pt"), map_location="cpu", weights_only=False)
         _set_rng_state(meta["rng"])
         ts = meta["train_state"]
-        return ResumeState(start_global_step=int(ts["global_step"]) + 1, start_epoch=int(ts["epoch"]),
+        return ResumeState(start_global_step=int(meta["next_step"]), start_epoch=int(ts["epoch"]),
                            pipeline_epoch=int(ts["pipeline_epoch"]))
 
     def on_step_end(self, *, model, optimizer_state, state: TrainState, ctx) -> None:
@@ -121,5 +129,7 @@ class DirectoryCheckpointManager:
             self.save(model=model, optimizer_state=optimizer_state, state=state, ctx=ctx)
 
     def on_run_end(self, *, model, optimizer_state, state: TrainState, ctx) -> None:
+        # At run end ``state.global_step`` counts the completed steps.
         if self.save_every > 0:
-            self.save(model=model, optimizer_state=optimizer_state, state=state, ctx=ctx)
+            self.save(model=model, optimizer_state=optimizer_state, state=state, ctx=ctx,
+                      next_step=state.global_step)

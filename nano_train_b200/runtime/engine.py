@@ -65,6 +65,9 @@ class RuntimeEngine:
                                components: RuntimeComponents) -> None:
         parallel = runtime_context.parallel
         sampler = train_data.sampler
+        # On resume, batches of the interrupted epoch that were already trained on are skipped
+        # (the sampler order is a function of the epoch, so the stream continues exactly).
+        skip = max(0, state.global_step - state.epoch * len(train_data.loader)) if state.global_step else 0
         for epoch in range(state.epoch, args.epochs):
             state.epoch = epoch
             if sampler is not None and hasattr(sampler, "set_epoch"):
@@ -73,6 +76,9 @@ class RuntimeEngine:
             objective_count = 0
             drop_count = 0
             for batch in train_data.loader:
+                if skip > 0:
+                    skip -= 1
+                    continue
                 if state.global_step >= args.max_steps:
                     break
                 out = schedule.run_step(StepContext(model=model, batch=batch, optimizer_state=optimizer_state,
@@ -110,6 +116,10 @@ class RuntimeEngine:
         if sampler is not None and first and hasattr(sampler, "set_epoch"):
             sampler.set_epoch(state.pipeline_epoch)
         data_iter = iter(train_data.loader) if first else None
+        if first and state.global_step:
+            # Resume: skip what this pipeline epoch already consumed.
+            for _ in range(max(0, state.global_step - state.pipeline_epoch * len(train_data.loader))):
+                next(data_iter, None)
         for step in range(state.global_step, args.max_steps):
             state.global_step = step
             batch = None
@@ -135,6 +145,7 @@ class RuntimeEngine:
                                                       ctx=runtime_context)
             if parallel.rank == 0 and self._should_log_step(args, step):
                 logger.info("step=%d task=%.6f aux=%.6f total=%.6f drop=%.4f", step, t, a, tot, d)
+            state.global_step = step + 1  # completed steps (matches the non-pipeline loop at run end)
 
     def _should_log_step(self, args: argparse.Namespace, step: int) -> bool:
         every = int(getattr(args, "log_every", 0))

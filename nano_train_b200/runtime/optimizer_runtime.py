@@ -52,6 +52,35 @@ class PrecisionAdamW:
                 off += k
             self._flat[dev] = (ps, master, ea, es)
 
+    # ------------------------------------------------------------------ checkpoint state
+    def state_dict(self) -> dict:
+        """Main params, moments and per-parameter step counts (flat, in parameter order)."""
+        flat = []
+        for dev, (ps, master, ea, es) in self._flat.items():
+            flat.append({"main_param": master.detach().cpu().clone(), "exp_avg": ea.detach().cpu().clone(),
+                         "exp_avg_sq": es.detach().cpu().clone(),
+                         "steps": [int(self.state[p]["step"]) for p in ps], "numel": [p.numel() for p in ps]})
+        g0 = self.param_groups[0]
+        return {"format": "precision_adamw_v1", "global_step": self._global_step, "flat": flat,
+                "param_groups": [{k: v for k, v in g0.items() if k != "params"}]}
+
+    def load_state_dict(self, state: dict) -> None:
+        if state.get("format") != "precision_adamw_v1":
+            raise ValueError("not a PrecisionAdamW state dict")
+        if len(state["flat"]) != len(self._flat):
+            raise ValueError("optimizer state has a different number of device buffers")
+        for (dev, (ps, master, ea, es)), st in zip(self._flat.items(), state["flat"]):
+            if st["numel"] != [p.numel() for p in ps]:
+                raise ValueError("optimizer state does not match the parameter layout")
+            master.copy_(st["main_param"].to(master.dtype))
+            ea.copy_(st["exp_avg"].to(ea.dtype))
+            es.copy_(st["exp_avg_sq"].to(es.dtype))
+            for p, n in zip(ps, st["steps"]):
+                self.state[p]["step"] = int(n)
+        self._global_step = int(state["global_step"])
+        for k, v in state["param_groups"][0].items():
+            self.param_groups[0][k] = v
+
     def zero_grad(self, set_to_none: bool = True) -> None:
         for p in self._params:
             if p.grad is not None:
