@@ -70,6 +70,7 @@ void ag_gemm(const at::Tensor& x_local, at::Tensor& x_full_out, const at::Tensor
 void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
              bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> tctrs, at::Tensor& ctrs, int64_t rank,
              int64_t epoch, const c10::optional<at::Tensor>& trace);
+void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns);
 // symm.cpp
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t bytes);
 int64_t symm_open(py::bytes handle);
@@ -113,6 +114,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &ntb::gemm_rs, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("b_mn"),
         py::arg("recv"), py::arg("tctrs"), py::arg("ctrs"), py::arg("rank"), py::arg("epoch"),
         py::arg("trace") = py::none());
+  m.def("wait_flag", &ntb::wait_flag, py::arg("flag"), py::arg("expect"), py::arg("limit_ns"));
   m.def("symm_alloc", &ntb::symm_alloc);
   m.def("symm_open", &ntb::symm_open);
   m.def("symm_close", &ntb::symm_close);

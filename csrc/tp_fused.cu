@@ -787,4 +787,34 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
   }
 }
 
+
+// ================================================================== bounded flag wait
+// One thread waits until *flag >= expect (acquire, system scope) for at most
+// limit_ns; on expiry it records kStatusTimeoutPeer in the device status word
+// and returns. This is the wait the fused kernels use on peer flags, exposed
+// on its own so the host-side timeout handling can be exercised with a flag
+// that nothing sets.
+__global__ void wait_flag_kernel(const unsigned int* flag, unsigned int expect, unsigned long long limit_ns,
+                                 int* status) {
+  if (threadIdx.x != 0 || blockIdx.x != 0) return;
+  const uint64_t t0 = globaltimer_ns();
+  while (ld_acquire_sys_u32(flag) < expect) {
+    if (globaltimer_ns() - t0 > limit_ns) {
+      set_status(status, kStatusTimeoutPeer);
+      return;
+    }
+  }
+}
+
+void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns) {
+  TORCH_CHECK(flag.is_cuda() && flag.scalar_type() == at::kInt && flag.numel() >= 1, "wait_flag: int32 CUDA flag");
+  TORCH_CHECK(limit_ns > 0 && limit_ns <= 10'000'000'000LL, "wait_flag: limit in (0, 10 s]");
+  const int dev = flag.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
+  wait_flag_kernel<<<1, 32, 0, stream>>>(reinterpret_cast<const unsigned int*>(flag.data_ptr()),
+                                         static_cast<unsigned int>(expect),
+                                         static_cast<unsigned long long>(limit_ns), device_status(dev));
+  NTB_LAUNCH_CHECK(1);
+}
+
 }  // namespace ntb

@@ -1,0 +1,152 @@
+"""Failure detection: host-side heartbeats, process-group timeouts, device wait status.
+
+Three layers, none of which needs a GPU fault to be exercised:
+
+* ``HeartbeatMonitor`` - every rank writes a timestamp into the process
+  group's key-value store from a daemon thread; ``dead_ranks()`` lists peers
+  whose heartbeat is older than ``timeout_s``. A training loop calls
+  ``raise_if_peer_dead()`` between steps (never with a kernel or collective
+  in flight), so a crashed or wedged peer becomes a ``PeerFailureError`` on
+  the host before the next launch instead of a hang inside a collective.
+* Process-group timeouts - ``init_process_group(timeout=...)`` (the runtime's
+  ``--dist-timeout-s``) bounds every collective on the host side.
+* Device waits - every spin in the fused kernels (peer flags, arrival
+  counters, mbarriers) is bounded by a %globaltimer budget; on expiry the
+  kernel writes a code into a device status word and returns.
+  ``check_device(device)`` reads and clears it and raises
+  ``CommTimeoutError`` for communication waits.
+
+Plus ``assert_finite`` (fail fast on non-finite loss / norms, reference:
+src/trainer.py:1301-1304, 1371-1375).
+"""
+from __future__ import annotations
+
+import math
+import threading
+import time
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+
+class PeerFailureError(RuntimeError):
+    """A peer rank stopped heartbeating (crashed, killed or wedged)."""
+
+
+class CommTimeoutError(RuntimeError):
+    """A device-side communication wait ran out of its time budget."""
+
+
+class NonFiniteError(RuntimeError):
+    """A monitored scalar (loss, gradient norm, ...) is NaN or infinite."""
+
+
+_COMM_CODES = {5: "peer wait timed out", 7: "flag wait timed out"}
+
+
+def check_device(device: int = 0) -> None:
+    """Read and clear the device status word; raise on a failed bounded wait."""
+    from ..ops._ext import KernelStatusError, ext
+
+    code = int(ext().read_and_clear_status(device))
+    if code == 0:
+        return
+    if code in _COMM_CODES:
+        raise CommTimeoutError(f"device {device}: {_COMM_CODES[code]} (status {code})")
+    raise KernelStatusError(code)
+
+
+def assert_finite(name: str, value) -> float:
+    """Return ``value`` as a float; raise ``NonFiniteError`` if it is NaN/inf."""
+    v = float(value.detach().float().item()) if torch.is_tensor(value) else float(value)
+    if not math.isfinite(v):
+        raise NonFiniteError(f"{name} is not finite: {v}")
+    return v
+
+
+def _default_store():
+    from torch.distributed import distributed_c10d as c10d
+
+    return c10d._get_default_store()
+
+
+class HeartbeatMonitor:
+    """Store-based liveness of the ranks of the default process group.
+
+    ``start()`` launches a daemon thread that writes ``hb/<rank>`` every
+    ``interval_s``. ``dead_ranks()`` compares every peer's last beat against
+    ``timeout_s``. ``on_failure`` (optional) is called from the thread with the
+    list of dead ranks the first time one is seen.
+    """
+
+    def __init__(self, *, interval_s: float = 1.0, timeout_s: float = 10.0, store=None, rank: Optional[int] = None,
+                 world_size: Optional[int] = None, prefix: str = "ntb_hb",
+                 on_failure: Optional[Callable[[list[int]], None]] = None):
+        self.interval_s = interval_s
+        self.timeout_s = timeout_s
+        self.store = store if store is not None else _default_store()
+        self.rank = dist.get_rank() if rank is None else rank
+        self.world_size = dist.get_world_size() if world_size is None else world_size
+        self.prefix = prefix
+        self.on_failure = on_failure
+        self._stop = threading.Event()
+        self._thread: Optional[threading.Thread] = None
+        self._reported = False
+        self._start_time = time.time()
+
+    def _key(self, r: int) -> str:
+        return f"{self.prefix}/{r}"
+
+    def beat(self) -> None:
+        self.store.set(self._key(self.rank), repr(time.time()))
+
+    def _run(self) -> None:
+        while not self._stop.is_set():
+            try:
+                self.beat()
+                if self.on_failure is not None and not self._reported:
+                    dead = self.dead_ranks()
+                    if dead:
+                        self._reported = True
+                        self.on_failure(dead)
+            except Exception:  # the store itself went away: nothing more to report from here
+                return
+            self._stop.wait(self.interval_s)
+
+    def start(self) -> "HeartbeatMonitor":
+        self.beat()
+        self._thread = threading.Thread(target=self._run, name="ntb-heartbeat", daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self) -> None:
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join(timeout=5 * self.interval_s + 1)
+
+    def last_beat(self, r: int) -> Optional[float]:
+        key = self._key(r)
+        try:
+            if not self.store.check([key]):
+                return None
+            return float(self.store.get(key).decode())
+        except Exception:
+            return None
+
+    def dead_ranks(self) -> list[int]:
+        now = time.time()
+        dead = []
+        for r in range(self.world_size):
+            if r == self.rank:
+                continue
+            t = self.last_beat(r)
+            ref = t if t is not None else self._start_time
+            if now - ref > self.timeout_s:
+                dead.append(r)
+        return dead
+
+    def raise_if_peer_dead(self) -> None:
+        dead = self.dead_ranks()
+        if dead:
+            raise PeerFailureError(f"rank {self.rank}: no heartbeat from ranks {dead} for > {self.timeout_s}s")

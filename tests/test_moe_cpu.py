@@ -34,7 +34,7 @@ def test_router_group_limited_topk(scoring):
         allowed_groups = set(torch.topk(gmax, TG).indices.tolist())
         chosen = out.topk_indices[t].tolist()
         assert all(e // (E // G) in allowed_groups for e in chosen)
-        masked = torch.tensor([scores[t, e] if e // (E // G) in allowed_groups else -1.0 for e in range(E)])
+        masked = torch.tensor([float(scores[t, e]) if e // (E // G) in allowed_groups else -1.0 for e in range(E)])
         assert set(chosen) == set(torch.topk(masked, K).indices.tolist())
         raw = scores[t, out.topk_indices[t]]
         expect = raw / raw.sum() if scoring == "sigmoid" else torch.softmax(raw, -1)
