@@ -1,0 +1,88 @@
+"""Small, self-contained launches of the hot kernels for Nsight Compute captures.
+
+    python bench/profile_kernels.py <case> [--iters N]
+
+Each case allocates a few hundred MB at most (inputs larger than the 126 MB
+L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
+``--iters`` launches, and checks the kernel status word. Cases:
+
+  gemm_fwd      tcgen05 GEMM 4096 x 6144 x 4096 (Llama-8B QKV, K-major A and B)
+  gemm_wgrad    4096 x 14336 x 4096 with M-major A / N-major B (weight gradient)
+  attn_fwd      flash attention fwd, B=1 S=4096 32q/8kv heads d=128 causal
+  attn_bwd      flash attention bwd, same shape
+  rmsnorm_bwd   RMSNorm backward 8192 x 4096 bf16
+  adamw         fused flat AdamW over 64M fp32 elements
+  swiglu        SwiGLU fwd 8192 x 14336
+  ce            vocab cross-entropy stats+bwd 4096 x 32064
+"""
+import argparse
+import os
+import sys
+
+import torch
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+from nano_train_b200.ops._ext import check_status, ext  # noqa: E402
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("case")
+    ap.add_argument("--iters", type=int, default=3)
+    a = ap.parse_args()
+    C = ext()
+    dev = torch.device("cuda", 0)
+    torch.manual_seed(0)
+    bf = dict(device=dev, dtype=torch.bfloat16)
+    if a.case == "gemm_fwd":
+        x, w = torch.randn(4096, 4096, **bf), torch.randn(6144, 4096, **bf)
+        y = torch.empty(4096, 6144, **bf)
+        fn = lambda: C.gemm_bf16(x, w, y, None, False, False, False, 1.0)  # noqa: E731
+    elif a.case == "gemm_wgrad":
+        dy, x = torch.randn(4096, 14336, **bf), torch.randn(4096, 4096, **bf)
+        dw = torch.zeros(14336, 4096, device=dev, dtype=torch.float32)
+        fn = lambda: C.gemm_bf16(dy, x, dw, None, True, True, True, 1.0)  # noqa: E731
+    elif a.case in ("attn_fwd", "attn_bwd"):
+        q = torch.randn(1, 4096, 32, 128, **bf)
+        k = torch.randn(1, 4096, 8, 128, **bf)
+        v = torch.randn(1, 4096, 8, 128, **bf)
+        scale = 128 ** -0.5
+        o, lse = C.flash_attn_fwd(q, k, v, scale, True)
+        if a.case == "attn_fwd":
+            fn = lambda: C.flash_attn_fwd(q, k, v, scale, True)  # noqa: E731
+        else:
+            do = torch.randn_like(o)
+            fn = lambda: C.flash_attn_bwd(do, q, k, v, o, lse, scale, True)  # noqa: E731
+    elif a.case == "rmsnorm_bwd":
+        h = torch.randn(8192, 4096, **bf)
+        w = torch.randn(4096, **bf)
+        dy = torch.randn(8192, 4096, **bf)
+        rstd = torch.rand(8192, device=dev) + 0.5
+        fn = lambda: C.rmsnorm_bwd(dy, h, w, rstd, None)  # noqa: E731
+    elif a.case == "adamw":
+        n = 64 * 1024 * 1024
+        p, m, v, g = (torch.randn(n, device=dev) for _ in range(4))
+        m.zero_()
+        v.zero_()
+        pb = torch.empty(n, **bf)
+        sc = torch.ones(1, device=dev)
+        fn = lambda: C.adamw_flat_(p, m, v, g, pb, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, sc, None)  # noqa: E731
+    elif a.case == "swiglu":
+        gu = torch.randn(8192, 2 * 14336, **bf)
+        fn = lambda: C.swiglu_fwd(gu)  # noqa: E731
+    elif a.case == "ce":
+        logits = torch.randn(4096, 32064, **bf)
+        labels = torch.randint(0, 32064, (4096,), device=dev)
+        fn = lambda: C.ce_stats(logits, labels, 0, -100)  # noqa: E731
+    else:
+        raise SystemExit(f"unknown case {a.case}")
+    for _ in range(2 + a.iters):
+        fn()
+    torch.cuda.synchronize()
+    check_status(0)
+    print(f"{a.case}: ok")
+
+
+if __name__ == "__main__":
+    main()
