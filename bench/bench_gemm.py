@@ -27,6 +27,9 @@ LLAMA8B = [
     ("down_wgrad", 4096, 14336, 4096, True, True),
     ("gateup_wgrad", 28672, 4096, 4096, True, True),
     ("sq8192", 8192, 8192, 8192, False, False),
+    # weight gradients as training runs them: accumulated into the fp32 main_grad
+    ("down_wgrad_f32acc", 4096, 14336, 4096, True, True),
+    ("qkv_wgrad_f32acc", 6144, 4096, 4096, True, True),
 ]
 
 
@@ -60,13 +63,21 @@ def main():
     for name, M, N, K, a_mn, b_mn in LLAMA8B:
         A = torch.randn(K, M, device="cuda", dtype=torch.bfloat16) if a_mn else torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
         B = torch.randn(K, N, device="cuda", dtype=torch.bfloat16) if b_mn else torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
-        out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
-        t_ours = time_fn(lambda: C.gemm_bf16(A, B, out, None, a_mn, b_mn, False, 1.0), args.iters, flush=flush)
+        acc = name.endswith("_f32acc")
+        out = torch.zeros(M, N, device="cuda", dtype=torch.float32 if acc else torch.bfloat16)
+        t_ours = time_fn(lambda: C.gemm_bf16(A, B, out, None, a_mn, b_mn, acc, 1.0), args.iters, flush=flush)
         Aop = A.t() if a_mn else A
         Bop = B if b_mn else B.t()
-        t_cublas = time_fn(lambda: torch.matmul(Aop, Bop, out=out), args.iters, flush=flush)
+        if acc:  # cuBLAS bf16 GEMM into a bf16 temporary + fp32 accumulate (what eager PyTorch does)
+            t_cublas = time_fn(lambda: out.add_(torch.matmul(Aop, Bop)), args.iters, flush=flush)
+            out.zero_()
+        else:
+            t_cublas = time_fn(lambda: torch.matmul(Aop, Bop, out=out), args.iters, flush=flush)
         ref = Aop.float() @ Bop.float() if M * N * K <= 4096 * 6144 * 4096 else None
         C.gemm_bf16(A, B, out, None, a_mn, b_mn, False, 1.0)
+        if acc:
+            C.gemm_bf16(A, B, out, None, a_mn, b_mn, True, 1.0)
+            ref = 2 * ref if ref is not None else None
         err = None
         if ref is not None:
             err = ((out.float() - ref).norm() / ref.norm()).item()

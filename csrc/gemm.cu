@@ -79,10 +79,36 @@ template <int BN>
 __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, const GemmParams& p, long m0, int n0,
                                               bool vec_ok) {
   const int lane = threadIdx.x & 31;
+  const bool f32 = p.c_f32 != 0;
+  const bool acc = p.accumulate != 0;
 #pragma unroll 1
   for (int g = 0; g < BN; g += 64) {
     const int cg = n0 + g;
     if (cg >= p.N) break;  // warp-uniform
+    // With accumulation, the previous C of this 64-column group is requested first so
+    // its DRAM latency overlaps the TMEM read and the staging below.
+    float4 old[16];
+    if (acc) {
+      if (f32) {
+#pragma unroll
+        for (int it = 0; it < 16; ++it) {
+          const int row = it * 2 + (lane >> 4), col = cg + (lane & 15) * 4;
+          const long m = m0 + row;
+          old[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (m < p.M && vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0)
+            old[it] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.C) + m * p.ldc + col);
+        }
+      } else {
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int row = it * 4 + (lane >> 3), col = cg + (lane & 7) * 8;
+          const long m = m0 + row;
+          old[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (m < p.M && vec_ok && col + 8 <= p.N)
+            old[it] = *reinterpret_cast<const float4*>(reinterpret_cast<const __nv_bfloat16*>(p.C) + m * p.ldc + col);
+        }
+      }
+    }
     uint32_t r0[32], r1[32];
     tmem_ld32(t_row + g, r0);
     tmem_ld32(t_row + g + 32, r1);
@@ -101,9 +127,9 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
       *reinterpret_cast<float4*>(stage + lane * 64 + ((j ^ (lane & 15)) * 4)) = v;
     }
     __syncwarp();
-    if (p.c_f32) {
+    if (f32) {
       float* C = reinterpret_cast<float*>(p.C);
-#pragma unroll 4
+#pragma unroll
       for (int it = 0; it < 16; ++it) {
         const int row = it * 2 + (lane >> 4), ch = lane & 15;
         const long m = m0 + row;
@@ -112,19 +138,18 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
         float4 v = *reinterpret_cast<const float4*>(stage + row * 64 + ((ch ^ (row & 15)) * 4));
         float* dst = C + m * p.ldc + col;
         if (vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0) {
-          if (p.accumulate) {
-            const float4 old = *reinterpret_cast<const float4*>(dst);
-            v.x += old.x; v.y += old.y; v.z += old.z; v.w += old.w;
+          if (acc) {
+            v.x += old[it].x; v.y += old[it].y; v.z += old[it].z; v.w += old[it].w;
           }
           *reinterpret_cast<float4*>(dst) = v;
         } else {
           const float* vv = &v.x;
-          for (int u = 0; u < 4 && col + u < p.N; ++u) dst[u] = vv[u] + (p.accumulate ? dst[u] : 0.f);
+          for (int u = 0; u < 4 && col + u < p.N; ++u) dst[u] = vv[u] + (acc ? dst[u] : 0.f);
         }
       }
     } else {
       __nv_bfloat16* C = reinterpret_cast<__nv_bfloat16*>(p.C);
-#pragma unroll 4
+#pragma unroll
       for (int it = 0; it < 8; ++it) {
         const int row = it * 4 + (lane >> 3), c8 = lane & 7;
         const long m = m0 + row;
@@ -135,12 +160,12 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
         float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
         __nv_bfloat16* dst = C + m * p.ldc + col;
         if (vec_ok && col + 8 <= p.N) {
-          if (p.accumulate) {
-            const uint4 old = *reinterpret_cast<const uint4*>(dst);
-            v[0] += bf16_lo(old.x); v[1] += bf16_hi(old.x);
-            v[2] += bf16_lo(old.y); v[3] += bf16_hi(old.y);
-            v[4] += bf16_lo(old.z); v[5] += bf16_hi(old.z);
-            v[6] += bf16_lo(old.w); v[7] += bf16_hi(old.w);
+          if (acc) {
+            const uint4 o4 = *reinterpret_cast<const uint4*>(&old[it]);
+            v[0] += bf16_lo(o4.x); v[1] += bf16_hi(o4.x);
+            v[2] += bf16_lo(o4.y); v[3] += bf16_hi(o4.y);
+            v[4] += bf16_lo(o4.z); v[5] += bf16_hi(o4.z);
+            v[6] += bf16_lo(o4.w); v[7] += bf16_hi(o4.w);
           }
           uint4 o;
           o.x = pack_bf16x2(v[0], v[1]);
@@ -150,7 +175,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
           *reinterpret_cast<uint4*>(dst) = o;
         } else {
           for (int u = 0; u < 8 && col + u < p.N; ++u)
-            dst[u] = __float2bfloat16(v[u] + (p.accumulate ? __bfloat162float(dst[u]) : 0.f));
+            dst[u] = __float2bfloat16(v[u] + (acc ? __bfloat162float(dst[u]) : 0.f));
         }
       }
     }
