@@ -190,6 +190,16 @@ def run_ours(args, rank, local, world):
     ms = start.elapsed_time(end) / args.steps
     ms = max_over_ranks(ms, world)
     check_status(torch.cuda.current_device())
+    fused_paths = None
+    if world > 1:
+        from nano_train_b200.parallel.fused import get_communicator
+
+        a = get_communicator(dist.group.WORLD)
+        if a is not None and hasattr(a, "choice"):
+            fused_paths = {f"{k[0]} x{list(k[1])} w{list(k[2])}{' bmn' if k[3] else ''}":
+                           {"path": v, "fused_ms": round(a.timings.get(k, (0, 0))[0], 4),
+                            "nccl_gemm_ms": round(a.timings.get(k, (0, 0))[1], 4)}
+                           for k, v in a.choice.items()}
 
     e2e = None
     if not args.no_e2e:
@@ -205,7 +215,7 @@ def run_ours(args, rank, local, world):
         e2e = {"value": tok / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": 2 * GLOBAL_BATCH * args.seq * 8, "d2h_bytes_per_step": 4,
                "api": "nano_train_b200.training.LMTrainer.train_step"}
-    return ms, layers, launches, sampler.summary(), e2e
+    return ms, layers, launches, sampler.summary(), e2e, fused_paths
 
 
 # ---------------------------------------------------------------- reference arm
@@ -227,8 +237,9 @@ def main():
             if res is None:
                 return
             ms, layers, launches, clocks, e2e = res
+            fused_paths = None
         else:
-            ms, layers, launches, clocks, e2e = run_ours(args, rank, local, world)
+            ms, layers, launches, clocks, e2e, fused_paths = run_ours(args, rank, local, world)
         tokens = GLOBAL_BATCH * args.seq
         value = tokens / (ms / 1e3)
         if rank == 0:
@@ -257,6 +268,7 @@ def main():
                 },
                 "clocks": clocks,
                 "e2e": e2e,
+                "fused_tp_paths": fused_paths,
                 "gpu_launches": launches,
             }
             if args.impl == "reference":

@@ -175,7 +175,7 @@ __device__ __forceinline__ void rotated_tile(int t, int tiles_per_chunk, int mti
 // Shared-memory layout of one CTA (after 1024-byte alignment):
 //   [0, STAGES*A)            A ring        [STAGES*A, STAGES*(A+B))   B ring
 //   epilogue staging (4 x 4 KB)
-//   barriers: full[S] empty[S] tfull[2] tempty[2] tdone[2] drain tring_full[4] tring_empty[4]
+//   barriers: full[S] empty[S] tfull[2] tempty[2] tdone[4] drain tring_full[4] tring_empty[4]
 //   tile ring int[4], TMEM base slot
 template <int BN>
 struct FusedSmem {
@@ -195,13 +195,15 @@ struct FusedSmem {
     tfull = empty + Cfg::STAGES;
     tempty = tfull + 2;
     tdone = tempty + 2;
-    drain = tdone + 2;
+    drain = tdone + 4;
     tring_full = drain + 1;
     tring_empty = tring_full + 4;
     tring = reinterpret_cast<int*>(tring_empty + 4);
     tmem_slot = reinterpret_cast<uint32_t*>(tring + 4);
   }
-  __device__ __forceinline__ void init() {
+  // publisher: a seventh warp releases every finished tile to its destination (reduce-scatter);
+  // ring slots then also wait for it.
+  __device__ __forceinline__ void init(bool publisher) {
     for (int s = 0; s < Cfg::STAGES; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
@@ -209,11 +211,11 @@ struct FusedSmem {
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
       mbar_init(&tempty[b], 128);
-      mbar_init(&tdone[b], 128);
     }
     for (int b = 0; b < 4; ++b) {
+      mbar_init(&tdone[b], 128);
       mbar_init(&tring_full[b], 1);
-      mbar_init(&tring_empty[b], 128);
+      mbar_init(&tring_empty[b], publisher ? 129 : 128);
     }
     mbar_init(drain, 1);
     mbar_fence_init();
@@ -405,6 +407,25 @@ __device__ __forceinline__ void gemm_phase(FusedSmem<BN>& sm, uint32_t tmem_base
       umma_commit(sm.drain);
       mbar_wait(sm.drain, 0, nullptr, 0);
     }
+  } else if (warp == 6) {
+    // Publisher (reduce-scatter only): per tile, in ring order, wait until the epilogue stored it,
+    // then one system-scope fence + the arrival increment at the destination.
+    if constexpr (PUBLISH) {
+      if (lane == 0) {
+        for (int i = 0;; ++i) {
+          const int slot = i & 3;
+          const uint32_t par = static_cast<uint32_t>((i >> 2) & 1);
+          if (!mbar_wait(&sm.tring_full[slot], par, status, kStatusTimeoutEpilogue)) break;
+          const int t = sm.tring[slot];
+          if (t < 0) break;
+          int mb, nb, chunk;
+          tile_of(t, mb, nb, chunk);
+          if (!mbar_wait(&sm.tdone[slot], par, status, kStatusTimeoutEpilogue)) break;
+          published(mb, nb, chunk);
+          mbar_arrive(&sm.tring_empty[slot]);
+        }
+      }
+    }
   } else {
     const int q = warp & 3;
     pre_epilogue();
@@ -427,13 +448,9 @@ __device__ __forceinline__ void gemm_phase(FusedSmem<BN>& sm, uint32_t tmem_base
       store(t_row, mb, nb, chunk);
       tc_fence_before();
       mbar_arrive(&sm.tempty[acc]);
-      if constexpr (PUBLISH) {
-        if (chunk != own_chunk) __threadfence_system();
-        mbar_arrive(&sm.tdone[acc]);
-        if (warp == 2 && lane == 0) {
-          if (mbar_wait(&sm.tdone[acc], acc_phase, status, kStatusTimeoutEpilogue)) published(mb, nb, chunk);
-        }
-      }
+      // Stores of this tile are done (mbarrier arrive = CTA-scope release); the publisher
+      // warp makes them visible system-wide and signals the destination.
+      if constexpr (PUBLISH) mbar_arrive(&sm.tdone[slot]);
       mbar_arrive(&sm.tring_empty[slot]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1;
@@ -453,7 +470,7 @@ __global__ void __launch_bounds__(192, 1)
   FusedSmem<BN> sm(smem);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) sm.init();
+  if (threadIdx.x == 0) sm.init(false);
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -514,15 +531,15 @@ __global__ void __launch_bounds__(192, 1)
       uint4* dst = reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.full + static_cast<long>(j) * p.T_local * p.K) + off);
       uint4* dst2 = j == p.rank ? reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.my_slot) + off) : nullptr;
 #pragma unroll 1
-      for (int base = 0; base < nvec; base += 32 * 8) {
-        uint4 v[8];
+      for (int base = 0; base < nvec; base += 32 * 16) {
+        uint4 v[16];
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
           const int i = base + u * 32 + lane;
           if (i < nvec) v[u] = src[i];
         }
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
+        for (int u = 0; u < 16; ++u) {
           const int i = base + u * 32 + lane;
           if (i < nvec) {
             dst[i] = v[u];
@@ -570,7 +587,7 @@ __global__ void __launch_bounds__(192, 1)
 
 // ================================================================== GEMM + RS
 template <int BN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(224, 1)
     gemm_rs_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, RsParams p) {
   using Cfg = FusedCfg<BN>;
   constexpr int BM = Cfg::BM;
@@ -582,7 +599,7 @@ __global__ void __launch_bounds__(192, 1)
   const int num_n = (p.N + BN - 1) / BN;
   const int tpc = mt_chunk * num_n;
 
-  if (threadIdx.x == 0) sm.init();
+  if (threadIdx.x == 0) sm.init(true);
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
@@ -624,8 +641,12 @@ __global__ void __launch_bounds__(192, 1)
   };
   auto published = [&](int mb, int nb, int chunk) {
     const int idx = nb * mt_chunk + (mb - chunk * mt_chunk);
-    if (chunk != p.rank) red_release_sys_add(p.peer_tctr[chunk] + idx, 1u);
-    else p.my_tctr[idx] = 0u;  // consumed: rewind for this parity's next use (two calls later)
+    if (chunk != p.rank) {
+      __threadfence_system();  // the tile's remote stores (ordered before via the tdone barrier)
+      red_release_sys_add(p.peer_tctr[chunk] + idx, 1u);
+    } else {
+      p.my_tctr[idx] = 0u;  // consumed: rewind for this parity's next use (two calls later)
+    }
   };
   gemm_phase<BN, B_MN, true>(sm, tmem_base, &tmA, &tmB, p.K, tpc * p.n, p.ctr, p.status, tile_of, wait_chunk,
                              pre_epilogue, store, published, p.trace, nullptr, p.rank, mt_chunk);
@@ -643,7 +664,7 @@ __global__ void __launch_bounds__(192, 1)
 // resident yet - copy pieces and GEMM tiles are claimed dynamically by the CTAs
 // that are running, and a tile only waits on pieces or peer tiles claimed earlier.
 template <typename Kern>
-static void fused_launch(Kern kern, int grid, int smem, void** args, cudaStream_t stream) {
+static void fused_launch(Kern kern, int grid, int smem, void** args, cudaStream_t stream, int threads = 192) {
   // The dynamic shared-memory opt-in is set once per (device, kernel).
   static std::mutex mu;
   static std::set<std::pair<int, const void*>> done;
@@ -655,7 +676,7 @@ static void fused_launch(Kern kern, int grid, int smem, void** args, cudaStream_
     if (done.insert({dev, key}).second)
       NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
   }
-  NTB_CUDA_CHECK(cudaLaunchKernel(key, dim3(grid), dim3(192), args, static_cast<size_t>(smem), stream));
+  NTB_CUDA_CHECK(cudaLaunchKernel(key, dim3(grid), dim3(threads), args, static_cast<size_t>(smem), stream));
   NTB_LAUNCH_CHECK(1);
 }
 
@@ -779,11 +800,11 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
   NTB_CUDA_CHECK(cudaMemsetAsync(ctrs.data_ptr(), 0, sizeof(int64_t), stream));
   void* args[3] = {&ts.m[0], &ts.m[1], &p};
   if (wide) {
-    if (b_mn) fused_launch(gemm_rs_kernel<256, true>, grid, FusedCfg<256>::SMEM_BYTES, args, stream);
-    else fused_launch(gemm_rs_kernel<256, false>, grid, FusedCfg<256>::SMEM_BYTES, args, stream);
+    if (b_mn) fused_launch(gemm_rs_kernel<256, true>, grid, FusedCfg<256>::SMEM_BYTES, args, stream, 224);
+    else fused_launch(gemm_rs_kernel<256, false>, grid, FusedCfg<256>::SMEM_BYTES, args, stream, 224);
   } else {
-    if (b_mn) fused_launch(gemm_rs_kernel<128, true>, grid, FusedCfg<128>::SMEM_BYTES, args, stream);
-    else fused_launch(gemm_rs_kernel<128, false>, grid, FusedCfg<128>::SMEM_BYTES, args, stream);
+    if (b_mn) fused_launch(gemm_rs_kernel<128, true>, grid, FusedCfg<128>::SMEM_BYTES, args, stream, 224);
+    else fused_launch(gemm_rs_kernel<128, false>, grid, FusedCfg<128>::SMEM_BYTES, args, stream, 224);
   }
 }
 

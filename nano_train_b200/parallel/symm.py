@@ -86,6 +86,16 @@ class TPCommunicator:
         return (not self.closed and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
                 and x.dim() == 2 and x.shape[-1] % 8 == 0)
 
+    def all_gather_gemm_fits(self, x_shard: torch.Tensor, weight: torch.Tensor, b_mn: bool = False) -> bool:
+        T_local, K = x_shard.shape
+        return T_local <= self.max_local_rows and K <= self.max_k and T_local % 128 == 0
+
+    def gemm_reduce_scatter_fits(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False) -> bool:
+        T = x.shape[0]
+        N = weight.shape[1] if b_mn else weight.shape[0]
+        T_local = T // self.n
+        return T % self.n == 0 and T_local <= self.max_local_rows and N <= self.max_rs_n and T_local % 128 == 0
+
     # ------------------------------------------------------------------ fused ops
     def all_gather_gemm(self, x_shard: torch.Tensor, weight: torch.Tensor, bias=None, b_mn: bool = False):
         T_local, K = x_shard.shape
@@ -126,30 +136,85 @@ class TPCommunicator:
 
 
 class _FusedAdapter:
-    """Adapts TPCommunicator to the fused-dispatch interface (falls back when a shape is out of range)."""
+    """Fused-dispatch interface over a TPCommunicator.
 
-    def __init__(self, c: TPCommunicator):
+    Shapes the communicator cannot take fall back to NCCL + GEMM. With
+    ``autotune`` (default, ``NTB_FUSED_AUTOTUNE=0`` disables it) the first
+    call of every (op, shape, layout) times the fused kernel against NCCL +
+    GEMM on the device (CUDA events, a few repetitions, max over the group so
+    every rank takes the same decision) and later calls use the faster one:
+    the point-to-point reduce-scatter epilogue, for instance, wins at two
+    ranks and loses to NCCL's reduce-scatter at eight on this hardware.
+    """
+
+    REPS = 3
+
+    def __init__(self, c: TPCommunicator, autotune: bool = True):
         self.c = c
+        self.autotune = autotune
+        self.choice: dict = {}  # key -> "fused" | "nccl"
+        self.timings: dict = {}
 
     def supports(self, x, w):
         return self.c.supports(x, w)
 
-    def all_gather_gemm(self, x_shard, weight, bias, b_mn=False):
-        r = self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn)
-        if r is None:
-            from ..ops.linear import gemm
+    # ------------------------------------------------------------------ baseline paths
+    def _ag_nccl(self, x_shard, weight, bias, b_mn):
+        from ..ops.linear import gemm
 
-            full = comm.all_gather_dim0(x_shard, self.c.group)
-            return gemm(full, weight, bias=bias, b_mn=b_mn), full
-        return r
+        full = comm.all_gather_dim0(x_shard, self.c.group)
+        return gemm(full, weight, bias=bias, b_mn=b_mn), full
+
+    def _rs_nccl(self, x, weight, b_mn):
+        from ..ops.linear import gemm
+
+        return comm.reduce_scatter_dim0(gemm(x, weight, b_mn=b_mn), self.c.group)
+
+    def _time(self, fn) -> float:
+        fn()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(self.REPS):
+            fn()
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e) / self.REPS
+
+    def _decide(self, key, fused_fn, nccl_fn) -> str:
+        ch = self.choice.get(key)
+        if ch is not None:
+            return ch
+        if not self.autotune:
+            self.choice[key] = "fused"
+            return "fused"
+        t = torch.tensor([self._time(fused_fn), self._time(nccl_fn)], dtype=torch.float64,
+                         device=self.c.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.c.group)
+        tf, tn = float(t[0]), float(t[1])
+        ch = "fused" if tf <= tn else "nccl"
+        self.choice[key] = ch
+        self.timings[key] = (tf, tn)
+        return ch
+
+    # ------------------------------------------------------------------ fused ops
+    def all_gather_gemm(self, x_shard, weight, bias, b_mn=False):
+        key = ("ag", tuple(x_shard.shape), tuple(weight.shape), b_mn, bias is not None)
+        if self.c.all_gather_gemm_fits(x_shard, weight, b_mn):
+            ch = self._decide(key, lambda: self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn),
+                              lambda: self._ag_nccl(x_shard, weight, bias, b_mn))
+            if ch == "fused":
+                return self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn)
+        return self._ag_nccl(x_shard, weight, bias, b_mn)
 
     def gemm_reduce_scatter(self, x, weight, b_mn=False):
-        r = self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn)
-        if r is None:
-            from ..ops.linear import gemm
-
-            return comm.reduce_scatter_dim0(gemm(x, weight, b_mn=b_mn), self.c.group)
-        return r
+        key = ("rs", tuple(x.shape), tuple(weight.shape), b_mn)
+        if self.c.gemm_reduce_scatter_fits(x, weight, b_mn):
+            ch = self._decide(key, lambda: self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn),
+                              lambda: self._rs_nccl(x, weight, b_mn))
+            if ch == "fused":
+                return self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn)
+        return self._rs_nccl(x, weight, b_mn)
 
     def all_gather(self, x_shard):
         return comm.all_gather_dim0(x_shard, self.c.group)
@@ -170,6 +235,6 @@ def maybe_attach_communicator(group, *, max_local_rows: int = 4096, max_k: int =
     if dist.get_backend(group) != "nccl":
         return None
     c = TPCommunicator(group, max_local_rows=max_local_rows, max_k=max_k, max_rs_n=max_rs_n)
-    a = _FusedAdapter(c)
+    a = _FusedAdapter(c, autotune=os.environ.get("NTB_FUSED_AUTOTUNE", "1") != "0")
     register_communicator(group, a)
     return a
