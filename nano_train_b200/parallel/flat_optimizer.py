@@ -151,6 +151,9 @@ class FlatAdamW:
             self.shards.append(dict(lo=lo, hi=hi, master=master, exp_avg=torch.zeros_like(master),
                                     exp_avg_sq=torch.zeros_like(master)))
         self._hooks = _install_grad_hooks(all_params)
+        # torch-optimizer-style groups (one per buffer): schedulers set "lr" here.
+        self.param_groups = [dict(params=buf.params, lr=float(lr), weight_decay=float(wd), betas=tuple(betas),
+                                  eps=float(eps), name=buf.name) for buf, wd in zip(self.buffers, self.group_wd)]
         dev = self.buffers[0].param_data.device if self.buffers else torch.device("cpu")
         self._stats = torch.zeros(2, dtype=torch.float32, device=dev)
         self._stats_rep = torch.zeros(2, dtype=torch.float32, device=dev)
@@ -184,8 +187,8 @@ class FlatAdamW:
 
     @torch.no_grad()
     def step(self, lr: Optional[float] = None) -> None:
+        """One update. ``lr`` overrides the groups' learning rates for this step."""
         self.step_count += 1
-        lr = self.lr if lr is None else lr
         grads = self._reduce_grads()
         inv_dp = 1.0 / self.dp_size
         if self.max_grad_norm is not None and self.max_grad_norm > 0:
@@ -208,11 +211,12 @@ class FlatAdamW:
             torch.mul(coef, inv_dp, out=self._scale)
         else:
             self._scale.fill_(inv_dp)
-        for buf, sh, g, wd in zip(self.buffers, self.shards, grads, self.group_wd):
+        for buf, sh, g, wd, pg in zip(self.buffers, self.shards, grads, self.group_wd, self.param_groups):
             pb = buf.param_data[sh["lo"]: sh["hi"]]
             bf16_out = pb if pb.dtype == torch.bfloat16 else None
-            ops.adamw_flat_(sh["master"], sh["exp_avg"], sh["exp_avg_sq"], g, lr=lr, beta1=self.betas[0],
-                            beta2=self.betas[1], eps=self.eps, weight_decay=wd, step=self.step_count,
+            glr = float(pg["lr"]) if lr is None else float(lr)
+            ops.adamw_flat_(sh["master"], sh["exp_avg"], sh["exp_avg_sq"], g, lr=glr, beta1=self.betas[0],
+                            beta2=self.betas[1], eps=self.eps, weight_decay=float(pg["weight_decay"]), step=self.step_count,
                             param_bf16=bf16_out, grad_scale=self._scale)
             if bf16_out is None:
                 pb.copy_(sh["master"])
@@ -221,6 +225,39 @@ class FlatAdamW:
 
     def state_tensors(self) -> list[dict]:
         return self.shards
+
+    # ------------------------------------------------------------------ checkpoint state
+    def state_dict(self) -> dict:
+        """This rank's optimizer state: fp32 master shard and moments per buffer, step, group LRs."""
+        return {"format": "flat_adamw_v1", "step_count": self.step_count, "strategy": self.strategy,
+                "dp_size": self.dp_size, "dp_rank": self.dp_rank,
+                "buffers": [{"name": b.name, "numel": b.numel, "lo": sh["lo"], "hi": sh["hi"],
+                             "master": sh["master"].detach().cpu().clone(),
+                             "exp_avg": sh["exp_avg"].detach().cpu().clone(),
+                             "exp_avg_sq": sh["exp_avg_sq"].detach().cpu().clone()}
+                            for b, sh in zip(self.buffers, self.shards)],
+                "param_groups": [{"lr": g["lr"], "weight_decay": g["weight_decay"]} for g in self.param_groups]}
+
+    @torch.no_grad()
+    def load_state_dict(self, state: dict) -> None:
+        if state.get("format") != "flat_adamw_v1":
+            raise ValueError("not a FlatAdamW state dict")
+        if len(state["buffers"]) != len(self.buffers):
+            raise ValueError("optimizer state has a different number of buffers")
+        for b, sh, st in zip(self.buffers, self.shards, state["buffers"]):
+            if st["numel"] != b.numel or (st["lo"], st["hi"]) != (sh["lo"], sh["hi"]):
+                raise ValueError(f"buffer {b.name}: layout or sharding differs from the checkpoint")
+            sh["master"].copy_(st["master"])
+            sh["exp_avg"].copy_(st["exp_avg"])
+            sh["exp_avg_sq"].copy_(st["exp_avg_sq"])
+            b.param_data[sh["lo"]: sh["hi"]].copy_(sh["master"])
+            if self.strategy != "no_shard" and self.dp_size > 1:
+                dist.all_gather_into_tensor(b.param_data, b.param_data[sh["lo"]: sh["hi"]].clone(),
+                                            group=self.dp_group)
+        self.step_count = int(state["step_count"])
+        for g, st in zip(self.param_groups, state["param_groups"]):
+            g["lr"] = float(st["lr"])
+            g["weight_decay"] = float(st["weight_decay"])
 
 
 def split_decay_groups(model: torch.nn.Module, weight_decay: float, *, split_tp_replicated: bool = False) -> list[dict]:

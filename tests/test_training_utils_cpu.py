@@ -1,0 +1,162 @@
+"""Scheduler, loss module, optimizer factory, dataset, monitoring math, model report and Trainer (CPU)."""
+import math
+import os
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+from nano_train_b200 import monitoring as mon
+from nano_train_b200.config import Config, ModelConfig, TrainingConfig, _NoOpPrecisionResolver
+from nano_train_b200.dataset import SyntheticTokenDataset, TextDataset, create_dataloader
+from nano_train_b200.losses import CrossEntropyLoss
+from nano_train_b200.models.transformer import TransformerModel, llama3_8b_config
+from nano_train_b200.optimizer import create_optimizer
+from nano_train_b200.scheduler import CosineAnnealingScheduler
+from nano_train_b200.trainer import Trainer
+from nano_train_b200.utils.model_info import ParallelismAssumptions, dump_model_info, estimate
+
+
+def _tiny_cfg(**kw):
+    d = dict(param_dtype=torch.float32, param_device=torch.device("cpu"), precision_resolver=_NoOpPrecisionResolver(),
+             hidden_size=32, num_layers=2, num_attention_heads=4, intermediate_size=64, vocab_size=64,
+             max_position_embeddings=64, dropout=0.0)
+    d.update(kw)
+    return ModelConfig(**d)
+
+
+def test_cosine_schedule():
+    p = torch.nn.Parameter(torch.zeros(1))
+    opt = torch.optim.SGD([p], lr=1.0)
+    s = CosineAnnealingScheduler(opt, warmup_steps=4, max_steps=12, min_lr=0.1)
+    lrs = [s.step() for _ in range(14)]
+    assert lrs[:4] == [0.25, 0.5, 0.75, 1.0]
+    assert abs(lrs[7] - (0.1 + 0.45 * (1 + math.cos(math.pi * 0.5)))) < 1e-12
+    assert abs(lrs[11] - 0.1) < 1e-12 and abs(lrs[13] - 0.1) < 1e-12
+    st = s.state_dict()
+    s2 = CosineAnnealingScheduler(opt, 4, 12, 0.1)
+    s2.load_state_dict(st)
+    assert s2.get_lr() == s.get_lr() and opt.param_groups[0]["lr"] == s.get_lr()
+    with pytest.raises(ValueError):
+        CosineAnnealingScheduler(opt, 12, 12)
+
+
+def test_cross_entropy_module():
+    torch.manual_seed(0)
+    logits, t = torch.randn(2, 3, 9), torch.randint(0, 9, (2, 3))
+    t[1, 1] = -100
+    torch.testing.assert_close(CrossEntropyLoss()(logits, t), F.cross_entropy(logits.reshape(-1, 9), t.reshape(-1)))
+    assert CrossEntropyLoss(reduction="none")(logits, t).shape == (2, 3)
+    with pytest.raises(ValueError):
+        CrossEntropyLoss()(logits, t[:, :2])
+
+
+def test_create_optimizer_groups_and_step():
+    torch.manual_seed(1)
+    model = TransformerModel(_tiny_cfg())
+    opt = create_optimizer(model, 1e-2, 0.1)
+    names = {n for n, _ in model.named_parameters()}
+    nd = {id(p) for g in opt.param_groups if g["weight_decay"] == 0.0 for p in g["params"]}
+    for n, p in model.named_parameters():
+        expect_nd = "bias" in n.lower() or "ln_" in n.lower()
+        assert (id(p) in nd) == expect_nd, n
+    ids = torch.randint(0, 64, (2, 8))
+    before = {n: p.detach().clone() for n, p in model.named_parameters()}
+    model.forward_loss(ids, ids).backward()
+    opt.step()
+    assert any(not torch.equal(before[n], p) for n, p in model.named_parameters())
+    st = opt.state_dict()
+    opt2 = create_optimizer(TransformerModel(_tiny_cfg()), 1e-2, 0.1)
+    opt2.load_state_dict(st)
+    assert opt2.step_count == 1
+    assert names
+
+
+def test_text_dataset(tmp_path):
+    p = tmp_path / "t.txt"
+    p.write_text("hello world, hello b200!" * 3)
+    ds = TextDataset(str(p), max_seq_length=9)
+    assert ds.pad_id == 0 and ds.chars[0] == "<pad>"
+    item = ds[1]
+    assert item["input_ids"].shape == (8,) and item["labels"].shape == (8,)
+    assert torch.equal(item["input_ids"][1:], item["labels"][:-1])
+    assert len(ds) == (len("hello world, hello b200!" * 3) - 9) // 4 + 1
+    short = tmp_path / "s.txt"
+    short.write_text("abc")
+    it = TextDataset(str(short), max_seq_length=8)[0]
+    assert (it["labels"] == -100).sum() == 5
+    dl = create_dataloader(ds, 4)
+    assert next(iter(dl))["input_ids"].shape == (4, 8)
+
+
+def test_monitoring_math():
+    assert mon.resolve_sentinel_blocks(12) == (0, 6, 11)
+    assert mon.resolve_sentinel_blocks(1) == (0,)
+    assert mon.resolve_sentinel_blocks(4, [5, 1, 1]) == (1,)
+    assert mon.clip_coef(10.0, 1.0) == pytest.approx(1.0 / (10.0 + 1e-6))
+    assert mon.clip_coef(0.5, 1.0) == 1.0 and mon.clip_coef(3.0, 0.0) == 1.0
+    assert mon.global_update_ratio(0.1, grad_norm_pre_clip=2.0, clip_coef_value=0.5, param_norm=4.0) == \
+        pytest.approx(0.025)
+    assert mon.achieved_tflops(1e3, 8_000_000_000) == pytest.approx(48.0)
+    assert mon.mfu(500.0, 2000.0) == 0.25
+    h1 = mon.eval_artifact_hash(input_ids_bytes=b"ab", labels_bytes=b"cd", input_dtype="torch.int64",
+                                labels_dtype="torch.int64", input_shape=(1, 2), labels_shape=(1, 2), vocab_size=10,
+                                max_seq_length=3, seed=1)
+    h2 = mon.eval_artifact_hash(input_ids_bytes=b"ab", labels_bytes=b"ce", input_dtype="torch.int64",
+                                labels_dtype="torch.int64", input_shape=(1, 2), labels_shape=(1, 2), vocab_size=10,
+                                max_seq_length=3, seed=1)
+    assert h1 != h2 and len(h1) == 64
+
+
+def test_model_report_llama8b(tmp_path):
+    model = TransformerModel(llama3_8b_config(param_device=torch.device("meta"), sequence_parallel=False))
+    info = dump_model_info(model, str(tmp_path / "r.md"), batch=8, seq_len=4096,
+                           parallel=ParallelismAssumptions(tp=8))
+    assert 8.0e9 < info.total_params < 8.1e9
+    train = next(m for m in info.modes if m.mode == "train")
+    assert train.flops == pytest.approx(6 * 32768 * (info.total_params - 128256 * 4096), rel=0.08)
+    assert train.net_bytes > 0
+    assert os.path.exists(tmp_path / "r.md") and os.path.exists(tmp_path / "r.json")
+
+
+def test_trainer_runs_and_checkpoints(tmp_path):
+    torch.manual_seed(0)
+    mcfg = _tiny_cfg()
+    cfg = Config(model=mcfg, training=TrainingConfig(batch_size=4, micro_batch_size=2, learning_rate=3e-3,
+                                                     max_steps=12, warmup_steps=2, log_steps=4, eval_steps=6,
+                                                     save_steps=6, clip_grad=1.0),
+                 output_dir=str(tmp_path / "out"), log_dir=str(tmp_path / "logs"))
+    cfg.monitoring.probe_steps = 6
+    cfg.monitoring.update_ratio_steps = 4
+    cfg.monitoring.opt_state_check_steps = 4
+    ds = SyntheticTokenDataset(32, 16, 64, seed=0)
+    tr = Trainer(TransformerModel(mcfg), cfg, create_dataloader(ds, 4), "cpu",
+                 val_loader=create_dataloader(ds, 4, shuffle=False))
+    out = tr.train()
+    assert out["step"] == 12 and math.isfinite(out["loss"]) and "eval" in out
+    ck = tmp_path / "out" / "checkpoint-step-12"
+    for f in ("model.pt", "optimizer.pt", "scheduler.pt", "config.json", "trainer_state.json"):
+        assert (ck / f).exists(), f
+    tr2 = Trainer(TransformerModel(mcfg), cfg, create_dataloader(ds, 4), "cpu")
+    assert tr2.load_checkpoint(str(ck)) == 12
+    for (n, a), (_, b) in zip(tr.model.state_dict().items(), tr2.model.state_dict().items()):
+        torch.testing.assert_close(a, b, msg=n)
+    assert tr2.scheduler.current_step == 12
+
+
+@pytest.mark.parametrize("script,args,expect", [
+    ("examples/train_tp.py", ["--max_steps", "12", "--log_every", "5"], "step 10"),
+    ("examples/train_ddp.py", ["--epochs", "1", "--num_samples", "128"], "mean loss"),
+])
+def test_examples_via_launcher(script, args, expect):
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    cmd = [sys.executable, "examples/launch.py", "--world-size", "2", "--backend", "gloo", "--script", script,
+           "--script-args"] + args
+    env = dict(os.environ, OMP_NUM_THREADS="1", MASTER_ADDR="127.0.0.1")
+    p = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert expect in p.stdout
