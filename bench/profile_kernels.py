@@ -10,6 +10,7 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   gemm_wgrad    4096 x 14336 x 4096 with M-major A / N-major B (weight gradient)
   attn_fwd      flash attention fwd, B=1 S=4096 32q/8kv heads d=128 causal
   attn_bwd      flash attention bwd, same shape
+  attn_fwd_tc   tcgen05 flash attention fwd, same shape
   rmsnorm_bwd   RMSNorm backward 8192 x 4096 bf16
   adamw         fused flat AdamW over 64M fp32 elements
   swiglu        SwiGLU fwd 8192 x 14336
@@ -43,6 +44,10 @@ def main():
         dy, x = torch.randn(4096, 14336, **bf), torch.randn(4096, 4096, **bf)
         dw = torch.zeros(14336, 4096, device=dev, dtype=torch.float32)
         fn = lambda: C.gemm_bf16(dy, x, dw, None, True, True, True, 1.0)  # noqa: E731
+    elif a.case == "attn_fwd_tc":
+        qkv = torch.randn(1, 4096, 48, 128, **bf)
+        q, k, v = qkv[:, :, :32], qkv[:, :, 32:40], qkv[:, :, 40:]
+        fn = lambda: C.flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)  # noqa: E731
     elif a.case in ("attn_fwd", "attn_bwd"):
         q = torch.randn(1, 4096, 32, 128, **bf)
         k = torch.randn(1, 4096, 8, 128, **bf)

@@ -59,6 +59,9 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
                                        const at::Tensor& v, const at::Tensor& out, const at::Tensor& lse, double scale,
                                        bool causal, const c10::optional<at::Tensor>& dq,
                                        const c10::optional<at::Tensor>& dk, const c10::optional<at::Tensor>& dv);
+// attention_tc.cu
+std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
+                                          bool causal);
 // quant.cu
 std::vector<at::Tensor> fp8_quantize(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
 at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
@@ -105,6 +108,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_bwd", &ntb::flash_attn_bwd, py::arg("dout"), py::arg("q"), py::arg("k"), py::arg("v"),
         py::arg("out"), py::arg("lse"), py::arg("scale"), py::arg("causal"), py::arg("dq") = py::none(),
         py::arg("dk") = py::none(), py::arg("dv") = py::none());
+  m.def("flash_attn_fwd_tc", &ntb::flash_attn_fwd_tc);
   m.def("fp8_quantize", &ntb::fp8_quantize);
   m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
   m.def("fp8_dequantize", &ntb::fp8_dequantize);

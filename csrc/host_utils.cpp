@@ -107,6 +107,27 @@ void make_tma_2d(CUtensorMap* out, void* base, CUtensorMapDataType dtype, int el
               " ld=", ld, " box=", box0, "x", box1);
 }
 
+void make_tma_4d_bf16(CUtensorMap* out, const void* base, const int64_t (&dims)[4], const int64_t (&strides)[3],
+                      const int (&box)[4]) {
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(out) & 63) == 0, "tensor map storage must be 64-byte aligned");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(base) & 15) == 0, "tensor map base must be 16-byte aligned");
+  cuuint64_t d[4], st[3];
+  cuuint32_t bx[4], estr[4] = {1, 1, 1, 1};
+  for (int i = 0; i < 4; ++i) {
+    d[i] = static_cast<cuuint64_t>(dims[i]);
+    bx[i] = static_cast<cuuint32_t>(box[i]);
+  }
+  for (int i = 0; i < 3; ++i) {
+    TORCH_CHECK((strides[i] * 2) % 16 == 0, "tensor map strides must be multiples of 16 bytes");
+    st[i] = static_cast<cuuint64_t>(strides[i] * 2);
+  }
+  bind_current_context();
+  CUresult r = encode_fn()(out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), d, st, bx, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "cuTensorMapEncodeTiled (4-D) failed (", static_cast<int>(r), ")");
+}
+
 void make_tma_2d_bf16(CUtensorMap* out, void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1) {
   make_tma_2d(out, base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, d0, d1, ld, box0, box1, CU_TENSOR_MAP_SWIZZLE_128B);
 }

@@ -53,6 +53,9 @@ void bind_current_context();
 // 2-D TMA descriptor for a bf16 matrix with inner extent d0 (contiguous),
 // outer extent d1, row pitch ld (elements), box box0 x box1, 128-byte swizzle.
 void make_tma_2d_bf16(CUtensorMap* out, void* base, int64_t d0, int64_t d1, int64_t ld, int box0, int box1);
+// bf16, 128-byte swizzle; dims innermost first, strides (in elements) of dims 1..3.
+void make_tma_4d_bf16(CUtensorMap* out, const void* base, const int64_t (&dims)[4], const int64_t (&strides)[3],
+                      const int (&box)[4]);
 
 // Same for an arbitrary element size in bytes with a chosen swizzle.
 void make_tma_2d(CUtensorMap* out, void* base, CUtensorMapDataType dtype, int elem_bytes, int64_t d0, int64_t d1,

@@ -18,6 +18,14 @@ from ._ext import ext
 _KERNEL_HEAD_DIMS = {(64, 64), (128, 128), (192, 128)}
 
 
+def _fwd(q, k, v, scale: float, causal: bool):
+    """Forward kernel choice: the tcgen05 kernel for head dim 128, the mma.sync kernel otherwise."""
+    C = ext()
+    if q.shape[-1] == 128 and v.shape[-1] == 128:
+        return C.flash_attn_fwd_tc(q, k, v, float(scale), bool(causal))
+    return C.flash_attn_fwd(q, k, v, float(scale), bool(causal))
+
+
 def _kernel_ok(q, k, v) -> bool:
     return (q.is_cuda and q.dtype == torch.bfloat16 and (q.shape[-1], v.shape[-1]) in _KERNEL_HEAD_DIMS
             and hasattr(ext(), "flash_attn_fwd"))
@@ -50,7 +58,7 @@ def attention_reference(q, k, v, causal=True, scale=None, mask=None):
 class _FlashAttnFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, scale, causal):
-        o, lse = ext().flash_attn_fwd(q, k, v, float(scale), bool(causal))
+        o, lse = _fwd(q, k, v, scale, causal)
         ctx.save_for_backward(q, k, v, o, lse)
         ctx.scale, ctx.causal = scale, causal
         return o
@@ -116,7 +124,7 @@ class _QKVAttentionFn(torch.autograd.Function):
             C.rope_(kv, None, off, rope_dim, S, float(rope_theta), MODES[rope_mode], False)
         ctx.mark_dirty(qkv)
         q4, k4, v4 = _split4(q2, B, S, nq, nkv, dqk, dv)
-        o, lse = C.flash_attn_fwd(q4, k4, v4, float(scale), bool(causal))
+        o, lse = _fwd(q4, k4, v4, scale, causal)
         ctx.save_for_backward(qkv, o, lse)
         ctx.meta = (B, S, nq, nkv, dqk, dv, scale, rope_dim, rope_theta, rope_mode, causal)
         return qkv, o.view(B, S, nq * dv)

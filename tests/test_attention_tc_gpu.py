@@ -1,0 +1,49 @@
+"""tcgen05 flash-attention forward (head dim 128) vs fp32 PyTorch and the mma.sync kernel."""
+import pytest
+import torch
+
+from nano_train_b200.ops.attention import attention_reference
+
+pytestmark = pytest.mark.gpu
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / b.float().norm()).item()
+
+
+@pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 8, 2, False),
+                                               (1, 1024, 8, 8, True), (1, 130, 2, 1, False)])
+def test_flash_fwd_tc_matches_reference(B, S, hq, hkv, causal):
+    from nano_train_b200.ops._ext import check_status, ext
+
+    torch.manual_seed(B * 1000 + S + hq)
+    dev = torch.device("cuda", 0)
+    qkv = torch.randn(B, S, hq + 2 * hkv, 128, device=dev, dtype=torch.bfloat16)  # fused-projection layout
+    q, k, v = qkv[:, :, :hq], qkv[:, :, hq:hq + hkv], qkv[:, :, hq + hkv:]
+    scale = 128 ** -0.5
+    o, lse = ext().flash_attn_fwd_tc(q, k, v, scale, causal)
+    torch.cuda.synchronize()
+    check_status(0)
+    ref = attention_reference(q.float(), k.float(), v.float(), causal=causal, scale=scale)
+    assert _rel(o, ref) < 1e-2
+    o2, lse2 = ext().flash_attn_fwd(q, k, v, scale, causal)
+    assert _rel(o, o2) < 1e-2
+    torch.testing.assert_close(lse, lse2, rtol=1e-3, atol=1e-3)
+
+
+def test_flash_fwd_tc_large_scores_rescale_path():
+    """Scores with a growing max along the keys exercise the lazy O correction."""
+    from nano_train_b200.ops._ext import check_status, ext
+
+    torch.manual_seed(7)
+    dev = torch.device("cuda", 0)
+    S = 640
+    q = torch.randn(1, S, 2, 128, device=dev) * 4
+    k = torch.randn(1, S, 2, 128, device=dev) * torch.linspace(0.2, 3.0, S, device=dev)[None, :, None, None]
+    v = torch.randn(1, S, 2, 128, device=dev)
+    q, k, v = (t.to(torch.bfloat16) for t in (q, k, v))
+    o, lse = ext().flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)
+    torch.cuda.synchronize()
+    check_status(0)
+    ref = attention_reference(q.float(), k.float(), v.float(), causal=True, scale=128 ** -0.5)
+    assert _rel(o, ref) < 1e-2
