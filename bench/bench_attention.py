@@ -50,8 +50,18 @@ def main():
         f = fl * (1 if causal else 2)
         t_tc = t_ms(lambda: C.flash_attn_fwd_tc(q, k, v, sc, causal))
         t_old = t_ms(lambda: C.flash_attn_fwd(q, k, v, sc, causal))
-        rows.append(dict(causal=causal, S=S, H=H, HK=HK, tc_ms=t_tc, mma_sync_ms=t_old,
+        rows.append(dict(kind="fwd", causal=causal, S=S, H=H, HK=HK, tc_ms=t_tc, mma_sync_ms=t_old,
                          tc_tflops=f / t_tc / 1e9, mma_sync_tflops=f / t_old / 1e9, speedup=t_old / t_tc))
+        print(json.dumps(rows[-1]), flush=True)
+        o, lse = C.flash_attn_fwd_tc(q, k, v, sc, causal)
+        do = torch.randn_like(o)
+        t_tc = t_ms(lambda: C.flash_attn_bwd(do, q, k, v, o, lse, sc, causal))
+        os.environ["NTB_ATTN_BWD_LEGACY"] = "1"
+        t_old = t_ms(lambda: C.flash_attn_bwd(do, q, k, v, o, lse, sc, causal))
+        del os.environ["NTB_ATTN_BWD_LEGACY"]
+        fb = 2.5 * f
+        rows.append(dict(kind="bwd", causal=causal, S=S, H=H, HK=HK, tc_ms=t_tc, mma_sync_ms=t_old,
+                         tc_tflops=fb / t_tc / 1e9, mma_sync_tflops=fb / t_old / 1e9, speedup=t_old / t_tc))
         print(json.dumps(rows[-1]), flush=True)
     check_status(0)
 

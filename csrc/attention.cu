@@ -22,12 +22,19 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <torch/extension.h>
 
+#include <cstdlib>
+
 #include "common.cuh"
 #include "host_utils.h"
 
 namespace ntb {
 
 using bf16 = __nv_bfloat16;
+
+// tcgen05 backward for head dim 128 (attention_tc.cu).
+void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+                              const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dk,
+                              at::Tensor& dv, double scale, bool causal);
 
 // ---------------------------------------------------------------- helpers
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g, bool valid) {
@@ -711,6 +718,10 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   p.dk = reinterpret_cast<bf16*>(dk.data_ptr());
   p.dv = reinterpret_cast<bf16*>(dv.data_ptr());
   bool launched = false;
+  if (DQK == 128 && DV == 128 && std::getenv("NTB_ATTN_BWD_LEGACY") == nullptr) {
+    flash_attn_bwd_tc_launch(q, k, v, dout, lse, delta, dq_acc, dk, dv, scale, causal);
+    launched = true;
+  }
 #define NTB_BWD(DQ, DVV)                                                             \
   if (!launched && DQK == DQ && DV == DVV) {                                         \
     using Cfg = BwdCfg<DQ, DVV>;                                                     \

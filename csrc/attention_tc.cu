@@ -390,4 +390,375 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor&
   return {o, lse};
 }
 
+
+// ================================================================== backward
+// One CTA per (128-key block, kv head, batch), 192 threads; the CTA loops over the
+// query heads of its GQA group and the query blocks at or after the key block
+// (causal) and accumulates dK and dV in TMEM:
+//   per query block i:  S^T = K Q_i^T   (TMEM cols   0..127, lanes = keys)
+//                       dP^T = V dO_i^T (TMEM cols 128..255)
+//   threads (one per key row): P^T = 2^(S^T * scale_log2 - lse) -> smem (bf16)
+//                       dV += P^T dO_i  (cols 384..511)
+//   threads: dS^T = P^T (dP^T - delta) -> smem (bf16)
+//                       dK += dS^T Q_i  (cols 256..383)
+//                       dQ_i = dS K     (cols 0..127, lanes = queries; A = dS^T read MN-major)
+//   threads (one per query row): dQ_i added into the fp32 accumulator with vector
+//   reductions (the softmax scale is applied when it is converted to bf16).
+// Shared memory: K, V resident (32 KB each), Q_i, dO_i (32 KB each), P^T, dS^T
+// (32 KB each); every tile is two 16 KB [128 x 64] boxes with 128-byte swizzle.
+namespace attn_tc_bwd {
+constexpr int BM = 128, BN = 128, D = 128;
+constexpr int TILE = BM * D * 2, BOX = TILE / 2;
+constexpr int S_K = 0, S_V = S_K + TILE, S_Q = S_V + TILE, S_DO = S_Q + TILE, S_P = S_DO + TILE, S_DS = S_P + TILE;
+constexpr int S_LSE = S_DS + TILE;            // float[2][128] lse, float[2][128] delta (by iteration parity)
+constexpr int S_BAR = S_LSE + 4 * 128 * 4;
+constexpr int SMEM_BYTES = 1024 + S_BAR + 256;
+constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DK = 256, COL_DV = 384, TMEM_COLS = 512;
+}  // namespace attn_tc_bwd
+
+struct AttnTcBwdParams {
+  const float* lse;    // [B, Hq, S] (log2 domain)
+  const float* delta;  // [B, Hq, S]
+  float* dq_acc;       // [B, Hq, S, D] fp32, unscaled dS K
+  __nv_bfloat16* dk;   // strided [B, S, Hkv, D]
+  __nv_bfloat16* dv;
+  int64_t dk_sb, dk_ss, dk_sh, dv_sb, dv_ss, dv_sh;
+  int B, S, Hq, Hkv;
+  float scale, scale_log2;
+  int causal;
+  int* status;
+};
+
+__device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(192, 1)
+    flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                        AttnTcBwdParams p) {
+  using namespace attn_tc_bwd;
+  using attn_tc::ex2_approx;
+  using attn_tc::warp_wait;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;
+  uint64_t* do_full = bars + 2;
+  uint64_t* q_free = bars + 3;
+  uint64_t* do_free = bars + 4;
+  uint64_t* s_full = bars + 5;   // S^T and dP^T ready
+  uint64_t* p_ready = bars + 6;  // P^T in smem (128 arrivals)
+  uint64_t* ds_ready = bars + 7; // dS^T in smem (128 arrivals)
+  uint64_t* dq_full = bars + 8;
+  uint64_t* dq_free = bars + 9;  // dQ read back (128 arrivals)
+  uint64_t* kv_done = bars + 10;
+  uint64_t* stats_ready = bars + 11;  // lse/delta of the iteration written (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  float* s_lse_all = reinterpret_cast<float*>(smem + S_LSE);  // [2][128]
+  float* s_delta_all = s_lse_all + 256;                        // [2][128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = blockIdx.x;  // heaviest (lowest) key blocks first
+  const int hk = blockIdx.y, b = blockIdx.z;
+  const int group = p.Hq / p.Hkv;
+  const int k0 = kb * BN;
+  const int nqb = (p.S + BM - 1) / BM;
+  const int qb_first = p.causal ? kb : 0;
+  const int per_head = nqb - qb_first;
+  const int iters = group * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    mbar_init(q_full, 1);
+    mbar_init(do_full, 1);
+    mbar_init(q_free, 1);
+    mbar_init(do_free, 1);
+    mbar_init(s_full, 1);
+    mbar_init(p_ready, 128);
+    mbar_init(ds_ready, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(kv_done, 1);
+    mbar_init(stats_ready, 128);
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(kv_full, 2 * TILE);
+      for (int c = 0; c < 2; ++c) {
+        tma_load_4d(smem + S_K + c * BOX, &tmK, kv_full, c * 64, k0, hk, b);
+        tma_load_4d(smem + S_V + c * BOX, &tmV, kv_full, c * 64, k0, hk, b);
+      }
+      for (int it = 0; it < iters; ++it) {
+        const int h = hk * group + it / per_head;
+        const int q0 = (qb_first + it % per_head) * BM;
+        const uint32_t par = static_cast<uint32_t>(it & 1);
+        if (!mbar_wait(q_free, par ^ 1, p.status, kStatusTimeoutProducer)) break;
+        mbar_expect_tx(q_full, TILE);
+        for (int c = 0; c < 2; ++c) tma_load_4d(smem + S_Q + c * BOX, &tmQ, q_full, c * 64, q0, h, b);
+        if (!mbar_wait(do_free, par ^ 1, p.status, kStatusTimeoutProducer)) break;
+        mbar_expect_tx(do_full, TILE);
+        for (int c = 0; c < 2; ++c) tma_load_4d(smem + S_DO + c * BOX, &tmDO, do_full, c * 64, q0, h, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_KK = make_idesc_f16(BM, BN, false, false);   // S^T, dP^T: both operands K-major (K = d)
+      constexpr uint32_t ID_KN = make_idesc_f16(BM, D, false, true);     // dV, dK: A K-major (K = q), B N-major
+      constexpr uint32_t ID_NN = make_idesc_f16(BM, D, true, true);      // dQ: A M-major (dS^T), B N-major (K)
+      const uint32_t sK = smem_u32(smem + S_K), sV = smem_u32(smem + S_V), sQ = smem_u32(smem + S_Q),
+                     sDO = smem_u32(smem + S_DO), sP = smem_u32(smem + S_P), sDS = smem_u32(smem + S_DS);
+      auto kdesc = [](uint32_t base, int kk) {  // K-major, K chunks of 64 in 16 KB boxes
+        return make_smem_desc_sw128(base + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024);
+      };
+      auto ndesc = [](uint32_t base, int kk) {  // MN-major: 64-wide MN chunks 16 KB apart, k16 = 16 rows
+        return make_smem_desc_sw128(base + kk * 2048, BOX, 1024);
+      };
+      bool ok = mbar_wait(kv_full, 0, p.status, kStatusTimeoutMma);
+      for (int it = 0; ok && it < iters; ++it) {
+        const uint32_t par = static_cast<uint32_t>(it & 1);
+        if (!mbar_wait(q_full, par, p.status, kStatusTimeoutMma) ||
+            !mbar_wait(do_full, par, p.status, kStatusTimeoutMma) ||
+            !mbar_wait(dq_free, par ^ 1, p.status, kStatusTimeoutMma))
+          break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_S, kdesc(sK, kk), kdesc(sQ, kk), ID_KK, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DP, kdesc(sV, kk), kdesc(sDO, kk), ID_KK, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+        if (!mbar_wait(p_ready, par, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DV, kdesc(sP, kk), ndesc(sDO, kk), ID_KN, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(do_free);
+        if (!mbar_wait(ds_ready, par, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DK, kdesc(sDS, kk), ndesc(sQ, kk), ID_KN, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(q_free);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_S, ndesc(sDS, kk), ndesc(sK, kk), ID_NN, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+      }
+      umma_commit(kv_done);
+      mbar_wait(kv_done, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // key row for S^T/dP^T/dK/dV; query row for dQ
+    const int key = k0 + r;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int ctid = threadIdx.x - 64;
+    uint8_t* sP = smem + S_P;
+    uint8_t* sDS = smem + S_DS;
+    bool ok = true;
+    for (int it = 0; it < iters; ++it) {
+      const int h = hk * group + it / per_head;
+      const int q0 = (qb_first + it % per_head) * BM;
+      const uint32_t par = static_cast<uint32_t>(it & 1);
+      // lse / delta of this query block (+inf / 0 beyond S: P = 0 there), double-buffered by
+      // iteration parity: a thread writes buffer it & 1 only after every compute thread arrived
+      // for iteration it - 1, i.e. finished with iteration it - 2's buffer.
+      float* s_lse = s_lse_all + (it & 1) * 128;
+      float* s_delta = s_delta_all + (it & 1) * 128;
+      {
+        const int q = q0 + ctid;
+        const int64_t o = (static_cast<int64_t>(b) * p.Hq + h) * p.S + q;
+        s_lse[ctid] = q < p.S ? p.lse[o] : INFINITY;
+        s_delta[ctid] = q < p.S ? p.delta[o] : 0.f;
+      }
+      mbar_arrive(stats_ready);
+      if (!warp_wait(stats_ready, par, p.status, kStatusTimeoutEpilogue) ||
+          !warp_wait(s_full, par, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = p.causal && q0 == k0;
+      const bool row_dead = key >= p.S;
+      // P^T row (keys x queries): kept packed in registers for dS, stored to smem for dV.
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(tmem_base + lane_addr + COL_S + c * 32, sr);
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const int qa = c * 32 + t;
+          float e0 = ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -s_lse[qa]));
+          float e1 = ex2_approx(fmaf(__uint_as_float(sr[t + 1]), p.scale_log2, -s_lse[qa + 1]));
+          if (row_dead || (diag && r > qa)) e0 = 0.f;
+          if (row_dead || (diag && r > qa + 1)) e1 = 0.f;
+          pk[(c * 32 + t) >> 1] = pack_bf16x2(e0, e1);
+        }
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        const uint4 v = make_uint4(pk[c16 * 4], pk[c16 * 4 + 1], pk[c16 * 4 + 2], pk[c16 * 4 + 3]);
+        *reinterpret_cast<uint4*>(sP + (c16 >> 3) * BOX + r * 128 + (((c16 & 7) ^ (r & 7)) << 4)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(p_ready);
+      // dS^T = P^T * (dP^T - delta)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t dr[32];
+        tmem_ld32(tmem_base + lane_addr + COL_DP + c * 32, dr);
+        uint32_t ds[16];
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const int qa = c * 32 + t;
+          const uint32_t pp = pk[qa >> 1];
+          const float d0 = bf16_lo(pp) * (__uint_as_float(dr[t]) - s_delta[qa]);
+          const float d1 = bf16_hi(pp) * (__uint_as_float(dr[t + 1]) - s_delta[qa + 1]);
+          ds[t >> 1] = pack_bf16x2(d0, d1);
+        }
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int c16 = c * 4 + q4;
+          const uint4 v = make_uint4(ds[q4 * 4], ds[q4 * 4 + 1], ds[q4 * 4 + 2], ds[q4 * 4 + 3]);
+          *reinterpret_cast<uint4*>(sDS + (c16 >> 3) * BOX + r * 128 + (((c16 & 7) ^ (r & 7)) << 4)) = v;
+        }
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+      // dQ_i (lanes = queries) -> fp32 accumulator.
+      if (!warp_wait(dq_full, par, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q = q0 + r;
+      float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.S + (q < p.S ? q : 0)) * D;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t qr[32];
+        tmem_ld32(tmem_base + lane_addr + COL_S + c * 32, qr);
+        if (q < p.S) {
+#pragma unroll
+          for (int t = 0; t < 32; t += 4)
+            red_add_v4(dst + c * 32 + t, __uint_as_float(qr[t]), __uint_as_float(qr[t + 1]),
+                       __uint_as_float(qr[t + 2]), __uint_as_float(qr[t + 3]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    // dK (scaled) and dV rows of this key block.
+    if (ok && warp_wait(kv_done, 0, p.status, kStatusTimeoutEpilogue)) {
+      tc_fence_after();
+      const bool valid = key < p.S;
+      __nv_bfloat16* dkr = p.dk + b * p.dk_sb + static_cast<int64_t>(valid ? key : 0) * p.dk_ss + hk * p.dk_sh;
+      __nv_bfloat16* dvr = p.dv + b * p.dv_sb + static_cast<int64_t>(valid ? key : 0) * p.dv_ss + hk * p.dv_sh;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col = which == 0 ? COL_DK : COL_DV;
+        const float sc = which == 0 ? p.scale : 1.f;
+        __nv_bfloat16* out = which == 0 ? dkr : dvr;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + lane_addr + col + c * 32, v);
+          if (valid) {
+#pragma unroll
+            for (int t = 0; t < 32; t += 8) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(v[t]) * sc, __uint_as_float(v[t + 1]) * sc);
+              o.y = pack_bf16x2(__uint_as_float(v[t + 2]) * sc, __uint_as_float(v[t + 3]) * sc);
+              o.z = pack_bf16x2(__uint_as_float(v[t + 4]) * sc, __uint_as_float(v[t + 5]) * sc);
+              o.w = pack_bf16x2(__uint_as_float(v[t + 6]) * sc, __uint_as_float(v[t + 7]) * sc);
+              *reinterpret_cast<uint4*>(out + c * 32 + t) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, attn_tc_bwd::TMEM_COLS);
+  }
+}
+
+// Launches the tcgen05 backward (head dim 128). dq_acc must be zeroed; dk/dv are
+// written in full (every key row of every kv head).
+void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
+                              const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dk,
+                              at::Tensor& dv, double scale, bool causal) {
+  using namespace attn_tc_bwd;
+  TORCH_CHECK(q.size(3) == D && k.size(3) == D && v.size(3) == D, "flash_attn_bwd_tc: head dim 128");
+  TORCH_CHECK(dout.is_contiguous() && dq_acc.is_contiguous(), "flash_attn_bwd_tc: contiguous dO and dq_acc");
+  const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), Hkv = k.size(2);
+  AttnTcBwdParams p{};
+  p.lse = lse.data_ptr<float>();
+  p.delta = delta.data_ptr<float>();
+  p.dq_acc = dq_acc.data_ptr<float>();
+  p.dk = reinterpret_cast<__nv_bfloat16*>(dk.data_ptr());
+  p.dv = reinterpret_cast<__nv_bfloat16*>(dv.data_ptr());
+  p.dk_sb = dk.stride(0); p.dk_ss = dk.stride(1); p.dk_sh = dk.stride(2);
+  p.dv_sb = dv.stride(0); p.dv_ss = dv.stride(1); p.dv_sh = dv.stride(2);
+  p.B = static_cast<int>(B);
+  p.S = static_cast<int>(S);
+  p.Hq = static_cast<int>(Hq);
+  p.Hkv = static_cast<int>(Hkv);
+  p.scale = static_cast<float>(scale);
+  p.scale_log2 = static_cast<float>(scale * 1.4426950408889634);
+  p.causal = causal ? 1 : 0;
+  const int dev = q.get_device();
+  p.status = device_status(dev);
+  TmaSlots& ts = tls_tma_slots();
+  const int box[4] = {64, BM, 1, 1};
+  auto map = [&](CUtensorMap* m, const at::Tensor& t) {
+    const int64_t dims[4] = {D, S, t.size(2), B};
+    const int64_t str[3] = {t.stride(1), t.stride(2), t.stride(0)};
+    make_tma_4d_bf16(m, t.data_ptr(), dims, str, box);
+  };
+  map(&ts.m[0], q);
+  map(&ts.m[1], k);
+  map(&ts.m[2], v);
+  map(&ts.m[3], dout);
+  static bool attr_done[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((S + BN - 1) / BN), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  void* args[5] = {&ts.m[0], &ts.m[1], &ts.m[2], &ts.m[3], &p};
+  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(flash_bwd_tc_kernel), grid, dim3(192), args,
+                                  static_cast<size_t>(SMEM_BYTES), at::cuda::getCurrentCUDAStream(dev)));
+  NTB_LAUNCH_CHECK(1);
+}
+
 }  // namespace ntb

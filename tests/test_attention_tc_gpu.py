@@ -47,3 +47,29 @@ def test_flash_fwd_tc_large_scores_rescale_path():
     check_status(0)
     ref = attention_reference(q.float(), k.float(), v.float(), causal=True, scale=128 ** -0.5)
     assert _rel(o, ref) < 1e-2
+
+
+@pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 8, 2, False),
+                                               (1, 130, 2, 1, True), (1, 1024, 4, 1, True)])
+def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, monkeypatch):
+    from nano_train_b200.ops._ext import check_status, ext
+
+    torch.manual_seed(S + hq * 7 + int(causal))
+    dev = torch.device("cuda", 0)
+    qkv = torch.randn(B, S, hq + 2 * hkv, 128, device=dev, dtype=torch.bfloat16)
+    q, k, v = qkv[:, :, :hq], qkv[:, :, hq:hq + hkv], qkv[:, :, hq + hkv:]
+    scale = 128 ** -0.5
+    o, lse = ext().flash_attn_fwd_tc(q, k, v, scale, causal)
+    do = torch.randn_like(o)
+    dq, dk, dv = ext().flash_attn_bwd(do, q, k, v, o, lse, scale, causal)
+    torch.cuda.synchronize()
+    check_status(0)
+    qf, kf, vf = (t.float().detach().requires_grad_(True) for t in (q, k, v))
+    attention_reference(qf, kf, vf, causal=causal, scale=scale).backward(do.float())
+    for name, g, r in (("dq", dq, qf.grad), ("dk", dk, kf.grad), ("dv", dv, vf.grad)):
+        assert _rel(g, r) < 2e-2, (name, _rel(g, r))
+    monkeypatch.setenv("NTB_ATTN_BWD_LEGACY", "1")
+    dq2, dk2, dv2 = ext().flash_attn_bwd(do, q, k, v, o, lse, scale, causal)
+    torch.cuda.synchronize()
+    for name, g, r in (("dq", dq, dq2), ("dk", dk, dk2), ("dv", dv, dv2)):
+        assert _rel(g, r) < 2e-2, (name, "vs legacy", _rel(g, r))
