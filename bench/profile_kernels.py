@@ -11,6 +11,7 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   attn_fwd      flash attention fwd, B=1 S=4096 32q/8kv heads d=128 causal
   attn_bwd      flash attention bwd, same shape
   attn_fwd_tc   tcgen05 flash attention fwd, same shape
+  attn_bwd_tc   tcgen05 flash attention bwd (the default backward for head dim 128), same shape
   rmsnorm_bwd   RMSNorm backward 8192 x 4096 bf16
   adamw         fused flat AdamW over 64M fp32 elements
   swiglu        SwiGLU fwd 8192 x 14336
@@ -48,6 +49,12 @@ def main():
         qkv = torch.randn(1, 4096, 48, 128, **bf)
         q, k, v = qkv[:, :, :32], qkv[:, :, 32:40], qkv[:, :, 40:]
         fn = lambda: C.flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)  # noqa: E731
+    elif a.case == "attn_bwd_tc":
+        qkv = torch.randn(1, 4096, 48, 128, **bf)
+        q, k, v = qkv[:, :, :32], qkv[:, :, 32:40], qkv[:, :, 40:]
+        o, lse = C.flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)
+        do = torch.randn_like(o)
+        fn = lambda: C.flash_attn_bwd(do, q, k, v, o, lse, 128 ** -0.5, True)  # noqa: E731
     elif a.case in ("attn_fwd", "attn_bwd"):
         q = torch.randn(1, 4096, 32, 128, **bf)
         k = torch.randn(1, 4096, 8, 128, **bf)
@@ -57,6 +64,7 @@ def main():
         if a.case == "attn_fwd":
             fn = lambda: C.flash_attn_fwd(q, k, v, scale, True)  # noqa: E731
         else:
+            os.environ["NTB_ATTN_BWD_LEGACY"] = "1"  # the mma.sync kernel
             do = torch.randn_like(o)
             fn = lambda: C.flash_attn_bwd(do, q, k, v, o, lse, scale, True)  # noqa: E731
     elif a.case == "rmsnorm_bwd":

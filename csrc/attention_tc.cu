@@ -579,21 +579,28 @@ __global__ void __launch_bounds__(192, 1)
     uint8_t* sP = smem + S_P;
     uint8_t* sDS = smem + S_DS;
     bool ok = true;
+    // lse / delta of one query block (+inf / 0 beyond S: P = 0 there); the next block's values
+    // are loaded one iteration ahead so the global-memory latency is off the critical path.
+    auto load_stats = [&](int itx, float& lv, float& dv) {
+      const int hx = hk * group + itx / per_head;
+      const int qx = (qb_first + itx % per_head) * BM + ctid;
+      const int64_t o = (static_cast<int64_t>(b) * p.Hq + hx) * p.S + qx;
+      lv = qx < p.S ? p.lse[o] : INFINITY;
+      dv = qx < p.S ? p.delta[o] : 0.f;
+    };
+    float next_lse = 0.f, next_delta = 0.f;
+    if (iters > 0) load_stats(0, next_lse, next_delta);
     for (int it = 0; it < iters; ++it) {
       const int h = hk * group + it / per_head;
       const int q0 = (qb_first + it % per_head) * BM;
       const uint32_t par = static_cast<uint32_t>(it & 1);
-      // lse / delta of this query block (+inf / 0 beyond S: P = 0 there), double-buffered by
-      // iteration parity: a thread writes buffer it & 1 only after every compute thread arrived
-      // for iteration it - 1, i.e. finished with iteration it - 2's buffer.
+      // Double-buffered by iteration parity: a thread writes buffer it & 1 only after every
+      // compute thread arrived for iteration it - 1, i.e. finished with iteration it - 2's buffer.
       float* s_lse = s_lse_all + (it & 1) * 128;
       float* s_delta = s_delta_all + (it & 1) * 128;
-      {
-        const int q = q0 + ctid;
-        const int64_t o = (static_cast<int64_t>(b) * p.Hq + h) * p.S + q;
-        s_lse[ctid] = q < p.S ? p.lse[o] : INFINITY;
-        s_delta[ctid] = q < p.S ? p.delta[o] : 0.f;
-      }
+      s_lse[ctid] = next_lse;
+      s_delta[ctid] = next_delta;
+      if (it + 1 < iters) load_stats(it + 1, next_lse, next_delta);
       mbar_arrive(stats_ready);
       if (!warp_wait(stats_ready, par, p.status, kStatusTimeoutEpilogue) ||
           !warp_wait(s_full, par, p.status, kStatusTimeoutEpilogue)) {

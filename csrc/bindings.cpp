@@ -27,6 +27,8 @@ namespace ntb {
 // gemm.cu
 void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const c10::optional<at::Tensor>& bias,
                bool a_mn, bool b_mn, bool accumulate, double alpha);
+void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& offsets,
+                       int64_t mode, bool b_mn, bool accumulate);
 // ops.cu
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
                                     const at::Tensor& w, double eps);
@@ -89,6 +91,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_bf16", &ntb::gemm_bf16, "tcgen05 bf16 GEMM", py::arg("a"), py::arg("b"), py::arg("out"),
         py::arg("bias") = py::none(), py::arg("a_mn") = false, py::arg("b_mn") = false, py::arg("accumulate") = false,
         py::arg("alpha") = 1.0);
+  m.def("gemm_grouped_bf16", &ntb::gemm_grouped_bf16, "grouped (mixture-of-experts) tcgen05 GEMM", py::arg("a"),
+        py::arg("b"), py::arg("out"), py::arg("offsets"), py::arg("mode"), py::arg("b_mn") = false,
+        py::arg("accumulate") = false);
   m.def("rmsnorm_fwd", &ntb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &ntb::rmsnorm_bwd);
   m.def("layernorm_fwd", &ntb::layernorm_fwd);

@@ -42,6 +42,11 @@ struct GemmParams {
   int accumulate;  // 1: C = result + C (C read in its own dtype)
   int c_f32;       // 1: C is fp32, else bf16
   int* status;
+  // Grouped (mixture-of-experts) modes, see gemm_grouped_bf16:
+  const int* offsets;  // [groups + 1] row offsets, multiples of 128
+  int groups;
+  int b_group_rows;    // rows of one group's slice of the stacked B (mode 1)
+  long m_limit;        // rows of C that exist (mode 2: per-group output rows)
 };
 
 template <int BN>
@@ -56,6 +61,27 @@ struct GemmCfg {
   static constexpr int SMEM_BYTES =
       1024 /*align slack*/ + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256 /*barriers*/;
 };
+
+// Grouped GEMM modes (template parameter GM):
+//   0  plain GEMM
+//   1  M-grouped (expert forward / input gradient): rows of A and C are grouped by
+//      expert, each group padded to a multiple of 128 rows; B is a stack of per-expert
+//      matrices and a tile reads the slice of the expert that owns its first row.
+//   2  K-grouped (expert weight gradient): the output is a stack of per-expert
+//      [M, N] blocks; tile = (expert, m, n) and K runs over that expert's rows.
+struct TileInfo {
+  int mb, nb, group, kb0, nkb;
+};
+
+__device__ __forceinline__ int group_of_row(const int* offsets, int groups, int row) {
+  int lo = 0, hi = groups - 1;  // last g with offsets[g] <= row
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(offsets + mid) <= row) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mb, int& nb) {
   constexpr int GROUP = 16;
@@ -77,7 +103,7 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 // final rounding. m0: first row of the warp; n0: first column of the tile.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, const GemmParams& p, long m0, int n0,
-                                              bool vec_ok) {
+                                              bool vec_ok, long m_end) {
   const int lane = threadIdx.x & 31;
   const bool f32 = p.c_f32 != 0;
   const bool acc = p.accumulate != 0;
@@ -95,7 +121,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
           const int row = it * 2 + (lane >> 4), col = cg + (lane & 15) * 4;
           const long m = m0 + row;
           old[it] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (m < p.M && vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0)
+          if (m < m_end && vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0)
             old[it] = *reinterpret_cast<const float4*>(reinterpret_cast<const float*>(p.C) + m * p.ldc + col);
         }
       } else {
@@ -104,7 +130,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
           const int row = it * 4 + (lane >> 3), col = cg + (lane & 7) * 8;
           const long m = m0 + row;
           old[it] = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (m < p.M && vec_ok && col + 8 <= p.N)
+          if (m < m_end && vec_ok && col + 8 <= p.N)
             old[it] = *reinterpret_cast<const float4*>(reinterpret_cast<const __nv_bfloat16*>(p.C) + m * p.ldc + col);
         }
       }
@@ -134,7 +160,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
         const int row = it * 2 + (lane >> 4), ch = lane & 15;
         const long m = m0 + row;
         const int col = cg + ch * 4;
-        if (m >= p.M || col >= p.N) continue;
+        if (m >= m_end || col >= p.N) continue;
         float4 v = *reinterpret_cast<const float4*>(stage + row * 64 + ((ch ^ (row & 15)) * 4));
         float* dst = C + m * p.ldc + col;
         if (vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0) {
@@ -154,7 +180,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
         const int row = it * 4 + (lane >> 3), c8 = lane & 7;
         const long m = m0 + row;
         const int col = cg + c8 * 8;
-        if (m >= p.M || col >= p.N) continue;
+        if (m >= m_end || col >= p.N) continue;
         const float4 a = *reinterpret_cast<const float4*>(stage + row * 64 + (((2 * c8) ^ (row & 15)) * 4));
         const float4 b = *reinterpret_cast<const float4*>(stage + row * 64 + (((2 * c8 + 1) ^ (row & 15)) * 4));
         float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
@@ -183,7 +209,27 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
   }
 }
 
-template <int BN, bool A_MN, bool B_MN>
+template <int GM>
+__device__ __forceinline__ TileInfo tile_info(const GemmParams& p, int tile, int num_m, int num_n, int num_kb,
+                                              int BM, int BK) {
+  TileInfo t{};
+  if constexpr (GM == 2) {
+    const int per = num_m * num_n;
+    t.group = tile / per;
+    tile_coords(tile - t.group * per, num_m, num_n, t.mb, t.nb);
+    const int r0 = __ldg(p.offsets + t.group), r1 = __ldg(p.offsets + t.group + 1);
+    t.kb0 = r0 / BK;
+    t.nkb = (r1 - r0) / BK;
+  } else {
+    tile_coords(tile, num_m, num_n, t.mb, t.nb);
+    t.group = GM == 1 ? group_of_row(p.offsets, p.groups, t.mb * BM) : 0;
+    t.kb0 = 0;
+    t.nkb = num_kb;
+  }
+  return t;
+}
+
+template <int BN, bool A_MN, bool B_MN, int GM = 0>
 __global__ void __launch_bounds__(192, 1)
     gemm_bf16_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                      GemmParams p) {
@@ -206,7 +252,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
+  const int num_tiles = num_m * num_n * (GM == 2 ? p.groups : 1);
   const int num_kb = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -244,9 +290,12 @@ __global__ void __launch_bounds__(192, 1)
       for (int s = 0; s < STAGES; ++s) last_phase[s] = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        int mb, nb;
-        tile_coords(tile, num_m, num_n, mb, nb);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const TileInfo ti = tile_info<GM>(p, tile, num_m, num_n, num_kb, BM, BK);
+        const int mb = ti.mb, nb = ti.nb;
+        // Mode 1: the expert's slice of the stacked B starts at group * b_group_rows rows.
+        const int b_row0 = GM == 1 ? ti.group * p.b_group_rows : 0;
+        for (int kq = 0; kq < ti.nkb; ++kq) {
+          const int kb = ti.kb0 + kq;
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kStatusTimeoutProducer)) {
             ok = false;
             break;
@@ -261,10 +310,11 @@ __global__ void __launch_bounds__(192, 1)
             for (int j = 0; j < BM / 64; ++j) tma_load_2d(a_dst + j * 8192, &tmA, &full[stage], mb * BM + j * 64, kb * BK);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, nb * BN);
+            tma_load_2d(b_dst, &tmB, &full[stage], kb * BK, b_row0 + nb * BN);
           } else {
 #pragma unroll
-            for (int j = 0; j < BN / 64; ++j) tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], nb * BN + j * 64, kb * BK);
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(b_dst + j * 8192, &tmB, &full[stage], nb * BN + j * 64, b_row0 + kb * BK);
           }
           filled_mask |= 1u << stage;
           last_phase[stage] = phase;
@@ -286,10 +336,11 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int tile_nkb = GM == 2 ? tile_info<GM>(p, tile, num_m, num_n, num_kb, BM, BK).nkb : num_kb;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = 0; kb < tile_nkb; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
             ok = false;
             break;
@@ -332,12 +383,19 @@ __global__ void __launch_bounds__(192, 1)
     float* stage = reinterpret_cast<float*>(stage_base + q * 8192);
     (void)row;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
-      int mb, nb;
-      tile_coords(tile, num_m, num_n, mb, nb);
+      const TileInfo ti = tile_info<GM>(p, tile, num_m, num_n, num_kb, BM, BK);
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue)) break;
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      epilogue_tile<BN>(t_row, stage, p, static_cast<long>(mb) * BM + q * 32, nb * BN, vec_ok);
+      if (GM != 2) {
+        epilogue_tile<BN>(t_row, stage, p, static_cast<long>(ti.mb) * BM + q * 32, ti.nb * BN, vec_ok, p.M);
+      } else if (ti.nkb > 0) {
+        // Expert block: rows [group * M, group * M + M) of the stacked output; an expert without
+        // rows contributes nothing (its accumulator was never written).
+        const long base = static_cast<long>(ti.group) * p.M;
+        epilogue_tile<BN>(t_row, stage, p, base + static_cast<long>(ti.mb) * BM + q * 32, ti.nb * BN, vec_ok,
+                          base + p.M);
+      }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
@@ -355,10 +413,10 @@ __global__ void __launch_bounds__(192, 1)
 
 // ------------------------------------------------------------------ host side
 
-template <int BN, bool A_MN, bool B_MN>
+template <int BN, bool A_MN, bool B_MN, int GM = 0>
 static void launch_gemm(const CUtensorMap* ta, const CUtensorMap* tb, GemmParams p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
-  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN>;
+  auto kern = gemm_bf16_kernel<BN, A_MN, B_MN, GM>;
   static bool attr_set[16] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -366,7 +424,7 @@ static void launch_gemm(const CUtensorMap* ta, const CUtensorMap* tb, GemmParams
     NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     attr_set[dev & 15] = true;
   }
-  const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN);
+  const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN) * (GM == 2 ? p.groups : 1);
   const int grid = std::min(num_tiles, num_sms(dev));
   void* args[3] = {const_cast<CUtensorMap*>(ta), const_cast<CUtensorMap*>(tb), &p};
   NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(192), args,
@@ -421,6 +479,9 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   p.accumulate = accumulate ? 1 : 0;
   p.c_f32 = out.scalar_type() == at::kFloat ? 1 : 0;
   p.status = device_status(a.get_device());
+  p.offsets = nullptr;
+  p.groups = 1;
+  p.b_group_rows = 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
   // Narrow problems waste half of a 256-wide tile: use 128.
   const bool wide = N > 128;
@@ -442,6 +503,78 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
     NTB_GEMM_CASE(128, true, true)
   }
 #undef NTB_GEMM_CASE
+}
+
+// Grouped GEMM for mixture-of-experts layers. `offsets` (int32 [G + 1], device) are the
+// row offsets of the G expert segments of the token-major operands; every offset must
+// be a multiple of 128 (segments are padded with zero rows).
+//   mode 1 (M-grouped): out[rows of g] = a[rows of g] . op(B_g)^T
+//        a: [R, K] tokens;  b: stacked [G * N, K] (b_mn=false, forward)
+//                              or [G * K, N] (b_mn=true, input gradient);  out: [R, N]
+//   mode 2 (K-grouped): out[g] (+)= a[rows of g]^T . b[rows of g]
+//        a: [R, M] (e.g. dY), b: [R, N] (e.g. X), out: stacked [G * M, N] (fp32 weight gradient)
+void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& offsets,
+                       int64_t mode, bool b_mn, bool accumulate) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda() && offsets.is_cuda(), "gemm_grouped: CUDA tensors");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_grouped: bf16 operands");
+  TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.dim() == 1 && offsets.numel() >= 2 &&
+                  offsets.is_contiguous(),
+              "gemm_grouped: int32 offsets [G + 1]");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2 && a.stride(1) == 1 && b.stride(1) == 1 &&
+                  out.stride(1) == 1,
+              "gemm_grouped: 2-D tensors with unit inner stride");
+  TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_grouped: 16-byte row strides");
+  const int G = static_cast<int>(offsets.numel() - 1);
+  GemmParams p{};
+  p.offsets = offsets.data_ptr<int>();
+  p.groups = G;
+  p.alpha = 1.f;
+  p.accumulate = accumulate ? 1 : 0;
+  p.c_f32 = out.scalar_type() == at::kFloat ? 1 : 0;
+  p.C = out.data_ptr();
+  p.ldc = out.stride(0);
+  p.bias = nullptr;
+  p.status = device_status(a.get_device());
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
+  TmaSlots& slots = tls_tma_slots();
+  if (mode == 1) {
+    TORCH_CHECK(b.size(0) % G == 0, "gemm_grouped: stacked B rows must divide by the group count");
+    const int64_t R = a.size(0), K = a.size(1);
+    const int64_t rows_g = b.size(0) / G;
+    const int64_t N = b_mn ? b.size(1) : rows_g;
+    TORCH_CHECK((b_mn ? rows_g : b.size(1)) == K, "gemm_grouped: K mismatch");
+    TORCH_CHECK(out.size(0) == R && out.size(1) == N, "gemm_grouped: out shape");
+    TORCH_CHECK(R % 128 == 0, "gemm_grouped: rows must be padded to a multiple of 128");
+    if (R == 0 || N == 0) return;
+    p.M = static_cast<int>(R);
+    p.N = static_cast<int>(N);
+    p.K = static_cast<int>(K);
+    p.b_group_rows = static_cast<int>(rows_g);
+    const bool wide = N > 128;
+    operand_map(&slots.m[0], a, false, 128);
+    operand_map(&slots.m[1], b, b_mn, wide ? 256 : 128);
+    if (wide) {
+      if (b_mn) launch_gemm<256, false, true, 1>(&slots.m[0], &slots.m[1], p, stream);
+      else launch_gemm<256, false, false, 1>(&slots.m[0], &slots.m[1], p, stream);
+    } else {
+      if (b_mn) launch_gemm<128, false, true, 1>(&slots.m[0], &slots.m[1], p, stream);
+      else launch_gemm<128, false, false, 1>(&slots.m[0], &slots.m[1], p, stream);
+    }
+    return;
+  }
+  TORCH_CHECK(mode == 2, "gemm_grouped: mode 1 or 2");
+  TORCH_CHECK(a.size(0) == b.size(0), "gemm_grouped: a and b must have the same rows");
+  const int64_t M = a.size(1), N = b.size(1);
+  TORCH_CHECK(out.size(0) == G * M && out.size(1) == N, "gemm_grouped: out must be [G * M, N]");
+  if (M == 0 || N == 0) return;
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(a.size(0));
+  const bool wide = N > 128;
+  operand_map(&slots.m[0], a, true, 128);
+  operand_map(&slots.m[1], b, true, wide ? 256 : 128);
+  if (wide) launch_gemm<256, true, true, 2>(&slots.m[0], &slots.m[1], p, stream);
+  else launch_gemm<128, true, true, 2>(&slots.m[0], &slots.m[1], p, stream);
 }
 
 }  // namespace ntb

@@ -30,6 +30,7 @@ import torch.nn.functional as F
 
 from .. import ops
 from ..layers import Dropout, Linear
+from ..ops.grouped import _StackCache, grouped_kernel_ok, grouped_swiglu_experts
 from ..precision.backends import fp8_quant_dequant, quantize_dequantize
 
 
@@ -197,6 +198,7 @@ class LocalRoutedMoE(nn.Module):
         self._last_aux_loss = torch.zeros(())
         self._last_dropped_fraction = 0.0
         self._last_token_counts = torch.zeros(num_experts, dtype=torch.long)
+        self._stack_cache = _StackCache()
 
     def _compute_capacity(self, num_tokens: int) -> int:
         if num_tokens <= 0:
@@ -225,8 +227,12 @@ class LocalRoutedMoE(nn.Module):
         ro = self.router(tokens)
         cap = self._compute_capacity(tokens.size(0))
         tok, slot, _, counts = capacity_select(ro.topk_indices, ro.topk_weights, self.num_experts, cap)
-        counts_list = counts.tolist()
-        y = run_experts_grouped(self.experts, tokens[tok], counts_list)
+        if grouped_kernel_ok(tokens, self.experts):
+            # One grouped tcgen05 GEMM per matrix over all experts, no host sync on the counts.
+            y = grouped_swiglu_experts(tokens[tok], counts, self.experts, self._stack_cache,
+                                       max_rows=ro.topk_indices.numel() + self.num_experts * 127)
+        else:
+            y = run_experts_grouped(self.experts, tokens[tok], counts.tolist())
         w = ro.topk_weights[tok, slot].unsqueeze(-1)
         out = torch.zeros_like(tokens).index_add(0, tok, (y * w).to(tokens.dtype))
         if len(self.shared_experts):
@@ -234,7 +240,7 @@ class LocalRoutedMoE(nn.Module):
             out = out + shared / float(len(self.shared_experts))
         total = ro.topk_indices.numel()
         self._last_aux_loss = ro.aux_loss
-        self._last_dropped_fraction = float((total - sum(counts_list)) / max(total, 1))
+        self._last_dropped_fraction = float((total - int(counts.sum())) / max(total, 1))
         self._last_token_counts = counts
         return out.view(B, S, H)
 
@@ -306,6 +312,7 @@ class ExpertParallelMoE(nn.Module):
         self._last_aux_loss = torch.zeros(())
         self._last_dropped_fraction = 0.0
         self._last_token_counts = torch.zeros(self.experts_per_rank, dtype=torch.long)
+        self._stack_cache = _StackCache()
 
     last_aux_loss = property(lambda self: self._last_aux_loss)
     last_dropped_fraction = property(lambda self: self._last_dropped_fraction)
@@ -359,7 +366,11 @@ class ExpertParallelMoE(nn.Module):
         keep = rank_in < capacity
         kept = o2[keep]
         kept_counts = torch.bincount(le_sorted[keep], minlength=epr)
-        y_kept = run_experts_grouped(self.experts, recv_x[kept], kept_counts.tolist())
+        if grouped_kernel_ok(recv_x, self.experts):
+            y_kept = grouped_swiglu_experts(recv_x[kept], kept_counts, self.experts, self._stack_cache,
+                                            max_rows=recv_x.shape[0] + epr * 127)
+        else:
+            y_kept = run_experts_grouped(self.experts, recv_x[kept], kept_counts.tolist())
         y_back = torch.zeros_like(recv_x).index_copy(0, kept, y_kept.to(recv_x.dtype))
         y_back = _comm_quant_dequant(y_back, self.comm_quant_granularity, self.comm_quant_rounding,
                                      self.comm_quant_backend)

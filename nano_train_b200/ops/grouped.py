@@ -1,0 +1,134 @@
+"""Grouped (mixture-of-experts) SwiGLU expert MLP on the tcgen05 grouped GEMM.
+
+Tokens routed to experts are laid out expert by expert, each expert's segment
+padded with zero rows to a multiple of 128 (``pad_segments``), so one
+persistent kernel runs every expert's GEMM (``gemm_grouped_bf16`` mode 1) and
+the weight gradients are one more launch per matrix (mode 2, K = the
+expert's rows). The per-expert ``nn.Linear`` parameters stay separate
+parameters (checkpoint keys unchanged); their stacked copies are rebuilt only
+when a parameter changed (once per optimizer step, not per micro-batch), and
+their gradients are written into ``main_grad`` when the optimizer provides
+one, otherwise returned as ordinary ``.grad``.
+
+Reference parity: src/models/moe.py:146-193 (ExpertMLP) and the per-expert
+loops of LocalRoutedMoE / ExpertParallelMoE (moe.py:456-509, 888-962).
+"""
+from __future__ import annotations
+
+import torch
+
+from ._ext import ext
+
+SEG = 128
+
+
+def pad_segments(counts: torch.Tensor, max_rows: int | None = None):
+    """Padded row offsets (int32 [E + 1], multiples of 128) and an upper bound on the rows.
+
+    ``max_rows`` (host int) avoids a device->host sync: T*K + E*127 rounded up works for any routing.
+    """
+    padded = (counts + (SEG - 1)) // SEG * SEG
+    offsets = torch.zeros(counts.numel() + 1, dtype=torch.int32, device=counts.device)
+    offsets[1:] = torch.cumsum(padded, 0).to(torch.int32)
+    if max_rows is None:
+        max_rows = int(offsets[-1])
+    return offsets, (max_rows + SEG - 1) // SEG * SEG
+
+
+def scatter_rows_to_segments(x_sorted: torch.Tensor, counts: torch.Tensor, offsets: torch.Tensor, rows: int):
+    """x_sorted [n, H] grouped by expert (counts per expert) -> zero-padded [rows, H] and the destination index."""
+    n = x_sorted.shape[0]
+    starts = torch.cumsum(counts, 0) - counts
+    expert_of = torch.repeat_interleave(torch.arange(counts.numel(), device=counts.device), counts, output_size=n)
+    dest = offsets[:-1].long()[expert_of] + (torch.arange(n, device=counts.device) - starts[expert_of])
+    out = x_sorted.new_zeros(rows, x_sorted.shape[1])
+    out.index_copy_(0, dest, x_sorted)
+    return out, dest
+
+
+class _StackCache:
+    """Stacked expert weights, rebuilt only when a source parameter changed."""
+
+    def __init__(self):
+        self.key = None
+        self.w1 = None
+        self.w2 = None
+
+    def get(self, experts):
+        params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
+        key = tuple((p.data_ptr(), p._version) for p in params)
+        if key != self.key:
+            with torch.no_grad():
+                self.w1 = torch.cat([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in experts], 0)
+                self.w2 = torch.cat([e.down_proj.weight for e in experts], 0)
+            self.key = key
+        return self.w1, self.w2
+
+
+class _GroupedSwiGLUFn(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x_pad, offsets, w1, w2, n_experts, *params):
+        C = ext()
+        R = x_pad.shape[0]
+        I2 = w1.shape[0] // n_experts
+        H = w2.shape[0] // n_experts
+        h = torch.empty(R, I2, device=x_pad.device, dtype=x_pad.dtype)
+        C.gemm_grouped_bf16(x_pad, w1, h, offsets, 1)
+        a = C.swiglu_fwd(h)
+        y = torch.empty(R, H, device=x_pad.device, dtype=x_pad.dtype)
+        C.gemm_grouped_bf16(a, w2, y, offsets, 1)
+        ctx.save_for_backward(x_pad, offsets, w1, w2, h, a)
+        ctx.n_experts = n_experts
+        ctx.params = params
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        C = ext()
+        x_pad, offsets, w1, w2, h, a = ctx.saved_tensors
+        E = ctx.n_experts
+        dy = dy.contiguous()
+        I2 = w1.shape[0] // E
+        H = w2.shape[0] // E
+        I = I2 // 2
+        da = torch.empty_like(a)
+        C.gemm_grouped_bf16(dy, w2, da, offsets, 1, b_mn=True)          # dA = dY . W2_e
+        dw2 = torch.zeros(E * H, I, device=dy.device, dtype=torch.float32)
+        C.gemm_grouped_bf16(dy, a, dw2, offsets, 2, b_mn=True)          # dW2_e = dY_e^T A_e
+        dh = C.swiglu_bwd(da, h)
+        dx = torch.empty_like(x_pad)
+        C.gemm_grouped_bf16(dh, w1, dx, offsets, 1, b_mn=True)          # dX = dH . W1_e
+        dw1 = torch.zeros(E * I2, x_pad.shape[1], device=dy.device, dtype=torch.float32)
+        C.gemm_grouped_bf16(dh, x_pad, dw1, offsets, 2, b_mn=True)      # dW1_e = dH_e^T X_e
+        grads = []
+        for e in range(E):
+            slices = (dw1[e * I2:e * I2 + I], dw1[e * I2 + I:(e + 1) * I2], dw2[e * H:(e + 1) * H])
+            for p, g in zip(ctx.params[3 * e:3 * e + 3], slices):
+                mg = getattr(p, "main_grad", None)
+                if mg is not None:
+                    mg.add_(g)
+                    grads.append(None)
+                else:
+                    grads.append(g.to(p.dtype))
+        return (dx, None, None, None, None, *grads)
+
+
+def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts, cache: _StackCache,
+                           max_rows: int | None = None) -> torch.Tensor:
+    """Apply expert e to its rows of ``x_sorted`` (rows grouped by expert, ``counts`` per expert)."""
+    offsets, rows = pad_segments(counts, max_rows)
+    x_pad, dest = scatter_rows_to_segments(x_sorted, counts, offsets, rows)
+    w1, w2 = cache.get(experts)
+    params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
+    y_pad = _GroupedSwiGLUFn.apply(x_pad, offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), *params)
+    return y_pad.index_select(0, dest)
+
+
+def grouped_kernel_ok(x: torch.Tensor, experts) -> bool:
+    if not (x.is_cuda and x.dtype == torch.bfloat16 and len(experts) > 0):
+        return False
+    e0 = experts[0]
+    if e0.gate_proj._lowbit_active() or e0.up_proj._lowbit_active() or e0.down_proj._lowbit_active():
+        return False
+    H, I = e0.gate_proj.weight.shape[1], e0.gate_proj.weight.shape[0]
+    return H % 8 == 0 and I % 8 == 0
