@@ -64,6 +64,9 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
 // attention_tc.cu
 std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
                                           bool causal);
+// gemm_fp8.cu
+void gemm_fp8_blockscaled(const at::Tensor& a_q, const at::Tensor& sa, const at::Tensor& b_q, const at::Tensor& sb,
+                          at::Tensor& out, const c10::optional<at::Tensor>& bias);
 // quant.cu
 std::vector<at::Tensor> fp8_quantize(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
 at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
@@ -114,6 +117,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("out"), py::arg("lse"), py::arg("scale"), py::arg("causal"), py::arg("dq") = py::none(),
         py::arg("dk") = py::none(), py::arg("dv") = py::none());
   m.def("flash_attn_fwd_tc", &ntb::flash_attn_fwd_tc);
+  m.def("gemm_fp8_blockscaled", &ntb::gemm_fp8_blockscaled, py::arg("a_q"), py::arg("sa"), py::arg("b_q"),
+        py::arg("sb"), py::arg("out"), py::arg("bias") = py::none());
   m.def("fp8_quantize", &ntb::fp8_quantize);
   m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
   m.def("fp8_dequantize", &ntb::fp8_dequantize);

@@ -209,8 +209,58 @@ def e4m3_stochastic_round(y: torch.Tensor, generator=None) -> torch.Tensor:
     return r.clamp(-E4M3_MAX, E4M3_MAX)
 
 
+_WQ_CACHE: dict = {}
+
+
+def _quantized_weight(w: torch.Tensor):
+    """e4m3 copy of a weight in 128 x 128 blocks, re-quantised only when the weight changed."""
+    key = id(w)
+    ent = _WQ_CACHE.get(key)
+    if ent is not None and ent[0] == (w.data_ptr(), w._version):
+        return ent[1], ent[2]
+    wq, sw = ops.ext().fp8_quantize(w.detach().contiguous(), 128, False, 0)
+    _WQ_CACHE[key] = ((w.data_ptr(), w._version), wq, sw)
+    return wq, sw
+
+
+class _FP8LinearFn(torch.autograd.Function):
+    """Forward on the block-scaled e4m3 tensor cores; straight-through backward on the
+    dequantised operands (bf16 GEMMs), with the fp8 copies saved instead of bf16 activations."""
+
+    @staticmethod
+    def forward(ctx, x2, weight, bias, stochastic, seed):
+        C = ops.ext()
+        xq, sx = C.fp8_quantize(x2.contiguous(), 1, bool(stochastic), int(seed))
+        wq, sw = _quantized_weight(weight)
+        y = torch.empty(x2.shape[0], weight.shape[0], device=x2.device, dtype=torch.bfloat16)
+        C.gemm_fp8_blockscaled(xq, sx, wq, sw, y, None if bias is None else bias.to(torch.bfloat16))
+        ctx.save_for_backward(xq, sx, wq, sw)
+        ctx.weight = weight
+        ctx.has_bias = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..ops.linear import accumulate_weight_grad, gemm
+
+        C = ops.ext()
+        xq, sx, wq, sw = ctx.saved_tensors
+        dy = dy.contiguous()
+        wdq = C.fp8_dequantize(wq, sw, 128, torch.bfloat16)
+        dx = gemm(dy, wdq, b_mn=True)
+        xdq = C.fp8_dequantize(xq, sx, 1, torch.bfloat16)
+        dw = accumulate_weight_grad(ctx.weight, dy, xdq)
+        db = dy.float().sum(0).to(torch.bfloat16) if ctx.has_bias else None
+        return dx, dw, db, None, None
+
+
 class NativeFP8Backend:
-    """e4m3 operands with fp32 tile/block scales; STE gradients in bf16/fp32."""
+    """e4m3 operands with fp32 tile/block scales; STE gradients in bf16/fp32.
+
+    On CUDA with the recipe's tile_1x128 activations and block_128x128 weights the
+    forward GEMM runs natively on the e4m3 tensor cores (``gemm_fp8_blockscaled``);
+    other granularities and CPU tensors use quantise-dequantise + bf16/fp32 GEMM.
+    """
 
     name = "native"
 
@@ -227,7 +277,19 @@ class NativeFP8Backend:
             self._weight_granularity = str(kernel_spec.weight_quant_granularity)
             self._rounding_mode = str(kernel_spec.rounding_mode)
 
+    def _native_ok(self, x, weight) -> bool:
+        return (x.is_cuda and x.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16 and ops.available()
+                and hasattr(ops.ext(), "gemm_fp8_blockscaled") and self._activation_granularity == "tile_1x128"
+                and self._weight_granularity == "block_128x128" and x.shape[-1] % 128 == 0
+                and weight.shape[0] % 8 == 0)
+
     def linear(self, input_tensor, weight, bias, module=None):
+        if self._native_ok(input_tensor, weight):
+            lead = input_tensor.shape[:-1]
+            x2 = input_tensor.reshape(-1, input_tensor.shape[-1])
+            self._seed = getattr(self, "_seed", 0) + 1
+            y = _FP8LinearFn.apply(x2, weight, bias, self._rounding_mode == "stochastic", self._seed)
+            return y.view(*lead, weight.shape[0])
         xdq = fp8_quant_dequant(input_tensor.detach(), granularity=self._activation_granularity,
                                 rounding_mode=self._rounding_mode, channel_axis=-1)
         wdq = fp8_quant_dequant(weight.detach(), granularity=self._weight_granularity,
