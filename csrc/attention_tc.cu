@@ -392,9 +392,10 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor&
 
 
 // ================================================================== backward
-// One CTA per (128-key block, kv head, batch), 192 threads; the CTA loops over the
-// query heads of its GQA group and the query blocks at or after the key block
-// (causal) and accumulates dK and dV in TMEM:
+// One CTA per (128-key block, query head, batch), 192 threads; the CTA loops over the
+// query blocks at or after the key block (causal) and accumulates its query head's
+// share of dK and dV in TMEM (for GQA the shares of the heads of one group are then
+// added with vector reductions into fp32 accumulators and converted to bf16):
 //   per query block i:  S^T = K Q_i^T   (TMEM cols   0..127, lanes = keys)
 //                       dP^T = V dO_i^T (TMEM cols 128..255)
 //   threads (one per key row): P^T = 2^(S^T * scale_log2 - lse) -> smem (bf16)
@@ -422,6 +423,8 @@ struct AttnTcBwdParams {
   float* dq_acc;       // [B, Hq, S, D] fp32, unscaled dS K
   __nv_bfloat16* dk;   // strided [B, S, Hkv, D]
   __nv_bfloat16* dv;
+  float* dk_acc;       // GQA: fp32 [B, S, Hkv, D] accumulators (one CTA per query head adds into them)
+  float* dv_acc;
   int64_t dk_sb, dk_ss, dk_sh, dv_sb, dv_ss, dv_sh;
   int B, S, Hq, Hkv;
   float scale, scale_log2;
@@ -462,13 +465,14 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int kb = blockIdx.x;  // heaviest (lowest) key blocks first
-  const int hk = blockIdx.y, b = blockIdx.z;
+  const int hq = blockIdx.y, b = blockIdx.z;
   const int group = p.Hq / p.Hkv;
+  const int hk = hq / group;
   const int k0 = kb * BN;
   const int nqb = (p.S + BM - 1) / BM;
   const int qb_first = p.causal ? kb : 0;
   const int per_head = nqb - qb_first;
-  const int iters = group * per_head;
+  const int iters = per_head;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -509,8 +513,8 @@ __global__ void __launch_bounds__(192, 1)
         tma_load_4d(smem + S_V + c * BOX, &tmV, kv_full, c * 64, k0, hk, b);
       }
       for (int it = 0; it < iters; ++it) {
-        const int h = hk * group + it / per_head;
-        const int q0 = (qb_first + it % per_head) * BM;
+        const int h = hq;
+        const int q0 = (qb_first + it) * BM;
         const uint32_t par = static_cast<uint32_t>(it & 1);
         if (!mbar_wait(q_free, par ^ 1, p.status, kStatusTimeoutProducer)) break;
         mbar_expect_tx(q_full, TILE);
@@ -582,8 +586,8 @@ __global__ void __launch_bounds__(192, 1)
     // lse / delta of one query block (+inf / 0 beyond S: P = 0 there); the next block's values
     // are loaded one iteration ahead so the global-memory latency is off the critical path.
     auto load_stats = [&](int itx, float& lv, float& dv) {
-      const int hx = hk * group + itx / per_head;
-      const int qx = (qb_first + itx % per_head) * BM + ctid;
+      const int hx = hq;
+      const int qx = (qb_first + itx) * BM + ctid;
       const int64_t o = (static_cast<int64_t>(b) * p.Hq + hx) * p.S + qx;
       lv = qx < p.S ? p.lse[o] : INFINITY;
       dv = qx < p.S ? p.delta[o] : 0.f;
@@ -591,8 +595,8 @@ __global__ void __launch_bounds__(192, 1)
     float next_lse = 0.f, next_delta = 0.f;
     if (iters > 0) load_stats(0, next_lse, next_delta);
     for (int it = 0; it < iters; ++it) {
-      const int h = hk * group + it / per_head;
-      const int q0 = (qb_first + it % per_head) * BM;
+      const int h = hq;
+      const int q0 = (qb_first + it) * BM;
       const uint32_t par = static_cast<uint32_t>(it & 1);
       // Double-buffered by iteration parity: a thread writes buffer it & 1 only after every
       // compute thread arrived for iteration it - 1, i.e. finished with iteration it - 2's buffer.
@@ -680,22 +684,31 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_before();
       mbar_arrive(dq_free);
     }
-    // dK (scaled) and dV rows of this key block.
+    // dK (scaled) and dV rows of this key block: stored directly (one query head per kv head)
+    // or added into the fp32 accumulators (GQA).
     if (ok && warp_wait(kv_done, 0, p.status, kStatusTimeoutEpilogue)) {
       tc_fence_after();
       const bool valid = key < p.S;
-      __nv_bfloat16* dkr = p.dk + b * p.dk_sb + static_cast<int64_t>(valid ? key : 0) * p.dk_ss + hk * p.dk_sh;
-      __nv_bfloat16* dvr = p.dv + b * p.dv_sb + static_cast<int64_t>(valid ? key : 0) * p.dv_ss + hk * p.dv_sh;
+      const int64_t krow = valid ? key : 0;
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
         const uint32_t col = which == 0 ? COL_DK : COL_DV;
         const float sc = which == 0 ? p.scale : 1.f;
-        __nv_bfloat16* out = which == 0 ? dkr : dvr;
+        float* accp = which == 0 ? p.dk_acc : p.dv_acc;
+        __nv_bfloat16* out = which == 0 ? p.dk + b * p.dk_sb + krow * p.dk_ss + hk * p.dk_sh
+                                        : p.dv + b * p.dv_sb + krow * p.dv_ss + hk * p.dv_sh;
+        float* acc_row = accp != nullptr ? accp + ((static_cast<int64_t>(b) * p.S + krow) * p.Hkv + hk) * D : nullptr;
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint32_t v[32];
           tmem_ld32(tmem_base + lane_addr + col + c * 32, v);
-          if (valid) {
+          if (!valid) continue;
+          if (acc_row != nullptr) {
+#pragma unroll
+            for (int t = 0; t < 32; t += 4)
+              red_add_v4(acc_row + c * 32 + t, __uint_as_float(v[t]) * sc, __uint_as_float(v[t + 1]) * sc,
+                         __uint_as_float(v[t + 2]) * sc, __uint_as_float(v[t + 3]) * sc);
+          } else {
 #pragma unroll
             for (int t = 0; t < 32; t += 8) {
               uint4 o;
@@ -716,6 +729,25 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, attn_tc_bwd::TMEM_COLS);
+  }
+}
+
+// fp32 [B, S, H, D] accumulator -> bf16 strided [B, S, H, D] view.
+__global__ void acc_to_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int B, int S, int H,
+                                   int D, int64_t sb, int64_t ss, int64_t sh) {
+  const int64_t total = static_cast<int64_t>(B) * S * H * D / 4;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int64_t e = i * 4;
+    const int d = static_cast<int>(e % D);
+    const int64_t r = e / D;
+    const int h = static_cast<int>(r % H);
+    const int64_t bs = r / H;
+    const int s = static_cast<int>(bs % S);
+    const int bb = static_cast<int>(bs / S);
+    const float4 v = *reinterpret_cast<const float4*>(acc + e);
+    __nv_bfloat16* o = out + bb * sb + s * ss + h * sh + d;
+    *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
   }
 }
 
@@ -761,11 +793,31 @@ void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at
     NTB_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
     attr_done[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((S + BN - 1) / BN), static_cast<unsigned>(Hkv), static_cast<unsigned>(B));
+  at::Tensor dk_acc, dv_acc;
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
+  if (Hq != Hkv) {
+    dk_acc = at::zeros({B, S, Hkv, D}, q.options().dtype(at::kFloat));
+    dv_acc = at::zeros({B, S, Hkv, D}, q.options().dtype(at::kFloat));
+    p.dk_acc = dk_acc.data_ptr<float>();
+    p.dv_acc = dv_acc.data_ptr<float>();
+  }
+  dim3 grid(static_cast<unsigned>((S + BN - 1) / BN), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
   void* args[5] = {&ts.m[0], &ts.m[1], &ts.m[2], &ts.m[3], &p};
   NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(flash_bwd_tc_kernel), grid, dim3(192), args,
-                                  static_cast<size_t>(SMEM_BYTES), at::cuda::getCurrentCUDAStream(dev)));
+                                  static_cast<size_t>(SMEM_BYTES), stream));
   NTB_LAUNCH_CHECK(1);
+  if (Hq != Hkv) {
+    TORCH_CHECK(dk.stride(3) == 1 && dv.stride(3) == 1 && dk.stride(2) % 4 == 0 && dk.stride(1) % 4 == 0 &&
+                    dv.stride(2) % 4 == 0 && dv.stride(1) % 4 == 0,
+                "flash_attn_bwd_tc: dk/dv strides must keep 8-byte alignment");
+    const int64_t n4 = B * S * Hkv * D / 4;
+    const int blocks = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, 148 * 8));
+    acc_to_bf16_kernel<<<blocks, 256, 0, stream>>>(dk_acc.data_ptr<float>(), p.dk, p.B, p.S, p.Hkv, D, p.dk_sb,
+                                                   p.dk_ss, p.dk_sh);
+    acc_to_bf16_kernel<<<blocks, 256, 0, stream>>>(dv_acc.data_ptr<float>(), p.dv, p.B, p.S, p.Hkv, D, p.dv_sb,
+                                                   p.dv_ss, p.dv_sh);
+    NTB_LAUNCH_CHECK(2);
+  }
 }
 
 }  // namespace ntb

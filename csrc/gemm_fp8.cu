@@ -8,16 +8,18 @@
 // both K-major, K a multiple of 128; C bf16. The scales are exactly what the e4m3
 // quantizer in quant.cu produces (tile_1x128 / block_128x128).
 //
-// Persistent CTAs, 320 threads, 128 x 128 output tiles:
-//   warp 0      TMA producer: per K block one [128 x 128 B] box of A and of B (128-byte
+// Persistent CTAs, 320 threads, 128 x 256 output tiles (a 256-wide B tile halves the shared-
+// memory operand traffic per FLOP relative to 128, which the doubled fp8 rate needs):
+//   warp 0      TMA producer: per K block one [128 x 128 B] box of A and two of B (128-byte
 //               swizzle: one swizzle row = one 128-wide K block of 8-bit elements)
-//   warp 1      MMA issuer: 4 x tcgen05.mma kind::f8f6f4 (K = 32 each) per K block into one
-//               of four TMEM partial buffers (fresh accumulation per K block)
-//   warps 2..9  promotion: two warps per TMEM lane quarter (32 rows), each owning 64 of the
-//               128 columns; per K block they read the partial product, scale it by
-//               sa[row, kb] * sb[nb, kb] and add it to fp32 registers, then release the
-//               buffer, so the tensor core computes K block k+1 while block k is promoted;
-//               after the last K block they add the bias and store bf16.
+//   warp 1      MMA issuer: 4 x tcgen05.mma kind::f8f6f4 (128 x 256 x 32) per K block into
+//               one of two TMEM partial buffers (fresh accumulation per K block)
+//   warps 2..9  promotion: two warps per TMEM lane quarter (32 rows), each owning one
+//               128-column half = one weight-scale block; per K block they read the partial
+//               product, scale it by sa[row, kb] * sb[block, kb] and add it to fp32
+//               registers, then release the buffer, so the tensor core computes K block k+1
+//               while block k is promoted; after the last K block they add the bias and
+//               store bf16.
 // Every wait is bounded (common.cuh).
 //
 // Reference parity: src/runtime/te_backend.py:229-260 (emulated fp8 linear: fake-quantised
@@ -31,13 +33,13 @@
 namespace ntb {
 
 namespace fp8g {
-constexpr int BM = 128, BN = 128, BK = 128;  // BK in elements = bytes
-constexpr int STAGES = 6;
+constexpr int BM = 128, BN = 256, BK = 128;  // BK in elements = bytes; BN = two weight-scale blocks
+constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK, B_BYTES = BN * BK;
 constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + 512;
 constexpr int THREADS = 320;
-constexpr int NBUF = 4;              // TMEM partial buffers: the tensor core runs up to 3 K blocks ahead
-constexpr uint32_t TMEM_COLS = NBUF * 128;
+constexpr int NBUF = 2;              // TMEM partial buffers of BN columns (the tensor core runs a K block ahead)
+constexpr uint32_t TMEM_COLS = NBUF * BN;
 }  // namespace fp8g
 
 struct Fp8GemmParams {
@@ -66,7 +68,7 @@ __host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N) {
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-__global__ void __launch_bounds__(320, 1)
+__global__ void __maxnreg__(192)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     Fp8GemmParams p) {
   using namespace fp8g;
@@ -126,6 +128,7 @@ __global__ void __launch_bounds__(320, 1)
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
           tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
+          tma_load_2d(sB + stage * B_BYTES + 128 * BK, &tmB, &full[stage], kb * BK, nb * BN + 128);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -168,7 +171,7 @@ __global__ void __launch_bounds__(320, 1)
       mbar_wait(drain, 0, nullptr, 0);
     }
   } else {
-    // Promotion warps: lane quarter (warp % 4) -> rows; warps 2..5 columns 0..63, 6..9 columns 64..127.
+    // Promotion warps: lane quarter (warp % 4) -> rows; warps 2..5 columns 0..127, 6..9 columns 128..255.
     const int q = warp & 3;
     const int half = (warp - 2) >> 2;
     const int row = q * 32 + lane;
@@ -180,13 +183,14 @@ __global__ void __launch_bounds__(320, 1)
       const int mb = tile % num_m, nb = tile / num_m;
       const long m = static_cast<long>(mb) * BM + row;
       const float* sa_row = p.sa + (m < p.M ? m : 0) * nk;
-      const float* sb_row = p.sb + static_cast<long>(nb) * nk;
-      float acc[64];
+      const float* sb_row = p.sb + static_cast<long>(nb * 2 + half) * nk;  // this half's weight block
+      const bool half_live = nb * BN + half * 128 < p.N;
+      float acc[128];
 #pragma unroll
-      for (int c = 0; c < 64; ++c) acc[c] = 0.f;
+      for (int c = 0; c < 128; ++c) acc[c] = 0.f;
       bool ok = true;
       for (int kb = 0; kb < nkb; ++kb) {
-        const float sc = __ldg(sa_row + kb) * __ldg(sb_row + kb);
+        const float sc = half_live ? __ldg(sa_row + kb) * __ldg(sb_row + kb) : 0.f;
         const bool got = mbar_wait(&pfull[buf], bphase, p.status, kStatusTimeoutEpilogue);
         if (!__all_sync(0xffffffffu, got)) {
           ok = false;
@@ -194,9 +198,9 @@ __global__ void __launch_bounds__(320, 1)
         }
         tc_fence_after();
 #pragma unroll
-        for (int c = 0; c < 2; ++c) {
+        for (int c = 0; c < 4; ++c) {
           uint32_t r[32];
-          tmem_ld32(tmem_base + lane_addr + buf * BN + half * 64 + c * 32, r);
+          tmem_ld32(tmem_base + lane_addr + buf * BN + half * 128 + c * 32, r);
 #pragma unroll
           for (int t = 0; t < 32; ++t) acc[c * 32 + t] = fmaf(__uint_as_float(r[t]), sc, acc[c * 32 + t]);
         }
@@ -208,11 +212,11 @@ __global__ void __launch_bounds__(320, 1)
         }
       }
       if (!ok) break;
-      const int n0 = nb * BN + half * 64;
-      if (m < p.M) {
+      const int n0 = nb * BN + half * 128;
+      if (m < p.M && half_live) {
         __nv_bfloat16* crow = p.C + m * p.ldc + n0;
 #pragma unroll
-        for (int c = 0; c < 64; c += 8) {
+        for (int c = 0; c < 128; c += 8) {
           if (n0 + c + 8 <= p.N) {
             float v[8];
 #pragma unroll
