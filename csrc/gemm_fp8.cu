@@ -68,7 +68,7 @@ __host__ __device__ constexpr uint32_t make_idesc_e4m3(int M, int N) {
   return (1u << 4) | (static_cast<uint32_t>(N >> 3) << 17) | (static_cast<uint32_t>(M >> 4) << 24);
 }
 
-__global__ void __maxnreg__(192)
+__global__ void __launch_bounds__(320, 1)
     gemm_fp8_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                     Fp8GemmParams p) {
   using namespace fp8g;
