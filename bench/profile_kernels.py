@@ -12,6 +12,8 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   attn_bwd      flash attention bwd, same shape
   attn_fwd_tc   tcgen05 flash attention fwd, same shape
   attn_bwd_tc   tcgen05 flash attention bwd (the default backward for head dim 128), same shape
+  fp8_gemm      block-scaled e4m3 GEMM 8192 x 2048 x 7168 (DeepSeek-V3 recipe scales)
+  grouped_fwd   grouped expert GEMM, 64 experts, 49152 routed rows x 2816 x 2048 (DeepSeek-V2-Lite gate|up)
   rmsnorm_bwd   RMSNorm backward 8192 x 4096 bf16
   adamw         fused flat AdamW over 64M fp32 elements
   swiglu        SwiGLU fwd 8192 x 14336
@@ -49,6 +51,22 @@ def main():
         qkv = torch.randn(1, 4096, 48, 128, **bf)
         q, k, v = qkv[:, :, :32], qkv[:, :, 32:40], qkv[:, :, 40:]
         fn = lambda: C.flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)  # noqa: E731
+    elif a.case == "fp8_gemm":
+        x = torch.randn(8192, 7168, **bf)
+        w = torch.randn(2048, 7168, **bf)
+        xq, sx = C.fp8_quantize(x, 1, False, 0)
+        wq, sw = C.fp8_quantize(w, 128, False, 0)
+        y = torch.empty(8192, 2048, **bf)
+        fn = lambda: C.gemm_fp8_blockscaled(xq, sx, wq, sw, y)  # noqa: E731
+    elif a.case == "grouped_fwd":
+        from nano_train_b200.ops.grouped import pad_segments
+
+        counts = torch.bincount(torch.randint(0, 64, (49152,), device=dev), minlength=64)
+        off, rows = pad_segments(counts)
+        x = torch.randn(rows, 2048, **bf)
+        w = torch.randn(64 * 2816, 2048, **bf)
+        y = torch.empty(rows, 2816, **bf)
+        fn = lambda: C.gemm_grouped_bf16(x, w, y, off, 1)  # noqa: E731
     elif a.case == "attn_bwd_tc":
         qkv = torch.randn(1, 4096, 48, 128, **bf)
         q, k, v = qkv[:, :, :32], qkv[:, :, 32:40], qkv[:, :, 40:]
