@@ -79,6 +79,25 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
              bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> tctrs, at::Tensor& ctrs, int64_t rank,
              int64_t epoch, const c10::optional<at::Tensor>& trace);
 void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns);
+// moe_ep.cu
+void ep_dispatch(const at::Tensor& x, const at::Tensor& tok, const at::Tensor& dest, const at::Tensor& slot,
+                 const at::Tensor& lexp, const at::Tensor& kslot, const at::Tensor& w, const at::Tensor& send_counts,
+                 std::vector<int64_t> payload, std::vector<int64_t> pscale, std::vector<int64_t> meta,
+                 std::vector<int64_t> flag, std::vector<int64_t> info, const at::Tensor& done, int64_t P,
+                 int64_t epoch, bool fp8, bool stochastic, int64_t seed);
+void ep_wait(int64_t flags_ptr, int64_t n, int64_t epoch, int64_t device);
+void ep_signal(std::vector<int64_t> flag, int64_t epoch, int64_t device);
+void ep_gather(at::Tensor& out, const at::Tensor& rows_used, const at::Tensor& row_src, const at::Tensor& row_slot,
+               int64_t payload_ptr, int64_t scale_ptr, int64_t P, int64_t n, bool fp8);
+void ep_quant_rows(const at::Tensor& y, const at::Tensor& rows_used, int64_t q_ptr, int64_t scale_ptr,
+                   bool stochastic, int64_t seed);
+void ep_pull(at::Tensor& out, const at::Tensor& dest_tk, const at::Tensor& slot_tk,
+             const c10::optional<at::Tensor>& w_tk, const c10::optional<at::Tensor>& pos_in,
+             std::vector<int64_t> rowmap, std::vector<int64_t> src, std::vector<int64_t> src_scale, int64_t P,
+             int64_t rows_cap, bool fp8, const c10::optional<at::Tensor>& y_save,
+             const c10::optional<at::Tensor>& pos_out);
+void ep_combine_bwd(at::Tensor& dy, const at::Tensor& rows_used, const at::Tensor& row_src, const at::Tensor& row_tok,
+                    const at::Tensor& row_w, std::vector<int64_t> dout, int64_t T);
 // symm.cpp
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t bytes);
 int64_t symm_open(py::bytes handle);
@@ -129,6 +148,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("recv"), py::arg("tctrs"), py::arg("ctrs"), py::arg("rank"), py::arg("epoch"),
         py::arg("trace") = py::none());
   m.def("wait_flag", &ntb::wait_flag, py::arg("flag"), py::arg("expect"), py::arg("limit_ns"));
+  m.def("ep_dispatch", &ntb::ep_dispatch, py::arg("x"), py::arg("tok"), py::arg("dest"), py::arg("slot"),
+        py::arg("lexp"), py::arg("kslot"), py::arg("w"), py::arg("send_counts"), py::arg("payload"),
+        py::arg("pscale"), py::arg("meta"), py::arg("flag"), py::arg("info"), py::arg("done"), py::arg("P"),
+        py::arg("epoch"), py::arg("fp8"), py::arg("stochastic"), py::arg("seed"));
+  m.def("ep_wait", &ntb::ep_wait);
+  m.def("ep_signal", &ntb::ep_signal);
+  m.def("ep_gather", &ntb::ep_gather);
+  m.def("ep_quant_rows", &ntb::ep_quant_rows);
+  m.def("ep_pull", &ntb::ep_pull, py::arg("out"), py::arg("dest_tk"), py::arg("slot_tk"), py::arg("w_tk"),
+        py::arg("pos_in"), py::arg("rowmap"), py::arg("src"), py::arg("src_scale"), py::arg("P"),
+        py::arg("rows_cap"), py::arg("fp8"), py::arg("y_save") = py::none(), py::arg("pos_out") = py::none());
+  m.def("ep_combine_bwd", &ntb::ep_combine_bwd);
   m.def("symm_alloc", &ntb::symm_alloc);
   m.def("symm_open", &ntb::symm_open);
   m.def("symm_close", &ntb::symm_close);

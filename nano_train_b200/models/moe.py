@@ -313,10 +313,37 @@ class ExpertParallelMoE(nn.Module):
         self._last_dropped_fraction = 0.0
         self._last_token_counts = torch.zeros(self.experts_per_rank, dtype=torch.long)
         self._stack_cache = _StackCache()
+        self.last_path = None  # "fused" (peer-memory kernels) or "all_to_all", set by forward
 
     last_aux_loss = property(lambda self: self._last_aux_loss)
-    last_dropped_fraction = property(lambda self: self._last_dropped_fraction)
     last_token_counts = property(lambda self: self._last_token_counts)
+
+    @property
+    def last_dropped_fraction(self) -> float:
+        d = self._last_dropped_fraction
+        if isinstance(d, torch.Tensor):  # fused path: device stats, read only when asked for
+            s = d.tolist()
+            d = float(s[0] / max(s[1], 1.0))
+            self._last_dropped_fraction = d
+        return d
+
+    def _fused_payload(self):
+        """(use the fused kernels, e4m3 payload) for this layer's settings."""
+        g = self.comm_quant_granularity
+        if g in (None, "none"):
+            return True, False
+        if self.comm_quant_backend == "native" and g in ("tile_1x128", "block_128x128") \
+                and self.hidden_size % 128 == 0:
+            return True, True
+        return False, False  # emulated payload numerics stay on the all-to-all path
+
+    def _fused_ok(self, tokens: torch.Tensor) -> bool:
+        if not (tokens.is_cuda and tokens.dtype == torch.bfloat16 and self.top_k <= 8 and tokens.shape[0] > 0
+                and self.hidden_size % 8 == 0):
+            return False
+        from ..parallel.ep_fused import fused_ep_enabled
+
+        return fused_ep_enabled(self.ep_group) and grouped_kernel_ok(tokens, self.experts) and self._fused_payload()[0]
 
     def _compute_capacity(self, global_tokens: int) -> int:
         if global_tokens <= 0:
@@ -330,6 +357,9 @@ class ExpertParallelMoE(nn.Module):
         tokens = x.reshape(-1, H)
         T = tokens.size(0)
         ro = self.router(tokens)
+        if self._fused_ok(tokens):
+            return self._forward_fused(tokens, ro).view(B, S, H)
+        self.last_path = "all_to_all"
         E, epr, K = self.num_experts, self.experts_per_rank, self.top_k
         # Global token count -> capacity (every EP rank sees the same capacity).
         t_all = torch.tensor([float(T)], device=tokens.device)
@@ -387,3 +417,25 @@ class ExpertParallelMoE(nn.Module):
         self._last_dropped_fraction = float(s[0] / max(s[1], 1.0))
         self._last_token_counts = kept_counts
         return out.view(B, S, H)
+
+    def _forward_fused(self, tokens: torch.Tensor, ro: RouterOutput) -> torch.Tensor:
+        """Dispatch / experts / combine through the peer-memory kernels, no host synchronisation.
+
+        Every EP rank must route the same number of tokens per call (capacity is computed from
+        T * ep_size on the host to size the buffers; the device value is clamped to it).
+        """
+        from ..parallel.ep_fused import fused_ep_moe
+
+        _, fp8 = self._fused_payload()
+        out, stats, kept_counts = fused_ep_moe(
+            tokens, ro.topk_indices, ro.topk_weights, self.experts, self._stack_cache, group=self.ep_group,
+            num_experts=self.num_experts, capacity_factor=self.capacity_factor, fp8_payload=fp8,
+            stochastic=fp8 and self.comm_quant_rounding == "stochastic")
+        if len(self.shared_experts):
+            out = out + sum(se(tokens) for se in self.shared_experts) / float(len(self.shared_experts))
+        dist.all_reduce(stats, group=self.ep_group)  # enqueued on the stream; read lazily
+        self._last_aux_loss = ro.aux_loss
+        self._last_dropped_fraction = stats
+        self._last_token_counts = kept_counts
+        self.last_path = "fused"
+        return out

@@ -65,9 +65,18 @@ class _StackCache:
         return self.w1, self.w2
 
 
+class GroupedBuffers:
+    """Optional caller-owned outputs: ``y_out`` receives the expert outputs, ``dx_out``
+    the input gradient (the expert-parallel path points both at peer-visible memory)."""
+
+    def __init__(self, y_out: torch.Tensor | None = None, dx_out: torch.Tensor | None = None):
+        self.y_out = y_out
+        self.dx_out = dx_out
+
+
 class _GroupedSwiGLUFn(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x_pad, offsets, w1, w2, n_experts, *params):
+    def forward(ctx, x_pad, offsets, w1, w2, n_experts, bufs, *params):
         C = ext()
         R = x_pad.shape[0]
         I2 = w1.shape[0] // n_experts
@@ -75,11 +84,13 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
         h = torch.empty(R, I2, device=x_pad.device, dtype=x_pad.dtype)
         C.gemm_grouped_bf16(x_pad, w1, h, offsets, 1)
         a = C.swiglu_fwd(h)
-        y = torch.empty(R, H, device=x_pad.device, dtype=x_pad.dtype)
+        y = bufs.y_out if bufs is not None and bufs.y_out is not None else \
+            torch.empty(R, H, device=x_pad.device, dtype=x_pad.dtype)
         C.gemm_grouped_bf16(a, w2, y, offsets, 1)
         ctx.save_for_backward(x_pad, offsets, w1, w2, h, a)
         ctx.n_experts = n_experts
         ctx.params = params
+        ctx.bufs = bufs
         return y
 
     @staticmethod
@@ -96,7 +107,8 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
         dw2 = torch.zeros(E * H, I, device=dy.device, dtype=torch.float32)
         C.gemm_grouped_bf16(dy, a, dw2, offsets, 2, b_mn=True)          # dW2_e = dY_e^T A_e
         dh = C.swiglu_bwd(da, h)
-        dx = torch.empty_like(x_pad)
+        bufs = ctx.bufs
+        dx = bufs.dx_out if bufs is not None and bufs.dx_out is not None else torch.empty_like(x_pad)
         C.gemm_grouped_bf16(dh, w1, dx, offsets, 1, b_mn=True)          # dX = dH . W1_e
         dw1 = torch.zeros(E * I2, x_pad.shape[1], device=dy.device, dtype=torch.float32)
         C.gemm_grouped_bf16(dh, x_pad, dw1, offsets, 2, b_mn=True)      # dW1_e = dH_e^T X_e
@@ -110,7 +122,7 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
                     grads.append(None)
                 else:
                     grads.append(g.to(p.dtype))
-        return (dx, None, None, None, None, *grads)
+        return (dx, None, None, None, None, None, *grads)
 
 
 def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts, cache: _StackCache,
@@ -120,7 +132,8 @@ def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts
     x_pad, dest = scatter_rows_to_segments(x_sorted, counts, offsets, rows)
     w1, w2 = cache.get(experts)
     params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
-    y_pad = _GroupedSwiGLUFn.apply(x_pad, offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), *params)
+    y_pad = _GroupedSwiGLUFn.apply(x_pad, offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), None,
+                                   *params)
     return y_pad.index_select(0, dest)
 
 
