@@ -33,6 +33,8 @@ def main():
     ap.add_argument("--fp8", action="store_true", help="e4m3 1x128 payload (native comm quant)")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--fused-first", action="store_true")
+    ap.add_argument("--no-main-grad", action="store_true", help="per-parameter .grad instead of flat fp32 main_grad")
     ap.add_argument("--breakdown", action="store_true",
                     help="print the top kernels of two fused iterations (torch.profiler; diagnosis only, not timing)")
     a = ap.parse_args()
@@ -45,10 +47,15 @@ def main():
                             ep_group=dist.group.WORLD, param_dtype=torch.bfloat16, param_device="cuda",
                             n_shared_experts=a.shared, scoring_func="softmax", capacity_factor=a.capacity_factor,
                             comm_quant_granularity="tile_1x128" if a.fp8 else None, comm_quant_backend="native")
+    if not a.no_main_grad:
+        # as under the flat optimizer: fp32 main_grad views of one buffer, weight gradients accumulate there
+        from nano_train_b200.parallel.flat_optimizer import FlatParamBuffer
+
+        FlatParamBuffer(list(moe.parameters()))
     x = torch.randn(1, a.tokens, a.hidden, device="cuda", dtype=torch.bfloat16, requires_grad=True)
     dy = torch.randn(1, a.tokens, a.hidden, device="cuda", dtype=torch.bfloat16)
     res = {}
-    for mode in ("all_to_all", "fused"):
+    for mode in (("fused", "all_to_all") if a.fused_first else ("all_to_all", "fused")):
         os.environ["NTB_FUSED_EP"] = "1" if mode == "fused" else "0"
 
         def step():
@@ -59,15 +66,29 @@ def main():
             step()
         dist.barrier()
         torch.cuda.synchronize()
+        m0 = torch.cuda.memory_stats()
         s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev = [torch.cuda.Event(enable_timing=True) for _ in range(a.iters + 1)]
+        import time
+
+        host = 0.0
         s.record()
-        for _ in range(a.iters):
+        ev[0].record()
+        for i in range(a.iters):
+            h0 = time.perf_counter()
             step()
+            host += time.perf_counter() - h0
+            ev[i + 1].record()
         e.record()
         torch.cuda.synchronize()
+        per_iter = [round(ev[i].elapsed_time(ev[i + 1]), 2) for i in range(a.iters)]
         t = torch.tensor([s.elapsed_time(e) / a.iters], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        res[mode] = {"ms": round(float(t), 3), "path": moe.last_path}
+        m1 = torch.cuda.memory_stats()
+        res[mode] = {"ms": round(float(t), 3), "path": moe.last_path, "host_enqueue_ms": round(host * 1e3 / a.iters, 2),
+                     "per_iter_ms_rank0": per_iter,
+                     "allocator": {k: m1.get(k, 0) - m0.get(k, 0)
+                                   for k in ("num_device_alloc", "num_device_free", "num_alloc_retries")}}
     if a.breakdown:
         os.environ["NTB_FUSED_EP"] = "1"
         from torch.profiler import ProfilerActivity, profile

@@ -28,7 +28,7 @@ namespace ntb {
 void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const c10::optional<at::Tensor>& bias,
                bool a_mn, bool b_mn, bool accumulate, double alpha);
 void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& offsets,
-                       int64_t mode, bool b_mn, bool accumulate);
+                       int64_t mode, bool b_mn, bool accumulate, int64_t c_group_stride);
 // ops.cu
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
                                     const at::Tensor& w, double eps);
@@ -79,12 +79,23 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
              bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> tctrs, at::Tensor& ctrs, int64_t rank,
              int64_t epoch, const c10::optional<at::Tensor>& trace);
 void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns);
+// router.cu
+std::vector<at::Tensor> router_fwd(const at::Tensor& logits, int64_t K, bool softmax, int64_t n_group,
+                                   int64_t topk_group, bool norm_topk, double scale);
+at::Tensor router_bwd(const at::Tensor& logits, const at::Tensor& idx, const at::Tensor& dw, const at::Tensor& dpsum,
+                      int64_t K, bool softmax, int64_t n_group, int64_t topk_group, bool norm_topk, double scale);
 // moe_ep.cu
-void ep_dispatch(const at::Tensor& x, const at::Tensor& tok, const at::Tensor& dest, const at::Tensor& slot,
-                 const at::Tensor& lexp, const at::Tensor& kslot, const at::Tensor& w, const at::Tensor& send_counts,
-                 std::vector<int64_t> payload, std::vector<int64_t> pscale, std::vector<int64_t> meta,
-                 std::vector<int64_t> flag, std::vector<int64_t> info, const at::Tensor& done, int64_t P,
-                 int64_t epoch, bool fp8, bool stochastic, int64_t seed);
+void ep_dispatch(const at::Tensor& x, const at::Tensor& idx, const at::Tensor& w, at::Tensor& dest_tk,
+                 at::Tensor& slot_tk, const at::Tensor& ctr, int64_t epr, std::vector<int64_t> payload,
+                 std::vector<int64_t> pscale, std::vector<int64_t> meta, std::vector<int64_t> flag,
+                 std::vector<int64_t> info, const at::Tensor& done, int64_t P, int64_t epoch, bool fp8,
+                 bool stochastic, int64_t seed);
+void ep_recv_keys(int64_t meta_ptr, int64_t info_ptr, at::Tensor& keys, at::Tensor& counts, int64_t P, int64_t n,
+                  int64_t epr, int64_t K);
+void ep_recv_layout(const at::Tensor& skeys, const at::Tensor& order, int64_t meta_ptr, int64_t info_ptr,
+                    const at::Tensor& counts, at::Tensor& offsets, at::Tensor& row_src, at::Tensor& row_slot,
+                    at::Tensor& row_tok, at::Tensor& row_w, int64_t rowmap_ptr, at::Tensor& stats, int64_t P,
+                    int64_t n, int64_t epr, int64_t K, int64_t E, double capacity_factor, int64_t host_cap);
 void ep_wait(int64_t flags_ptr, int64_t n, int64_t epoch, int64_t device);
 void ep_signal(std::vector<int64_t> flag, int64_t epoch, int64_t device);
 void ep_gather(at::Tensor& out, const at::Tensor& rows_used, const at::Tensor& row_src, const at::Tensor& row_slot,
@@ -115,7 +126,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("alpha") = 1.0);
   m.def("gemm_grouped_bf16", &ntb::gemm_grouped_bf16, "grouped (mixture-of-experts) tcgen05 GEMM", py::arg("a"),
         py::arg("b"), py::arg("out"), py::arg("offsets"), py::arg("mode"), py::arg("b_mn") = false,
-        py::arg("accumulate") = false);
+        py::arg("accumulate") = false, py::arg("c_group_stride") = 0);
   m.def("rmsnorm_fwd", &ntb::rmsnorm_fwd);
   m.def("rmsnorm_bwd", &ntb::rmsnorm_bwd);
   m.def("layernorm_fwd", &ntb::layernorm_fwd);
@@ -148,11 +159,15 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("recv"), py::arg("tctrs"), py::arg("ctrs"), py::arg("rank"), py::arg("epoch"),
         py::arg("trace") = py::none());
   m.def("wait_flag", &ntb::wait_flag, py::arg("flag"), py::arg("expect"), py::arg("limit_ns"));
-  m.def("ep_dispatch", &ntb::ep_dispatch, py::arg("x"), py::arg("tok"), py::arg("dest"), py::arg("slot"),
-        py::arg("lexp"), py::arg("kslot"), py::arg("w"), py::arg("send_counts"), py::arg("payload"),
-        py::arg("pscale"), py::arg("meta"), py::arg("flag"), py::arg("info"), py::arg("done"), py::arg("P"),
-        py::arg("epoch"), py::arg("fp8"), py::arg("stochastic"), py::arg("seed"));
+  m.def("ep_dispatch", &ntb::ep_dispatch, py::arg("x"), py::arg("idx"), py::arg("w"), py::arg("dest_tk"),
+        py::arg("slot_tk"), py::arg("ctr"), py::arg("epr"), py::arg("payload"), py::arg("pscale"), py::arg("meta"),
+        py::arg("flag"), py::arg("info"), py::arg("done"), py::arg("P"), py::arg("epoch"), py::arg("fp8"),
+        py::arg("stochastic"), py::arg("seed"));
+  m.def("ep_recv_keys", &ntb::ep_recv_keys);
+  m.def("ep_recv_layout", &ntb::ep_recv_layout);
   m.def("ep_wait", &ntb::ep_wait);
+  m.def("router_fwd", &ntb::router_fwd);
+  m.def("router_bwd", &ntb::router_bwd);
   m.def("ep_signal", &ntb::ep_signal);
   m.def("ep_gather", &ntb::ep_gather);
   m.def("ep_quant_rows", &ntb::ep_quant_rows);

@@ -47,6 +47,7 @@ struct GemmParams {
   int groups;
   int b_group_rows;    // rows of one group's slice of the stacked B (mode 1)
   long m_limit;        // rows of C that exist (mode 2: per-group output rows)
+  long c_group_stride; // mode 2: rows of C between consecutive groups' blocks (0 = M, a dense stack)
 };
 
 template <int BN>
@@ -392,7 +393,7 @@ __global__ void __launch_bounds__(192, 1)
       } else if (ti.nkb > 0) {
         // Expert block: rows [group * M, group * M + M) of the stacked output; an expert without
         // rows contributes nothing (its accumulator was never written).
-        const long base = static_cast<long>(ti.group) * p.M;
+        const long base = static_cast<long>(ti.group) * (p.c_group_stride > 0 ? p.c_group_stride : p.M);
         epilogue_tile<BN>(t_row, stage, p, base + static_cast<long>(ti.mb) * BM + q * 32, ti.nb * BN, vec_ok,
                           base + p.M);
       }
@@ -514,7 +515,7 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
 //   mode 2 (K-grouped): out[g] (+)= a[rows of g]^T . b[rows of g]
 //        a: [R, M] (e.g. dY), b: [R, N] (e.g. X), out: stacked [G * M, N] (fp32 weight gradient)
 void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const at::Tensor& offsets,
-                       int64_t mode, bool b_mn, bool accumulate) {
+                       int64_t mode, bool b_mn, bool accumulate, int64_t c_group_stride) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda() && offsets.is_cuda(), "gemm_grouped: CUDA tensors");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_grouped: bf16 operands");
   TORCH_CHECK(offsets.scalar_type() == at::kInt && offsets.dim() == 1 && offsets.numel() >= 2 &&
@@ -565,7 +566,15 @@ void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
   TORCH_CHECK(mode == 2, "gemm_grouped: mode 1 or 2");
   TORCH_CHECK(a.size(0) == b.size(0), "gemm_grouped: a and b must have the same rows");
   const int64_t M = a.size(1), N = b.size(1);
-  TORCH_CHECK(out.size(0) == G * M && out.size(1) == N, "gemm_grouped: out must be [G * M, N]");
+  if (c_group_stride > 0) {
+    // Group g's [M, N] block starts at row g * c_group_stride of out (e.g. per-expert gradients inside a
+    // flat buffer that interleaves other parameters between the experts' blocks).
+    TORCH_CHECK(c_group_stride >= M && out.size(1) == N && out.size(0) >= (G - 1) * c_group_stride + M,
+                "gemm_grouped: out must hold (G - 1) * c_group_stride + M rows of N");
+    p.c_group_stride = c_group_stride;
+  } else {
+    TORCH_CHECK(out.size(0) == G * M && out.size(1) == N, "gemm_grouped: out must be [G * M, N]");
+  }
   if (M == 0 || N == 0) return;
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);

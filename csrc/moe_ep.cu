@@ -105,17 +105,15 @@ __device__ __forceinline__ void dequant8(const uint2& q, float s, float (&v)[8])
 
 // ------------------------------------------------------------------ dispatch
 struct EpDispatchParams {
-  const bf16* x;  // [T, H] this rank's tokens
+  const bf16* x;              // [T, H] this rank's tokens
   long H;
-  int T;
-  int n_assign;             // T * K
-  const int* tok;           // token of each destination-sorted assignment
-  const int* dest;          // destination rank
-  const int* slot;          // row inside this source's block of the destination slab
-  const int* lexp;          // expert index local to the destination
-  const int* kslot;         // top-k slot of the assignment
-  const float* w;           // routing weight (fp32)
-  const int* send_counts;   // [n] rows sent to each destination
+  int T, K, epr;
+  const int64_t* idx;         // [T, K] global expert of each assignment (router output)
+  const void* w;              // [T, K] routing weight (bf16 or fp32)
+  int w_f32;
+  int* dest_tk;               // out [T*K] destination rank of assignment (t, k)
+  int* slot_tk;               // out [T*K] row in this source's block of the destination slab
+  int* ctr;                   // [n] local slot counters (zero at rest)
   uint8_t* payload[kEpMaxRanks];  // destination slab payload, this source's block already applied
   float* pscale[kEpMaxRanks];     // fp8 payload scales (same block)
   int4* meta[kEpMaxRanks];        // per-row records (same block)
@@ -130,13 +128,35 @@ struct EpDispatchParams {
   int* status;
 };
 
+// One warp per (token, k) assignment in token order. Lane 0 reserves the next
+// row of this source's block in the destination slab (atomic on a local
+// counter), so no sort precedes the exchange; the receiver orders rows by a
+// total key, which makes the result independent of the reservation order.
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchParams p) {
   const int lane = threadIdx.x & 31;
   const long nwarps = static_cast<long>(gridDim.x) * kWarps;
-  for (long i = static_cast<long>(blockIdx.x) * kWarps + (threadIdx.x >> 5); i < p.n_assign; i += nwarps) {
-    const int t = __ldg(p.tok + i), d = __ldg(p.dest + i), s = __ldg(p.slot + i);
-    if (t < 0 || t >= p.T || d < 0 || d >= p.n || s < 0 || s >= p.P) {
-      if (lane == 0) set_status(p.status, kStatusBadShape);
+  const long n_assign = static_cast<long>(p.T) * p.K;
+  for (long a = static_cast<long>(blockIdx.x) * kWarps + (threadIdx.x >> 5); a < n_assign; a += nwarps) {
+    const int t = static_cast<int>(a / p.K), k = static_cast<int>(a % p.K);
+    const long e = __ldg(p.idx + a);
+    const int d = static_cast<int>(e / p.epr);
+    if (e < 0 || d >= p.n) {
+      if (lane == 0) {
+        set_status(p.status, kStatusBadShape);
+        p.dest_tk[a] = 0;
+        p.slot_tk[a] = -1;
+      }
+      continue;
+    }
+    int s = 0;
+    if (lane == 0) s = atomicAdd(p.ctr + d, 1);
+    s = __shfl_sync(0xffffffffu, s, 0);
+    if (s >= p.P) {  // cannot happen for T*K <= P; never write past the block
+      if (lane == 0) {
+        set_status(p.status, kStatusBadShape);
+        p.dest_tk[a] = d;
+        p.slot_tk[a] = -1;
+      }
       continue;
     }
     const bf16* src = p.x + static_cast<long>(t) * p.H;
@@ -162,13 +182,18 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchParams
         const float scale = amax > 0.f ? amax / 448.f : 1.f;
         if (act) {
           *reinterpret_cast<uint2*>(dst + c) =
-              quant8(v, scale, p.stochastic != 0, p.seed, static_cast<uint64_t>(i) * p.H + c);
+              quant8(v, scale, p.stochastic != 0, p.seed, static_cast<uint64_t>(a) * p.H + c);
           if ((lane & 15) == 0) sc[c / 128] = scale;
         }
       }
     }
-    if (lane == 0)
-      p.meta[d][s] = make_int4(__ldg(p.lexp + i), t, __float_as_int(__ldg(p.w + i)), __ldg(p.kslot + i));
+    if (lane == 0) {
+      const float wv = p.w_f32 ? reinterpret_cast<const float*>(p.w)[a]
+                               : __bfloat162float(reinterpret_cast<const bf16*>(p.w)[a]);
+      p.meta[d][s] = make_int4(static_cast<int>(e - static_cast<long>(d) * p.epr), t, __float_as_int(wv), k);
+      p.dest_tk[a] = d;
+      p.slot_tk[a] = s;
+    }
   }
   // The last CTA to finish publishes: counts, then the epoch, to every destination.
   __syncthreads();
@@ -178,13 +203,150 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchParams
     if (prev == gridDim.x - 1) {
       __threadfence_system();
       for (int d = 0; d < p.n; ++d) {
-        p.info[d][0] = p.send_counts[d];
+        p.info[d][0] = min(p.ctr[d], static_cast<int>(p.P));
         p.info[d][1] = p.T;
+        p.ctr[d] = 0;
       }
       __threadfence_system();
       for (int d = 0; d < p.n; ++d) st_release_sys_u64(p.flag[d], p.epoch);
       *p.done = 0u;
     }
+  }
+}
+
+// ------------------------------------------------------------------ receiver: capacity selection
+// Sort key of a received row (int64, ascending = keep first):
+//   bits 55..62 local expert (epr for an empty slab row), 23..54 the routing weight in
+//   descending order, 20..22 source rank, 0..19 the source's flat assignment t * K + k.
+// The unfused module keeps, per expert, the highest weights with ties in arrival order
+// (source rank, then the source's assignments in token order): the same total order.
+struct EpKeyParams {
+  const int4* meta;       // local slab records [n][P]
+  const int* info;        // [n][4] rows received from each source
+  long long* keys;        // [n * P]
+  int* counts;            // [epr] rows per local expert (zeroed by the caller)
+  long P;
+  int n, epr, K;
+};
+
+__device__ __forceinline__ unsigned int desc_weight_key(int bits) {
+  const unsigned int b = static_cast<unsigned int>(bits);
+  const unsigned int asc = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return 0xFFFFFFFFu - asc;
+}
+
+__global__ void __launch_bounds__(256) ep_recv_keys_kernel(const EpKeyParams p) {
+  __shared__ int s_cnt[256];
+  for (int e = threadIdx.x; e < p.epr; e += blockDim.x) s_cnt[e] = 0;
+  __syncthreads();
+  const long total = static_cast<long>(p.n) * p.P;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const int s = static_cast<int>(i / p.P);
+    const long r = i - static_cast<long>(s) * p.P;
+    long long key;
+    if (r < min(static_cast<long>(p.info[s * 4]), p.P)) {
+      const int4 m = p.meta[i];
+      const int le = min(max(m.x, 0), p.epr - 1);
+      const long flat = static_cast<long>(m.y) * p.K + m.w;
+      key = (static_cast<long long>(le) << 55) | (static_cast<long long>(desc_weight_key(m.z)) << 23) |
+            (static_cast<long long>(s) << 20) | (flat & 0xFFFFF);
+      atomicAdd(&s_cnt[le], 1);
+    } else {
+      key = static_cast<long long>(p.epr) << 55 | (i & 0x7FFFFFFFFFFFLL);
+    }
+    p.keys[i] = key;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < p.epr; e += blockDim.x)
+    if (s_cnt[e]) atomicAdd(p.counts + e, s_cnt[e]);
+}
+
+struct EpLayoutParams {
+  const long long* skeys;  // sorted keys [n * P]
+  const int64_t* order;    // original slab index of each sorted key
+  const int4* meta;
+  const int* info;         // for the capacity: sum of the sources' token counts
+  const int* counts;       // [epr]
+  int* offsets;            // out [epr + 1]
+  int* row_src;            // out [rows]
+  int* row_slot;
+  int* row_tok;
+  float* row_w;
+  int* rowmap;             // out [n * P] (local symmetric memory)
+  float* stats;            // out [2] dropped, received
+  long P, rows;
+  int n, epr, K, E;
+  double capacity_factor;
+  long host_cap;
+};
+
+// Prefix sums of the (capacity-clamped, 128-padded) expert counts in shared memory,
+// then: kept sorted rows -> their grouped row; padding rows -> source -1.
+__global__ void __launch_bounds__(256) ep_recv_layout_kernel(const EpLayoutParams p) {
+  __shared__ int s_start[257], s_off[257], s_kept[256];
+  __shared__ long s_cap;
+  if (threadIdx.x == 0) {
+    long t_all = 0;
+    for (int s = 0; s < p.n; ++s) t_all += p.info[s * 4 + 1];
+    double c = ceil(p.capacity_factor * static_cast<double>(t_all) * p.K / static_cast<double>(p.E));
+    long cap = c < 1.0 ? 1 : static_cast<long>(c);
+    s_cap = cap < p.host_cap ? cap : p.host_cap;
+    int st = 0, off = 0;
+    for (int e = 0; e < p.epr; ++e) {
+      const int c_e = p.counts[e];
+      const int kept = static_cast<int>(c_e < s_cap ? c_e : s_cap);
+      s_start[e] = st;
+      s_off[e] = off;
+      s_kept[e] = kept;
+      st += c_e;
+      off += (kept + 127) / 128 * 128;
+    }
+    s_start[p.epr] = st;
+    s_off[p.epr] = off;
+    if (blockIdx.x == 0) {
+      for (int e = 0; e <= p.epr; ++e) p.offsets[e] = s_off[e];
+      long kept_total = 0;
+      for (int e = 0; e < p.epr; ++e) kept_total += s_kept[e];
+      p.stats[0] = static_cast<float>(st - kept_total);
+      p.stats[1] = static_cast<float>(st);
+    }
+  }
+  __syncthreads();
+  const long valid = s_start[p.epr];
+  const long stride = static_cast<long>(gridDim.x) * blockDim.x;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < valid; i += stride) {
+    const long long key = p.skeys[i];
+    const int le = static_cast<int>(key >> 55);
+    const long o = p.order[i];
+    if (le >= p.epr || o < 0 || o >= static_cast<long>(p.n) * p.P) continue;
+    const long r = i - s_start[le];
+    if (r < s_kept[le]) {
+      const long pos = s_off[le] + r;
+      if (pos < p.rows) {
+        const int4 m = p.meta[o];
+        p.row_src[pos] = static_cast<int>(o / p.P);
+        p.row_slot[pos] = static_cast<int>(o % p.P);
+        p.row_tok[pos] = m.y;
+        p.row_w[pos] = __int_as_float(m.z);
+        p.rowmap[o] = static_cast<int>(pos);
+      } else {
+        p.rowmap[o] = -1;
+      }
+    } else {
+      p.rowmap[o] = -1;
+    }
+  }
+  // padding rows of every expert segment
+  const long used = min(static_cast<long>(s_off[p.epr]), p.rows);
+  for (long r = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; r < used; r += stride) {
+    int lo = 0, hi = p.epr - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (s_off[mid] <= r) lo = mid;
+      else hi = mid - 1;
+    }
+    if (r - s_off[lo] >= s_kept[lo]) p.row_src[r] = -1;
   }
 }
 
@@ -446,11 +608,11 @@ void check_i32(const at::Tensor& t, int64_t n, const char* what) {
 }  // namespace
 
 // ------------------------------------------------------------------ host entry points
-void ep_dispatch(const at::Tensor& x, const at::Tensor& tok, const at::Tensor& dest, const at::Tensor& slot,
-                 const at::Tensor& lexp, const at::Tensor& kslot, const at::Tensor& w, const at::Tensor& send_counts,
-                 std::vector<int64_t> payload, std::vector<int64_t> pscale, std::vector<int64_t> meta,
-                 std::vector<int64_t> flag, std::vector<int64_t> info, const at::Tensor& done, int64_t P,
-                 int64_t epoch, bool fp8, bool stochastic, int64_t seed) {
+void ep_dispatch(const at::Tensor& x, const at::Tensor& idx, const at::Tensor& w, at::Tensor& dest_tk,
+                 at::Tensor& slot_tk, const at::Tensor& ctr, int64_t epr, std::vector<int64_t> payload,
+                 std::vector<int64_t> pscale, std::vector<int64_t> meta, std::vector<int64_t> flag,
+                 std::vector<int64_t> info, const at::Tensor& done, int64_t P, int64_t epoch, bool fp8,
+                 bool stochastic, int64_t seed) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.dim() == 2 && x.is_contiguous(),
               "ep_dispatch: x bf16 [T, H] contiguous");
   TORCH_CHECK(reinterpret_cast<uintptr_t>(x.data_ptr()) % 16 == 0, "ep_dispatch: x must be 16-byte aligned");
@@ -458,24 +620,32 @@ void ep_dispatch(const at::Tensor& x, const at::Tensor& tok, const at::Tensor& d
   TORCH_CHECK(n >= 1 && n <= kEpMaxRanks && meta.size() == payload.size() && flag.size() == payload.size() &&
                   info.size() == payload.size(),
               "ep_dispatch: 1..8 destinations");
-  const int64_t H = x.size(1), nA = tok.numel();
+  const int64_t T = x.size(0), H = x.size(1);
   TORCH_CHECK(H % (fp8 ? 128 : 8) == 0, "ep_dispatch: H must be a multiple of ", fp8 ? 128 : 8);
-  for (const at::Tensor* t : {&tok, &dest, &slot, &lexp, &kslot}) check_i32(*t, nA, "ep_dispatch");
-  TORCH_CHECK(w.is_cuda() && w.scalar_type() == at::kFloat && w.numel() >= nA, "ep_dispatch: w fp32");
-  check_i32(send_counts, n, "ep_dispatch: send_counts");
+  TORCH_CHECK(idx.is_cuda() && idx.scalar_type() == at::kLong && idx.dim() == 2 && idx.size(0) == T &&
+                  idx.is_contiguous(),
+              "ep_dispatch: idx int64 [T, K]");
+  const int64_t K = idx.size(1);
+  TORCH_CHECK(T * K <= P && T * K < (1 << 20), "ep_dispatch: T * K must fit the slab block and 20 bits");
+  TORCH_CHECK(w.is_cuda() && w.is_contiguous() && w.numel() == T * K &&
+                  (w.scalar_type() == at::kFloat || w.scalar_type() == at::kBFloat16),
+              "ep_dispatch: w [T, K] fp32 or bf16");
+  check_i32(dest_tk, T * K, "ep_dispatch: dest_tk");
+  check_i32(slot_tk, T * K, "ep_dispatch: slot_tk");
+  check_i32(ctr, n, "ep_dispatch: ctr");
   TORCH_CHECK(done.is_cuda() && done.scalar_type() == at::kInt && done.numel() >= 1, "ep_dispatch: done int32");
   EpDispatchParams p{};
   p.x = reinterpret_cast<const bf16*>(x.data_ptr());
   p.H = H;
-  p.T = static_cast<int>(x.size(0));
-  p.n_assign = static_cast<int>(nA);
-  p.tok = tok.data_ptr<int>();
-  p.dest = dest.data_ptr<int>();
-  p.slot = slot.data_ptr<int>();
-  p.lexp = lexp.data_ptr<int>();
-  p.kslot = kslot.data_ptr<int>();
-  p.w = w.data_ptr<float>();
-  p.send_counts = send_counts.data_ptr<int>();
+  p.T = static_cast<int>(T);
+  p.K = static_cast<int>(K);
+  p.epr = static_cast<int>(epr);
+  p.idx = idx.data_ptr<int64_t>();
+  p.w = w.data_ptr();
+  p.w_f32 = w.scalar_type() == at::kFloat ? 1 : 0;
+  p.dest_tk = dest_tk.data_ptr<int>();
+  p.slot_tk = slot_tk.data_ptr<int>();
+  p.ctr = ctr.data_ptr<int>();
   fill_ptrs(p.payload, payload);
   if (fp8) fill_ptrs(p.pscale, pscale);
   fill_ptrs(p.meta, meta);
@@ -491,7 +661,74 @@ void ep_dispatch(const at::Tensor& x, const at::Tensor& tok, const at::Tensor& d
   const int dev = x.get_device();
   p.status = device_status(dev);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
-  ep_dispatch_kernel<<<row_grid(dev, std::max<int64_t>(nA, 1)), 256, 0, stream>>>(p);
+  ep_dispatch_kernel<<<row_grid(dev, std::max<int64_t>(T * K, 1)), 256, 0, stream>>>(p);
+  NTB_LAUNCH_CHECK(1);
+}
+
+void ep_recv_keys(int64_t meta_ptr, int64_t info_ptr, at::Tensor& keys, at::Tensor& counts, int64_t P, int64_t n,
+                  int64_t epr, int64_t K) {
+  TORCH_CHECK(keys.is_cuda() && keys.scalar_type() == at::kLong && keys.numel() == n * P, "ep_recv_keys: keys");
+  check_i32(counts, epr, "ep_recv_keys: counts");
+  TORCH_CHECK(epr >= 1 && epr <= 255 && n <= kEpMaxRanks && P < (1LL << 40), "ep_recv_keys: sizes");
+  EpKeyParams p{};
+  p.meta = reinterpret_cast<const int4*>(meta_ptr);
+  p.info = reinterpret_cast<const int*>(info_ptr);
+  p.keys = reinterpret_cast<long long*>(keys.data_ptr<int64_t>());
+  p.counts = counts.data_ptr<int>();
+  p.P = P;
+  p.n = static_cast<int>(n);
+  p.epr = static_cast<int>(epr);
+  p.K = static_cast<int>(K);
+  const int dev = keys.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
+  const long total = n * P;
+  const int grid = static_cast<int>(std::max<long>(1, std::min<long>((total + 255) / 256, num_sms(dev) * 4)));
+  ep_recv_keys_kernel<<<grid, 256, 0, stream>>>(p);
+  NTB_LAUNCH_CHECK(1);
+}
+
+void ep_recv_layout(const at::Tensor& skeys, const at::Tensor& order, int64_t meta_ptr, int64_t info_ptr,
+                    const at::Tensor& counts, at::Tensor& offsets, at::Tensor& row_src, at::Tensor& row_slot,
+                    at::Tensor& row_tok, at::Tensor& row_w, int64_t rowmap_ptr, at::Tensor& stats, int64_t P,
+                    int64_t n, int64_t epr, int64_t K, int64_t E, double capacity_factor, int64_t host_cap) {
+  const int64_t rows = row_src.numel();
+  TORCH_CHECK(skeys.scalar_type() == at::kLong && order.scalar_type() == at::kLong && skeys.numel() == n * P &&
+                  order.numel() == n * P,
+              "ep_recv_layout: sorted keys / order int64 [n * P]");
+  check_i32(counts, epr, "ep_recv_layout: counts");
+  check_i32(offsets, epr + 1, "ep_recv_layout: offsets");
+  check_i32(row_slot, rows, "ep_recv_layout: row_slot");
+  check_i32(row_tok, rows, "ep_recv_layout: row_tok");
+  TORCH_CHECK(row_w.scalar_type() == at::kFloat && row_w.numel() == rows && stats.scalar_type() == at::kFloat &&
+                  stats.numel() == 2,
+              "ep_recv_layout: row_w / stats fp32");
+  TORCH_CHECK(epr >= 1 && epr <= 255, "ep_recv_layout: at most 255 local experts");
+  EpLayoutParams p{};
+  p.skeys = reinterpret_cast<const long long*>(skeys.data_ptr<int64_t>());
+  p.order = order.data_ptr<int64_t>();
+  p.meta = reinterpret_cast<const int4*>(meta_ptr);
+  p.info = reinterpret_cast<const int*>(info_ptr);
+  p.counts = counts.data_ptr<int>();
+  p.offsets = offsets.data_ptr<int>();
+  p.row_src = row_src.data_ptr<int>();
+  p.row_slot = row_slot.data_ptr<int>();
+  p.row_tok = row_tok.data_ptr<int>();
+  p.row_w = row_w.data_ptr<float>();
+  p.rowmap = reinterpret_cast<int*>(rowmap_ptr);
+  p.stats = stats.data_ptr<float>();
+  p.P = P;
+  p.rows = rows;
+  p.n = static_cast<int>(n);
+  p.epr = static_cast<int>(epr);
+  p.K = static_cast<int>(K);
+  p.E = static_cast<int>(E);
+  p.capacity_factor = capacity_factor;
+  p.host_cap = host_cap;
+  const int dev = skeys.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
+  const long work = std::max<long>(n * P, rows);
+  const int grid = static_cast<int>(std::max<long>(1, std::min<long>((work + 255) / 256, num_sms(dev) * 4)));
+  ep_recv_layout_kernel<<<grid, 256, 0, stream>>>(p);
   NTB_LAUNCH_CHECK(1);
 }
 

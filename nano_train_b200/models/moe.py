@@ -67,6 +67,29 @@ class ExpertMLP(nn.Module):
         return self.dropout(self.down_proj(h))
 
 
+class _RouterFn(torch.autograd.Function):
+    """Fused router kernel (csrc/router.cu): scores, group-limited top-k, weight normalisation,
+    per-expert counts and aux-loss probability sums in one launch; one launch for the backward."""
+
+    @staticmethod
+    def forward(ctx, logits, cfg):
+        idx, w, counts, psum = ops.ext().router_fwd(logits, *cfg)
+        ctx.save_for_backward(logits, idx)
+        ctx.cfg = cfg
+        ctx.mark_non_differentiable(idx, counts)
+        return w, idx, counts, psum
+
+    @staticmethod
+    def backward(ctx, dw, _didx, _dcounts, dpsum):
+        logits, idx = ctx.saved_tensors
+        if dw is None:
+            dw = torch.zeros(idx.shape, dtype=logits.dtype, device=logits.device)
+        if dpsum is None:
+            dpsum = torch.zeros(logits.shape[1], dtype=torch.float32, device=logits.device)
+        return ops.ext().router_bwd(logits, idx, dw.contiguous().to(logits.dtype), dpsum.contiguous().float(),
+                                    *ctx.cfg), None
+
+
 class TopKRouter(nn.Module):
     def __init__(self, hidden_size: int, num_experts: int, top_k: int, *, param_dtype=torch.float32,
                  param_device=None, precision_resolver=None, module_prefix: str = "router",
@@ -91,6 +114,21 @@ class TopKRouter(nn.Module):
         self.routed_scaling_factor = routed_scaling_factor
         self.router = Linear(hidden_size, num_experts, bias=False, param_dtype=param_dtype, param_device=param_device,
                              module_path=f"{module_prefix}.router", precision_resolver=precision_resolver)
+
+    def _kernel_ok(self, logits: torch.Tensor) -> bool:
+        import os
+
+        return (logits.is_cuda and logits.dtype in (torch.bfloat16, torch.float32) and self.num_experts <= 512
+                and self.top_k <= 8 and self.n_group <= 32 and os.environ.get("NTB_ROUTER_KERNEL", "1") != "0")
+
+    def _forward_kernel(self, logits: torch.Tensor) -> RouterOutput:
+        T = logits.shape[0]
+        cfg = (self.top_k, self.scoring_func == "softmax", self.n_group, self.topk_group, self.norm_topk_prob,
+               float(self.routed_scaling_factor))
+        w, idx, counts, psum = _RouterFn.apply(logits.contiguous(), cfg)
+        frac = counts.float() / float(T * self.top_k)
+        aux = ((frac * (psum / float(T))).sum() * float(self.num_experts)).to(logits.dtype)
+        return RouterOutput(idx, w, aux, 0.0)
 
     def _score_experts(self, logits: torch.Tensor) -> torch.Tensor:
         if self.scoring_func == "sigmoid":
@@ -128,6 +166,8 @@ class TopKRouter(nn.Module):
             return RouterOutput(z.long(), z.to(tokens.dtype), torch.zeros((), dtype=tokens.dtype,
                                                                            device=tokens.device), 0.0)
         logits = self.router(tokens)
+        if self._kernel_ok(logits):
+            return self._forward_kernel(logits)
         scores = self._score_experts(logits)
         routed = self._apply_group_routing(scores)
         w, idx = torch.topk(routed, k=self.top_k, dim=-1)

@@ -53,9 +53,16 @@ class _StackCache:
         self.key = None
         self.w1 = None
         self.w2 = None
+        self._params = None
+
+    def params(self, experts):
+        """[gate_0, up_0, down_0, gate_1, ...] weights (list built once per module)."""
+        if self._params is None or len(self._params) != 3 * len(experts):
+            self._params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
+        return self._params
 
     def get(self, experts):
-        params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
+        params = self.params(experts)
         key = tuple((p.data_ptr(), p._version) for p in params)
         if key != self.key:
             with torch.no_grad():
@@ -63,6 +70,48 @@ class _StackCache:
                 self.w2 = torch.cat([e.down_proj.weight for e in experts], 0)
             self.key = key
         return self.w1, self.w2
+
+
+_FLAT_CACHE: dict = {}
+
+
+def _flat_main_grads(params, E: int, I: int, H: int):
+    """Cached form of _flat_main_grads_uncached (keyed by the first and last gradient addresses)."""
+    m0, m1 = getattr(params[0], "main_grad", None), getattr(params[-1], "main_grad", None)
+    if m0 is None or m1 is None:
+        return None
+    key = (m0.data_ptr(), m1.data_ptr(), len(params), E, I, H)
+    hit = _FLAT_CACHE.get(key, 0)
+    if hit == 0:
+        if len(_FLAT_CACHE) > 256:
+            _FLAT_CACHE.clear()
+        hit = _FLAT_CACHE[key] = _flat_main_grads_uncached(params, E, I, H)
+    return hit
+
+
+def _flat_main_grads_uncached(params, E: int, I: int, H: int):
+    """Views for accumulating every expert's weight gradient in one launch per matrix.
+
+    When the fp32 ``main_grad`` of the experts lie in one flat buffer as
+    (gate [I, H], up [I, H], down [H, I]) per expert at a constant stride (the
+    flat optimizer's layout for consecutive ExpertMLPs), returns
+    (rows of pitch H starting at expert 0's gate gradient, rows of pitch I
+    starting at expert 0's down gradient); otherwise None.
+    """
+    mgs = [getattr(p, "main_grad", None) for p in params]
+    if len(mgs) != 3 * E or any(m is None or m.dtype != torch.float32 or not m.is_contiguous() for m in mgs):
+        return None
+    base, step, es = mgs[0].data_ptr(), 3 * I * H, 4
+    st = mgs[0].untyped_storage().data_ptr()
+    for e in range(E):
+        g, u, d = mgs[3 * e:3 * e + 3]
+        if (g.data_ptr() != base + e * step * es or u.data_ptr() != base + (e * step + I * H) * es
+                or d.data_ptr() != base + (e * step + 2 * I * H) * es or g.untyped_storage().data_ptr() != st
+                or u.untyped_storage().data_ptr() != st or d.untyped_storage().data_ptr() != st):
+            return None
+    out1 = mgs[0].as_strided(((E - 1) * 3 * I + 2 * I, H), (H, 1))
+    out2 = mgs[2].as_strided(((E - 1) * 3 * H + H, I), (I, 1))
+    return out1, out2
 
 
 class GroupedBuffers:
@@ -104,24 +153,36 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
         I = I2 // 2
         da = torch.empty_like(a)
         C.gemm_grouped_bf16(dy, w2, da, offsets, 1, b_mn=True)          # dA = dY . W2_e
-        dw2 = torch.zeros(E * H, I, device=dy.device, dtype=torch.float32)
-        C.gemm_grouped_bf16(dy, a, dw2, offsets, 2, b_mn=True)          # dW2_e = dY_e^T A_e
+        flat = _flat_main_grads(ctx.params, E, I, H)
+        dw2 = None
+        if flat is not None:                                              # dW2_e += dY_e^T A_e into main_grad
+            C.gemm_grouped_bf16(dy, a, flat[1], offsets, 2, b_mn=True, accumulate=True, c_group_stride=3 * H)
+        else:
+            dw2 = torch.zeros(E * H, I, device=dy.device, dtype=torch.float32)
+            C.gemm_grouped_bf16(dy, a, dw2, offsets, 2, b_mn=True)      # dW2_e = dY_e^T A_e
         dh = C.swiglu_bwd(da, h)
         bufs = ctx.bufs
         dx = bufs.dx_out if bufs is not None and bufs.dx_out is not None else torch.empty_like(x_pad)
         C.gemm_grouped_bf16(dh, w1, dx, offsets, 1, b_mn=True)          # dX = dH . W1_e
+        if flat is not None:                                              # dW1_e += dH_e^T X_e into main_grad
+            C.gemm_grouped_bf16(dh, x_pad, flat[0], offsets, 2, b_mn=True, accumulate=True, c_group_stride=3 * I)
+            return (dx, None, None, None, None, None, *([None] * len(ctx.params)))
         dw1 = torch.zeros(E * I2, x_pad.shape[1], device=dy.device, dtype=torch.float32)
         C.gemm_grouped_bf16(dh, x_pad, dw1, offsets, 2, b_mn=True)      # dW1_e = dH_e^T X_e
-        grads = []
+        slices = []
         for e in range(E):
-            slices = (dw1[e * I2:e * I2 + I], dw1[e * I2 + I:(e + 1) * I2], dw2[e * H:(e + 1) * H])
-            for p, g in zip(ctx.params[3 * e:3 * e + 3], slices):
-                mg = getattr(p, "main_grad", None)
-                if mg is not None:
-                    mg.add_(g)
-                    grads.append(None)
-                else:
-                    grads.append(g.to(p.dtype))
+            slices += [dw1[e * I2:e * I2 + I], dw1[e * I2 + I:(e + 1) * I2], dw2[e * H:(e + 1) * H]]
+        mgs = [getattr(p, "main_grad", None) for p in ctx.params]
+        if all(m is not None for m in mgs):
+            torch._foreach_add_(mgs, slices)
+            grads = [None] * len(ctx.params)
+        else:
+            # one cast per stacked gradient; each parameter receives a view of it
+            dt = ctx.params[0].dtype
+            dw1c, dw2c = dw1.to(dt), dw2.to(dt)
+            grads = []
+            for e in range(E):
+                grads += [dw1c[e * I2:e * I2 + I], dw1c[e * I2 + I:(e + 1) * I2], dw2c[e * H:(e + 1) * H]]
         return (dx, None, None, None, None, None, *grads)
 
 

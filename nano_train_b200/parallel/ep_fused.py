@@ -97,22 +97,35 @@ class RecvPlan:
     stats: torch.Tensor        # fp32 [2] (dropped, received)
 
 
+def receive_keys(recv_counts: torch.Tensor, meta: torch.Tensor, experts_per_rank: int, top_k: int):
+    """Total order of the received rows (ascending = kept first), as ep_recv_keys computes it:
+    local expert (empty rows last), weight descending, source rank, the source's t * K + k."""
+    n, P = meta.shape[0], meta.shape[1]
+    epr = experts_per_rank
+    valid = torch.arange(P, device=meta.device)[None, :] < recv_counts.clamp(0, P).view(n, 1)
+    le = torch.where(valid, meta[..., 0].clamp(0, epr - 1), torch.full_like(meta[..., 0], epr)).reshape(-1).long()
+    src = torch.arange(n, device=meta.device).view(n, 1).expand(n, P).reshape(-1)
+    flat = (meta[..., 1].long() * top_k + meta[..., 3].long()).reshape(-1) & 0xFFFFF
+    key = (le << 55) | (_desc_float_key(meta[..., 2].reshape(-1)) << 23) | (src << 20) | flat
+    return key, valid, le
+
+
 def plan_receive(recv_counts: torch.Tensor, meta: torch.Tensor, experts_per_rank: int, capacity: torch.Tensor,
-                 rows_bound: int) -> RecvPlan:
-    """Capacity selection and the expert-grouped layout of the received rows.
+                 rows_bound: int, top_k: int) -> RecvPlan:
+    """Capacity selection and the expert-grouped layout of the received rows (PyTorch form of
+    ep_recv_keys + sort + ep_recv_layout, used by the CPU tests).
 
     ``meta`` int32 [n, P, 4] holds {local expert, token, weight bits, k} per slab
     row; rows p >= recv_counts[s] of source s are empty. Each expert keeps its
-    ``capacity`` highest-weight assignments (ties in arrival order: source rank,
-    then the source's sorted order), exactly the unfused module's rule.
+    ``capacity`` highest-weight assignments, ties in arrival order of the unfused
+    module (source rank, then the source's assignments in token order) whatever
+    order the rows landed in the slab.
     """
     n, P = meta.shape[0], meta.shape[1]
     epr = experts_per_rank
     dev = meta.device
-    valid = torch.arange(P, device=dev)[None, :] < recv_counts.clamp(0, P).view(n, 1)
-    le = torch.where(valid, meta[..., 0].clamp(0, epr - 1), torch.full_like(meta[..., 0], epr)).reshape(-1)
-    key = (le.long() << 32) | _desc_float_key(meta[..., 2].reshape(-1))
-    o = torch.argsort(key, stable=True)
+    key, valid, le = receive_keys(recv_counts, meta, epr, top_k)
+    o = torch.argsort(key)
     le_s = le[o]
     counts_all = torch.bincount(le_s, minlength=epr + 1)
     starts = torch.cumsum(counts_all, 0) - counts_all
@@ -271,6 +284,7 @@ class EPWorkspace:
                 self.ptrs.append(p)
                 self._opened.append(p)
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.ctr = torch.zeros(MAX_RANKS, dtype=torch.int32, device=self.device)
         self.epoch = [0, 0, 0, 0]
         self.closed = False
         dist.barrier(group=group)
@@ -311,15 +325,19 @@ class EPWorkspace:
         self._C.ep_wait(self.local + kind * MAX_RANKS * 8, self.n, e, self.device.index)
 
     # -------------------------------------------------------------- steps
-    def dispatch(self, tokens: torch.Tensor, sp: SendPlan, *, stochastic: bool, seed: int):
-        T = tokens.shape[0]
+    def dispatch(self, tokens: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, *, stochastic: bool,
+                 seed: int):
+        """Sends every (token, k) row; returns (dest_tk, slot_tk) int32 [T*K]."""
+        T, K = topk_idx.shape
         if T > self.T:
             raise ValueError(f"EPWorkspace sized for {self.T} tokens per rank, got {T}")
         me, P, H = self.rank, self.P, self.H
         pay_row = H * (1 if self.fp8 else 2)
+        dest_tk = torch.empty(T * K, dtype=torch.int32, device=self.device)
+        slot_tk = torch.empty(T * K, dtype=torch.int32, device=self.device)
         e = self._next(FLAG_DISPATCH)
         self._C.ep_dispatch(
-            tokens, sp.tok, sp.dest, sp.slot, sp.lexp, sp.kslot, sp.w, sp.send_counts,
+            tokens, topk_idx, topk_w, dest_tk, slot_tk, self.ctr, self.epr,
             [p + self.off_payload + me * P * pay_row for p in self.ptrs],
             [p + self.off_pscale + me * P * (H // 128) * 4 for p in self.ptrs] if self.fp8 else [],
             [p + self.off_meta + me * P * 16 for p in self.ptrs],
@@ -327,6 +345,29 @@ class EPWorkspace:
             [p + 256 + me * 16 for p in self.ptrs],
             self.done, P, e, self.fp8, stochastic, seed)
         self._C.ep_wait(self.local + FLAG_DISPATCH * MAX_RANKS * 8, self.n, e, self.device.index)
+        return dest_tk, slot_tk
+
+    def plan(self, *, num_experts: int, capacity_factor: float, host_cap: int) -> RecvPlan:
+        """Capacity selection + grouped layout of what arrived (ep_recv_keys, one sort, ep_recv_layout);
+        writes the row map into the workspace for the sources' combine."""
+        n, P, epr = self.n, self.P, self.epr
+        dev = self.device
+        counts = torch.zeros(epr, dtype=torch.int32, device=dev)
+        keys = torch.empty(n * P, dtype=torch.int64, device=dev)
+        self._C.ep_recv_keys(self.local + self.off_meta, self.local + 256, keys, counts, P, n, epr, self.K)
+        skeys, order = torch.sort(keys)
+        rows = (rows_bound(n, P, epr, host_cap) + SEG - 1) // SEG * SEG
+        offsets = torch.empty(epr + 1, dtype=torch.int32, device=dev)
+        row_src = torch.empty(rows, dtype=torch.int32, device=dev)
+        row_slot = torch.empty(rows, dtype=torch.int32, device=dev)
+        row_tok = torch.empty(rows, dtype=torch.int32, device=dev)
+        row_w = torch.empty(rows, dtype=torch.float32, device=dev)
+        stats = torch.empty(2, dtype=torch.float32, device=dev)
+        self._C.ep_recv_layout(skeys, order, self.local + self.off_meta, self.local + 256, counts, offsets, row_src,
+                               row_slot, row_tok, row_w, self.local + self.off_rowmap, stats, P, n, epr, self.K,
+                               num_experts, float(capacity_factor), int(host_cap))
+        return RecvPlan(offsets=offsets, rows=rows, row_src=row_src, row_slot=row_slot, row_tok=row_tok, row_w=row_w,
+                        rowmap=None, kept_counts=torch.clamp(counts, max=host_cap), stats=stats)
 
     def gather(self, rp: RecvPlan) -> torch.Tensor:
         x = torch.empty(rp.rows, self.H, dtype=torch.bfloat16, device=self.device)
@@ -340,13 +381,13 @@ class EPWorkspace:
                                   self.local + self.off_ys, stochastic, seed)
         self._signal_and_wait(FLAG_Y)
 
-    def pull_combine(self, sp: SendPlan, w_tk: torch.Tensor, T: int, save: bool):
+    def pull_combine(self, dest_tk: torch.Tensor, slot_tk: torch.Tensor, w_tk: torch.Tensor, T: int, save: bool):
         K = self.K
         out = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
         y_save = torch.empty(T * K, self.H, dtype=torch.bfloat16, device=self.device) if save else None
         pos = torch.empty(T * K, dtype=torch.int32, device=self.device)
         src = [p + (self.off_yq if self.fp8 else self.off_y) for p in self.ptrs]
-        self._C.ep_pull(out, sp.dest_tk, sp.slot_tk, w_tk, None,
+        self._C.ep_pull(out, dest_tk, slot_tk, w_tk, None,
                         [p + self.off_rowmap + self.rank * self.P * 4 for p in self.ptrs], src,
                         [p + self.off_ys for p in self.ptrs] if self.fp8 else [], self.P, self.R, self.fp8,
                         y_save=y_save, pos_out=pos)
@@ -360,12 +401,12 @@ class EPWorkspace:
                                [p + self.off_dout for p in self.ptrs], T)
         return dy
 
-    def dispatch_backward(self, g_xpad: torch.Tensor, sp: SendPlan, pos_tk: torch.Tensor, T: int) -> torch.Tensor:
+    def dispatch_backward(self, g_xpad: torch.Tensor, dest_tk: torch.Tensor, pos_tk: torch.Tensor, T: int):
         if g_xpad.data_ptr() != self.local + self.off_dx:
             self.dx(g_xpad.shape[0]).copy_(g_xpad)
         self._signal_and_wait(FLAG_DX)
         dx = torch.empty(T, self.H, dtype=torch.bfloat16, device=self.device)
-        self._C.ep_pull(dx, sp.dest_tk, sp.slot_tk, None, pos_tk, [], [p + self.off_dx for p in self.ptrs], [],
+        self._C.ep_pull(dx, dest_tk, dest_tk, None, pos_tk, [], [p + self.off_dx for p in self.ptrs], [],
                         self.P, self.R, False)
         return dx
 
@@ -412,16 +453,17 @@ def fused_ep_enabled(group) -> bool:
 @dataclass
 class _CallState:
     ws: EPWorkspace
-    sp: SendPlan
+    topk_idx: torch.Tensor
+    topk_w: torch.Tensor
     T: int
     host_cap: int
     capacity_factor: float
     num_experts: int
-    fp8: bool
     stochastic: bool
+    dest_tk: Optional[torch.Tensor] = None
+    slot_tk: Optional[torch.Tensor] = None
     rp: Optional[RecvPlan] = None
     pos_tk: Optional[torch.Tensor] = None
-    extra: dict = field(default_factory=dict)
 
 
 def _seed(stochastic: bool) -> int:
@@ -432,20 +474,16 @@ class _EPDispatchFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, tokens, st: _CallState):
         ws = st.ws
-        ws.dispatch(tokens.contiguous(), st.sp, stochastic=st.stochastic, seed=_seed(st.stochastic))
-        info = ws.info()
-        t_all = info[:, 1].sum()
-        cap = capacity_tensor(t_all, st.capacity_factor, ws.K, st.num_experts, st.host_cap)
-        rp = plan_receive(info[:, 0], ws.meta(), ws.epr, cap, rows_bound(ws.n, ws.P, ws.epr, st.host_cap))
-        ws.rowmap().copy_(rp.rowmap)
-        st.rp = rp
+        st.dest_tk, st.slot_tk = ws.dispatch(tokens.contiguous(), st.topk_idx, st.topk_w.detach().contiguous(),
+                                             stochastic=st.stochastic, seed=_seed(st.stochastic))
+        st.rp = ws.plan(num_experts=st.num_experts, capacity_factor=st.capacity_factor, host_cap=st.host_cap)
         ctx.st = st
-        return ws.gather(rp)
+        return ws.gather(st.rp)
 
     @staticmethod
     def backward(ctx, g):
         st = ctx.st
-        return st.ws.dispatch_backward(g.contiguous(), st.sp, st.pos_tk, st.T), None
+        return st.ws.dispatch_backward(g.contiguous(), st.dest_tk, st.pos_tk, st.T), None
 
 
 class _EPCombineFn(torch.autograd.Function):
@@ -453,7 +491,8 @@ class _EPCombineFn(torch.autograd.Function):
     def forward(ctx, y, w_tk, st: _CallState):
         ws = st.ws
         ws.publish_y(st.rp, stochastic=st.stochastic, seed=_seed(st.stochastic))
-        out, y_save, pos = ws.pull_combine(st.sp, w_tk.detach().contiguous(), st.T, save=ctx.needs_input_grad[1])
+        out, y_save, pos = ws.pull_combine(st.dest_tk, st.slot_tk, w_tk.detach().contiguous(), st.T,
+                                           save=ctx.needs_input_grad[1])
         st.pos_tk = pos
         ctx.st = st
         ctx.save_for_backward(y_save if y_save is not None else torch.empty(0))
@@ -483,14 +522,13 @@ def fused_ep_moe(tokens: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Ten
     epr = num_experts // n
     ws = get_workspace(group, tokens=T, hidden=H, top_k=K, experts_per_rank=epr, fp8=fp8_payload)
     host_cap = max(int(math.ceil(capacity_factor * (n * T) * K / float(num_experts))), 1)
-    st = _CallState(ws=ws, sp=plan_send(topk_idx, topk_w, epr, n), T=T, host_cap=host_cap,
-                    capacity_factor=capacity_factor, num_experts=num_experts, fp8=fp8_payload, stochastic=stochastic)
+    st = _CallState(ws=ws, topk_idx=topk_idx.contiguous(), topk_w=topk_w, T=T, host_cap=host_cap,
+                    capacity_factor=capacity_factor, num_experts=num_experts, stochastic=stochastic)
     x_pad = _EPDispatchFn.apply(tokens, st)
     rp = st.rp
     w1, w2 = stack_cache.get(experts)
-    params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
     bufs = GroupedBuffers(y_out=ws.y(rp.rows), dx_out=ws.dx(rp.rows))
     y = _GroupedSwiGLUFn.apply(x_pad, rp.offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), bufs,
-                               *params)
+                               *stack_cache.params(experts))
     out = _EPCombineFn.apply(y, topk_w.float().reshape(-1), st)
     return out.to(tokens.dtype), rp.stats, rp.kept_counts

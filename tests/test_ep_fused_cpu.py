@@ -5,6 +5,7 @@ pull); the send / receive plans are the production code. The result must
 equal a single-process MoE over every rank's tokens with the reference's
 capacity rule (highest-weight assignments per expert, ties in arrival order).
 """
+import dataclasses
 import math
 
 import pytest
@@ -13,6 +14,18 @@ import torch
 from nano_train_b200.models.moe import capacity_select
 from nano_train_b200.parallel.ep_fused import (_desc_float_key, capacity_tensor, emulate_exchange, emulate_gather,
                                                emulate_pull, plan_receive, plan_send, rows_bound)
+
+
+def _shuffle_slots(sp, n, K, gen):
+    """The kernel reserves slab rows with atomics: any permutation of a destination block is possible."""
+    slot = sp.slot.clone()
+    for d in range(n):
+        sel = (sp.dest == d).nonzero().flatten()
+        slot[sel] = slot[sel][torch.randperm(sel.numel(), generator=gen)]
+    slot_tk = torch.empty_like(slot)
+    order = sp.tok.long() * K + sp.kslot.long()
+    slot_tk[order] = slot
+    return dataclasses.replace(sp, slot=slot, slot_tk=slot_tk)
 
 
 def _expert_fn(x: torch.Tensor, e: int) -> torch.Tensor:
@@ -27,9 +40,10 @@ def _route(T, E, K, gen, tie_grid=None):
     return idx, w
 
 
-@pytest.mark.parametrize("n,E,K,T,cf,tie", [(3, 6, 2, 7, 0.5, None), (2, 8, 3, 16, 1.0, None),
-                                            (4, 8, 2, 9, 0.4, 4), (2, 4, 1, 5, 4.0, None)])
-def test_fused_plan_matches_capacity_semantics(n, E, K, T, cf, tie):
+@pytest.mark.parametrize("n,E,K,T,cf,tie,shuffle", [(3, 6, 2, 7, 0.5, None, False), (2, 8, 3, 16, 1.0, None, True),
+                                                    (4, 8, 2, 9, 0.4, 4, True), (4, 8, 2, 9, 0.4, 4, False),
+                                                    (2, 4, 1, 5, 4.0, None, True)])
+def test_fused_plan_matches_capacity_semantics(n, E, K, T, cf, tie, shuffle):
     gen = torch.Generator().manual_seed(n * 100 + E + K + T)
     H = 16
     epr = E // n
@@ -38,6 +52,8 @@ def test_fused_plan_matches_capacity_semantics(n, E, K, T, cf, tie):
     P = T * K
     host_cap = max(int(math.ceil(cf * (n * T) * K / float(E))), 1)
     plans = [plan_send(idx, w, epr, n) for idx, w in routes]
+    if shuffle:
+        plans = [_shuffle_slots(sp, n, K, gen) for sp in plans]
     for sp in plans:  # each destination's block is filled by contiguous slots 0..count-1
         for d in range(n):
             sl = sp.slot[sp.dest == d].sort().values
@@ -48,7 +64,7 @@ def test_fused_plan_matches_capacity_semantics(n, E, K, T, cf, tie):
         counts, meta, payload = exch[d]
         t_all = torch.tensor(n * T)
         cap = capacity_tensor(t_all, cf, K, E, host_cap)
-        rp = plan_receive(counts, meta, epr, cap, rows_bound(n, P, epr, host_cap))
+        rp = plan_receive(counts, meta, epr, cap, rows_bound(n, P, epr, host_cap), K)
         x = emulate_gather(payload, rp)
         y = torch.zeros_like(x)
         for e in range(epr):
@@ -85,7 +101,7 @@ def test_dispatch_backward_pull_sums_k_copies():
     plans = [plan_send(i, w, epr, n) for i, w in routes]
     exch = emulate_exchange(tokens, plans, epr, P)
     host_cap = 10 ** 6
-    rps = [plan_receive(c, m, epr, torch.tensor(host_cap), rows_bound(n, P, epr, host_cap)) for c, m, _ in exch]
+    rps = [plan_receive(c, m, epr, torch.tensor(host_cap), rows_bound(n, P, epr, host_cap), K) for c, m, _ in exch]
     gx = [emulate_gather(exch[d][2], rps[d]) for d in range(n)]  # gradient rows = the payload itself
     for s in range(n):
         dx = emulate_pull(T, K, plans[s], [rp.rowmap for rp in rps], gx, None, s, P)

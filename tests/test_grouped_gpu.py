@@ -58,14 +58,27 @@ def test_grouped_gemm_three_forms(counts, H, N):
         assert float(y[pad].abs().sum()) == 0.0
 
 
-def test_grouped_swiglu_experts_matches_loop():
+@pytest.mark.parametrize("grad_mode", ["grad", "flat_main_grad", "separate_main_grad"])
+def test_grouped_swiglu_experts_matches_loop(grad_mode):
+    """.grad outputs; fp32 main_grad in a flat buffer (accumulated by the weight-gradient GEMM in place,
+    one launch per matrix); fp32 main_grad tensors at unrelated addresses (one multi-tensor add)."""
     from nano_train_b200.models.moe import ExpertMLP
-    from nano_train_b200.ops.grouped import _StackCache, grouped_swiglu_experts
+    from nano_train_b200.ops.grouped import _StackCache, _flat_main_grads, grouped_swiglu_experts
+    from nano_train_b200.parallel.flat_optimizer import FlatParamBuffer
 
     dev = torch.device("cuda", 0)
     torch.manual_seed(3)
     E, H, I = 5, 256, 192
     experts = torch.nn.ModuleList([ExpertMLP(H, I, param_dtype=torch.bfloat16, param_device=dev) for _ in range(E)])
+    plist = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
+    if grad_mode == "flat_main_grad":
+        buf = FlatParamBuffer(plist)
+        assert _flat_main_grads(plist, E, I, H) is not None
+        buf.grad_data.fill_(0.25)  # accumulation must add to what is there
+    elif grad_mode == "separate_main_grad":
+        for p in plist:
+            p.main_grad = torch.full(p.shape, 0.25, device=dev, dtype=torch.float32)
+        assert _flat_main_grads(plist, E, I, H) is None
     counts = torch.tensor([37, 0, 129, 64, 3], device=dev)
     x = torch.randn(int(counts.sum()), H, device=dev, dtype=torch.bfloat16, requires_grad=True)
     y = grouped_swiglu_experts(x, counts, experts, _StackCache())
@@ -88,8 +101,16 @@ def test_grouped_swiglu_experts_matches_loop():
     assert _rel(y, yr) < 2e-2
     assert _rel(x.grad, xr.grad) < 2e-2
     for e in range(E):
-        if counts[e] == 0:
-            continue
         for p, r in zip((experts[e].gate_proj.weight, experts[e].up_proj.weight, experts[e].down_proj.weight),
                         ref_params[e]):
-            assert _rel(p.grad, r.grad) < 3e-2, e
+            if grad_mode == "grad":
+                if counts[e] == 0:
+                    continue
+                assert _rel(p.grad, r.grad) < 3e-2, e
+            else:
+                assert p.grad is None
+                got = p.main_grad - 0.25
+                if counts[e] == 0:
+                    assert got.abs().max().item() == 0.0, e
+                else:
+                    assert _rel(got, r.grad) < 3e-2, e
