@@ -109,6 +109,16 @@ void ep_pull(at::Tensor& out, const at::Tensor& dest_tk, const at::Tensor& slot_
              const c10::optional<at::Tensor>& pos_out);
 void ep_combine_bwd(at::Tensor& dy, const at::Tensor& rows_used, const at::Tensor& row_src, const at::Tensor& row_tok,
                     const at::Tensor& row_w, std::vector<int64_t> dout, int64_t T);
+// zero_fused.cu
+void zero_reduce_scatter(std::vector<std::vector<int64_t>> grad_ptrs, const std::vector<at::Tensor>& red,
+                         std::vector<int64_t> cls, at::Tensor& stats_acc, std::vector<int64_t> stats_slots,
+                         std::vector<int64_t> flag_stats, const at::Tensor& done, int64_t me, int64_t epoch);
+void zero_adam_allgather(std::vector<std::vector<int64_t>> param_ptrs, const std::vector<at::Tensor>& red,
+                         const std::vector<at::Tensor>& master, const std::vector<at::Tensor>& m,
+                         const std::vector<at::Tensor>& v, std::vector<double> lr, std::vector<double> wd,
+                         int64_t stats_in_ptr, int64_t my_stats_flags_ptr, std::vector<int64_t> flag_params,
+                         const at::Tensor& done, int64_t me, int64_t epoch, double b1, double b2, double eps,
+                         int64_t step, double inv_dp, double max_norm, at::Tensor& grad_norm, at::Tensor& scale_out);
 // symm.cpp
 std::tuple<int64_t, py::bytes> symm_alloc(int64_t bytes);
 int64_t symm_open(py::bytes handle);
@@ -167,6 +177,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_recv_layout", &ntb::ep_recv_layout);
   m.def("ep_wait", &ntb::ep_wait);
   m.def("router_fwd", &ntb::router_fwd);
+  m.def("zero_reduce_scatter", &ntb::zero_reduce_scatter);
+  m.def("zero_adam_allgather", &ntb::zero_adam_allgather);
   m.def("router_bwd", &ntb::router_bwd);
   m.def("ep_signal", &ntb::ep_signal);
   m.def("ep_gather", &ntb::ep_gather);

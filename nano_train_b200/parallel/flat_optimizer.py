@@ -57,8 +57,20 @@ class _Slot:
 class FlatParamBuffer:
     """Contiguous storage of a parameter group and its fp32 gradient."""
 
+    @staticmethod
+    def padded_numel(params: list[torch.nn.Parameter], dp_size: int = 1) -> int:
+        """Elements of the buffer FlatParamBuffer(params, dp_size=...) allocates."""
+        seen, off = set(), 0
+        for p in params:
+            if id(p) not in seen:
+                seen.add(id(p))
+                off = _round_up(off + p.numel(), _ALIGN)
+        return _round_up(max(off, 1), _ALIGN * dp_size)
+
     def __init__(self, params: list[torch.nn.Parameter], *, dp_size: int = 1, grad_dtype=torch.float32,
-                 name: str = "buffer"):
+                 name: str = "buffer", storage: Optional[tuple] = None):
+        """``storage``: optional caller-owned (param_data, grad_data) 1-D tensors of the padded size
+        (e.g. views of peer-visible memory); zeroed here."""
         self.name = name
         seen = set()
         uniq = []
@@ -79,8 +91,16 @@ class FlatParamBuffer:
         total = _round_up(max(off, 1), _ALIGN * dp_size)
         self.numel = total
         self.dtype = dtype
-        self.param_data = torch.zeros(total, dtype=dtype, device=device)
-        self.grad_data = torch.zeros(total, dtype=grad_dtype, device=device)
+        if storage is None:
+            self.param_data = torch.zeros(total, dtype=dtype, device=device)
+            self.grad_data = torch.zeros(total, dtype=grad_dtype, device=device)
+        else:
+            self.param_data, self.grad_data = storage
+            if (self.param_data.numel() != total or self.grad_data.numel() != total or self.param_data.dtype != dtype
+                    or self.grad_data.dtype != grad_dtype):
+                raise ValueError(f"{name}: storage must be ({total} x {dtype}, {total} x {grad_dtype})")
+            self.param_data.zero_()
+            self.grad_data.zero_()
         for s in self.slots:
             view = self.param_data[s.offset: s.offset + s.numel].view_as(s.param)
             view.copy_(s.param.data)
@@ -112,7 +132,9 @@ class FlatAdamW:
     def __init__(self, param_groups: list[dict], *, lr: float = 1e-3, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, dp_group=None, strategy: str = "no_shard",
                  max_grad_norm: Optional[float] = None, grad_norm_group=None, tp_group=None,
-                 sequence_parallel: bool = False):
+                 sequence_parallel: bool = False, fused_dp: Optional[bool] = None):
+        """``fused_dp``: run the sharded step as the peer-memory kernels of parallel/zero_fused.py
+        (None: whenever the group allows it; NTB_FUSED_ZERO=0 turns it off)."""
         if strategy not in ("no_shard", "optim", "optim_grads"):
             raise ValueError(f"unknown sharding strategy {strategy}")
         self.lr = lr
@@ -133,11 +155,20 @@ class FlatAdamW:
         self.shards: list[dict] = []
         dp_for_pad = self.dp_size if self.strategy != "no_shard" else 1
         all_params = []
-        for i, g in enumerate(param_groups):
-            params = [p for p in g["params"] if p.requires_grad]
-            if not params:
-                continue
-            buf = FlatParamBuffer(params, dp_size=dp_for_pad, name=g.get("name", f"group{i}"))
+        groups = [(i, g, [p for p in g["params"] if p.requires_grad]) for i, g in enumerate(param_groups)]
+        groups = [(i, g, ps) for i, g, ps in groups if ps]
+        self._zsym = None
+        if self.strategy != "no_shard" and fused_dp is not False and groups:
+            from .zero_fused import ZeroSymm, fused_zero_available
+
+            dts = [p.dtype for _, _, ps in groups for p in ps]
+            if fused_zero_available(dp_group, dts, grad_norm_group=self.grad_norm_group) \
+                    and all(p.is_cuda for _, _, ps in groups for p in ps):
+                self._zsym = ZeroSymm(dp_group, [FlatParamBuffer.padded_numel(ps, dp_for_pad) for _, _, ps in groups],
+                                      groups[0][2][0].device)
+        for bi, (i, g, params) in enumerate(groups):
+            storage = self._zsym.views(bi) if self._zsym is not None else None
+            buf = FlatParamBuffer(params, dp_size=dp_for_pad, name=g.get("name", f"group{i}"), storage=storage)
             self.buffers.append(buf)
             self.group_wd.append(g.get("weight_decay", weight_decay))
             self.group_replicated.append(bool(g.get("tp_replicated", False)))
@@ -185,10 +216,26 @@ class FlatAdamW:
             out.append(g[sh["lo"]: sh["hi"]])
         return out
 
+    @property
+    def fused_dp(self) -> bool:
+        """True when the sharded step runs as the peer-memory kernels (no NCCL)."""
+        return self._zsym is not None
+
     @torch.no_grad()
     def step(self, lr: Optional[float] = None) -> None:
         """One update. ``lr`` overrides the groups' learning rates for this step."""
         self.step_count += 1
+        if self._zsym is not None:
+            for buf, rep in zip(self.buffers, self.group_replicated):
+                if rep and self.sequence_parallel:
+                    dist.all_reduce(buf.grad_data, group=self.tp_group)
+            lrs = [float(pg["lr"]) if lr is None else float(lr) for pg in self.param_groups]
+            self._zsym.step(self.shards, lrs, [float(pg["weight_decay"]) for pg in self.param_groups],
+                            self.group_replicated, step=self.step_count, betas=self.betas, eps=self.eps,
+                            inv_dp=1.0 / self.dp_size, max_norm=float(self.max_grad_norm or 0.0))
+            self.last_grad_norm = self._zsym.grad_norm
+            self._scale = self._zsym.scale
+            return
         grads = self._reduce_grads()
         inv_dp = 1.0 / self.dp_size
         if self.max_grad_norm is not None and self.max_grad_norm > 0:

@@ -1,0 +1,90 @@
+"""Fused ZeRO step (peer-memory reduce-scatter + AdamW + all-gather) vs the NCCL step (2 GPUs).
+
+Two copies of the same model per rank: one under FlatAdamW with the fused
+kernels, one with NCCL reduce-scatter / all-gather. After every step the
+parameters and the gradient norm must agree, and the fused copy must be
+bit-identical on every rank (each shard is written once, by its owner, into
+every rank's buffer).
+"""
+import datetime
+import os
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from conftest import free_port
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(seed):
+    torch.manual_seed(seed)
+    m = torch.nn.Sequential(torch.nn.Linear(256, 320), torch.nn.GELU(), torch.nn.Linear(320, 100),
+                            torch.nn.LayerNorm(100), torch.nn.Linear(100, 36))
+    return m.to(device="cuda", dtype=torch.bfloat16)
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from nano_train_b200.ops._ext import check_status
+        from nano_train_b200.parallel.flat_optimizer import FlatAdamW, split_decay_groups
+
+        res = []
+        for strategy, clip in (("optim_grads", 1.0), ("optim", None)):
+            ma, mb = _model(0), _model(0)
+            oa = FlatAdamW(split_decay_groups(ma, 0.1), lr=3e-3, weight_decay=0.1, dp_group=dist.group.WORLD,
+                           strategy=strategy, max_grad_norm=clip, fused_dp=True)
+            ob = FlatAdamW(split_decay_groups(mb, 0.1), lr=3e-3, weight_decay=0.1, dp_group=dist.group.WORLD,
+                           strategy=strategy, max_grad_norm=clip, fused_dp=False)
+            assert oa.fused_dp and not ob.fused_dp
+            for it in range(4):
+                g = torch.Generator(device="cuda").manual_seed(10 * it + rank)
+                x = torch.randn(64, 256, device="cuda", dtype=torch.bfloat16, generator=g)
+                for m, o in ((ma, oa), (mb, ob)):
+                    o.zero_grad()
+                    (m(x).float().pow(2).mean() * 10).backward()
+                    o.step()
+                pa = torch.cat([p.detach().float().flatten() for p in ma.parameters()])
+                pb = torch.cat([p.detach().float().flatten() for p in mb.parameters()])
+                rel = ((pa - pb).norm() / pb.norm()).item()
+                gn = (float(oa.last_grad_norm.reshape(-1)[0]), float(ob.last_grad_norm.reshape(-1)[0])) \
+                    if clip else (0.0, 0.0)
+                allp = [torch.empty_like(pa) for _ in range(world)]
+                dist.all_gather(allp, pa)
+                same = all(torch.equal(allp[0], t) for t in allp)
+                res.append((strategy, it, rel, gn, same))
+        torch.cuda.synchronize()
+        check_status(rank)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, res, None))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        import traceback
+
+        q.put((rank, None, repr(e) + traceback.format_exc()))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_zero_step_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = [q.get(timeout=300) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    for rank, res, exc in results:
+        assert exc is None, f"rank {rank}: {exc}"
+        for strategy, it, rel, gn, same in res:
+            print(rank, strategy, it, rel, gn, same)
+            assert same, (strategy, it)
+            assert rel < 5e-3, (strategy, it, rel)
+            assert abs(gn[0] - gn[1]) <= 1e-3 * max(abs(gn[1]), 1e-6), (strategy, it, gn)
