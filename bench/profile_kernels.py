@@ -18,6 +18,13 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   adamw         fused flat AdamW over 64M fp32 elements
   swiglu        SwiGLU fwd 8192 x 14336
   ce            vocab cross-entropy stats+bwd 4096 x 32064
+  router        fused top-k router fwd, 16384 tokens x 64 experts, top-6 softmax (bf16)
+  router_bwd    its backward
+  ep_layer      expert-parallel dispatch -> receive plan -> gather -> pull-combine of one MoE layer
+                (8192 tokens x 2048, top-6 of 64 experts), run as a 1-rank group: every "peer" pointer
+                is this GPU's own memory, so the kernels' code and memory behaviour are captured on one GPU
+  zero_step     fused ZeRO step (reduce-scatter pull + AdamW + parameter stores) over 64M parameters,
+                1-rank group (same reason)
 """
 import argparse
 import os
@@ -106,6 +113,55 @@ def main():
         logits = torch.randn(4096, 32064, **bf)
         labels = torch.randint(0, 32064, (4096,), device=dev)
         fn = lambda: C.ce_stats(logits, labels, 0, -100)  # noqa: E731
+    elif a.case in ("router", "router_bwd"):
+        logits = torch.randn(16384, 64, **bf)
+        cfg = (6, True, 1, 1, True, 1.0)
+        idx, w, _, _ = C.router_fwd(logits, *cfg)
+        dw = torch.randn_like(w)
+        dps = torch.randn(64, device=dev)
+        if a.case == "router":
+            fn = lambda: C.router_fwd(logits, *cfg)  # noqa: E731
+        else:
+            fn = lambda: C.router_bwd(logits, idx, dw, dps, *cfg)  # noqa: E731
+    elif a.case in ("ep_layer", "zero_step"):
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", rank=0, world_size=1, init_method="tcp://127.0.0.1:29561",
+                                device_id=dev)
+        if a.case == "ep_layer":
+            from nano_train_b200.parallel.ep_fused import EPWorkspace
+
+            T, H, K, E = 8192, 2048, 6, 64
+            ws = EPWorkspace(dist.group.WORLD, max_tokens=T, hidden=H, top_k=K, experts_per_rank=E,
+                             fp8_payload=False, device=dev)
+            tokens = torch.randn(T, H, **bf)
+            w, idx = torch.topk(torch.softmax(torch.randn(T, E, device=dev), -1), K, dim=-1)
+            wf = w.reshape(-1).contiguous()
+            host_cap = int(1.25 * T * K / E) + 1
+
+            def fn():
+                dest, slot = ws.dispatch(tokens, idx, w, stochastic=False, seed=0)
+                rp = ws.plan(num_experts=E, capacity_factor=1.25, host_cap=host_cap)
+                x = ws.gather(rp)
+                ws.y(rp.rows).copy_(x)
+                ws.publish_y(rp, stochastic=False, seed=0)
+                ws.pull_combine(dest, slot, wf, T, save=True)
+        else:
+            from nano_train_b200.parallel.zero_fused import ZeroSymm
+
+            P = 64 * 2 ** 20
+            zs = ZeroSymm(dist.group.WORLD, [P], dev)
+            pv, gv = zs.views(0)
+            pv.normal_(0, 0.02)
+            gv.normal_(0, 1e-3)
+            sh = dict(lo=0, hi=P, master=pv.float(), exp_avg=torch.zeros(P, device=dev),
+                      exp_avg_sq=torch.zeros(P, device=dev))
+            it = [0]
+
+            def fn():
+                it[0] += 1
+                zs.step([sh], [1e-4], [0.1], [0], step=it[0], betas=(0.9, 0.95), eps=1e-8, inv_dp=1.0,
+                        max_norm=1.0)
     else:
         raise SystemExit(f"unknown case {a.case}")
     for _ in range(2 + a.iters):
