@@ -197,9 +197,7 @@ def run_ours(args, rank, local, world):
         a = get_communicator(dist.group.WORLD)
         if a is not None and hasattr(a, "choice"):
             fused_paths = {f"{k[0]} x{list(k[1])} w{list(k[2])}{' bmn' if k[3] else ''}":
-                           {"path": v, "fused_ms": round(a.timings.get(k, (0, 0))[0], 4),
-                            "nccl_gemm_ms": round(a.timings.get(k, (0, 0))[1], 4)}
-                           for k, v in a.choice.items()}
+                           {"path": v, "ms": a.timings.get(k, {})} for k, v in a.choice.items()}
 
     e2e = None
     if not args.no_e2e:

@@ -132,6 +132,7 @@ def main():
             w = torch.randn(K, N, device="cuda", dtype=torch.bfloat16) if b_mn else \
                 torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
             fused = lambda: c.gemm_reduce_scatter(x, w, b_mn=b_mn)
+            pull = lambda: c.gemm_reduce_scatter_pull(x, w, b_mn=b_mn)
             nccl = lambda: comm.reduce_scatter_dim0(gemm(x, w, b_mn=b_mn), g)
             alone = lambda: gemm(x, w, b_mn=b_mn)
             flops = 2.0 * T * N * K
@@ -151,6 +152,11 @@ def main():
         roof = max(flops / (peak * 1e12), nvl_bytes / (NVLINK_GBS * 1e9)) * 1e3
         row = dict(op=name, n=n, T=T, K=K, N=N, fused_ms=tf, nccl_ms=tn, gemm_ms=ta, roof_ms=roof,
                    frac=roof / tf, speedup_vs_nccl=tn / tf, peak=f"{peak} TFLOP/s ({peak_kind})")
+        if kind == "rs":
+            ref = nccl().float()
+            rel = ((pull().float() - ref).norm() / ref.norm()).item()
+            tp = timeit(pull, args.iters)
+            row.update(pull_ms=tp, pull_frac=roof / tp, pull_speedup_vs_nccl=tn / tp, pull_rel_err_vs_nccl=rel)
         rows.append(row)
         if rank == 0:
             print(json.dumps(row), flush=True)

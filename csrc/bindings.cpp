@@ -79,6 +79,7 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
              bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> tctrs, at::Tensor& ctrs, int64_t rank,
              int64_t epoch, const c10::optional<at::Tensor>& trace);
 void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns);
+void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank);
 // router.cu
 std::vector<at::Tensor> router_fwd(const at::Tensor& logits, int64_t K, bool softmax, int64_t n_group,
                                    int64_t topk_group, bool norm_topk, double scale);
@@ -168,6 +169,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &ntb::gemm_rs, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("b_mn"),
         py::arg("recv"), py::arg("tctrs"), py::arg("ctrs"), py::arg("rank"), py::arg("epoch"),
         py::arg("trace") = py::none());
+  m.def("rs_pull", &ntb::rs_pull, py::arg("parts"), py::arg("out"), py::arg("bias"), py::arg("rank"));
   m.def("wait_flag", &ntb::wait_flag, py::arg("flag"), py::arg("expect"), py::arg("limit_ns"));
   m.def("ep_dispatch", &ntb::ep_dispatch, py::arg("x"), py::arg("idx"), py::arg("w"), py::arg("dest_tk"),
         py::arg("slot_tk"), py::arg("ctr"), py::arg("epr"), py::arg("payload"), py::arg("pscale"), py::arg("meta"),

@@ -755,6 +755,79 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
 }
 
 
+// ================================================================== pull reduce-scatter
+// out[T_local, N] = sum_r part_r[rank * T_local : (rank + 1) * T_local, :] (+ bias), part_r being rank r's
+// full GEMM partial in its symmetric slot. Called after every rank published its partial; each
+// thread issues its n peer loads before it adds them (fixed rank order, so every rank reduces
+// its rows the same way), 16 bytes per load.
+struct RsPullParams {
+  const bf16* part[kMaxRanks];  // rank r's partial, already offset to this rank's first row
+  bf16* out;
+  const bf16* bias;
+  long rows, N, ld_part, ld_out;
+  int n;
+};
+
+__global__ void __launch_bounds__(256) rs_pull_kernel(const __grid_constant__ RsPullParams p) {
+  const long cpr = p.N / 8;  // 16-byte chunks per row
+  const long total = p.rows * cpr;
+  for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
+       i += static_cast<long>(gridDim.x) * blockDim.x) {
+    const long r = i / cpr, c = (i - r * cpr) * 8;
+    uint4 v[kMaxRanks];
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s)
+      if (s < p.n) v[s] = *reinterpret_cast<const uint4*>(p.part[s] + r * p.ld_part + c);
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int s = 0; s < kMaxRanks; ++s)
+      if (s < p.n) {
+        acc[0] += bf16_lo(v[s].x); acc[1] += bf16_hi(v[s].x); acc[2] += bf16_lo(v[s].y); acc[3] += bf16_hi(v[s].y);
+        acc[4] += bf16_lo(v[s].z); acc[5] += bf16_hi(v[s].z); acc[6] += bf16_lo(v[s].w); acc[7] += bf16_hi(v[s].w);
+      }
+    if (p.bias != nullptr) {
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] += __bfloat162float(p.bias[c + u]);
+    }
+    uint4 o;
+    o.x = pack_bf16x2(acc[0], acc[1]);
+    o.y = pack_bf16x2(acc[2], acc[3]);
+    o.z = pack_bf16x2(acc[4], acc[5]);
+    o.w = pack_bf16x2(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(p.out + r * p.ld_out + c) = o;
+  }
+}
+
+// parts: int64 [n] device addresses of every rank's partial [n * T_local, N] (row pitch N)
+void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank) {
+  const int n = static_cast<int>(parts.size());
+  TORCH_CHECK(n >= 1 && n <= kMaxRanks && rank >= 0 && rank < n, "rs_pull: 1..8 ranks");
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.is_contiguous(),
+              "rs_pull: out bf16 [T_local, N]");
+  const int64_t rows = out.size(0), N = out.size(1);
+  TORCH_CHECK(N % 8 == 0, "rs_pull: N multiple of 8");
+  if (bias.has_value())
+    TORCH_CHECK(bias->scalar_type() == at::kBFloat16 && bias->numel() == N && bias->is_contiguous(), "rs_pull: bias");
+  RsPullParams p{};
+  for (int i = 0; i < n; ++i) {
+    TORCH_CHECK(parts[i] % 16 == 0, "rs_pull: 16-byte aligned partials");
+    p.part[i] = reinterpret_cast<const bf16*>(parts[i]) + rank * rows * N;
+  }
+  p.out = reinterpret_cast<bf16*>(out.data_ptr());
+  p.bias = bias.has_value() ? reinterpret_cast<const bf16*>(bias->data_ptr()) : nullptr;
+  p.rows = rows;
+  p.N = N;
+  p.ld_part = N;
+  p.ld_out = N;
+  p.n = n;
+  const int dev = out.get_device();
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
+  const long chunks = rows * (N / 8);
+  const int grid = static_cast<int>(std::max<long>(1, std::min<long>((chunks + 255) / 256, num_sms(dev) * 8L)));
+  rs_pull_kernel<<<grid, 256, 0, stream>>>(p);
+  NTB_LAUNCH_CHECK(1);
+}
+
 // ================================================================== bounded flag wait
 // One thread waits until *flag >= expect (acquire, system scope) for at most
 // limit_ns; on expiry it records kStatusTimeoutPeer in the device status word

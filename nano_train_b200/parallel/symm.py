@@ -5,11 +5,15 @@ layout (``cudaMalloc`` + CUDA IPC handle, exchanged once through the process
 group) and opens every peer's buffer, so the fused kernels address peer
 memory directly over NVLink:
 
-    [0, 4 KiB)          control words: AG ready epoch (u64 @0)
+    [0, 4 KiB)          control words: AG ready epoch (u64 @0); pull reduce-scatter
+                        "partial written" epochs (u64 [8 sources] @512)
     RS tile counters x2 per-tile arrival counters (u32, one per 128 x 128 output
                         tile of this rank's chunk) per epoch parity; zero at rest
     AG slots  x2        this rank's activation shard [T_local, K] per epoch parity
-    RS recv   x2        partial tiles from every source rank [n][T_local][N]
+    RS recv   x2        partial tiles from every source rank [n][T_local][N] (fused push
+                        reduce-scatter), or this rank's whole GEMM partial [n*T_local][N]
+                        that the peers read (pull reduce-scatter); both kinds share one
+                        epoch counter, so a slot is reused only two reduce-scatters later
 
 Only this rank's own buffer is ever viewed as a torch tensor; peer pointers
 are handed to the fused kernels only.
@@ -111,6 +115,29 @@ class TPCommunicator:
                       self.ctrs, self.rank, self.ag_epoch, trace=self.trace)
         return y, full
 
+    def gemm_reduce_scatter_pull(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False, bias=None):
+        """GEMM into this rank's symmetric slot, publish, then one pull kernel sums this rank's rows of
+        every rank's partial (peer loads, fixed rank order)."""
+        from ..ops.linear import gemm
+
+        T, K = x.shape
+        N = weight.shape[1] if b_mn else weight.shape[0]
+        T_local = T // self.n
+        if T % self.n or T_local > self.max_local_rows or N > self.max_rs_n or N % 8:
+            return None
+        self.rs_epoch += 1
+        parity = self.rs_epoch & 1
+        C = ext()
+        dev = x.device.index
+        part = C.symm_local_view(self.local_ptr, self.rs_off + parity * self.rs_slot_bytes, [T, N], torch.bfloat16,
+                                 dev)
+        gemm(x, weight, out=part, b_mn=b_mn)
+        C.ep_signal([p + 512 + self.rank * 8 for p in self.ptrs], self.rs_epoch, dev)
+        C.ep_wait(self.local_ptr + 512, self.n, self.rs_epoch, dev)
+        out = torch.empty(T_local, N, dtype=torch.bfloat16, device=x.device)
+        C.rs_pull(self._rs_recv_ptrs(parity), out, bias, self.rank)
+        return out
+
     def gemm_reduce_scatter(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False, bias=None):
         T, K = x.shape
         N = weight.shape[1] if b_mn else weight.shape[0]
@@ -140,11 +167,13 @@ class _FusedAdapter:
 
     Shapes the communicator cannot take fall back to NCCL + GEMM. With
     ``autotune`` (default, ``NTB_FUSED_AUTOTUNE=0`` disables it) the first
-    call of every (op, shape, layout) times the fused kernel against NCCL +
-    GEMM on the device (CUDA events, a few repetitions, max over the group so
-    every rank takes the same decision) and later calls use the faster one:
-    the point-to-point reduce-scatter epilogue, for instance, wins at two
-    ranks and loses to NCCL's reduce-scatter at eight on this hardware.
+    call of every (op, shape, layout) times the candidates on the device
+    (CUDA events, a few repetitions, max over the group so every rank takes
+    the same decision) and later calls use the fastest: for the all-gather,
+    the fused kernel vs NCCL + GEMM; for the reduce-scatter, the fused
+    push-epilogue kernel, GEMM + the pull reduce-scatter kernel, and GEMM +
+    NCCL (the push epilogue wins at two ranks, its remote stores limit it at
+    eight).
     """
 
     REPS = 3
@@ -181,28 +210,30 @@ class _FusedAdapter:
         e.synchronize()
         return s.elapsed_time(e) / self.REPS
 
-    def _decide(self, key, fused_fn, nccl_fn) -> str:
+    def _decide(self, key, candidates: dict) -> str:
+        """Name of the fastest candidate (first one when autotune is off); timed on the device, max over
+        the group, so every rank takes the same decision."""
         ch = self.choice.get(key)
         if ch is not None:
             return ch
+        names = list(candidates)
         if not self.autotune:
-            self.choice[key] = "fused"
-            return "fused"
-        t = torch.tensor([self._time(fused_fn), self._time(nccl_fn)], dtype=torch.float64,
-                         device=self.c.device)
+            self.choice[key] = names[0]
+            return names[0]
+        t = torch.tensor([self._time(candidates[k]) for k in names], dtype=torch.float64, device=self.c.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.c.group)
-        tf, tn = float(t[0]), float(t[1])
-        ch = "fused" if tf <= tn else "nccl"
+        times = [float(v) for v in t]
+        ch = names[min(range(len(names)), key=lambda i: times[i])]
         self.choice[key] = ch
-        self.timings[key] = (tf, tn)
+        self.timings[key] = dict(zip(names, (round(v, 4) for v in times)))
         return ch
 
     # ------------------------------------------------------------------ fused ops
     def all_gather_gemm(self, x_shard, weight, bias, b_mn=False):
         key = ("ag", tuple(x_shard.shape), tuple(weight.shape), b_mn, bias is not None)
         if self.c.all_gather_gemm_fits(x_shard, weight, b_mn):
-            ch = self._decide(key, lambda: self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn),
-                              lambda: self._ag_nccl(x_shard, weight, bias, b_mn))
+            ch = self._decide(key, {"fused": lambda: self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn),
+                                    "nccl": lambda: self._ag_nccl(x_shard, weight, bias, b_mn)})
             if ch == "fused":
                 return self.c.all_gather_gemm(x_shard, weight, bias, b_mn=b_mn)
         return self._ag_nccl(x_shard, weight, bias, b_mn)
@@ -210,10 +241,13 @@ class _FusedAdapter:
     def gemm_reduce_scatter(self, x, weight, b_mn=False):
         key = ("rs", tuple(x.shape), tuple(weight.shape), b_mn)
         if self.c.gemm_reduce_scatter_fits(x, weight, b_mn):
-            ch = self._decide(key, lambda: self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn),
-                              lambda: self._rs_nccl(x, weight, b_mn))
+            ch = self._decide(key, {"fused": lambda: self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn),
+                                    "pull": lambda: self.c.gemm_reduce_scatter_pull(x, weight, b_mn=b_mn),
+                                    "nccl": lambda: self._rs_nccl(x, weight, b_mn)})
             if ch == "fused":
                 return self.c.gemm_reduce_scatter(x, weight, b_mn=b_mn)
+            if ch == "pull":
+                return self.c.gemm_reduce_scatter_pull(x, weight, b_mn=b_mn)
         return self._rs_nccl(x, weight, b_mn)
 
     def all_gather(self, x_shard):

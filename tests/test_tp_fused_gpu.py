@@ -49,6 +49,7 @@ def _worker(rank, world, port, q):
             ref = torch.empty(T_local, 512, device="cuda", dtype=torch.float32)
             dist.reduce_scatter_tensor(ref, part)
             errs.append(("rs", _rel(out, ref)))
+            errs.append(("rs_pull", _rel(c.gemm_reduce_scatter_pull(xr, wr), ref)))
             wrt = torch.randn(K, 512, device="cuda", dtype=torch.bfloat16, generator=torch.Generator(device="cuda").manual_seed(17 + it))
             out2 = c.gemm_reduce_scatter(xr, wrt, b_mn=True)
             part2 = (xr.float() @ wrt.float()).contiguous()
@@ -66,11 +67,13 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+# NTB_TEST_WORLD=4 (or 8) runs the same checks on more ranks when the GPUs are there.
 def test_fused_ag_gemm_and_gemm_rs_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    world = max(2, min(int(os.environ.get("NTB_TEST_WORLD", "2")), torch.cuda.device_count()))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=240) for _ in procs]

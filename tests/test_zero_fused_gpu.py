@@ -71,11 +71,13 @@ def _worker(rank, world, port, q):
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+# NTB_TEST_WORLD=4 (or 8) runs the same checks on more ranks when the GPUs are there.
 def test_fused_zero_step_two_gpus():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    world = max(2, min(int(os.environ.get("NTB_TEST_WORLD", "2")), torch.cuda.device_count()))
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     results = [q.get(timeout=300) for _ in procs]
