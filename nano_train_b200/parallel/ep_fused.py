@@ -34,6 +34,7 @@ import torch
 import torch.distributed as dist
 
 from . import comm
+from .region import RegionLayout
 
 FLAG_DISPATCH, FLAG_Y, FLAG_DOUT, FLAG_DX = range(4)
 MAX_RANKS = 8
@@ -259,17 +260,18 @@ class EPWorkspace:
         self.P = P = max_tokens * top_k
         self.R = R = _align(n * P + experts_per_rank * SEG, SEG)
         pay_elem = 1 if fp8_payload else 2
-        off = 4096
-        self.off_meta = off; off = _align(off + n * P * 16)
-        self.off_payload = off; off = _align(off + n * P * H * pay_elem)
-        self.off_pscale = off; off = _align(off + (n * P * (H // 128) * 4 if fp8_payload else 0))
-        self.off_rowmap = off; off = _align(off + n * P * 4)
-        self.off_y = off; off = _align(off + R * H * 2)
-        self.off_yq = off; off = _align(off + (R * H if fp8_payload else 0))
-        self.off_ys = off; off = _align(off + (R * (H // 128) * 4 if fp8_payload else 0))
-        self.off_dx = off; off = _align(off + R * H * 2)
-        self.off_dout = off; off = _align(off + max_tokens * H * 2)
-        self.bytes = off
+        lay = RegionLayout(4096)
+        self.off_meta = lay.add("meta", n * P * 16)
+        self.off_payload = lay.add("payload", n * P * H * pay_elem)
+        self.off_pscale = lay.add("pscale", n * P * (H // 128) * 4 if fp8_payload else 0)
+        self.off_rowmap = lay.add("rowmap", n * P * 4)
+        self.off_y = lay.add("y", R * H * 2)
+        self.off_yq = lay.add("yq", R * H if fp8_payload else 0)
+        self.off_ys = lay.add("ys", R * (H // 128) * 4 if fp8_payload else 0)
+        self.off_dx = lay.add("dx", R * H * 2)
+        self.off_dout = lay.add("dout", max_tokens * H * 2)
+        self.layout = lay
+        self.bytes = lay.total
         C = ext()
         self._C = C
         self.local, handle = C.symm_alloc(self.bytes)
@@ -285,6 +287,7 @@ class EPWorkspace:
                 self._opened.append(p)
         self.done = torch.zeros(1, dtype=torch.int32, device=self.device)
         self.ctr = torch.zeros(MAX_RANKS, dtype=torch.int32, device=self.device)
+        lay.fill(C, self.local, self.device.index)
         self.epoch = [0, 0, 0, 0]
         self.closed = False
         dist.barrier(group=group)
@@ -410,6 +413,10 @@ class EPWorkspace:
                         self.P, self.R, False)
         return dx
 
+    def check_canaries(self) -> list[str]:
+        """Sections of this rank's region whose trailing canary was overwritten (synchronises)."""
+        return self.layout.check(self._C, self.local, self.device.index)
+
     def close(self):
         if self.closed:
             return
@@ -421,6 +428,10 @@ class EPWorkspace:
 
 
 _WORKSPACES: dict = {}
+
+
+def workspaces() -> list:
+    return list(_WORKSPACES.values())
 
 
 def get_workspace(group, *, tokens: int, hidden: int, top_k: int, experts_per_rank: int, fp8: bool) -> EPWorkspace:

@@ -14,6 +14,8 @@ memory directly over NVLink:
                         reduce-scatter), or this rank's whole GEMM partial [n*T_local][N]
                         that the peers read (pull reduce-scatter); both kinds share one
                         epoch counter, so a slot is reused only two reduce-scatters later
+Every section after the control words is followed by a 256-byte canary
+(``check_canaries``, parallel/region.py).
 
 Only this rank's own buffer is ever viewed as a torch tensor; peer pointers
 are handed to the fused kernels only.
@@ -28,6 +30,7 @@ import torch.distributed as dist
 from ..ops._ext import ext
 from . import comm
 from .fused import register_communicator
+from .region import RegionLayout
 
 _CTRL = 4096
 
@@ -47,10 +50,12 @@ class TPCommunicator:
         self.rs_slot_bytes = self.n * max_local_rows * max_rs_n * 2
         n_tiles = (max_local_rows // 128) * ((max_rs_n + 127) // 128)
         self.tctr_bytes = (n_tiles * 4 + 4095) // 4096 * 4096
-        self.tctr_off = _CTRL
-        self.ag_off = self.tctr_off + 2 * self.tctr_bytes
-        self.rs_off = self.ag_off + 2 * self.ag_slot_bytes
-        total = self.rs_off + 2 * self.rs_slot_bytes
+        lay = RegionLayout(_CTRL)
+        self.tctr_offs = [lay.add(f"rs_tile_counters{i}", self.tctr_bytes) for i in range(2)]
+        self.ag_offs = [lay.add(f"ag_slot{i}", self.ag_slot_bytes) for i in range(2)]
+        self.rs_offs = [lay.add(f"rs_slot{i}", self.rs_slot_bytes) for i in range(2)]
+        self.layout = lay
+        total = lay.total
         C = ext()
         self.local_ptr, handle = C.symm_alloc(total)
         handles = [None] * self.n
@@ -69,6 +74,7 @@ class TPCommunicator:
         self.ag_epoch = 0
         self.rs_epoch = 0
         self.closed = False
+        lay.fill(C, self.local_ptr, self.device.index)
         # Optional int64 [num_sms, 8] tensor: per-CTA %globaltimer stamps of the last fused call.
         self.trace = None
         dist.barrier(group=group)
@@ -78,13 +84,17 @@ class TPCommunicator:
         return [p + 0 for p in self.ptrs]
 
     def _ag_slot_ptrs(self, parity: int):
-        return [p + self.ag_off + parity * self.ag_slot_bytes for p in self.ptrs]
+        return [p + self.ag_offs[parity] for p in self.ptrs]
 
     def _rs_recv_ptrs(self, parity: int):
-        return [p + self.rs_off + parity * self.rs_slot_bytes for p in self.ptrs]
+        return [p + self.rs_offs[parity] for p in self.ptrs]
 
     def _rs_tctr_ptrs(self, parity: int):
-        return [p + self.tctr_off + parity * self.tctr_bytes for p in self.ptrs]
+        return [p + self.tctr_offs[parity] for p in self.ptrs]
+
+    def check_canaries(self) -> list[str]:
+        """Sections of this rank's region whose trailing canary was overwritten (synchronises)."""
+        return self.layout.check(ext(), self.local_ptr, self.device.index)
 
     def supports(self, x: torch.Tensor, w: torch.Tensor) -> bool:
         return (not self.closed and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
@@ -129,8 +139,7 @@ class TPCommunicator:
         parity = self.rs_epoch & 1
         C = ext()
         dev = x.device.index
-        part = C.symm_local_view(self.local_ptr, self.rs_off + parity * self.rs_slot_bytes, [T, N], torch.bfloat16,
-                                 dev)
+        part = C.symm_local_view(self.local_ptr, self.rs_offs[parity], [T, N], torch.bfloat16, dev)
         gemm(x, weight, out=part, b_mn=b_mn)
         C.ep_signal([p + 512 + self.rank * 8 for p in self.ptrs], self.rs_epoch, dev)
         C.ep_wait(self.local_ptr + 512, self.n, self.rs_epoch, dev)

@@ -15,7 +15,8 @@ step over all buffers.
 Layout of the region:
     [0, 256)        flags u64 [3 kinds][8 source ranks]: gradients ready, partial norm, parameters written
     [256, 320)      partial sums of squares fp32 [8 source ranks][2]
-    4 KiB ...       per buffer: parameters bf16 [numel], gradients fp32 [numel] (256-byte aligned)
+    4 KiB ...       per buffer: parameters bf16 [numel], gradients fp32 [numel] (256-byte aligned,
+                    each followed by a 256-byte canary, see parallel/region.py)
 """
 from __future__ import annotations
 
@@ -26,6 +27,7 @@ import torch
 import torch.distributed as dist
 
 from . import comm
+from .region import RegionLayout
 
 GRADS, STATS, PARAMS = range(3)
 MAX_RANKS = 8
@@ -64,14 +66,13 @@ class ZeroSymm:
         self.rank = comm.group_rank(dp_group)
         self.device = device
         self.numels = list(numels)
-        off = 4096
+        lay = RegionLayout(4096)
         self.poff, self.goff = [], []
-        for k in self.numels:
-            self.poff.append(off)
-            off = _align(off + k * 2)
-            self.goff.append(off)
-            off = _align(off + k * 4)
-        self.bytes = off
+        for i, k in enumerate(self.numels):
+            self.poff.append(lay.add(f"params{i}", k * 2))
+            self.goff.append(lay.add(f"grads{i}", k * 4))
+        self.layout = lay
+        self.bytes = lay.total
         C = ext()
         self._C = C
         self.local, handle = C.symm_alloc(self.bytes)
@@ -91,6 +92,7 @@ class ZeroSymm:
         self.scale = torch.ones(1, dtype=torch.float32, device=device)
         self.epoch = 0
         self.closed = False
+        lay.fill(C, self.local, device.index)
         dist.barrier(group=dp_group)
 
     def views(self, i: int):
@@ -127,6 +129,10 @@ class ZeroSymm:
                               me, e, float(betas[0]), float(betas[1]), float(eps), int(step), float(inv_dp),
                               float(max_norm), self.grad_norm, self.scale)
         C.ep_wait(self.local + PARAMS * MAX_RANKS * 8, n, e, dev)
+
+    def check_canaries(self) -> list[str]:
+        """Sections of this rank's region whose trailing canary was overwritten (synchronises)."""
+        return self.layout.check(self._C, self.local, self.device.index)
 
     def close(self):
         if self.closed:

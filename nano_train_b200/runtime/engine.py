@@ -21,6 +21,7 @@ import torch.distributed as dist
 from ..logging import get_logger
 from .context import RuntimeContext, TrainState
 from .contracts import RuntimeComponents, StepContext
+from ..utils.nvtx import nvtx_range
 
 logger = get_logger(__name__)
 
@@ -81,8 +82,9 @@ class RuntimeEngine:
                     continue
                 if state.global_step >= args.max_steps:
                     break
-                out = schedule.run_step(StepContext(model=model, batch=batch, optimizer_state=optimizer_state,
-                                                    runtime_context=runtime_context, train_state=state))
+                with nvtx_range(f"step {state.global_step}"):
+                    out = schedule.run_step(StepContext(model=model, batch=batch, optimizer_state=optimizer_state,
+                                                        runtime_context=runtime_context, train_state=state))
                 sums[0] += out.task_loss
                 sums[1] += out.aux_loss
                 sums[2] += out.total_loss
@@ -134,8 +136,9 @@ class RuntimeEngine:
                         sampler.set_epoch(state.pipeline_epoch)
                     data_iter = iter(train_data.loader)
                     batch = next(data_iter)
-            out = schedule.run_step(StepContext(model=model, batch=batch, optimizer_state=optimizer_state,
-                                                runtime_context=runtime_context, train_state=state))
+            with nvtx_range(f"step {state.global_step}"):
+                out = schedule.run_step(StepContext(model=model, batch=batch, optimizer_state=optimizer_state,
+                                                    runtime_context=runtime_context, train_state=state))
             t, a, tot, d = self._reduce_metric_sums(task_sum=out.task_loss, aux_sum=out.aux_loss,
                                                     total_sum=out.total_loss, drop_sum=out.drop_fraction,
                                                     objective_count=out.counters.get("objective_count", 1),

@@ -16,6 +16,7 @@ from typing import Optional
 import torch
 
 from .parallel.flat_optimizer import FlatAdamW, split_decay_groups
+from .utils.nvtx import nvtx_range
 
 
 class LMTrainer:
@@ -36,16 +37,20 @@ class LMTrainer:
                                    sequence_parallel=bool(getattr(model, "sequence_parallel", False)))
 
     def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor, lr: Optional[float] = None) -> torch.Tensor:
-        ids = input_ids.to(self.device, non_blocking=True)
-        lab = labels.to(self.device, non_blocking=True)
+        with nvtx_range("h2d"):
+            ids = input_ids.to(self.device, non_blocking=True)
+            lab = labels.to(self.device, non_blocking=True)
         self.optimizer.zero_grad()
         B = ids.shape[0]
         mb = self.micro_batch_size
         n_mb = max(1, B // mb)
         total = torch.zeros((), dtype=torch.float32, device=self.device)
         for i in range(n_mb):
-            loss = self.model.forward_loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
-            (loss / n_mb).backward()
+            with nvtx_range(f"forward mb{i}"):
+                loss = self.model.forward_loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
+            with nvtx_range(f"backward mb{i}"):
+                (loss / n_mb).backward()
             total += loss.detach().float()
-        self.optimizer.step(lr=lr)
+        with nvtx_range("optimizer"):
+            self.optimizer.step(lr=lr)
         return total / n_mb

@@ -112,3 +112,19 @@ def test_desc_float_key_orders_descending():
     v = torch.tensor([0.5, -1.0, 2.0, 0.0, -0.25, 1e-30, 3.5])
     key = _desc_float_key(v.view(torch.int32))
     assert torch.equal(torch.argsort(key), torch.argsort(v, descending=True))
+
+
+def test_region_layout_sections_and_canaries_do_not_overlap():
+    from nano_train_b200.parallel.region import CANARY_BYTES, RegionLayout
+
+    lay = RegionLayout(4096)
+    sizes = {"a": 100, "b": 0, "c": 4096, "d": 7}
+    offs = {k: lay.add(k, v) for k, v in sizes.items()}
+    spans = [(o, o + sizes[k]) for k, o in offs.items()] + [(c, c + CANARY_BYTES) for _, c in lay.canaries]
+    spans.sort()
+    for (a0, a1), (b0, b1) in zip(spans, spans[1:]):
+        assert a1 <= b0
+    assert all(o % 256 == 0 for o in offs.values()) and all(c % 256 == 0 for _, c in lay.canaries)
+    for (name, c), (k, o) in zip(lay.canaries, offs.items()):
+        assert name == k and c >= o + sizes[k]
+    assert lay.total == lay.canaries[-1][1] + CANARY_BYTES

@@ -67,6 +67,11 @@ def _worker(rank, world, port, q):
                 results.append((str(gran), rep, errs))
         torch.cuda.synchronize()
         check_status(rank)
+        from nano_train_b200.parallel.ep_fused import workspaces
+
+        for ws in workspaces():
+            bad = ws.check_canaries()
+            assert not bad, f"canaries overwritten after {bad}"
         clear_workspaces()
         dist.barrier()
         dist.destroy_process_group()

@@ -58,6 +58,8 @@ def _worker(rank, world, port, q):
             errs.append(("rs_bmn", _rel(out2, ref2)))
         torch.cuda.synchronize()
         check_status(rank)
+        bad = c.check_canaries()
+        assert not bad, f"canaries overwritten after {bad}"
         c.close()
         dist.barrier()
         dist.destroy_process_group()

@@ -59,6 +59,8 @@ def _worker(rank, world, port, q):
                 dist.all_gather(allp, pa)
                 same = all(torch.equal(allp[0], t) for t in allp)
                 res.append((strategy, it, rel, gn, same))
+            bad = oa._zsym.check_canaries()
+            assert not bad, f"canaries overwritten after {bad}"
         torch.cuda.synchronize()
         check_status(rank)
         dist.barrier()
