@@ -160,3 +160,52 @@ def test_examples_via_launcher(script, args, expect):
     p = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     assert expect in p.stdout
+
+
+def test_model_report_sweeps_and_sensitivity(tmp_path):
+    from nano_train_b200.utils.model_info import (DecodeEPExplorationConfig, decode_ep_exploration, decode_sweep,
+                                                  default_roofline_targets, sensitivity_grid)
+
+    model = TransformerModel(llama3_8b_config(param_device=torch.device("meta"), sequence_parallel=False))
+    pts = sensitivity_grid(model)
+    assert len(pts) == 2 * 3 * 3 * 3 * 4 * 2  # kv dtype x top-k x kv rank x hidden x context x exec model
+    # longer contexts never make decode faster; fp8 KV never slower than bf16
+    for p in pts:
+        if p.cache_len == 2048:
+            q = next(o for o in pts if (o.exec_model, o.kv_dtype_bytes, o.top_k, o.kv_rank_scale, o.hidden_scale,
+                                        o.cache_len) == (p.exec_model, p.kv_dtype_bytes, p.top_k, p.kv_rank_scale,
+                                                         p.hidden_scale, 16384))
+            assert q.t_est_ms >= p.t_est_ms
+    rows = decode_sweep(model, targets=default_roofline_targets()[:2])
+    assert rows[0]["bound"]["B200 fp8"] == "hbm"      # batch 1 decode streams the weights
+    bc = rows[0]["b_crit"]["B200 fp8"]
+    assert bc is None or bc > 8
+    info = dump_model_info(model, str(tmp_path / "full.md"), batch=8, seq_len=4096)
+    text = (tmp_path / "full.md").read_text()
+    for sec in ("Parameters by category", "Mode estimates", "Decode batch sweep", "Prefill batch sweep",
+                "Sensitivity grid (432 points"):
+        assert sec in text, sec
+    assert {k.exec_model for k in info.kpis} == {"naive", "efficient"}
+    naive = next(k for k in info.kpis if k.mode == "prefill" and k.exec_model == "naive")
+    eff = next(k for k in info.kpis if k.mode == "prefill" and k.exec_model == "efficient"
+               and k.target == naive.target)
+    assert naive.bytes_temporary > 0 and eff.bytes_temporary == 0 and eff.bytes_hbm < naive.bytes_hbm
+    # routed-expert model: EP exploration rows and partial expert coverage at small decode batches
+    from nano_train_b200.config import _NoOpPrecisionResolver
+    from nano_train_b200.models.deepseek import DeepSeekModel, DeepSeekModelConfig
+
+    cfg = DeepSeekModelConfig(param_dtype=torch.bfloat16, param_device=torch.device("meta"),
+                              precision_resolver=_NoOpPrecisionResolver(), vocab_size=1024, hidden_size=256,
+                              num_hidden_layers=2, num_attention_heads=4, num_key_value_heads=4,
+                              n_routed_experts=16, num_experts_per_tok=2, moe_intermediate_size=128,
+                              intermediate_size=512, first_k_dense_replace=1, kv_lora_rank=64, q_lora_rank=96,
+                              qk_nope_head_dim=32, qk_rope_head_dim=16, v_head_dim=32, n_shared_experts=1,
+                              max_position_embeddings=1024)
+    ds = DeepSeekModel(cfg)
+    ex = decode_ep_exploration(ds, DecodeEPExplorationConfig(ep_sizes=[1, 2, 4], cache_lengths=[1024]))
+    assert [r["ep"] for r in ex] == [1, 2, 4]
+    e1 = estimate(ds, batch=1, decode_ctx=1024)
+    e64 = estimate(ds, batch=64, decode_ctx=1024)
+    w1 = next(k for k in e1.kpis if k.mode == "decode").bytes_weights
+    w64 = next(k for k in e64.kpis if k.mode == "decode").bytes_weights
+    assert w1 < w64  # one token touches top_k of the experts, 64 tokens nearly all of them
