@@ -28,6 +28,9 @@ logger = get_logger(__name__)
 
 class RuntimeEngine:
     def run(self, components: RuntimeComponents, args: argparse.Namespace) -> None:
+        from ..distributed.debug import enable_from_env
+
+        enable_from_env()  # NTB_CHECK_COLLECTIVES=1: every collective is order-checked across its group
         ctx = components.bootstrap.build_context(args)
         self._log_runtime_topology(ctx)
         model = components.model_provider.build_model(ctx)
