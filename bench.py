@@ -43,6 +43,16 @@ SEQ = 4096
 GLOBAL_BATCH = 8
 MICRO_BATCH = 1
 
+# Other configurations of the same metric (not the driver's default run):
+#   gpt1.3b-fp4-dp: GPT-1.3B shape (H 2048, 24 layers, 16 heads, GELU 8192, vocab 50304), NVFP4
+#   linears (e2m1 operands in 1x16 blocks with e4m3 scales on the fp4 tensor cores, bf16 params,
+#   fp32 master / moments), DP = N with ZeRO-1, seq 2048, micro-batch 8 per rank (weak scaling).
+CONFIGS = {
+    "llama8b-tp": dict(model=MODEL_NAME, seq=SEQ, batch_per_rank=None, vocab=128256),
+    "gpt1.3b-fp4-dp": dict(model="GPT-1.3B-shape dense TransformerModel (H2048, 24 layers, 16 heads, GELU 8192, "
+                                 "vocab 50304), NVFP4 linears", seq=2048, batch_per_rank=8, vocab=50304),
+}
+
 
 def parse():
     ap = argparse.ArgumentParser()
@@ -50,8 +60,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b-tp",
+                    help="benchmark configuration (default: the headline Llama-3-8B-shape TP run)")
     ap.add_argument("--layers", type=int, default=None, help="override layer count (not a valid headline run)")
-    ap.add_argument("--seq", type=int, default=SEQ)
+    ap.add_argument("--seq", type=int, default=None, help="sequence length (default: the config's)")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
 
@@ -131,21 +143,48 @@ def barrier(world):
     torch.cuda.synchronize()
 
 
-def make_batches(n, seq, vocab, seed=0):
+def make_batches(n, seq, vocab, seed=0, batch=GLOBAL_BATCH):
     g = torch.Generator().manual_seed(seed)
     out = []
     for _ in range(n):
-        ids = torch.randint(0, vocab, (GLOBAL_BATCH, seq + 1), generator=g, dtype=torch.int64)
+        ids = torch.randint(0, vocab, (batch, seq + 1), generator=g, dtype=torch.int64)
         out.append((ids[:, :-1].contiguous().pin_memory(), ids[:, 1:].contiguous().pin_memory()))
     return out
 
 
 # ---------------------------------------------------------------- our framework
+def build_gpt_fp4(args, rank, world):
+    """GPT-1.3B shape with NVFP4 linears, DP = world with ZeRO-1 (sharded fp32 master / moments)."""
+    sys.path.insert(0, ROOT)
+    from nano_train_b200.models.transformer import TransformerModel, gpt_1p3b_config
+    from nano_train_b200.precision.mixed_precision import (build_module_precision_resolver,
+                                                           finalize_module_precision_resolver,
+                                                           resolve_precision_config)
+    from nano_train_b200.training import LMTrainer
+
+    layers = args.layers or 24
+    pc = resolve_precision_config(argparse.Namespace(fp4=True, fp4_backend="native", params_dtype="bf16"),
+                                  torch.device("cuda"))
+    resolver = build_module_precision_resolver(pc)
+    torch.manual_seed(1234)  # identical initial weights on every DP rank
+    model = TransformerModel(gpt_1p3b_config(num_layers=layers, param_device=torch.device("cuda"),
+                                             precision_resolver=resolver))
+    finalize_module_precision_resolver(resolver)
+    dp = dist.group.WORLD if world > 1 else None
+    trainer = LMTrainer(model, lr=3e-4, weight_decay=0.1, max_grad_norm=1.0,
+                        micro_batch_size=CONFIGS["gpt1.3b-fp4-dp"]["batch_per_rank"], dp_group=dp,
+                        strategy="optim" if world > 1 else "no_shard")
+    return trainer, layers
+
+
 def build_ours(args, rank, world):
     sys.path.insert(0, ROOT)
     from nano_train_b200.config import TPConfig
     from nano_train_b200.models.transformer import TransformerModel, llama3_8b_config
     from nano_train_b200.training import LMTrainer
+
+    if args.config == "gpt1.3b-fp4-dp":
+        return build_gpt_fp4(args, rank, world)
 
     layers = args.layers or (8 if world == 1 else 32)
     tp = world
@@ -166,7 +205,11 @@ def run_ours(args, rank, local, world):
     from nano_train_b200.ops._ext import check_status, ext
 
     trainer, layers = build_ours(args, rank, world)
-    batches = make_batches(4, args.seq, 128256)
+    cfg = CONFIGS[args.config]
+    if cfg["batch_per_rank"]:
+        batches = make_batches(4, args.seq, cfg["vocab"], seed=rank, batch=cfg["batch_per_rank"])
+    else:
+        batches = make_batches(4, args.seq, cfg["vocab"])
     dev_batches = [(a.cuda(), b.cuda()) for a, b in batches]
     for i in range(args.warmup):
         trainer.train_step(*dev_batches[i % len(dev_batches)])
@@ -209,11 +252,18 @@ def run_ours(args, rank, local, world):
             float(loss)  # device -> host read of the step's result
         barrier(world)
         e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps, world)
-        tok = GLOBAL_BATCH * args.seq
+        rows = batches[0][0].shape[0]
+        tok = tokens_per_step(args, world)
         e2e = {"value": tok / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
-               "h2d_bytes_per_step": 2 * GLOBAL_BATCH * args.seq * 8, "d2h_bytes_per_step": 4,
+               "h2d_bytes_per_step": 2 * rows * args.seq * 8, "d2h_bytes_per_step": 4,
                "api": "nano_train_b200.training.LMTrainer.train_step"}
     return ms, layers, launches, sampler.summary(), e2e, fused_paths
+
+
+def tokens_per_step(args, world):
+    """Whole-job tokens per step: TP ranks share one batch; DP ranks each run their own."""
+    per_rank = CONFIGS[args.config]["batch_per_rank"]
+    return (per_rank * world if per_rank else GLOBAL_BATCH) * args.seq
 
 
 # ---------------------------------------------------------------- reference arm
@@ -226,9 +276,17 @@ def run_reference(args, rank, local, world):
 
 def main():
     args = parse()
+    if args.seq is None:
+        args.seq = CONFIGS[args.config]["seq"]
     n = args.gpus
     rank, local, world = init_dist(n)
     try:
+        if args.impl == "reference" and args.config != "llama8b-tp":
+            if rank == 0:
+                print(json.dumps({"impl": "reference", "config": args.config,
+                                  "unavailable": "the reference arm is wired for the default llama8b-tp config only"}),
+                      flush=True)
+            return
         if args.impl == "reference":
             sys.path.insert(0, ROOT)
             res = run_reference(args, rank, local, world)
@@ -238,8 +296,10 @@ def main():
             fused_paths = None
         else:
             ms, layers, launches, clocks, e2e, fused_paths = run_ours(args, rank, local, world)
-        tokens = GLOBAL_BATCH * args.seq
+        tokens = tokens_per_step(args, world)
         value = tokens / (ms / 1e3)
+        cfg = CONFIGS[args.config]
+        dp_run = bool(cfg["batch_per_rank"])
         if rank == 0:
             line = {
                 "metric": METRIC,
@@ -250,17 +310,19 @@ def main():
                 "warmup": args.warmup,
                 "ms_per_step": ms,
                 "higher_is_better": True,
-                "scaling": "strong",
+                "scaling": "weak" if dp_run else "strong",
                 "vs_baseline": None,
-                "dtype": "bf16",
+                "dtype": "nvfp4 GEMM operands, bf16 activations" if dp_run else "bf16",
                 "data": "synthetic (uniform token ids, seeded); random-init N(0,0.02) weights",
                 "config": {
-                    "model": MODEL_NAME,
+                    "name": args.config,
+                    "model": cfg["model"],
                     "layers": layers,
-                    "global_batch": GLOBAL_BATCH,
-                    "micro_batch": MICRO_BATCH,
+                    "global_batch": cfg["batch_per_rank"] * world if dp_run else GLOBAL_BATCH,
+                    "micro_batch": cfg["batch_per_rank"] if dp_run else MICRO_BATCH,
                     "seq_len": args.seq,
-                    "parallelism": f"tp{world}" + ("+sp" if world > 1 else ""),
+                    "parallelism": (f"dp{world}" + ("+zero1" if world > 1 else "")) if dp_run else
+                                   (f"tp{world}" + ("+sp" if world > 1 else "")),
                     "optimizer": "AdamW fp32 master/moments, bf16 params, fp32 main grads, clip 1.0",
                     "l2": "working set >> 126 MB L2 (no explicit flush)",
                 },

@@ -13,6 +13,7 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   attn_fwd_tc   tcgen05 flash attention fwd, same shape
   attn_bwd_tc   tcgen05 flash attention bwd (the default backward for head dim 128), same shape
   fp8_gemm      block-scaled e4m3 GEMM 8192 x 2048 x 7168 (DeepSeek-V3 recipe scales)
+  fp4_gemm      NVFP4 GEMM 16384 x 8192 x 2048 (GPT-1.3B MLP fc1 shape, e2m1 with e4m3 1x16 scales)
   grouped_fwd   grouped expert GEMM, 64 experts, 49152 routed rows x 2816 x 2048 (DeepSeek-V2-Lite gate|up)
   rmsnorm_bwd   RMSNorm backward 8192 x 4096 bf16
   adamw         fused flat AdamW over 64M fp32 elements
@@ -65,6 +66,13 @@ def main():
         wq, sw = C.fp8_quantize(w, 128, False, 0)
         y = torch.empty(8192, 2048, **bf)
         fn = lambda: C.gemm_fp8_blockscaled(xq, sx, wq, sw, y)  # noqa: E731
+    elif a.case == "fp4_gemm":
+        from nano_train_b200.ops import fp4
+
+        a4 = fp4.quantize(torch.randn(16384, 2048, **bf))
+        b4 = fp4.quantize(torch.randn(8192, 2048, **bf))
+        y = torch.empty(16384, 8192, **bf)
+        fn = lambda: fp4.gemm(a4, b4, out=y)  # noqa: E731
     elif a.case == "grouped_fwd":
         from nano_train_b200.ops.grouped import pad_segments
 

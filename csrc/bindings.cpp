@@ -67,6 +67,13 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor&
 // gemm_fp8.cu
 void gemm_fp8_blockscaled(const at::Tensor& a_q, const at::Tensor& sa, const at::Tensor& b_q, const at::Tensor& sb,
                           at::Tensor& out, const c10::optional<at::Tensor>& bias);
+// dropout.cu
+at::Tensor dropout_apply(const at::Tensor& x, double p, int64_t seed);
+// gemm_fp4.cu
+std::vector<at::Tensor> nvfp4_quantize(const at::Tensor& x);
+at::Tensor nvfp4_dequantize(const at::Tensor& q, const at::Tensor& sf, const at::Tensor& gs, at::ScalarType dtype);
+void gemm_nvfp4(const at::Tensor& a_q, const at::Tensor& sfa, const at::Tensor& gsa, const at::Tensor& b_q,
+                const at::Tensor& sfb, const at::Tensor& gsb, at::Tensor& out, const c10::optional<at::Tensor>& bias);
 // quant.cu
 std::vector<at::Tensor> fp8_quantize(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
 at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
@@ -161,6 +168,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fp8_blockscaled", &ntb::gemm_fp8_blockscaled, py::arg("a_q"), py::arg("sa"), py::arg("b_q"),
         py::arg("sb"), py::arg("out"), py::arg("bias") = py::none());
   m.def("fp8_quantize", &ntb::fp8_quantize);
+  m.def("nvfp4_quantize", &ntb::nvfp4_quantize);
+  m.def("dropout_apply", &ntb::dropout_apply);
+  m.def("nvfp4_dequantize", &ntb::nvfp4_dequantize);
+  m.def("gemm_nvfp4", &ntb::gemm_nvfp4, py::arg("a_q"), py::arg("sfa"), py::arg("gsa"), py::arg("b_q"),
+        py::arg("sfb"), py::arg("gsb"), py::arg("out"), py::arg("bias") = py::none());
   m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
   m.def("fp8_dequantize", &ntb::fp8_dequantize);
   m.def("ag_gemm", &ntb::ag_gemm, py::arg("x_local"), py::arg("x_full_out"), py::arg("w"), py::arg("y"),

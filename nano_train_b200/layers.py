@@ -294,7 +294,9 @@ class VocabParallelEmbedding(ModulePrecisionStateMixin, nn.Module):
 
 
 class Dropout(nn.Module):
-    """Inverted dropout; identity when p == 0 or in eval mode."""
+    """Inverted dropout; identity when p == 0 or in eval mode. On CUDA the mask comes from a
+    counter-based generator inside one kernel and is regenerated in the backward pass
+    (``ops/dropout.py``); on CPU it is a bernoulli draw."""
 
     def __init__(self, p: float = 0.5):
         super().__init__()
@@ -307,6 +309,10 @@ class Dropout(nn.Module):
             return x
         if self.p == 1.0:
             return torch.zeros_like(x)
+        if x.is_cuda:
+            from .ops.dropout import dropout
+
+            return dropout(x, self.p)
         mask = torch.empty_like(x).bernoulli_(1.0 - self.p)
         return x * mask / (1.0 - self.p)
 

@@ -300,3 +300,19 @@ def llama3_8b_config(*, num_layers: int = 32, param_dtype=torch.bfloat16, param_
                tie_word_embeddings=False, sequence_parallel=sequence_parallel, init_std=0.02)
     cfg.update(overrides)
     return ModelConfig(**cfg)
+
+
+def gpt_1p3b_config(*, num_layers: int = 24, param_dtype=torch.bfloat16, param_device=None, precision_resolver=None,
+                    **overrides) -> ModelConfig:
+    """GPT-1.3B shape: H 2048, 24 layers, 16 heads, GELU FFN 8192, vocab 50304, LayerNorm, learned
+    positions (2048), tied embeddings. ``precision_resolver`` selects the low-bit compute of the
+    linears (e.g. the NVFP4 backend under ``--fp4 --fp4-backend native``)."""
+    from ..config import _default_precision_resolver
+
+    cfg = dict(param_dtype=param_dtype, param_device=param_device,
+               precision_resolver=precision_resolver or _default_precision_resolver(), hidden_size=2048,
+               num_layers=num_layers, num_attention_heads=16, intermediate_size=8192, max_position_embeddings=2048,
+               vocab_size=50304, dropout=0.0, norm="layernorm", norm_eps=1e-5, position="learned", mlp="gelu",
+               bias=True, tie_word_embeddings=True, sequence_parallel=False, init_std=0.02)
+    cfg.update(overrides)
+    return ModelConfig(**cfg)

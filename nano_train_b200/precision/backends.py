@@ -10,8 +10,9 @@
   activation tile and per 128x128 weight block (the DeepSeek-V3 recipe) and
   stochastic or nearest rounding, run through the sm_100a quantiser kernels;
   the product of the dequantised operands is computed on the tcgen05 GEMM.
-* ``NativeFP4Backend`` - NVFP4 numerics: e2m1 values in 1x16 blocks with an
-  e4m3 scale per block and an fp32 per-tensor scale.
+* ``NativeFP4Backend`` - NVFP4: e2m1 values in 1x16 blocks with an e4m3
+  scale per block and an fp32 per-tensor scale; the forward GEMM runs on the
+  e2m1 block-scaled tensor cores (``ops/fp4.py``, ``csrc/gemm_fp4.cu``).
 * ``TransformerEngineBackend`` - wraps ``transformer_engine`` when it is
   installed (it is not on this image; selecting it raises at resolution time,
   like the reference).
@@ -331,7 +332,63 @@ def nvfp4_quant_dequant(x: torch.Tensor, block: int = 16) -> torch.Tensor:
     return dq.reshape(shape).to(x.dtype)
 
 
+_W4_CACHE: dict = {}
+
+
+def _nvfp4_weight(w: torch.Tensor):
+    """NVFP4 copy of a weight, re-quantised only when the weight changed."""
+    from ..ops import fp4
+
+    key = id(w)
+    ent = _W4_CACHE.get(key)
+    if ent is not None and ent[0] == (w.data_ptr(), w._version):
+        return ent[1]
+    packed = fp4.quantize(w.detach().to(torch.bfloat16))
+    _W4_CACHE[key] = ((w.data_ptr(), w._version), packed)
+    return packed
+
+
+class _FP4LinearFn(torch.autograd.Function):
+    """Forward on the e2m1 block-scaled tensor cores (``gemm_nvfp4``); straight-through
+    backward on the dequantised operands (bf16 GEMMs), saving the 4.5-bit copies instead of
+    bf16 activations."""
+
+    @staticmethod
+    def forward(ctx, x2, weight, bias):
+        from ..ops import fp4
+
+        xq = fp4.quantize(x2.contiguous())
+        wq = _nvfp4_weight(weight)
+        y = fp4.gemm(xq, wq, bias=None if bias is None else bias.to(torch.bfloat16))
+        ctx.save_for_backward(*xq, *wq)
+        ctx.weight = weight
+        ctx.has_bias = bias is not None
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..ops import fp4
+        from ..ops.linear import accumulate_weight_grad, gemm
+
+        xq, sx, gx, wq, sw, gw = ctx.saved_tensors
+        dy = dy.contiguous()
+        wdq = fp4.dequantize(wq, sw, gw, torch.bfloat16)
+        dx = gemm(dy, wdq, b_mn=True)
+        xdq = fp4.dequantize(xq, sx, gx, torch.bfloat16)
+        dw = accumulate_weight_grad(ctx.weight, dy, xdq)
+        db = dy.float().sum(0).to(torch.bfloat16) if ctx.has_bias else None
+        return dx, dw, db
+
+
 class NativeFP4Backend:
+    """NVFP4: e2m1 values in 1x16 blocks, e4m3 block scales, fp32 per-tensor scale.
+
+    On CUDA with bf16 activations and GEMM-compatible shapes (K % 256 == 0, N % 8 == 0)
+    the forward GEMM runs on the e2m1 tensor cores (``tcgen05.mma kind::mxf4nvf4``, the
+    block scales applied by the hardware); other shapes and CPU tensors use the same
+    quantisation through quantise-dequantise + bf16/fp32 GEMM.
+    """
+
     name = "native"
 
     def __init__(self, *, mode: str = "fp4", kernel_spec=None) -> None:
@@ -340,8 +397,21 @@ class NativeFP4Backend:
         self.mode = mode
 
     def linear(self, input_tensor, weight, bias, module=None):
-        xdq = nvfp4_quant_dequant(input_tensor.detach())
-        wdq = nvfp4_quant_dequant(weight.detach())
+        from ..ops import fp4
+
+        K = input_tensor.shape[-1]
+        if (input_tensor.is_cuda and input_tensor.dtype == torch.bfloat16 and weight.dim() == 2
+                and fp4.gemm_supported(K, weight.shape[0])):
+            lead = input_tensor.shape[:-1]
+            x2 = input_tensor.reshape(-1, K)
+            y = _FP4LinearFn.apply(x2, weight, bias)
+            return y.view(*lead, weight.shape[0])
+        if K % 64 == 0:
+            xdq = fp4.quant_dequant_reference(input_tensor.detach())
+            wdq = fp4.quant_dequant_reference(weight.detach())
+        else:
+            xdq = nvfp4_quant_dequant(input_tensor.detach())
+            wdq = nvfp4_quant_dequant(weight.detach())
         xq = input_tensor + (xdq - input_tensor).detach()
         wq = weight + (wdq.to(weight.dtype) - weight).detach()
         if input_tensor.is_cuda and input_tensor.dtype == torch.bfloat16:

@@ -364,7 +364,7 @@ def resolve_precision_config(args, device: torch.device) -> PrecisionConfig:
     if mode == "fp8" and hist < 1:
         raise ValueError("--fp8-amax-history-len must be >= 1")
     if mode == "fp4" and fp4_backend not in ("emulated", "native"):
-        raise ValueError("--fp4-backend currently supports only emulated")
+        raise ValueError("--fp4-backend must be emulated or native")
     if ownership not in ("module", "optimizer"):
         raise ValueError("--lowbit-master-ownership must be module or optimizer")
     dts = {
