@@ -67,6 +67,10 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor&
 // gemm_fp8.cu
 void gemm_fp8_blockscaled(const at::Tensor& a_q, const at::Tensor& sa, const at::Tensor& b_q, const at::Tensor& sb,
                           at::Tensor& out, const c10::optional<at::Tensor>& bias);
+// persistent.cu
+std::vector<at::Tensor> persistent_quantize(const at::Tensor& w, bool nf4, bool per_tensor);
+at::Tensor persistent_dequantize(const at::Tensor& codes, const at::Tensor& scale, int64_t rows, int64_t cols,
+                                 bool nf4, at::ScalarType dtype);
 // dropout.cu
 at::Tensor dropout_apply(const at::Tensor& x, double p, int64_t seed);
 // gemm_fp4.cu
@@ -170,6 +174,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fp8_quantize", &ntb::fp8_quantize);
   m.def("nvfp4_quantize", &ntb::nvfp4_quantize);
   m.def("dropout_apply", &ntb::dropout_apply);
+  m.def("persistent_quantize", &ntb::persistent_quantize);
+  m.def("persistent_dequantize", &ntb::persistent_dequantize);
   m.def("nvfp4_dequantize", &ntb::nvfp4_dequantize);
   m.def("gemm_nvfp4", &ntb::gemm_nvfp4, py::arg("a_q"), py::arg("sfa"), py::arg("gsa"), py::arg("b_q"),
         py::arg("sfb"), py::arg("gsb"), py::arg("out"), py::arg("bias") = py::none());

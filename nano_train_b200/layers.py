@@ -204,9 +204,9 @@ class LayerNorm(ModulePrecisionStateMixin, nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = self._module_compute_dtype_override()
-        if dt is not None and dt != x.dtype:
+        if dt is not None:  # the override is the compute and the output dtype
             return ops.layer_norm(x.to(dt), self.weight.to(dt), None if self.bias is None else self.bias.to(dt),
-                                  self.eps).to(x.dtype)
+                                  self.eps)
         return ops.layer_norm(x, self.weight, self.bias, self.eps)
 
 
@@ -226,8 +226,8 @@ class RMSNorm(ModulePrecisionStateMixin, nn.Module):
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         dt = self.compute_dtype or self._module_compute_dtype_override()
-        if dt is not None and dt != x.dtype:
-            return ops.rms_norm(x.to(dt), self.weight.to(dt), self.eps).to(x.dtype)
+        if dt is not None:  # the override is the compute and the output dtype
+            return ops.rms_norm(x.to(dt), self.weight.to(dt), self.eps)
         return ops.rms_norm(x, self.weight.to(x.dtype), self.eps)
 
     def forward_residual(self, x: torch.Tensor, residual: torch.Tensor):

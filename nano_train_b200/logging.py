@@ -25,21 +25,36 @@ class ColoredFormatter(logging.Formatter):
         return text
 
 
-def setup_logging(level: str = "INFO", log_file: Optional[str] = None, use_colors: bool = True,
-                  name: str = _ROOT) -> logging.Logger:
-    logger = logging.getLogger(name)
-    logger.setLevel(getattr(logging, level.upper(), logging.INFO))
-    logger.handlers.clear()
+def setup_logging(log_level: str = "INFO", log_file: Optional[str] = None, use_colors: bool = True,
+                  log_format: Optional[str] = None, *, level: Optional[str] = None) -> logging.Logger:
+    """Configure the root logger: colour console handler (when the console is a terminal) and an
+    optional plain-text file handler (appending). ``level`` is accepted as an alias of
+    ``log_level``. Unknown level names raise ``ValueError``."""
+    name = (level or log_level).upper()
+    if not isinstance(getattr(logging, name, None), int):
+        raise ValueError(f"Unsupported log level: {level or log_level}. "
+                         "Expected one of DEBUG, INFO, WARNING, ERROR, CRITICAL.")
+    lvl = int(getattr(logging, name))
+    fmt = log_format or "%(asctime)s | %(levelname)-8s | %(name)s: %(message)s"
+    datefmt = None if log_format else "%Y-%m-%d %H:%M:%S"
+    root = logging.getLogger()
+    root.setLevel(lvl)
+    root.handlers.clear()
     h = logging.StreamHandler(sys.stdout)
-    h.setFormatter(ColoredFormatter(use_colors=use_colors and sys.stdout.isatty()))
-    logger.addHandler(h)
+    h.setLevel(lvl)
+    h.setFormatter(ColoredFormatter(fmt, datefmt=datefmt, use_colors=use_colors and sys.stdout.isatty()))
+    root.addHandler(h)
     if log_file:
         os.makedirs(os.path.dirname(os.path.abspath(log_file)), exist_ok=True)
-        fh = logging.FileHandler(log_file)
-        fh.setFormatter(ColoredFormatter(use_colors=False))
-        logger.addHandler(fh)
-    logger.propagate = False
-    return logger
+        fh = logging.FileHandler(log_file, mode="a")
+        fh.setLevel(lvl)
+        fh.setFormatter(logging.Formatter(fmt, datefmt=datefmt))
+        root.addHandler(fh)
+    pkg = logging.getLogger(_ROOT)  # the package logger propagates to the configured root
+    pkg.handlers.clear()
+    pkg.setLevel(logging.NOTSET)
+    pkg.propagate = True
+    return root
 
 
 def get_logger(name: str) -> logging.Logger:

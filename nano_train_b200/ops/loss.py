@@ -74,8 +74,11 @@ def cross_entropy(logits: torch.Tensor, labels: torch.Tensor, ignore_index: int 
         return _CEFn.apply(logits, labels, ignore_index, reduction, vocab_start, group, inplace_grad)
     if group is not None and dist.get_world_size(group) > 1:
         return _vocab_parallel_ce_reference(logits, labels, ignore_index, reduction, vocab_start, group)
-    return F.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), labels.reshape(-1),
-                           ignore_index=ignore_index, reduction=reduction)
+    lg, lab = logits.reshape(-1, logits.shape[-1]).float(), labels.reshape(-1)
+    if reduction == "mean":  # 0 (not NaN) when every target is ignored
+        total = F.cross_entropy(lg, lab, ignore_index=ignore_index, reduction="sum")
+        return total / (lab != ignore_index).sum().clamp_min(1).to(total.dtype)
+    return F.cross_entropy(lg, lab, ignore_index=ignore_index, reduction=reduction)
 
 
 class _VPCERef(torch.autograd.Function):

@@ -422,37 +422,76 @@ class NativeFP4Backend:
 
 # ------------------------------------------------------------------ Transformer Engine (optional)
 class TransformerEngineBackend:
+    """Routes fp8 linears through Transformer Engine's ``te.Linear`` (optional dependency, not
+    installed on this image). One TE module per layer, built from the layer's kernel spec and
+    bound to the layer's own trainable parameters (``bind_parameters``, called at layer init);
+    tensors that are not the bound parameters (e.g. straight-through weights) take ``F.linear``.
+    Reference parity: src/runtime/te_backend.py:263-385."""
+
     name = "transformer_engine"
 
     def __init__(self, *, mode: str, fp8_format: str, amax_history_len: int, amax_compute_algo: str,
                  kernel_spec=None) -> None:
+        if mode != "fp8":
+            raise ValueError("TransformerEngineBackend only supports fp8 mode")
+        if kernel_spec is None:
+            raise RuntimeError("Transformer Engine backend requires a per-module LowBitKernelSpec")
         try:
             import transformer_engine.pytorch as te  # type: ignore
-            from transformer_engine.common import recipe as te_recipe  # type: ignore
         except Exception as exc:  # pragma: no cover - TE absent on this image
-            raise RuntimeError("fp8 backend 'transformer_engine' requires transformer_engine to be installed") from exc
+            raise RuntimeError("Transformer Engine backend requested but transformer_engine is unavailable") from exc
         self.mode = mode
         self._te = te
-        fmt = te_recipe.Format.E4M3 if fp8_format == "e4m3" else te_recipe.Format.HYBRID
-        self._recipe = te_recipe.DelayedScaling(fp8_format=fmt, amax_history_len=amax_history_len,
-                                                amax_compute_algo=amax_compute_algo)
-        self._modules: dict[int, object] = {}
+        self._fp8_format = fp8_format
+        self._amax_history_len = int(amax_history_len)
+        self._amax_compute_algo = str(amax_compute_algo)
+        self._kernel_spec = kernel_spec
+        self._te_linear = te.Linear(in_features=int(kernel_spec.in_features),
+                                    out_features=int(kernel_spec.out_features), bias=bool(kernel_spec.has_bias))
+        self._bound_weight = None
+        self._bound_bias = None
+
+    def bind_parameters(self, weight: torch.nn.Parameter, bias: Optional[torch.nn.Parameter]) -> None:
+        spec = self._kernel_spec
+        if not isinstance(weight, torch.nn.Parameter):
+            raise TypeError("TransformerEngineBackend expects nn.Parameter weight binding")
+        if tuple(weight.shape) != (int(spec.out_features), int(spec.in_features)):
+            raise ValueError(f"TE backend weight shape mismatch: expected={(spec.out_features, spec.in_features)} "
+                             f"got={tuple(weight.shape)}")
+        if spec.has_bias:
+            if not isinstance(bias, torch.nn.Parameter) or tuple(bias.shape) != (int(spec.out_features),):
+                raise ValueError("TE backend expected a bias parameter of shape (out_features,)")
+            self._te_linear.bias = bias
+            self._bound_bias = bias
+        else:
+            self._bound_bias = None
+        self._te_linear.weight = weight
+        self._bound_weight = weight
+
+    def _autocast(self):
+        ac = getattr(self._te, "autocast", None) or getattr(self._te, "fp8_autocast", None)
+        if ac is None:
+            return nullcontext()
+        try:  # the recipe object exists only in full TE installs
+            from transformer_engine.common import recipe as te_recipe  # type: ignore
+
+            fmt = te_recipe.Format.E4M3 if self._fp8_format == "e4m3" else te_recipe.Format.HYBRID
+            rec = te_recipe.DelayedScaling(fp8_format=fmt, amax_history_len=self._amax_history_len,
+                                           amax_compute_algo=self._amax_compute_algo)
+        except Exception:
+            return ac(enabled=True)
+        return ac(enabled=True, fp8_recipe=rec)
 
     def linear(self, input_tensor, weight, bias, module=None):
-        if not isinstance(weight, torch.nn.Parameter):
+        if self._bound_weight is None:
+            raise RuntimeError("Transformer Engine backend used before parameter binding. "
+                               "Layer init must bind module-owned trainable parameters.")
+        te_linear = self._te_linear.to(device=input_tensor.device)
+        with self._autocast():
+            if weight is self._bound_weight and (bias is self._bound_bias or
+                                                 (bias is None and self._bound_bias is None)):
+                return te_linear(input_tensor)
             return F.linear(input_tensor, weight, bias)
-        key = id(weight)
-        te_linear = self._modules.get(key)
-        if te_linear is None:
-            te_linear = self._te.Linear(weight.shape[1], weight.shape[0], bias=bias is not None,
-                                        params_dtype=weight.dtype, device=weight.device)
-            te_linear.weight = weight
-            if bias is not None:
-                te_linear.bias = bias
-            self._modules[key] = te_linear
-        ctx = self._te.fp8_autocast(enabled=True, fp8_recipe=self._recipe) if input_tensor.is_cuda else nullcontext()
-        with ctx:
-            return te_linear(input_tensor)
 
 
 def build_lowbit_backend_for_mode(config, *, mode: str, kernel_spec=None):

@@ -32,7 +32,7 @@ class ModulePrecisionStateMixin:
                                                              lowbit_capable_type=lowbit_capable_type,
                                                              kernel_spec=kernel_spec)
         self._module_path = module_path
-        self._precision_init_state = state
+        self._module_precision_state = state
         self._precision_assignment = getattr(state, "assignment", None)
         self._lowbit_backend = getattr(state, "lowbit_backend", None)
 
@@ -67,6 +67,9 @@ class LowBitLinearMixin(ModulePrecisionStateMixin):
         from .persistent import init_persistent_buffers
 
         init_persistent_buffers(self)
+        bind = getattr(self._lowbit_backend, "bind_parameters", None)
+        if callable(bind):  # backends that own a kernel module use the layer's trainable parameters
+            bind(self.weight, self.bias)
 
     @property
     def master_ownership_mode(self) -> str:
@@ -109,12 +112,14 @@ class LowBitLinearMixin(ModulePrecisionStateMixin):
 
     def _linear(self, x: torch.Tensor, bias: Optional[torch.Tensor]) -> torch.Tensor:
         w = self._effective_weight()
-        if self._lowbit_active():
-            return self._lowbit_backend.linear(x, w, bias, module=self)
+        if self._compute_lowbit_mode() is not None:
+            if self._lowbit_backend is None:
+                raise RuntimeError(f"Module {type(self).__name__} ({self._module_path}) requested compute mode "
+                                   f"{self._compute_lowbit_mode()} without a bound low-bit backend")
+            return self._lowbit_backend.linear(x, w, bias)
         dt = self._module_compute_dtype_override()
-        if dt is not None and dt != x.dtype:
-            y = ops.linear(x.to(dt), w.to(dt), None if bias is None else bias.to(dt))
-            return y.to(x.dtype)
+        if dt is not None:  # the override is the compute and the output dtype
+            return ops.linear(x.to(dt), w.to(dt), None if bias is None else bias.to(dt))
         if w.dtype != x.dtype:
             w = w.to(x.dtype)
             bias = None if bias is None else bias.to(x.dtype)

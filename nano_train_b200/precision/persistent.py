@@ -2,6 +2,11 @@
 scales, or NF4 codes packed two per byte) kept as module buffers and used
 through a straight-through estimator in the forward pass.
 
+On CUDA the refresh (scales + codes, once per optimizer step) and the
+dequantisation of the straight-through forward run in the kernels of
+``csrc/persistent.cu`` (same fp32 arithmetic, same bits); the PyTorch
+statements below are the CPU path and the tests' oracle.
+
 Reference parity: src/layers.py:60-184 (NF4 codebook, pack/unpack,
 quantizers) and 216-436 (buffers, refresh, STE forward).
 """
@@ -34,7 +39,16 @@ def _amax(w: torch.Tensor, granularity: str) -> torch.Tensor:
     return wf.abs().amax(dim=1)
 
 
+def _native(w: torch.Tensor) -> bool:
+    return w.is_cuda and w.dim() == 2 and w.dtype in (torch.bfloat16, torch.float32)
+
+
 def quantize_fp8_persistent(w: torch.Tensor, granularity: str):
+    if _native(w):
+        from ..ops._ext import ext
+
+        q, scale = ext().persistent_quantize(w.detach().contiguous(), False, granularity == "per_tensor")
+        return q.view(torch.float8_e4m3fn), scale
     scale = _safe_scale(_amax(w, granularity), FP8_E4M3_MAX)
     s = scale if granularity == "per_tensor" else scale[:, None]
     q = (w.detach().float() / s).clamp(-FP8_E4M3_MAX, FP8_E4M3_MAX).to(torch.float8_e4m3fn)
@@ -42,6 +56,10 @@ def quantize_fp8_persistent(w: torch.Tensor, granularity: str):
 
 
 def dequantize_fp8_persistent(q: torch.Tensor, scale: torch.Tensor, granularity: str, dtype) -> torch.Tensor:
+    if q.is_cuda and q.dim() == 2 and dtype in (torch.bfloat16, torch.float32):
+        from ..ops._ext import ext
+
+        return ext().persistent_dequantize(q.view(torch.uint8), scale, q.shape[0], q.shape[1], False, dtype)
     s = scale if granularity == "per_tensor" else scale[:, None]
     return (q.float() * s).to(dtype)
 
@@ -61,6 +79,11 @@ def unpack_nibbles(packed: torch.Tensor, numel: int) -> torch.Tensor:
 
 
 def quantize_nf4_persistent(w: torch.Tensor, granularity: str):
+    if _native(w):
+        from ..ops._ext import ext
+
+        codes, scale = ext().persistent_quantize(w.detach().contiguous(), True, granularity == "per_tensor")
+        return codes, scale
     scale = _safe_scale(_amax(w, granularity), 1.0)
     s = scale if granularity == "per_tensor" else scale[:, None]
     normed = (w.detach().float() / s).reshape(-1, 1)
@@ -70,6 +93,10 @@ def quantize_nf4_persistent(w: torch.Tensor, granularity: str):
 
 
 def dequantize_nf4_persistent(codes: torch.Tensor, scale: torch.Tensor, shape, granularity: str, dtype):
+    if codes.is_cuda and len(shape) == 2 and dtype in (torch.bfloat16, torch.float32):
+        from ..ops._ext import ext
+
+        return ext().persistent_dequantize(codes, scale, shape[0], shape[1], True, dtype)
     numel = 1
     for d in shape:
         numel *= d
