@@ -286,17 +286,25 @@ class LocalRoutedMoE(nn.Module):
 
 
 # ------------------------------------------------------------------ expert parallel
-def _comm_quant_dequant(x: torch.Tensor, granularity: str, rounding: str, backend: str) -> torch.Tensor:
-    """Payload quantisation for the dispatch/combine exchange (straight-through)."""
+def _comm_quant_dequant(x: torch.Tensor, granularity: Optional[str] = None, rounding_mode: str = "nearest",
+                        backend: str = "emulated", *, bits: int = 8) -> torch.Tensor:
+    """Payload quantisation for the dispatch/combine exchange (straight-through; shape and dtype kept).
+
+    A payload row is one token, so the 128x128 block of the recipe is applied as 1x128 tiles: each
+    row keeps its own scales and can be quantised where it is sent (the fused dispatch does exactly
+    this in flight)."""
     if granularity in (None, "none") or x.numel() == 0:
         return x
-    if backend == "native":
-        gran = {"block_128x128": "tile_1x128"}.get(granularity, granularity)
-        dq = fp8_quant_dequant(x.detach(), granularity=gran, rounding_mode=rounding, channel_axis=-1)
+    gran = {"block_128x128": "tile_1x128"}.get(granularity, granularity)
+    if backend == "native" and bits == 8:
+        dq = fp8_quant_dequant(x.detach(), granularity=gran, rounding_mode=rounding_mode, channel_axis=-1)
     else:
-        dq = quantize_dequantize(x.detach(), bits=8, granularity={"block_128x128": "tile_1x128"}.get(
-            granularity, granularity), rounding_mode=rounding, channel_axis=-1)
+        dq = quantize_dequantize(x.detach(), bits=bits, granularity=gran, rounding_mode=rounding_mode,
+                                 channel_axis=-1)
     return x + (dq.to(x.dtype) - x).detach()
+
+
+_UNSET = object()
 
 
 class _AllToAll(torch.autograd.Function):
@@ -322,7 +330,7 @@ class ExpertParallelMoE(nn.Module):
                  param_device=None, precision_resolver=None, module_prefix: str = "moe", dropout: float = 0.0,
                  n_shared_experts: int = 0, scoring_func: str = "sigmoid", n_group: int = 1, topk_group: int = 1,
                  norm_topk_prob: bool = True, routed_scaling_factor: float = 1.0, capacity_factor: float = 1.0,
-                 comm_quant_granularity: Optional[str] = None, comm_quant_rounding: str = "nearest",
+                 comm_quant_granularity=_UNSET, comm_quant_rounding: Optional[str] = None,
                  comm_quant_backend: str = "emulated"):
         super().__init__()
         if expert_tp_size != 1:
@@ -332,7 +340,17 @@ class ExpertParallelMoE(nn.Module):
         self.hidden_size, self.num_experts, self.top_k = hidden_size, num_experts, top_k
         self.ep_rank, self.ep_size, self.ep_group = ep_rank, ep_size, ep_group
         self.experts_per_rank = num_experts // ep_size
+        self.global_expert_start = ep_rank * self.experts_per_rank
         self.capacity_factor = capacity_factor
+        # Payload quantisation: explicit arguments win; otherwise the DeepSeek-V3 recipe of the
+        # precision resolver decides (on, block_128x128, its rounding mode), as in the reference.
+        recipe_fn = getattr(precision_resolver, "deepseek_v3_recipe", None)
+        recipe = recipe_fn() if callable(recipe_fn) else None
+        if comm_quant_granularity is _UNSET:
+            comm_quant_granularity = (str(recipe.comm_quant_granularity)
+                                      if recipe is not None and recipe.comm_quant_enabled else None)
+        if comm_quant_rounding is None:
+            comm_quant_rounding = str(recipe.rounding_mode) if recipe is not None else "nearest"
         self.comm_quant_granularity = comm_quant_granularity
         self.comm_quant_rounding = comm_quant_rounding
         self.comm_quant_backend = comm_quant_backend
@@ -357,6 +375,10 @@ class ExpertParallelMoE(nn.Module):
 
     last_aux_loss = property(lambda self: self._last_aux_loss)
     last_token_counts = property(lambda self: self._last_token_counts)
+    last_local_expert_counts = property(lambda self: self._last_token_counts)
+    _comm_quant_enabled = property(lambda self: self.comm_quant_granularity not in (None, "none"))
+    _comm_quant_granularity = property(lambda self: self.comm_quant_granularity or "tensor")
+    _comm_quant_rounding_mode = property(lambda self: self.comm_quant_rounding)
 
     @property
     def last_dropped_fraction(self) -> float:

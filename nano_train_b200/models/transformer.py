@@ -17,6 +17,7 @@ full-precision logits.
 """
 from __future__ import annotations
 
+import math
 from typing import Optional
 
 import torch
@@ -41,11 +42,26 @@ def _norm(config: ModelConfig, path: str):
 
 
 class MultiHeadAttention(nn.Module):
-    """Fused-QKV causal self-attention (MHA or GQA), column/row tensor-parallel."""
+    """Fused-QKV self-attention (MHA or GQA), column/row tensor-parallel.
 
-    def __init__(self, config: ModelConfig, tp_config: TPConfig, module_prefix: str):
+    Two entry points:
+
+    * ``forward(x, attention_mask=None)`` — the reference's module API (src/models/attention.py:
+      134-220): x [B, S, H]; an additive mask [B, 1, S, S] or none (no mask means no masking);
+    * ``forward_tokens(x2d, batch, seq)`` — the training path: token-major [B*S(/tp), H], implicit
+      causal mask, RoPE and flash attention on the fused projection output.
+
+    Masks, attention-probability dropout in training and monitoring (``set_monitoring``: max logit,
+    entropy, normalised entropy, fraction of logits above tau) need the probabilities, so they run
+    the materialised path: scores in the input dtype, fp32 softmax, probabilities cast to V's dtype
+    (the reference's numerics).
+    """
+
+    def __init__(self, config: ModelConfig, tp_config: Optional[TPConfig] = None, module_prefix: str = "attention"):
         super().__init__()
+        tp_config = tp_config or TPConfig()
         H = config.hidden_size
+        self.hidden_size = H
         self.num_heads = config.num_attention_heads
         self.num_kv_heads = config.num_key_value_heads or self.num_heads
         if H % self.num_heads != 0:
@@ -54,9 +70,12 @@ class MultiHeadAttention(nn.Module):
         tp = tp_config.size if tp_config.enabled else 1
         if self.num_heads % tp or self.num_kv_heads % tp:
             raise ValueError("attention heads must be divisible by tp_size")
+        self.tp_enabled = tp_config.enabled
         self.tp_size = tp
         self.nq = self.num_heads // tp
         self.nkv = self.num_kv_heads // tp
+        self.tp_num_heads = self.nq
+        self.scale = self.head_dim ** -0.5
         self.rope = config.position == "rope"
         self.rope_theta = config.rope_theta
         D = self.head_dim
@@ -70,24 +89,81 @@ class MultiHeadAttention(nn.Module):
             self.out_proj = RowParallelLinear(H, H, tp_config.rank, tp, bias=config.bias, tp_group=tp_config.group,
                                               module_path=f"{module_prefix}.out_proj",
                                               sequence_parallel=config.sequence_parallel, **common)
-            self._regroup_qkv_shards(tp_config.rank, tp)
         else:
             self.qkv_proj = Linear(H, qkv_out, bias=config.bias, module_path=f"{module_prefix}.qkv_proj", **common)
             self.out_proj = Linear(H, H, bias=config.bias, module_path=f"{module_prefix}.out_proj", **common)
         self.dropout = Dropout(config.dropout)
+        self._monitor_enabled = False
+        self._monitor_tau = 100.0
+        self._monitor_stats: Optional[dict] = None
 
-    def _regroup_qkv_shards(self, rank: int, tp: int) -> None:
-        """Column shards are laid out [q_local | k_local | v_local] per rank (heads stay whole)."""
-        # Weights are random-initialised per shard already; only the layout contract matters.
-        return None
+    def set_monitoring(self, enabled: bool, *, tau: float = 100.0) -> None:
+        """Enable/disable the attention vitals (host reads; opt-in) and set tau."""
+        self._monitor_enabled = bool(enabled)
+        self._monitor_tau = float(tau)
+        if not self._monitor_enabled:
+            self._monitor_stats = None
 
-    def forward(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
+    def _needs_probs(self, attention_mask) -> bool:
+        return attention_mask is not None or self._monitor_enabled or (self.training and self.dropout.p > 0)
+
+    def _materialized(self, qkv: torch.Tensor, batch: int, seq: int, attention_mask, causal: bool) -> torch.Tensor:
+        from ..ops.rope import apply_rope
+
+        nq, nkv, D = self.nq, self.nkv, self.head_dim
+        q = qkv[:, : nq * D].view(batch, seq, nq, D)
+        k = qkv[:, nq * D: (nq + nkv) * D].view(batch, seq, nkv, D)
+        v = qkv[:, (nq + nkv) * D:].view(batch, seq, nkv, D)
+        if self.rope:
+            q, k = apply_rope(q, self.rope_theta, "half"), apply_rope(k, self.rope_theta, "half")
+        q, k, v = (t.permute(0, 2, 1, 3) for t in (q, k, v))
+        if nkv != nq:
+            k = k.repeat_interleave(nq // nkv, dim=1)
+            v = v.repeat_interleave(nq // nkv, dim=1)
+        scores = torch.matmul(q, k.transpose(-2, -1)) * self.scale
+        if attention_mask is not None:
+            scores = scores + attention_mask
+        elif causal:
+            scores = scores.masked_fill(torch.ones(seq, seq, dtype=torch.bool, device=scores.device).triu(1),
+                                        float("-inf"))
+        sm = scores if scores.dtype in (torch.float32, torch.float64) else scores.float()
+        probs = torch.softmax(sm, dim=-1).to(v.dtype)
+        if self._monitor_enabled:
+            with torch.no_grad():
+                pf = probs.float().clamp_min(1e-12)
+                ent = float((-(pf * pf.log()).sum(-1)).mean().item())
+                self._monitor_stats = {
+                    "max_attn_logit": float(scores.max().item()),
+                    "attn_entropy": ent,
+                    "attn_entropy_norm": float(ent / math.log(seq)) if seq > 1 else 0.0,
+                    "frac_logits_gt_tau": float((scores > self._monitor_tau).float().mean().item()),
+                }
+        probs = self.dropout(probs)
+        o = torch.matmul(probs, v).permute(0, 2, 1, 3)
+        return o.reshape(batch * seq, nq * D)
+
+    def forward_tokens(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
         qkv = self.qkv_proj(x)  # [T, (nq + 2 nkv) D] (full T under sequence parallelism)
         D = self.head_dim
-        o = qkv_attention(qkv, batch, seq, self.nq, self.nkv, D, D, rope_dim=D if self.rope else 0,
-                          rope_theta=self.rope_theta, rope_mode="half")
-        o = self.dropout(o)
+        if self._needs_probs(None):
+            o = self._materialized(qkv, batch, seq, None, causal=True)
+        else:
+            o = qkv_attention(qkv, batch, seq, self.nq, self.nkv, D, D, rope_dim=D if self.rope else 0,
+                              rope_theta=self.rope_theta, rope_mode="half")
         return self.out_proj(o)
+
+    def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x.dim() != 3:
+            raise ValueError("x must have shape [batch_size, seq_len, hidden_size]")
+        B, S, _ = x.shape
+        qkv = self.qkv_proj(x.reshape(B * S, -1))
+        D = self.head_dim
+        if self._needs_probs(attention_mask):
+            o = self._materialized(qkv, B, S, attention_mask, causal=False)
+        else:
+            o = qkv_attention(qkv, B, S, self.nq, self.nkv, D, D, rope_dim=D if self.rope else 0,
+                              rope_theta=self.rope_theta, rope_mode="half", causal=False)
+        return self.out_proj(o).view(B, S, -1)
 
 
 class MLP(nn.Module):
@@ -121,28 +197,35 @@ class MLP(nn.Module):
 
 
 class TransformerBlock(nn.Module):
-    """Pre-norm block: x + attn(norm1(x)), then x + mlp(norm2(x))."""
+    """Pre-norm block: x + attention(attn_norm(x)), then x + mlp(mlp_norm(x)) (the reference's
+    submodule names, so state dicts carry over). RMSNorm models fuse the residual add into the
+    second norm."""
 
-    def __init__(self, config: ModelConfig, layer_idx: int = 0, tp_config: Optional[TPConfig] = None,
+    def __init__(self, config: ModelConfig, layer_idx: int = 0, tp_config: Optional[TPConfig] = None, *,
                  module_prefix: str = "blocks.0"):
         super().__init__()
         tp_config = tp_config or TPConfig()
         self.layer_idx = layer_idx
-        self.ln1 = _norm(config, f"{module_prefix}.ln1")
-        self.attn = MultiHeadAttention(config, tp_config, f"{module_prefix}.attn")
-        self.ln2 = _norm(config, f"{module_prefix}.ln2")
+        self.attention = MultiHeadAttention(config, tp_config, f"{module_prefix}.attention")
+        self.attn_norm = _norm(config, f"{module_prefix}.attn_norm")
         self.mlp = MLP(config, tp_config, f"{module_prefix}.mlp")
-        self.dropout = Dropout(config.dropout)
-        self._fused_residual = isinstance(self.ln2, RMSNorm)
+        self.mlp_norm = _norm(config, f"{module_prefix}.mlp_norm")
+        self._fused_residual = isinstance(self.mlp_norm, RMSNorm)
 
-    def forward(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
-        a = self.dropout(self.attn(self.ln1(x), batch, seq))
+    def forward_tokens(self, x: torch.Tensor, batch: int, seq: int) -> torch.Tensor:
+        a = self.attention.forward_tokens(self.attn_norm(x), batch, seq)
         if self._fused_residual:
-            h, x = self.ln2.forward_residual(a, x)
+            h, x = self.mlp_norm.forward_residual(a, x)
         else:
             x = x + a
-            h = self.ln2(x)
+            h = self.mlp_norm(x)
         return x + self.mlp(h)
+
+    def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
+        if x.dim() != 3:
+            raise ValueError("x must have shape [batch_size, seq_len, hidden_size]")
+        x = x + self.attention(self.attn_norm(x), attention_mask)
+        return x + self.mlp(self.mlp_norm(x))
 
 
 class TransformerModel(nn.Module):
@@ -216,16 +299,31 @@ class TransformerModel(nn.Module):
             raise ValueError("batch*seq must be divisible by tp_size under sequence parallelism")
         x = self._embed(input_ids)
         for block in self.blocks:
-            x = block(x, B, S)
+            x = block.forward_tokens(x, B, S)
         return self.ln_f(x)
 
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
-        if attention_mask is not None:
-            raise NotImplementedError("only the implicit causal mask is supported")
+        """Logits [B, S, V(/tp)]. Without a mask the blocks run the fused causal path; an explicit
+        additive mask [B, 1, S, S] (as the reference builds with ``_create_causal_mask``) runs the
+        materialised attention with that mask."""
+        if input_ids.dim() != 2:
+            raise ValueError("input_ids must have shape [batch_size, seq_len]")
         B, S = input_ids.shape
-        h = self.hidden_states(input_ids)
-        logits = self.lm_head(h)  # [T, V(/tp)]
-        return logits.view(B, S, -1)
+        if attention_mask is None:
+            h = self.hidden_states(input_ids)
+            return self.lm_head(h).view(B, S, -1)  # [T, V(/tp)] -> [B, S, V(/tp)]
+        if self.sequence_parallel:
+            raise ValueError("explicit attention masks are not supported under sequence parallelism")
+        x = self._embed(input_ids).view(B, S, -1)
+        for block in self.blocks:
+            x = block(x, attention_mask)
+        return self.lm_head(self.ln_f(x))
+
+    @staticmethod
+    def _create_causal_mask(batch_size: int, seq_len: int, device) -> torch.Tensor:
+        """Additive causal mask [B, 1, S, S] (0 on and below the diagonal, -inf above)."""
+        m = torch.full((seq_len, seq_len), float("-inf"), device=device).triu(1)
+        return m.view(1, 1, seq_len, seq_len).expand(batch_size, -1, -1, -1)
 
     def forward_loss(self, input_ids: torch.Tensor, labels: torch.Tensor, ignore_index: int = -100) -> torch.Tensor:
         """Mean next-token cross-entropy; ``labels`` are already aligned to positions.
@@ -255,8 +353,8 @@ class TransformerModel(nn.Module):
         r, tp = self.tp_rank, self.tp_size
         out = {}
         for name, t in full.items():
-            if name.endswith("attn.qkv_proj.weight") or name.endswith("attn.qkv_proj.bias"):
-                attn = self.blocks[0].attn
+            if name.endswith("attention.qkv_proj.weight") or name.endswith("attention.qkv_proj.bias"):
+                attn = self.blocks[0].attention
                 D = attn.head_dim
                 nq, nkv = attn.num_heads * D, attn.num_kv_heads * D
                 q, k, v = t[:nq], t[nq:nq + nkv], t[nq + nkv:]
@@ -266,7 +364,7 @@ class TransformerModel(nn.Module):
                 out[name] = torch.cat([g.chunk(tp)[r], u.chunk(tp)[r]], 0).contiguous()
             elif name.endswith("mlp.fc1.weight") or name.endswith("mlp.fc1.bias"):
                 out[name] = t.chunk(tp, 0)[r].contiguous()
-            elif name.endswith(("attn.out_proj.weight", "mlp.fc2.weight")):
+            elif name.endswith(("attention.out_proj.weight", "mlp.fc2.weight")):
                 out[name] = t.chunk(tp, 1)[r].contiguous()
             elif name in ("lm_head.weight",) or (name == "token_embeddings.weight"
                                                  and not isinstance(self.token_embeddings, Embedding)):

@@ -34,7 +34,7 @@ def resolve_sentinel_blocks(num_layers: int, requested: Optional[Iterable[int]] 
 def block_main_weight_names(block_idx: int) -> list[str]:
     """The four main matrices of a TransformerModel block (this framework's parameter names)."""
     b = int(block_idx)
-    return [f"blocks.{b}.attn.qkv_proj.weight", f"blocks.{b}.attn.out_proj.weight",
+    return [f"blocks.{b}.attention.qkv_proj.weight", f"blocks.{b}.attention.out_proj.weight",
             f"blocks.{b}.mlp.fc1.weight", f"blocks.{b}.mlp.fc2.weight"]
 
 

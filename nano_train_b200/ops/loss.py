@@ -75,10 +75,13 @@ def cross_entropy(logits: torch.Tensor, labels: torch.Tensor, ignore_index: int 
     if group is not None and dist.get_world_size(group) > 1:
         return _vocab_parallel_ce_reference(logits, labels, ignore_index, reduction, vocab_start, group)
     lg, lab = logits.reshape(-1, logits.shape[-1]).float(), labels.reshape(-1)
-    if reduction == "mean":  # 0 (not NaN) when every target is ignored
-        total = F.cross_entropy(lg, lab, ignore_index=ignore_index, reduction="sum")
-        return total / (lab != ignore_index).sum().clamp_min(1).to(total.dtype)
-    return F.cross_entropy(lg, lab, ignore_index=ignore_index, reduction=reduction)
+    rows = F.cross_entropy(lg, lab, ignore_index=ignore_index, reduction="none")  # 0 on ignored rows
+    if reduction == "none":
+        return rows
+    total = rows.sum()  # "sum" and "mean" reduce the same per-row values in the same order
+    if reduction == "sum":
+        return total
+    return total / (lab != ignore_index).sum().clamp_min(1).to(total.dtype)  # 0, not NaN, if all ignored
 
 
 class _VPCERef(torch.autograd.Function):

@@ -71,6 +71,21 @@ class LowBitLinearMixin(ModulePrecisionStateMixin):
         if callable(bind):  # backends that own a kernel module use the layer's trainable parameters
             bind(self.weight, self.bias)
 
+    _PERSISTENT_SUFFIXES = ("_persistent_fp8_weight", "_persistent_fp4_codes", "_persistent_scale",
+                            "_persistent_numel")
+
+    def _load_from_state_dict(self, state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                              error_msgs):
+        """Checkpoints written without the persistent low-bit buffers still load strictly; the
+        buffers are then rebuilt from the loaded weight."""
+        super()._load_from_state_dict(state_dict, prefix, local_metadata, strict, missing_keys, unexpected_keys,
+                                      error_msgs)
+        optional = {prefix + k for k in self._PERSISTENT_SUFFIXES}
+        absent = [k for k in missing_keys if k in optional]
+        missing_keys[:] = [k for k in missing_keys if k not in optional]
+        if absent and self._persistent_mode() != "off":
+            self.refresh_persistent_lowbit_params()
+
     @property
     def master_ownership_mode(self) -> str:
         a = self._precision_assignment
