@@ -13,7 +13,7 @@ from pathlib import Path
 from typing import Optional, TypedDict
 
 import torch
-from torch.utils.data import DataLoader, Dataset, Sampler
+from torch.utils.data import DataLoader, Dataset, RandomSampler, Sampler
 
 from .logging import get_logger
 
@@ -85,3 +85,32 @@ def create_dataloader(dataset: Dataset, batch_size: int, shuffle: bool = True,
         raise ValueError("batch_size must be positive")
     return DataLoader(dataset, batch_size=batch_size, shuffle=bool(shuffle) and sampler is None, sampler=sampler,
                       num_workers=0, drop_last=False, pin_memory=pin_memory)
+
+
+class EpochSeedRandomSampler(RandomSampler):
+    """A shuffling sampler whose order is exactly that of ``RandomSampler`` without a generator:
+    each epoch's seed is drawn from the global torch RNG when iteration starts (so a run follows
+    the same batch order as the reference's ``DataLoader(shuffle=True)``). The drawn seed is kept
+    in ``epoch_seed``; ``force_next_seed`` makes the next epoch reuse a recorded seed without
+    drawing, which is how a resumed run continues the interrupted epoch in the same order."""
+
+    def __init__(self, data_source) -> None:
+        super().__init__(data_source)
+        self.epoch_seed: Optional[int] = None
+        self._forced: Optional[int] = None
+
+    def force_next_seed(self, seed: Optional[int]) -> None:
+        self._forced = None if seed is None else int(seed)
+
+    def __iter__(self):
+        if self._forced is not None:
+            seed, self._forced = self._forced, None
+        else:
+            seed = int(torch.empty((), dtype=torch.int64).random_().item())
+        self.epoch_seed = seed
+        self.generator = torch.Generator().manual_seed(seed)
+        try:
+            yield from super().__iter__()
+        finally:
+            self.generator = None
+

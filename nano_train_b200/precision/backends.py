@@ -290,7 +290,9 @@ class NativeFP8Backend:
             x2 = input_tensor.reshape(-1, input_tensor.shape[-1])
             self._seed = getattr(self, "_seed", 0) + 1
             y = _FP8LinearFn.apply(x2, weight, bias, self._rounding_mode == "stochastic", self._seed)
-            return y.view(*lead, weight.shape[0])
+            # a 2-D input gets the Function's own output (not a view of it), so consumers that
+            # modify it in place under autograd (the fused QKV attention) can
+            return y if len(lead) == 1 else y.view(*lead, weight.shape[0])
         xdq = fp8_quant_dequant(input_tensor.detach(), granularity=self._activation_granularity,
                                 rounding_mode=self._rounding_mode, channel_axis=-1)
         wdq = fp8_quant_dequant(weight.detach(), granularity=self._weight_granularity,
@@ -405,7 +407,9 @@ class NativeFP4Backend:
             lead = input_tensor.shape[:-1]
             x2 = input_tensor.reshape(-1, K)
             y = _FP4LinearFn.apply(x2, weight, bias)
-            return y.view(*lead, weight.shape[0])
+            # a 2-D input gets the Function's own output (not a view of it), so consumers that
+            # modify it in place under autograd (the fused QKV attention) can
+            return y if len(lead) == 1 else y.view(*lead, weight.shape[0])
         if K % 64 == 0:
             xdq = fp4.quant_dequant_reference(input_tensor.detach())
             wdq = fp4.quant_dequant_reference(weight.detach())

@@ -106,33 +106,42 @@ def dequantize_nf4_persistent(codes: torch.Tensor, scale: torch.Tensor, shape, g
     return (vals * s).to(dtype)
 
 
+def _empty_buffers(module) -> None:
+    dev = module.weight.device
+    module._persistent_fp8_weight = torch.empty(0, device=dev)
+    module._persistent_fp4_codes = torch.empty(0, dtype=torch.uint8, device=dev)
+    module._persistent_scale = torch.empty(0, device=dev)
+    module._persistent_numel = torch.zeros((), dtype=torch.int64, device=dev)
+
+
 def init_persistent_buffers(module) -> None:
-    module.register_buffer("_persistent_fp8_weight", None, persistent=True)
-    module.register_buffer("_persistent_fp4_codes", None, persistent=True)
-    module.register_buffer("_persistent_scale", None, persistent=True)
-    module.register_buffer("_persistent_numel", None, persistent=True)
-    if module._persistent_mode() != "off" and module.weight.device.type != "meta":
+    """Register the four buffers (empty when the mode is off, as in the reference, so state dicts
+    always carry the same keys) and fill them for an active persistent mode."""
+    dev = module.weight.device
+    module.register_buffer("_persistent_fp8_weight", torch.empty(0, device=dev), persistent=True)
+    module.register_buffer("_persistent_fp4_codes", torch.empty(0, dtype=torch.uint8, device=dev), persistent=True)
+    module.register_buffer("_persistent_scale", torch.empty(0, device=dev), persistent=True)
+    module.register_buffer("_persistent_numel", torch.zeros((), dtype=torch.int64, device=dev), persistent=True)
+    if module._persistent_mode() != "off" and dev.type != "meta":
         refresh_persistent(module)
 
 
 def refresh_persistent(module) -> None:
     mode = module._persistent_mode()
     if mode == "off" or module.weight.device.type == "meta":
-        module._persistent_fp8_weight = None
-        module._persistent_fp4_codes = None
-        module._persistent_scale = None
-        module._persistent_numel = None
+        _empty_buffers(module)
         return
     gran = module._persistent_granularity()
+    dev = module.weight.device
     with torch.no_grad():
         if mode == "fp8":
             q, s = quantize_fp8_persistent(module.weight, gran)
             module._persistent_fp8_weight = q
-            module._persistent_fp4_codes = None
+            module._persistent_fp4_codes = torch.empty(0, dtype=torch.uint8, device=dev)
         elif mode == "fp4":
             codes, s = quantize_nf4_persistent(module.weight, gran)
             module._persistent_fp4_codes = codes
-            module._persistent_fp8_weight = None
+            module._persistent_fp8_weight = torch.empty(0, device=dev)
         else:
             raise ValueError(f"unknown persistent low-bit mode {mode}")
         module._persistent_scale = s
@@ -144,9 +153,9 @@ def persistent_weight_ste(module) -> torch.Tensor:
     w = module.weight
     mode = module._persistent_mode()
     gran = module._persistent_granularity()
-    if mode == "fp8" and module._persistent_fp8_weight is not None:
+    if mode == "fp8" and module._persistent_fp8_weight.numel() > 0:
         dq = dequantize_fp8_persistent(module._persistent_fp8_weight, module._persistent_scale, gran, w.dtype)
-    elif mode == "fp4" and module._persistent_fp4_codes is not None:
+    elif mode == "fp4" and module._persistent_fp4_codes.numel() > 0:
         dq = dequantize_nf4_persistent(module._persistent_fp4_codes, module._persistent_scale, tuple(w.shape), gran,
                                        w.dtype)
     else:

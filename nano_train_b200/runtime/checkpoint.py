@@ -122,7 +122,7 @@ class DirectoryCheckpointManager:
         _set_rng_state(meta["rng"])
         ts = meta["train_state"]
         return ResumeState(start_global_step=int(meta["next_step"]), start_epoch=int(ts["epoch"]),
-                           pipeline_epoch=int(ts["pipeline_epoch"]))
+                           pipeline_epoch=int(ts["pipeline_epoch"]), data_seed=ts.get("data_seed"))
 
     def on_step_end(self, *, model, optimizer_state, state: TrainState, ctx) -> None:
         if self.save_every > 0 and (state.global_step + 1) % self.save_every == 0:

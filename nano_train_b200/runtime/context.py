@@ -34,3 +34,4 @@ class TrainState:
     global_step: int = 0
     epoch: int = 0
     pipeline_epoch: int = 0
+    data_seed: Optional[int] = None  # shuffle seed of the current epoch (EpochSeedRandomSampler)

@@ -215,6 +215,7 @@ class ResumeState:
     start_global_step: int = 0
     start_epoch: int = 0
     pipeline_epoch: int = 0
+    data_seed: Optional[int] = None
 
 
 class ModelProvider(Protocol):

@@ -40,7 +40,7 @@ class RuntimeEngine:
         resume = components.checkpoint_manager.load(model=model, optimizer_state=optimizer_state, ctx=ctx)
         model.train()
         state = TrainState(global_step=resume.start_global_step, epoch=resume.start_epoch,
-                           pipeline_epoch=resume.pipeline_epoch)
+                           pipeline_epoch=resume.pipeline_epoch, data_seed=getattr(resume, "data_seed", None))
         try:
             if ctx.parallel.pipeline_model_parallel_size == 1:
                 self._run_non_pipeline_mode(args=args, model=model, train_data=train_data,
@@ -72,6 +72,8 @@ class RuntimeEngine:
         # On resume, batches of the interrupted epoch that were already trained on are skipped
         # (the sampler order is a function of the epoch, so the stream continues exactly).
         skip = max(0, state.global_step - state.epoch * len(train_data.loader)) if state.global_step else 0
+        if skip > 0 and hasattr(sampler, "force_next_seed"):
+            sampler.force_next_seed(state.data_seed)  # continue the interrupted epoch in its own order
         for epoch in range(state.epoch, args.epochs):
             state.epoch = epoch
             if sampler is not None and hasattr(sampler, "set_epoch"):
@@ -80,6 +82,7 @@ class RuntimeEngine:
             objective_count = 0
             drop_count = 0
             for batch in train_data.loader:
+                state.data_seed = getattr(sampler, "epoch_seed", None)
                 if skip > 0:
                     skip -= 1
                     continue
@@ -120,10 +123,13 @@ class RuntimeEngine:
         first = bool(getattr(model, "is_first_pp_stage", False))
         if sampler is not None and first and hasattr(sampler, "set_epoch"):
             sampler.set_epoch(state.pipeline_epoch)
+        consumed = max(0, state.global_step - state.pipeline_epoch * len(train_data.loader)) if first else 0
+        if consumed > 0 and hasattr(sampler, "force_next_seed"):
+            sampler.force_next_seed(state.data_seed)  # continue the interrupted epoch in its own order
         data_iter = iter(train_data.loader) if first else None
         if first and state.global_step:
             # Resume: skip what this pipeline epoch already consumed.
-            for _ in range(max(0, state.global_step - state.pipeline_epoch * len(train_data.loader))):
+            for _ in range(consumed):
                 next(data_iter, None)
         for step in range(state.global_step, args.max_steps):
             state.global_step = step
@@ -139,6 +145,7 @@ class RuntimeEngine:
                         sampler.set_epoch(state.pipeline_epoch)
                     data_iter = iter(train_data.loader)
                     batch = next(data_iter)
+                state.data_seed = getattr(sampler, "epoch_seed", None)
             with nvtx_range(f"step {state.global_step}"):
                 out = schedule.run_step(StepContext(model=model, batch=batch, optimizer_state=optimizer_state,
                                                     runtime_context=runtime_context, train_state=state))

@@ -142,12 +142,16 @@ def build_tiny_deepseek_config(args, *, param_dtype, param_device, precision_res
 
 
 def create_data_loader(dataset: Dataset, batch_size: int, dp_size: int, dp_rank: int, seed: int) -> TrainDataBundle:
-    sampler: Optional[DistributedSampler] = None
+    """DP > 1: DistributedSampler(shuffle, seed). DP = 1: the reference's shuffle order (an epoch seed
+    drawn from the global RNG, as DataLoader(shuffle=True) does), recorded for exact resume."""
+    from ..dataset import EpochSeedRandomSampler
+
     if dp_size > 1:
         sampler = DistributedSampler(dataset, num_replicas=dp_size, rank=dp_rank, shuffle=True, seed=seed)
-    g = torch.Generator().manual_seed(seed)
-    loader = DataLoader(dataset, batch_size=batch_size, shuffle=sampler is None, sampler=sampler, generator=g,
-                        num_workers=0, drop_last=False)
+    else:
+        sampler = EpochSeedRandomSampler(dataset)
+    loader = DataLoader(dataset, batch_size=batch_size, shuffle=False, sampler=sampler, num_workers=0,
+                        drop_last=False)
     return TrainDataBundle(loader=loader, sampler=sampler)
 
 
