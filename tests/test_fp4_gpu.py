@@ -13,10 +13,11 @@ def _rel(a, b):
     return ((a.float() - b.float()).norm() / b.float().norm()).item()
 
 
-# Bound for the e2m1 GEMM against the fp32 product of the dequantised operands. It covers the
-# bf16 rounding of the output (~1.7e-3 on these operands) and the block-scaled MMA's own
-# accumulation, which is not an exact fp32 sum: 5.2e-3 was measured on K = 512 randn operands.
-GEMM_TOL = 1e-2
+# Bound for the e2m1 GEMM against the fp32 product of its dequantised operands: the measured error
+# is the bf16 rounding of the output alone (1.66e-3 for K from 256 to 16384). Quantisation oracles
+# run on the CPU: the kernels divide exactly, while PyTorch on CUDA turns a division by a Python
+# scalar into a multiplication by its reciprocal, which moves some e4m3 / e2m1 roundings.
+GEMM_TOL = 5e-3
 
 
 @pytest.mark.parametrize("R,K,dtype", [(300, 512, torch.bfloat16), (128, 64, torch.float32), (1000, 2048, torch.bfloat16)])
@@ -72,8 +73,8 @@ def test_native_fp4_linear_forward_backward():
     y = be.linear(x, w, None)
     g = torch.randn_like(y)
     y.backward(g)
-    xq = fp4.quant_dequant_reference(x.detach().float().view(-1, 512))
-    wq = fp4.quant_dequant_reference(w.detach().float())
+    xq = fp4.quant_dequant_reference(x.detach().float().cpu().view(-1, 512)).to(dev)
+    wq = fp4.quant_dequant_reference(w.detach().float().cpu()).to(dev)
     yr = (xq @ wq.t()).view_as(y)
     assert _rel(y, yr) < GEMM_TOL
     assert _rel(x.grad.view(-1, 512), g.float().view(-1, 768) @ wq) < 1e-2
