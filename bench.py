@@ -47,10 +47,19 @@ MICRO_BATCH = 1
 #   gpt1.3b-fp4-dp: GPT-1.3B shape (H 2048, 24 layers, 16 heads, GELU 8192, vocab 50304), NVFP4
 #   linears (e2m1 operands in 1x16 blocks with e4m3 scales on the fp4 tensor cores, bf16 params,
 #   fp32 master / moments), DP = N with ZeRO-1, seq 2048, micro-batch 8 per rank (weak scaling).
+#   dsv2lite-fp8-ep: DeepSeek-V2-Lite shape under the deepseek_v3 fp8 recipe (1x128 activation and
+#   128x128 weight e4m3 scales, stochastic rounding, e4m3 MoE payload), EP = N folded inside DP = N
+#   (every rank its own batch), seq 4096, micro-batch 2 per rank; 27 layers for N > 1 and 8 (1 dense
+#   + 7 MoE) on one GPU, whose 180 GB cannot hold 27 layers of 64 experts with fp32 master weights
+#   and moments. The reference's MLA always factorises q, so both arms use a q-LoRA of rank 1536.
 CONFIGS = {
     "llama8b-tp": dict(model=MODEL_NAME, seq=SEQ, batch_per_rank=None, vocab=128256),
     "gpt1.3b-fp4-dp": dict(model="GPT-1.3B-shape dense TransformerModel (H2048, 24 layers, 16 heads, GELU 8192, "
                                  "vocab 50304), NVFP4 linears", seq=2048, batch_per_rank=8, vocab=50304),
+    "dsv2lite-fp8-ep": dict(model="DeepSeek-V2-Lite-shape MoE DeepSeekModel (H2048, MLA 16 heads kv_lora 512 "
+                                  "q-LoRA 1536 nope 128 rope 64 v 128, first layer dense FFN 10944, 64 routed experts "
+                                  "top-6 + 2 shared, expert FFN 1408, vocab 102400), deepseek_v3 fp8 recipe",
+                            seq=4096, batch_per_rank=2, vocab=102400),
 }
 
 
@@ -177,6 +186,90 @@ def build_gpt_fp4(args, rank, world):
     return trainer, layers
 
 
+def build_dsv2lite(args, rank, world):
+    """DeepSeek-V2-Lite shape, fp8 recipe on the native backend, EP = world folded inside DP = world
+    (dense parameters replicated and ZeRO-1 sharded over the world; expert parameters unique per rank)."""
+    sys.path.insert(0, ROOT)
+    from nano_train_b200.distributed.topology import initialize_model_parallel
+    from nano_train_b200.models.deepseek import DeepSeekModel, DeepSeekModelConfig, DeepSeekParallelContext
+    from nano_train_b200.parallel.flat_optimizer import FlatAdamW, split_decay_groups
+    from nano_train_b200.precision.mixed_precision import (build_module_precision_resolver,
+                                                           finalize_module_precision_resolver,
+                                                           resolve_precision_config)
+
+    layers = args.layers or (8 if world == 1 else 27)
+    pc = resolve_precision_config(argparse.Namespace(precision_recipe="deepseek_v3", fp8=True, fp8_backend="native",
+                                                     params_dtype="bf16"), torch.device("cuda"))
+    resolver = build_module_precision_resolver(pc)
+    ep_group, ep_rank = None, 0
+    if world > 1:
+        par = initialize_model_parallel(tensor_model_parallel_size=1, pipeline_model_parallel_size=1,
+                                        expert_model_parallel_size=world, context_parallel_size=1,
+                                        expert_layout="fold_dp")
+        ep_group, ep_rank = par.expert_model_parallel_group, par.expert_model_parallel_rank
+    torch.manual_seed(1234 + rank)  # experts differ per rank; dense weights are broadcast below
+    cfg = DeepSeekModelConfig(param_dtype=torch.bfloat16, param_device=torch.device("cuda"),
+                              precision_resolver=resolver, vocab_size=102400, hidden_size=2048,
+                              num_hidden_layers=layers, num_attention_heads=16, num_key_value_heads=16,
+                              intermediate_size=10944, max_position_embeddings=4096, q_lora_rank=1536,
+                              kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+                              moe_intermediate_size=1408, n_routed_experts=64, n_shared_experts=2,
+                              num_experts_per_tok=6, first_k_dense_replace=1, scoring_func="softmax", n_group=1,
+                              topk_group=1, norm_topk_prob=False, routed_scaling_factor=1.0,
+                              comm_quant_backend="native")
+    pctx = DeepSeekParallelContext(expert_model_parallel_rank=ep_rank,
+                                   expert_model_parallel_size=world, expert_model_parallel_group=ep_group)
+    model = DeepSeekModel(cfg, parallel_context=pctx)
+    finalize_module_precision_resolver(resolver)
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.dim() >= 2:
+                p.normal_(0.0, 0.006)
+    dense = [p for p in model.parameters() if not getattr(p, "expert_model_parallel", False)]
+    experts = [p for p in model.parameters() if getattr(p, "expert_model_parallel", False)]
+    if world > 1:
+        for p in dense:
+            dist.broadcast(p.data, src=0)
+
+    class _Params(torch.nn.Module):  # split_decay_groups over a subset of the parameters
+        def __init__(self, params):
+            super().__init__()
+            self.ps = torch.nn.ParameterList(params)
+
+    opts = [FlatAdamW(split_decay_groups(_Params(dense), 0.1), lr=3e-4, weight_decay=0.1, max_grad_norm=1.0,
+                      dp_group=dist.group.WORLD if world > 1 else None, strategy="optim" if world > 1 else "no_shard")]
+    if experts:
+        opts.append(FlatAdamW(split_decay_groups(_Params(experts), 0.1), lr=3e-4, weight_decay=0.1,
+                              max_grad_norm=1.0))
+    return _MoETrainer(model, opts), layers
+
+
+class _MoETrainer:
+    """One step: forward, fused cross-entropy + 0.01 x router aux loss, backward, both optimizers
+    (dense over the DP group, experts local). The loss stays on the device."""
+
+    def __init__(self, model, opts):
+        from nano_train_b200.models.moe import ExpertParallelMoE, LocalRoutedMoE
+
+        self.model, self.opts = model, opts
+        self.moes = [m for m in model.modules() if isinstance(m, (ExpertParallelMoE, LocalRoutedMoE))]
+
+    def train_step(self, input_ids, labels):
+        from nano_train_b200 import ops
+
+        ids = input_ids.to("cuda", non_blocking=True)
+        lab = labels.to("cuda", non_blocking=True)
+        for o in self.opts:
+            o.zero_grad()
+        logits = self.model(ids)
+        task = ops.cross_entropy(logits.view(-1, logits.shape[-1]), lab.reshape(-1), inplace_grad=True)
+        aux = torch.stack([m.last_aux_loss.float().reshape(()) for m in self.moes]).sum() if self.moes else 0.0
+        (task + 0.01 * aux).backward()
+        for o in self.opts:
+            o.step()
+        return task.detach()
+
+
 def build_ours(args, rank, world):
     sys.path.insert(0, ROOT)
     from nano_train_b200.config import TPConfig
@@ -185,6 +278,8 @@ def build_ours(args, rank, world):
 
     if args.config == "gpt1.3b-fp4-dp":
         return build_gpt_fp4(args, rank, world)
+    if args.config == "dsv2lite-fp8-ep":
+        return build_dsv2lite(args, rank, world)
 
     layers = args.layers or (8 if world == 1 else 32)
     tp = world
@@ -312,7 +407,9 @@ def main():
                 "higher_is_better": True,
                 "scaling": "weak" if dp_run else "strong",
                 "vs_baseline": None,
-                "dtype": "nvfp4 GEMM operands, bf16 activations" if dp_run else "bf16",
+                "dtype": {"gpt1.3b-fp4-dp": "nvfp4 GEMM operands, bf16 activations",
+                          "dsv2lite-fp8-ep": "e4m3 GEMM operands (deepseek_v3 recipe), bf16 activations"}.get(
+                              args.config, "bf16"),
                 "data": "synthetic (uniform token ids, seeded); random-init N(0,0.02) weights",
                 "config": {
                     "name": args.config,
@@ -321,7 +418,8 @@ def main():
                     "global_batch": cfg["batch_per_rank"] * world if dp_run else GLOBAL_BATCH,
                     "micro_batch": cfg["batch_per_rank"] if dp_run else MICRO_BATCH,
                     "seq_len": args.seq,
-                    "parallelism": (f"dp{world}" + ("+zero1" if world > 1 else "")) if dp_run else
+                    "parallelism": (f"ep{world}+dp{world}" if args.config == "dsv2lite-fp8-ep" else
+                                    f"dp{world}" + ("+zero1" if world > 1 else "")) if dp_run else
                                    (f"tp{world}" + ("+sp" if world > 1 else "")),
                     "optimizer": "AdamW fp32 master/moments, bf16 params, fp32 main grads, clip 1.0",
                     "l2": "working set >> 126 MB L2 (no explicit flush)",

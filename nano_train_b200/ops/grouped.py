@@ -61,13 +61,16 @@ class _StackCache:
             self._params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
         return self._params
 
-    def get(self, experts):
+    def get(self, experts, fp8: bool = False):
+        """(w1, w2); with ``fp8`` every expert matrix is rounded through e4m3 in 128 x 128 blocks
+        first (the recipe's weight quantisation), so the bf16 GEMMs see the fp8 values."""
         params = self.params(experts)
-        key = tuple((p.data_ptr(), p._version) for p in params)
+        key = (bool(fp8),) + tuple((p.data_ptr(), p._version) for p in params)
         if key != self.key:
             with torch.no_grad():
-                self.w1 = torch.cat([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in experts], 0)
-                self.w2 = torch.cat([e.down_proj.weight for e in experts], 0)
+                q = (lambda w: ext().fp8_quant_dequant(w.contiguous(), 128, False, 0)) if fp8 else (lambda w: w)
+                self.w1 = torch.cat([torch.cat([q(e.gate_proj.weight), q(e.up_proj.weight)], 0) for e in experts], 0)
+                self.w2 = torch.cat([q(e.down_proj.weight) for e in experts], 0)
             self.key = key
         return self.w1, self.w2
 
@@ -123,16 +126,29 @@ class GroupedBuffers:
         self.dx_out = dx_out
 
 
+_FP8_SEED = [0]
+
+
 class _GroupedSwiGLUFn(torch.autograd.Function):
+    """``fp8``: None, or the rounding of the e4m3 activation quantisation ("nearest" /
+    "stochastic"): both GEMM inputs are rounded through e4m3 in 1 x 128 tiles (the weights
+    arrive already rounded in 128 x 128 blocks), the backward is straight-through on those
+    rounded operands, as in the fp8 linear backend."""
+
     @staticmethod
-    def forward(ctx, x_pad, offsets, w1, w2, n_experts, bufs, *params):
+    def forward(ctx, x_pad, offsets, w1, w2, n_experts, bufs, fp8, *params):
         C = ext()
         R = x_pad.shape[0]
         I2 = w1.shape[0] // n_experts
         H = w2.shape[0] // n_experts
+        if fp8 is not None:
+            _FP8_SEED[0] += 1
+            x_pad = C.fp8_quant_dequant(x_pad.contiguous(), 1, fp8 == "stochastic", _FP8_SEED[0])
         h = torch.empty(R, I2, device=x_pad.device, dtype=x_pad.dtype)
         C.gemm_grouped_bf16(x_pad, w1, h, offsets, 1)
         a = C.swiglu_fwd(h)
+        if fp8 is not None:
+            a = C.fp8_quant_dequant(a, 1, fp8 == "stochastic", _FP8_SEED[0] + (1 << 40))
         y = bufs.y_out if bufs is not None and bufs.y_out is not None else \
             torch.empty(R, H, device=x_pad.device, dtype=x_pad.dtype)
         C.gemm_grouped_bf16(a, w2, y, offsets, 1)
@@ -166,7 +182,7 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
         C.gemm_grouped_bf16(dh, w1, dx, offsets, 1, b_mn=True)          # dX = dH . W1_e
         if flat is not None:                                              # dW1_e += dH_e^T X_e into main_grad
             C.gemm_grouped_bf16(dh, x_pad, flat[0], offsets, 2, b_mn=True, accumulate=True, c_group_stride=3 * I)
-            return (dx, None, None, None, None, None, *([None] * len(ctx.params)))
+            return (dx, None, None, None, None, None, None, *([None] * len(ctx.params)))
         dw1 = torch.zeros(E * I2, x_pad.shape[1], device=dy.device, dtype=torch.float32)
         C.gemm_grouped_bf16(dh, x_pad, dw1, offsets, 2, b_mn=True)      # dW1_e = dH_e^T X_e
         slices = []
@@ -183,7 +199,7 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
             grads = []
             for e in range(E):
                 grads += [dw1c[e * I2:e * I2 + I], dw1c[e * I2 + I:(e + 1) * I2], dw2c[e * H:(e + 1) * H]]
-        return (dx, None, None, None, None, None, *grads)
+        return (dx, None, None, None, None, None, None, *grads)
 
 
 def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts, cache: _StackCache,
@@ -191,18 +207,36 @@ def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts
     """Apply expert e to its rows of ``x_sorted`` (rows grouped by expert, ``counts`` per expert)."""
     offsets, rows = pad_segments(counts, max_rows)
     x_pad, dest = scatter_rows_to_segments(x_sorted, counts, offsets, rows)
-    w1, w2 = cache.get(experts)
+    fp8 = grouped_fp8_rounding(experts)
+    w1, w2 = cache.get(experts, fp8=fp8 is not None)
     params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
     y_pad = _GroupedSwiGLUFn.apply(x_pad, offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), None,
-                                   *params)
+                                   fp8, *params)
     return y_pad.index_select(0, dest)
+
+
+def grouped_fp8_rounding(experts):
+    """The activation rounding mode when the experts' linears run the native fp8 backend with the
+    DeepSeek-V3 granularities (the grouped path then reproduces their numerics); else None."""
+    from ..precision.backends import NativeFP8Backend
+
+    e0 = experts[0]
+    lins = (e0.gate_proj, e0.up_proj, e0.down_proj)
+    if not any(lin._lowbit_active() for lin in lins):
+        return None
+    bes = [lin._lowbit_backend for lin in lins]
+    if all(isinstance(b, NativeFP8Backend) and b._activation_granularity == "tile_1x128"
+           and b._weight_granularity == "block_128x128" for b in bes):
+        return bes[0]._rounding_mode
+    return None
 
 
 def grouped_kernel_ok(x: torch.Tensor, experts) -> bool:
     if not (x.is_cuda and x.dtype == torch.bfloat16 and len(experts) > 0):
         return False
     e0 = experts[0]
-    if e0.gate_proj._lowbit_active() or e0.up_proj._lowbit_active() or e0.down_proj._lowbit_active():
-        return False
     H, I = e0.gate_proj.weight.shape[1], e0.gate_proj.weight.shape[0]
+    if any(lin._lowbit_active() for lin in (e0.gate_proj, e0.up_proj, e0.down_proj)):
+        # low-bit experts take the grouped path only where it reproduces their numerics
+        return grouped_fp8_rounding(experts) is not None and H % 128 == 0 and I % 128 == 0
     return H % 8 == 0 and I % 8 == 0

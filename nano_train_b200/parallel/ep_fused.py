@@ -525,7 +525,7 @@ class _EPCombineFn(torch.autograd.Function):
 def fused_ep_moe(tokens: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts, stack_cache, *,
                  group, num_experts: int, capacity_factor: float, fp8_payload: bool, stochastic: bool):
     """Routed-expert output [T, H] of an expert-parallel MoE layer and (stats, kept_counts) device tensors."""
-    from ..ops.grouped import GroupedBuffers, _GroupedSwiGLUFn
+    from ..ops.grouped import GroupedBuffers, _GroupedSwiGLUFn, grouped_fp8_rounding
 
     n = comm.group_size(group)
     T, H = tokens.shape
@@ -537,9 +537,10 @@ def fused_ep_moe(tokens: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Ten
                     capacity_factor=capacity_factor, num_experts=num_experts, stochastic=stochastic)
     x_pad = _EPDispatchFn.apply(tokens, st)
     rp = st.rp
-    w1, w2 = stack_cache.get(experts)
+    fp8 = grouped_fp8_rounding(experts)
+    w1, w2 = stack_cache.get(experts, fp8=fp8 is not None)
     bufs = GroupedBuffers(y_out=ws.y(rp.rows), dx_out=ws.dx(rp.rows))
-    y = _GroupedSwiGLUFn.apply(x_pad, rp.offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), bufs,
+    y = _GroupedSwiGLUFn.apply(x_pad, rp.offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), bufs, fp8,
                                *stack_cache.params(experts))
     out = _EPCombineFn.apply(y, topk_w.float().reshape(-1), st)
     return out.to(tokens.dtype), rp.stats, rp.kept_counts
