@@ -376,13 +376,23 @@ def main():
     n = args.gpus
     rank, local, world = init_dist(n)
     try:
-        if args.impl == "reference" and args.config != "llama8b-tp":
+        if args.impl == "reference" and args.config == "dsv2lite-fp8-ep":
+            sys.path.insert(0, ROOT)
+            from bench_reference import run_deepseek
+
+            res = run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks, ClockSampler,
+                               batch=CONFIGS[args.config]["batch_per_rank"])
+            if res is None:
+                return
+            ms, layers, launches, clocks, e2e = res
+            fused_paths = None
+        elif args.impl == "reference" and args.config != "llama8b-tp":
             if rank == 0:
                 print(json.dumps({"impl": "reference", "config": args.config,
                                   "unavailable": "the reference arm is wired for the default llama8b-tp config only"}),
                       flush=True)
             return
-        if args.impl == "reference":
+        elif args.impl == "reference":
             sys.path.insert(0, ROOT)
             res = run_reference(args, rank, local, world)
             if res is None:

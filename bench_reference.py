@@ -181,3 +181,93 @@ def run(args, rank, local, world, global_batch, micro_batch, make_batches, barri
                "h2d_bytes_per_step": 2 * global_batch * args.seq * 8, "d2h_bytes_per_step": 4,
                "api": "reference primitives (src.layers / src.models.deepseek) + PrecisionAdamW"}
     return ms, layers, 0, sampler.summary(), e2e
+
+
+def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks, ClockSampler, batch, dims=None):
+    """The DeepSeek-V2-Lite-shape fp8 configuration through the reference's own public API:
+    ``src.models.deepseek.DeepSeekModel`` built from its config under the reference's
+    ``resolve_precision_config`` with the deepseek_v3 recipe on its stock (emulated) fp8 backend,
+    its router aux losses, ``PrecisionAdamW`` with fp32 main weights and moments. One GPU (EP = 1):
+    the reference cannot fold EP into DP. ``dims`` shrinks the model for a CPU check of this code."""
+    ref = _import_reference()
+    if ref is None:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}), flush=True)
+        return None
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "config": args.config, "unavailable":
+                              "the reference rejects EP folded into DP (EP = N forces DP = 1); measured at N = 1"}),
+                  flush=True)
+        return None
+    import argparse as _ap
+
+    from src.models.deepseek import DeepSeekModel, DeepSeekModelConfig
+    from src.models.moe import ExpertParallelMoE, LocalRoutedMoE
+    from src.runtime.mixed_precision import build_module_precision_resolver, resolve_precision_config
+    from src.runtime.optimizer_runtime import PrecisionAdamW
+
+    dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+    pargs = _ap.Namespace(precision_recipe="deepseek_v3", bf16=False, fp16=False, fp8=True, fp4=False,
+                          fp8_backend="emulated", params_dtype="bf16" if dev.type == "cuda" else "fp32")
+    pc = resolve_precision_config(pargs, dev)
+    res = build_module_precision_resolver(pc)
+    d = dict(vocab_size=102400, hidden_size=2048, num_hidden_layers=args.layers or 8, num_attention_heads=16,
+             num_key_value_heads=16, intermediate_size=10944, max_position_embeddings=4096, q_lora_rank=1536,
+             kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+             moe_intermediate_size=1408, n_routed_experts=64, n_shared_experts=2, num_experts_per_tok=6,
+             first_k_dense_replace=1, scoring_func="softmax", n_group=1, topk_group=1, norm_topk_prob=False,
+             routed_scaling_factor=1.0)
+    d.update(dims or {})
+    torch.manual_seed(1234)
+    dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
+    model = DeepSeekModel(DeepSeekModelConfig(param_dtype=dt, param_device=dev, precision_resolver=res, **d))
+    with torch.no_grad():
+        for p in model.parameters():
+            if p.dim() >= 2:
+                p.normal_(0.0, 0.006)
+    moes = [m for m in model.modules() if isinstance(m, (LocalRoutedMoE, ExpertParallelMoE))]
+    opt = PrecisionAdamW(model.parameters(), lr=3e-4, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8,
+                         main_params_dtype="fp32", main_grads_dtype="fp32", exp_avg_dtype="fp32",
+                         exp_avg_sq_dtype="fp32")
+
+    def step(ids_h, lab_h):
+        ids, lab = ids_h.to(dev, non_blocking=True), lab_h.to(dev, non_blocking=True)
+        opt.zero_grad()
+        logits = model(ids)
+        loss = F.cross_entropy(logits.float().view(-1, logits.size(-1)), lab.reshape(-1))
+        aux = torch.stack([m.last_aux_loss.float().reshape(()) for m in moes]).sum()
+        (loss + 0.01 * aux).backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return loss.detach()
+
+    batches = make_batches(2, args.seq, d["vocab_size"], batch=batch)
+    for i in range(args.warmup):
+        step(*batches[i % len(batches)])
+    if dev.type != "cuda":
+        return float(step(*batches[0]))
+    barrier(world)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        step(*batches[i % len(batches)])
+    e.record()
+    barrier(world)
+    sampler.stop()
+    ms = s.elapsed_time(e) / args.steps
+    e2e = None
+    if not args.no_e2e:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            float(step(*batches[i % len(batches)]))
+        torch.cuda.synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        e2e = {"value": batch * args.seq / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": 2 * batch * args.seq * 8, "d2h_bytes_per_step": 4,
+               "api": "src.models.deepseek.DeepSeekModel + PrecisionAdamW (deepseek_v3 recipe, emulated fp8)"}
+    return ms, d["num_hidden_layers"], 0, sampler.summary(), e2e
