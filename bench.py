@@ -351,7 +351,8 @@ def run_ours(args, rank, local, world):
         tok = tokens_per_step(args, world)
         e2e = {"value": tok / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": 2 * rows * args.seq * 8, "d2h_bytes_per_step": 4,
-               "api": "nano_train_b200.training.LMTrainer.train_step"}
+               "api": ("DeepSeekModel + FlatAdamW step (bench.py _MoETrainer)" if args.config == "dsv2lite-fp8-ep"
+                       else "nano_train_b200.training.LMTrainer.train_step")}
     return ms, layers, launches, sampler.summary(), e2e, fused_paths
 
 
@@ -420,7 +421,8 @@ def main():
                 "dtype": {"gpt1.3b-fp4-dp": "nvfp4 GEMM operands, bf16 activations",
                           "dsv2lite-fp8-ep": "e4m3 GEMM operands (deepseek_v3 recipe), bf16 activations"}.get(
                               args.config, "bf16"),
-                "data": "synthetic (uniform token ids, seeded); random-init N(0,0.02) weights",
+                "data": "synthetic (uniform token ids, seeded); random-init N(0,%s) weights"
+                        % ("0.006" if args.config == "dsv2lite-fp8-ep" else "0.02"),
                 "config": {
                     "name": args.config,
                     "model": cfg["model"],
