@@ -387,6 +387,16 @@ def main():
                 return
             ms, layers, launches, clocks, e2e = res
             fused_paths = None
+        elif args.impl == "reference" and args.config == "gpt1.3b-fp4-dp":
+            sys.path.insert(0, ROOT)
+            from bench_reference import run_gpt_fp4
+
+            res = run_gpt_fp4(args, rank, local, world, make_batches, barrier, ClockSampler,
+                              batch=CONFIGS[args.config]["batch_per_rank"])
+            if res is None:
+                return
+            ms, layers, launches, clocks, e2e = res
+            fused_paths = None
         elif args.impl == "reference" and args.config != "llama8b-tp":
             if rank == 0:
                 print(json.dumps({"impl": "reference", "config": args.config,

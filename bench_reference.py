@@ -271,3 +271,80 @@ def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks
                "h2d_bytes_per_step": 2 * batch * args.seq * 8, "d2h_bytes_per_step": 4,
                "api": "src.models.deepseek.DeepSeekModel + PrecisionAdamW (deepseek_v3 recipe, emulated fp8)"}
     return ms, d["num_hidden_layers"], 0, sampler.summary(), e2e
+
+
+def run_gpt_fp4(args, rank, local, world, make_batches, barrier, ClockSampler, batch, dims=None):
+    """The GPT-1.3B-shape fp4 configuration through the reference's own ``TransformerModel`` (GPT-2
+    block, materialised attention, tied head) under its ``resolve_precision_config`` with ``--fp4`` on
+    its stock (emulated, integer-grid) fp4 backend, ``PrecisionAdamW`` with fp32 main weights and
+    moments. One GPU: the reference wires ZeRO only for its DeepSeekModel."""
+    ref = _import_reference()
+    if ref is None:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}), flush=True)
+        return None
+    if world > 1:
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "config": args.config, "unavailable":
+                              "the reference wires ZeRO-1 only for DeepSeekModel; measured at N = 1"}), flush=True)
+        return None
+    import argparse as _ap
+
+    from src.config import ModelConfig
+    from src.models.transformer import TransformerModel
+    from src.runtime.mixed_precision import build_module_precision_resolver, resolve_precision_config
+    from src.runtime.optimizer_runtime import PrecisionAdamW
+
+    dev = torch.device("cuda") if torch.cuda.is_available() else torch.device("cpu")
+    pargs = _ap.Namespace(precision_recipe="default", bf16=False, fp16=False, fp8=False, fp4=True,
+                          fp4_backend="emulated", params_dtype="bf16" if dev.type == "cuda" else "fp32")
+    res = build_module_precision_resolver(resolve_precision_config(pargs, dev))
+    d = dict(hidden_size=2048, num_layers=args.layers or 24, num_attention_heads=16, intermediate_size=8192,
+             max_position_embeddings=2048, vocab_size=50304, dropout=0.0)
+    d.update(dims or {})
+    torch.manual_seed(1234)
+    dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
+    model = TransformerModel(ModelConfig(param_dtype=dt, param_device=dev, precision_resolver=res, **d))
+    opt = PrecisionAdamW(model.parameters(), lr=3e-4, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8,
+                         main_params_dtype="fp32", main_grads_dtype="fp32", exp_avg_dtype="fp32",
+                         exp_avg_sq_dtype="fp32")
+
+    def step(ids_h, lab_h):
+        ids, lab = ids_h.to(dev, non_blocking=True), lab_h.to(dev, non_blocking=True)
+        opt.zero_grad()
+        logits = model(ids)
+        loss = F.cross_entropy(logits.float().view(-1, logits.size(-1)), lab.reshape(-1))
+        loss.backward()
+        torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+        opt.step()
+        return loss.detach()
+
+    batches = make_batches(2, args.seq, d["vocab_size"], batch=batch)
+    for i in range(args.warmup):
+        step(*batches[i % len(batches)])
+    if dev.type != "cuda":
+        return float(step(*batches[0]))
+    barrier(world)
+    sampler = ClockSampler(local)
+    sampler.start()
+    time.sleep(0.3)
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(args.steps):
+        step(*batches[i % len(batches)])
+    e.record()
+    barrier(world)
+    sampler.stop()
+    ms = s.elapsed_time(e) / args.steps
+    e2e = None
+    if not args.no_e2e:
+        t0 = time.perf_counter()
+        for i in range(args.steps):
+            float(step(*batches[i % len(batches)]))
+        torch.cuda.synchronize()
+        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        e2e = {"value": batch * args.seq / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
+               "h2d_bytes_per_step": 2 * batch * args.seq * 8, "d2h_bytes_per_step": 4,
+               "api": "src.models.transformer.TransformerModel + PrecisionAdamW (--fp4, emulated backend)"}
+    return ms, d["num_layers"], 0, sampler.summary(), e2e
