@@ -428,8 +428,11 @@ def main():
                 "higher_is_better": True,
                 "scaling": "weak" if dp_run else "strong",
                 "vs_baseline": None,
-                "dtype": {"gpt1.3b-fp4-dp": "nvfp4 GEMM operands, bf16 activations",
-                          "dsv2lite-fp8-ep": "e4m3 GEMM operands (deepseek_v3 recipe), bf16 activations"}.get(
+                "dtype": ({"gpt1.3b-fp4-dp": "reference fp4 emulation (integer grid, fp32 GEMM), bf16 params",
+                           "dsv2lite-fp8-ep": "reference fp8 emulation (deepseek_v3 recipe, fp32 GEMM), bf16 params"}
+                          if args.impl == "reference" else
+                          {"gpt1.3b-fp4-dp": "nvfp4 GEMM operands, bf16 activations",
+                           "dsv2lite-fp8-ep": "e4m3 GEMM operands (deepseek_v3 recipe), bf16 activations"}).get(
                               args.config, "bf16"),
                 "data": "synthetic (uniform token ids, seeded); random-init N(0,%s) weights"
                         % ("0.006" if args.config == "dsv2lite-fp8-ep" else "0.02"),
