@@ -625,9 +625,42 @@ def render_markdown(info: ModelInfo, extras: Optional[dict] = None) -> str:
     return "\n".join(lines) + "\n"
 
 
+def plot_roofline(info: ModelInfo, path: str, targets: Optional[list] = None) -> str:
+    """Roofline of every target (attainable TFLOP/s against FLOP per HBM byte) with the model's
+    operating points (one per mode and execution model, on the first target) as an SVG file."""
+    from .svg_plot import Series, loglog_svg
+
+    targets = targets or default_roofline_targets()
+    kp = [k for k in info.kpis if k.t_est_ms > 0 and k.ai_hbm > 0]
+    lo = min([k.ai_hbm for k in kp] + [1.0]) / 4
+    hi = max([k.ai_hbm for k in kp] + [t.knee for t in targets]) * 4
+    xs = [lo * (hi / lo) ** (i / 60) for i in range(61)]
+    series = [Series(f"{t.name} roof", xs, [min(t.peak_tflops, x * t.hbm_gbs / 1e3) for x in xs], dashed=True)
+              for t in targets]
+    first = targets[0].name if targets else None
+    for xm in sorted({k.exec_model for k in kp}):
+        pts = [k for k in kp if k.exec_model == xm and k.target == first]
+        series.append(Series(f"{xm} ({first})", [k.ai_hbm for k in pts],
+                             [k.flops_realizable / (k.t_est_ms * 1e-3) / 1e12 for k in pts], kind="points",
+                             point_labels=[k.mode for k in pts]))
+    return loglog_svg(path, series, title="Roofline and operating points", xlabel="FLOP per HBM byte",
+                      ylabel="TFLOP/s per GPU")
+
+
+def plot_decode_sweep(rows: list, path: str) -> str:
+    """Decode tokens/s per GPU against the batch size, one line per target, as an SVG file."""
+    from .svg_plot import Series, loglog_svg
+
+    names = list(rows[0]["tokens_per_s"]) if rows else []
+    series = [Series(n, [r["batch"] for r in rows], [r["tokens_per_s"][n] for r in rows]) for n in names]
+    return loglog_svg(path, series, title="Decode throughput against batch", xlabel="batch (sequences)",
+                      ylabel="tokens/s")
+
+
 def dump_model_info(model: nn.Module, output_path: str, *, sweeps: bool = True,
-                    sensitivity: Optional[SensitivityConfig] = None, **kw) -> ModelInfo:
-    """Write the Markdown report (and a JSON twin) for ``model``; returns the estimate."""
+                    sensitivity: Optional[SensitivityConfig] = None, plots: bool = True, **kw) -> ModelInfo:
+    """Write the Markdown report (and a JSON twin, and with ``plots`` SVG charts beside them:
+    ``<name>_roofline.svg``, ``<name>_decode_sweep.svg``) for ``model``; returns the estimate."""
     info = estimate(model, **kw)
     extras: dict = {}
     if sweeps:
@@ -640,8 +673,17 @@ def dump_model_info(model: nn.Module, output_path: str, *, sweeps: bool = True,
             extras["ep_exploration"] = decode_ep_exploration(model)
         extras["sensitivity"] = sensitivity_grid(model, sensitivity, parallel=par)
     os.makedirs(os.path.dirname(os.path.abspath(output_path)), exist_ok=True)
+    base = os.path.splitext(output_path)[0]
+    plot_files = []
+    if plots:
+        plot_files.append(plot_roofline(info, base + "_roofline.svg", kw.get("targets")))
+        if extras.get("decode_sweep"):
+            plot_files.append(plot_decode_sweep(extras["decode_sweep"], base + "_decode_sweep.svg"))
     with open(output_path, "w") as f:
         f.write(render_markdown(info, extras))
+        if plot_files:
+            f.write("\n## Plots\n\n" + "\n".join(f"![{os.path.basename(p)}]({os.path.basename(p)})"
+                                                     for p in plot_files) + "\n")
     js = {"architecture": info.architecture, "total_params": info.total_params,
           "active_params_per_token": info.active_params_per_token, "params_by_kind": info.params_by_kind,
           "kv_cache_bytes_per_token": info.kv_cache_bytes_per_token,
@@ -652,7 +694,8 @@ def dump_model_info(model: nn.Module, output_path: str, *, sweeps: bool = True,
         js["prefill_sweep"] = [asdict(k) for k in extras["prefill_sweep"]]
         js["ep_exploration"] = extras.get("ep_exploration", [])
         js["sensitivity"] = [asdict(p) for p in extras["sensitivity"]]
-    with open(os.path.splitext(output_path)[0] + ".json", "w") as f:
+    js["plots"] = [os.path.basename(p) for p in plot_files]
+    with open(base + ".json", "w") as f:
         json.dump(js, f, indent=1)
     return info
 
@@ -660,4 +703,4 @@ def dump_model_info(model: nn.Module, output_path: str, *, sweeps: bool = True,
 __all__ = ["RooflineConfig", "default_roofline_targets", "ExecutionModel", "default_execution_models",
            "TensorCoreModel", "ParallelismAssumptions", "ModelInfo", "ModeKpi", "estimate", "dump_model_info",
            "render_markdown", "decode_sweep", "prefill_sweep", "DecodeEPExplorationConfig", "decode_ep_exploration",
-           "SensitivityConfig", "SensitivityPoint", "sensitivity_grid"]
+           "SensitivityConfig", "SensitivityPoint", "sensitivity_grid", "plot_roofline", "plot_decode_sweep"]

@@ -117,6 +117,10 @@ def test_model_report_llama8b(tmp_path):
     assert train.flops == pytest.approx(6 * 32768 * (info.total_params - 128256 * 4096), rel=0.08)
     assert train.net_bytes > 0
     assert os.path.exists(tmp_path / "r.md") and os.path.exists(tmp_path / "r.json")
+    for name in ("r_roofline.svg", "r_decode_sweep.svg"):  # dependency-free SVG charts beside the report
+        svg = (tmp_path / name).read_text()
+        assert svg.startswith("<svg") and svg.rstrip().endswith("</svg>") and "<polyline" in svg
+    assert "r_roofline.svg" in (tmp_path / "r.md").read_text()
 
 
 def test_trainer_runs_and_checkpoints(tmp_path):
