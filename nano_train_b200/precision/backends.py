@@ -19,6 +19,7 @@
 """
 from __future__ import annotations
 
+import weakref
 from contextlib import nullcontext
 from typing import Optional, Protocol
 
@@ -213,6 +214,15 @@ def e4m3_stochastic_round(y: torch.Tensor, generator=None) -> torch.Tensor:
 _WQ_CACHE: dict = {}
 
 
+def _remember(cache: dict, w: torch.Tensor, entry) -> None:
+    """Store ``entry`` for weight ``w`` (keyed by ``id(w)``); the entry goes away with the weight,
+    so quantised copies of dead weights are not kept alive and a reused id never hits a stale one."""
+    key = id(w)
+    if key not in cache:
+        weakref.finalize(w, cache.pop, key, None)
+    cache[key] = entry
+
+
 def _quantized_weight(w: torch.Tensor):
     """e4m3 copy of a weight in 128 x 128 blocks, re-quantised only when the weight changed."""
     key = id(w)
@@ -220,7 +230,7 @@ def _quantized_weight(w: torch.Tensor):
     if ent is not None and ent[0] == (w.data_ptr(), w._version):
         return ent[1], ent[2]
     wq, sw = ops.ext().fp8_quantize(w.detach().contiguous(), 128, False, 0)
-    _WQ_CACHE[key] = ((w.data_ptr(), w._version), wq, sw)
+    _remember(_WQ_CACHE, w, ((w.data_ptr(), w._version), wq, sw))
     return wq, sw
 
 
@@ -346,7 +356,7 @@ def _nvfp4_weight(w: torch.Tensor):
     if ent is not None and ent[0] == (w.data_ptr(), w._version):
         return ent[1]
     packed = fp4.quantize(w.detach().to(torch.bfloat16))
-    _W4_CACHE[key] = ((w.data_ptr(), w._version), packed)
+    _remember(_W4_CACHE, w, ((w.data_ptr(), w._version), packed))
     return packed
 
 

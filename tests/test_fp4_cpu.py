@@ -65,3 +65,18 @@ def test_native_fp4_backend_cpu_ste():
     # straight-through: gradients are those of the unquantised linear on the quantised operands
     torch.testing.assert_close(w.grad, (torch.ones(16, 64).t() @ fp4.quant_dequant_reference(x.detach()).view(16, 128)),
                                rtol=1e-5, atol=1e-5)
+
+
+def test_quantised_weight_cache_entries_die_with_the_weight():
+    import gc
+
+    from nano_train_b200.precision.backends import _remember
+
+    cache = {}
+    w = torch.nn.Parameter(torch.randn(4, 4))
+    _remember(cache, w, "quantised copy")
+    _remember(cache, w, "refreshed copy")  # same weight, new version: one entry
+    assert list(cache.values()) == ["refreshed copy"]
+    del w
+    gc.collect()
+    assert cache == {}
