@@ -43,7 +43,7 @@ class DeepSeekModelConfig:
     intermediate_size: int = 18432
     max_position_embeddings: int = 163840
     rms_norm_eps: float = 1e-6
-    q_lora_rank: int = 1536
+    q_lora_rank: Optional[int] = 1536  # 0 / None: a direct q projection (DeepSeek-V2-Lite)
     kv_lora_rank: int = 512
     qk_nope_head_dim: int = 128
     qk_rope_head_dim: int = 64
@@ -298,17 +298,25 @@ class MultiHeadLatentAttention(nn.Module):
                   precision_resolver=config.precision_resolver)
         tpkw = dict(tp_rank=self.attention_tensor_model_parallel_rank, tp_size=tp,
                     tp_group=self.attention_tensor_model_parallel_group)
-        self.q_a_proj = Linear(self.hidden_size, config.q_lora_rank, bias=False, module_path=f"{module_prefix}.q_a_proj",
-                               **kw)
-        self.q_a_norm = RMSNorm(config.q_lora_rank, eps=config.rms_norm_eps, module_path=f"{module_prefix}.q_a_norm",
-                                **kw)
-        self.kv_a_proj = None
-        if tp > 1:
-            self.q_b_proj = ColumnParallelLinear(config.q_lora_rank, self.num_heads * self.qk_head_dim, bias=False,
-                                                 module_path=f"{module_prefix}.q_b_proj", **tpkw, **kw)
+        q_out = self.num_heads * self.qk_head_dim
+        self.q_proj = self.q_a_proj = self.q_a_norm = self.q_b_proj = None
+        if config.q_lora_rank:
+            self.q_a_proj = Linear(self.hidden_size, config.q_lora_rank, bias=False,
+                                   module_path=f"{module_prefix}.q_a_proj", **kw)
+            self.q_a_norm = RMSNorm(config.q_lora_rank, eps=config.rms_norm_eps,
+                                    module_path=f"{module_prefix}.q_a_norm", **kw)
+            if tp > 1:
+                self.q_b_proj = ColumnParallelLinear(config.q_lora_rank, q_out, bias=False,
+                                                     module_path=f"{module_prefix}.q_b_proj", **tpkw, **kw)
+            else:
+                self.q_b_proj = Linear(config.q_lora_rank, q_out, bias=False, module_path=f"{module_prefix}.q_b_proj",
+                                       **kw)
+        elif tp > 1:  # no q-LoRA (DeepSeek-V2-Lite): one projection to the heads
+            self.q_proj = ColumnParallelLinear(self.hidden_size, q_out, bias=False,
+                                               module_path=f"{module_prefix}.q_proj", **tpkw, **kw)
         else:
-            self.q_b_proj = Linear(config.q_lora_rank, self.num_heads * self.qk_head_dim, bias=False,
-                                   module_path=f"{module_prefix}.q_b_proj", **kw)
+            self.q_proj = Linear(self.hidden_size, q_out, bias=False, module_path=f"{module_prefix}.q_proj", **kw)
+        self.kv_a_proj = None
         self.kv_a_proj = Linear(self.hidden_size, config.kv_lora_rank + self.qk_rope_head_dim, bias=False,
                                 module_path=f"{module_prefix}.kv_a_proj", **kw)
         self.kv_a_norm = RMSNorm(config.kv_lora_rank, eps=config.rms_norm_eps, module_path=f"{module_prefix}.kv_a_norm",
@@ -329,7 +337,8 @@ class MultiHeadLatentAttention(nn.Module):
     def _qkv(self, x: torch.Tensor):
         B, S, _ = x.shape
         h = self.local_num_heads
-        q = self.q_b_proj(self.q_a_norm(self.q_a_proj(x))).view(B, S, h, self.qk_head_dim)
+        q = self.q_proj(x) if self.q_proj is not None else self.q_b_proj(self.q_a_norm(self.q_a_proj(x)))
+        q = q.view(B, S, h, self.qk_head_dim)
         kv_a = self.kv_a_proj(x)
         kv_latent, k_rope = torch.split(kv_a, [self.kv_a_norm.weight.shape[0], self.qk_rope_head_dim], dim=-1)
         kv = self.kv_b_proj(self.kv_a_norm(kv_latent)).view(B, S, h, self.qk_nope_head_dim + self.v_head_dim)

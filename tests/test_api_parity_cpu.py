@@ -183,3 +183,28 @@ def test_moe_payload_quantisation_follows_the_recipe():
     assert y.shape == x.shape and y.dtype == x.dtype
     y.sum().backward()
     assert x.grad is not None
+
+
+def test_mla_without_q_lora_projects_q_directly():
+    from nano_train_b200.models.deepseek import DeepSeekModel, DeepSeekModelConfig
+
+    def cfg(q_lora):
+        return DeepSeekModelConfig(param_dtype=torch.float32, param_device=None, precision_resolver=_resolver(),
+                                   vocab_size=97, hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                                   num_key_value_heads=4, intermediate_size=128, q_lora_rank=q_lora, kv_lora_rank=16,
+                                   qk_nope_head_dim=8, qk_rope_head_dim=8, v_head_dim=8, moe_intermediate_size=32,
+                                   n_routed_experts=4, num_experts_per_tok=2, n_group=1, topk_group=1,
+                                   max_position_embeddings=32)
+
+    torch.manual_seed(0)
+    m = DeepSeekModel(cfg(None))
+    names = set(dict(m.named_parameters()))
+    assert "blocks.0.attn.q_proj.weight" in names and not any("q_a_proj" in n for n in names)
+    assert tuple(m.blocks[0].attn.q_proj.weight.shape) == (4 * 16, 64)
+    ids = torch.randint(0, 97, (2, 9))
+    logits = m(ids)
+    assert logits.shape == (2, 9, 97) and torch.isfinite(logits).all()
+    logits.float().mean().backward()
+    assert m.blocks[0].attn.q_proj.weight.grad is not None
+    with_lora = DeepSeekModel(cfg(24))
+    assert "blocks.0.attn.q_a_proj.weight" in dict(with_lora.named_parameters())
