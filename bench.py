@@ -415,6 +415,9 @@ def main():
         else:
             ms, layers, launches, clocks, e2e, fused_paths = run_ours(args, rank, local, world)
         tokens = tokens_per_step(args, world)
+        ref_ep_same_batch = args.impl == "reference" and args.config == "dsv2lite-fp8-ep" and world > 1
+        if ref_ep_same_batch:  # reference: EP = N with DP = 1, every rank on the same batch
+            tokens = CONFIGS[args.config]["batch_per_rank"] * args.seq
         value = tokens / (ms / 1e3)
         cfg = CONFIGS[args.config]
         dp_run = bool(cfg["batch_per_rank"])
@@ -442,10 +445,13 @@ def main():
                     "name": args.config,
                     "model": cfg["model"],
                     "layers": layers,
-                    "global_batch": cfg["batch_per_rank"] * world if dp_run else GLOBAL_BATCH,
+                    "global_batch": (cfg["batch_per_rank"] if ref_ep_same_batch else cfg["batch_per_rank"] * world)
+                                    if dp_run else GLOBAL_BATCH,
                     "micro_batch": cfg["batch_per_rank"] if dp_run else MICRO_BATCH,
                     "seq_len": args.seq,
-                    "parallelism": (f"ep{world}+dp{world}" if args.config == "dsv2lite-fp8-ep" else
+                    "parallelism": (f"ep{world}+dp1 (the reference cannot fold EP into DP; tokens counted once)"
+                                    if ref_ep_same_batch else
+                                    f"ep{world}+dp{world}" if args.config == "dsv2lite-fp8-ep" else
                                     f"dp{world}" + ("+zero1" if world > 1 else "")) if dp_run else
                                    (f"tp{world}" + ("+sp" if world > 1 else "")),
                     "optimizer": "AdamW fp32 master/moments, bf16 params, fp32 main grads, clip 1.0",

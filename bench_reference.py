@@ -187,22 +187,17 @@ def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks
     """The DeepSeek-V2-Lite-shape fp8 configuration through the reference's own public API:
     ``src.models.deepseek.DeepSeekModel`` built from its config under the reference's
     ``resolve_precision_config`` with the deepseek_v3 recipe on its stock (emulated) fp8 backend,
-    its router aux losses, ``PrecisionAdamW`` with fp32 main weights and moments. One GPU (EP = 1):
-    the reference cannot fold EP into DP. ``dims`` shrinks the model for a CPU check of this code."""
+    its router aux losses, ``PrecisionAdamW`` with fp32 main weights and moments. With N ranks it runs
+    EP = N and DP = 1 (the reference cannot fold EP into DP): every rank trains on the same batch, so the
+    tokens of a step are one batch. ``dims`` shrinks the model for a CPU check of this code."""
     ref = _import_reference()
     if ref is None:
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}), flush=True)
         return None
-    if world > 1:
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "config": args.config, "unavailable":
-                              "the reference rejects EP folded into DP (EP = N forces DP = 1); measured at N = 1"}),
-                  flush=True)
-        return None
     import argparse as _ap
 
-    from src.models.deepseek import DeepSeekModel, DeepSeekModelConfig
+    from src.models.deepseek import DeepSeekModel, DeepSeekModelConfig, DeepSeekParallelContext
     from src.models.moe import ExpertParallelMoE, LocalRoutedMoE
     from src.runtime.mixed_precision import build_module_precision_resolver, resolve_precision_config
     from src.runtime.optimizer_runtime import PrecisionAdamW
@@ -219,9 +214,21 @@ def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks
              first_k_dense_replace=1, scoring_func="softmax", n_group=1, topk_group=1, norm_topk_prob=False,
              routed_scaling_factor=1.0)
     d.update(dims or {})
-    torch.manual_seed(1234)
+    pctx = None
+    if world > 1:
+        # The reference cannot fold EP into DP: EP = N forces DP = 1, so every rank runs the same batch
+        # (the caller counts its tokens once) and dense gradients need no reduction.
+        from src.distributed.topology import initialize_model_parallel
+
+        par = initialize_model_parallel(tensor_model_parallel_size=1, pipeline_model_parallel_size=1,
+                                        expert_model_parallel_size=world)
+        pctx = DeepSeekParallelContext(expert_model_parallel_rank=par.expert_model_parallel_rank,
+                                       expert_model_parallel_size=world,
+                                       expert_model_parallel_group=par.expert_model_parallel_group)
+    torch.manual_seed(1234)  # the same on every rank: identical dense weights
     dt = torch.bfloat16 if dev.type == "cuda" else torch.float32
-    model = DeepSeekModel(DeepSeekModelConfig(param_dtype=dt, param_device=dev, precision_resolver=res, **d))
+    model = DeepSeekModel(DeepSeekModelConfig(param_dtype=dt, param_device=dev, precision_resolver=res, **d),
+                          parallel_context=pctx)
     with torch.no_grad():
         for p in model.parameters():
             if p.dim() >= 2:
@@ -242,7 +249,7 @@ def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks
         opt.step()
         return loss.detach()
 
-    batches = make_batches(2, args.seq, d["vocab_size"], batch=batch)
+    batches = make_batches(2, args.seq, d["vocab_size"], batch=batch)  # same seed on every rank: one batch
     for i in range(args.warmup):
         step(*batches[i % len(batches)])
     if dev.type != "cuda":
@@ -259,14 +266,15 @@ def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks
     e.record()
     barrier(world)
     sampler.stop()
-    ms = s.elapsed_time(e) / args.steps
+    ms = max_over_ranks(s.elapsed_time(e) / args.steps, world)
     e2e = None
     if not args.no_e2e:
+        barrier(world)
         t0 = time.perf_counter()
         for i in range(args.steps):
             float(step(*batches[i % len(batches)]))
-        torch.cuda.synchronize()
-        e2e_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+        barrier(world)
+        e2e_ms = max_over_ranks((time.perf_counter() - t0) * 1e3 / args.steps, world)
         e2e = {"value": batch * args.seq / (e2e_ms / 1e3), "unit": "tokens/s", "ms_per_step": e2e_ms,
                "h2d_bytes_per_step": 2 * batch * args.seq * 8, "d2h_bytes_per_step": 4,
                "api": "src.models.deepseek.DeepSeekModel + PrecisionAdamW (deepseek_v3 recipe, emulated fp8)"}
