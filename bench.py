@@ -186,7 +186,7 @@ def build_gpt_fp4(args, rank, world):
     return trainer, layers
 
 
-def build_dsv2lite(args, rank, world):
+def build_dsv2lite(args, rank, world, *, device=None, dims=None):
     """DeepSeek-V2-Lite shape, fp8 recipe on the native backend, EP = world folded inside DP = world
     (dense parameters replicated and ZeRO-1 sharded over the world; expert parameters unique per rank)."""
     sys.path.insert(0, ROOT)
@@ -198,8 +198,10 @@ def build_dsv2lite(args, rank, world):
                                                            resolve_precision_config)
 
     layers = args.layers or (8 if world == 1 else 27)
+    dev = torch.device(device or "cuda")
+    pdt = torch.bfloat16 if dev.type == "cuda" else torch.float32
     pc = resolve_precision_config(argparse.Namespace(precision_recipe="deepseek_v3", fp8=True, fp8_backend="native",
-                                                     params_dtype="bf16"), torch.device("cuda"))
+                                                     params_dtype="bf16" if dev.type == "cuda" else "fp32"), dev)
     resolver = build_module_precision_resolver(pc)
     ep_group, ep_rank = None, 0
     if world > 1:
@@ -208,15 +210,15 @@ def build_dsv2lite(args, rank, world):
                                         expert_layout="fold_dp")
         ep_group, ep_rank = par.expert_model_parallel_group, par.expert_model_parallel_rank
     torch.manual_seed(1234 + rank)  # experts differ per rank; dense weights are broadcast below
-    cfg = DeepSeekModelConfig(param_dtype=torch.bfloat16, param_device=torch.device("cuda"),
-                              precision_resolver=resolver, vocab_size=102400, hidden_size=2048,
-                              num_hidden_layers=layers, num_attention_heads=16, num_key_value_heads=16,
-                              intermediate_size=10944, max_position_embeddings=4096, q_lora_rank=1536,
-                              kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
-                              moe_intermediate_size=1408, n_routed_experts=64, n_shared_experts=2,
-                              num_experts_per_tok=6, first_k_dense_replace=1, scoring_func="softmax", n_group=1,
-                              topk_group=1, norm_topk_prob=False, routed_scaling_factor=1.0,
-                              comm_quant_backend="native")
+    shape = dict(vocab_size=102400, hidden_size=2048, num_hidden_layers=layers, num_attention_heads=16,
+                 num_key_value_heads=16, intermediate_size=10944, max_position_embeddings=4096, q_lora_rank=1536,
+                 kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128,
+                 moe_intermediate_size=1408, n_routed_experts=64, n_shared_experts=2, num_experts_per_tok=6,
+                 first_k_dense_replace=1, scoring_func="softmax", n_group=1, topk_group=1, norm_topk_prob=False,
+                 routed_scaling_factor=1.0)
+    shape.update(dims or {})
+    cfg = DeepSeekModelConfig(param_dtype=pdt, param_device=dev, precision_resolver=resolver,
+                              comm_quant_backend="native", **shape)
     pctx = DeepSeekParallelContext(expert_model_parallel_rank=ep_rank,
                                    expert_model_parallel_size=world, expert_model_parallel_group=ep_group)
     model = DeepSeekModel(cfg, parallel_context=pctx)
@@ -241,24 +243,24 @@ def build_dsv2lite(args, rank, world):
     if experts:
         opts.append(FlatAdamW(split_decay_groups(_Params(experts), 0.1), lr=3e-4, weight_decay=0.1,
                               max_grad_norm=1.0))
-    return _MoETrainer(model, opts), layers
+    return _MoETrainer(model, opts, dev), layers
 
 
 class _MoETrainer:
     """One step: forward, fused cross-entropy + 0.01 x router aux loss, backward, both optimizers
     (dense over the DP group, experts local). The loss stays on the device."""
 
-    def __init__(self, model, opts):
+    def __init__(self, model, opts, device):
         from nano_train_b200.models.moe import ExpertParallelMoE, LocalRoutedMoE
 
-        self.model, self.opts = model, opts
+        self.model, self.opts, self.device = model, opts, device
         self.moes = [m for m in model.modules() if isinstance(m, (ExpertParallelMoE, LocalRoutedMoE))]
 
     def train_step(self, input_ids, labels):
         from nano_train_b200 import ops
 
-        ids = input_ids.to("cuda", non_blocking=True)
-        lab = labels.to("cuda", non_blocking=True)
+        ids = input_ids.to(self.device, non_blocking=True)
+        lab = labels.to(self.device, non_blocking=True)
         for o in self.opts:
             o.zero_grad()
         logits = self.model(ids)

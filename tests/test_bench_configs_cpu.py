@@ -1,0 +1,70 @@
+"""The multi-rank logic of bench.py's DeepSeek-V2-Lite fp8 configuration on CPU (gloo, 2 ranks, tiny
+dimensions): EP folded inside DP (every rank its own batch), dense parameters replicated and sharded by
+ZeRO-1 over the world, expert parameters local to their rank."""
+import os
+import sys
+
+import torch
+import torch.multiprocessing as mp
+
+from conftest import ROOT, free_port
+
+DIMS = dict(vocab_size=128, hidden_size=64, num_attention_heads=4, num_key_value_heads=4, intermediate_size=128,
+            q_lora_rank=32, kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=8, v_head_dim=8,
+            moe_intermediate_size=32, n_routed_experts=4, num_experts_per_tok=2, n_shared_experts=1,
+            max_position_embeddings=64)
+
+
+def _worker(rank, world, port, q):
+    try:
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port))
+        sys.path.insert(0, ROOT)
+        import argparse
+
+        import torch.distributed as dist
+
+        import bench
+
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        args = argparse.Namespace(layers=2)
+        trainer, _ = bench.build_dsv2lite(args, rank, world, device="cpu", dims=DIMS)
+        g = torch.Generator().manual_seed(rank)
+        losses = []
+        for _ in range(2):
+            ids = torch.randint(0, 128, (2, 17), generator=g)
+            losses.append(float(trainer.train_step(ids[:, :-1], ids[:, 1:])))
+        model = trainer.model
+        dense = [p.detach().clone() for p in model.parameters() if not getattr(p, "expert_model_parallel", False)]
+        expert = [p.detach().clone() for p in model.parameters() if getattr(p, "expert_model_parallel", False)]
+        same = True
+        for t in dense:
+            other = [torch.zeros_like(t) for _ in range(world)]
+            dist.all_gather(other, t)
+            same = same and all(torch.equal(other[0], o) for o in other)
+        ex = [torch.zeros_like(expert[0]) for _ in range(world)]
+        dist.all_gather(ex, expert[0])
+        q.put((rank, losses, same, not torch.equal(ex[0], ex[1]), len(expert) > 0, None))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        import traceback
+
+        q.put((rank, None, None, None, None, traceback.format_exc()))
+
+
+def test_dsv2lite_ep_inside_dp_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    for rank, losses, same, experts_differ, has_experts, err in res:
+        assert err is None, f"rank {rank}:\n{err}"
+        assert all(l == l and 0 < l < 20 for l in losses)
+        assert same, "dense parameters diverged across ranks"
+        assert has_experts and experts_differ, "expert parameters should be local to each rank"
+    assert res[0][1] != res[1][1]  # each rank trains on its own batch
