@@ -162,7 +162,7 @@ def make_batches(n, seq, vocab, seed=0, batch=GLOBAL_BATCH):
 
 
 # ---------------------------------------------------------------- our framework
-def build_gpt_fp4(args, rank, world):
+def build_gpt_fp4(args, rank, world, *, device=None, dims=None):
     """GPT-1.3B shape with NVFP4 linears, DP = world with ZeRO-1 (sharded fp32 master / moments)."""
     sys.path.insert(0, ROOT)
     from nano_train_b200.models.transformer import TransformerModel, gpt_1p3b_config
@@ -172,12 +172,14 @@ def build_gpt_fp4(args, rank, world):
     from nano_train_b200.training import LMTrainer
 
     layers = args.layers or 24
-    pc = resolve_precision_config(argparse.Namespace(fp4=True, fp4_backend="native", params_dtype="bf16"),
-                                  torch.device("cuda"))
+    dev = torch.device(device or "cuda")
+    pc = resolve_precision_config(argparse.Namespace(fp4=True, fp4_backend="native",
+                                                     params_dtype="bf16" if dev.type == "cuda" else "fp32"), dev)
     resolver = build_module_precision_resolver(pc)
     torch.manual_seed(1234)  # identical initial weights on every DP rank
-    model = TransformerModel(gpt_1p3b_config(num_layers=layers, param_device=torch.device("cuda"),
-                                             precision_resolver=resolver))
+    model = TransformerModel(gpt_1p3b_config(num_layers=layers, param_device=dev, precision_resolver=resolver,
+                                             param_dtype=torch.bfloat16 if dev.type == "cuda" else torch.float32,
+                                             **(dims or {})))
     finalize_module_precision_resolver(resolver)
     dp = dist.group.WORLD if world > 1 else None
     trainer = LMTrainer(model, lr=3e-4, weight_decay=0.1, max_grad_norm=1.0,

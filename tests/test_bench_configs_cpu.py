@@ -1,6 +1,7 @@
-"""The multi-rank logic of bench.py's DeepSeek-V2-Lite fp8 configuration on CPU (gloo, 2 ranks, tiny
+"""The multi-rank logic of bench.py's DeepSeek-V2-Lite fp8 and GPT-1.3B fp4 configurations on CPU (gloo, 2 ranks, tiny
 dimensions): EP folded inside DP (every rank its own batch), dense parameters replicated and sharded by
-ZeRO-1 over the world, expert parameters local to their rank."""
+ZeRO-1 over the world, expert parameters local to their rank; for the GPT config, DP replicas kept
+identical by the ZeRO-1 step while each rank trains on its own batch."""
 import os
 import sys
 
@@ -68,3 +69,53 @@ def test_dsv2lite_ep_inside_dp_two_ranks():
         assert same, "dense parameters diverged across ranks"
         assert has_experts and experts_differ, "expert parameters should be local to each rank"
     assert res[0][1] != res[1][1]  # each rank trains on its own batch
+
+
+def _gpt_worker(rank, world, port, q):
+    try:
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port))
+        sys.path.insert(0, ROOT)
+        import argparse
+
+        import torch.distributed as dist
+
+        import bench
+
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        trainer, _ = bench.build_gpt_fp4(argparse.Namespace(layers=2), rank, world, device="cpu",
+                                         dims=dict(hidden_size=64, num_attention_heads=4, intermediate_size=128,
+                                                   vocab_size=128, max_position_embeddings=32))
+        g = torch.Generator().manual_seed(rank)
+        losses = []
+        for _ in range(2):
+            ids = torch.randint(0, 128, (2, 17), generator=g)
+            losses.append(float(trainer.train_step(ids[:, :-1], ids[:, 1:])))
+        same = True
+        for p in trainer.model.parameters():
+            other = [torch.zeros_like(p) for _ in range(world)]
+            dist.all_gather(other, p.detach().contiguous())
+            same = same and torch.equal(other[0], other[1])
+        q.put((rank, losses, same, None))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        import traceback
+
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def test_gpt_fp4_dp_zero1_two_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_gpt_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    for rank, losses, same, err in res:
+        assert err is None, f"rank {rank}:\n{err}"
+        assert all(l == l and 0 < l < 20 for l in losses)
+        assert same, "DP replicas diverged"
+    assert res[0][1] != res[1][1]
