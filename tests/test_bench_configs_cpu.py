@@ -1,7 +1,7 @@
-"""The multi-rank logic of bench.py's DeepSeek-V2-Lite fp8 and GPT-1.3B fp4 configurations on CPU (gloo, 2 ranks, tiny
-dimensions): EP folded inside DP (every rank its own batch), dense parameters replicated and sharded by
-ZeRO-1 over the world, expert parameters local to their rank; for the GPT config, DP replicas kept
-identical by the ZeRO-1 step while each rank trains on its own batch."""
+"""The multi-rank logic of bench.py's DeepSeek-V2-Lite fp8 and GPT-1.3B fp4 configurations on CPU
+(gloo, 2 ranks, tiny dimensions). DeepSeek: EP folded inside DP (every rank its own batch), dense
+parameters replicated and sharded by ZeRO-1 over the world, expert parameters local to their rank.
+GPT: DP replicas kept identical by the ZeRO-1 step while each rank trains on its own batch."""
 import os
 import sys
 
