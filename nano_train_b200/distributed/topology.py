@@ -69,13 +69,16 @@ class ModelParallelTopology:
     def rank_from_coords(self, data_parallel_rank: int, pipeline_model_parallel_rank: int,
                          tensor_model_parallel_rank: int, expert_model_parallel_rank: int,
                          context_parallel_rank: int = 0) -> int:
+        """Global rank of a coordinate. With ``expert_layout="fold_dp"`` the rank grid has no EP axis
+        (the EP rank is ``data_parallel_rank % EP``), so the expert rank argument is not used."""
+        fold = self.expert_layout == "fold_dp"
         return rank_from_coords(data_parallel_rank=data_parallel_rank,
                                 pipeline_model_parallel_rank=pipeline_model_parallel_rank,
                                 tensor_model_parallel_rank=tensor_model_parallel_rank,
-                                expert_model_parallel_rank=expert_model_parallel_rank,
+                                expert_model_parallel_rank=0 if fold else expert_model_parallel_rank,
                                 pipeline_model_parallel_size=self.pipeline_model_parallel_size,
                                 tensor_model_parallel_size=self.tensor_model_parallel_size,
-                                expert_model_parallel_size=self.expert_model_parallel_size,
+                                expert_model_parallel_size=1 if fold else self.expert_model_parallel_size,
                                 context_parallel_rank=context_parallel_rank,
                                 context_parallel_size=self.context_parallel_size)
 

@@ -72,6 +72,23 @@ def test_fold_dp_layout(monkeypatch):
     assert [3, 7] in t.expert_data_parallel_group_table
 
 
+def test_fold_dp_rank_from_coords_round_trips_with_tp_and_pp(monkeypatch):
+    """With EP inside DP the rank grid has no EP axis: every rank's own coordinates map back to it, and
+    the broadcast sources of its replica groups (dp = 0) and its pipeline peers are members of them."""
+    for r in range(8):
+        t = _make(monkeypatch, 8, r, tensor_model_parallel_size=2, pipeline_model_parallel_size=2,
+                  expert_model_parallel_size=2, expert_layout="fold_dp")
+        me = t.rank_from_coords(t.data_parallel_rank, t.pipeline_model_parallel_rank, t.tensor_model_parallel_rank,
+                                t.expert_model_parallel_rank, t.context_parallel_rank)
+        assert me == r
+        assert t.expert_model_parallel_rank == t.data_parallel_rank % 2
+        src = t.rank_from_coords(0, t.pipeline_model_parallel_rank, t.tensor_model_parallel_rank, 0)
+        assert any(src in g and r in g for g in t.data_parallel_group_table)
+        other = t.rank_from_coords(t.data_parallel_rank, 1 - t.pipeline_model_parallel_rank,
+                                   t.tensor_model_parallel_rank, t.expert_model_parallel_rank)
+        assert any(other in g and r in g for g in t.pipeline_model_parallel_group_table)
+
+
 def test_world_not_divisible(monkeypatch):
     with pytest.raises(ValueError, match="divisible"):
         _make(monkeypatch, 6, 0, tensor_model_parallel_size=4, pipeline_model_parallel_size=1,

@@ -62,3 +62,16 @@ def test_train_4d_resume_is_exact(tmp_path, layout):
     assert sorted(resumed) == [3, 4, 5], out[-2000:]
     for s in (3, 4, 5):
         assert abs(resumed[s] - full[s]) < 1e-6 * max(1.0, abs(full[s])), (s, resumed[s], full[s])
+
+
+def test_train_4d_full_4d_layout_eight_ranks():
+    """BASELINE config #4's layout at toy size: TP2 x PP2 x DP2 with EP2 folded inside DP, ZeRO-2, 1F1B
+    with 8 microbatches, on 8 gloo ranks."""
+    out, steps = _run(["--tensor-model-parallel-size", "2", "--pipeline-model-parallel-size", "2",
+                       "--expert-model-parallel-size", "2", "--expert-layout", "fold_dp", "--use-distributed-optimizer",
+                       "--data-parallel-sharding-strategy", "optim_grads", "--num_microbatches", "8",
+                       "--num_experts", "16", "--max_steps", "2"], world=8, timeout=600)
+    assert "Training completed" in out
+    assert sorted(steps) == [0, 1]
+    assert all(v == v and abs(v) < 100 for v in steps.values())
+
