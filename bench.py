@@ -47,6 +47,10 @@ MICRO_BATCH = 1
 #   gpt1.3b-fp4-dp: GPT-1.3B shape (H 2048, 24 layers, 16 heads, GELU 8192, vocab 50304), NVFP4
 #   linears (e2m1 operands in 1x16 blocks with e4m3 scales on the fp4 tensor cores, bf16 params,
 #   fp32 master / moments), DP = N with ZeRO-1, seq 2048, micro-batch 8 per rank (weak scaling).
+#   deepseek-4d: the full 4-D runtime on 8 GPUs, TP2 x PP2 x DP2 with EP2 folded inside DP, ZeRO-2,
+#   1F1B with 8 microbatches of 1 x 2048 tokens per data-parallel replica, bf16 params with fp32 main
+#   grads / master / moments; driven through the train_4d runtime components (bootstrap, model provider,
+#   optimizer runtime, pipeline schedule). Needs exactly 8 ranks.
 #   dsv2lite-fp8-ep: DeepSeek-V2-Lite shape under the deepseek_v3 fp8 recipe (1x128 activation and
 #   128x128 weight e4m3 scales, stochastic rounding, e4m3 MoE payload), EP = N folded inside DP = N
 #   (every rank its own batch), seq 4096, micro-batch 2 per rank; 27 layers for N > 1 and 8 (1 dense
@@ -56,6 +60,9 @@ CONFIGS = {
     "llama8b-tp": dict(model=MODEL_NAME, seq=SEQ, batch_per_rank=None, vocab=128256),
     "gpt1.3b-fp4-dp": dict(model="GPT-1.3B-shape dense TransformerModel (H2048, 24 layers, 16 heads, GELU 8192, "
                                  "vocab 50304), NVFP4 linears", seq=2048, batch_per_rank=8, vocab=50304),
+    "deepseek-4d": dict(model="DeepSeekModel (H4096, 16 layers, MLA 32 heads with q-LoRA 1536 / kv-LoRA 512, 16 "
+                              "routed experts top-2 + 1 shared, expert FFN 4096 SwiGLU, vocab 32000), 4-D runtime",
+                        seq=2048, batch_per_rank=8, vocab=32000),
     "dsv2lite-fp8-ep": dict(model="DeepSeek-V2-Lite-shape MoE DeepSeekModel (H2048, MLA 16 heads kv_lora 512 "
                                   "q-LoRA 1536 nope 128 rope 64 v 128, first layer dense FFN 10944, 64 routed experts "
                                   "top-6 + 2 shared, expert FFN 1408, vocab 102400), deepseek_v3 fp8 recipe",
@@ -188,6 +195,53 @@ def build_gpt_fp4(args, rank, world, *, device=None, dims=None):
     return trainer, layers
 
 
+def build_4d(args, rank, world, *, dims=None):
+    """The 4-D runtime of examples/train_4d.py, one step per ``train_step`` call."""
+    sys.path.insert(0, ROOT)
+    from nano_train_b200.runtime import train4d as T
+    from nano_train_b200.runtime.context import TrainState
+    from nano_train_b200.runtime.contracts import StepContext
+
+    if world != 8:
+        raise SystemExit("deepseek-4d needs 8 ranks (TP2 x PP2 x DP2 with EP2 inside DP)")
+    shape = dict(hidden_size=4096, num_layers=args.layers or 16, num_heads=32, num_kv_heads=32,
+                 intermediate_size=4096, moe_intermediate_size=4096, num_experts=16, top_k=2, n_shared_experts=1,
+                 vocab_size=32000, q_lora_rank=1536, kv_lora_rank=512, qk_nope_head_dim=128, qk_rope_head_dim=64,
+                 v_head_dim=128, seq_len=args.seq, batch_size=CONFIGS["deepseek-4d"]["batch_per_rank"])
+    shape.update(dims or {})
+    flags = ["--tensor-model-parallel-size", "2", "--pipeline-model-parallel-size", "2",
+             "--expert-model-parallel-size", "2", "--expert-layout", "fold_dp", "--use-distributed-optimizer",
+             "--data-parallel-sharding-strategy", "optim_grads", "--num_microbatches", "8", "--seed", "1234",
+             "--max_position_embeddings", str(shape["seq_len"])]
+    flags += ["--bf16"] if torch.cuda.is_available() else []
+    for k, v in shape.items():
+        flags += [f"--{k}", str(v)]
+    targs = T.parse_args(flags)
+    comps = T.build_train_4d_components()
+    ctx = comps.bootstrap.build_context(targs)
+    model = comps.model_provider.build_model(ctx)
+    opt = comps.optimizer_runtime.initialize(model, ctx)
+    sched = comps.schedule_selector.select(ctx)
+
+    class _Stepper:
+        dp_rank = ctx.parallel.data_parallel_rank
+        dp_size = ctx.parallel.data_parallel_size
+
+        def __init__(self):
+            self.state = TrainState()
+            self.first = bool(getattr(model, "is_first_pp_stage", True))
+
+        def train_step(self, input_ids, labels):
+            # train_4d batches are token sequences; the schedule shifts them into inputs and labels itself
+            ids = input_ids.to(ctx.parallel.device, non_blocking=True)
+            out = sched.run_step(StepContext(model=model, batch={"input_ids": ids} if self.first else None,
+                                             optimizer_state=opt, runtime_context=ctx, train_state=self.state))
+            self.state.global_step += 1
+            return torch.tensor(out.total_loss / max(1, out.counters.get("objective_count", 1)))
+
+    return _Stepper(), shape["num_layers"]
+
+
 def build_dsv2lite(args, rank, world, *, device=None, dims=None):
     """DeepSeek-V2-Lite shape, fp8 recipe on the native backend, EP = world folded inside DP = world
     (dense parameters replicated and ZeRO-1 sharded over the world; expert parameters unique per rank)."""
@@ -284,6 +338,8 @@ def build_ours(args, rank, world):
         return build_gpt_fp4(args, rank, world)
     if args.config == "dsv2lite-fp8-ep":
         return build_dsv2lite(args, rank, world)
+    if args.config == "deepseek-4d":
+        return build_4d(args, rank, world)
 
     layers = args.layers or (8 if world == 1 else 32)
     tp = world
@@ -305,7 +361,9 @@ def run_ours(args, rank, local, world):
 
     trainer, layers = build_ours(args, rank, world)
     cfg = CONFIGS[args.config]
-    if cfg["batch_per_rank"]:
+    if args.config == "deepseek-4d":  # one batch per data-parallel replica, shared by its TP / PP ranks
+        batches = make_batches(4, args.seq, cfg["vocab"], seed=trainer.dp_rank, batch=cfg["batch_per_rank"])
+    elif cfg["batch_per_rank"]:
         batches = make_batches(4, args.seq, cfg["vocab"], seed=rank, batch=cfg["batch_per_rank"])
     else:
         batches = make_batches(4, args.seq, cfg["vocab"])
@@ -365,6 +423,8 @@ def run_ours(args, rank, local, world):
 def tokens_per_step(args, world):
     """Whole-job tokens per step: TP ranks share one batch; DP ranks each run their own."""
     per_rank = CONFIGS[args.config]["batch_per_rank"]
+    if args.config == "deepseek-4d":  # 8 microbatches per data-parallel replica, DP = world / (TP x PP) = 2
+        return per_rank * (world // 4) * args.seq
     return (per_rank * world if per_rank else GLOBAL_BATCH) * args.seq
 
 
@@ -449,11 +509,13 @@ def main():
                     "name": args.config,
                     "model": cfg["model"],
                     "layers": layers,
-                    "global_batch": (cfg["batch_per_rank"] if ref_ep_same_batch else cfg["batch_per_rank"] * world)
+                    "global_batch": tokens_per_step(args, world) // args.seq if args.config == "deepseek-4d" else
+                                    (cfg["batch_per_rank"] if ref_ep_same_batch else cfg["batch_per_rank"] * world)
                                     if dp_run else GLOBAL_BATCH,
                     "micro_batch": cfg["batch_per_rank"] if dp_run else MICRO_BATCH,
                     "seq_len": args.seq,
-                    "parallelism": (f"ep{world}+dp1 (the reference cannot fold EP into DP; tokens counted once)"
+                    "parallelism": ("tp2 x pp2 x dp2, ep2 inside dp, zero2, 1f1b x8" if args.config == "deepseek-4d"
+                                    else f"ep{world}+dp1 (the reference cannot fold EP into DP; tokens counted once)"
                                     if ref_ep_same_batch else
                                     f"ep{world}+dp{world}" if args.config == "dsv2lite-fp8-ep" else
                                     f"dp{world}" + ("+zero1" if world > 1 else "")) if dp_run else

@@ -1,7 +1,8 @@
 """The multi-rank logic of bench.py's DeepSeek-V2-Lite fp8 and GPT-1.3B fp4 configurations on CPU
 (gloo, 2 ranks, tiny dimensions). DeepSeek: EP folded inside DP (every rank its own batch), dense
 parameters replicated and sharded by ZeRO-1 over the world, expert parameters local to their rank.
-GPT: DP replicas kept identical by the ZeRO-1 step while each rank trains on its own batch."""
+GPT: DP replicas kept identical by the ZeRO-1 step while each rank trains on its own batch. 4-D: the
+train_4d runtime components stepped by bench.py on 8 ranks (TP2 x PP2 x DP2, EP2 inside DP, ZeRO-2, 1F1B)."""
 import os
 import sys
 
@@ -119,3 +120,47 @@ def test_gpt_fp4_dp_zero1_two_ranks():
         assert all(l == l and 0 < l < 20 for l in losses)
         assert same, "DP replicas diverged"
     assert res[0][1] != res[1][1]
+
+
+def _4d_worker(rank, world, port, q):
+    try:
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port), OMP_NUM_THREADS="1")
+        sys.path.insert(0, ROOT)
+        import argparse
+
+        import torch.distributed as dist
+
+        import bench
+
+        stepper, _ = bench.build_4d(argparse.Namespace(layers=4, seq=16), rank, world,
+                                    dims=dict(hidden_size=64, num_heads=4, num_kv_heads=4, intermediate_size=128,
+                                              moe_intermediate_size=64, vocab_size=128, q_lora_rank=32,
+                                              kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=8,
+                                              v_head_dim=8))
+        g = torch.Generator().manual_seed(stepper.dp_rank)
+        losses = []
+        for _ in range(2):
+            ids = torch.randint(0, 128, (8, 17), generator=g)
+            losses.append(float(stepper.train_step(ids[:, :-1], ids[:, 1:])))
+        q.put((rank, losses, stepper.dp_size, None))
+        dist.destroy_process_group()
+    except Exception:  # pragma: no cover - reported to the parent
+        import traceback
+
+        q.put((rank, None, None, traceback.format_exc()))
+
+
+def test_deepseek_4d_config_eight_ranks():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_4d_worker, args=(r, 8, port, q)) for r in range(8)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=600) for _ in ps)
+    for p in ps:
+        p.join(timeout=60)
+    for rank, losses, dp, err in res:
+        assert err is None, f"rank {rank}:\n{err}"
+        assert dp == 2 and all(l == l and abs(l) < 100 for l in losses)
