@@ -68,9 +68,14 @@ class _StackCache:
         key = (bool(fp8),) + tuple((p.data_ptr(), p._version) for p in params)
         if key != self.key:
             with torch.no_grad():
-                q = (lambda w: ext().fp8_quant_dequant(w.contiguous(), 128, False, 0)) if fp8 else (lambda w: w)
-                self.w1 = torch.cat([torch.cat([q(e.gate_proj.weight), q(e.up_proj.weight)], 0) for e in experts], 0)
-                self.w2 = torch.cat([q(e.down_proj.weight) for e in experts], 0)
+                self.w1 = torch.cat([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in experts], 0)
+                self.w2 = torch.cat([e.down_proj.weight for e in experts], 0)
+                if fp8:
+                    # One launch per stack: every expert matrix has a multiple of 128 rows (the fp8 grouped
+                    # path requires H % 128 == 0 and I % 128 == 0), so no 128 x 128 block spans two matrices
+                    # and the result equals rounding each matrix on its own.
+                    self.w1 = ext().fp8_quant_dequant(self.w1, 128, False, 0)
+                    self.w2 = ext().fp8_quant_dequant(self.w2, 128, False, 0)
             self.key = key
         return self.w1, self.w2
 
