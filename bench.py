@@ -466,7 +466,8 @@ def main():
         elif args.impl == "reference" and args.config != "llama8b-tp":
             if rank == 0:
                 print(json.dumps({"impl": "reference", "config": args.config,
-                                  "unavailable": "the reference arm is wired for the default llama8b-tp config only"}),
+                                  "unavailable": "the reference rejects TP > 1 together with EP > 1 "
+                                                 "(src/runtime/validation.py) and cannot fold EP into DP"}),
                       flush=True)
             return
         elif args.impl == "reference":
