@@ -4,7 +4,8 @@
 
 Character-level TextDataset when ``--data`` points at a text file, seeded
 synthetic tokens otherwise. GPT-2-style TransformerModel (the reference's
-default block) in bf16 on CUDA (fp32 on CPU), fused AdamW, cosine LR,
+default block) under the shared precision flags (bf16 on CUDA and fp32 on CPU by default; --fp8 / --fp4
+with their backends, loss scaling where the mode needs it), fused AdamW, cosine LR,
 TensorBoard/JSONL metrics and checkpoints under ``--output_dir``.
 (reference: examples/train_mvp.py)
 """
@@ -16,10 +17,15 @@ import torch
 
 sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
 
-from nano_train_b200.config import Config, ModelConfig, TrainingConfig, _NoOpPrecisionResolver  # noqa: E402
+from nano_train_b200.config import Config, ModelConfig, TrainingConfig  # noqa: E402
 from nano_train_b200.dataset import SyntheticTokenDataset, TextDataset, create_dataloader  # noqa: E402
 from nano_train_b200.logging import setup_logging  # noqa: E402
 from nano_train_b200.models.transformer import TransformerModel  # noqa: E402
+from nano_train_b200.precision.mixed_precision import (MixedPrecisionController,  # noqa: E402
+                                                       build_module_precision_resolver, dtype_alias_to_torch,
+                                                       finalize_module_precision_resolver)
+from nano_train_b200.precision.precision_args import (add_mixed_precision_args,  # noqa: E402
+                                                      normalize_and_resolve_precision)
 from nano_train_b200.trainer import Trainer  # noqa: E402
 
 
@@ -35,10 +41,13 @@ def main():
     ap.add_argument("--num_heads", type=int, default=4)
     ap.add_argument("--lr", type=float, default=3e-4)
     ap.add_argument("--output_dir", default="outputs/nano_train_mvp")
+    add_mixed_precision_args(ap)  # --bf16 / --fp16 / --fp8 / --fp4, backends, recipe, per-module rules
     a = ap.parse_args()
     setup_logging()
     torch.manual_seed(a.seed)
     dev = torch.device("cuda" if torch.cuda.is_available() else "cpu")
+    pc = normalize_and_resolve_precision(a, dev)
+    resolver = build_module_precision_resolver(pc)
     if a.data and os.path.exists(a.data):
         ds = TextDataset(a.data, max_seq_length=a.seq_len + 1)
         vocab = ds.vocab_size
@@ -48,8 +57,8 @@ def main():
     n_val = max(1, len(ds) // 10)
     train_ds, val_ds = torch.utils.data.random_split(ds, [len(ds) - n_val, n_val],
                                                      generator=torch.Generator().manual_seed(a.seed))
-    mcfg = ModelConfig(param_dtype=torch.bfloat16 if dev.type == "cuda" else torch.float32, param_device=dev,
-                       precision_resolver=_NoOpPrecisionResolver(), hidden_size=a.hidden_size,
+    mcfg = ModelConfig(param_dtype=dtype_alias_to_torch(pc.params_dtype), param_device=dev,
+                       precision_resolver=resolver, hidden_size=a.hidden_size,
                        num_layers=a.num_layers, num_attention_heads=a.num_heads, intermediate_size=4 * a.hidden_size,
                        vocab_size=vocab, max_position_embeddings=max(1024, a.seq_len), dropout=0.0)
     cfg = Config(model=mcfg, training=TrainingConfig(batch_size=a.batch_size, micro_batch_size=a.batch_size,
@@ -58,8 +67,10 @@ def main():
                                                      eval_steps=max(10, a.max_steps // 4), save_steps=0),
                  output_dir=a.output_dir, log_dir=os.path.join(a.output_dir, "logs"), seed=a.seed)
     model = TransformerModel(mcfg)
+    finalize_module_precision_resolver(resolver)
     trainer = Trainer(model, cfg, create_dataloader(train_ds, a.batch_size), dev,
-                      val_loader=create_dataloader(val_ds, a.batch_size, shuffle=False))
+                      val_loader=create_dataloader(val_ds, a.batch_size, shuffle=False),
+                      precision_controller=MixedPrecisionController(pc, device=dev))
     print(trainer.train())
 
 

@@ -24,24 +24,29 @@ from nano_train_b200.distributed.topology import initialize_model_parallel  # no
 from nano_train_b200.layers import ColumnParallelLinear, Linear, RowParallelLinear  # noqa: E402
 from nano_train_b200 import ops  # noqa: E402
 from nano_train_b200.parallel.flat_optimizer import FlatAdamW  # noqa: E402
+from nano_train_b200.precision.mixed_precision import (dtype_alias_to_torch,  # noqa: E402
+                                                       finalize_module_precision_resolver,
+                                                       refresh_persistent_lowbit_params)
+from nano_train_b200.precision.precision_args import add_mixed_precision_args, build_precision_runtime  # noqa: E402
 
 
 class ParallelMLP(nn.Module):
-    def __init__(self, hidden, inter, tp_rank, tp_size, tp_group):
+    def __init__(self, hidden, inter, tp_rank, tp_size, tp_group, **kw):
         super().__init__()
-        self.fc1 = ColumnParallelLinear(hidden, inter, tp_rank, tp_size, tp_group=tp_group)
-        self.fc2 = RowParallelLinear(inter, hidden, tp_rank, tp_size, tp_group=tp_group)
+        self.fc1 = ColumnParallelLinear(hidden, inter, tp_rank, tp_size, tp_group=tp_group, module_path="mlp.fc1", **kw)
+        self.fc2 = RowParallelLinear(inter, hidden, tp_rank, tp_size, tp_group=tp_group, module_path="mlp.fc2", **kw)
 
     def forward(self, x):
         return self.fc2(ops.gelu(self.fc1(x)))
 
 
 class TutorialModel(nn.Module):
-    def __init__(self, input_size, hidden, inter, tp_rank, tp_size, tp_group):
+    def __init__(self, input_size, hidden, inter, tp_rank, tp_size, tp_group, **kw):
+        """``kw``: param_dtype / param_device / precision_resolver of every layer."""
         super().__init__()
-        self.inp = Linear(input_size, hidden)
-        self.mlp = ParallelMLP(hidden, inter, tp_rank, tp_size, tp_group)
-        self.out = Linear(hidden, 1)
+        self.inp = Linear(input_size, hidden, module_path="inp", **kw)
+        self.mlp = ParallelMLP(hidden, inter, tp_rank, tp_size, tp_group, **kw)
+        self.out = Linear(hidden, 1, module_path="out", **kw)
 
     def forward(self, x):
         return self.out(self.mlp(ops.gelu(self.inp(x))))
@@ -62,6 +67,7 @@ def main():
     ap.add_argument("--intermediate_size", type=int, default=1024)
     ap.add_argument("--seed", type=int, default=42)
     ap.add_argument("--log_every", type=int, default=10)
+    add_mixed_precision_args(ap)
     a = ap.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     tp = a.tensor_model_parallel_size or a.tp_size or world
@@ -69,7 +75,11 @@ def main():
                                      expert_model_parallel_size=1, timeout=datetime.timedelta(seconds=300))
     dev = topo.device
     torch.manual_seed(a.seed + topo.dp_rank)  # same replicated init within a TP group
-    model = TutorialModel(a.input_size, a.hidden_size, a.intermediate_size, topo.tp_rank, tp, topo.tp_group).to(dev)
+    pc, resolver, pcc = build_precision_runtime(a, dev)
+    model = TutorialModel(a.input_size, a.hidden_size, a.intermediate_size, topo.tp_rank, tp, topo.tp_group,
+                          param_dtype=dtype_alias_to_torch(pc.params_dtype), param_device=dev,
+                          precision_resolver=resolver)
+    finalize_module_precision_resolver(resolver)
     opt = FlatAdamW([dict(params=list(model.parameters()), weight_decay=a.weight_decay)], lr=a.lr,
                     dp_group=topo.dp_group)
     g = torch.Generator().manual_seed(a.seed)
@@ -83,9 +93,15 @@ def main():
             if step >= a.max_steps:
                 break
             opt.zero_grad()
-            loss = torch.nn.functional.mse_loss(model(X[i:i + a.batch_size]), Y[i:i + a.batch_size])
-            loss.backward()
-            opt.step()
+            with pcc.autocast_context():
+                pred = model(X[i:i + a.batch_size].to(dtype_alias_to_torch(pc.params_dtype)))
+            loss = torch.nn.functional.mse_loss(pred.float(), Y[i:i + a.batch_size])
+            pcc.backward(loss)
+            applied = pcc.prepare_optimizer_step(model) if pcc.uses_loss_scaling else True
+            if applied:
+                opt.step()
+                refresh_persistent_lowbit_params(model)
+            pcc.update_after_step(step_applied=applied)
             if topo.rank == 0 and a.log_every and step % a.log_every == 0:
                 print(f"epoch {epoch} step {step} loss {float(loss.detach()):.6f}", flush=True)
             step += 1

@@ -80,3 +80,13 @@ def add_mixed_precision_args(parser: argparse.ArgumentParser) -> None:
 
 def normalize_and_resolve_precision(args: argparse.Namespace, device: torch.device) -> PrecisionConfig:
     return resolve_precision_config(args, device)
+
+
+def build_precision_runtime(args: argparse.Namespace, device: torch.device):
+    """``(precision_config, module_resolver, controller)`` from the shared flags: the resolver is passed
+    to every layer's constructor (then ``finalize_module_precision_resolver``), the controller gives the
+    autocast context, loss scaling and the non-finite skip of a training step."""
+    from .mixed_precision import MixedPrecisionController, build_module_precision_resolver
+
+    pc = normalize_and_resolve_precision(args, device)
+    return pc, build_module_precision_resolver(pc), MixedPrecisionController(pc, device=device)

@@ -79,7 +79,14 @@ def _make_writer(log_dir: str, run_name: str, config: Config):
 
 
 class Trainer:
-    def __init__(self, model, config: Config, train_loader, device, val_loader=None):
+    def __init__(self, model, config: Config, train_loader, device, val_loader=None, precision_controller=None):
+        """``precision_controller`` (a ``MixedPrecisionController``, optional): forward passes run in its
+        autocast context, backward passes through its loss scaling, and a step whose unscaled gradients
+        are not finite on some rank is skipped (the scale backs off), as the reference's scripts do."""
+        self.precision_controller = precision_controller
+        # modules keeping persistent low-bit weight copies refresh them after every applied step
+        self._persistent_lowbit = [m for m in model.modules()
+                                   if callable(getattr(m, "_persistent_mode", None)) and m._persistent_mode() != "off"]
         self.device = torch.device(device)
         self.model = model.to(self.device)
         self.config = config
@@ -135,9 +142,15 @@ class Trainer:
         mb = min(self.micro_batch_size, B)
         n_mb = max(1, (B + mb - 1) // mb)
         total = torch.zeros((), device=self.device, dtype=torch.float32)
+        pcc = self.precision_controller
         for i in range(n_mb):
-            loss = self._loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
-            (loss / n_mb).backward()
+            if pcc is not None:
+                with pcc.autocast_context():
+                    loss = self._loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
+                pcc.backward(loss / n_mb)
+            else:
+                loss = self._loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
+                (loss / n_mb).backward()
             total += loss.detach().float()
         return total / n_mb, int((lab != -100).sum())
 
@@ -296,7 +309,18 @@ class Trainer:
                 self.optimizer.zero_grad()
                 loss_t, tokens = self.training_step(batch)
                 lr = self.scheduler.step()
-                self.optimizer.step()
+                pcc = self.precision_controller
+                applied = True
+                if pcc is not None and pcc.uses_loss_scaling:
+                    applied = pcc.prepare_optimizer_step(self.model)  # unscale; skip on inf/nan
+                    if applied:
+                        self.optimizer.step()
+                    pcc.update_after_step(step_applied=applied)
+                else:
+                    self.optimizer.step()
+                if applied:
+                    for m in self._persistent_lowbit:
+                        m.refresh_persistent_lowbit_params()
                 step += 1
                 tokens_window += tokens
                 if step % self.log_steps == 0 or step == tc.max_steps:

@@ -151,6 +151,10 @@ def test_trainer_runs_and_checkpoints(tmp_path):
 @pytest.mark.parametrize("script,args,expect", [
     ("examples/train_tp.py", ["--max_steps", "12", "--log_every", "5"], "step 10"),
     ("examples/train_ddp.py", ["--epochs", "1", "--num_samples", "128"], "mean loss"),
+    ("examples/train_tp.py", ["--max_steps", "12", "--log_every", "5", "--fp8", "--fp8-backend", "emulated"],
+     "step 10"),
+    ("examples/train_ddp.py", ["--epochs", "1", "--num_samples", "128", "--fp4", "--fp4-backend", "emulated"],
+     "mean loss"),
 ])
 def test_examples_via_launcher(script, args, expect):
     import subprocess
@@ -164,6 +168,26 @@ def test_examples_via_launcher(script, args, expect):
     p = subprocess.run(cmd, capture_output=True, text=True, timeout=300, cwd=ROOT, env=env)
     assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
     assert expect in p.stdout
+
+
+def test_example_scripts_share_the_precision_flags(tmp_path):
+    """Every training entry point takes the same precision flags (the reference's shared builder)."""
+    import subprocess
+    import sys
+
+    from conftest import ROOT
+
+    for script in ("train_mvp.py", "train_tp.py", "train_ddp.py", "train_4d.py"):
+        out = subprocess.run([sys.executable, f"examples/{script}", "--help"], capture_output=True, text=True,
+                             cwd=ROOT, timeout=120).stdout
+        for flag in ("--fp8", "--fp4", "--fp8-backend", "--fp4-backend", "--precision-recipe", "--params-dtype"):
+            assert flag in out, (script, flag)
+    p = subprocess.run([sys.executable, "examples/train_mvp.py", "--max_steps", "2", "--seq_len", "64",
+                        "--hidden_size", "64", "--num_layers", "1", "--batch_size", "2", "--fp4", "--fp4-backend",
+                        "native", "--output_dir", str(tmp_path / "mvp")], capture_output=True, text=True, cwd=ROOT,
+                       timeout=300, env=dict(os.environ, OMP_NUM_THREADS="1"))
+    assert p.returncode == 0, p.stdout[-2000:] + p.stderr[-2000:]
+    assert "'step': 2" in p.stdout
 
 
 def test_model_report_sweeps_and_sensitivity(tmp_path):
