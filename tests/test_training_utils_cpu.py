@@ -237,3 +237,27 @@ def test_model_report_sweeps_and_sensitivity(tmp_path):
     w1 = next(k for k in e1.kpis if k.mode == "decode").bytes_weights
     w64 = next(k for k in e64.kpis if k.mode == "decode").bytes_weights
     assert w1 < w64  # one token touches top_k of the experts, 64 tokens nearly all of them
+
+
+def test_view_logs_renders_jsonl_metrics(tmp_path):
+    """The offline log viewer turns metrics.jsonl runs into one HTML page of SVG charts, including
+    flat series at large magnitude (tick generation is bounded)."""
+    import json
+
+    from nano_train_b200.utils.svg_plot import _lin_ticks
+    from nano_train_b200.utils.view_logs import main
+
+    for run, off in (("a", 0.0), ("b", 0.1)):
+        d = tmp_path / "logs" / run
+        d.mkdir(parents=True)
+        with open(d / "metrics.jsonl", "w") as f:
+            for s in range(5):
+                f.write(json.dumps({"tag": "Loss/train", "value": 5.0 - s * 0.3 + off, "step": s}) + "\n")
+                f.write(json.dumps({"tag": "Throughput/tokens", "value": 1e9 + s * 1e-7, "step": s}) + "\n")
+            f.write('{"tag": "Loss/train", "val')  # a partly written last line is skipped
+    out = tmp_path / "m.html"
+    assert main(["--logdir", str(tmp_path / "logs"), "--html", str(out)]) == 0
+    html = out.read_text()
+    assert html.count("<svg") == 2 and "Loss/train" in html and html.count("<polyline") == 4
+    for lo, hi in ((1e9, 1e9 + 1e-7), (0.0, 0.0), (-1.0, 1.0), (1e-12, 2e-12)):
+        assert 1 <= len(_lin_ticks(lo, hi)) <= 8
