@@ -164,3 +164,46 @@ def test_deepseek_4d_config_eight_ranks():
     for rank, losses, dp, err in res:
         assert err is None, f"rank {rank}:\n{err}"
         assert dp == 2 and all(l == l and abs(l) < 100 for l in losses)
+
+
+def _bench_line(monkeypatch, capsys, argv, world=1, ms=500.0):
+    """Run bench.main() with the GPU parts stubbed: returns the JSON line rank 0 prints."""
+    import json
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    monkeypatch.setattr(sys, "argv", ["bench.py"] + argv)
+    monkeypatch.setattr(bench, "init_dist", lambda n: (0, 0, world))
+    clocks = {"sm_mhz": 1900.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 5}
+    e2e = {"value": 1.0, "unit": "tokens/s", "ms_per_step": ms, "h2d_bytes_per_step": 8, "d2h_bytes_per_step": 4}
+    monkeypatch.setattr(bench, "run_ours", lambda args, rank, local, w: (ms, 8, 1234, clocks, e2e, None))
+    bench.main()
+    out = [l for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(out) == 1
+    return json.loads(out[0])
+
+
+def test_bench_json_line_contract(monkeypatch, capsys):
+    """The default run's line carries every key the driver reads, with value = whole-job tokens / s."""
+    line = _bench_line(monkeypatch, capsys, ["--steps", "3", "--warmup", "3"])
+    for k in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "ms_per_step", "higher_is_better", "scaling",
+              "vs_baseline", "dtype", "data", "config", "clocks", "e2e", "gpu_launches"):
+        assert k in line, k
+    assert line["n_gpus"] == 1 and line["steps"] == 3 and line["warmup"] == 3 and line["higher_is_better"] is True
+    assert line["value"] == 8 * 4096 / 0.5 and line["dtype"] == "bf16" and line["gpu_launches"] == 1234
+    assert line["config"]["global_batch"] == 8 and line["config"]["seq_len"] == 4096
+    assert line["config"]["parallelism"] == "tp1" and line["scaling"] == "strong"
+    assert "flush" in line["config"]["l2"] or "L2" in line["config"]["l2"]
+    line8 = _bench_line(monkeypatch, capsys, ["--gpus", "8"], world=8)
+    assert line8["config"]["parallelism"] == "tp8+sp" and line8["value"] == 8 * 4096 / 0.5
+
+
+def test_bench_json_line_other_configs(monkeypatch, capsys):
+    gpt = _bench_line(monkeypatch, capsys, ["--config", "gpt1.3b-fp4-dp", "--gpus", "4"], world=4)
+    assert gpt["scaling"] == "weak" and gpt["config"]["seq_len"] == 2048 and gpt["config"]["global_batch"] == 32
+    assert gpt["value"] == 8 * 4 * 2048 / 0.5 and gpt["config"]["parallelism"] == "dp4+zero1"
+    ds = _bench_line(monkeypatch, capsys, ["--config", "dsv2lite-fp8-ep", "--gpus", "8"], world=8)
+    assert ds["config"]["parallelism"] == "ep8+dp8" and ds["value"] == 2 * 8 * 4096 / 0.5
+    d4 = _bench_line(monkeypatch, capsys, ["--config", "deepseek-4d", "--gpus", "8"], world=8)
+    assert d4["config"]["global_batch"] == 16 and d4["value"] == 16 * 2048 / 0.5
