@@ -207,3 +207,20 @@ def test_bench_json_line_other_configs(monkeypatch, capsys):
     assert ds["config"]["parallelism"] == "ep8+dp8" and ds["value"] == 2 * 8 * 4096 / 0.5
     d4 = _bench_line(monkeypatch, capsys, ["--config", "deepseek-4d", "--gpus", "8"], world=8)
     assert d4["config"]["global_batch"] == 16 and d4["value"] == 16 * 2048 / 0.5
+
+
+def test_bench_reference_arm_lines(monkeypatch, capsys):
+    import json
+
+    sys.path.insert(0, ROOT)
+    import bench
+
+    clocks = {"sm_mhz": 1900.0, "sm_max_mhz": 1965.0, "reasons": [], "samples": 5}
+    monkeypatch.setattr(bench, "run_reference", lambda args, rank, local, w: (1000.0, 8, 0, clocks, None))
+    line = _bench_line(monkeypatch, capsys, ["--impl", "reference"])
+    assert line["impl"] == "reference" and line["value"] == 8 * 4096 / 1.0 and line["metric"] == bench.METRIC
+    monkeypatch.setattr(sys, "argv", ["bench.py", "--impl", "reference", "--config", "deepseek-4d", "--gpus", "8"])
+    monkeypatch.setattr(bench, "init_dist", lambda n: (0, 0, 8))
+    bench.main()
+    out = [json.loads(l) for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
+    assert len(out) == 1 and out[0]["impl"] == "reference" and "unavailable" in out[0]
