@@ -24,10 +24,9 @@ from __future__ import annotations
 import hashlib
 import json
 import logging
-import math
 import os
 from dataclasses import asdict, dataclass
-from typing import Dict, Literal, Optional, Set
+from typing import Dict, Literal, Set
 
 import torch
 import torch.distributed as dist

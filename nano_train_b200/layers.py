@@ -19,7 +19,6 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 import torch.nn as nn
-import torch.nn.functional as F
 
 from . import ops
 from .config import _default_precision_resolver

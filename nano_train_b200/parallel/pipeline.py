@@ -21,7 +21,6 @@ from typing import Callable, Optional
 
 import torch
 import torch.distributed as dist
-import torch.nn as nn
 import torch.nn.functional as F
 
 import os

@@ -16,7 +16,6 @@ Reference parity: src/runtime/sync.py:20-219.
 """
 from __future__ import annotations
 
-from typing import Optional
 
 import torch
 import torch.distributed as dist

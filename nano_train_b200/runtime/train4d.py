@@ -16,7 +16,6 @@ from __future__ import annotations
 import argparse
 import os
 from dataclasses import dataclass
-from typing import Optional
 
 import torch
 import torch.nn as nn
