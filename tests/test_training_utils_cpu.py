@@ -261,3 +261,12 @@ def test_view_logs_renders_jsonl_metrics(tmp_path):
     assert html.count("<svg") == 2 and "Loss/train" in html and html.count("<polyline") == 4
     for lo, hi in ((1e9, 1e9 + 1e-7), (0.0, 0.0), (-1.0, 1.0), (1e-12, 2e-12)):
         assert 1 <= len(_lin_ticks(lo, hi)) <= 8
+
+
+def test_gpt_1p3b_config_shape():
+    from nano_train_b200.models.transformer import gpt_1p3b_config
+
+    m = TransformerModel(gpt_1p3b_config(param_device=torch.device("meta")))
+    n = sum(p.numel() for p in m.parameters())  # tied head: the embedding is counted once
+    assert 1.30e9 < n < 1.33e9, n
+    assert m.config.hidden_size == 2048 and len(m.blocks) == 24 and m.config.vocab_size == 50304
