@@ -185,7 +185,7 @@ def test_persistent_lowbit_weights_train_through_the_master_parameter(flag):
         assert fc.weight.grad is not None and fc.weight.grad.abs().sum() > 0  # STE reaches the master
         opt.step()
         fc.refresh_persistent_lowbit_params()
-        losses.append(float(loss))
+        losses.append(loss.item())
     assert losses[-1] < 0.7 * losses[0]
     assert not torch.equal(fc.weight.detach(), w0)
 
@@ -213,3 +213,36 @@ def test_default_schedule_selector():
     ctx = lambda pp: SimpleNamespace(parallel=SimpleNamespace(pipeline_model_parallel_size=pp))  # noqa: E731
     assert sel.select(ctx(1)) is plain
     assert sel.select(ctx(2)) is pipe and sel.select(ctx(4)) is pipe
+
+
+def _tiny_deepseek(resolver, overrides):
+    from nano_train_b200.models.deepseek import DeepSeekModel, DeepSeekModelConfig
+
+    cfg = DeepSeekModelConfig(param_dtype=torch.float32, param_device=None, precision_resolver=resolver,
+                              vocab_size=97, hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                              num_key_value_heads=4, intermediate_size=128, q_lora_rank=24, kv_lora_rank=16,
+                              qk_nope_head_dim=8, qk_rope_head_dim=8, v_head_dim=8, moe_intermediate_size=32,
+                              n_routed_experts=4, num_experts_per_tok=2, n_group=1, topk_group=1,
+                              max_position_embeddings=32, module_compute_dtype_overrides=overrides)
+    return DeepSeekModel(cfg), cfg
+
+
+def test_deepseek_exact_path_overrides_disable_lowbit_for_that_module():
+    torch.manual_seed(0)
+    # out_proj feeds the residual add, so a bf16 output there mixes with the fp32 stream by promotion
+    model, cfg = _tiny_deepseek(_fp8(), {"blocks.0.attn.out_proj": "bf16"})
+    finalize_module_precision_resolver(cfg.precision_resolver)
+    over, other = model.blocks[0].attn.out_proj, model.blocks[1].attn.out_proj
+    assert over._compute_lowbit_mode() is None and over._lowbit_backend is None
+    assert over._module_compute_dtype_override() == torch.bfloat16
+    assert other._compute_lowbit_mode() == "fp8"
+    logits = model(torch.randint(0, 97, (2, 7)))
+    assert logits.shape == (2, 7, 97) and torch.isfinite(logits).all()
+
+
+def test_deepseek_exact_path_override_must_match_a_module():
+    model, cfg = _tiny_deepseek(_fp8(), {"blocks.9.attn.q_b_proj": "fp32"})
+    with pytest.raises(ValueError, match="matched zero modules"):
+        finalize_module_precision_resolver(cfg.precision_resolver)
+    with pytest.raises(ValueError, match="values must be one of"):
+        _tiny_deepseek(_resolver(), {"blocks.0.attn.q_b_proj": "int4"})
