@@ -224,3 +224,43 @@ def test_bench_reference_arm_lines(monkeypatch, capsys):
     bench.main()
     out = [json.loads(l) for l in capsys.readouterr().out.splitlines() if l.startswith("{")]
     assert len(out) == 1 and out[0]["impl"] == "reference" and "unavailable" in out[0]
+
+
+def test_clock_sampler_reads_nvidia_smi_and_summarises(tmp_path, monkeypatch):
+    """The sampler polls nvidia-smi during the timed region; the summary keeps the median SM clock, the
+    maximum clock and every throttle reason that was Active in any sample ("Not Active" is not a reason)."""
+    sys.path.insert(0, ROOT)
+    import bench
+
+    rows = ["0, 1800, 1965, 950.1, 0x4, Not Active, Not Active, Not Active, Active",
+            "0, 1900, 1965, 990.0, 0x0, Not Active, Not Active, Not Active, Not Active",
+            "0, 1850, 1965, 999.9, 0x4, Not Active, Not Active, Not Active, Active"]
+    fake = tmp_path / "nvidia-smi"
+    counter = tmp_path / "n"
+    counter.write_text("0")
+    # a stand-in for nvidia-smi that answers the query with the next canned row
+    fake.write_text("#!/bin/sh\n"
+                    f"n=$(cat {counter}); echo $((n + 1)) > {counter}\n"
+                    "case $((n % 3)) in\n" +
+                    "".join(f"  {i}) echo '{r}';;\n" for i, r in enumerate(rows)) +
+                    "esac\n")
+    fake.chmod(0o755)
+    monkeypatch.setenv("PATH", f"{tmp_path}:{os.environ['PATH']}")
+    s = bench.ClockSampler(0)
+    s.start()
+    import time
+
+    deadline = time.time() + 20
+    while len(s.samples) < 3 and time.time() < deadline:
+        time.sleep(0.05)
+    s.stop()
+    got = s.summary()
+    assert got["samples"] >= 3 and got["sm_max_mhz"] == 1965.0
+    assert got["sm_mhz"] in (1800.0, 1850.0, 1900.0)
+    assert got["reasons"] == ["sw_power_cap"]
+
+    s = bench.ClockSampler(0)
+    s.samples = [[x.strip() for x in rows[1].replace("Not Active, Not Active, Not Active, Not Active",
+                                                         "Active, Not Active, Active, Not Active").split(",")]]
+    assert s.summary()["reasons"] == ["hw_slowdown", "sw_thermal_slowdown"]
+    assert bench.ClockSampler(0).summary() == {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
