@@ -15,8 +15,8 @@ from nano_train_b200.precision.mixed_precision import build_module_precision_res
 def _cfg(layers=5, **kw):
     resolver = build_module_precision_resolver(resolve_precision_config(argparse.Namespace(), torch.device("cpu")))
     base = dict(precision_resolver=resolver, param_dtype=torch.float32, param_device=None, vocab_size=97,
-                hidden_size=64, num_hidden_layers=layers, num_attention_heads=4, num_key_value_heads=4, intermediate_size=128,
-                q_lora_rank=24, kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=8, v_head_dim=8,
+                hidden_size=64, num_hidden_layers=layers, num_attention_heads=4, num_key_value_heads=4,
+                intermediate_size=128, q_lora_rank=24, kv_lora_rank=16, qk_nope_head_dim=8, qk_rope_head_dim=8, v_head_dim=8,
                 moe_intermediate_size=32, n_routed_experts=4, num_experts_per_tok=2, n_group=1, topk_group=1,
                 max_position_embeddings=32, first_k_dense_replace=1)
     base.update(kw)
