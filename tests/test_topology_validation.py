@@ -141,3 +141,36 @@ def test_pp_layer_splits():
                      ((0, 5, 5), "strictly")]:
         with pytest.raises(ValueError, match=msg):
             validate_args(_args(pipeline_model_parallel_size=2), 2, bad)
+
+
+def test_train_4d_parser_requires_the_canonical_parallel_flags():
+    from nano_train_b200.runtime.train4d import parse_args
+
+    with pytest.raises(SystemExit):
+        parse_args([])
+    a = parse_args(["--tensor-model-parallel-size", "1", "--pipeline-model-parallel-size", "2",
+                    "--expert-model-parallel-size", "4", "--use-distributed-optimizer",
+                    "--data-parallel-sharding-strategy", "optim"])
+    assert (a.tensor_model_parallel_size, a.pipeline_model_parallel_size, a.expert_model_parallel_size) == (1, 2, 4)
+    assert a.use_distributed_optimizer and a.data_parallel_sharding_strategy == "optim"
+
+
+def test_train_4d_parser_takes_the_shared_precision_flags():
+    import torch
+
+    from nano_train_b200.precision.mixed_precision import resolve_precision_config
+    from nano_train_b200.runtime.train4d import parse_args
+
+    canon = ["--tensor-model-parallel-size", "1", "--pipeline-model-parallel-size", "1",
+             "--expert-model-parallel-size", "1"]
+    a = parse_args(canon + ["--fp8", "--fp8-backend", "emulated", "--fp8-format", "hybrid",
+                            "--fp8-amax-history-len", "32", "--fp8-amax-compute-algo", "max"])
+    cfg = resolve_precision_config(a, torch.device("cpu"))
+    assert (cfg.mode, cfg.fp8_backend, cfg.fp8_format, cfg.fp8_amax_history_len, cfg.fp8_amax_compute_algo) == \
+        ("fp8", "emulated", "hybrid", 32, "max")
+    with pytest.raises(ValueError, match="At most one"):
+        resolve_precision_config(parse_args(canon + ["--fp8", "--fp16"]), torch.device("cpu"))
+    bad = parse_args(canon + ["--fp8"])
+    bad.fp8_backend = "cublas"
+    with pytest.raises(ValueError, match="--fp8-backend"):
+        resolve_precision_config(bad, torch.device("cpu"))
