@@ -188,3 +188,94 @@ def test_signature_is_stable_for_the_same_architecture_and_sees_shape_and_expert
     assert expert.parameter_signature_hash() != a.parameter_signature_hash()
     meta = expert._meta_by_name["0.weight"]
     assert meta.is_expert_param and (meta.shard_start, meta.shard_end, meta.group_size) == (0, 64, 1)
+
+
+def _padamw(model, **dt):
+    from nano_train_b200.runtime.optimizer_runtime import PrecisionAdamW
+
+    d = dict(main_params_dtype="fp32", main_grads_dtype="fp32", exp_avg_dtype="fp32", exp_avg_sq_dtype="fp32")
+    d.update(dt)
+    return PrecisionAdamW(model.parameters(), lr=1e-2, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8, **d)
+
+
+def test_precision_adamw_matches_torch_and_skips_parameters_without_gradients():
+    torch.manual_seed(0)
+    model, ref = nn.Sequential(nn.Linear(6, 5), nn.Linear(5, 3)), nn.Sequential(nn.Linear(6, 5), nn.Linear(5, 3))
+    ref.load_state_dict(model.state_dict())
+    opt = _padamw(model)
+    ref_opt = torch.optim.AdamW(ref.parameters(), lr=1e-2, weight_decay=0.1, betas=(0.9, 0.95), eps=1e-8)
+    x = torch.randn(8, 6)
+    for step in range(4):
+        for m, o in ((model, opt), (ref, ref_opt)):
+            o.zero_grad()
+            m(x).square().mean().backward()
+            if step == 3:  # the first layer's bias gets no gradient: value and state stay as they are
+                m[0].bias.grad = None
+            o.step()
+    for p, r in zip(model.parameters(), ref.parameters()):
+        torch.testing.assert_close(p, r, atol=1e-6, rtol=1e-5)
+    assert opt.state[model[0].bias]["step"] == 3 and opt.state[model[0].weight]["step"] == 4
+
+
+def test_precision_adamw_state_dict_resumes_identically_with_low_precision_moments():
+    torch.manual_seed(1)
+    a = nn.Linear(7, 4)
+    b = nn.Linear(7, 4)
+    b.load_state_dict(a.state_dict())
+    oa = _padamw(a, exp_avg_dtype="bf16", exp_avg_sq_dtype="bf16")
+    assert oa.state[a.weight]["exp_avg"].dtype == torch.bfloat16
+    x = torch.randn(5, 7)
+
+    def step(m, o):
+        o.zero_grad()
+        m(x).square().mean().backward()
+        o.step()
+
+    step(a, oa)
+    ob = _padamw(b, exp_avg_dtype="bf16", exp_avg_sq_dtype="bf16")
+    ob.load_state_dict(oa.state_dict())
+    b.load_state_dict(a.state_dict())
+    step(a, oa)
+    step(b, ob)
+    assert torch.equal(a.weight, b.weight) and torch.equal(a.bias, b.bias)
+    with pytest.raises(ValueError, match="not a PrecisionAdamW"):
+        ob.load_state_dict({"format": "other"})
+    with pytest.raises(ValueError, match="parameter layout"):
+        _padamw(nn.Linear(7, 5)).load_state_dict(oa.state_dict())
+
+
+def test_step_with_sync_policy_syncs_then_steps_or_uses_ready_grads():
+    from types import SimpleNamespace
+
+    from nano_train_b200.runtime.contracts import OptimizerState, ParamShardInfo
+    from nano_train_b200.runtime.optimizer_runtime import step_with_sync_policy, zero_grad_optimizer
+
+    calls = []
+
+    class Opt:
+        def zero_grad(self, set_to_none=True):
+            calls.append(("zero_grad", set_to_none))
+
+        def step(self):
+            calls.append(("step",))
+
+        def step_with_ready_grads(self):
+            calls.append(("ready",))
+
+    parallel = SimpleNamespace(data_parallel_size=2, expert_data_parallel_size=2, data_parallel_group="dp",
+                               expert_data_parallel_group="edp")
+    state = OptimizerState(optimizer=Opt(), shard_info=ParamShardInfo(set(), set()))
+
+    def sync(**kw):
+        calls.append(("sync", kw["data_parallel_group"], kw["expert_data_parallel_group"]))
+
+    zero_grad_optimizer(state)
+    ctx = SimpleNamespace(parallel=parallel, run_config=SimpleNamespace(args=SimpleNamespace(
+        use_distributed_optimizer=False)))
+    step_with_sync_policy(model=nn.Linear(1, 1), state=state, ctx=ctx, synchronize_gradients_fn=sync)
+    ctx.run_config.args.use_distributed_optimizer = True
+    step_with_sync_policy(model=nn.Linear(1, 1), state=state, ctx=ctx, synchronize_gradients_fn=sync)
+    assert calls == [("zero_grad", True), ("sync", "dp", "edp"), ("step",), ("ready",)]
+    with pytest.raises(TypeError, match="step_with_ready_grads"):
+        step_with_sync_policy(model=nn.Linear(1, 1), state=OptimizerState(optimizer=object(), shard_info=None),
+                              ctx=ctx, synchronize_gradients_fn=sync)
