@@ -270,3 +270,33 @@ def test_gpt_1p3b_config_shape():
     n = sum(p.numel() for p in m.parameters())  # tied head: the embedding is counted once
     assert 1.30e9 < n < 1.33e9, n
     assert m.config.hidden_size == 2048 and len(m.blocks) == 24 and m.config.vocab_size == 50304
+
+
+def test_logged_gradient_norm_is_the_norm_of_the_steps_gradient(tmp_path):
+    """The pre-clip gradient norm the Trainer logs is taken from the step's gradients before they are
+    cleared: it equals the norm of the same batch's gradient computed independently."""
+    import copy
+
+    torch.manual_seed(0)
+    mcfg = _tiny_cfg()
+    model = TransformerModel(mcfg)
+    twin = copy.deepcopy(model)
+    cfg = Config(model=mcfg, training=TrainingConfig(batch_size=4, micro_batch_size=4, learning_rate=1e-3,
+                                                     max_steps=1, warmup_steps=0, log_steps=1, eval_steps=100,
+                                                     save_steps=100, clip_grad=0.05),
+                 output_dir=str(tmp_path / "out"), log_dir=str(tmp_path / "logs"))
+    ds = SyntheticTokenDataset(16, 16, 64, seed=0)
+    loader = create_dataloader(ds, 4, shuffle=False)
+    tr = Trainer(model, cfg, loader, "cpu")
+    logged = {}
+    tr.writer = type("W", (), {"add_scalar": lambda self, tag, v, step: logged.setdefault((tag, step), float(v)),
+                               "flush": lambda self: None, "close": lambda self: None})()
+    tr.train()
+    batch = next(iter(create_dataloader(ds, 4, shuffle=False)))
+    logits = twin(batch["input_ids"])
+    torch.nn.functional.cross_entropy(logits.reshape(-1, logits.shape[-1]).float(), batch["labels"].reshape(-1),
+                                      ignore_index=-100).backward()
+    expect = float(torch.sqrt(sum(p.grad.float().pow(2).sum() for p in twin.parameters() if p.grad is not None)))
+    got = logged[("Gradients/global_norm_pre_clip", 1)]
+    assert got == pytest.approx(expect, rel=1e-4)
+    assert got > 0.05 and logged[("Gradients/clip_coef", 1)] == pytest.approx(0.05 / (expect + 1e-6), rel=1e-4)
