@@ -28,7 +28,7 @@ def test_router_group_limited_topk(scoring):
     x = torch.randn(50, 32)
     out = r(x)
     logits = x @ r.router.weight.t()
-    scores = torch.sigmoid(logits) if scoring == "sigmoid" else torch.softmax(logits, -1)
+    scores = (torch.sigmoid(logits) if scoring == "sigmoid" else torch.softmax(logits, -1)).detach()
     for t in range(50):
         gmax = scores[t].view(G, E // G).max(-1).values
         allowed_groups = set(torch.topk(gmax, TG).indices.tolist())
@@ -69,7 +69,8 @@ def _moe_oracle(moe, x):
     cap = max(int(math.ceil(moe.capacity_factor * T * K / moe.num_experts)), 1)
     out = torch.zeros_like(tokens)
     for e in range(moe.num_experts):
-        cand = [(float(ro.topk_weights[t, s]), t, s) for t in range(T) for s in range(K) if ro.topk_indices[t, s] == e]
+        w = ro.topk_weights.detach()
+        cand = [(float(w[t, s]), t, s) for t in range(T) for s in range(K) if ro.topk_indices[t, s] == e]
         cand.sort(key=lambda c: -c[0])
         for _, t, s in cand[:cap]:
             ex = moe.experts[e]
