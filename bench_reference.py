@@ -28,12 +28,75 @@ import torch.nn.functional as F
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 REF = os.path.join(ROOT, "baseline", "_ref")
+WHEELHOUSE = "/opt/wheelhouse"
+_UNAVAILABLE_WHY = ""
+
+
+def _reference_sources():
+    """Source trees the reference can be installed from, in the order they are tried:
+    ``$NTB_REFERENCE_PATH``, then ``reference_path`` of ``BASELINE.json`` next to this file."""
+    out = []
+    env = os.environ.get("NTB_REFERENCE_PATH")
+    if env:
+        out.append(env)
+    try:
+        with open(os.path.join(ROOT, "BASELINE.json")) as f:
+            p = json.load(f).get("reference_path")
+        if p:
+            out.append(p)
+    except (OSError, ValueError):
+        pass
+    return out
+
+
+def _install_reference(tried):
+    """``pip install --no-deps`` of the unmodified reference into ``baseline/_ref`` (offline, from the
+    image's wheelhouse; the image's torch is used, which is why dependency resolution is skipped). The
+    source tree may be read-only, so the build runs from a copy in a temporary directory. One process
+    per host installs; the others wait on the same file lock and then find the installed copy."""
+    import fcntl
+    import shutil
+    import subprocess
+    import tempfile
+
+    os.makedirs(os.path.dirname(REF), exist_ok=True)
+    with open(os.path.join(os.path.dirname(REF), ".install.lock"), "w") as lock:
+        fcntl.flock(lock, fcntl.LOCK_EX)
+        if os.path.isdir(os.path.join(REF, "src")):
+            return True
+        for srcdir in _reference_sources():
+            if not os.path.isfile(os.path.join(srcdir, "setup.py")):
+                tried.append(f"{srcdir}: no setup.py")
+                continue
+            with tempfile.TemporaryDirectory(prefix="ntb_ref_") as tmp:
+                copy = os.path.join(tmp, "reference")
+                shutil.copytree(srcdir, copy, ignore=shutil.ignore_patterns(".git", "__pycache__"))
+                cmd = [sys.executable, "-m", "pip", "install", "--no-index", "--no-build-isolation", "--no-deps",
+                       "--find-links", WHEELHOUSE, "--target", REF, copy]
+                r = subprocess.run(cmd, capture_output=True, text=True)
+            if r.returncode == 0 and os.path.isdir(os.path.join(REF, "src")):
+                return True
+            err = (r.stderr or r.stdout).strip().splitlines()
+            tried.append(f"pip install {srcdir}: rc={r.returncode} {err[-1] if err else ''}")
+    return False
 
 
 def _import_reference():
-    if not os.path.isdir(os.path.join(REF, "src")):
+    """Import the reference's ``src`` package from ``baseline/_ref`` (or ``$NTB_REFERENCE_SRC``, a
+    directory holding an installed ``src``), installing it first when it is absent. Returns None
+    and records every path tried and the pip error when no copy can be had."""
+    global _UNAVAILABLE_WHY
+    tried = []
+    roots = [r for r in (os.environ.get("NTB_REFERENCE_SRC"), REF) if r]
+    root = next((r for r in roots if os.path.isdir(os.path.join(r, "src"))), None)
+    if root is None:
+        tried += [f"{r}/src: absent" for r in roots]
+        if _install_reference(tried):
+            root = REF
+    if root is None:
+        _UNAVAILABLE_WHY = "reference not installed; tried " + "; ".join(tried)
         return None
-    sys.path.insert(0, REF)
+    sys.path.insert(0, root)
     for k in [m for m in sys.modules if m == "src" or m.startswith("src.")]:
         del sys.modules[k]
     import src  # noqa: F401
@@ -43,6 +106,14 @@ def _import_reference():
     from src.runtime.optimizer_runtime import PrecisionAdamW
 
     return L, DS, PrecisionAdamW, _default_precision_resolver
+
+
+def _print_unavailable(rank, config=None):
+    if rank == 0:
+        line = {"impl": "reference", "unavailable": _UNAVAILABLE_WHY or "reference not installed"}
+        if config:
+            line["config"] = config
+        print(json.dumps(line), flush=True)
 
 
 def build_model(ref, layers, rank, world, group, seq):
@@ -126,8 +197,7 @@ def build_model(ref, layers, rank, world, group, seq):
 def run(args, rank, local, world, global_batch, micro_batch, make_batches, barrier, max_over_ranks, ClockSampler):
     ref = _import_reference()
     if ref is None:
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}), flush=True)
+        _print_unavailable(rank)
         return None
     _, _, PrecisionAdamW, _ = ref
     layers = args.layers or (8 if world == 1 else 32)
@@ -192,8 +262,7 @@ def run_deepseek(args, rank, local, world, make_batches, barrier, max_over_ranks
     tokens of a step are one batch. ``dims`` shrinks the model for a CPU check of this code."""
     ref = _import_reference()
     if ref is None:
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}), flush=True)
+        _print_unavailable(rank)
         return None
     import argparse as _ap
 
@@ -288,8 +357,7 @@ def run_gpt_fp4(args, rank, local, world, make_batches, barrier, ClockSampler, b
     moments. One GPU: the reference wires ZeRO only for its DeepSeekModel."""
     ref = _import_reference()
     if ref is None:
-        if rank == 0:
-            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}), flush=True)
+        _print_unavailable(rank)
         return None
     if world > 1:
         if rank == 0:
