@@ -556,15 +556,15 @@ class DeepSeekModel(nn.Module):
 def gather_moe_metrics(model: nn.Module) -> tuple[torch.Tensor, float, int]:
     """(sum of MoE aux losses, sum of dropped fractions, number of MoE layers) of the last forward."""
     aux = None
-    drop = 0.0
-    n = 0
+    drops = []
     for m in model.modules():
         if isinstance(m, (LocalRoutedMoE, ExpertParallelMoE)):
             a = m.last_aux_loss
             aux = a if aux is None else aux + a
-            drop += float(m.last_dropped_fraction)
-            n += 1
+            drops.append(m.last_dropped_fraction_tensor.float().reshape(()))
     if aux is None:
         p = next(model.parameters())
         aux = torch.zeros((), device=p.device, dtype=torch.float32)
-    return aux, drop, n
+    # One host read for every layer's dropped fraction.
+    drop = float(torch.stack([d.to(aux.device) for d in drops]).sum()) if drops else 0.0
+    return aux, drop, len(drops)

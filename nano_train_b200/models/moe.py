@@ -251,7 +251,18 @@ class LocalRoutedMoE(nn.Module):
 
     @property
     def last_dropped_fraction(self) -> float:
-        return self._last_dropped_fraction
+        """Dropped fraction of the last forward; read from the device (once) when asked for."""
+        d = self._last_dropped_fraction
+        if isinstance(d, torch.Tensor):
+            d = float(d)
+            self._last_dropped_fraction = d
+        return d
+
+    @property
+    def last_dropped_fraction_tensor(self) -> torch.Tensor:
+        """Dropped fraction of the last forward as a scalar tensor, with no host synchronisation."""
+        d = self._last_dropped_fraction
+        return d if isinstance(d, torch.Tensor) else torch.tensor(float(d))
 
     @property
     def last_token_counts(self) -> torch.Tensor:
@@ -280,7 +291,7 @@ class LocalRoutedMoE(nn.Module):
             out = out + shared / float(len(self.shared_experts))
         total = ro.topk_indices.numel()
         self._last_aux_loss = ro.aux_loss
-        self._last_dropped_fraction = float((total - int(counts.sum())) / max(total, 1))
+        self._last_dropped_fraction = (total - counts.sum()).float() / float(max(total, 1))  # read lazily
         self._last_token_counts = counts
         return out.view(B, S, H)
 
@@ -382,12 +393,22 @@ class ExpertParallelMoE(nn.Module):
 
     @property
     def last_dropped_fraction(self) -> float:
+        """Dropped fraction of the last forward over the EP group; the device statistics
+        (dropped, routed) are read only when asked for."""
         d = self._last_dropped_fraction
-        if isinstance(d, torch.Tensor):  # fused path: device stats, read only when asked for
+        if isinstance(d, torch.Tensor):
             s = d.tolist()
             d = float(s[0] / max(s[1], 1.0))
             self._last_dropped_fraction = d
         return d
+
+    @property
+    def last_dropped_fraction_tensor(self) -> torch.Tensor:
+        """Dropped fraction of the last forward as a scalar tensor, with no host synchronisation."""
+        d = self._last_dropped_fraction
+        if isinstance(d, torch.Tensor):
+            return d[0] / d[1].clamp_min(1.0)
+        return torch.tensor(float(d))
 
     def _fused_payload(self):
         """(use the fused kernels, e4m3 payload) for this layer's settings."""
@@ -424,9 +445,6 @@ class ExpertParallelMoE(nn.Module):
         self.last_path = "all_to_all"
         E, epr, K = self.num_experts, self.experts_per_rank, self.top_k
         # Global token count -> capacity (every EP rank sees the same capacity).
-        t_all = torch.tensor([float(T)], device=tokens.device)
-        dist.all_reduce(t_all, group=self.ep_group)
-        capacity = self._compute_capacity(int(t_all.item()))
         # Assignments sorted by destination expert (hence by destination rank).
         flat_e = ro.topk_indices.reshape(-1)
         order = torch.argsort(flat_e, stable=True)
@@ -434,8 +452,12 @@ class ExpertParallelMoE(nn.Module):
         send_counts = torch.bincount(dest_e // epr, minlength=self.ep_size)
         recv_counts = torch.empty_like(send_counts)
         dist.all_to_all_single(recv_counts, send_counts, group=self.ep_group)
-        cnt = torch.stack([send_counts, recv_counts]).tolist()
+        t_all = torch.full((self.ep_size,), T, dtype=send_counts.dtype, device=tokens.device)
+        dist.all_reduce(t_all, group=self.ep_group)  # each entry becomes the global token count
+        # One host read per layer: the splits NCCL needs and the global token count (capacity).
+        cnt = torch.stack([send_counts, recv_counts, t_all]).tolist()
         send_splits, recv_splits = cnt[0], cnt[1]
+        capacity = self._compute_capacity(int(cnt[2][0]))
         tok_idx = order // K
         slot_idx = order % K
         payload = _comm_quant_dequant(tokens[tok_idx], self.comm_quant_granularity, self.comm_quant_rounding,
@@ -473,10 +495,9 @@ class ExpertParallelMoE(nn.Module):
         if len(self.shared_experts):
             out = out + sum(se(tokens) for se in self.shared_experts) / float(len(self.shared_experts))
         stats = torch.tensor([float(recv_w.numel() - kept.numel()), float(recv_w.numel())], device=tokens.device)
-        dist.all_reduce(stats, group=self.ep_group)
-        s = stats.tolist()
+        dist.all_reduce(stats, group=self.ep_group)  # enqueued; read lazily by last_dropped_fraction
         self._last_aux_loss = ro.aux_loss
-        self._last_dropped_fraction = float(s[0] / max(s[1], 1.0))
+        self._last_dropped_fraction = stats
         self._last_token_counts = kept_counts
         return out.view(B, S, H)
 

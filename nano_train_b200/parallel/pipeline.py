@@ -8,11 +8,23 @@ forwards, steady one-forward-one-backward, cool-down backwards; activations
 30000+mb); the last stage computes CE / M (+ aux * coef / M) and non-last
 stages back-propagate ``[output, aux]`` with ``[dY, coef / M * loss_scale]``.
 
+Issue order. NCCL ignores tags: between one pair of ranks it matches sends
+and receives of one direction in the order they were issued. With PP = 2 the
+first stage is also the last stage's previous stage, so the label and the
+activation of a micro-batch travel the same pair in the same direction. Every
+sender therefore issues, per micro-batch, the label first and the activation
+second, and every receiver posts its receives of a micro-batch through
+``_post_stage_inputs`` in that same order (label, then activation), early
+posting (``NTB_PP_PREFETCH=1``) included. Gradients travel the other
+direction and are matched on their own.
+
 Receives are posted as non-blocking requests. Posting the next micro-batch's
-receive early (``NTB_PP_PREFETCH=1``) lets the transfer run under the current
-micro-batch's compute, but NCCL executes point-to-point operations of one
-communicator in issue order, so an early receive can sit in front of a send
-the peer is waiting for; it is therefore off by default.
+receives early (``NTB_PP_PREFETCH=1``) lets the transfer run under the current
+micro-batch's compute, but an early receive can sit in front of a send the
+peer is waiting for; it is therefore off by default.
+
+Losses and MoE statistics stay on the device during the step (no ``.item()``
+per micro-batch); ``train_step_pipeline`` reads them once, after the schedule.
 """
 from __future__ import annotations
 
@@ -62,10 +74,11 @@ class PipelineStepState:
     grad_send_reqs: list = field(default_factory=list)
     grad_send_buffers: list = field(default_factory=list)
     pending_act_recv: dict = field(default_factory=dict)
+    pending_label_recv: dict = field(default_factory=dict)
     pending_grad_recv: dict = field(default_factory=dict)
-    task_loss_sum: float = 0.0
-    aux_loss_sum: float = 0.0
-    drop_sum: float = 0.0
+    task_loss_sum: object = 0.0  # device scalars during the step, floats after finalize_pipeline_metrics
+    aux_loss_sum: object = 0.0
+    drop_sum: object = 0.0
     drop_count: int = 0
 
 
@@ -94,11 +107,17 @@ def prepare_microbatches(batch, model, expected_local_batch: int, num_microbatch
     return list(torch.chunk(ids, num_microbatches, dim=0))
 
 
-def _post_act_recv(state, mb, shape, dtype, device, src):
-    if mb in state.pending_act_recv:
-        return
-    buf = torch.empty(shape, device=device, dtype=dtype)
-    state.pending_act_recv[mb] = (buf, dist.irecv(buf, src=src, tag=activation_tag(mb)))
+def _post_stage_inputs(state, mb, model, peers, shape, dtype, device):
+    """Post this stage's receives of micro-batch ``mb``: the label (last stage only) before the
+    activation (non-first stages), the order in which the senders issue them."""
+    if model.is_last_pp_stage and not model.is_first_pp_stage and mb not in state.pending_label_recv:
+        lab = torch.empty(shape[:2], dtype=torch.long, device=device)
+        state.pending_label_recv[mb] = (lab, dist.irecv(lab, src=peers.first_stage_rank, tag=label_tag(mb)))
+    if not model.is_first_pp_stage and mb not in state.pending_act_recv:
+        if peers.prev_rank is None:
+            raise RuntimeError("Missing previous PP rank")
+        buf = torch.empty(shape, device=device, dtype=dtype)
+        state.pending_act_recv[mb] = (buf, dist.irecv(buf, src=peers.prev_rank, tag=activation_tag(mb)))
 
 
 def _post_grad_recv(state, mb, shape, dtype, device, src):
@@ -121,6 +140,7 @@ def pipeline_forward_microbatch(microbatch_idx: int, model, microbatches, peers:
         if ids is None:
             raise RuntimeError("Missing first-stage microbatch")
         if not model.is_last_pp_stage:
+            # Label before activation: the receiver posts them in this order (module docstring).
             state.label_send_reqs.append(dist.isend(ids.contiguous(), dst=peers.last_stage_rank,
                                                     tag=label_tag(microbatch_idx)))
         with ctx:
@@ -128,22 +148,21 @@ def pipeline_forward_microbatch(microbatch_idx: int, model, microbatches, peers:
         if model.is_last_pp_stage:
             label = ids
     else:
-        if peers.prev_rank is None:
-            raise RuntimeError("Missing previous PP rank")
-        _post_act_recv(state, microbatch_idx, shape, activation_dtype, device, peers.prev_rank)
+        _post_stage_inputs(state, microbatch_idx, model, peers, shape, activation_dtype, device)
+        if model.is_last_pp_stage:
+            label, label_req = state.pending_label_recv.pop(microbatch_idx)
         buf, req = state.pending_act_recv.pop(microbatch_idx)
         req.wait()
         if PREFETCH and num_microbatches is not None and microbatch_idx + 1 < num_microbatches:
-            _post_act_recv(state, microbatch_idx + 1, shape, activation_dtype, device, peers.prev_rank)
+            _post_stage_inputs(state, microbatch_idx + 1, model, peers, shape, activation_dtype, device)
         stage_input = buf.requires_grad_(True)
         with ctx:
             out = model.forward_stage(input_ids=None, hidden_states=stage_input, attention_mask=None)
         if model.is_last_pp_stage:
-            label = torch.empty((microbatch_batch_size, seq_len), dtype=torch.long, device=device)
-            dist.recv(label, src=peers.first_stage_rank, tag=label_tag(microbatch_idx))
+            label_req.wait()
     aux, drop = gather_moe_metrics_fn(model, device=device)
-    state.aux_loss_sum += float(aux.detach().item())
-    state.drop_sum += float(drop)
+    state.aux_loss_sum = state.aux_loss_sum + aux.detach().float().reshape(())
+    state.drop_sum = state.drop_sum + drop
     state.drop_count += 1
     if not model.is_last_pp_stage:
         if peers.next_rank is None:
@@ -180,7 +199,7 @@ def pipeline_backward_microbatch(microbatch_idx: int, model, peers: PipelinePeer
             task = out.sum() * 0.0
         else:
             task = F.cross_entropy(out[:, :-1, :].reshape(-1, out.size(-1)).float(), labels[:, 1:].reshape(-1))
-        state.task_loss_sum += float(task.detach().item())
+        state.task_loss_sum = state.task_loss_sum + task.detach().float()
         scale = 1.0 / float(num_microbatches)
         total = task * scale + aux_loss_coef * scale * aux
         if precision_controller is None:
@@ -230,12 +249,26 @@ def execute_1f1b_schedule(parallel, num_microbatches: int, run_forward: Callable
 def finalize_pipeline_sends(state: PipelineStepState) -> None:
     for r in state.activation_send_reqs + state.grad_send_reqs + state.label_send_reqs:
         r.wait()
-    for _, (_, r) in list(state.pending_act_recv.items()) + list(state.pending_grad_recv.items()):
+    pending = (list(state.pending_label_recv.items()) + list(state.pending_act_recv.items())
+               + list(state.pending_grad_recv.items()))
+    for _, (_, r) in pending:
         r.wait()
+    state.pending_label_recv.clear()
     state.pending_act_recv.clear()
     state.pending_grad_recv.clear()
     state.activation_send_buffers.clear()
     state.grad_send_buffers.clear()
+
+
+def finalize_pipeline_metrics(state: PipelineStepState) -> None:
+    """Turn the step's device-side sums into floats with one host read."""
+    vals = [state.task_loss_sum, state.aux_loss_sum, state.drop_sum]
+    dev = next((v for v in vals if isinstance(v, torch.Tensor)), None)
+    if dev is None:
+        return
+    out = torch.stack([v.detach().float().reshape(()) if isinstance(v, torch.Tensor)
+                       else torch.tensor(float(v), device=dev.device) for v in vals]).tolist()
+    state.task_loss_sum, state.aux_loss_sum, state.drop_sum = out
 
 
 def train_step_pipeline(model, optimizer, use_distributed_optimizer: bool, batch, parallel, num_microbatches: int,
@@ -268,6 +301,7 @@ def train_step_pipeline(model, optimizer, use_distributed_optimizer: bool, batch
                                                             mbs, seq_len, hidden, act_dtype, device,
                                                             precision_controller))
     finalize_pipeline_sends(state)
+    finalize_pipeline_metrics(state)
     should_step = True
     if precision_controller is not None:
         should_step = precision_controller.prepare_optimizer_step(model)

@@ -155,14 +155,16 @@ def create_data_loader(dataset: Dataset, batch_size: int, dp_size: int, dp_rank:
 
 
 def gather_moe_metrics(model: nn.Module, device: torch.device):
-    """Sum of aux losses and mean dropped fraction over all MoE layers of the last forward."""
+    """Sum of aux losses and mean dropped fraction over all MoE layers of the last forward, both as
+    device scalars: nothing is read back to the host here (callers read once per step)."""
     aux, drops = [], []
     for m in model.modules():
         if isinstance(m, (ExpertParallelMoE, LocalRoutedMoE)):
             aux.append(m.last_aux_loss.reshape(()))
-            drops.append(m.last_dropped_fraction)
+            drops.append(m.last_dropped_fraction_tensor.to(device=device, dtype=torch.float32).reshape(()))
     a = torch.stack(aux).sum() if aux else torch.zeros((), device=device)
-    return a, float(sum(drops) / len(drops)) if drops else 0.0
+    d = torch.stack(drops).mean() if drops else torch.zeros((), device=device)
+    return a, d
 
 
 def _infer_mode(parallel) -> str:
@@ -340,8 +342,9 @@ class Train4PNonPipelineSchedule:
                 logger.info("precision step=%d mode=%s loss_scale=%.4f skipped_steps=%d",
                             step_ctx.train_state.global_step, ctrl.config.mode, ctrl.runtime_state.loss_scale,
                             ctrl.runtime_state.skipped_steps)
-        vals = torch.stack([task.detach().float(), aux.detach().float().reshape(()), total.detach().float()]).tolist()
-        return StepOutput(task_loss=vals[0], aux_loss=vals[1], total_loss=vals[2], drop_fraction=drop,
+        vals = torch.stack([task.detach().float(), aux.detach().float().reshape(()), total.detach().float(),
+                            drop.float().reshape(())]).tolist()
+        return StepOutput(task_loss=vals[0], aux_loss=vals[1], total_loss=vals[2], drop_fraction=vals[3],
                           counters={"objective_count": 1, "drop_count": 1})
 
 
