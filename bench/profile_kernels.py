@@ -42,7 +42,10 @@ def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("case")
     ap.add_argument("--iters", type=int, default=3)
+    ap.add_argument("--time", type=int, default=0,
+                    help="also time this many launches with CUDA events (after the warm-up) and print ms / GB/s")
     a = ap.parse_args()
+    nbytes = 0  # algorithmic DRAM bytes of one launch, where the case defines them
     C = ext()
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
@@ -105,6 +108,7 @@ def main():
         w = torch.randn(4096, **bf)
         dy = torch.randn(8192, 4096, **bf)
         rstd = torch.rand(8192, device=dev) + 0.5
+        nbytes = 3 * 8192 * 4096 * 2 + 8192 * 4 + 4096 * (2 + 4 + 2)  # dy, h, dx; rstd; w, dw (fp32 + bf16)
         fn = lambda: C.rmsnorm_bwd(dy, h, w, rstd, None)  # noqa: E731
     elif a.case == "adamw":
         n = 64 * 1024 * 1024
@@ -177,6 +181,25 @@ def main():
     torch.cuda.synchronize()
     check_status(0)
     print(f"{a.case}: ok")
+    if a.time:
+        # Each launch is timed on its own between two events, with a 256 MB write before it so the
+        # inputs are not served from the 126 MB L2; the median is reported.
+        flush = torch.empty(256 * 2 ** 20, dtype=torch.uint8, device=dev)
+        ts = []
+        for _ in range(a.time):
+            flush.fill_(1)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            fn()
+            e.record()
+            e.synchronize()
+            ts.append(s.elapsed_time(e))
+        ts.sort()
+        ms = ts[len(ts) // 2]
+        line = f"{a.case}: median {ms * 1e3:.1f} us over {a.time} launches"
+        if nbytes:
+            line += f", {nbytes / ms / 1e6:.0f} GB/s algorithmic"
+        print(line)
 
 
 if __name__ == "__main__":

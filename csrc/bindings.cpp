@@ -33,7 +33,8 @@ void gemm_grouped_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out
 std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at::Tensor>& residual,
                                     const at::Tensor& w, double eps);
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& h, const at::Tensor& w,
-                                    const at::Tensor& rstd, const c10::optional<at::Tensor>& dres);
+                                    const at::Tensor& rstd, const c10::optional<at::Tensor>& dres,
+                                    const c10::optional<at::Tensor>& dw_into);
 std::vector<at::Tensor> layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& b,
                                       double eps);
 std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& w,
@@ -150,7 +151,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("b"), py::arg("out"), py::arg("offsets"), py::arg("mode"), py::arg("b_mn") = false,
         py::arg("accumulate") = false, py::arg("c_group_stride") = 0);
   m.def("rmsnorm_fwd", &ntb::rmsnorm_fwd);
-  m.def("rmsnorm_bwd", &ntb::rmsnorm_bwd);
+  m.def("rmsnorm_bwd", &ntb::rmsnorm_bwd, py::arg("dy"), py::arg("h"), py::arg("w"), py::arg("rstd"),
+        py::arg("dres"), py::arg("dw_into") = py::none());
   m.def("layernorm_fwd", &ntb::layernorm_fwd);
   m.def("layernorm_bwd", &ntb::layernorm_bwd);
   m.def("rope_", &ntb::rope_);

@@ -20,6 +20,7 @@
 #include "host_utils.h"
 #include "no_alloc.h"
 
+#include <atomic>
 #include <cstdio>
 #include <mutex>
 
@@ -178,10 +179,12 @@ __global__ void rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict_
 }
 
 // dx = rstd * (g - n * mean(g * n)), g = dy * w, n = h * rstd; dw partials per block.
-template <typename T, bool VEC>
-__global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ h, const T* __restrict__ w,
-                                   const float* __restrict__ rstd, const T* __restrict__ dres, T* __restrict__ dx,
-                                   float* __restrict__ dw_part, int64_t rows, int H, int rows_per_block) {
+// Scalar form, for rows whose width or pointers do not allow 16-byte vectors.
+template <typename T>
+__global__ void rmsnorm_bwd_scalar_kernel(const T* __restrict__ dy, const T* __restrict__ h, const T* __restrict__ w,
+                                          const float* __restrict__ rstd, const T* __restrict__ dres,
+                                          T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int H,
+                                          int rows_per_block) {
   __shared__ float red[32];
   const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
   float* dwp = dw_part + static_cast<int64_t>(blockIdx.x) * H;
@@ -191,54 +194,263 @@ __global__ void rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict
     const T* dyr = dy + row * H;
     const T* hr = h + row * H;
     float dot = 0.f;
-    if (VEC) {
-      for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-        float a[8], b[8], c[8];
-        ld8(dyr + i, a);
-        ld8(hr + i, b);
-        ld8(w + i, c);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) dot += a[j] * c[j] * b[j];
-      }
-    } else {
-      for (int i = threadIdx.x; i < H; i += blockDim.x) dot += to_f(dyr[i]) * to_f(w[i]) * to_f(hr[i]);
-    }
+    for (int i = threadIdx.x; i < H; i += blockDim.x) dot += to_f(dyr[i]) * to_f(w[i]) * to_f(hr[i]);
     dot = block_sum(dot, red);
     const float mean_gn = dot * rs / H;  // mean(g * n)
-    if (VEC) {
-      for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-        float a[8], b[8], c[8], o[8];
-        ld8(dyr + i, a);
-        ld8(hr + i, b);
-        ld8(w + i, c);
-        float d[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-        if (dres) ld8(dres + row * H + i, d);
-#pragma unroll
-        for (int j = 0; j < 8; ++j) {
-          const float n = b[j] * rs;
-          o[j] = rs * (a[j] * c[j] - n * mean_gn) + d[j];
-          dwp[i + j] += a[j] * n;
-        }
-        st8(dx + row * H + i, o);
-      }
-    } else {
-      for (int i = threadIdx.x; i < H; i += blockDim.x) {
-        const float a = to_f(dyr[i]), n = to_f(hr[i]) * rs;
-        float o = rs * (a * to_f(w[i]) - n * mean_gn);
-        if (dres) o += to_f(dres[row * H + i]);
-        dx[row * H + i] = from_f<T>(o);
-        dwp[i] += a * n;
-      }
+    for (int i = threadIdx.x; i < H; i += blockDim.x) {
+      const float a = to_f(dyr[i]), n = to_f(hr[i]) * rs;
+      float o = rs * (a * to_f(w[i]) - n * mean_gn);
+      if (dres) o += to_f(dres[row * H + i]);
+      dx[row * H + i] = from_f<T>(o);
+      dwp[i] += a * n;
     }
   }
 }
 
-__global__ void colsum_kernel(const float* __restrict__ part, int nparts, int H, float* __restrict__ out) {
-  const int i = blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= H) return;
-  float s = 0.f;
-  for (int p = 0; p < nparts; ++p) s += part[static_cast<int64_t>(p) * H + i];
-  out[i] = s;
+// Vector form. A CTA owns a contiguous run of rows and streams them through a ring of shared-memory
+// stages filled by the TMA engine (one 1-D bulk copy per source row: dy, h and, when given, dres),
+// so several rows are in flight per CTA without holding them in registers. Each thread owns NCH
+// chunks of 8 columns, the same ones for every row, so its dW contribution stays in registers
+// for the whole run and is written once, as this CTA's partial row.
+// Per row there is exactly one CTA barrier. Before it, each thread reads its slice of the stage
+// (dot product g*h with g = dy*w, and the dW update, which needs no reduction); the barrier
+// completes the reduction; after it the thread reads the slice again and writes
+// dx = rs*g - c2*h (+ dres), c2 = rs^3 * mean(g*h). Row i's barrier also proves that every thread
+// finished row i-1, so that stage is refilled then (stages - 1 rows stay in flight ahead).
+// Every mbarrier wait is bounded; on a timeout (status raised) the CTA waits, again bounded, for
+// the copies it issued and returns without writing its partial.
+template <typename T, int NCH, bool RES>
+__global__ void __launch_bounds__(512, 1) rmsnorm_bwd_ring_kernel(
+    const T* __restrict__ dy, const T* __restrict__ h, const T* __restrict__ w, const float* __restrict__ rstd,
+    const T* __restrict__ dres, T* __restrict__ dx, float* __restrict__ dw_part, int64_t rows, int H,
+    int rows_per_block, int stages, int* status) {
+  extern __shared__ __align__(128) uint8_t ring_smem[];
+  __shared__ uint64_t full[8];
+  __shared__ __align__(16) float red[2][16];
+  constexpr int kSrc = RES ? 3 : 2;
+  const uint32_t row_bytes = static_cast<uint32_t>(H) * sizeof(T);
+  T* ring = reinterpret_cast<T*>(ring_smem);
+  const int64_t r0 = static_cast<int64_t>(blockIdx.x) * rows_per_block;
+  const int64_t r_end = rows < r0 + rows_per_block ? rows : r0 + rows_per_block;
+  const int n = r_end > r0 ? static_cast<int>(r_end - r0) : 0;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int nw4 = (blockDim.x + 127) >> 7;  // float4 groups of warp partials (blockDim <= 512: <= 4)
+  if (tid == 0) {
+    for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+    mbar_fence_init();
+  }
+  if (tid < 32) red[tid >> 4][tid & 15] = 0.f;  // unused warp slots read as zero
+  __syncthreads();
+  int issued = 0;  // rows whose copies were issued (thread 0 only)
+  auto issue_next = [&]() {
+    const int slot = issued % stages;
+    const int64_t row = r0 + issued;
+    mbar_expect_tx(&full[slot], kSrc * row_bytes);
+    T* base = ring + static_cast<int64_t>(slot) * kSrc * H;
+    bulk_load_1d(base, dy + row * H, row_bytes, &full[slot]);
+    bulk_load_1d(base + H, h + row * H, row_bytes, &full[slot]);
+    if (RES) bulk_load_1d(base + 2 * H, dres + row * H, row_bytes, &full[slot]);
+    ++issued;
+  };
+  if (tid == 0)
+    while (issued < stages && issued < n) issue_next();
+  float wv[NCH][8], dwa[NCH][8];
+  bool act[NCH];
+#pragma unroll
+  for (int c = 0; c < NCH; ++c) {
+    const int col = (c * blockDim.x + tid) * 8;
+    act[c] = col < H;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dwa[c][j] = wv[c][j] = 0.f;
+    if (act[c]) ld8(w + col, wv[c]);
+  }
+  const float inv_h = 1.f / static_cast<float>(H);
+  bool failed = false;
+  int i = 0;
+  for (; i < n; ++i) {
+    const int slot = i % stages;
+    const uint32_t parity = static_cast<uint32_t>(i / stages) & 1u;
+    const int64_t row = r0 + i;
+    const float rs = rstd[row];
+    const bool ok = mbar_wait(&full[slot], parity, status, kStatusTimeoutProducer);
+    const T* base = ring + static_cast<int64_t>(slot) * kSrc * H;
+    float dot = 0.f;
+    if (ok) {
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        if (!act[c]) continue;
+        const int col = (c * blockDim.x + tid) * 8;
+        float a[8], b[8];
+        ld8(base + col, a);
+        ld8(base + H + col, b);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          dot = fmaf(a[j] * wv[c][j], b[j], dot);
+          dwa[c][j] = fmaf(a[j] * rs, b[j], dwa[c][j]);
+        }
+      }
+    }
+    dot = warp_sum(dot);
+    if (lane == 0) red[i & 1][wid] = dot;
+    if (__syncthreads_or(!ok)) {
+      failed = true;
+      break;
+    }
+    // Every thread is past row i-1: its stage takes the next row.
+    if (tid == 0 && i >= 1 && issued < n) issue_next();
+    float tot = 0.f;
+    for (int k = 0; k < nw4; ++k) {
+      const float4 q = reinterpret_cast<const float4*>(red[i & 1])[k];
+      tot += (q.x + q.y) + (q.z + q.w);
+    }
+    const float c2 = rs * rs * rs * tot * inv_h;
+#pragma unroll
+    for (int c = 0; c < NCH; ++c) {
+      if (!act[c]) continue;
+      const int col = (c * blockDim.x + tid) * 8;
+      float a[8], b[8], d[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, o[8];
+      ld8(base + col, a);
+      ld8(base + H + col, b);
+      if (RES) ld8(base + 2 * H + col, d);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) o[j] = fmaf(-c2, b[j], fmaf(rs, a[j] * wv[c][j], d[j]));
+      st8(dx + row * H + col, o);
+    }
+  }
+  if (failed) {
+    // Drain: wait (bounded) for every copy issued and not consumed, then return.
+    if (tid == 0) {
+      for (int k = i; k < issued; ++k) {
+        const uint64_t t0 = globaltimer_ns();
+        while (!mbar_try_wait(&full[k % stages], static_cast<uint32_t>(k / stages) & 1u) &&
+               globaltimer_ns() - t0 < NTB_WAIT_LIMIT_NS) {
+        }
+      }
+    }
+    __syncthreads();
+    return;
+  }
+  float* dwp = dw_part + static_cast<int64_t>(blockIdx.x) * H;
+#pragma unroll
+  for (int c = 0; c < NCH; ++c)
+    if (act[c]) st8(dwp + (c * blockDim.x + tid) * 8, dwa[c]);
+}
+
+// out[i] (+)= sum over p of part[p, i], in a fixed order (deterministic for a given partial count).
+// A CTA covers 32 columns with 8 warps: lane = column, warps stride over the partial rows with four
+// loads in flight each, then the 8 warp sums are added in warp order. OutT is the stored type of
+// the result (the weight's dtype, or fp32); ACC adds into `out` (an fp32 gradient bucket).
+template <typename OutT, bool ACC>
+__global__ void __launch_bounds__(256) colsum_kernel(const float* __restrict__ part, int nparts, int H,
+                                                     OutT* __restrict__ out) {
+  __shared__ float acc_s[8][33];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int col = blockIdx.x * 32 + lane;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  if (col < H) {
+    int p = wid;
+    for (; p + 24 < nparts; p += 32) {
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc[u] += part[static_cast<int64_t>(p + 8 * u) * H + col];
+    }
+    for (int u = 0; p < nparts; p += 8, ++u) acc[u & 3] += part[static_cast<int64_t>(p) * H + col];
+  }
+  acc_s[wid][lane] = (acc[0] + acc[1]) + (acc[2] + acc[3]);
+  __syncthreads();
+  if (wid == 0 && col < H) {
+    float t = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) t += acc_s[k][lane];
+    if (ACC) t += to_f(out[col]);
+    out[col] = from_f<OutT>(t);
+  }
+}
+
+// Launch plan of the RMSNorm backward for `rows` x H: vector ring kernel when H % 8 == 0 and every
+// pointer is 16-byte aligned, else the scalar kernel. `max_parts` bounds the number of CTAs (one
+// partial row of `part` each). Returns the number of partial rows written, which colsum reduces.
+struct RmsBwdPlan {
+  bool ring = false;
+  int nch = 1, threads = 32, blocks = 1, rows_per_block = 1, stages = 2;
+  size_t smem = 0;
+};
+
+static RmsBwdPlan plan_rmsnorm_bwd(int64_t rows, int H, int elem_bytes, bool vec, bool res, int nsm, int max_parts) {
+  RmsBwdPlan p;
+  const int k_src = res ? 3 : 2;
+  const size_t stage_bytes = static_cast<size_t>(k_src) * H * elem_bytes;
+  const int chunks = (H + 7) / 8;
+  // Two 8-column chunks per thread (one when the row is narrow), at most 512 threads: the per-row
+  // cost (barrier, wait, cross-warp sum) is shared by 16 columns. Rows up to 8192 wide.
+  p.threads = std::min(512, ((chunks + 1) / 2 + 31) / 32 * 32);
+  p.nch = (chunks + p.threads - 1) / p.threads;
+  // Ring: at least two stages in the 200 KB a CTA may use, at most four.
+  const int fit = static_cast<int>(std::min<size_t>(4, (200u * 1024u) / std::max<size_t>(stage_bytes, 1)));
+  p.ring = vec && H % 8 == 0 && p.nch <= 2 && fit >= 2;
+  if (p.ring) {
+    p.stages = fit;
+    p.smem = p.stages * stage_bytes;
+    // Up to three CTAs per SM, as shared memory (about 220 KB usable) allows.
+    const int per_sm = static_cast<int>(std::max<size_t>(1, std::min<size_t>(3, (220u * 1024u) / p.smem)));
+    p.blocks = static_cast<int>(std::min<int64_t>({rows, static_cast<int64_t>(nsm) * per_sm,
+                                                   static_cast<int64_t>(max_parts)}));
+  } else {
+    p.threads = row_threads(H);
+    p.nch = 1;
+    p.blocks = static_cast<int>(std::min<int64_t>({rows, static_cast<int64_t>(nsm) * 4,
+                                                   static_cast<int64_t>(max_parts)}));
+  }
+  p.blocks = std::max(p.blocks, 1);
+  p.rows_per_block = static_cast<int>((rows + p.blocks - 1) / p.blocks);
+  return p;
+}
+
+template <typename T, int NCH, bool RES>
+static cudaError_t launch_ring(const RmsBwdPlan& p, const T* dy, const T* h, const T* w, const float* rstd,
+                               const T* dres, T* dx, float* part, int64_t rows, int H, int* status,
+                               cudaStream_t stream) {
+  auto kern = rmsnorm_bwd_ring_kernel<T, NCH, RES>;
+  // The dynamic shared-memory limit is raised once per device to the largest size seen so far.
+  static std::atomic<int> smem_set[64];
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::atomic<int>& cur = smem_set[dev & 63];
+  if (cur.load() < static_cast<int>(p.smem)) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(p.smem));
+    if (e != cudaSuccess) return e;
+    cur.store(static_cast<int>(p.smem));
+  }
+  kern<<<p.blocks, p.threads, p.smem, stream>>>(dy, h, w, rstd, dres, dx, part, rows, H, p.rows_per_block, p.stages,
+                                                status);
+  return cudaSuccess;
+}
+
+// Queues the two kernels of the RMSNorm backward (the per-CTA pass writing `part`, then the column
+// sum) and returns the first CUDA error of the set-up or launches. The column sum stores dW as T in
+// `dw_t`, or as fp32 in `dw_f32` (added to its contents when `accumulate`); exactly one is given.
+template <typename T>
+static cudaError_t launch_rmsnorm_bwd(const T* dy, const T* h, const T* w, const float* rstd, const T* dres, T* dx,
+                                      float* part, T* dw_t, float* dw_f32, bool accumulate, int64_t rows, int H,
+                                      bool vec, int nsm, int max_parts, int* status, cudaStream_t stream) {
+  const RmsBwdPlan p = plan_rmsnorm_bwd(rows, H, sizeof(T), vec, dres != nullptr, nsm, max_parts);
+  cudaError_t e = cudaSuccess;
+  if (p.ring) {
+    const bool r = dres != nullptr;
+    if (p.nch == 1) e = r ? launch_ring<T, 1, true>(p, dy, h, w, rstd, dres, dx, part, rows, H, status, stream)
+                          : launch_ring<T, 1, false>(p, dy, h, w, rstd, dres, dx, part, rows, H, status, stream);
+    else e = r ? launch_ring<T, 2, true>(p, dy, h, w, rstd, dres, dx, part, rows, H, status, stream)
+               : launch_ring<T, 2, false>(p, dy, h, w, rstd, dres, dx, part, rows, H, status, stream);
+  } else {
+    rmsnorm_bwd_scalar_kernel<T><<<p.blocks, p.threads, 0, stream>>>(dy, h, w, rstd, dres, dx, part, rows, H,
+                                                                     p.rows_per_block);
+  }
+  if (e != cudaSuccess) return e;
+  const int grid = (H + 31) / 32;
+  if (dw_f32 && accumulate) colsum_kernel<float, true><<<grid, 256, 0, stream>>>(part, p.blocks, H, dw_f32);
+  else if (dw_f32) colsum_kernel<float, false><<<grid, 256, 0, stream>>>(part, p.blocks, H, dw_f32);
+  else colsum_kernel<T, false><<<grid, 256, 0, stream>>>(part, p.blocks, H, dw_t);
+  return cudaGetLastError();
 }
 
 static bool vec8_ok(const at::Tensor& t, int64_t H) {
@@ -279,48 +491,63 @@ std::vector<at::Tensor> rmsnorm_fwd(const at::Tensor& x, const c10::optional<at:
 }
 
 // Returns (dx, dw). dres (optional) is added into dx (gradient flowing along the residual stream).
+// With dw_into (an fp32 tensor of H elements, e.g. the weight's main_grad view of a gradient bucket)
+// the weight gradient is added into it and the returned dw is undefined (None in Python).
 std::vector<at::Tensor> rmsnorm_bwd(const at::Tensor& dy, const at::Tensor& h, const at::Tensor& w,
-                                    const at::Tensor& rstd, const c10::optional<at::Tensor>& dres) {
+                                    const at::Tensor& rstd, const c10::optional<at::Tensor>& dres,
+                                    const c10::optional<at::Tensor>& dw_into) {
   TORCH_CHECK(dy.is_contiguous() && h.is_contiguous(), "rmsnorm_bwd: contiguous");
   const int64_t H = h.size(-1);
   const int64_t rows = h.numel() / H;
+  const bool into = dw_into.has_value();
+  if (into)
+    TORCH_CHECK(dw_into->is_cuda() && dw_into->scalar_type() == at::kFloat && dw_into->is_contiguous() &&
+                    dw_into->numel() == H,
+                "rmsnorm_bwd: dw_into must be a contiguous fp32 CUDA tensor of H elements");
   auto dx = at::empty_like(h);
-  auto dw = at::zeros({H}, h.options().dtype(at::kFloat));
-  if (rows == 0) return {dx, dw.to(w.scalar_type())};
-  const int nsm = num_sms(h.get_device());
-  const int blocks = static_cast<int>(std::min<int64_t>(rows, nsm * 4));
-  const int rpb = static_cast<int>((rows + blocks - 1) / blocks);
-  auto part = at::empty({blocks, H}, h.options().dtype(at::kFloat));
-  auto stream = at::cuda::getCurrentCUDAStream();
-  const int threads = row_threads(H);
+  at::Tensor dw = into ? at::Tensor() : at::empty({H}, w.options());
+  if (rows == 0) {
+    if (!into) dw.zero_();
+    return {dx, dw};
+  }
+  const int dev = h.get_device();
+  const int nsm = num_sms(dev);
   bool vec = vec8_ok(dy, H) && vec8_ok(h, H) && vec8_ok(w, H) && vec8_ok(dx, H);
   if (dres.has_value()) vec = vec && vec8_ok(*dres, H);
+  const int max_parts = 8 * nsm;
+  const RmsBwdPlan plan = plan_rmsnorm_bwd(rows, static_cast<int>(H), h.element_size(), vec, dres.has_value(), nsm,
+                                           max_parts);
+  auto part = at::empty({plan.blocks, H}, h.options().dtype(at::kFloat));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  cudaError_t e = cudaSuccess;
   NTB_DISPATCH_FLOAT(h.scalar_type(), "rmsnorm_bwd", [&] {
+    TORCH_CHECK(w.scalar_type() == h.scalar_type(), "rmsnorm_bwd: weight dtype");
     const scalar_t* dr = dres.has_value() ? P<scalar_t>(*dres) : nullptr;
-    if (vec)
-      rmsnorm_bwd_kernel<scalar_t, true><<<blocks, threads, 0, stream>>>(
-          P<scalar_t>(dy), P<scalar_t>(h), P<scalar_t>(w), rstd.data_ptr<float>(), dr,
-          P<scalar_t>(dx), part.data_ptr<float>(), rows, H, rpb);
-    else
-      rmsnorm_bwd_kernel<scalar_t, false><<<blocks, threads, 0, stream>>>(
-          P<scalar_t>(dy), P<scalar_t>(h), P<scalar_t>(w), rstd.data_ptr<float>(), dr,
-          P<scalar_t>(dx), part.data_ptr<float>(), rows, H, rpb);
+    e = launch_rmsnorm_bwd<scalar_t>(P<scalar_t>(dy), P<scalar_t>(h), P<scalar_t>(w), rstd.data_ptr<float>(), dr,
+                                     P<scalar_t>(dx), part.data_ptr<float>(), into ? nullptr : P<scalar_t>(dw),
+                                     into ? dw_into->data_ptr<float>() : nullptr, into, rows, static_cast<int>(H),
+                                     vec, nsm, max_parts, device_status(dev), stream);
   });
-  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(part.data_ptr<float>(), blocks, H, dw.data_ptr<float>());
-  NTB_LAUNCH_CHECK(2);
-  return {dx, dw.to(w.scalar_type())};
+  note_launches(2);
+  NTB_CUDA_CHECK(e);
+  return {dx, dw};
 }
 
 // ----------------------------------------------------------- allocation-free RMSNorm backward
-// Variant of rmsnorm_bwd for callers that cannot allocate (see no_alloc.h): the same two
-// kernels, with the per-block dW partials in a file-scope device array instead of a
-// per-call tensor. Each block overwrites its own partial row before accumulating into it,
-// so the array needs no initialisation.
+// Variant of rmsnorm_bwd for callers that cannot allocate (see no_alloc.h): the same kernels and
+// launch plan, with the per-CTA dW partials in a file-scope device array instead of a per-call
+// tensor, and at most kNoAllocBlocks CTAs. Each CTA overwrites its whole partial row, so the array
+// needs no initialisation.
 constexpr int kNoAllocBlocks = 128;
 static __device__ __align__(256) float g_rmsnorm_bwd_scratch[kNoAllocBlocks * NTB_NOALLOC_RMSNORM_MAX_H];
 
 constexpr int kNoAllocMaxDevices = 64;
-static float* g_noalloc_scratch_ptr[kNoAllocMaxDevices] = {};
+struct NoAllocSetup {
+  unsigned long long ctx_id = 0;  // cuCtxGetId of the context the address was resolved in (0: none)
+  float* scratch = nullptr;
+  int nsm = 0;
+};
+static NoAllocSetup g_noalloc_setup[kNoAllocMaxDevices];
 static std::mutex g_noalloc_mu;
 static thread_local char g_noalloc_err[256] = "";
 
@@ -330,6 +557,29 @@ static int noalloc_fail(int code, const char* what, cudaError_t e) {
   else
     std::snprintf(g_noalloc_err, sizeof(g_noalloc_err), "%s", what);
   return code;
+}
+
+// Id of the current context (unique for the process's lifetime, unlike the handle), through the
+// driver entry point so that the extension does not link against libcuda directly.
+static cudaError_t current_context_id(unsigned long long* id) {
+  using GetCurrent = CUresult (*)(CUcontext*);
+  using GetId = CUresult (*)(CUcontext, unsigned long long*);
+  static GetCurrent get_current = nullptr;
+  static GetId get_id = nullptr;
+  if (!get_current || !get_id) {
+    void* f1 = nullptr;
+    void* f2 = nullptr;
+    cudaDriverEntryPointQueryResult q1, q2;
+    cudaError_t e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &f1, cudaEnableDefault, &q1);
+    if (e != cudaSuccess || q1 != cudaDriverEntryPointSuccess) return e != cudaSuccess ? e : cudaErrorNotSupported;
+    e = cudaGetDriverEntryPoint("cuCtxGetId", &f2, cudaEnableDefault, &q2);
+    if (e != cudaSuccess || q2 != cudaDriverEntryPointSuccess) return e != cudaSuccess ? e : cudaErrorNotSupported;
+    get_current = reinterpret_cast<GetCurrent>(f1);
+    get_id = reinterpret_cast<GetId>(f2);
+  }
+  CUcontext ctx = nullptr;
+  if (get_current(&ctx) != CUDA_SUCCESS || ctx == nullptr) return cudaErrorDeviceUninitialized;
+  return get_id(ctx, id) == CUDA_SUCCESS ? cudaSuccess : cudaErrorDeviceUninitialized;
 }
 
 }  // namespace ntb
@@ -349,42 +599,44 @@ extern "C" __attribute__((visibility("default"))) int ntb_rmsnorm_bwd_bf16_noall
                   static_cast<long long>(rows), NTB_NOALLOC_RMSNORM_MAX_H);
     return 1;
   }
+  // An error left by earlier work on this thread is reported as such and left pending for its owner.
+  cudaError_t e = cudaPeekAtLastError();
+  if (e != cudaSuccess) return noalloc_fail(3, "an earlier CUDA error is pending (not cleared)", e);
   int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return noalloc_fail(2, "cudaGetDevice", e);
   if (dev < 0 || dev >= kNoAllocMaxDevices) return noalloc_fail(2, "device index beyond the set-up table", cudaSuccess);
-  float* scratch = nullptr;
+  unsigned long long ctx_id = 0;
+  e = current_context_id(&ctx_id);
+  if (e != cudaSuccess) return noalloc_fail(2, "cuCtxGetCurrent / cuCtxGetId", e);
+  NoAllocSetup setup;
   {
-    // One-time set-up per device, with that device current: resolve the scratch array's address.
+    // Set-up per device and context, with that device current: resolve the scratch array's
+    // address. A new context on the device (after cudaDeviceReset, say) resolves it again.
     std::lock_guard<std::mutex> lock(g_noalloc_mu);
-    if (g_noalloc_scratch_ptr[dev] == nullptr) {
+    NoAllocSetup& s = g_noalloc_setup[dev];
+    if (s.ctx_id != ctx_id || s.scratch == nullptr) {
       void* ptr = nullptr;
       e = cudaGetSymbolAddress(&ptr, g_rmsnorm_bwd_scratch);
       if (e != cudaSuccess) return noalloc_fail(2, "cudaGetSymbolAddress(scratch)", e);
-      g_noalloc_scratch_ptr[dev] = static_cast<float*>(ptr);
+      int nsm = 0;
+      e = cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+      if (e != cudaSuccess) return noalloc_fail(2, "cudaDeviceGetAttribute(SM count)", e);
+      s.scratch = static_cast<float*>(ptr);
+      s.nsm = nsm;
+      s.ctx_id = ctx_id;
     }
-    scratch = g_noalloc_scratch_ptr[dev];
+    setup = s;
   }
   g_noalloc_err[0] = '\0';
   if (rows == 0) return 0;
-  const int blocks = static_cast<int>(rows < kNoAllocBlocks ? rows : kNoAllocBlocks);
-  const int rpb = static_cast<int>((rows + blocks - 1) / blocks);
-  const int threads = row_threads(H);
   const bool vec = (H % 8 == 0) && ((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(h) |
                                      reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(dx) |
                                      (dres ? reinterpret_cast<uintptr_t>(dres) : 0)) &
                                     15) == 0;
-  const T* dr = static_cast<const T*>(dres);
-  if (vec)
-    rmsnorm_bwd_kernel<T, true><<<blocks, threads, 0, stream>>>(
-        static_cast<const T*>(dy), static_cast<const T*>(h), static_cast<const T*>(w), rstd, dr, static_cast<T*>(dx),
-        scratch, rows, H, rpb);
-  else
-    rmsnorm_bwd_kernel<T, false><<<blocks, threads, 0, stream>>>(
-        static_cast<const T*>(dy), static_cast<const T*>(h), static_cast<const T*>(w), rstd, dr, static_cast<T*>(dx),
-        scratch, rows, H, rpb);
-  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(scratch, blocks, H, dw);
-  e = cudaGetLastError();
+  e = launch_rmsnorm_bwd<T>(static_cast<const T*>(dy), static_cast<const T*>(h), static_cast<const T*>(w), rstd,
+                            static_cast<const T*>(dres), static_cast<T*>(dx), setup.scratch, nullptr, dw, false, rows,
+                            H, vec, setup.nsm, kNoAllocBlocks, nullptr, stream);
   if (e != cudaSuccess) return noalloc_fail(2, "kernel launch", e);
   return 0;
 }
@@ -491,8 +743,10 @@ std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x,
         P<scalar_t>(dyc), P<scalar_t>(x), P<scalar_t>(w), mean.data_ptr<float>(),
         rstd.data_ptr<float>(), P<scalar_t>(dx), pw.data_ptr<float>(), pb.data_ptr<float>(), rows, H, rpb);
   });
-  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(pw.data_ptr<float>(), blocks, H, dw.data_ptr<float>());
-  colsum_kernel<<<(H + 255) / 256, 256, 0, stream>>>(pb.data_ptr<float>(), blocks, H, db.data_ptr<float>());
+  colsum_kernel<float, false><<<(H + 31) / 32, 256, 0, stream>>>(pw.data_ptr<float>(), blocks, H,
+                                                                  dw.data_ptr<float>());
+  colsum_kernel<float, false><<<(H + 31) / 32, 256, 0, stream>>>(pb.data_ptr<float>(), blocks, H,
+                                                                  db.data_ptr<float>());
   NTB_LAUNCH_CHECK(3);
   return {dx, dw.to(w.scalar_type()), db.to(w.scalar_type())};
 }

@@ -15,6 +15,20 @@ def _native(t):
     return t.is_cuda and t.dtype in (torch.bfloat16, torch.float32)
 
 
+def _rmsnorm_bwd(dy, h, weight, rstd, dres):
+    """(dx, dw) of the RMSNorm; when the weight carries an fp32 ``main_grad`` view of a gradient
+    bucket, dW is added into it by the column-sum kernel and dw is None (as for the linears)."""
+    mg = getattr(weight, "main_grad", None)
+    into = mg if (mg is not None and mg.dtype == torch.float32 and mg.is_cuda and mg.is_contiguous()) else None
+    dx, dw = ext().rmsnorm_bwd(dy.contiguous(), h, weight.contiguous(), rstd, dres, into)
+    if into is not None:
+        hook = getattr(weight, "_ntb_grad_ready_hook", None)
+        if hook is not None:
+            hook(weight)
+        return dx, None
+    return dx, dw
+
+
 class _RMSNormFn(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, weight, eps):
@@ -26,7 +40,7 @@ class _RMSNormFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         h, weight, rstd = ctx.saved_tensors
-        dx, dw = ext().rmsnorm_bwd(dy.contiguous(), h, weight.contiguous(), rstd, None)
+        dx, dw = _rmsnorm_bwd(dy, h, weight, rstd, None)
         return dx, dw, None
 
 
@@ -42,8 +56,7 @@ class _AddRMSNormFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy, dh):
         h, weight, rstd = ctx.saved_tensors
-        dx, dw = ext().rmsnorm_bwd(dy.contiguous(), h, weight.contiguous(), rstd,
-                                   dh.contiguous() if dh is not None else None)
+        dx, dw = _rmsnorm_bwd(dy, h, weight, rstd, dh.contiguous() if dh is not None else None)
         return dx, dx, dw, None
 
 

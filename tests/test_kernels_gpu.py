@@ -107,6 +107,51 @@ def test_rmsnorm(dtype, H):
     assert rel_err(y2, xr * torch.rsqrt(xr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr) < tol
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("rows,H", [(5003, 4096), (4099, 2048), (3001, 1536), (2999, 512), (1201, 8192),
+                                    (777, 7168), (9, 4096)])
+@pytest.mark.parametrize("with_res", [False, True])
+def test_rmsnorm_bwd_many_rows(dtype, rows, H, with_res):
+    """Each CTA streams many rows through its shared-memory ring (stage reuse, parity flips,
+    a remainder of rows in the last CTA); checked against fp32 PyTorch autograd."""
+    from nano_train_b200.ops._ext import check_status, ext
+    g = torch.Generator(device="cuda").manual_seed(rows * 7 + H)
+    h = torch.randn(rows, H, device="cuda", dtype=dtype, generator=g)
+    w = (1 + 0.1 * torch.randn(H, device="cuda", generator=g)).to(dtype)
+    dy = torch.randn(rows, H, device="cuda", dtype=dtype, generator=g)
+    dres = torch.randn(rows, H, device="cuda", dtype=dtype, generator=g) if with_res else None
+    rstd = torch.rsqrt(h.float().pow(2).mean(-1) + 1e-5).contiguous()
+    dx, dw = ext().rmsnorm_bwd(dy, h, w, rstd, dres)
+    check_status(0)
+    hf = h.float().requires_grad_(True)
+    wf = w.float().requires_grad_(True)
+    (hf * torch.rsqrt(hf.pow(2).mean(-1, keepdim=True) + 1e-5) * wf).backward(dy.float())
+    ref_dx = hf.grad + (dres.float() if with_res else 0)
+    tol = 1e-2 if dtype == torch.bfloat16 else 1e-5
+    assert rel_err(dx, ref_dx) < tol
+    assert rel_err(dw, wf.grad) < tol
+
+
+def test_rmsnorm_weight_grad_into_main_grad():
+    """A weight with an fp32 main_grad bucket view gets dW added there (no .grad, no bf16 rounding)."""
+    from nano_train_b200.ops.norm import add_rms_norm
+    H, rows = 2048, 3000
+    x = torch.randn(rows, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    r = torch.randn(rows, H, device="cuda", dtype=torch.bfloat16, requires_grad=True)
+    w = torch.nn.Parameter((1 + 0.1 * torch.randn(H, device="cuda")).to(torch.bfloat16))
+    w.main_grad = torch.full((H,), 0.5, device="cuda")
+    ready = []
+    w._ntb_grad_ready_hook = lambda p: ready.append(p)
+    y, h = add_rms_norm(x, r, w, 1e-5)
+    gy = torch.randn_like(y)
+    (y * gy).sum().backward()
+    assert w.grad is None and len(ready) == 1
+    hr = (x.detach().float() + r.detach().float())
+    wr = w.detach().float().requires_grad_()
+    (hr * torch.rsqrt(hr.pow(2).mean(-1, keepdim=True) + 1e-5) * wr * gy.float()).sum().backward()
+    assert rel_err(w.main_grad - 0.5, wr.grad) < 1e-2
+
+
 def test_layernorm():
     from nano_train_b200.ops.norm import layer_norm
     x = torch.randn(32, 192, device="cuda", requires_grad=True)
