@@ -1,134 +1,169 @@
-"""Argument validation for the 4-D runtime path.
+"""Argument validation for the 4-D runtime path, as an ordered table of rules.
 
-Same checks and error texts as the reference (src/runtime/validation.py:9-191)
-so existing scripts and tests see identical failures. Two guards relax when
-the B200-build option ``--expert-layout fold_dp`` is given (EP carved out of
-the data-parallel axis, Megatron style): TP>1 with EP>1 becomes legal, and
-dropout under TP/EP is allowed because expert replicas synchronise over the
-expert-data-parallel group.
+Each ``Rule`` states one constraint on the parsed arguments as a predicate over a ``_Layout`` (the
+arguments plus the derived quantities: the model-parallel product, the expert axis that counts
+against the world size, the data-parallel size); ``validate_args`` walks the table in order and
+raises ``ValueError`` with the first broken rule's message. The rule set and the message texts are
+those of the reference (src/runtime/validation.py:9-191), because existing launch scripts and
+tests match on the texts; the table form is this framework's.
+
+Two rules relax under ``--expert-layout fold_dp`` (EP carved out of the data-parallel axis, Megatron
+style): TP > 1 with EP > 1 becomes legal, and dropout under TP / EP is allowed because expert
+replicas synchronise over the expert-data-parallel group. In exchange the data-parallel size must
+split into EP groups.
 """
 from __future__ import annotations
 
 import argparse
-from typing import Optional
+from dataclasses import dataclass
+from typing import Callable, Optional, Union
+
+SHARDING_STRATEGIES = ("no_shard", "optim", "optim_grads", "optim_grads_params")
 
 
 def parse_pp_layer_splits(raw_splits: Optional[str]) -> Optional[tuple[int, ...]]:
-    if raw_splits is None:
-        return None
-    text = raw_splits.strip()
-    if not text:
-        return None
-    parts = [p.strip() for p in text.split(",") if p.strip()]
-    if not parts:
+    """``"0,3,8"`` -> ``(0, 3, 8)``; None or a blank / comma-only string -> None."""
+    fields = [f.strip() for f in (raw_splits or "").split(",")]
+    fields = [f for f in fields if f]
+    if not fields:
         return None
     try:
-        return tuple(int(p) for p in parts)
-    except ValueError as exc:
-        raise ValueError("pp_layer_splits must be a comma-separated integer list") from exc
+        return tuple(int(f) for f in fields)
+    except ValueError:
+        raise ValueError("pp_layer_splits must be a comma-separated integer list") from None
 
 
-def _fold(args) -> bool:
-    return getattr(args, "expert_layout", "separate") == "fold_dp"
+@dataclass(frozen=True)
+class _Layout:
+    a: argparse.Namespace
+    world: int
+    splits: Optional[tuple[int, ...]]
+
+    @property
+    def fold(self) -> bool:
+        return getattr(self.a, "expert_layout", "separate") == "fold_dp"
+
+    @property
+    def mp(self) -> int:
+        """Ranks of one model replica: TP x PP x CP, times EP unless EP is folded into DP."""
+        ep_axis = 1 if self.fold else self.a.expert_model_parallel_size
+        return (self.a.tensor_model_parallel_size * self.a.pipeline_model_parallel_size * ep_axis
+                * self.a.context_parallel_size)
+
+    @property
+    def tp_ep(self) -> bool:
+        return self.a.tensor_model_parallel_size > 1 or self.a.expert_model_parallel_size > 1
+
+    def get(self, name: str, default):
+        return getattr(self.a, name, default)
 
 
-def _validate_parallel_factorization(args: argparse.Namespace, world_size: int) -> None:
-    sizes = (args.tensor_model_parallel_size, args.pipeline_model_parallel_size, args.expert_model_parallel_size,
-             args.context_parallel_size)
-    if any(s < 1 for s in sizes):
-        raise ValueError("parallel sizes must be >= 1")
-    ep_axis = 1 if _fold(args) else args.expert_model_parallel_size
-    mp = args.tensor_model_parallel_size * args.pipeline_model_parallel_size * ep_axis * args.context_parallel_size
-    if mp > world_size:
-        raise ValueError("tensor*pipeline*expert*context cannot exceed world_size")
-    if world_size % mp != 0:
-        raise ValueError(f"world_size ({world_size}) must be divisible by tensor*pipeline*expert*context ({mp})")
-    if _fold(args):
-        dp = world_size // mp
-        if dp % args.expert_model_parallel_size != 0:
-            raise ValueError("data_parallel_size must be divisible by expert_model_parallel_size with fold_dp")
+Message = Union[str, Callable[[_Layout], str]]
 
 
-def _validate_model_dimension_compatibility(args: argparse.Namespace) -> None:
-    tp = max(1, args.tensor_model_parallel_size)
-    if args.intermediate_size % tp != 0:
-        raise ValueError("intermediate_size must be divisible by tensor_model_parallel_size")
-    if args.num_heads % tp != 0:
-        raise ValueError("num_heads must be divisible by tensor_model_parallel_size")
-    if args.num_experts % args.expert_model_parallel_size != 0:
-        raise ValueError("num_experts must be divisible by expert_model_parallel_size")
-    if args.seq_len < 2:
-        raise ValueError("seq_len must be >= 2 for causal LM loss")
-    if args.tensor_model_parallel_size > 1 and args.seq_len % args.tensor_model_parallel_size != 0:
-        raise ValueError("seq_len must be divisible by tensor_model_parallel_size for sequence-parallel MoE")
+@dataclass(frozen=True)
+class Rule:
+    broken: Callable[[_Layout], bool]
+    message: Message
+
+    def text(self, lay: _Layout) -> str:
+        return self.message(lay) if callable(self.message) else self.message
 
 
-def _validate_tutorial_guards(args: argparse.Namespace) -> None:
-    if args.context_parallel_size != 1:
-        raise ValueError("context_parallel_size > 1 is not yet implemented in this tutorial")
-    if args.expert_tensor_parallel_size != 1:
-        raise ValueError("expert_tensor_parallel_size must be 1 in this tutorial")
-    if args.tensor_model_parallel_size > 1 and args.expert_model_parallel_size > 1 and not _fold(args):
-        raise ValueError(
-            "This tutorial disallows tensor_model_parallel_size>1 with expert_model_parallel_size>1 when "
-            "expert_tensor_parallel_size=1. That setup replicates expert shards across TP lanes. "
-            "Use tensor_model_parallel_size=1 for MoE EP runs.")
-    if args.dropout > 0.0 and (args.tensor_model_parallel_size > 1 or args.expert_model_parallel_size > 1) \
-            and not _fold(args):
-        raise ValueError(
-            "dropout must be 0.0 when tensor_model_parallel_size>1 or expert_model_parallel_size>1 in this "
-            "tutorial. This keeps replicated non-sharded parameter paths deterministic without extra "
-            "model-parallel gradient synchronization.")
+def _sizes(lay: _Layout) -> tuple[int, ...]:
+    a = lay.a
+    return (a.tensor_model_parallel_size, a.pipeline_model_parallel_size, a.expert_model_parallel_size,
+            a.context_parallel_size)
 
 
-def _validate_zero_optimizer_settings(args: argparse.Namespace) -> None:
-    strategy = args.data_parallel_sharding_strategy
-    if strategy not in {"no_shard", "optim", "optim_grads", "optim_grads_params"}:
-        raise ValueError("data_parallel_sharding_strategy must be one of no_shard, optim, optim_grads, "
-                         "optim_grads_params")
-    if strategy == "optim_grads_params":
-        raise ValueError("optim_grads_params (ZeRO-3) is out of scope in this tutorial. "
-                         "Use no_shard, optim, or optim_grads.")
-    if args.num_distributed_optimizer_instances != 1:
-        raise ValueError("num_distributed_optimizer_instances must be 1 in this tutorial implementation")
-    if strategy != "no_shard" and not args.use_distributed_optimizer:
-        raise ValueError("use_distributed_optimizer must be enabled when sharding strategy is not no_shard")
-    if args.use_distributed_optimizer and strategy == "no_shard":
-        raise ValueError("When use_distributed_optimizer is set, select sharding strategy optim or optim_grads")
-    if bool(getattr(args, "zero_debug", False)) and not args.use_distributed_optimizer:
-        raise ValueError("zero_debug requires use_distributed_optimizer=True")
-    if int(getattr(args, "zero_debug_max_steps", 1)) < 1:
-        raise ValueError("zero_debug_max_steps must be >= 1")
-    if int(getattr(args, "zero_debug_max_params", 8)) < 1:
-        raise ValueError("zero_debug_max_params must be >= 1")
+def _splits_broken(lay: _Layout) -> Optional[str]:
+    s = lay.splits
+    if s is None:
+        return None
+    if len(s) != lay.a.pipeline_model_parallel_size + 1:
+        return "pp_layer_splits length must equal pipeline_model_parallel_size + 1"
+    if s[0] != 0:
+        return "pp_layer_splits must start with 0"
+    if s[-1] != lay.a.num_layers:
+        return "pp_layer_splits must end at num_layers"
+    if any(b <= a for a, b in zip(s, s[1:])):
+        return "pp_layer_splits must be strictly increasing"
+    return None
 
 
-def _validate_pipeline_batching(args: argparse.Namespace, pp_layer_splits: Optional[tuple[int, ...]]) -> None:
-    if args.num_microbatches < 1:
-        raise ValueError("num_microbatches must be >= 1")
-    if args.batch_size % args.num_microbatches != 0:
-        raise ValueError("batch_size must be divisible by num_microbatches for fixed-shape 1F1B")
-    if pp_layer_splits is not None:
-        if len(pp_layer_splits) != args.pipeline_model_parallel_size + 1:
-            raise ValueError("pp_layer_splits length must equal pipeline_model_parallel_size + 1")
-        if pp_layer_splits[0] != 0:
-            raise ValueError("pp_layer_splits must start with 0")
-        if pp_layer_splits[-1] != args.num_layers:
-            raise ValueError("pp_layer_splits must end at num_layers")
-        for i in range(1, len(pp_layer_splits)):
-            if pp_layer_splits[i] <= pp_layer_splits[i - 1]:
-                raise ValueError("pp_layer_splits must be strictly increasing")
+_TP_EP_MSG = ("This tutorial disallows tensor_model_parallel_size>1 with expert_model_parallel_size>1 when "
+              "expert_tensor_parallel_size=1. That setup replicates expert shards across TP lanes. "
+              "Use tensor_model_parallel_size=1 for MoE EP runs.")
+_DROPOUT_MSG = ("dropout must be 0.0 when tensor_model_parallel_size>1 or expert_model_parallel_size>1 in this "
+                "tutorial. This keeps replicated non-sharded parameter paths deterministic without extra "
+                "model-parallel gradient synchronization.")
+
+RULES: tuple[Rule, ...] = (
+    # parallel factorisation
+    Rule(lambda l: any(s < 1 for s in _sizes(l)), "parallel sizes must be >= 1"),
+    Rule(lambda l: l.mp > l.world, "tensor*pipeline*expert*context cannot exceed world_size"),
+    Rule(lambda l: l.world % l.mp != 0,
+         lambda l: f"world_size ({l.world}) must be divisible by tensor*pipeline*expert*context ({l.mp})"),
+    Rule(lambda l: l.fold and (l.world // l.mp) % l.a.expert_model_parallel_size != 0,
+         "data_parallel_size must be divisible by expert_model_parallel_size with fold_dp"),
+    # model dimensions against the parallel sizes
+    Rule(lambda l: l.a.intermediate_size % max(1, l.a.tensor_model_parallel_size) != 0,
+         "intermediate_size must be divisible by tensor_model_parallel_size"),
+    Rule(lambda l: l.a.num_heads % max(1, l.a.tensor_model_parallel_size) != 0,
+         "num_heads must be divisible by tensor_model_parallel_size"),
+    Rule(lambda l: l.a.num_experts % l.a.expert_model_parallel_size != 0,
+         "num_experts must be divisible by expert_model_parallel_size"),
+    Rule(lambda l: l.a.seq_len < 2, "seq_len must be >= 2 for causal LM loss"),
+    Rule(lambda l: l.a.tensor_model_parallel_size > 1 and l.a.seq_len % l.a.tensor_model_parallel_size != 0,
+         "seq_len must be divisible by tensor_model_parallel_size for sequence-parallel MoE"),
+    # features the runtime does not have
+    Rule(lambda l: l.a.context_parallel_size != 1, "context_parallel_size > 1 is not yet implemented in this tutorial"),
+    Rule(lambda l: l.a.expert_tensor_parallel_size != 1, "expert_tensor_parallel_size must be 1 in this tutorial"),
+    Rule(lambda l: l.a.tensor_model_parallel_size > 1 and l.a.expert_model_parallel_size > 1 and not l.fold,
+         _TP_EP_MSG),
+    Rule(lambda l: l.a.dropout > 0.0 and l.tp_ep and not l.fold, _DROPOUT_MSG),
+    # ZeRO / distributed optimizer
+    Rule(lambda l: l.a.data_parallel_sharding_strategy not in SHARDING_STRATEGIES,
+         "data_parallel_sharding_strategy must be one of no_shard, optim, optim_grads, optim_grads_params"),
+    Rule(lambda l: l.a.data_parallel_sharding_strategy == "optim_grads_params",
+         "optim_grads_params (ZeRO-3) is out of scope in this tutorial. Use no_shard, optim, or optim_grads."),
+    Rule(lambda l: l.a.num_distributed_optimizer_instances != 1,
+         "num_distributed_optimizer_instances must be 1 in this tutorial implementation"),
+    Rule(lambda l: l.a.data_parallel_sharding_strategy != "no_shard" and not l.a.use_distributed_optimizer,
+         "use_distributed_optimizer must be enabled when sharding strategy is not no_shard"),
+    Rule(lambda l: l.a.use_distributed_optimizer and l.a.data_parallel_sharding_strategy == "no_shard",
+         "When use_distributed_optimizer is set, select sharding strategy optim or optim_grads"),
+    Rule(lambda l: bool(l.get("zero_debug", False)) and not l.a.use_distributed_optimizer,
+         "zero_debug requires use_distributed_optimizer=True"),
+    Rule(lambda l: int(l.get("zero_debug_max_steps", 1)) < 1, "zero_debug_max_steps must be >= 1"),
+    Rule(lambda l: int(l.get("zero_debug_max_params", 8)) < 1, "zero_debug_max_params must be >= 1"),
+    # 1F1B batching and stage boundaries (precision flags are checked where precision is resolved)
+    Rule(lambda l: l.a.num_microbatches < 1, "num_microbatches must be >= 1"),
+    Rule(lambda l: l.a.batch_size % l.a.num_microbatches != 0,
+         "batch_size must be divisible by num_microbatches for fixed-shape 1F1B"),
+    Rule(lambda l: _splits_broken(l) is not None, lambda l: _splits_broken(l)),
+)
 
 
-def _validate_precision_args(args: argparse.Namespace) -> None:
-    """Precision flags are validated where precision is resolved."""
-    del args
+def broken_rules(args: argparse.Namespace, world_size: int,
+                 pp_layer_splits: Optional[tuple[int, ...]]) -> list[str]:
+    """Messages of every rule the arguments break, in table order (to report all of them at once).
+    A rule that cannot be evaluated (a division by a zero parallel size, itself reported by the
+    first rule) is skipped."""
+    lay = _Layout(args, world_size, pp_layer_splits)
+    out = []
+    for rule in RULES:
+        try:
+            if rule.broken(lay):
+                out.append(rule.text(lay))
+        except ZeroDivisionError:
+            continue
+    return out
 
 
 def validate_args(args: argparse.Namespace, world_size: int, pp_layer_splits: Optional[tuple[int, ...]]) -> None:
-    _validate_parallel_factorization(args, world_size)
-    _validate_model_dimension_compatibility(args)
-    _validate_tutorial_guards(args)
-    _validate_zero_optimizer_settings(args)
-    _validate_pipeline_batching(args, pp_layer_splits)
-    _validate_precision_args(args)
+    """Raise ValueError with the first broken rule's message."""
+    lay = _Layout(args, world_size, pp_layer_splits)
+    for rule in RULES:
+        if rule.broken(lay):
+            raise ValueError(rule.text(lay))
