@@ -52,14 +52,10 @@ def collect_param_shard_info(model: nn.Module, tensor_model_parallel_group=None)
                     ep_ids.add(id(p))
     store = get_lowbit_master_store(model)
     if store is not None:
-        for key, meta in store.metadata.items():
-            if key not in store.masters:
-                continue
-            p = store.masters[key]
-            if meta.shard_domain == "tensor_model_parallel":
-                tp_ids.add(id(p))
-            elif meta.shard_domain == "expert_model_parallel":
-                ep_ids.add(id(p))
+        from ..precision.master_store import EXPERT, TENSOR
+
+        tp_ids.update(id(p) for p in store.params_in(TENSOR))
+        ep_ids.update(id(p) for p in store.params_in(EXPERT))
     return ParamShardInfo(tensor_model_parallel_sharded_param_ids=tp_ids, expert_model_parallel_sharded_param_ids=ep_ids)
 
 
