@@ -235,15 +235,12 @@ def pipeline_backward_microbatch(microbatch_idx: int, model, peers: PipelinePeer
 
 def execute_1f1b_schedule(parallel, num_microbatches: int, run_forward: Callable[[int], None],
                           run_backward: Callable[[int], None]) -> None:
-    warm = min(parallel.pipeline_model_parallel_size - parallel.pipeline_model_parallel_rank - 1, num_microbatches)
-    rest = num_microbatches - warm
-    for i in range(warm):
-        run_forward(i)
-    for i in range(rest):
-        run_forward(i + warm)
-        run_backward(i)
-    for i in range(warm):
-        run_backward(rest + i)
+    """Run this stage's forwards and backwards in 1F1B order (runtime/schedules/pipeline_1f1b.py)."""
+    from ..runtime.schedules.pipeline_1f1b import one_f_one_b
+
+    for kind, mb in one_f_one_b(parallel.pipeline_model_parallel_size, parallel.pipeline_model_parallel_rank,
+                                num_microbatches):
+        (run_forward if kind == "F" else run_backward)(mb)
 
 
 def finalize_pipeline_sends(state: PipelineStepState) -> None:
