@@ -76,6 +76,10 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--profile-dir", default=None,
+                    help="after the timed phases, profile one more step on rank 0 (torch.profiler; every rank "
+                         "runs the step) and write its kernel table and GPU-busy fraction here; no number of "
+                         "the bench line is taken under the profiler")
     ap.add_argument("--config", choices=sorted(CONFIGS), default="llama8b-tp",
                     help="benchmark configuration (default: the headline Llama-3-8B-shape TP run)")
     ap.add_argument("--layers", type=int, default=None, help="override layer count (not a valid headline run)")
@@ -399,7 +403,8 @@ def run_ours(args, rank, local, world):
         a = get_communicator(dist.group.WORLD)
         if a is not None and hasattr(a, "choice"):
             fused_paths = {f"{k[0]} x{list(k[1])} w{list(k[2])}{' bmn' if k[3] else ''}":
-                           {"path": v, "ms": a.timings.get(k, {})} for k, v in a.choice.items()}
+                           {"path": v, "ms": a.timings.get(k, {}), "rel_err": getattr(a, "rel_err", {}).get(k, {})}
+                           for k, v in a.choice.items()}
 
     e2e = None
     if not args.no_e2e:
@@ -417,7 +422,58 @@ def run_ours(args, rank, local, world):
                "h2d_bytes_per_step": 2 * rows * args.seq * 8, "d2h_bytes_per_step": 4,
                "api": ("DeepSeekModel + FlatAdamW step (bench.py _MoETrainer)" if args.config == "dsv2lite-fp8-ep"
                        else "nano_train_b200.training.LMTrainer.train_step")}
+    if args.profile_dir:
+        profile_one_step(args, rank, world, trainer, batches)
     return ms, layers, launches, sampler.summary(), e2e, fused_paths
+
+
+def profile_one_step(args, rank, world, trainer, batches):
+    """One extra step with torch.profiler on rank 0: the top kernels by device time, and how much of
+    the step's wall time the GPU was busy (the union of kernel intervals). A low busy fraction means
+    the host (Python, launches) limits the step."""
+    from torch.profiler import ProfilerActivity, profile
+
+    os.makedirs(args.profile_dir, exist_ok=True)
+    barrier(world)
+    a, b = batches[0]
+    if rank != 0:
+        trainer.train_step(a, b)
+        torch.cuda.synchronize()
+        barrier(world)
+        return
+    with profile(activities=[ProfilerActivity.CPU, ProfilerActivity.CUDA]) as prof:
+        t0 = time.perf_counter()
+        trainer.train_step(a, b)
+        torch.cuda.synchronize()
+        wall_us = (time.perf_counter() - t0) * 1e6
+    barrier(world)
+    kern = [e for e in prof.events() if e.device_type.name == "CUDA" and e.time_range.elapsed_us() > 0]
+    iv = sorted((e.time_range.start, e.time_range.end) for e in kern)
+    busy, cur_s, cur_e = 0.0, None, None
+    for s_, e_ in iv:
+        if cur_e is None or s_ > cur_e:
+            if cur_e is not None:
+                busy += cur_e - cur_s
+            cur_s, cur_e = s_, e_
+        else:
+            cur_e = max(cur_e, e_)
+    if cur_e is not None:
+        busy += cur_e - cur_s
+    span = (iv[-1][1] - iv[0][0]) if iv else 0.0
+    by_name = {}
+    for e in kern:
+        by_name.setdefault(e.name, [0, 0.0])
+        by_name[e.name][0] += 1
+        by_name[e.name][1] += e.time_range.elapsed_us()
+    top = sorted(by_name.items(), key=lambda kv: -kv[1][1])[:40]
+    tot = sum(v[1] for v in by_name.values())
+    lines = [f"config {args.config} n_gpus {world} seq {args.seq}",
+             f"step wall {wall_us / 1e3:.1f} ms; kernel span {span / 1e3:.1f} ms; GPU busy (union of kernels) "
+             f"{busy / 1e3:.1f} ms = {busy / max(span, 1e-9):.2f} of the span; {len(kern)} kernels",
+             "", "| kernel | launches | device ms | share |", "|---|---|---|---|"]
+    lines += [f"| {n[:110]} | {c} | {t / 1e3:.2f} | {t / max(tot, 1e-9):.3f} |" for n, (c, t) in top]
+    with open(os.path.join(args.profile_dir, f"step_profile_n{world}_{args.config}.md"), "w") as f:
+        f.write("\n".join(lines) + "\n")
 
 
 def tokens_per_step(args, world):
@@ -426,6 +482,43 @@ def tokens_per_step(args, world):
     if args.config == "deepseek-4d":  # 8 microbatches per data-parallel replica, DP = world / (TP x PP) = 2
         return per_rank * (world // 4) * args.seq
     return (per_rank * world if per_rank else GLOBAL_BATCH) * args.seq
+
+
+def _mla_moe_flops_per_token(H, heads, q_lora, kv_lora, nope, rope, vdim, ffn_active):
+    """Forward matmul FLOPs per token of one MLA + feed-forward layer (2 x multiply-adds)."""
+    qk = nope + rope
+    attn = H * q_lora + q_lora * heads * qk + H * (kv_lora + rope) + kv_lora * heads * (nope + vdim) + heads * vdim * H
+    return 2 * (attn + ffn_active)
+
+
+def model_flops_per_step(args, world, layers):
+    """Algorithmic training FLOPs of one step of the whole job (forward + backward = 3 x forward):
+    every matmul of the model's active parameters for every token, plus causal attention
+    (QK^T and PV over the lower triangle). Used for ``model_tflops_per_gpu``, which compares runs
+    with different layer counts and GPU counts (1 GPU runs 8 layers, N > 1 the full depth)."""
+    tokens = tokens_per_step(args, world)
+    S = args.seq
+    nseq = tokens / S
+    if args.config == "llama8b-tp":
+        H, Hq, Hkv, D, I, V = 4096, 32, 8, 128, 14336, 128256
+        per_tok = 2 * (layers * (H * (Hq + 2 * Hkv) * D + Hq * D * H + 3 * H * I) + H * V)
+        attn = layers * nseq * S * S * Hq * (D + D)
+    elif args.config == "gpt1.3b-fp4-dp":
+        H, heads, D, I, V = 2048, 16, 128, 8192, 50304
+        per_tok = 2 * (layers * (4 * H * H + 2 * H * I) + H * V)
+        attn = layers * nseq * S * S * heads * (D + D)
+    elif args.config == "dsv2lite-fp8-ep":
+        H, heads, V = 2048, 16, 102400
+        dense = _mla_moe_flops_per_token(H, heads, 1536, 512, 128, 64, 128, 3 * H * 10944)
+        moe = _mla_moe_flops_per_token(H, heads, 1536, 512, 128, 64, 128, (6 + 2) * 3 * H * 1408 + H * 64)
+        per_tok = dense + (layers - 1) * moe + 2 * H * V
+        attn = layers * nseq * S * S * heads * (192 + 128)
+    else:  # deepseek-4d
+        H, heads, V = 4096, 32, 32000
+        moe = _mla_moe_flops_per_token(H, heads, 1536, 512, 128, 64, 128, (2 + 1) * 3 * H * 4096 + H * 16)
+        per_tok = layers * moe + 2 * H * V
+        attn = layers * nseq * S * S * heads * (192 + 128)
+    return 3.0 * (per_tok * tokens + attn)
 
 
 # ---------------------------------------------------------------- reference arm
@@ -524,6 +617,7 @@ def main():
                     "optimizer": "AdamW fp32 master/moments, bf16 params, fp32 main grads, clip 1.0",
                     "l2": "working set >> 126 MB L2 (no explicit flush)",
                 },
+                "model_tflops_per_gpu": model_flops_per_step(args, world, layers) / (ms / 1e3) / world / 1e12,
                 "clocks": clocks,
                 "e2e": e2e,
                 "fused_tp_paths": fused_paths,

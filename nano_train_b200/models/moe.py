@@ -383,6 +383,7 @@ class ExpertParallelMoE(nn.Module):
         self._last_token_counts = torch.zeros(self.experts_per_rank, dtype=torch.long)
         self._stack_cache = _StackCache()
         self.last_path = None  # "fused" (peer-memory kernels) or "all_to_all", set by forward
+        self.fused_rel_err: Optional[float] = None  # first fused call's error against the all-to-all path
 
     last_aux_loss = property(lambda self: self._last_aux_loss)
     last_token_counts = property(lambda self: self._last_token_counts)
@@ -441,10 +442,36 @@ class ExpertParallelMoE(nn.Module):
         T = tokens.size(0)
         ro = self.router(tokens)
         if self._fused_ok(tokens):
-            return self._forward_fused(tokens, ro).view(B, S, H)
+            out = self._forward_fused(tokens, ro)
+            if self.fused_rel_err is None:
+                self._check_fused_against_all_to_all(tokens, ro, out)
+            return out.view(B, S, H)
+        return self._forward_all_to_all(tokens, ro).view(B, S, H)
+
+    FUSED_REL_TOL = {False: 2e-2, True: 1e-1}  # by e4m3 payload (independent rounding of the two paths)
+
+    @torch.no_grad()
+    def _check_fused_against_all_to_all(self, tokens: torch.Tensor, ro: RouterOutput, out: torch.Tensor) -> None:
+        """First fused call of this layer: the all-to-all path recomputes the same layer output from
+        the same routing; the relative L2 error (max over the EP group) is kept in
+        ``fused_rel_err`` and a disagreement beyond tolerance raises. Runs once per layer, inside
+        every multi-GPU job that takes the fused path."""
+        saved = (self._last_aux_loss, self._last_dropped_fraction, self._last_token_counts, self.last_path)
+        ref = self._forward_all_to_all(tokens.detach(), ro).float()
+        self._last_aux_loss, self._last_dropped_fraction, self._last_token_counts, self.last_path = saved
+        err = ((out.detach().float() - ref).norm() / ref.norm().clamp_min(1e-30)).reshape(1)
+        dist.all_reduce(err, op=dist.ReduceOp.MAX, group=self.ep_group)
+        self.fused_rel_err = float(err)
+        tol = self.FUSED_REL_TOL[self._fused_payload()[1]]
+        if not self.fused_rel_err <= tol:
+            raise RuntimeError(f"fused expert-parallel output differs from the all-to-all path: relative error "
+                               f"{self.fused_rel_err:.3e} > {tol}")
+
+    def _forward_all_to_all(self, tokens: torch.Tensor, ro: RouterOutput) -> torch.Tensor:
+        """Dispatch / experts / combine with NCCL all-to-all (one host read of the split sizes)."""
+        T, H = tokens.shape
         self.last_path = "all_to_all"
         E, epr, K = self.num_experts, self.experts_per_rank, self.top_k
-        # Global token count -> capacity (every EP rank sees the same capacity).
         # Assignments sorted by destination expert (hence by destination rank).
         flat_e = ro.topk_indices.reshape(-1)
         order = torch.argsort(flat_e, stable=True)
@@ -499,7 +526,7 @@ class ExpertParallelMoE(nn.Module):
         self._last_aux_loss = ro.aux_loss
         self._last_dropped_fraction = stats
         self._last_token_counts = kept_counts
-        return out.view(B, S, H)
+        return out
 
     def _forward_fused(self, tokens: torch.Tensor, ro: RouterOutput) -> torch.Tensor:
         """Dispatch / experts / combine through the peer-memory kernels, no host synchronisation.

@@ -298,9 +298,28 @@ class TransformerModel(nn.Module):
         if self.sequence_parallel and (B * S) % self.tp_size != 0:
             raise ValueError("batch*seq must be divisible by tp_size under sequence parallelism")
         x = self._embed(input_ids)
-        for block in self.blocks:
-            x = block.forward_tokens(x, B, S)
+        observers = self.__dict__.get("_block_observers")
+        for i, block in enumerate(self.blocks):
+            y = block.forward_tokens(x, B, S)
+            if observers:
+                for fn in list(observers.values()):
+                    fn(i, x, y)
+            x = y
         return self.ln_f(x)
+
+    def register_block_observer(self, fn):
+        """Call ``fn(block_index, block_input, block_output)`` after every block of the token-major
+        forward (the residual stream around each block); returns a handle with ``remove()``. The
+        blocks run through ``forward_tokens``, which module forward hooks do not see."""
+        obs = self.__dict__.setdefault("_block_observers", {})
+        key = object()
+        obs[key] = fn
+
+        class _Handle:
+            def remove(self_inner):
+                obs.pop(key, None)
+
+        return _Handle()
 
     def forward(self, input_ids: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Logits [B, S, V(/tp)]. Without a mask the blocks run the fused causal path; an explicit

@@ -269,6 +269,15 @@ class FlatAdamW:
             if self.strategy != "no_shard" and self.dp_size > 1:
                 dist.all_gather_into_tensor(buf.param_data, pb.clone(), group=self.dp_group)
 
+    @torch.no_grad()
+    def grad_norm(self) -> torch.Tensor:
+        """L2 norm of this rank's accumulated gradients (all buffers, before any clipping or DP
+        reduction), as a device scalar: nothing is read back to the host."""
+        sq = torch.zeros((), dtype=torch.float32, device=self._stats.device)
+        for buf in self.buffers:
+            sq += buf.grad_data.float().pow(2).sum()
+        return sq.sqrt()
+
     def state_tensors(self) -> list[dict]:
         return self.shards
 

@@ -278,8 +278,6 @@ def train_step_pipeline(model, optimizer, use_distributed_optimizer: bool, batch
     device = parallel.device
     act_dtype = (next(model.parameters()).dtype if precision_config is None
                  else dtype_alias_to_torch(precision_config.activation_dtype))
-    if precision_config is not None and act_dtype != torch.float32 and device.type == "cpu":
-        act_dtype = next(model.parameters()).dtype
     hidden = model.config.hidden_size
     mbs = expected_local_batch // num_microbatches
     peers = resolve_pipeline_peers(parallel)
@@ -288,15 +286,20 @@ def train_step_pipeline(model, optimizer, use_distributed_optimizer: bool, batch
         optimizer.zero_grad(set_to_none=True)
     else:
         zero_grad_fn(optimizer)
-    mbatches = prepare_microbatches(batch, model, expected_local_batch, num_microbatches, device)
+    # The helpers are called by keyword: scripts and tests may substitute any of them.
+    mbatches = prepare_microbatches(batch=batch, model=model, expected_local_batch=expected_local_batch,
+                                    num_microbatches=num_microbatches, device=device)
     execute_1f1b_schedule(
-        parallel, num_microbatches,
-        run_forward=lambda i: pipeline_forward_microbatch(i, model, mbatches, peers, state, mbs, seq_len, hidden,
-                                                          act_dtype, device, gather_moe_metrics_fn,
-                                                          precision_controller, num_microbatches),
-        run_backward=lambda i: pipeline_backward_microbatch(i, model, peers, state, num_microbatches, aux_loss_coef,
-                                                            mbs, seq_len, hidden, act_dtype, device,
-                                                            precision_controller))
+        parallel=parallel, num_microbatches=num_microbatches,
+        run_forward=lambda i: pipeline_forward_microbatch(
+            microbatch_idx=i, model=model, microbatches=mbatches, peers=peers, state=state,
+            microbatch_batch_size=mbs, seq_len=seq_len, hidden_size=hidden, activation_dtype=act_dtype,
+            device=device, gather_moe_metrics_fn=gather_moe_metrics_fn, precision_controller=precision_controller,
+            num_microbatches=num_microbatches),
+        run_backward=lambda i: pipeline_backward_microbatch(
+            microbatch_idx=i, model=model, peers=peers, state=state, num_microbatches=num_microbatches,
+            aux_loss_coef=aux_loss_coef, microbatch_batch_size=mbs, seq_len=seq_len, hidden_size=hidden,
+            activation_dtype=act_dtype, device=device, precision_controller=precision_controller))
     finalize_pipeline_sends(state)
     finalize_pipeline_metrics(state)
     should_step = True

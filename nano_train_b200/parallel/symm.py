@@ -186,12 +186,15 @@ class _FusedAdapter:
     """
 
     REPS = 3
+    REF = "nccl"       # the NCCL + GEMM candidate is the numerical reference of the others
+    REL_TOL = 2e-2     # bf16 outputs; the candidates differ only in summation order
 
     def __init__(self, c: TPCommunicator, autotune: bool = True):
         self.c = c
         self.autotune = autotune
         self.choice: dict = {}  # key -> "fused" | "nccl"
         self.timings: dict = {}
+        self.rel_err: dict = {}  # key -> {candidate: max over ranks of |y - y_nccl| / |y_nccl|}
 
     def supports(self, x, w):
         return self.c.supports(x, w)
@@ -221,7 +224,12 @@ class _FusedAdapter:
 
     def _decide(self, key, candidates: dict) -> str:
         """Name of the fastest candidate (first one when autotune is off); timed on the device, max over
-        the group, so every rank takes the same decision."""
+        the group, so every rank takes the same decision.
+
+        Before timing, every candidate's output on this call's operands is compared with the NCCL +
+        GEMM candidate's (relative L2 error, max over the group, recorded in ``rel_err``); a fused
+        kernel that disagrees beyond ``REL_TOL`` raises instead of being used. This is the multi-GPU
+        correctness check of the fused kernels that runs inside every multi-GPU job."""
         ch = self.choice.get(key)
         if ch is not None:
             return ch
@@ -229,9 +237,26 @@ class _FusedAdapter:
         if not self.autotune:
             self.choice[key] = names[0]
             return names[0]
-        t = torch.tensor([self._time(candidates[k]) for k in names], dtype=torch.float64, device=self.c.device)
+        order = [self.REF] + [k for k in names if k != self.REF] if self.REF in names else names
+        ref, errs = None, {}
+        for k in order:
+            out = candidates[k]()
+            y = (out[0] if isinstance(out, tuple) else out).detach().float()
+            if k == self.REF:
+                ref = y.clone()
+            elif ref is not None:
+                errs[k] = float(((y - ref).norm() / ref.norm().clamp_min(1e-30)).item())
+        err_names = list(errs)
+        vals = [self._time(candidates[k]) for k in names] + [errs[k] for k in err_names]
+        t = torch.tensor(vals, dtype=torch.float64, device=self.c.device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.c.group)
-        times = [float(v) for v in t]
+        got = [float(v) for v in t]
+        times, err_max = got[:len(names)], dict(zip(err_names, got[len(names):]))
+        self.rel_err[key] = {k: float(f"{v:.3e}") for k, v in err_max.items()}
+        bad = {k: v for k, v in err_max.items() if not v <= self.REL_TOL}
+        if bad:
+            raise RuntimeError(f"fused kernel output differs from NCCL + GEMM for {key}: relative error {bad} "
+                               f"> {self.REL_TOL}")
         ch = names[min(range(len(names)), key=lambda i: times[i])]
         self.choice[key] = ch
         self.timings[key] = dict(zip(names, (round(v, 4) for v in times)))
