@@ -41,6 +41,8 @@ std::vector<at::Tensor> layernorm_bwd(const at::Tensor& dy, const at::Tensor& x,
                                       const at::Tensor& mean, const at::Tensor& rstd);
 void rope_(at::Tensor& x, const c10::optional<at::Tensor>& positions, int64_t off, int64_t R, int64_t seq_len,
            double theta, int64_t mode, bool inverse);
+void rope_table_(at::Tensor& x, const at::Tensor& table, int64_t off, int64_t R, int64_t seq_len, int64_t mode,
+                 bool inverse);
 at::Tensor swiglu_fwd(const at::Tensor& gu);
 at::Tensor swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu);
 at::Tensor gelu_fwd(const at::Tensor& x);
@@ -156,6 +158,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_fwd", &ntb::layernorm_fwd);
   m.def("layernorm_bwd", &ntb::layernorm_bwd);
   m.def("rope_", &ntb::rope_);
+  m.def("rope_table_", &ntb::rope_table_);
   m.def("swiglu_fwd", &ntb::swiglu_fwd);
   m.def("swiglu_bwd", &ntb::swiglu_bwd);
   m.def("gelu_fwd", &ntb::gelu_fwd);

@@ -824,6 +824,94 @@ void rope_(at::Tensor& x, const c10::optional<at::Tensor>& positions, int64_t of
   NTB_LAUNCH_CHECK(1);
 }
 
+// Table-driven, vectorised RoPE for rows of a fused projection. cs[pos * (R/2) + k] = (cos, sin) of
+// pos * theta^(-2k/R), built once per (seq_len, R, theta) on the host side of the binding's caller;
+// positions are t % seq_len. Each thread rotates one 16-byte chunk (8 elements) in place: for the
+// half-split layout the chunk of columns [i0, i0+8) together with its partner chunk [i0+R/2, ...),
+// for the interleaved layout 4 adjacent (2i, 2i+1) pairs. x is [T, heads, D] with the rotary part
+// at columns [off, off + R); every address involved is 16-byte aligned (checked by the binding).
+template <typename T, int MODE>
+__global__ void __launch_bounds__(256) rope_table_kernel(T* __restrict__ x, const float2* __restrict__ cs,
+                                                         int64_t T_, int heads, int64_t sx, int64_t sh, int off,
+                                                         int R, int seq_len, bool inverse) {
+  const int half = R / 2;
+  const int chunks = (MODE == 0 ? half : R) / 8;
+  const int64_t total = T_ * heads * chunks;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % chunks);
+    const int64_t th = idx / chunks;
+    const int hd = static_cast<int>(th % heads);
+    const int64_t t = th / heads;
+    const float2* row = cs + static_cast<int64_t>(t % seq_len) * half;
+    T* base = x + t * sx + hd * sh + off;
+    const float sgn = inverse ? -1.f : 1.f;
+    if (MODE == 0) {
+      const int i0 = c * 8;
+      float a[8], b[8], oa[8], ob[8];
+      ld8(base + i0, a);
+      ld8(base + i0 + half, b);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float2 q = row[i0 + j];
+        const float sn = sgn * q.y;
+        oa[j] = a[j] * q.x - b[j] * sn;
+        ob[j] = b[j] * q.x + a[j] * sn;
+      }
+      st8(base + i0, oa);
+      st8(base + i0 + half, ob);
+    } else {
+      const int j0 = c * 8;
+      float v[8], o[8];
+      ld8(base + j0, v);
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float2 q0 = row[(j0 + 2 * m) % half], q1 = row[(j0 + 2 * m + 1) % half];
+        const float a = v[2 * m], b = v[2 * m + 1];
+        if (!inverse) {
+          o[2 * m] = a * q0.x - b * q0.y;
+          o[2 * m + 1] = b * q1.x + a * q1.y;
+        } else {
+          o[2 * m] = a * q0.x + b * q1.y;
+          o[2 * m + 1] = b * q1.x - a * q0.y;
+        }
+      }
+      st8(base + j0, o);
+    }
+  }
+}
+
+// In-place RoPE on x[T, heads, D] (last dim contiguous) from a (cos, sin) table [seq_len, R/2, 2] fp32.
+void rope_table_(at::Tensor& x, const at::Tensor& table, int64_t off, int64_t R, int64_t seq_len, int64_t mode,
+                 bool inverse) {
+  TORCH_CHECK(x.dim() == 3 && x.stride(-1) == 1, "rope_table_: x must be [T, heads, D] with contiguous D");
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kFloat && table.is_contiguous() &&
+                  table.numel() == seq_len * R,
+              "rope_table_: table must be contiguous fp32 [seq_len, R/2, 2]");
+  TORCH_CHECK(R % 16 == 0 && off % 8 == 0 && off + R <= x.size(-1), "rope_table_: rotary range");
+  const int64_t sx = x.stride(0), sh = x.stride(1);
+  TORCH_CHECK(sx % 8 == 0 && sh % 8 == 0 && (reinterpret_cast<uintptr_t>(x.data_ptr()) & 15) == 0,
+              "rope_table_: rows and heads must start on 16-byte boundaries");
+  const int64_t T_ = x.size(0);
+  const int heads = static_cast<int>(x.size(1));
+  if (T_ == 0 || heads == 0) return;
+  const int64_t total = T_ * heads * (mode == 0 ? R / 2 : R) / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 16L * num_sms(x.get_device())));
+  auto stream = at::cuda::getCurrentCUDAStream();
+  const float2* cs = reinterpret_cast<const float2*>(table.data_ptr<float>());
+  NTB_DISPATCH_FLOAT(x.scalar_type(), "rope_table_", [&] {
+    if (mode == 0)
+      rope_table_kernel<scalar_t, 0><<<blocks, 256, 0, stream>>>(P<scalar_t>(x), cs, T_, heads, sx, sh,
+                                                                 static_cast<int>(off), static_cast<int>(R),
+                                                                 static_cast<int>(seq_len), inverse);
+    else
+      rope_table_kernel<scalar_t, 1><<<blocks, 256, 0, stream>>>(P<scalar_t>(x), cs, T_, heads, sx, sh,
+                                                                 static_cast<int>(off), static_cast<int>(R),
+                                                                 static_cast<int>(seq_len), inverse);
+  });
+  NTB_LAUNCH_CHECK(1);
+}
+
 // =========================================================== activations
 // SwiGLU over a packed [rows, 2I] tensor: gate = cols [0, I), up = cols [I, 2I).
 template <typename T>

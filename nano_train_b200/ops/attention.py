@@ -111,17 +111,16 @@ class _QKVAttentionFn(torch.autograd.Function):
 
     @staticmethod
     def forward(ctx, qkv, B, S, nq, nkv, dqk, dv, scale, rope_dim, rope_theta, rope_mode, causal):
-        from .rope import MODES
+        from .rope import rope_rows_
 
         C = ext()
         T = B * S
         q2 = qkv.view(T, -1)
         qv = q2[:, : nq * dqk].view(T, nq, dqk)
         kv = q2[:, nq * dqk: (nq + nkv) * dqk].view(T, nkv, dqk)
-        if rope_dim:
-            off = dqk - rope_dim
-            C.rope_(qv, None, off, rope_dim, S, float(rope_theta), MODES[rope_mode], False)
-            C.rope_(kv, None, off, rope_dim, S, float(rope_theta), MODES[rope_mode], False)
+        if rope_dim:  # q and k heads are adjacent in the row: one launch rotates both
+            rope_rows_(q2[:, : (nq + nkv) * dqk].view(T, nq + nkv, dqk), dqk - rope_dim, rope_dim, S,
+                       float(rope_theta), rope_mode, False)
         ctx.mark_dirty(qkv)
         q4, k4, v4 = _split4(q2, B, S, nq, nkv, dqk, dv)
         o, lse = _fwd(q4, k4, v4, scale, causal)
@@ -131,7 +130,7 @@ class _QKVAttentionFn(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, _g_qkv, do):
-        from .rope import MODES
+        from .rope import rope_rows_
 
         qkv, o, lse = ctx.saved_tensors
         B, S, nq, nkv, dqk, dv, scale, rope_dim, rope_theta, rope_mode, causal = ctx.meta
@@ -144,11 +143,8 @@ class _QKVAttentionFn(torch.autograd.Function):
         C.flash_attn_bwd(do.reshape(B, S, nq, dv).contiguous(), q4, k4, v4, o, lse, float(scale), bool(causal),
                          dq4, dk4, dv4)
         if rope_dim:
-            off = dqk - rope_dim
-            C.rope_(dqkv[:, : nq * dqk].view(T, nq, dqk), None, off, rope_dim, S, float(rope_theta),
-                    MODES[rope_mode], True)
-            C.rope_(dqkv[:, nq * dqk: (nq + nkv) * dqk].view(T, nkv, dqk), None, off, rope_dim, S,
-                    float(rope_theta), MODES[rope_mode], True)
+            rope_rows_(dqkv[:, : (nq + nkv) * dqk].view(T, nq + nkv, dqk), dqk - rope_dim, rope_dim, S,
+                       float(rope_theta), rope_mode, True)
         return (dqkv.view_as(qkv),) + (None,) * 11
 
 

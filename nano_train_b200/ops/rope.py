@@ -20,6 +20,34 @@ def _inv_freq(R: int, theta: float, device) -> torch.Tensor:
     return 1.0 / (theta ** (torch.arange(0, R, 2, device=device, dtype=torch.float32) / R))
 
 
+_TABLES: dict = {}
+
+
+def rope_table(seq_len: int, R: int, theta: float, device) -> torch.Tensor:
+    """(cos, sin) of pos * theta^(-2k/R) for pos < seq_len, k < R/2, as fp32 [seq_len, R/2, 2]: the
+    same fp32 angles as ``rope_reference``. Built once per (seq_len, R, theta, device) and kept."""
+    key = (int(seq_len), int(R), float(theta), str(device))
+    t = _TABLES.get(key)
+    if t is None:
+        ang = torch.arange(seq_len, device=device, dtype=torch.float32)[:, None] * _inv_freq(R, theta, device)[None]
+        t = torch.stack([ang.cos(), ang.sin()], dim=-1).contiguous()
+        _TABLES[key] = t
+    return t
+
+
+def rope_rows_(x: torch.Tensor, off: int, R: int, seq_len: int, theta: float, mode: str, inverse: bool) -> None:
+    """In-place RoPE of columns [off, off + R) of every head of x [T, heads, D] (positions t % seq_len).
+    One vectorised launch from the cached table when the layout allows 16-byte access, else the
+    per-element kernel."""
+    C = ext()
+    ok = (R % 16 == 0 and off % 8 == 0 and x.dim() == 3 and x.stride(-1) == 1 and x.stride(0) % 8 == 0
+          and x.stride(1) % 8 == 0 and x.data_ptr() % 16 == 0)
+    if ok:
+        C.rope_table_(x, rope_table(seq_len, R, theta, x.device), off, R, seq_len, MODES[mode], inverse)
+    else:
+        C.rope_(x, None, off, R, seq_len, float(theta), MODES[mode], inverse)
+
+
 def rope_reference(x: torch.Tensor, positions: torch.Tensor, theta: float, mode: str, inverse=False) -> torch.Tensor:
     """PyTorch math of both layouts on x[..., S, heads, R] (positions [S] or broadcastable)."""
     R = x.shape[-1]

@@ -184,6 +184,28 @@ def test_rope(mode):
     assert rel_err(x.grad, xr.grad) < 1e-5
 
 
+@pytest.mark.parametrize("mode", ["half", "deepseek"])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("dqk,R", [(128, 128), (192, 64)])
+@pytest.mark.parametrize("inverse", [False, True])
+def test_rope_table_rows(mode, dtype, dqk, R, inverse):
+    """Vectorised table RoPE on q|k heads of a fused projection row (rotary part at the end of each
+    head, as in MLA's [nope | rope]) against the fp32 PyTorch statement."""
+    from nano_train_b200.ops.rope import rope_reference, rope_rows_
+    B, S, nq, nkv = 2, 200, 4, 2
+    width = (nq + nkv) * dqk + nkv * 128
+    x = torch.randn(B * S, width, device="cuda", dtype=dtype)
+    ref = x.clone()
+    heads = x[:, : (nq + nkv) * dqk].view(B * S, nq + nkv, dqk)
+    rope_rows_(heads, dqk - R, R, S, 5e5, mode, inverse)
+    r = ref[:, : (nq + nkv) * dqk].view(B, S, nq + nkv, dqk)[..., dqk - R:]
+    exp = rope_reference(r.float(), torch.arange(S, device="cuda"), 5e5, mode, inverse=inverse)
+    got = x[:, : (nq + nkv) * dqk].view(B, S, nq + nkv, dqk)
+    assert rel_err(got[..., dqk - R:], exp) < (1e-5 if dtype == torch.float32 else 8e-3)
+    torch.testing.assert_close(got[..., : dqk - R], ref[:, : (nq + nkv) * dqk].view(B, S, nq + nkv, dqk)[..., : dqk - R])
+    torch.testing.assert_close(x[:, (nq + nkv) * dqk:], ref[:, (nq + nkv) * dqk:])  # v untouched
+
+
 def test_swiglu_gelu():
     from nano_train_b200.ops.activation import gelu, swiglu
     gu = torch.randn(40, 2 * 96, device="cuda", requires_grad=True)
