@@ -208,7 +208,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const EpDispatchParams
         p.ctr[d] = 0;
       }
       __threadfence_system();
-      for (int d = 0; d < p.n; ++d) st_release_sys_u64(p.flag[d], p.epoch);
+      for (int d = 0; d < p.n; ++d) st_relaxed_sys_u64(p.flag[d], p.epoch);
       *p.done = 0u;
     }
   }
@@ -366,7 +366,7 @@ struct EpSignalParams {
 __global__ void ep_signal_kernel(const EpSignalParams p) {
   if (threadIdx.x != 0) return;
   __threadfence_system();
-  for (int d = 0; d < p.n; ++d) st_release_sys_u64(p.flag[d], p.epoch);
+  for (int d = 0; d < p.n; ++d) st_relaxed_sys_u64(p.flag[d], p.epoch);
 }
 
 // ------------------------------------------------------------------ receiver: slab -> grouped GEMM input

@@ -9,6 +9,13 @@ namespace ntb {
 __device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
 }
+// Relaxed system-scope store. After one fence.sc.sys (__threadfence_system) by the same thread,
+// relaxed stores publish everything ordered before the fence (a release pattern of the PTX memory
+// model) without the per-store fence that st.release.sys carries: publishing one epoch to n peers
+// costs one fence instead of n.
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
 __device__ __forceinline__ unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
   unsigned long long v;
   asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");

@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(256) zero_rs_kernel(const __grid_constant__ Ze
         p.stats_slot[r][1] = a1;
       }
       __threadfence_system();
-      for (int r = 0; r < p.n; ++r) st_release_sys_u64(p.flag_stats[r], p.epoch);
+      for (int r = 0; r < p.n; ++r) st_relaxed_sys_u64(p.flag_stats[r], p.epoch);
       p.stats_acc[0] = 0.f;
       p.stats_acc[1] = 0.f;
       *p.done = 0u;
@@ -217,7 +217,7 @@ __global__ void __launch_bounds__(256) zero_adam_kernel(const __grid_constant__ 
     const unsigned int prev = atomicAdd(p.done, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
-      for (int r = 0; r < p.n; ++r) st_release_sys_u64(p.flag_params[r], p.epoch);
+      for (int r = 0; r < p.n; ++r) st_relaxed_sys_u64(p.flag_params[r], p.epoch);
       *p.done = 0u;
     }
   }

@@ -185,7 +185,7 @@ class _FusedAdapter:
     eight).
     """
 
-    REPS = 3
+    REPS = 10
     REF = "nccl"       # the NCCL + GEMM candidate is the numerical reference of the others
     REL_TOL = 2e-2     # bf16 outputs; the candidates differ only in summation order
 
