@@ -29,32 +29,20 @@ class _PrecisionResolverLike(Protocol):
         ...
 
 
-@dataclass(frozen=True)
-class _NoOpAssignment:
-    module_name: str
-    module_type: str
-    compute_lowbit_mode: Optional[str] = None
-    persistent_lowbit_mode: str = "off"
-    persistent_scale_granularity: str = "per_channel"
-    fp4_persistent_format: str = "nf4"
-    compute_dtype_override: Optional[str] = None
-    master_ownership: str = "module"
-
-
-@dataclass(frozen=True)
-class _NoOpInitState:
-    assignment: _NoOpAssignment
-    lowbit_backend: Optional[object] = None
-    lowbit_capable_type: Optional[object] = None
-
-
-class _NoOpPrecisionResolver:
-    """Resolver for call sites that enable no low-bit policy: every module runs in its param dtype."""
+class FullPrecisionResolver:
+    """Precision resolver of call sites without a low-bit policy: every module computes in its parameter
+    dtype. It answers with the runtime's own contract types (``ModulePrecisionInitState`` holding a
+    ``ModulePrecisionAssignment`` with low-bit compute and persistence off), so layers treat it exactly
+    like a resolver built from a precision config."""
 
     def resolve_module_init_state(self, *, module_path: str, module_type: str, lowbit_capable_type,
-                                  kernel_spec=None) -> _NoOpInitState:
+                                  kernel_spec=None):
+        from .runtime.contracts import ModulePrecisionAssignment, ModulePrecisionInitState
+
         del lowbit_capable_type, kernel_spec
-        return _NoOpInitState(assignment=_NoOpAssignment(module_name=module_path, module_type=module_type))
+        return ModulePrecisionInitState(assignment=ModulePrecisionAssignment(
+            module_name=module_path, module_type=module_type, compute_lowbit_mode=None,
+            persistent_lowbit_mode="off", persistent_scale_granularity="per_channel", fp4_persistent_format="nf4"))
 
     def finalize(self):
         return None
@@ -63,8 +51,11 @@ class _NoOpPrecisionResolver:
         return None
 
 
+_NoOpPrecisionResolver = FullPrecisionResolver  # name used by earlier scripts and tests
+
+
 def _default_precision_resolver() -> _PrecisionResolverLike:
-    return _NoOpPrecisionResolver()
+    return FullPrecisionResolver()
 
 
 @dataclass
