@@ -46,6 +46,7 @@ def main():
                     help="also time this many launches with CUDA events (after the warm-up) and print ms / GB/s")
     a = ap.parse_args()
     nbytes = 0  # algorithmic DRAM bytes of one launch, where the case defines them
+    nflops = 0  # algorithmic FLOPs of one launch, where the case defines them
     C = ext()
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
@@ -69,6 +70,12 @@ def main():
         wq, sw = C.fp8_quantize(w, 128, False, 0)
         y = torch.empty(8192, 2048, **bf)
         fn = lambda: C.gemm_fp8_blockscaled(xq, sx, wq, sw, y)  # noqa: E731
+    elif a.case in ("quant_tile", "quant_tile_sr"):
+        # 1x128 e4m3 activation quantiser of the DeepSeek recipe, 16384 x 2048 bf16 (the MoE payload shape)
+        x = torch.randn(16384, 2048, **bf)
+        sr = a.case.endswith("sr")
+        nbytes = x.numel() * (2 + 1) + x.numel() // 128 * 4  # read bf16, write codes and scales
+        fn = lambda: C.fp8_quantize(x, 1, sr, 7)  # noqa: E731
     elif a.case == "fp4_gemm":
         from nano_train_b200.ops import fp4
 
@@ -91,6 +98,25 @@ def main():
         o, lse = C.flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)
         do = torch.randn_like(o)
         fn = lambda: C.flash_attn_bwd(do, q, k, v, o, lse, 128 ** -0.5, True)  # noqa: E731
+    elif a.case in ("attn_fwd_mla", "attn_bwd_mla", "attn_fwd_tc128", "attn_bwd_tc128"):
+        # DeepSeek-V2-Lite MLA shape (2 x 4096 tokens, 16 heads, q/k 192, v 128) or the Llama shape
+        # (1 x 4096, 32 q / 8 kv heads, 128), causal; tcgen05 kernels
+        mla = a.case.endswith("mla")
+        Bq, Sq, hq, hkv, dqk, dvv = (2, 4096, 16, 16, 192, 128) if mla else (1, 4096, 32, 8, 128, 128)
+        buf = torch.randn(Bq, Sq, hq * dqk + hkv * (dqk + dvv), **bf)
+        q = buf[..., : hq * dqk].view(Bq, Sq, hq, dqk)
+        k = buf[..., hq * dqk: (hq + hkv) * dqk].view(Bq, Sq, hkv, dqk)
+        v = buf[..., (hq + hkv) * dqk:].view(Bq, Sq, hkv, dvv)
+        sc = dqk ** -0.5
+        o, lse = C.flash_attn_fwd_tc(q, k, v, sc, True)
+        fwd_flops = Bq * hq * Sq * Sq * (dqk + dvv)  # causal: half of 2 * S^2 * (dqk + dv) per head
+        if "fwd" in a.case:
+            nflops = fwd_flops
+            fn = lambda: C.flash_attn_fwd_tc(q, k, v, sc, True)  # noqa: E731
+        else:
+            nflops = fwd_flops * 5 // 2  # S recompute, dP, dV, dK, dQ
+            do = torch.randn_like(o)
+            fn = lambda: C.flash_attn_bwd(do, q, k, v, o, lse, sc, True)  # noqa: E731
     elif a.case in ("attn_fwd", "attn_bwd"):
         q = torch.randn(1, 4096, 32, 128, **bf)
         k = torch.randn(1, 4096, 8, 128, **bf)
@@ -199,6 +225,8 @@ def main():
         line = f"{a.case}: median {ms * 1e3:.1f} us over {a.time} launches"
         if nbytes:
             line += f", {nbytes / ms / 1e6:.0f} GB/s algorithmic"
+        if nflops:
+            line += f", {nflops / ms / 1e9:.0f} TFLOP/s algorithmic"
         print(line)
 
 

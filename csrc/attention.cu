@@ -35,6 +35,7 @@ using bf16 = __nv_bfloat16;
 void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
                               const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dk,
                               at::Tensor& dv, double scale, bool causal);
+bool flash_attn_bwd_tc_supported(int64_t dqk, int64_t dv);
 
 // ---------------------------------------------------------------- helpers
 __device__ __forceinline__ void cp_async16(uint32_t saddr, const void* g, bool valid) {
@@ -718,7 +719,7 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   p.dk = reinterpret_cast<bf16*>(dk.data_ptr());
   p.dv = reinterpret_cast<bf16*>(dv.data_ptr());
   bool launched = false;
-  if (DQK == 128 && DV == 128 && std::getenv("NTB_ATTN_BWD_LEGACY") == nullptr) {
+  if (flash_attn_bwd_tc_supported(DQK, DV) && std::getenv("NTB_ATTN_BWD_LEGACY") == nullptr) {
     flash_attn_bwd_tc_launch(q, k, v, dout, lse, delta, dq_acc, dk, dv, scale, causal);
     launched = true;
   }

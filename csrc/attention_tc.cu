@@ -37,16 +37,25 @@ namespace ntb {
 
 namespace attn_tc {
 
-constexpr int BM = 128, BN = 128, D = 128;
-constexpr int TILE_BYTES = BM * D * 2;          // 32 KB: two [128 x 64] swizzled boxes
-constexpr int BOX_BYTES = TILE_BYTES / 2;       // 16 KB
-constexpr int SMEM_Q = 0;
-constexpr int SMEM_K = SMEM_Q + TILE_BYTES;     // 2 stages
-constexpr int SMEM_V = SMEM_K + 2 * TILE_BYTES; // 2 stages
-constexpr int SMEM_P = SMEM_V + 2 * TILE_BYTES;
-constexpr int SMEM_BAR = SMEM_P + TILE_BYTES;
-constexpr int SMEM_BYTES = 1024 + SMEM_BAR + 256;
+constexpr int BM = 128, BN = 128;
+constexpr int BOX_BYTES = BM * 64 * 2;          // 16 KB: one [128 rows x 64] swizzled box
 constexpr uint32_t TMEM_COLS = 512, TMEM_S0 = 0, TMEM_O = 256;
+
+// Shared-memory plan of the forward for head dims DQK (q, k) and DV (v, o), with KS K stages and VS V
+// stages: Q (DQK/64 boxes), K ring, V ring, P (two boxes: 128 keys), barriers.
+template <int DQK, int DV, int KS, int VS>
+struct FwdCfg {
+  static_assert(DQK % 64 == 0 && DV % 64 == 0 && DQK <= 192 && DV <= 128, "head dims");
+  static constexpr int QB = DQK / 64, VB = DV / 64;
+  static constexpr int Q_BYTES = QB * BOX_BYTES, V_BYTES = VB * BOX_BYTES;
+  static constexpr int SMEM_Q = 0;
+  static constexpr int SMEM_K = SMEM_Q + Q_BYTES;
+  static constexpr int SMEM_V = SMEM_K + KS * Q_BYTES;
+  static constexpr int SMEM_P = SMEM_V + VS * V_BYTES;
+  static constexpr int SMEM_BAR = SMEM_P + 2 * BOX_BYTES;
+  static constexpr int SMEM_BYTES = 1024 + SMEM_BAR + 256;
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
 // 2^x on the special-function unit (PTX ex2.approx, flushes subnormal results to 0;
@@ -75,10 +84,14 @@ struct AttnTcParams {
   int* status;
 };
 
+template <int DQK, int DV, int KS, int VS>
 __global__ void __launch_bounds__(192, 1)
     flash_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, AttnTcParams p) {
   using namespace attn_tc;
+  using Cfg = FwdCfg<DQK, DV, KS, VS>;
+  constexpr int SMEM_Q = Cfg::SMEM_Q, SMEM_K = Cfg::SMEM_K, SMEM_V = Cfg::SMEM_V, SMEM_P = Cfg::SMEM_P,
+                SMEM_BAR = Cfg::SMEM_BAR;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + SMEM_BAR);
@@ -111,7 +124,7 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 128);
-    }
+    }  // rings with one stage use entry 0 only
     mbar_init(p_full, 128);
     mbar_init(o_done, 1);
     mbar_init(drain, 1);
@@ -134,34 +147,34 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_expect_tx(q_full, TILE_BYTES);
-      for (int c = 0; c < 2; ++c) tma_load_4d(smem + SMEM_Q + c * BOX_BYTES, &tmQ, q_full, c * 64, q0, h, b);
+      mbar_expect_tx(q_full, Cfg::Q_BYTES);
+      for (int c = 0; c < Cfg::QB; ++c) tma_load_4d(smem + SMEM_Q + c * BOX_BYTES, &tmQ, q_full, c * 64, q0, h, b);
       for (int j = 0; j < nkb; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
+        const int st = j % KS, sv = j % VS;
+        const uint32_t ph = static_cast<uint32_t>((j / KS) & 1), phv = static_cast<uint32_t>((j / VS) & 1);
         if (!mbar_wait(&k_empty[st], ph ^ 1, p.status, kStatusTimeoutProducer)) break;
-        mbar_expect_tx(&k_full[st], TILE_BYTES);
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(smem + SMEM_K + st * TILE_BYTES + c * BOX_BYTES, &tmK, &k_full[st], c * 64, j * BN, hk, b);
-        if (!mbar_wait(&v_empty[st], ph ^ 1, p.status, kStatusTimeoutProducer)) break;
-        mbar_expect_tx(&v_full[st], TILE_BYTES);
-        for (int c = 0; c < 2; ++c)
-          tma_load_4d(smem + SMEM_V + st * TILE_BYTES + c * BOX_BYTES, &tmV, &v_full[st], c * 64, j * BN, hk, b);
+        mbar_expect_tx(&k_full[st], Cfg::Q_BYTES);
+        for (int c = 0; c < Cfg::QB; ++c)
+          tma_load_4d(smem + SMEM_K + st * Cfg::Q_BYTES + c * BOX_BYTES, &tmK, &k_full[st], c * 64, j * BN, hk, b);
+        if (!mbar_wait(&v_empty[sv], phv ^ 1, p.status, kStatusTimeoutProducer)) break;
+        mbar_expect_tx(&v_full[sv], Cfg::V_BYTES);
+        for (int c = 0; c < Cfg::VB; ++c)
+          tma_load_4d(smem + SMEM_V + sv * Cfg::V_BYTES + c * BOX_BYTES, &tmV, &v_full[sv], c * 64, j * BN, hk, b);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t IDESC_S = make_idesc_f16(BM, BN, false, false);  // Q K-major, K K-major
-      constexpr uint32_t IDESC_O = make_idesc_f16(BM, D, false, true);    // P K-major, V N-major
+      constexpr uint32_t IDESC_O = make_idesc_f16(BM, DV, false, true);   // P K-major, V N-major
       const uint32_t sQ = smem_u32(smem + SMEM_Q), sP = smem_u32(smem + SMEM_P);
       bool ok = mbar_wait(q_full, 0, p.status, kStatusTimeoutMma);
       auto issue_pv = [&](int i) -> bool {
         if (!mbar_wait(p_full, static_cast<uint32_t>(i & 1), p.status, kStatusTimeoutMma)) return false;
-        const int st = i & 1;
-        if (!mbar_wait(&v_full[st], static_cast<uint32_t>((i >> 1) & 1), p.status, kStatusTimeoutMma)) return false;
+        const int st = i % VS;
+        if (!mbar_wait(&v_full[st], static_cast<uint32_t>((i / VS) & 1), p.status, kStatusTimeoutMma)) return false;
         tc_fence_after();
-        const uint32_t sV = smem_u32(smem + SMEM_V + st * TILE_BYTES);
+        const uint32_t sV = smem_u32(smem + SMEM_V + st * Cfg::V_BYTES);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           // A = P [128 q x 128 keys] K-major: 64-key chunks 16 KB apart, 32 B per k16 step inside.
@@ -175,19 +188,18 @@ __global__ void __launch_bounds__(192, 1)
         return true;
       };
       for (int j = 0; ok && j < nkb; ++j) {
-        const int st = j & 1;
-        const uint32_t ph = static_cast<uint32_t>((j >> 1) & 1);
-        if (!mbar_wait(&k_full[st], ph, p.status, kStatusTimeoutMma)) break;
-        if (!mbar_wait(&s_free[st], ph ^ 1, p.status, kStatusTimeoutMma)) break;
+        const int sb = j & 1, st = j % KS;  // S buffer, K stage
+        if (!mbar_wait(&k_full[st], static_cast<uint32_t>((j / KS) & 1), p.status, kStatusTimeoutMma)) break;
+        if (!mbar_wait(&s_free[sb], static_cast<uint32_t>(((j >> 1) & 1) ^ 1), p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
-        const uint32_t sK = smem_u32(smem + SMEM_K + st * TILE_BYTES);
+        const uint32_t sK = smem_u32(smem + SMEM_K + st * Cfg::Q_BYTES);
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
+        for (int kk = 0; kk < DQK / 16; ++kk) {
           const uint32_t off = (kk >> 2) * BOX_BYTES + (kk & 3) * 32;
-          umma_f16_ss(tmem_base + TMEM_S0 + st * BN, make_smem_desc_sw128(sQ + off, 16, 1024),
+          umma_f16_ss(tmem_base + TMEM_S0 + sb * BN, make_smem_desc_sw128(sQ + off, 16, 1024),
                       make_smem_desc_sw128(sK + off, 16, 1024), IDESC_S, kk > 0 ? 1u : 0u);
         }
-        umma_commit(&s_full[st]);
+        umma_commit(&s_full[sb]);
         umma_commit(&k_empty[st]);
         if (j >= 1 && !issue_pv(j - 1)) {
           ok = false;
@@ -284,7 +296,7 @@ __global__ void __launch_bounds__(192, 1)
       if (j > 0 && __any_sync(0xffffffffu, rescale)) {
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
+        for (int c = 0; c < DV / 32; ++c) {
           uint32_t r[32];
           const uint32_t ta = tmem_base + lane_addr + TMEM_O + c * 32;
           tmem_ld32(ta, r);
@@ -304,9 +316,9 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool valid = row < p.S;
-      __nv_bfloat16* og = p.o + ((static_cast<int64_t>(b) * p.S + (valid ? row : 0)) * p.Hq + h) * D;
+      __nv_bfloat16* og = p.o + ((static_cast<int64_t>(b) * p.S + (valid ? row : 0)) * p.Hq + h) * DV;
 #pragma unroll
-      for (int c = 0; c < D / 32; ++c) {
+      for (int c = 0; c < DV / 32; ++c) {
         uint32_t r[32];
         tmem_ld32(tmem_base + lane_addr + TMEM_O + c * 32, r);  // whole warp; stores below are per row
         if (valid) {
@@ -333,20 +345,54 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// q, k, v: [B, S, H, 128] bf16 views (head dim contiguous, 16-byte aligned strides).
+template <int DQK, int DV, int KS, int VS>
+static void launch_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, AttnTcParams& p, int dev) {
+  using namespace attn_tc;
+  using Cfg = FwdCfg<DQK, DV, KS, VS>;
+  TmaSlots& ts = tls_tma_slots();
+  const int box[4] = {64, BM, 1, 1};
+  auto map = [&](CUtensorMap* m, const at::Tensor& t, int d) {
+    const int64_t dims[4] = {d, t.size(1), t.size(2), t.size(0)};
+    const int64_t str[3] = {t.stride(1), t.stride(2), t.stride(0)};
+    make_tma_4d_bf16(m, t.data_ptr(), dims, str, box);
+  };
+  map(&ts.m[0], q, DQK);
+  map(&ts.m[1], k, DQK);
+  map(&ts.m[2], v, DV);
+  auto kern = flash_fwd_tc_kernel<DQK, DV, KS, VS>;
+  static bool attr_done[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((p.S + BM - 1) / BM), static_cast<unsigned>(p.Hq), static_cast<unsigned>(p.B));
+  void* args[4] = {&ts.m[0], &ts.m[1], &ts.m[2], &p};
+  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(192), args,
+                                  static_cast<size_t>(Cfg::SMEM_BYTES), at::cuda::getCurrentCUDAStream(dev)));
+  NTB_LAUNCH_CHECK(1);
+}
+
+bool flash_attn_fwd_tc_supported(int64_t dqk, int64_t dv) {
+  return (dqk == 128 && dv == 128) || (dqk == 192 && dv == 128) || (dqk == 64 && dv == 64);
+}
+
+// q, k: [B, S, H, DQK], v: [B, S, Hkv, DV] bf16 views (head dim contiguous, 16-byte aligned strides);
+// (DQK, DV) in {(128, 128), (192, 128) (MLA: [nope 128 | rope 64] x v 128), (64, 64)}.
 std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, double scale,
                                           bool causal) {
   using namespace attn_tc;
   TORCH_CHECK(q.dim() == 4 && k.dim() == 4 && v.dim() == 4, "flash_attn_fwd_tc: [B, S, H, D] tensors");
   TORCH_CHECK(q.scalar_type() == at::kBFloat16 && k.scalar_type() == at::kBFloat16 && v.scalar_type() == at::kBFloat16,
               "flash_attn_fwd_tc: bf16");
-  TORCH_CHECK(q.size(3) == D && k.size(3) == D && v.size(3) == D, "flash_attn_fwd_tc: head dim 128");
+  const int64_t DQK = q.size(3), DV = v.size(3);
+  TORCH_CHECK(k.size(3) == DQK && flash_attn_fwd_tc_supported(DQK, DV),
+              "flash_attn_fwd_tc: head dims (q/k, v) must be (128, 128), (192, 128) or (64, 64)");
   TORCH_CHECK(q.stride(3) == 1 && k.stride(3) == 1 && v.stride(3) == 1, "flash_attn_fwd_tc: head dim contiguous");
   TORCH_CHECK(k.size(1) == q.size(1) && v.size(1) == q.size(1) && k.size(0) == q.size(0) && v.size(0) == q.size(0),
               "flash_attn_fwd_tc: self-attention shapes");
   TORCH_CHECK(q.size(2) % k.size(2) == 0 && k.size(2) == v.size(2), "flash_attn_fwd_tc: GQA head ratio");
   const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), Hkv = k.size(2);
-  auto o = at::empty({B, S, Hq, D}, q.options());
+  auto o = at::empty({B, S, Hq, DV}, q.options());
   auto lse = at::empty({B, Hq, S}, q.options().dtype(at::kFloat));
   if (S == 0 || B == 0) return {o, lse};
   AttnTcParams p{};
@@ -360,33 +406,9 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor&
   p.causal = causal ? 1 : 0;
   const int dev = q.get_device();
   p.status = device_status(dev);
-  TmaSlots& ts = tls_tma_slots();
-  const int box[4] = {64, BM, 1, 1};
-  {
-    const int64_t dims[4] = {D, S, Hq, B};
-    const int64_t str[3] = {q.stride(1), q.stride(2), q.stride(0)};
-    make_tma_4d_bf16(&ts.m[0], q.data_ptr(), dims, str, box);
-  }
-  {
-    const int64_t dims[4] = {D, S, Hkv, B};
-    const int64_t str[3] = {k.stride(1), k.stride(2), k.stride(0)};
-    make_tma_4d_bf16(&ts.m[1], k.data_ptr(), dims, str, box);
-  }
-  {
-    const int64_t dims[4] = {D, S, Hkv, B};
-    const int64_t str[3] = {v.stride(1), v.stride(2), v.stride(0)};
-    make_tma_4d_bf16(&ts.m[2], v.data_ptr(), dims, str, box);
-  }
-  static bool attr_done[64] = {};
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    NTB_CUDA_CHECK(cudaFuncSetAttribute(flash_fwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_done[dev] = true;
-  }
-  dim3 grid(static_cast<unsigned>((S + BM - 1) / BM), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  void* args[4] = {&ts.m[0], &ts.m[1], &ts.m[2], &p};
-  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(flash_fwd_tc_kernel), grid, dim3(192), args,
-                                  static_cast<size_t>(SMEM_BYTES), at::cuda::getCurrentCUDAStream(dev)));
-  NTB_LAUNCH_CHECK(1);
+  if (DQK == 128) launch_fwd_tc<128, 128, 2, 2>(q, k, v, p, dev);
+  else if (DQK == 192) launch_fwd_tc<192, 128, 1, 2>(q, k, v, p, dev);
+  else launch_fwd_tc<64, 64, 2, 2>(q, k, v, p, dev);
   return {o, lse};
 }
 
@@ -408,13 +430,36 @@ std::vector<at::Tensor> flash_attn_fwd_tc(const at::Tensor& q, const at::Tensor&
 // Shared memory: K, V resident (32 KB each), Q_i, dO_i (32 KB each), P^T, dS^T
 // (32 KB each); every tile is two 16 KB [128 x 64] boxes with 128-byte swizzle.
 namespace attn_tc_bwd {
-constexpr int BM = 128, BN = 128, D = 128;
-constexpr int TILE = BM * D * 2, BOX = TILE / 2;
-constexpr int S_K = 0, S_V = S_K + TILE, S_Q = S_V + TILE, S_DO = S_Q + TILE, S_P = S_DO + TILE, S_DS = S_P + TILE;
-constexpr int S_LSE = S_DS + TILE;            // float[2][128] lse, float[2][128] delta (by iteration parity)
-constexpr int S_BAR = S_LSE + 4 * 128 * 4;
-constexpr int SMEM_BYTES = 1024 + S_BAR + 256;
-constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DK = 256, COL_DV = 384, TMEM_COLS = 512;
+constexpr int BM = 128, BN = 128;
+constexpr int BOX = BM * 64 * 2;  // one [128 x 64] swizzled box, 16 KB
+constexpr int PT = 2 * BOX;       // P^T / dS^T tile: 128 keys x 128 queries
+constexpr uint32_t TMEM_COLS = 512;
+
+// Plan of the backward for head dims DQK (q, k) and DV (v, o). SERIAL = false (DQK <= 128): S^T and
+// dP^T get their own TMEM columns and are issued together; dQ reuses S^T's columns. SERIAL = true
+// (MLA, DQK = 192): the TMEM cannot hold S^T, dP^T, dK (192) and dV at once, so dP^T is computed
+// into S^T's columns after P^T was read out, and dQ (192 columns) overlaps them and the free tail;
+// P^T and dS^T share one shared-memory tile (dS^T is written once dP^T, and with it the dV MMA
+// that read P^T, completed).
+template <int DQK, int DV, bool SERIAL>
+struct BwdCfg {
+  static_assert(DQK % 64 == 0 && DV % 64 == 0, "head dims");
+  static constexpr int QB = DQK / 64, VB = DV / 64;
+  static constexpr int Q_BYTES = QB * BOX, V_BYTES = VB * BOX;
+  static constexpr int S_K = 0, S_V = S_K + Q_BYTES, S_Q = S_V + V_BYTES, S_DO = S_Q + Q_BYTES, S_P = S_DO + V_BYTES;
+  static constexpr int S_DS = SERIAL ? S_P : S_P + PT;
+  static constexpr int S_LSE = S_DS + PT;  // float[2][128] lse, float[2][128] delta (by iteration parity)
+  static constexpr int S_BAR = S_LSE + 4 * 128 * 4;
+  static constexpr int SMEM_BYTES = 1024 + S_BAR + 256;
+  static constexpr uint32_t COL_S = SERIAL ? DQK + DV : 0;
+  static constexpr uint32_t COL_DP = SERIAL ? COL_S : 128;
+  static constexpr uint32_t COL_DK = SERIAL ? 0 : 256;
+  static constexpr uint32_t COL_DV = COL_DK + DQK;
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+  static_assert(COL_S + DQK <= TMEM_COLS && COL_DV + DV <= TMEM_COLS && (SERIAL || COL_DV + DV <= 512),
+                "TMEM columns");
+  static_assert(SERIAL || DQK <= 128, "dQ reuses the 128 columns of S^T");
+};
 }  // namespace attn_tc_bwd
 
 struct AttnTcBwdParams {
@@ -437,11 +482,16 @@ __device__ __forceinline__ void red_add_v4(float* addr, float a, float b, float 
                : "memory");
 }
 
+template <int DQK, int DV, bool SERIAL>
 __global__ void __launch_bounds__(192, 1)
     flash_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
                         const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
                         AttnTcBwdParams p) {
   using namespace attn_tc_bwd;
+  using Cfg = BwdCfg<DQK, DV, SERIAL>;
+  constexpr int S_K = Cfg::S_K, S_V = Cfg::S_V, S_Q = Cfg::S_Q, S_DO = Cfg::S_DO, S_P = Cfg::S_P, S_DS = Cfg::S_DS,
+                S_LSE = Cfg::S_LSE, S_BAR = Cfg::S_BAR;
+  constexpr uint32_t COL_S = Cfg::COL_S, COL_DP = Cfg::COL_DP, COL_DK = Cfg::COL_DK, COL_DV = Cfg::COL_DV;
   using attn_tc::ex2_approx;
   using attn_tc::warp_wait;
   extern __shared__ uint8_t smem_raw[];
@@ -459,7 +509,8 @@ __global__ void __launch_bounds__(192, 1)
   uint64_t* dq_free = bars + 9;  // dQ read back (128 arrivals)
   uint64_t* kv_done = bars + 10;
   uint64_t* stats_ready = bars + 11;  // lse/delta of the iteration written (128 arrivals)
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* dp_full = bars + 12;      // SERIAL: dP^T (and the dV MMA before it) complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 13);
   float* s_lse_all = reinterpret_cast<float*>(smem + S_LSE);  // [2][128]
   float* s_delta_all = s_lse_all + 256;                        // [2][128]
 
@@ -487,6 +538,7 @@ __global__ void __launch_bounds__(192, 1)
     mbar_init(dq_free, 128);
     mbar_init(kv_done, 1);
     mbar_init(stats_ready, 128);
+    mbar_init(dp_full, 1);
     mbar_fence_init();
   }
   if (warp == 0 && lane == 0) {
@@ -507,29 +559,28 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
     if (lane == 0) {
-      mbar_expect_tx(kv_full, 2 * TILE);
-      for (int c = 0; c < 2; ++c) {
-        tma_load_4d(smem + S_K + c * BOX, &tmK, kv_full, c * 64, k0, hk, b);
-        tma_load_4d(smem + S_V + c * BOX, &tmV, kv_full, c * 64, k0, hk, b);
-      }
+      mbar_expect_tx(kv_full, Cfg::Q_BYTES + Cfg::V_BYTES);
+      for (int c = 0; c < Cfg::QB; ++c) tma_load_4d(smem + S_K + c * BOX, &tmK, kv_full, c * 64, k0, hk, b);
+      for (int c = 0; c < Cfg::VB; ++c) tma_load_4d(smem + S_V + c * BOX, &tmV, kv_full, c * 64, k0, hk, b);
       for (int it = 0; it < iters; ++it) {
         const int h = hq;
         const int q0 = (qb_first + it) * BM;
         const uint32_t par = static_cast<uint32_t>(it & 1);
         if (!mbar_wait(q_free, par ^ 1, p.status, kStatusTimeoutProducer)) break;
-        mbar_expect_tx(q_full, TILE);
-        for (int c = 0; c < 2; ++c) tma_load_4d(smem + S_Q + c * BOX, &tmQ, q_full, c * 64, q0, h, b);
+        mbar_expect_tx(q_full, Cfg::Q_BYTES);
+        for (int c = 0; c < Cfg::QB; ++c) tma_load_4d(smem + S_Q + c * BOX, &tmQ, q_full, c * 64, q0, h, b);
         if (!mbar_wait(do_free, par ^ 1, p.status, kStatusTimeoutProducer)) break;
-        mbar_expect_tx(do_full, TILE);
-        for (int c = 0; c < 2; ++c) tma_load_4d(smem + S_DO + c * BOX, &tmDO, do_full, c * 64, q0, h, b);
+        mbar_expect_tx(do_full, Cfg::V_BYTES);
+        for (int c = 0; c < Cfg::VB; ++c) tma_load_4d(smem + S_DO + c * BOX, &tmDO, do_full, c * 64, q0, h, b);
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t ID_KK = make_idesc_f16(BM, BN, false, false);   // S^T, dP^T: both operands K-major (K = d)
-      constexpr uint32_t ID_KN = make_idesc_f16(BM, D, false, true);     // dV, dK: A K-major (K = q), B N-major
-      constexpr uint32_t ID_NN = make_idesc_f16(BM, D, true, true);      // dQ: A M-major (dS^T), B N-major (K)
+      constexpr uint32_t ID_DV = make_idesc_f16(BM, DV, false, true);    // dV: A K-major (K = q), B N-major
+      constexpr uint32_t ID_DK = make_idesc_f16(BM, DQK, false, true);   // dK: A K-major (K = q), B N-major
+      constexpr uint32_t ID_NN = make_idesc_f16(BM, DQK, true, true);    // dQ: A M-major (dS^T), B N-major (K)
       const uint32_t sK = smem_u32(smem + S_K), sV = smem_u32(smem + S_V), sQ = smem_u32(smem + S_Q),
                      sDO = smem_u32(smem + S_DO), sP = smem_u32(smem + S_P), sDS = smem_u32(smem + S_DS);
       auto kdesc = [](uint32_t base, int kk) {  // K-major, K chunks of 64 in 16 KB boxes
@@ -547,23 +598,31 @@ __global__ void __launch_bounds__(192, 1)
           break;
         tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
+        for (int kk = 0; kk < DQK / 16; ++kk)
           umma_f16_ss(tmem_base + COL_S, kdesc(sK, kk), kdesc(sQ, kk), ID_KK, kk > 0 ? 1u : 0u);
+        if (!SERIAL) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk)
-          umma_f16_ss(tmem_base + COL_DP, kdesc(sV, kk), kdesc(sDO, kk), ID_KK, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < DV / 16; ++kk)
+            umma_f16_ss(tmem_base + COL_DP, kdesc(sV, kk), kdesc(sDO, kk), ID_KK, kk > 0 ? 1u : 0u);
+        }
         umma_commit(s_full);
         if (!mbar_wait(p_ready, par, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
+        if (SERIAL) {  // S^T has been read out: dP^T into its columns
+#pragma unroll
+          for (int kk = 0; kk < DV / 16; ++kk)
+            umma_f16_ss(tmem_base + COL_DP, kdesc(sV, kk), kdesc(sDO, kk), ID_KK, kk > 0 ? 1u : 0u);
+        }
 #pragma unroll
         for (int kk = 0; kk < BM / 16; ++kk)
-          umma_f16_ss(tmem_base + COL_DV, kdesc(sP, kk), ndesc(sDO, kk), ID_KN, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ss(tmem_base + COL_DV, kdesc(sP, kk), ndesc(sDO, kk), ID_DV, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(do_free);
+        if (SERIAL) umma_commit(dp_full);
         if (!mbar_wait(ds_ready, par, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < BM / 16; ++kk)
-          umma_f16_ss(tmem_base + COL_DK, kdesc(sDS, kk), ndesc(sQ, kk), ID_KN, (it > 0 || kk > 0) ? 1u : 0u);
+          umma_f16_ss(tmem_base + COL_DK, kdesc(sDS, kk), ndesc(sQ, kk), ID_DK, (it > 0 || kk > 0) ? 1u : 0u);
         umma_commit(q_free);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk)
@@ -638,6 +697,13 @@ __global__ void __launch_bounds__(192, 1)
       asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
       tc_fence_before();
       mbar_arrive(p_ready);
+      if (SERIAL) {  // dP^T lands in S^T's columns; the dV MMA reading P^T completed before it
+        if (!warp_wait(dp_full, par, p.status, kStatusTimeoutEpilogue)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
       // dS^T = P^T * (dP^T - delta)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
@@ -669,9 +735,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       tc_fence_after();
       const int q = q0 + r;
-      float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.S + (q < p.S ? q : 0)) * D;
+      float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + h) * p.S + (q < p.S ? q : 0)) * DQK;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
+      for (int c = 0; c < DQK / 32; ++c) {
         uint32_t qr[32];
         tmem_ld32(tmem_base + lane_addr + COL_S + c * 32, qr);
         if (q < p.S) {
@@ -693,13 +759,15 @@ __global__ void __launch_bounds__(192, 1)
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
         const uint32_t col = which == 0 ? COL_DK : COL_DV;
+        const int width = which == 0 ? DQK : DV;
         const float sc = which == 0 ? p.scale : 1.f;
         float* accp = which == 0 ? p.dk_acc : p.dv_acc;
         __nv_bfloat16* out = which == 0 ? p.dk + b * p.dk_sb + krow * p.dk_ss + hk * p.dk_sh
                                         : p.dv + b * p.dv_sb + krow * p.dv_ss + hk * p.dv_sh;
-        float* acc_row = accp != nullptr ? accp + ((static_cast<int64_t>(b) * p.S + krow) * p.Hkv + hk) * D : nullptr;
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
+        float* acc_row =
+            accp != nullptr ? accp + ((static_cast<int64_t>(b) * p.S + krow) * p.Hkv + hk) * width : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < width / 32; ++c) {
           uint32_t v[32];
           tmem_ld32(tmem_base + lane_addr + col + c * 32, v);
           if (!valid) continue;
@@ -751,13 +819,46 @@ __global__ void acc_to_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16*
   }
 }
 
-// Launches the tcgen05 backward (head dim 128). dq_acc must be zeroed; dk/dv are
-// written in full (every key row of every kv head).
+bool flash_attn_bwd_tc_supported(int64_t dqk, int64_t dv) {
+  return (dqk == 128 && dv == 128) || (dqk == 192 && dv == 128) || (dqk == 64 && dv == 64);
+}
+
+template <int DQK, int DV, bool SERIAL>
+static void launch_bwd_tc(AttnTcBwdParams& p, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
+                          const at::Tensor& dout, int dev, cudaStream_t stream) {
+  using namespace attn_tc_bwd;
+  using Cfg = BwdCfg<DQK, DV, SERIAL>;
+  TmaSlots& ts = tls_tma_slots();
+  const int box[4] = {64, BM, 1, 1};
+  auto map = [&](CUtensorMap* m, const at::Tensor& t, int d) {
+    const int64_t dims[4] = {d, t.size(1), t.size(2), t.size(0)};
+    const int64_t str[3] = {t.stride(1), t.stride(2), t.stride(0)};
+    make_tma_4d_bf16(m, t.data_ptr(), dims, str, box);
+  };
+  map(&ts.m[0], q, DQK);
+  map(&ts.m[1], k, DQK);
+  map(&ts.m[2], v, DV);
+  map(&ts.m[3], dout, DV);
+  auto kern = flash_bwd_tc_kernel<DQK, DV, SERIAL>;
+  static bool attr_done[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  dim3 grid(static_cast<unsigned>((p.S + BN - 1) / BN), static_cast<unsigned>(p.Hq), static_cast<unsigned>(p.B));
+  void* args[5] = {&ts.m[0], &ts.m[1], &ts.m[2], &ts.m[3], &p};
+  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(192), args,
+                                  static_cast<size_t>(Cfg::SMEM_BYTES), stream));
+  NTB_LAUNCH_CHECK(1);
+}
+
+// Launches the tcgen05 backward for (q/k, v) head dims (128, 128), (192, 128) or (64, 64). dq_acc
+// (fp32 [B, Hq, S, DQK]) must be zeroed; dk/dv are written in full (every key row of every kv head).
 void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, const at::Tensor& dout,
                               const at::Tensor& lse, const at::Tensor& delta, at::Tensor& dq_acc, at::Tensor& dk,
                               at::Tensor& dv, double scale, bool causal) {
-  using namespace attn_tc_bwd;
-  TORCH_CHECK(q.size(3) == D && k.size(3) == D && v.size(3) == D, "flash_attn_bwd_tc: head dim 128");
+  const int64_t DQK = q.size(3), DV = v.size(3);
+  TORCH_CHECK(k.size(3) == DQK && flash_attn_bwd_tc_supported(DQK, DV), "flash_attn_bwd_tc: head dims");
   TORCH_CHECK(dout.is_contiguous() && dq_acc.is_contiguous(), "flash_attn_bwd_tc: contiguous dO and dq_acc");
   const int64_t B = q.size(0), S = q.size(1), Hq = q.size(2), Hkv = k.size(2);
   AttnTcBwdParams p{};
@@ -777,45 +878,28 @@ void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at
   p.causal = causal ? 1 : 0;
   const int dev = q.get_device();
   p.status = device_status(dev);
-  TmaSlots& ts = tls_tma_slots();
-  const int box[4] = {64, BM, 1, 1};
-  auto map = [&](CUtensorMap* m, const at::Tensor& t) {
-    const int64_t dims[4] = {D, S, t.size(2), B};
-    const int64_t str[3] = {t.stride(1), t.stride(2), t.stride(0)};
-    make_tma_4d_bf16(m, t.data_ptr(), dims, str, box);
-  };
-  map(&ts.m[0], q);
-  map(&ts.m[1], k);
-  map(&ts.m[2], v);
-  map(&ts.m[3], dout);
-  static bool attr_done[64] = {};
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    NTB_CUDA_CHECK(cudaFuncSetAttribute(flash_bwd_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_done[dev] = true;
-  }
   at::Tensor dk_acc, dv_acc;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
   if (Hq != Hkv) {
-    dk_acc = at::zeros({B, S, Hkv, D}, q.options().dtype(at::kFloat));
-    dv_acc = at::zeros({B, S, Hkv, D}, q.options().dtype(at::kFloat));
+    dk_acc = at::zeros({B, S, Hkv, DQK}, q.options().dtype(at::kFloat));
+    dv_acc = at::zeros({B, S, Hkv, DV}, q.options().dtype(at::kFloat));
     p.dk_acc = dk_acc.data_ptr<float>();
     p.dv_acc = dv_acc.data_ptr<float>();
   }
-  dim3 grid(static_cast<unsigned>((S + BN - 1) / BN), static_cast<unsigned>(Hq), static_cast<unsigned>(B));
-  void* args[5] = {&ts.m[0], &ts.m[1], &ts.m[2], &ts.m[3], &p};
-  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(flash_bwd_tc_kernel), grid, dim3(192), args,
-                                  static_cast<size_t>(SMEM_BYTES), stream));
-  NTB_LAUNCH_CHECK(1);
+  if (DQK == 128) launch_bwd_tc<128, 128, false>(p, q, k, v, dout, dev, stream);
+  else if (DQK == 192) launch_bwd_tc<192, 128, true>(p, q, k, v, dout, dev, stream);
+  else launch_bwd_tc<64, 64, false>(p, q, k, v, dout, dev, stream);
   if (Hq != Hkv) {
     TORCH_CHECK(dk.stride(3) == 1 && dv.stride(3) == 1 && dk.stride(2) % 4 == 0 && dk.stride(1) % 4 == 0 &&
                     dv.stride(2) % 4 == 0 && dv.stride(1) % 4 == 0,
                 "flash_attn_bwd_tc: dk/dv strides must keep 8-byte alignment");
-    const int64_t n4 = B * S * Hkv * D / 4;
-    const int blocks = static_cast<int>(std::min<int64_t>((n4 + 255) / 256, 148 * 8));
-    acc_to_bf16_kernel<<<blocks, 256, 0, stream>>>(dk_acc.data_ptr<float>(), p.dk, p.B, p.S, p.Hkv, D, p.dk_sb,
-                                                   p.dk_ss, p.dk_sh);
-    acc_to_bf16_kernel<<<blocks, 256, 0, stream>>>(dv_acc.data_ptr<float>(), p.dv, p.B, p.S, p.Hkv, D, p.dv_sb,
-                                                   p.dv_ss, p.dv_sh);
+    const int64_t nk = B * S * Hkv * DQK / 4, nv = B * S * Hkv * DV / 4;
+    const int bk = static_cast<int>(std::min<int64_t>((nk + 255) / 256, 148 * 8));
+    const int bv = static_cast<int>(std::min<int64_t>((nv + 255) / 256, 148 * 8));
+    acc_to_bf16_kernel<<<bk, 256, 0, stream>>>(dk_acc.data_ptr<float>(), p.dk, p.B, p.S, p.Hkv,
+                                               static_cast<int>(DQK), p.dk_sb, p.dk_ss, p.dk_sh);
+    acc_to_bf16_kernel<<<bv, 256, 0, stream>>>(dv_acc.data_ptr<float>(), p.dv, p.B, p.S, p.Hkv, static_cast<int>(DV),
+                                               p.dv_sb, p.dv_ss, p.dv_sh);
     NTB_LAUNCH_CHECK(2);
   }
 }

@@ -28,19 +28,17 @@ __device__ __forceinline__ float uniform01(uint64_t seed, uint64_t idx) {
   return (h >> 8) * (1.0f / 16777216.0f);
 }
 
-// Stochastic rounding of y (|y| <= 448) onto the e4m3 grid.
+// Stochastic rounding of y (|y| <= 448) onto the e4m3 grid, by exponent arithmetic: the grid
+// spacing at |y| is ulp = 2^(floor(log2|y|) - 3) (2^-9 below 2^-6, the subnormal spacing), a power
+// of two built from y's exponent field, so t = |y| / ulp is exact and floor(t + u) rounds |y| up to
+// the next grid point with probability frac(t). The sign is applied afterwards.
 __device__ __forceinline__ float e4m3_sr(float y, float u) {
-  const float a = fabsf(y);
-  if (a == 0.f) return 0.f;
-  int e;
-  frexpf(a, &e);           // a = m * 2^e, m in [0.5, 1)
-  int ex = e - 1;          // floor(log2 a)
-  if (ex < -6) ex = -6;    // subnormal spacing below 2^-6
-  const float ulp = ldexpf(1.f, ex - 3);
-  const float down = floorf(y / ulp) * ulp;
-  const float frac = (y - down) / ulp;
-  float r = (u < frac) ? down + ulp : down;
-  return fminf(fmaxf(r, -448.f), 448.f);
+  const int e = static_cast<int>((__float_as_uint(y) >> 23) & 0xFFu) - 127;  // floor(log2|y|) (normal y)
+  const int ex = (e < -6 ? -6 : e) - 3;                                       // log2 of the spacing
+  const float inv_ulp = __uint_as_float(static_cast<uint32_t>(127 - ex) << 23);
+  const float ulp = __uint_as_float(static_cast<uint32_t>(127 + ex) << 23);
+  const float r = floorf(fmaf(fabsf(y), inv_ulp, u)) * ulp;
+  return copysignf(fminf(r, 448.f), y);
 }
 
 __device__ __forceinline__ uint8_t to_e4m3(float y) {

@@ -24,104 +24,144 @@ namespace ntb {
 
 using bf16 = __nv_bfloat16;
 
-template <typename T>
-__device__ __forceinline__ float ldf(const T* p);
-template <>
-__device__ __forceinline__ float ldf<float>(const float* p) { return *p; }
-template <>
-__device__ __forceinline__ float ldf<bf16>(const bf16* p) { return __bfloat162float(*p); }
+// Eight consecutive elements <-> floats (16-byte bf16 or 2 x 16-byte fp32 accesses).
+__device__ __forceinline__ void load8(const bf16* p, float (&v)[8]) {
+  const uint4 u = *reinterpret_cast<const uint4*>(p);
+  v[0] = bf16_lo(u.x); v[1] = bf16_hi(u.x); v[2] = bf16_lo(u.y); v[3] = bf16_hi(u.y);
+  v[4] = bf16_lo(u.z); v[5] = bf16_hi(u.z); v[6] = bf16_lo(u.w); v[7] = bf16_hi(u.w);
+}
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+  const float4 a = *reinterpret_cast<const float4*>(p), b = *reinterpret_cast<const float4*>(p + 4);
+  v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(bf16* p, const float (&v)[8]) {
+  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
+                                            pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+  *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+  *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
 
-template <typename T>
-__device__ __forceinline__ void stf(T* p, float v);
-template <>
-__device__ __forceinline__ void stf<float>(float* p, float v) { *p = v; }
-template <>
-__device__ __forceinline__ void stf<bf16>(bf16* p, float v) { *p = __float2bfloat16(v); }
-
-// One warp per (row, 128-column tile). Writes q (optional), scale, and the
-// dequantised value (optional).
-template <typename T>
-__global__ void quant_tile_kernel(const T* __restrict__ x, int64_t rows, int cols, uint8_t* __restrict__ q,
-                                  float* __restrict__ scales, T* __restrict__ dq, int stochastic, uint64_t seed) {
-  const int warps = blockDim.x >> 5;
-  const int64_t tile = static_cast<int64_t>(blockIdx.x) * warps + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  const int ntc = cols / 128;
-  if (tile >= rows * ntc) return;
-  const int64_t r = tile / ntc;
-  const int tc = tile % ntc;
-  const int64_t base = r * cols + tc * 128;
-  float v[4];
-  float amax = 0.f;
+// Quantises 8 values with scale s (exact IEEE division, as the recipe states q = e4m3(x / s)),
+// optionally stochastically; returns the 8 codes packed little-endian, and the dequantised values.
+__device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, bool stochastic, uint64_t seed, int64_t idx0,
+                                        float (&dq)[8]) {
+  uint8_t b[8];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    v[j] = ldf(x + base + lane * 4 + j);
-    amax = fmaxf(amax, fabsf(v[j]));
+  for (int j = 0; j < 8; ++j) {
+    float y = fminf(fmaxf(__fdiv_rn(v[j], s), -448.f), 448.f);
+    if (stochastic) y = e4m3_sr(y, uniform01(seed, static_cast<uint64_t>(idx0 + j)));
+    b[j] = to_e4m3(y);
+    dq[j] = from_e4m3(b[j]) * s;
   }
-  amax = warp_max(amax);
-  const float s = amax > 0.f ? amax / 448.f : 1.f;
-  if (lane == 0) scales[r * ntc + tc] = s;
+  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (static_cast<uint32_t>(b[3]) << 24),
+                    b[4] | (b[5] << 8) | (b[6] << 16) | (static_cast<uint32_t>(b[7]) << 24));
+}
+
+// 1x128 tiles: a half-warp per (row, 128-column tile), 8 elements (one 16-byte load) per lane; the
+// tile's amax is reduced over the 16 lanes with shuffles. Writes the codes (8-byte stores), the
+// scale, and optionally the dequantised value. Grid-stride over tile pairs.
+template <typename T>
+__global__ void __launch_bounds__(256) quant_tile_kernel(const T* __restrict__ x, int64_t rows, int cols,
+                                                         uint8_t* __restrict__ q, float* __restrict__ scales,
+                                                         T* __restrict__ dq, int stochastic, uint64_t seed) {
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  const int ntc = cols / 128;
+  const int64_t tiles = rows * ntc;
+  const int64_t pairs = (tiles + 1) / 2;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < pairs;
+       w += nwarps) {
+    const int64_t tile = 2 * w + half;
+    const bool live = tile < tiles;
+    const int64_t r = live ? tile / ntc : 0;
+    const int tc = live ? static_cast<int>(tile % ntc) : 0;
+    const int64_t idx0 = r * cols + tc * 128 + hl * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (live) load8(x + idx0, v);
+    float amax = 0.f;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
-    const int64_t idx = base + lane * 4 + j;
-    float y = fminf(fmaxf(v[j] / s, -448.f), 448.f);
-    if (stochastic) y = e4m3_sr(y, uniform01(seed, static_cast<uint64_t>(idx)));
-    const uint8_t b = to_e4m3(y);
-    if (q) q[idx] = b;
-    if (dq) stf(dq + idx, from_e4m3(b) * s);
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+    if (!live) continue;
+    const float s = amax > 0.f ? amax / 448.f : 1.f;
+    if (hl == 0) scales[r * ntc + tc] = s;
+    float d[8];
+    const uint2 codes = quant8(v, s, stochastic != 0, seed, idx0, d);
+    if (q) *reinterpret_cast<uint2*>(q + idx0) = codes;
+    if (dq) store8(dq + idx0, d);
   }
 }
 
-// One CTA (256 threads) per 128 x 128 block.
+// 128x128 blocks: one CTA (256 threads) per block; pass 1 reduces the block's amax from 16-byte
+// loads (each thread 8 rows x 8 columns), pass 2 re-reads the block (L2-resident) and quantises.
+// The source may be a stack of groups read in place: row r lives at (r / rpg) * gstride + (r % rpg) *
+// cols (rpg = rows and gstride = 0 for a plain matrix; rpg a multiple of 128 otherwise, so no block
+// spans two groups). Codes, scales and dequantised values are written as one contiguous matrix.
 template <typename T>
-__global__ void quant_block_kernel(const T* __restrict__ x, int64_t rows, int cols, uint8_t* __restrict__ q,
-                                   float* __restrict__ scales, T* __restrict__ dq, int stochastic, uint64_t seed) {
+__global__ void __launch_bounds__(256) quant_block_kernel(const T* __restrict__ x, int64_t rows, int cols,
+                                                          uint8_t* __restrict__ q, float* __restrict__ scales,
+                                                          T* __restrict__ dq, int stochastic, uint64_t seed,
+                                                          int64_t rpg, int64_t gstride) {
   __shared__ float red[8];
   const int nbc = cols / 128;
   const int64_t br = blockIdx.x / nbc;
   const int bc = blockIdx.x % nbc;
   const int64_t r0 = br * 128;
+  const int c8 = (threadIdx.x & 15) * 8;  // column chunk of this thread
+  const int rsub = threadIdx.x >> 4;      // rows rsub, rsub + 16, ...
+  const T* xb = x + (r0 / rpg) * gstride - (r0 / rpg) * rpg * cols;  // row r of this block at xb + r * cols
   float amax = 0.f;
-  for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) {
-    const int64_t r = r0 + i / 128;
-    if (r < rows) amax = fmaxf(amax, fabsf(ldf(x + r * cols + bc * 128 + (i % 128))));
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = r0 + rsub + 16 * i;
+    if (r >= rows) break;
+    float v[8];
+    load8(xb + r * cols + bc * 128 + c8, v);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
   }
   amax = warp_max(amax);
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    t = warp_max(t);
-    if (threadIdx.x == 0) red[0] = t;
-  }
-  __syncthreads();
-  const float a = red[0];
+  float a = red[0];
+#pragma unroll
+  for (int k = 1; k < 8; ++k) a = fmaxf(a, red[k]);
   const float s = a > 0.f ? a / 448.f : 1.f;
   if (threadIdx.x == 0) scales[br * nbc + bc] = s;
-  for (int i = threadIdx.x; i < 128 * 128; i += blockDim.x) {
-    const int64_t r = r0 + i / 128;
-    if (r >= rows) continue;
-    const int64_t idx = r * cols + bc * 128 + (i % 128);
-    float y = fminf(fmaxf(ldf(x + idx) / s, -448.f), 448.f);
-    if (stochastic) y = e4m3_sr(y, uniform01(seed, static_cast<uint64_t>(idx)));
-    const uint8_t b = to_e4m3(y);
-    if (q) q[idx] = b;
-    if (dq) stf(dq + idx, from_e4m3(b) * s);
+  for (int i = 0; i < 8; ++i) {
+    const int64_t r = r0 + rsub + 16 * i;
+    if (r >= rows) break;
+    const int64_t idx0 = r * cols + bc * 128 + c8;
+    float v[8], d[8];
+    load8(xb + idx0, v);
+    const uint2 codes = quant8(v, s, stochastic != 0, seed, idx0, d);
+    if (q) *reinterpret_cast<uint2*>(q + idx0) = codes;
+    if (dq) store8(dq + idx0, d);
   }
 }
 
-// Dequantise e4m3 bytes with tile (block_rows = 1) or block (128) scales.
+// Dequantise e4m3 bytes with tile (block_rows = 1) or block (128) scales, 8 codes per thread.
 template <typename T>
-__global__ void dequant_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scales, int64_t rows, int cols,
-                               int block_rows, T* __restrict__ out) {
-  const int64_t n = rows * cols;
+__global__ void __launch_bounds__(256) dequant_kernel(const uint8_t* __restrict__ q, const float* __restrict__ scales,
+                                                      int64_t rows, int cols, int block_rows, T* __restrict__ out) {
+  const int64_t n8 = rows * cols / 8;
   const int ntc = cols / 128;
-  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < n8;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t r = i / cols;
-    const int c = i % cols;
+    const int64_t e = i * 8;
+    const int64_t r = e / cols;
+    const int c = static_cast<int>(e - r * cols);
     const float s = scales[(r / block_rows) * ntc + c / 128];
-    stf(out + i, from_e4m3(q[i]) * s);
+    const uint2 u = *reinterpret_cast<const uint2*>(q + e);
+    float v[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      v[j] = from_e4m3(static_cast<uint8_t>(u.x >> (8 * j))) * s;
+      v[4 + j] = from_e4m3(static_cast<uint8_t>(u.y >> (8 * j))) * s;
+    }
+    store8(out + e, v);
   }
 }
 
@@ -134,25 +174,27 @@ static void launch_quant(const at::Tensor& x, int block_rows, bool stochastic, i
   if (x.scalar_type() == at::kBFloat16) {
     const bf16* xp = reinterpret_cast<const bf16*>(x.data_ptr());
     if (block_rows == 1) {
-      const int64_t tiles = rows * (cols / 128);
-      quant_tile_kernel<bf16><<<(tiles + 7) / 8, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<bf16*>(dq),
-                                                                  stochastic, sd);
+      const int64_t pairs = (rows * (cols / 128) + 1) / 2;
+      const int grid = static_cast<int>(std::min<int64_t>((pairs + 7) / 8, 16L * num_sms(x.get_device())));
+      quant_tile_kernel<bf16><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<bf16*>(dq), stochastic,
+                                                        sd);
     } else {
       const int64_t blocks = ((rows + 127) / 128) * (cols / 128);
       quant_block_kernel<bf16><<<blocks, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<bf16*>(dq),
-                                                           stochastic, sd);
+                                                           stochastic, sd, rows, 0);
     }
   } else {
     TORCH_CHECK(x.scalar_type() == at::kFloat, "fp8 quantiser: bf16 or fp32 input");
     const float* xp = x.data_ptr<float>();
     if (block_rows == 1) {
-      const int64_t tiles = rows * (cols / 128);
-      quant_tile_kernel<float><<<(tiles + 7) / 8, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<float*>(dq),
-                                                                   stochastic, sd);
+      const int64_t pairs = (rows * (cols / 128) + 1) / 2;
+      const int grid = static_cast<int>(std::min<int64_t>((pairs + 7) / 8, 16L * num_sms(x.get_device())));
+      quant_tile_kernel<float><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<float*>(dq),
+                                                         stochastic, sd);
     } else {
       const int64_t blocks = ((rows + 127) / 128) * (cols / 128);
       quant_block_kernel<float><<<blocks, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<float*>(dq),
-                                                            stochastic, sd);
+                                                            stochastic, sd, rows, 0);
     }
   }
   NTB_LAUNCH_CHECK(1);
@@ -185,15 +227,40 @@ at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stoch
   return out;
 }
 
+// Rounds a stack of `groups` matrices [rows_per_group, cols] (bf16), read in place from `src` at
+// element offsets g * group_stride, through e4m3 with 128 x 128 block scales; returns the rounded
+// stack as one contiguous [groups * rows_per_group, cols] matrix. `src` only supplies the start
+// address (its storage must hold every group).
+at::Tensor fp8_quant_dequant_strided(const at::Tensor& src, int64_t groups, int64_t rows_per_group, int64_t cols,
+                                     int64_t group_stride) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16, "fp8_quant_dequant_strided: bf16 CUDA source");
+  TORCH_CHECK(groups >= 1 && rows_per_group % 128 == 0 && cols % 128 == 0 && group_stride >= rows_per_group * cols &&
+                  group_stride % 8 == 0,
+              "fp8_quant_dequant_strided: rows per group and columns must be multiples of 128, groups must not overlap");
+  const int64_t need = (src.storage_offset() + (groups - 1) * group_stride + rows_per_group * cols) * 2;
+  TORCH_CHECK(static_cast<int64_t>(src.storage().nbytes()) >= need && (reinterpret_cast<uintptr_t>(src.data_ptr()) & 15) == 0,
+              "fp8_quant_dequant_strided: source storage too small or misaligned");
+  const int64_t rows = groups * rows_per_group;
+  auto out = at::empty({rows, cols}, src.options());
+  auto s = at::empty({rows / 128, cols / 128}, src.options().dtype(at::kFloat));
+  const int64_t blocks = (rows / 128) * (cols / 128);
+  quant_block_kernel<bf16><<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(src.data_ptr()), rows, static_cast<int>(cols), nullptr, s.data_ptr<float>(),
+      reinterpret_cast<bf16*>(out.data_ptr()), 0, 0, rows_per_group, group_stride);
+  NTB_LAUNCH_CHECK(1);
+  return out;
+}
+
 at::Tensor fp8_dequantize(const at::Tensor& q, const at::Tensor& scales, int64_t block_rows, at::ScalarType dtype) {
   TORCH_CHECK(q.is_cuda() && q.dim() == 2 && q.is_contiguous() && q.scalar_type() == at::kByte, "fp8_dequantize: q");
   const int64_t rows = q.size(0);
   const int cols = static_cast<int>(q.size(1));
   auto out = at::empty({rows, cols}, q.options().dtype(dtype));
   if (rows == 0) return out;
+  TORCH_CHECK(cols % 128 == 0, "fp8_dequantize: columns must be a multiple of 128");
   auto stream = at::cuda::getCurrentCUDAStream();
-  const int64_t n = rows * cols;
-  const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 16));
+  const int64_t n8 = rows * cols / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((n8 + 255) / 256, 16L * num_sms(q.get_device())));
   if (dtype == at::kBFloat16)
     dequant_kernel<bf16><<<blocks, 256, 0, stream>>>(q.data_ptr<uint8_t>(), scales.data_ptr<float>(), rows, cols,
                                                      static_cast<int>(block_rows), reinterpret_cast<bf16*>(out.data_ptr()));

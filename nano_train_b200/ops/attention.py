@@ -19,9 +19,12 @@ _KERNEL_HEAD_DIMS = {(64, 64), (128, 128), (192, 128)}
 
 
 def _fwd(q, k, v, scale: float, causal: bool):
-    """Forward kernel choice: the tcgen05 kernel for head dim 128, the mma.sync kernel otherwise."""
+    """Forward kernel: the tcgen05 kernel for every supported head-dim pair ((128, 128), MLA's (192, 128),
+    (64, 64)); ``NTB_ATTN_FWD_LEGACY=1`` selects the mma.sync kernel (kept as a cross-check)."""
+    import os
+
     C = ext()
-    if q.shape[-1] == 128 and v.shape[-1] == 128:
+    if os.environ.get("NTB_ATTN_FWD_LEGACY") != "1":
         return C.flash_attn_fwd_tc(q, k, v, float(scale), bool(causal))
     return C.flash_attn_fwd(q, k, v, float(scale), bool(causal))
 

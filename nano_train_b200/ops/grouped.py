@@ -61,21 +61,51 @@ class _StackCache:
             self._params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
         return self._params
 
+    @staticmethod
+    def _expert_stride(params) -> int:
+        """Element stride between consecutive experts when every expert's (gate, up, down) sit back to
+        back in one storage at a constant stride (the flat optimizer's parameter layout), else 0."""
+        g0, u0, d0 = params[0], params[1], params[2]
+        if not (g0.is_cuda and g0.dtype == torch.bfloat16 and g0.is_contiguous()):
+            return 0
+        es = g0.element_size()
+        st = g0.untyped_storage().data_ptr()
+        stride = (params[3].data_ptr() - g0.data_ptr()) // es if len(params) > 3 else 0
+        for e in range(len(params) // 3):
+            g, u, d = params[3 * e: 3 * e + 3]
+            if (g.untyped_storage().data_ptr() != st or not (g.is_contiguous() and u.is_contiguous()
+                                                            and d.is_contiguous())
+                    or g.data_ptr() != g0.data_ptr() + e * stride * es
+                    or u.data_ptr() != g.data_ptr() + g.numel() * es
+                    or d.data_ptr() != d0.data_ptr() + e * stride * es):
+                return 0
+        return stride if len(params) > 3 else g0.numel() + u0.numel() + d0.numel()
+
     def get(self, experts, fp8: bool = False):
         """(w1, w2); with ``fp8`` every expert matrix is rounded through e4m3 in 128 x 128 blocks
-        first (the recipe's weight quantisation), so the bf16 GEMMs see the fp8 values."""
+        first (the recipe's weight quantisation), so the bf16 GEMMs see the fp8 values. When the
+        experts' weights lie at a constant stride in one buffer, the rounded stacks are written in
+        one pass from the parameters in place (no concatenation first)."""
         params = self.params(experts)
         key = (bool(fp8),) + tuple((p.data_ptr(), p._version) for p in params)
         if key != self.key:
             with torch.no_grad():
-                self.w1 = torch.cat([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in experts], 0)
-                self.w2 = torch.cat([e.down_proj.weight for e in experts], 0)
-                if fp8:
-                    # One launch per stack: every expert matrix has a multiple of 128 rows (the fp8 grouped
-                    # path requires H % 128 == 0 and I % 128 == 0), so no 128 x 128 block spans two matrices
-                    # and the result equals rounding each matrix on its own.
-                    self.w1 = ext().fp8_quant_dequant(self.w1, 128, False, 0)
-                    self.w2 = ext().fp8_quant_dequant(self.w2, 128, False, 0)
+                E = len(experts)
+                stride = self._expert_stride(params) if fp8 else 0
+                g, d = params[0], params[2]
+                if stride and g.shape[0] % 128 == 0 and g.shape[1] % 128 == 0 and d.shape[1] % 128 == 0:
+                    C = ext()
+                    self.w1 = C.fp8_quant_dequant_strided(g, E, 2 * g.shape[0], g.shape[1], stride)
+                    self.w2 = C.fp8_quant_dequant_strided(d, E, d.shape[0], d.shape[1], stride)
+                else:
+                    self.w1 = torch.cat([torch.cat([e.gate_proj.weight, e.up_proj.weight], 0) for e in experts], 0)
+                    self.w2 = torch.cat([e.down_proj.weight for e in experts], 0)
+                    if fp8:
+                        # Every expert matrix has a multiple of 128 rows (the fp8 grouped path requires
+                        # H % 128 == 0 and I % 128 == 0), so no 128 x 128 block spans two matrices and
+                        # rounding the stack equals rounding each matrix on its own.
+                        self.w1 = ext().fp8_quant_dequant(self.w1, 128, False, 0)
+                        self.w2 = ext().fp8_quant_dequant(self.w2, 128, False, 0)
             self.key = key
         return self.w1, self.w2
 

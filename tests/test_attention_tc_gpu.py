@@ -1,4 +1,4 @@
-"""tcgen05 flash-attention forward (head dim 128) vs fp32 PyTorch and the mma.sync kernel."""
+"""tcgen05 flash attention (head dims 128, MLA 192/128 and 64) vs fp32 PyTorch and the mma.sync kernel."""
 import pytest
 import torch
 
@@ -73,3 +73,35 @@ def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, monkeypatch):
     torch.cuda.synchronize()
     for name, g, r in (("dq", dq, dq2), ("dk", dk, dk2), ("dv", dv, dv2)):
         assert _rel(g, r) < 2e-2, (name, "vs legacy", _rel(g, r))
+
+
+@pytest.mark.parametrize("dqk,dv", [(192, 128), (64, 64)])
+@pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 2, 2, False),
+                                               (1, 130, 2, 1, True)])
+def test_flash_tc_mla_and_hd64_match_reference(dqk, dv, B, S, hq, hkv, causal):
+    """MLA head dims (q/k 192 = [nope 128 | rope 64], v 128) and head dim 64 on the tcgen05 kernels,
+    forward and backward, against fp32 PyTorch; q, k, v are strided views of one buffer."""
+    from nano_train_b200.ops._ext import check_status, ext
+
+    torch.manual_seed(dqk + S + hq * 3 + int(causal))
+    dev = torch.device("cuda", 0)
+    width = hq * dqk + hkv * (dqk + dv)
+    buf = torch.randn(B, S, width, device=dev, dtype=torch.bfloat16)
+    q = buf[..., : hq * dqk].view(B, S, hq, dqk)
+    k = buf[..., hq * dqk: hq * dqk + hkv * dqk].view(B, S, hkv, dqk)
+    v = buf[..., hq * dqk + hkv * dqk:].view(B, S, hkv, dv)
+    scale = dqk ** -0.5
+    o, lse = ext().flash_attn_fwd_tc(q, k, v, scale, causal)
+    do = torch.randn_like(o)
+    dq, dk, dvv = ext().flash_attn_bwd(do, q, k, v, o, lse, scale, causal)
+    torch.cuda.synchronize()
+    check_status(0)
+    qf, kf, vf = (t.float().detach().requires_grad_(True) for t in (q, k, v))
+    ref = attention_reference(qf, kf, vf, causal=causal, scale=scale)
+    assert _rel(o, ref) < 1e-2
+    ref.backward(do.float())
+    for name, g, r in (("dq", dq, qf.grad), ("dk", dk, kf.grad), ("dv", dvv, vf.grad)):
+        assert _rel(g, r) < 2e-2, (name, _rel(g, r))
+    o2, lse2 = ext().flash_attn_fwd(q, k, v, scale, causal)  # the mma.sync kernel as a second opinion
+    assert _rel(o, o2) < 1e-2
+    torch.testing.assert_close(lse, lse2, rtol=1e-3, atol=1e-3)
