@@ -116,12 +116,41 @@ class TensorCoreModel:
             if not (0.0 <= v <= 1.0):
                 raise ValueError(f"eligible[{k}] must be in [0, 1]")
 
+    def eta(self, rows: float) -> float:
+        """Tensor-core saturation at GEMM height ``rows`` (tokens per GEMM, or per active expert)."""
+        return 1.0 if not self.enabled else min(1.0, max(rows, 1e-9) / self.b_sat)
+
     def realizable(self, flops: float, rows: float, kind: str) -> float:
+        """Peak-equivalent FLOPs: eligible work at the tensor cores' saturation, the rest at eta_scalar
+        (so realizable / peak is the modelled compute time)."""
+        return self.breakdown(flops, rows, kind).realizable
+
+    def breakdown(self, flops: float, rows: float, kind: str) -> "FlopBreakdown":
         if not self.enabled or flops == 0:
-            return flops
+            return FlopBreakdown(flops, flops, flops, 1.0)
         e = self.eligible.get(kind, 0.0)
-        eta = min(1.0, max(rows, 1e-9) / self.b_sat)
-        return flops * (e / eta + (1.0 - e) / self.eta_scalar)
+        eta = self.eta(rows)
+        return FlopBreakdown(theory=flops, tensorcore=flops * e,
+                             realizable=flops * (e / eta + (1.0 - e) / self.eta_scalar), eta_tc=eta)
+
+
+@dataclass
+class FlopBreakdown:
+    """Theory FLOPs, the tensor-core-eligible part, the peak-equivalent (realizable) cost and the
+    tensor-core saturation of one piece of work; breakdowns add up across layers."""
+    theory: float
+    tensorcore: float
+    realizable: float
+    eta_tc: float = 1.0
+
+    def __add__(self, o: "FlopBreakdown") -> "FlopBreakdown":
+        tc = self.tensorcore + o.tensorcore
+        eta = (self.tensorcore * self.eta_tc + o.tensorcore * o.eta_tc) / tc if tc else 1.0  # eligible-FLOP weighted
+        return FlopBreakdown(self.theory + o.theory, tc, self.realizable + o.realizable, eta)
+
+    def p_effective_tflops(self, peak_tflops: float) -> float:
+        """Throughput the modelled execution sustains on this work: peak x theory / realizable."""
+        return peak_tflops * self.theory / self.realizable if self.realizable else peak_tflops
 
 
 @dataclass
@@ -230,6 +259,9 @@ class ModeKpi:
     tokens: int
     flops_theory: float
     flops_realizable: float
+    flops_tensorcore: float
+    eta_tc: float
+    p_effective_tflops: float
     bytes_weights: float
     bytes_activations: float
     bytes_kv: float
@@ -293,7 +325,7 @@ def _mode_kpi(arch, layers, mode, batch, seq_len, ctx, par: ParallelismAssumptio
     gpus = par.gpus
     # FLOPs, theory and realizable (per class, rows per GEMM per GPU)
     rows_dense = tokens / max(par.dp * par.ep, 1)
-    f_th = f_re = 0.0
+    fb = FlopBreakdown(0.0, 0.0, 0.0)
     w_dense = w_exp = 0.0
     for l in layers:
         if l.kind == "embedding":
@@ -302,16 +334,15 @@ def _mode_kpi(arch, layers, mode, batch, seq_len, ctx, par: ParallelismAssumptio
         frac = (K / E) if (l.kind == "expert" and E) else l.active_fraction
         f = mult * tokens * 2.0 * l.in_features * l.out_features * frac * hs * hs
         rows = rows_dense * (K / E if (l.kind == "expert" and E) else 1.0) * (par.ep if l.kind == "expert" else 1)
-        f_th += f
-        f_re += tc.realizable(f, rows, "linear")
+        fb = fb + tc.breakdown(f, rows, "linear")
         if l.kind == "expert":
             cover = 1.0 if mode != "decode" else 1.0 - (1.0 - (K / E if E else 1.0)) ** max(tokens, 1)
             w_exp += l.params * hs * hs * cover
         else:
             w_dense += l.params * hs * hs
     fa = mult * tokens * _attn_flops_per_token(arch, ctx, causal, hs)
-    f_th += fa
-    f_re += tc.realizable(fa, rows_dense, "attention")
+    fb = fb + tc.breakdown(fa, rows_dense, "attention")
+    f_th, f_re = fb.theory, fb.realizable
     # HBM bytes (whole job)
     wb = weight_bytes
     if train:  # forward + backward weight reads, fp32 gradient accumulate (8 B), optimizer pass (28 B)
@@ -358,7 +389,8 @@ def _mode_kpi(arch, layers, mode, batch, seq_len, ctx, par: ParallelismAssumptio
     regime = "compute" if t_est == t_comp else ("hbm" if t_est == t_hbm else "network")
     hbm_total = w_bytes + act + kv + temp
     return ModeKpi(mode=mode, exec_model=xm.name, target=target.name, tokens=tokens, flops_theory=f_th,
-                   flops_realizable=f_re, bytes_weights=w_bytes, bytes_activations=act, bytes_kv=kv,
+                   flops_realizable=f_re, flops_tensorcore=fb.tensorcore, eta_tc=fb.eta_tc,
+                   p_effective_tflops=fb.p_effective_tflops(target.peak_tflops), bytes_weights=w_bytes, bytes_activations=act, bytes_kv=kv,
                    bytes_temporary=temp, bytes_hbm=hbm_total, bytes_net=net * gpus,
                    ai_hbm=f_th / hbm_total if hbm_total else 0.0,
                    ai_total=f_th / (hbm_total + net * gpus) if hbm_total + net else 0.0,
@@ -581,10 +613,12 @@ def render_markdown(info: ModelInfo, extras: Optional[dict] = None) -> str:
     for l in sorted(info.layers, key=lambda l: -l.params)[:15]:
         lines.append(f"| {l.name} | {l.kind} | {_fmt(l.params)} | {l.active_fraction:.3f} |")
     lines += h("Mode estimates (per GPU)")
-    lines += ["| mode | exec | target | FLOP theory | FLOP realizable | HBM bytes | net bytes | AI | t_comp | t_hbm | "
-              "t_net | t_est | regime | MFU est | tok/s/GPU |", "|" + "---|" * 15]
+    lines += ["| mode | exec | target | FLOP theory | FLOP tensor-core | eta_tc | FLOP realizable | P_eff TFLOP/s | "
+              "HBM bytes | net bytes | AI | t_comp | t_hbm | t_net | t_est | regime | MFU est | tok/s/GPU |",
+              "|" + "---|" * 18]
     for k in info.kpis:
-        lines.append(f"| {k.mode} | {k.exec_model} | {k.target} | {_fmt(k.flops_theory)} | {_fmt(k.flops_realizable)} | "
+        lines.append(f"| {k.mode} | {k.exec_model} | {k.target} | {_fmt(k.flops_theory)} | {_fmt(k.flops_tensorcore)} | "
+                     f"{k.eta_tc:.3f} | {_fmt(k.flops_realizable)} | {k.p_effective_tflops:.0f} | "
                      f"{_fmt(k.bytes_hbm, 'B')} | {_fmt(k.bytes_net, 'B')} | {k.ai_hbm:.1f} | {k.t_comp_ms:.3f} | "
                      f"{k.t_hbm_ms:.3f} | {k.t_net_ms:.3f} | {k.t_est_ms:.3f} | {k.regime} | {k.mfu_est:.3f} | "
                      f"{k.tokens_per_s_per_gpu:.1f} |")
