@@ -800,6 +800,351 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
+// Pipelined backward for head dims <= 128 (flash_bwd_tc_pipe_kernel). Same math and outputs as
+// flash_bwd_tc_kernel, with a schedule that keeps the tensor core fed across query blocks:
+//   * Q is double-buffered in shared memory (Q(i+1) is loaded while block i is processed); P^T and
+//     dS^T share one tile (dS^T is stored once the dV MMA that reads P^T has completed);
+//   * dQ is computed into dP^T's TMEM columns, so S^T(i+1) = K Q(i+1)^T is issued right after the
+//     dK / dQ MMAs of block i and runs while the threads drain dQ(i) into the fp32 accumulator;
+//     dP^T(i+1) follows once that readout is done.
+// TMEM: S^T [0, 128), dP^T / dQ [128, 256), dK [256, 256 + DQK), dV [256 + DQK, ... + DV).
+namespace attn_tc_bwd {
+template <int DQK, int DV>
+struct BwdPipeCfg {
+  static_assert(DQK % 64 == 0 && DV % 64 == 0 && DQK <= 128 && DV <= 128, "head dims");
+  static constexpr int QB = DQK / 64, VB = DV / 64;
+  static constexpr int Q_BYTES = QB * BOX, V_BYTES = VB * BOX;
+  static constexpr int S_K = 0, S_V = S_K + Q_BYTES, S_Q = S_V + V_BYTES, S_DO = S_Q + 2 * Q_BYTES;
+  static constexpr int S_P = S_DO + V_BYTES;  // P^T, then dS^T
+  static constexpr int S_LSE = S_P + PT;
+  static constexpr int S_BAR = S_LSE + 4 * 128 * 4;
+  static constexpr int SMEM_BYTES = 1024 + S_BAR + 256;
+  static constexpr uint32_t COL_S = 0, COL_DP = 128, COL_DK = 256, COL_DV = 256 + DQK;
+  static_assert(SMEM_BYTES <= 232448, "shared memory");
+};
+}  // namespace attn_tc_bwd
+
+template <int DQK, int DV>
+__global__ void __launch_bounds__(192, 1)
+    flash_bwd_tc_pipe_kernel(const __grid_constant__ CUtensorMap tmQ, const __grid_constant__ CUtensorMap tmK,
+                             const __grid_constant__ CUtensorMap tmV, const __grid_constant__ CUtensorMap tmDO,
+                             AttnTcBwdParams p) {
+  using namespace attn_tc_bwd;
+  using attn_tc::ex2_approx;
+  using attn_tc::warp_wait;
+  using Cfg = BwdPipeCfg<DQK, DV>;
+  constexpr int S_K = Cfg::S_K, S_V = Cfg::S_V, S_Q = Cfg::S_Q, S_DO = Cfg::S_DO, S_P = Cfg::S_P,
+                S_LSE = Cfg::S_LSE, S_BAR = Cfg::S_BAR;
+  constexpr uint32_t COL_S = Cfg::COL_S, COL_DP = Cfg::COL_DP, COL_DK = Cfg::COL_DK, COL_DV = Cfg::COL_DV;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + S_BAR);
+  uint64_t* kv_full = bars + 0;
+  uint64_t* q_full = bars + 1;       // [2]
+  uint64_t* q_free = bars + 3;       // [2] dK of the block in this slot completed
+  uint64_t* do_full = bars + 5;
+  uint64_t* do_free = bars + 6;      // dP^T and dV of the block completed
+  uint64_t* s_full = bars + 7;       // S^T ready
+  uint64_t* dp_full = bars + 8;      // dP^T ready
+  uint64_t* p_ready = bars + 9;      // P^T in smem, S^T read (128 arrivals)
+  uint64_t* dv_done = bars + 10;     // dV MMA completed: the P^T tile may be overwritten
+  uint64_t* ds_ready = bars + 11;    // dS^T in smem, dP^T read (128 arrivals)
+  uint64_t* dq_full = bars + 12;     // dK and dQ MMAs completed
+  uint64_t* dq_free = bars + 13;     // dQ read out of TMEM (128 arrivals)
+  uint64_t* kv_done = bars + 14;
+  uint64_t* stats_ready = bars + 15; // lse/delta of the iteration written (128 arrivals)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
+  float* s_lse_all = reinterpret_cast<float*>(smem + S_LSE);  // [2][128]
+  float* s_delta_all = s_lse_all + 256;                        // [2][128]
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int kb = blockIdx.x;
+  const int hq = blockIdx.y, b = blockIdx.z;
+  const int hk = hq / (p.Hq / p.Hkv);
+  const int k0 = kb * BN;
+  const int nqb = (p.S + BM - 1) / BM;
+  const int qb_first = p.causal ? kb : 0;
+  const int iters = nqb - qb_first;
+
+  if (threadIdx.x == 0) {
+    mbar_init(kv_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&q_full[i], 1);
+      mbar_init(&q_free[i], 1);
+    }
+    mbar_init(do_full, 1);
+    mbar_init(do_free, 1);
+    mbar_init(s_full, 1);
+    mbar_init(dp_full, 1);
+    mbar_init(p_ready, 128);
+    mbar_init(dv_done, 1);
+    mbar_init(ds_ready, 128);
+    mbar_init(dq_full, 1);
+    mbar_init(dq_free, 128);
+    mbar_init(kv_done, 1);
+    mbar_init(stats_ready, 128);
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmQ);
+    tma_prefetch_desc(&tmK);
+    tma_prefetch_desc(&tmV);
+    tma_prefetch_desc(&tmDO);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      mbar_expect_tx(kv_full, Cfg::Q_BYTES + Cfg::V_BYTES);
+      for (int c = 0; c < Cfg::QB; ++c) tma_load_4d(smem + S_K + c * BOX, &tmK, kv_full, c * 64, k0, hk, b);
+      for (int c = 0; c < Cfg::VB; ++c) tma_load_4d(smem + S_V + c * BOX, &tmV, kv_full, c * 64, k0, hk, b);
+      for (int it = 0; it < iters; ++it) {
+        const int q0 = (qb_first + it) * BM;
+        const int qs = it & 1;
+        if (!mbar_wait(&q_free[qs], static_cast<uint32_t>((it >> 1) & 1) ^ 1u, p.status, kStatusTimeoutProducer))
+          break;
+        mbar_expect_tx(&q_full[qs], Cfg::Q_BYTES);
+        for (int c = 0; c < Cfg::QB; ++c)
+          tma_load_4d(smem + S_Q + qs * Cfg::Q_BYTES + c * BOX, &tmQ, &q_full[qs], c * 64, q0, hq, b);
+        if (!mbar_wait(do_free, static_cast<uint32_t>(it & 1) ^ 1u, p.status, kStatusTimeoutProducer)) break;
+        mbar_expect_tx(do_full, Cfg::V_BYTES);
+        for (int c = 0; c < Cfg::VB; ++c) tma_load_4d(smem + S_DO + c * BOX, &tmDO, do_full, c * 64, q0, hq, b);
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t ID_KK = make_idesc_f16(BM, BN, false, false);
+      constexpr uint32_t ID_DV = make_idesc_f16(BM, DV, false, true);
+      constexpr uint32_t ID_DK = make_idesc_f16(BM, DQK, false, true);
+      constexpr uint32_t ID_NN = make_idesc_f16(BM, DQK, true, true);
+      const uint32_t sK = smem_u32(smem + S_K), sV = smem_u32(smem + S_V), sDO = smem_u32(smem + S_DO),
+                     sP = smem_u32(smem + S_P);
+      auto kdesc = [](uint32_t base, int kk) { return make_smem_desc_sw128(base + (kk >> 2) * BOX + (kk & 3) * 32, 16, 1024); };
+      auto ndesc = [](uint32_t base, int kk) { return make_smem_desc_sw128(base + kk * 2048, BOX, 1024); };
+      auto sq = [&](int it) { return smem_u32(smem + S_Q + (it & 1) * Cfg::Q_BYTES); };
+      auto issue_s = [&](int it) {
+#pragma unroll
+        for (int kk = 0; kk < DQK / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_S, kdesc(sK, kk), kdesc(sq(it), kk), ID_KK, kk > 0 ? 1u : 0u);
+        umma_commit(s_full);
+      };
+      auto issue_dp = [&]() {
+#pragma unroll
+        for (int kk = 0; kk < DV / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DP, kdesc(sV, kk), kdesc(sDO, kk), ID_KK, kk > 0 ? 1u : 0u);
+        umma_commit(dp_full);
+      };
+      bool ok = mbar_wait(kv_full, 0, p.status, kStatusTimeoutMma) && iters > 0 &&
+                mbar_wait(&q_full[0], 0, p.status, kStatusTimeoutMma) && mbar_wait(do_full, 0, p.status, kStatusTimeoutMma);
+      if (ok) {
+        tc_fence_after();
+        issue_s(0);
+        issue_dp();
+      }
+      for (int it = 0; ok && it < iters; ++it) {
+        const uint32_t par = static_cast<uint32_t>(it & 1);
+        if (!mbar_wait(p_ready, par, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DV, kdesc(sP, kk), ndesc(sDO, kk), ID_DV, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(do_free);
+        umma_commit(dv_done);
+        if (!mbar_wait(ds_ready, par, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < BM / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DK, kdesc(sP, kk), ndesc(sq(it), kk), ID_DK, (it > 0 || kk > 0) ? 1u : 0u);
+        umma_commit(&q_free[it & 1]);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk)
+          umma_f16_ss(tmem_base + COL_DP, ndesc(sP, kk), ndesc(sK, kk), ID_NN, kk > 0 ? 1u : 0u);
+        umma_commit(dq_full);
+        if (it + 1 < iters) {
+          const int nx = it + 1;
+          if (!mbar_wait(&q_full[nx & 1], static_cast<uint32_t>((nx >> 1) & 1), p.status, kStatusTimeoutMma)) break;
+          tc_fence_after();
+          issue_s(nx);  // S^T(it) was read before p_ready(it)
+          if (!mbar_wait(do_full, static_cast<uint32_t>(nx & 1), p.status, kStatusTimeoutMma) ||
+              !mbar_wait(dq_free, par, p.status, kStatusTimeoutMma))
+            break;
+          tc_fence_after();
+          issue_dp();  // dQ(it) has been read out of these columns
+        }
+      }
+      umma_commit(kv_done);
+      mbar_wait(kv_done, 0, nullptr, 0);
+    }
+  } else {
+    // ------------------------------------------------------------ compute warps
+    const int quarter = warp & 3;
+    const int r = quarter * 32 + lane;  // key row for S^T/dP^T/dK/dV; query row for dQ
+    const int key = k0 + r;
+    const uint32_t lane_addr = static_cast<uint32_t>(quarter * 32) << 16;
+    const int ctid = threadIdx.x - 64;
+    uint8_t* sP = smem + S_P;
+    bool ok = true;
+    auto load_stats = [&](int itx, float& lv, float& dv) {
+      const int qx = (qb_first + itx) * BM + ctid;
+      const int64_t o = (static_cast<int64_t>(b) * p.Hq + hq) * p.S + qx;
+      lv = qx < p.S ? p.lse[o] : INFINITY;
+      dv = qx < p.S ? p.delta[o] : 0.f;
+    };
+    float next_lse = 0.f, next_delta = 0.f;
+    if (iters > 0) load_stats(0, next_lse, next_delta);
+    for (int it = 0; it < iters; ++it) {
+      const int q0 = (qb_first + it) * BM;
+      const uint32_t par = static_cast<uint32_t>(it & 1);
+      float* s_lse = s_lse_all + (it & 1) * 128;
+      float* s_delta = s_delta_all + (it & 1) * 128;
+      s_lse[ctid] = next_lse;
+      s_delta[ctid] = next_delta;
+      if (it + 1 < iters) load_stats(it + 1, next_lse, next_delta);
+      mbar_arrive(stats_ready);
+      if (!warp_wait(stats_ready, par, p.status, kStatusTimeoutEpilogue) ||
+          !warp_wait(s_full, par, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool diag = p.causal && q0 == k0;
+      const bool row_dead = key >= p.S;
+      // P^T row: packed bf16 in registers (for dS^T) and stored to the shared tile (for dV). The
+      // tile held dS^T(it - 1), whose MMAs completed before dq_full(it - 1) was observed.
+      uint32_t pk[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t sr[32];
+        tmem_ld32(tmem_base + lane_addr + COL_S + c * 32, sr);
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const int qa = c * 32 + t;
+          float e0 = ex2_approx(fmaf(__uint_as_float(sr[t]), p.scale_log2, -s_lse[qa]));
+          float e1 = ex2_approx(fmaf(__uint_as_float(sr[t + 1]), p.scale_log2, -s_lse[qa + 1]));
+          if (row_dead || (diag && r > qa)) e0 = 0.f;
+          if (row_dead || (diag && r > qa + 1)) e1 = 0.f;
+          pk[(c * 32 + t) >> 1] = pack_bf16x2(e0, e1);
+        }
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        const uint4 v = make_uint4(pk[c16 * 4], pk[c16 * 4 + 1], pk[c16 * 4 + 2], pk[c16 * 4 + 3]);
+        *reinterpret_cast<uint4*>(sP + (c16 >> 3) * BOX + r * 128 + (((c16 & 7) ^ (r & 7)) << 4)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(p_ready);
+      // dS^T = P^T * (dP^T - delta), kept packed until the dV MMA has finished reading P^T.
+      if (!warp_wait(dp_full, par, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t ds[64];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t dr[32];
+        tmem_ld32(tmem_base + lane_addr + COL_DP + c * 32, dr);
+#pragma unroll
+        for (int t = 0; t < 32; t += 2) {
+          const int qa = c * 32 + t;
+          const uint32_t pp = pk[qa >> 1];
+          const float d0 = bf16_lo(pp) * (__uint_as_float(dr[t]) - s_delta[qa]);
+          const float d1 = bf16_hi(pp) * (__uint_as_float(dr[t + 1]) - s_delta[qa + 1]);
+          ds[qa >> 1] = pack_bf16x2(d0, d1);
+        }
+      }
+      if (!warp_wait(dv_done, par, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+#pragma unroll
+      for (int c16 = 0; c16 < 16; ++c16) {
+        const uint4 v = make_uint4(ds[c16 * 4], ds[c16 * 4 + 1], ds[c16 * 4 + 2], ds[c16 * 4 + 3]);
+        *reinterpret_cast<uint4*>(sP + (c16 >> 3) * BOX + r * 128 + (((c16 & 7) ^ (r & 7)) << 4)) = v;
+      }
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(ds_ready);
+      // dQ(it) (lanes = queries) from dP^T's columns -> fp32 accumulator.
+      if (!warp_wait(dq_full, par, p.status, kStatusTimeoutEpilogue)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int q = q0 + r;
+      float* dst = p.dq_acc + ((static_cast<int64_t>(b) * p.Hq + hq) * p.S + (q < p.S ? q : 0)) * DQK;
+#pragma unroll
+      for (int c = 0; c < DQK / 32; ++c) {
+        uint32_t qr[32];
+        tmem_ld32(tmem_base + lane_addr + COL_DP + c * 32, qr);
+        if (q < p.S) {
+#pragma unroll
+          for (int t = 0; t < 32; t += 4)
+            red_add_v4(dst + c * 32 + t, __uint_as_float(qr[t]), __uint_as_float(qr[t + 1]),
+                       __uint_as_float(qr[t + 2]), __uint_as_float(qr[t + 3]));
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(dq_free);
+    }
+    if (ok && warp_wait(kv_done, 0, p.status, kStatusTimeoutEpilogue)) {
+      tc_fence_after();
+      const bool valid = key < p.S;
+      const int64_t krow = valid ? key : 0;
+#pragma unroll 1
+      for (int which = 0; which < 2; ++which) {
+        const uint32_t col = which == 0 ? COL_DK : COL_DV;
+        const int width = which == 0 ? DQK : DV;
+        const float sc = which == 0 ? p.scale : 1.f;
+        float* accp = which == 0 ? p.dk_acc : p.dv_acc;
+        __nv_bfloat16* out = which == 0 ? p.dk + b * p.dk_sb + krow * p.dk_ss + hk * p.dk_sh
+                                        : p.dv + b * p.dv_sb + krow * p.dv_ss + hk * p.dv_sh;
+        float* acc_row =
+            accp != nullptr ? accp + ((static_cast<int64_t>(b) * p.S + krow) * p.Hkv + hk) * width : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < width / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tmem_base + lane_addr + col + c * 32, v);
+          if (!valid) continue;
+          if (acc_row != nullptr) {
+#pragma unroll
+            for (int t = 0; t < 32; t += 4)
+              red_add_v4(acc_row + c * 32 + t, __uint_as_float(v[t]) * sc, __uint_as_float(v[t + 1]) * sc,
+                         __uint_as_float(v[t + 2]) * sc, __uint_as_float(v[t + 3]) * sc);
+          } else {
+#pragma unroll
+            for (int t = 0; t < 32; t += 8) {
+              uint4 o;
+              o.x = pack_bf16x2(__uint_as_float(v[t]) * sc, __uint_as_float(v[t + 1]) * sc);
+              o.y = pack_bf16x2(__uint_as_float(v[t + 2]) * sc, __uint_as_float(v[t + 3]) * sc);
+              o.z = pack_bf16x2(__uint_as_float(v[t + 4]) * sc, __uint_as_float(v[t + 5]) * sc);
+              o.w = pack_bf16x2(__uint_as_float(v[t + 6]) * sc, __uint_as_float(v[t + 7]) * sc);
+              *reinterpret_cast<uint4*>(out + c * 32 + t) = o;
+            }
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, attn_tc_bwd::TMEM_COLS);
+  }
+}
+
 // fp32 [B, S, H, D] accumulator -> bf16 strided [B, S, H, D] view.
 __global__ void acc_to_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int B, int S, int H,
                                    int D, int64_t sb, int64_t ss, int64_t sh) {
@@ -823,11 +1168,17 @@ bool flash_attn_bwd_tc_supported(int64_t dqk, int64_t dv) {
   return (dqk == 128 && dv == 128) || (dqk == 192 && dv == 128) || (dqk == 64 && dv == 64);
 }
 
-template <int DQK, int DV, bool SERIAL>
+template <int DQK, int DV, bool SERIAL, bool PIPE>
+constexpr int bwd_smem_bytes() {
+  if constexpr (PIPE) return attn_tc_bwd::BwdPipeCfg<DQK, DV>::SMEM_BYTES;
+  else return attn_tc_bwd::BwdCfg<DQK, DV, SERIAL>::SMEM_BYTES;
+}
+
+template <int DQK, int DV, bool SERIAL, bool PIPE = false>
 static void launch_bwd_tc(AttnTcBwdParams& p, const at::Tensor& q, const at::Tensor& k, const at::Tensor& v,
                           const at::Tensor& dout, int dev, cudaStream_t stream) {
   using namespace attn_tc_bwd;
-  using Cfg = BwdCfg<DQK, DV, SERIAL>;
+  constexpr int SMEM = bwd_smem_bytes<DQK, DV, SERIAL, PIPE>();
   TmaSlots& ts = tls_tma_slots();
   const int box[4] = {64, BM, 1, 1};
   auto map = [&](CUtensorMap* m, const at::Tensor& t, int d) {
@@ -839,16 +1190,18 @@ static void launch_bwd_tc(AttnTcBwdParams& p, const at::Tensor& q, const at::Ten
   map(&ts.m[1], k, DQK);
   map(&ts.m[2], v, DV);
   map(&ts.m[3], dout, DV);
-  auto kern = flash_bwd_tc_kernel<DQK, DV, SERIAL>;
+  void (*kern)(const CUtensorMap, const CUtensorMap, const CUtensorMap, const CUtensorMap, AttnTcBwdParams);
+  if constexpr (PIPE) kern = flash_bwd_tc_pipe_kernel<DQK, DV>;
+  else kern = flash_bwd_tc_kernel<DQK, DV, SERIAL>;
   static bool attr_done[64] = {};
   if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr_done[dev] = true;
   }
   dim3 grid(static_cast<unsigned>((p.S + BN - 1) / BN), static_cast<unsigned>(p.Hq), static_cast<unsigned>(p.B));
   void* args[5] = {&ts.m[0], &ts.m[1], &ts.m[2], &ts.m[3], &p};
   NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(192), args,
-                                  static_cast<size_t>(Cfg::SMEM_BYTES), stream));
+                                  static_cast<size_t>(SMEM), stream));
   NTB_LAUNCH_CHECK(1);
 }
 
@@ -886,8 +1239,15 @@ void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at
     p.dk_acc = dk_acc.data_ptr<float>();
     p.dv_acc = dv_acc.data_ptr<float>();
   }
-  if (DQK == 128) launch_bwd_tc<128, 128, false>(p, q, k, v, dout, dev, stream);
-  else if (DQK == 192) launch_bwd_tc<192, 128, true>(p, q, k, v, dout, dev, stream);
+  // The pipelined variant (double-buffered Q, S of the next block issued under this block's
+  // softmax) measured 1009 us against 941 us for the serial chain on the Llama shape (B=1,
+  // S=4096, 32q/8kv heads, d=128, causal), so it runs only with NTB_ATTN_BWD_PIPE=1.
+  const char* pipe_env = std::getenv("NTB_ATTN_BWD_PIPE");
+  const bool pipe = pipe_env != nullptr && pipe_env[0] == '1';
+  if (DQK == 192) launch_bwd_tc<192, 128, true>(p, q, k, v, dout, dev, stream);
+  else if (DQK == 128 && pipe) launch_bwd_tc<128, 128, false, true>(p, q, k, v, dout, dev, stream);
+  else if (DQK == 128) launch_bwd_tc<128, 128, false>(p, q, k, v, dout, dev, stream);
+  else if (pipe) launch_bwd_tc<64, 64, false, true>(p, q, k, v, dout, dev, stream);
   else launch_bwd_tc<64, 64, false>(p, q, k, v, dout, dev, stream);
   if (Hq != Hkv) {
     TORCH_CHECK(dk.stride(3) == 1 && dv.stride(3) == 1 && dk.stride(2) % 4 == 0 && dk.stride(1) % 4 == 0 &&

@@ -86,6 +86,11 @@ std::vector<at::Tensor> fp8_quantize(const at::Tensor& x, int64_t block_rows, bo
 at::Tensor fp8_quant_dequant(const at::Tensor& x, int64_t block_rows, bool stochastic, int64_t seed);
 at::Tensor fp8_quant_dequant_strided(const at::Tensor& src, int64_t groups, int64_t rows_per_group, int64_t cols,
                                      int64_t group_stride);
+std::vector<at::Tensor> fp8_quantize_strided(const at::Tensor& src, int64_t groups, int64_t rows_per_group,
+                                             int64_t cols, int64_t group_stride);
+std::vector<at::Tensor> fp8_quantize_with_dq(const at::Tensor& x, bool stochastic, int64_t seed);
+void gemm_fp8_grouped(const at::Tensor& a_q, const at::Tensor& sa, const at::Tensor& b_q, const at::Tensor& sb,
+                      at::Tensor& out, const at::Tensor& offsets);
 at::Tensor fp8_dequantize(const at::Tensor& q, const at::Tensor& scales, int64_t block_rows, at::ScalarType dtype);
 // tp_fused.cu
 void ag_gemm(const at::Tensor& x_local, at::Tensor& x_full_out, const at::Tensor& w, at::Tensor& y,
@@ -188,6 +193,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("sfb"), py::arg("gsb"), py::arg("out"), py::arg("bias") = py::none());
   m.def("fp8_quant_dequant", &ntb::fp8_quant_dequant);
   m.def("fp8_quant_dequant_strided", &ntb::fp8_quant_dequant_strided);
+  m.def("fp8_quantize_strided", &ntb::fp8_quantize_strided);
+  m.def("fp8_quantize_with_dq", &ntb::fp8_quantize_with_dq);
+  m.def("gemm_fp8_grouped", &ntb::gemm_fp8_grouped);
   m.def("fp8_dequantize", &ntb::fp8_dequantize);
   m.def("ag_gemm", &ntb::ag_gemm, py::arg("x_local"), py::arg("x_full_out"), py::arg("w"), py::arg("y"),
         py::arg("bias"), py::arg("b_mn"), py::arg("slots"), py::arg("ready"), py::arg("ctrs"), py::arg("rank"),

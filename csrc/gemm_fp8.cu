@@ -45,12 +45,29 @@ constexpr uint32_t TMEM_COLS = NBUF * BN;
 struct Fp8GemmParams {
   int M, N, K;
   const float* sa;  // [M, K/128]
-  const float* sb;  // [ceil(N/128), K/128]
+  const float* sb;  // [ceil(N/128), K/128], or for grouped B [groups * N / 128, K/128]
   __nv_bfloat16* C;
   long ldc;
   const __nv_bfloat16* bias;
   int* status;
+  // M-grouped mode (offsets != nullptr): the rows of A and C are expert segments, each padded to a
+  // multiple of 128 rows ([offsets[g], offsets[g+1])); B is a stack of per-expert [N, K] matrices.
+  const int* offsets;
+  int groups;
 };
+
+// Expert of the 128-row tile starting at `row`, or -1 beyond the last segment (tile skipped).
+__device__ __forceinline__ int fp8_group_of_tile(const Fp8GemmParams& p, int row) {
+  if (p.offsets == nullptr) return 0;
+  if (row >= __ldg(p.offsets + p.groups)) return -1;
+  int lo = 0, hi = p.groups - 1;  // last g with offsets[g] <= row
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (__ldg(p.offsets + mid) <= row) lo = mid;
+    else hi = mid - 1;
+  }
+  return lo;
+}
 
 __device__ __forceinline__ void umma_f8f6f4_ss(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
                                                uint32_t accumulate) {
@@ -120,6 +137,9 @@ __global__ void __launch_bounds__(320, 1)
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int mb = tile % num_m, nb = tile / num_m;
+        const int g = fp8_group_of_tile(p, mb * BM);
+        if (g < 0) continue;
+        const int b0 = g * p.N + nb * BN;  // first B row of this tile (this expert's slice)
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kStatusTimeoutProducer)) {
             ok = false;
@@ -127,8 +147,8 @@ __global__ void __launch_bounds__(320, 1)
           }
           mbar_expect_tx(&full[stage], A_BYTES + B_BYTES);
           tma_load_2d(sA + stage * A_BYTES, &tmA, &full[stage], kb * BK, mb * BM);
-          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, nb * BN);
-          tma_load_2d(sB + stage * B_BYTES + 128 * BK, &tmB, &full[stage], kb * BK, nb * BN + 128);
+          tma_load_2d(sB + stage * B_BYTES, &tmB, &full[stage], kb * BK, b0);
+          tma_load_2d(sB + stage * B_BYTES + 128 * BK, &tmB, &full[stage], kb * BK, b0 + 128);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -143,6 +163,7 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t phase = 0, bphase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        if (fp8_group_of_tile(p, (tile % num_m) * BM) < 0) continue;
         for (int kb = 0; kb < nkb; ++kb) {
           if (!mbar_wait(&pempty[buf], bphase ^ 1, p.status, kStatusTimeoutMma) ||
               !mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
@@ -181,9 +202,12 @@ __global__ void __launch_bounds__(320, 1)
     uint32_t bphase = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
       const int mb = tile % num_m, nb = tile / num_m;
+      const int g = fp8_group_of_tile(p, mb * BM);
+      if (g < 0) continue;
       const long m = static_cast<long>(mb) * BM + row;
       const float* sa_row = p.sa + (m < p.M ? m : 0) * nk;
-      const float* sb_row = p.sb + static_cast<long>(nb * 2 + half) * nk;  // this half's weight block
+      // this half's weight block (for a stacked B, inside expert g's slice of N / 128 blocks)
+      const float* sb_row = p.sb + (static_cast<long>(g) * (p.N / 128) + nb * 2 + half) * nk;
       const bool half_live = nb * BN + half * 128 < p.N;
       float acc[128];
 #pragma unroll
@@ -245,6 +269,65 @@ __global__ void __launch_bounds__(320, 1)
   }
 }
 
+static void launch_fp8(const at::Tensor& a_q, const at::Tensor& b_q, Fp8GemmParams& p, int64_t b_rows) {
+  using namespace fp8g;
+  const int dev = a_q.get_device();
+  p.status = device_status(dev);
+  TmaSlots& ts = tls_tma_slots();
+  make_tma_2d(&ts.m[0], a_q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, p.M, p.K, 128, 128,
+              CU_TENSOR_MAP_SWIZZLE_128B);
+  make_tma_2d(&ts.m[1], b_q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.K, b_rows, p.K, 128, 128,
+              CU_TENSOR_MAP_SWIZZLE_128B);
+  static bool attr_done[64] = {};
+  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
+    attr_done[dev] = true;
+  }
+  const int tiles = ((p.M + BM - 1) / BM) * ((p.N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms(dev));
+  void* args[3] = {&ts.m[0], &ts.m[1], &p};
+  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(gemm_fp8_kernel), dim3(grid), dim3(THREADS), args,
+                                  static_cast<size_t>(SMEM_BYTES), at::cuda::getCurrentCUDAStream(dev)));
+  NTB_LAUNCH_CHECK(1);
+}
+
+// Grouped (mixture-of-experts) form: out[rows of g] = a_q[rows of g] . b_q[g]^T with per-row 1x128
+// activation scales and 128x128 block scales of the stacked weights. a_q: e4m3 [R, K] whose rows are
+// expert segments padded to multiples of 128 (offsets int32 [G + 1], device, as the bf16 grouped
+// GEMM takes them); b_q: e4m3 [G * N, K]; sb: [G * N / 128, K / 128]; out bf16 [R, N]. Rows of out
+// beyond offsets[G] are not written.
+void gemm_fp8_grouped(const at::Tensor& a_q, const at::Tensor& sa, const at::Tensor& b_q, const at::Tensor& sb,
+                      at::Tensor& out, const at::Tensor& offsets) {
+  TORCH_CHECK(a_q.is_cuda() && b_q.is_cuda() && a_q.scalar_type() == at::kByte && b_q.scalar_type() == at::kByte &&
+                  a_q.is_contiguous() && b_q.is_contiguous() && a_q.dim() == 2 && b_q.dim() == 2,
+              "gemm_fp8_grouped: contiguous 2-D e4m3 operands (uint8)");
+  TORCH_CHECK(offsets.is_cuda() && offsets.scalar_type() == at::kInt && offsets.is_contiguous() && offsets.numel() >= 2,
+              "gemm_fp8_grouped: int32 offsets [G + 1]");
+  const int64_t R = a_q.size(0), K = a_q.size(1), G = offsets.numel() - 1;
+  TORCH_CHECK(b_q.size(1) == K && K % 128 == 0 && R % 128 == 0 && b_q.size(0) % G == 0,
+              "gemm_fp8_grouped: K multiple of 128, rows padded to 128, stacked B rows divisible by G");
+  const int64_t N = b_q.size(0) / G;
+  TORCH_CHECK(N % 128 == 0, "gemm_fp8_grouped: per-expert N must be a multiple of 128");
+  TORCH_CHECK(sa.scalar_type() == at::kFloat && sa.is_contiguous() && sa.size(0) == R && sa.size(1) == K / 128,
+              "gemm_fp8_grouped: activation scales [R, K/128]");
+  TORCH_CHECK(sb.scalar_type() == at::kFloat && sb.is_contiguous() && sb.size(0) == G * N / 128 && sb.size(1) == K / 128,
+              "gemm_fp8_grouped: weight scales [G * N / 128, K/128]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.size(0) == R && out.size(1) == N && out.stride(1) == 1,
+              "gemm_fp8_grouped: bf16 out [R, N]");
+  if (R == 0) return;
+  Fp8GemmParams p{};
+  p.M = static_cast<int>(R);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.sa = sa.data_ptr<float>();
+  p.sb = sb.data_ptr<float>();
+  p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  p.ldc = out.stride(0);
+  p.offsets = offsets.data_ptr<int>();
+  p.groups = static_cast<int>(G);
+  launch_fp8(a_q, b_q, p, G * N);
+}
+
 // out[M, N] (bf16) = dequant(a_q, sa) . dequant(b_q, sb)^T (+ bias), computed on the e4m3 operands.
 void gemm_fp8_blockscaled(const at::Tensor& a_q, const at::Tensor& sa, const at::Tensor& b_q, const at::Tensor& sb,
                           at::Tensor& out, const c10::optional<at::Tensor>& bias) {
@@ -274,24 +357,7 @@ void gemm_fp8_blockscaled(const at::Tensor& a_q, const at::Tensor& sa, const at:
   p.C = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
   p.ldc = out.stride(0);
   p.bias = bias.has_value() ? reinterpret_cast<const __nv_bfloat16*>(bias->data_ptr()) : nullptr;
-  const int dev = a_q.get_device();
-  p.status = device_status(dev);
-  TmaSlots& ts = tls_tma_slots();
-  make_tma_2d(&ts.m[0], a_q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, M, K, 128, 128,
-              CU_TENSOR_MAP_SWIZZLE_128B);
-  make_tma_2d(&ts.m[1], b_q.data_ptr(), CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, K, 128, 128,
-              CU_TENSOR_MAP_SWIZZLE_128B);
-  static bool attr_done[64] = {};
-  if (dev >= 0 && dev < 64 && !attr_done[dev]) {
-    NTB_CUDA_CHECK(cudaFuncSetAttribute(gemm_fp8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES));
-    attr_done[dev] = true;
-  }
-  const int tiles = static_cast<int>(((M + BM - 1) / BM) * ((N + BN - 1) / BN));
-  const int grid = std::min(tiles, num_sms(dev));
-  void* args[3] = {&ts.m[0], &ts.m[1], &p};
-  NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(gemm_fp8_kernel), dim3(grid), dim3(THREADS), args,
-                                  static_cast<size_t>(SMEM_BYTES), at::cuda::getCurrentCUDAStream(dev)));
-  NTB_LAUNCH_CHECK(1);
+  launch_fp8(a_q, b_q, p, N);
 }
 
 }  // namespace ntb

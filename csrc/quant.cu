@@ -66,32 +66,42 @@ template <typename T>
 __global__ void __launch_bounds__(256) quant_tile_kernel(const T* __restrict__ x, int64_t rows, int cols,
                                                          uint8_t* __restrict__ q, float* __restrict__ scales,
                                                          T* __restrict__ dq, int stochastic, uint64_t seed) {
+  // Tile t (1 x 128) of the contiguous [rows, cols] matrix covers elements [128 t, 128 t + 128) and
+  // owns scale t. A warp holds two tiles (one per half warp) and keeps two such pairs in flight per
+  // iteration, so each thread has 32 bytes of loads outstanding before it reduces.
   const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
-  const int ntc = cols / 128;
-  const int64_t tiles = rows * ntc;
+  const int64_t tiles = rows * (cols / 128);
   const int64_t pairs = (tiles + 1) / 2;
   const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
   for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < pairs;
-       w += nwarps) {
-    const int64_t tile = 2 * w + half;
-    const bool live = tile < tiles;
-    const int64_t r = live ? tile / ntc : 0;
-    const int tc = live ? static_cast<int>(tile % ntc) : 0;
-    const int64_t idx0 = r * cols + tc * 128 + hl * 8;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (live) load8(x + idx0, v);
-    float amax = 0.f;
+       w += 2 * nwarps) {
+    int64_t t[2];
+    bool live[2];
+    float v[2][8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[j]));
+    for (int u = 0; u < 2; ++u) {
+      t[u] = 2 * (w + u * nwarps) + half;
+      live[u] = t[u] < tiles;
 #pragma unroll
-    for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
-    if (!live) continue;
-    const float s = amax > 0.f ? amax / 448.f : 1.f;
-    if (hl == 0) scales[r * ntc + tc] = s;
-    float d[8];
-    const uint2 codes = quant8(v, s, stochastic != 0, seed, idx0, d);
-    if (q) *reinterpret_cast<uint2*>(q + idx0) = codes;
-    if (dq) store8(dq + idx0, d);
+      for (int j = 0; j < 8; ++j) v[u][j] = 0.f;
+      if (live[u]) load8(x + t[u] * 128 + hl * 8, v[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {
+      float amax = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) amax = fmaxf(amax, fabsf(v[u][j]));
+#pragma unroll
+      for (int o = 8; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+      if (!live[u]) continue;
+      const float s = amax > 0.f ? amax / 448.f : 1.f;
+      if (hl == 0) scales[t[u]] = s;
+      const int64_t idx0 = t[u] * 128 + hl * 8;
+      float d[8];
+      const uint2 codes = quant8(v[u], s, stochastic != 0, seed, idx0, d);
+      if (q) *reinterpret_cast<uint2*>(q + idx0) = codes;
+      if (dq) store8(dq + idx0, d);
+    }
   }
 }
 
@@ -249,6 +259,41 @@ at::Tensor fp8_quant_dequant_strided(const at::Tensor& src, int64_t groups, int6
       reinterpret_cast<bf16*>(out.data_ptr()), 0, 0, rows_per_group, group_stride);
   NTB_LAUNCH_CHECK(1);
   return out;
+}
+
+// Same reading of a strided stack, returning the e4m3 codes [groups * rows_per_group, cols] and the
+// 128 x 128 block scales [groups * rows_per_group / 128, cols / 128] (the B operand of the grouped
+// fp8 GEMM).
+std::vector<at::Tensor> fp8_quantize_strided(const at::Tensor& src, int64_t groups, int64_t rows_per_group,
+                                             int64_t cols, int64_t group_stride) {
+  TORCH_CHECK(src.is_cuda() && src.scalar_type() == at::kBFloat16, "fp8_quantize_strided: bf16 CUDA source");
+  TORCH_CHECK(groups >= 1 && rows_per_group % 128 == 0 && cols % 128 == 0 && group_stride >= rows_per_group * cols &&
+                  group_stride % 8 == 0,
+              "fp8_quantize_strided: rows per group and columns must be multiples of 128, groups must not overlap");
+  const int64_t need = (src.storage_offset() + (groups - 1) * group_stride + rows_per_group * cols) * 2;
+  TORCH_CHECK(static_cast<int64_t>(src.storage().nbytes()) >= need && (reinterpret_cast<uintptr_t>(src.data_ptr()) & 15) == 0,
+              "fp8_quantize_strided: source storage too small or misaligned");
+  const int64_t rows = groups * rows_per_group;
+  auto q = at::empty({rows, cols}, src.options().dtype(at::kByte));
+  auto s = at::empty({rows / 128, cols / 128}, src.options().dtype(at::kFloat));
+  const int64_t blocks = (rows / 128) * (cols / 128);
+  quant_block_kernel<bf16><<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      reinterpret_cast<const bf16*>(src.data_ptr()), rows, static_cast<int>(cols), q.data_ptr<uint8_t>(),
+      s.data_ptr<float>(), nullptr, 0, 0, rows_per_group, group_stride);
+  NTB_LAUNCH_CHECK(1);
+  return {q, s};
+}
+
+// Codes and scales of a 1x128-tile quantisation plus the dequantised (rounded) values, in one pass.
+std::vector<at::Tensor> fp8_quantize_with_dq(const at::Tensor& x, bool stochastic, int64_t seed) {
+  check_quant_input(x, 1);
+  const int64_t rows = x.size(0), cols = x.size(1);
+  auto q = at::empty({rows, cols}, x.options().dtype(at::kByte));
+  auto s = at::empty({rows, cols / 128}, x.options().dtype(at::kFloat));
+  auto dq = at::empty_like(x);
+  if (rows == 0) return {q, s, dq};
+  launch_quant(x, 1, stochastic, seed, q.data_ptr<uint8_t>(), s.data_ptr<float>(), dq.data_ptr());
+  return {q, s, dq};
 }
 
 at::Tensor fp8_dequantize(const at::Tensor& q, const at::Tensor& scales, int64_t block_rows, at::ScalarType dtype) {

@@ -46,6 +46,15 @@ def scatter_rows_to_segments(x_sorted: torch.Tensor, counts: torch.Tensor, offse
     return out, dest
 
 
+class Fp8Stacks:
+    """e4m3 codes + 128x128 block scales of the stacked expert weights: w1 [E * 2I, H] (gate|up),
+    w2 [E * H, I], and the per-expert transposes w1t [E * H, 2I], w2t [E * I, H]."""
+
+    def __init__(self, w1q, s1, w2q, s2, w1tq, s1t, w2tq, s2t):
+        self.w1q, self.s1, self.w2q, self.s2 = w1q, s1, w2q, s2
+        self.w1tq, self.s1t, self.w2tq, self.s2t = w1tq, s1t, w2tq, s2t
+
+
 class _StackCache:
     """Stacked expert weights, rebuilt only when a source parameter changed."""
 
@@ -54,6 +63,8 @@ class _StackCache:
         self.w1 = None
         self.w2 = None
         self._params = None
+        self.codes_key = None
+        self._codes = None
 
     def params(self, experts):
         """[gate_0, up_0, down_0, gate_1, ...] weights (list built once per module)."""
@@ -80,6 +91,32 @@ class _StackCache:
                     or d.data_ptr() != d0.data_ptr() + e * stride * es):
                 return 0
         return stride if len(params) > 3 else g0.numel() + u0.numel() + d0.numel()
+
+    def codes(self, experts) -> "Fp8Stacks | None":
+        """e4m3 codes and 128 x 128 block scales of the expert stacks, and of their per-expert
+        transposes (the B operands of the two input-gradient GEMMs), rebuilt when a weight changed;
+        None when the experts do not sit at a constant stride in one buffer or a dimension is not a
+        multiple of 128."""
+        params = self.params(experts)
+        key = ("codes",) + tuple((p.data_ptr(), p._version) for p in params)
+        if key == self.codes_key:
+            return self._codes
+        stride = self._expert_stride(params)
+        g, d = params[0], params[2]
+        I, H = g.shape
+        if not stride or I % 128 or H % 128:
+            self.codes_key, self._codes = key, None
+            return None
+        E = len(experts)
+        C = ext()
+        with torch.no_grad():
+            w1q, s1 = C.fp8_quantize_strided(g, E, 2 * I, H, stride)
+            w2q, s2 = C.fp8_quantize_strided(d, E, H, I, stride)
+            tr = lambda t, a, b: t.view(E, a, b).transpose(1, 2).contiguous().view(E * b, a)  # noqa: E731
+            self._codes = Fp8Stacks(w1q, s1, w2q, s2, tr(w1q, 2 * I, H), tr(s1, 2 * I // 128, H // 128),
+                                    tr(w2q, H, I), tr(s2, H // 128, I // 128))
+        self.codes_key = key
+        return self._codes
 
     def get(self, experts, fp8: bool = False):
         """(w1, w2); with ``fp8`` every expert matrix is rounded through e4m3 in 128 x 128 blocks
@@ -166,14 +203,41 @@ _FP8_SEED = [0]
 
 class _GroupedSwiGLUFn(torch.autograd.Function):
     """``fp8``: None, or the rounding of the e4m3 activation quantisation ("nearest" /
-    "stochastic"): both GEMM inputs are rounded through e4m3 in 1 x 128 tiles (the weights
-    arrive already rounded in 128 x 128 blocks), the backward is straight-through on those
-    rounded operands, as in the fp8 linear backend."""
+    "stochastic").
+
+    With ``codes`` (an ``Fp8Stacks``) the expert GEMMs run on e4m3 operands on the tensor cores:
+    the forward quantises X and SwiGLU(H) in 1 x 128 tiles and multiplies them with the weight
+    stacks' codes (128 x 128 block scales) in the grouped block-scaled GEMM; the backward quantises
+    dY and dH the same way for the two input-gradient GEMMs (against the per-expert transposed
+    weight codes). The weight gradients are bf16 grouped GEMMs on the rounded activations
+    (straight-through), accumulated in fp32.
+
+    Without ``codes`` both GEMM inputs are rounded through e4m3 (the weights arrive rounded in
+    128 x 128 blocks) and every GEMM is bf16: the same numerics, emulated."""
 
     @staticmethod
-    def forward(ctx, x_pad, offsets, w1, w2, n_experts, bufs, fp8, *params):
+    def forward(ctx, x_pad, offsets, w1, w2, n_experts, bufs, fp8, codes, *params):
         C = ext()
         R = x_pad.shape[0]
+        if codes is not None:
+            sr = fp8 == "stochastic"
+            _FP8_SEED[0] += 1
+            I2 = codes.w1q.shape[0] // n_experts
+            H = codes.w2q.shape[0] // n_experts
+            xq, sx, x_r = C.fp8_quantize_with_dq(x_pad.contiguous(), sr, _FP8_SEED[0])
+            h = torch.empty(R, I2, device=x_pad.device, dtype=x_pad.dtype)
+            C.gemm_fp8_grouped(xq, sx, codes.w1q, codes.s1, h, offsets)
+            aq, sa, a_r = C.fp8_quantize_with_dq(C.swiglu_fwd(h), sr, _FP8_SEED[0] + (1 << 40))
+            y = bufs.y_out if bufs is not None and bufs.y_out is not None else \
+                torch.empty(R, H, device=x_pad.device, dtype=x_pad.dtype)
+            C.gemm_fp8_grouped(aq, sa, codes.w2q, codes.s2, y, offsets)
+            ctx.save_for_backward(x_r, offsets, h, a_r)
+            ctx.codes = codes
+            ctx.n_experts = n_experts
+            ctx.params = params
+            ctx.bufs = bufs
+            return y
+        ctx.codes = None
         I2 = w1.shape[0] // n_experts
         H = w2.shape[0] // n_experts
         if fp8 is not None:
@@ -196,14 +260,23 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
     @staticmethod
     def backward(ctx, dy):
         C = ext()
-        x_pad, offsets, w1, w2, h, a = ctx.saved_tensors
         E = ctx.n_experts
         dy = dy.contiguous()
-        I2 = w1.shape[0] // E
-        H = w2.shape[0] // E
-        I = I2 // 2
-        da = torch.empty_like(a)
-        C.gemm_grouped_bf16(dy, w2, da, offsets, 1, b_mn=True)          # dA = dY . W2_e
+        codes = ctx.codes
+        if codes is not None:
+            x_pad, offsets, h, a = ctx.saved_tensors
+            I2, H = h.shape[1], x_pad.shape[1]
+            I = I2 // 2
+            da = torch.empty_like(a)
+            dyq, sdy = C.fp8_quantize(dy, 1, False, 0)
+            C.gemm_fp8_grouped(dyq, sdy, codes.w2tq, codes.s2t, da, offsets)   # dA = dY . W2_e (e4m3)
+        else:
+            x_pad, offsets, w1, w2, h, a = ctx.saved_tensors
+            I2 = w1.shape[0] // E
+            H = w2.shape[0] // E
+            I = I2 // 2
+            da = torch.empty_like(a)
+            C.gemm_grouped_bf16(dy, w2, da, offsets, 1, b_mn=True)          # dA = dY . W2_e
         flat = _flat_main_grads(ctx.params, E, I, H)
         dw2 = None
         if flat is not None:                                              # dW2_e += dY_e^T A_e into main_grad
@@ -214,10 +287,15 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
         dh = C.swiglu_bwd(da, h)
         bufs = ctx.bufs
         dx = bufs.dx_out if bufs is not None and bufs.dx_out is not None else torch.empty_like(x_pad)
-        C.gemm_grouped_bf16(dh, w1, dx, offsets, 1, b_mn=True)          # dX = dH . W1_e
+        if codes is not None:
+            dhq, sdh = C.fp8_quantize(dh, 1, False, 0)
+            C.gemm_fp8_grouped(dhq, sdh, codes.w1tq, codes.s1t, dx, offsets)  # dX = dH . W1_e (e4m3)
+        else:
+            C.gemm_grouped_bf16(dh, w1, dx, offsets, 1, b_mn=True)          # dX = dH . W1_e
+        nones = (None,) * 8
         if flat is not None:                                              # dW1_e += dH_e^T X_e into main_grad
             C.gemm_grouped_bf16(dh, x_pad, flat[0], offsets, 2, b_mn=True, accumulate=True, c_group_stride=3 * I)
-            return (dx, None, None, None, None, None, None, *([None] * len(ctx.params)))
+            return (dx, *nones[1:], *([None] * len(ctx.params)))
         dw1 = torch.zeros(E * I2, x_pad.shape[1], device=dy.device, dtype=torch.float32)
         C.gemm_grouped_bf16(dh, x_pad, dw1, offsets, 2, b_mn=True)      # dW1_e = dH_e^T X_e
         slices = []
@@ -234,7 +312,7 @@ class _GroupedSwiGLUFn(torch.autograd.Function):
             grads = []
             for e in range(E):
                 grads += [dw1c[e * I2:e * I2 + I], dw1c[e * I2 + I:(e + 1) * I2], dw2c[e * H:(e + 1) * H]]
-        return (dx, None, None, None, None, None, None, *grads)
+        return (dx, *nones[1:], *grads)
 
 
 def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts, cache: _StackCache,
@@ -243,11 +321,24 @@ def grouped_swiglu_experts(x_sorted: torch.Tensor, counts: torch.Tensor, experts
     offsets, rows = pad_segments(counts, max_rows)
     x_pad, dest = scatter_rows_to_segments(x_sorted, counts, offsets, rows)
     fp8 = grouped_fp8_rounding(experts)
-    w1, w2 = cache.get(experts, fp8=fp8 is not None)
+    w1, w2, codes = expert_operands(experts, cache, fp8, x_pad.dtype)
     params = [p for e in experts for p in (e.gate_proj.weight, e.up_proj.weight, e.down_proj.weight)]
-    y_pad = _GroupedSwiGLUFn.apply(x_pad, offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), None,
-                                   fp8, *params)
+    y_pad = _GroupedSwiGLUFn.apply(x_pad, offsets, w1, w2, len(experts), None, fp8, codes, *params)
     return y_pad.index_select(0, dest)
+
+
+def expert_operands(experts, cache: _StackCache, fp8, dtype):
+    """(w1, w2, codes) for ``_GroupedSwiGLUFn``: under the fp8 recipe the e4m3 codes of the stacks
+    (``NTB_FP8_GROUPED_NATIVE=0`` keeps the bf16 emulation), otherwise the bf16 stacks."""
+    import os
+
+    if fp8 is not None and os.environ.get("NTB_FP8_GROUPED_NATIVE", "1") != "0":
+        codes = cache.codes(experts)
+        if codes is not None:
+            empty = torch.empty(0, device=codes.w1q.device, dtype=dtype)
+            return empty, empty, codes
+    w1, w2 = cache.get(experts, fp8=fp8 is not None)
+    return w1.to(dtype), w2.to(dtype), None
 
 
 def grouped_fp8_rounding(experts):

@@ -457,7 +457,7 @@ def fused_ep_enabled(group) -> bool:
     if not (torch.cuda.is_available() and dist.is_initialized()):
         return False
     n = comm.group_size(group)
-    return 1 < n <= MAX_RANKS and dist.get_backend(group) == "nccl"
+    return comm.min_fused_ranks() <= n <= MAX_RANKS and dist.get_backend(group) == "nccl"
 
 
 # ---------------------------------------------------------------------------- autograd
@@ -525,7 +525,7 @@ class _EPCombineFn(torch.autograd.Function):
 def fused_ep_moe(tokens: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Tensor, experts, stack_cache, *,
                  group, num_experts: int, capacity_factor: float, fp8_payload: bool, stochastic: bool):
     """Routed-expert output [T, H] of an expert-parallel MoE layer and (stats, kept_counts) device tensors."""
-    from ..ops.grouped import GroupedBuffers, _GroupedSwiGLUFn, grouped_fp8_rounding
+    from ..ops.grouped import GroupedBuffers, _GroupedSwiGLUFn, expert_operands, grouped_fp8_rounding
 
     n = comm.group_size(group)
     T, H = tokens.shape
@@ -538,9 +538,9 @@ def fused_ep_moe(tokens: torch.Tensor, topk_idx: torch.Tensor, topk_w: torch.Ten
     x_pad = _EPDispatchFn.apply(tokens, st)
     rp = st.rp
     fp8 = grouped_fp8_rounding(experts)
-    w1, w2 = stack_cache.get(experts, fp8=fp8 is not None)
+    w1, w2, codes = expert_operands(experts, stack_cache, fp8, x_pad.dtype)
     bufs = GroupedBuffers(y_out=ws.y(rp.rows), dx_out=ws.dx(rp.rows))
-    y = _GroupedSwiGLUFn.apply(x_pad, rp.offsets, w1.to(x_pad.dtype), w2.to(x_pad.dtype), len(experts), bufs, fp8,
+    y = _GroupedSwiGLUFn.apply(x_pad, rp.offsets, w1, w2, len(experts), bufs, fp8, codes,
                                *stack_cache.params(experts))
     out = _EPCombineFn.apply(y, topk_w.float().reshape(-1), st)
     return out.to(tokens.dtype), rp.stats, rp.kept_counts

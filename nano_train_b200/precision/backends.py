@@ -234,9 +234,27 @@ def _quantized_weight(w: torch.Tensor):
     return wq, sw
 
 
+_WQT_CACHE: dict = {}
+
+
+def _quantized_weight_t(w: torch.Tensor, wq: torch.Tensor, sw: torch.Tensor):
+    """Codes and block scales of W^T (the B operand of the input-gradient GEMM), from W's e4m3 copy:
+    a 128 x 128 block of W^T is a transposed block of W, so its scale is the same number."""
+    key = id(w)
+    ent = _WQT_CACHE.get(key)
+    if ent is not None and ent[0] == (w.data_ptr(), w._version):
+        return ent[1], ent[2]
+    wtq, swt = wq.t().contiguous(), sw.t().contiguous()
+    _remember(_WQT_CACHE, w, ((w.data_ptr(), w._version), wtq, swt))
+    return wtq, swt
+
+
 class _FP8LinearFn(torch.autograd.Function):
-    """Forward on the block-scaled e4m3 tensor cores; straight-through backward on the
-    dequantised operands (bf16 GEMMs), with the fp8 copies saved instead of bf16 activations."""
+    """Forward on the block-scaled e4m3 tensor cores. Backward: the input gradient also on the e4m3
+    tensor cores when the output width is a multiple of 128 (dY quantised in 1 x 128 tiles, against
+    the weight's transposed codes; ``NTB_FP8_DGRAD_NATIVE=0`` keeps bf16), the weight gradient as a
+    bf16 GEMM on the dequantised activations accumulated in fp32 (straight-through); the fp8 copies
+    are saved instead of bf16 activations."""
 
     @staticmethod
     def forward(ctx, x2, weight, bias, stochastic, seed):
@@ -254,11 +272,19 @@ class _FP8LinearFn(torch.autograd.Function):
     def backward(ctx, dy):
         from ..ops.linear import accumulate_weight_grad, gemm
 
+        import os
+
         C = ops.ext()
         xq, sx, wq, sw = ctx.saved_tensors
         dy = dy.contiguous()
-        wdq = C.fp8_dequantize(wq, sw, 128, torch.bfloat16)
-        dx = gemm(dy, wdq, b_mn=True)
+        N, K = wq.shape
+        if N % 128 == 0 and K % 8 == 0 and os.environ.get("NTB_FP8_DGRAD_NATIVE", "1") != "0":
+            wtq, swt = _quantized_weight_t(ctx.weight, wq, sw)
+            dyq, sdy = C.fp8_quantize(dy, 1, False, 0)
+            dx = torch.empty(dy.shape[0], K, device=dy.device, dtype=torch.bfloat16)
+            C.gemm_fp8_blockscaled(dyq, sdy, wtq, swt, dx, None)
+        else:
+            dx = gemm(dy, C.fp8_dequantize(wq, sw, 128, torch.bfloat16), b_mn=True)
         xdq = C.fp8_dequantize(xq, sx, 1, torch.bfloat16)
         dw = accumulate_weight_grad(ctx.weight, dy, xdq)
         db = dy.float().sum(0).to(torch.bfloat16) if ctx.has_bias else None

@@ -51,9 +51,11 @@ def test_flash_fwd_tc_large_scores_rescale_path():
 
 @pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 8, 2, False),
                                                (1, 130, 2, 1, True), (1, 1024, 4, 1, True)])
-def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, monkeypatch):
+@pytest.mark.parametrize("pipe", ["0", "1"])  # serial chain (default) / pipelined variant
+def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, pipe, monkeypatch):
     from nano_train_b200.ops._ext import check_status, ext
 
+    monkeypatch.setenv("NTB_ATTN_BWD_PIPE", pipe)
     torch.manual_seed(S + hq * 7 + int(causal))
     dev = torch.device("cuda", 0)
     qkv = torch.randn(B, S, hq + 2 * hkv, 128, device=dev, dtype=torch.bfloat16)
@@ -78,7 +80,7 @@ def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, monkeypatch):
 @pytest.mark.parametrize("dqk,dv", [(192, 128), (64, 64)])
 @pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 2, 2, False),
                                                (1, 130, 2, 1, True)])
-def test_flash_tc_mla_and_hd64_match_reference(dqk, dv, B, S, hq, hkv, causal):
+def test_flash_tc_mla_and_hd64_match_reference(dqk, dv, B, S, hq, hkv, causal, monkeypatch):
     """MLA head dims (q/k 192 = [nope 128 | rope 64], v 128) and head dim 64 on the tcgen05 kernels,
     forward and backward, against fp32 PyTorch; q, k, v are strided views of one buffer."""
     from nano_train_b200.ops._ext import check_status, ext
@@ -105,3 +107,10 @@ def test_flash_tc_mla_and_hd64_match_reference(dqk, dv, B, S, hq, hkv, causal):
     o2, lse2 = ext().flash_attn_fwd(q, k, v, scale, causal)  # the mma.sync kernel as a second opinion
     assert _rel(o, o2) < 1e-2
     torch.testing.assert_close(lse, lse2, rtol=1e-3, atol=1e-3)
+    if dqk == 64:  # the pipelined backward variant exists for equal q/k and v widths
+        monkeypatch.setenv("NTB_ATTN_BWD_PIPE", "1")
+        dq3, dk3, dv3 = ext().flash_attn_bwd(do, q, k, v, o, lse, scale, causal)
+        torch.cuda.synchronize()
+        check_status(0)
+        for name, g, r in (("dq", dq3, qf.grad), ("dk", dk3, kf.grad), ("dv", dv3, vf.grad)):
+            assert _rel(g, r) < 2e-2, (name, "pipelined", _rel(g, r))

@@ -52,3 +52,27 @@ def test_native_fp8_linear_forward_backward():
     assert _rel(y, yr) < 6e-2
     assert _rel(x.grad, xr.grad) < 6e-2
     assert _rel(w.grad, wr.grad) < 6e-2
+
+
+def test_native_fp8_dgrad_matches_bf16_dgrad(monkeypatch):
+    """The input gradient on e4m3 operands (dY in 1x128 tiles, W^T codes) against the bf16 GEMM on
+    the dequantised weight, and the transposed weight codes against a transposed quantisation."""
+    from nano_train_b200.ops._ext import ext
+    from nano_train_b200.precision.backends import NativeFP8Backend, _quantized_weight, _quantized_weight_t
+
+    torch.manual_seed(1)
+    be = NativeFP8Backend()
+    x = torch.randn(300, 384, device="cuda", dtype=torch.bfloat16)
+    w = (torch.randn(640, 384, device="cuda", dtype=torch.bfloat16) * 0.05).requires_grad_(True)
+    g = torch.randn(300, 640, device="cuda", dtype=torch.bfloat16)
+    grads = {}
+    for native in ("1", "0"):
+        monkeypatch.setenv("NTB_FP8_DGRAD_NATIVE", native)
+        xx = x.clone().requires_grad_(True)
+        be.linear(xx, w, None).backward(g)
+        grads[native] = xx.grad
+    assert _rel(grads["1"], grads["0"]) < 5e-2
+    wq, sw = _quantized_weight(w)
+    wtq, swt = _quantized_weight_t(w, wq, sw)
+    q2, s2 = ext().fp8_quantize(w.detach().t().contiguous(), 128, False, 0)
+    assert torch.equal(wtq, q2) and torch.equal(swt, s2)
