@@ -10,6 +10,8 @@ _CopyToTensorParallelRegion) and 1499-1597 (sequence scatter / gather).
 """
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.distributed as dist
 
@@ -18,6 +20,14 @@ def group_size(group) -> int:
     if group is None or not dist.is_available() or not dist.is_initialized():
         return 1
     return dist.get_world_size(group)
+
+
+def min_fused_ranks() -> int:
+    """Smallest group on which the peer-memory kernels (fused EP dispatch / combine, fused ZeRO
+    step) replace NCCL: 2, or 1 with NTB_FUSED_ONE_RANK=1. In a one-rank group every "peer"
+    pointer is this GPU's own memory, so the kernels run their whole protocol (slabs, epochs,
+    bounded waits, canaries) on one GPU; tests use it to check them where only one GPU is present."""
+    return 1 if os.environ.get("NTB_FUSED_ONE_RANK", "0") == "1" else 2
 
 
 def group_rank(group) -> int:

@@ -142,7 +142,9 @@ class FlatAdamW:
         self.dp_group = dp_group
         self.dp_size = comm.group_size(dp_group)
         self.dp_rank = comm.group_rank(dp_group)
-        self.strategy = strategy if self.dp_size > 1 else "no_shard"
+        # One rank has nothing to shard, except when a one-rank group runs the peer-memory step
+        # (comm.min_fused_ranks) so that its kernels can be checked on one GPU.
+        self.strategy = strategy if self.dp_size >= comm.min_fused_ranks() else "no_shard"
         self.max_grad_norm = max_grad_norm
         self.grad_norm_group = grad_norm_group if grad_norm_group is not None else tp_group
         self.tp_group = tp_group

@@ -44,7 +44,7 @@ def fused_zero_available(dp_group, param_dtypes, *, grad_norm_group=None) -> boo
     if not (torch.cuda.is_available() and dist.is_initialized()):
         return False
     n = comm.group_size(dp_group)
-    if not (1 < n <= MAX_RANKS) or dist.get_backend(dp_group) != "nccl":
+    if not (comm.min_fused_ranks() <= n <= MAX_RANKS) or dist.get_backend(dp_group) != "nccl":
         return False
     if any(dt != torch.bfloat16 for dt in param_dtypes):
         return False

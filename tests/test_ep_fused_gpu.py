@@ -1,4 +1,4 @@
-"""Fused expert-parallel dispatch / combine (peer-memory kernels) vs the all-to-all path (2 GPUs).
+"""Fused expert-parallel dispatch / combine (peer-memory kernels) vs the all-to-all path (one rank on one GPU; 2+ GPUs).
 
 Same module, same inputs: forward output, input gradient, router and expert
 gradients and the dropped fraction must agree with the NCCL all-to-all
@@ -82,13 +82,19 @@ def _worker(rank, world, port, q):
         q.put((rank, None, repr(e) + traceback.format_exc()))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-# NTB_TEST_WORLD=4 (or 8) runs the same checks on more ranks when the GPUs are there.
-def test_fused_ep_dispatch_combine_two_gpus():
+# "one": a one-rank group on one GPU (every peer pointer is this GPU's memory), so the kernels'
+# protocol is checked where only one GPU is present; "multi": 2 ranks, or NTB_TEST_WORLD=4 (or 8).
+@pytest.mark.parametrize("ranks", ["one", "multi"])
+def test_fused_ep_dispatch_combine(ranks, monkeypatch):
+    if ranks == "multi" and torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    if ranks == "one":
+        monkeypatch.setenv("NTB_FUSED_ONE_RANK", "1")
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    world = max(2, min(int(os.environ.get("NTB_TEST_WORLD", "2")), torch.cuda.device_count()))
+    world = 1 if ranks == "one" else max(2, min(int(os.environ.get("NTB_TEST_WORLD", "2")),
+                                                torch.cuda.device_count()))
     procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
