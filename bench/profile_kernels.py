@@ -6,6 +6,8 @@ Each case allocates a few hundred MB at most (inputs larger than the 126 MB
 L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
 ``--iters`` launches, and checks the kernel status word. Cases:
 
+  gemm          any dense tcgen05 GEMM (--mnk M,N,K --layout fwd|dgrad|wgrad; --cublas for torch.matmul);
+                NTB_GEMM_BN=128|256 forces the tile width
   gemm_fwd      tcgen05 GEMM 4096 x 6144 x 4096 (Llama-8B QKV, K-major A and B)
   gemm_wgrad    4096 x 14336 x 4096 with M-major A / N-major B (weight gradient)
   attn_fwd      flash attention fwd, B=1 S=4096 32q/8kv heads d=128 causal
@@ -44,6 +46,9 @@ def main():
     ap.add_argument("--iters", type=int, default=3)
     ap.add_argument("--time", type=int, default=0,
                     help="also time this many launches with CUDA events (after the warm-up) and print ms / GB/s")
+    ap.add_argument("--mnk", default="4096,4096,4096", help="gemm case: M,N,K")
+    ap.add_argument("--layout", default="fwd", choices=("fwd", "dgrad", "wgrad"), help="gemm case: operand layout")
+    ap.add_argument("--cublas", action="store_true", help="gemm case: time torch.matmul instead")
     a = ap.parse_args()
     nbytes = 0  # algorithmic DRAM bytes of one launch, where the case defines them
     nflops = 0  # algorithmic FLOPs of one launch, where the case defines them
@@ -51,7 +56,27 @@ def main():
     dev = torch.device("cuda", 0)
     torch.manual_seed(0)
     bf = dict(device=dev, dtype=torch.bfloat16)
-    if a.case == "gemm_fwd":
+    if a.case == "gemm":
+        # any dense GEMM: --mnk M,N,K and --layout fwd (a [M,K], b [N,K]), dgrad (b [K,N]) or
+        # wgrad (a [K,M], b [K,N], fp32 accumulate); --cublas times torch.matmul of the same product
+        M, N, K = (int(v) for v in a.mnk.split(","))
+        nflops = 2 * M * N * K
+        if a.layout == "wgrad":
+            x, w = torch.randn(K, M, **bf), torch.randn(K, N, **bf)
+            y = torch.zeros(M, N, device=dev, dtype=torch.float32)
+            fn = lambda: C.gemm_bf16(x, w, y, None, True, True, True, 1.0)  # noqa: E731
+            yb = torch.empty(M, N, **bf)
+            ref = lambda: torch.matmul(x.t(), w, out=yb)  # noqa: E731  (bf16 out: cuBLAS has no fp32-accumulate form here)
+        else:
+            x = torch.randn(M, K, **bf)
+            w = torch.randn(K, N, **bf) if a.layout == "dgrad" else torch.randn(N, K, **bf)
+            y = torch.empty(M, N, **bf)
+            bmn = a.layout == "dgrad"
+            fn = lambda: C.gemm_bf16(x, w, y, None, False, bmn, False, 1.0)  # noqa: E731
+            ref = lambda: torch.matmul(x, w if bmn else w.t(), out=y)  # noqa: E731
+        if a.cublas:
+            fn = ref
+    elif a.case == "gemm_fwd":
         x, w = torch.randn(4096, 4096, **bf), torch.randn(6144, 4096, **bf)
         y = torch.empty(4096, 6144, **bf)
         fn = lambda: C.gemm_bf16(x, w, y, None, False, False, False, 1.0)  # noqa: E731

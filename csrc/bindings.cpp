@@ -100,7 +100,10 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
              bool b_mn, std::vector<int64_t> recv, std::vector<int64_t> tctrs, at::Tensor& ctrs, int64_t rank,
              int64_t epoch, const c10::optional<at::Tensor>& trace);
 void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns);
-void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank);
+void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank,
+             int64_t flags_ptr, int64_t epoch);
+void gemm_bf16_publish(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool b_mn,
+                       std::vector<int64_t> flags, int64_t epoch, at::Tensor& ctr);
 // router.cu
 std::vector<at::Tensor> router_fwd(const at::Tensor& logits, int64_t K, bool softmax, int64_t n_group,
                                    int64_t topk_group, bool norm_topk, double scale);
@@ -203,7 +206,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_rs", &ntb::gemm_rs, py::arg("x"), py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("b_mn"),
         py::arg("recv"), py::arg("tctrs"), py::arg("ctrs"), py::arg("rank"), py::arg("epoch"),
         py::arg("trace") = py::none());
-  m.def("rs_pull", &ntb::rs_pull, py::arg("parts"), py::arg("out"), py::arg("bias"), py::arg("rank"));
+  m.def("rs_pull", &ntb::rs_pull, py::arg("parts"), py::arg("out"), py::arg("bias"), py::arg("rank"),
+        py::arg("flags_ptr") = 0, py::arg("epoch") = 0);
+  m.def("gemm_bf16_publish", &ntb::gemm_bf16_publish, "tcgen05 bf16 GEMM whose last CTA publishes an epoch",
+        py::arg("a"), py::arg("b"), py::arg("out"), py::arg("b_mn"), py::arg("flags"), py::arg("epoch"),
+        py::arg("ctr"));
   m.def("wait_flag", &ntb::wait_flag, py::arg("flag"), py::arg("expect"), py::arg("limit_ns"));
   m.def("ep_dispatch", &ntb::ep_dispatch, py::arg("x"), py::arg("idx"), py::arg("w"), py::arg("dest_tk"),
         py::arg("slot_tk"), py::arg("ctr"), py::arg("epr"), py::arg("payload"), py::arg("pscale"), py::arg("meta"),

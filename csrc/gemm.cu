@@ -30,6 +30,7 @@
 
 #include "common.cuh"
 #include "host_utils.h"
+#include "peer.cuh"
 
 namespace ntb {
 
@@ -48,6 +49,17 @@ struct GemmParams {
   int b_group_rows;    // rows of one group's slice of the stacked B (mode 1)
   long m_limit;        // rows of C that exist (mode 2: per-group output rows)
   long c_group_stride; // mode 2: rows of C between consecutive groups' blocks (0 = M, a dense stack)
+  // Plain GEMM with an fp32 accumulated C only: K is cut into `splits` slices (1 = no split). Each
+  // (tile, slice) unit adds its partial product into C with vector atomics, so the sum's
+  // rounding order varies from run to run (fp32 low bits only).
+  int splits;
+  // Publication (plain GEMM, optional): when pub_n > 0, the last CTA to finish makes the whole C
+  // visible system-wide (fence.sc.sys) and stores pub_epoch into pub_flag[0..pub_n) - the epoch
+  // words of the peers that read C over NVLink. pub_ctr: a device u32 that is zero at rest.
+  unsigned long long* pub_flag[8];
+  int pub_n;
+  unsigned long long pub_epoch;
+  unsigned int* pub_ctr;
 };
 
 template <int BN>
@@ -71,7 +83,7 @@ struct GemmCfg {
 //   2  K-grouped (expert weight gradient): the output is a stack of per-expert
 //      [M, N] blocks; tile = (expert, m, n) and K runs over that expert's rows.
 struct TileInfo {
-  int mb, nb, group, kb0, nkb;
+  int mb, nb, group, kb0, nkb, slice;
 };
 
 __device__ __forceinline__ int group_of_row(const int* offsets, int groups, int row) {
@@ -104,10 +116,11 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
 // final rounding. m0: first row of the warp; n0: first column of the tile.
 template <int BN>
 __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, const GemmParams& p, long m0, int n0,
-                                              bool vec_ok, long m_end) {
+                                              bool vec_ok, long m_end, bool red = false) {
   const int lane = threadIdx.x & 31;
   const bool f32 = p.c_f32 != 0;
-  const bool acc = p.accumulate != 0;
+  // red: a K-slice of a split GEMM (fp32 C) - the partial is added with atomics, C is not read.
+  const bool acc = p.accumulate != 0 && !red;
 #pragma unroll 1
   for (int g = 0; g < BN; g += 64) {
     const int cg = n0 + g;
@@ -148,7 +161,7 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
         const int c = j * 4 + u;
         const uint32_t bits = c < 32 ? r0[c] : r1[c - 32];
         float x = __uint_as_float(bits) * p.alpha;
-        if (p.bias != nullptr && cg + c < p.N) x += __bfloat162float(p.bias[cg + c]);
+        if (p.bias != nullptr && !red && cg + c < p.N) x += __bfloat162float(p.bias[cg + c]);
         w[u] = x;
       }
       *reinterpret_cast<float4*>(stage + lane * 64 + ((j ^ (lane & 15)) * 4)) = v;
@@ -164,6 +177,15 @@ __device__ __forceinline__ void epilogue_tile(uint32_t t_row, float* stage, cons
         if (m >= m_end || col >= p.N) continue;
         float4 v = *reinterpret_cast<const float4*>(stage + row * 64 + ((ch ^ (row & 15)) * 4));
         float* dst = C + m * p.ldc + col;
+        if (red) {
+          if (vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0) {
+            red_add_v4(dst, v.x, v.y, v.z, v.w);
+          } else {
+            const float* vv = &v.x;
+            for (int u = 0; u < 4 && col + u < p.N; ++u) atomicAdd(dst + u, vv[u]);
+          }
+          continue;
+        }
         if (vec_ok && col + 4 <= p.N && (p.ldc & 3) == 0) {
           if (acc) {
             v.x += old[it].x; v.y += old[it].y; v.z += old[it].z; v.w += old[it].w;
@@ -221,6 +243,14 @@ __device__ __forceinline__ TileInfo tile_info(const GemmParams& p, int tile, int
     const int r0 = __ldg(p.offsets + t.group), r1 = __ldg(p.offsets + t.group + 1);
     t.kb0 = r0 / BK;
     t.nkb = (r1 - r0) / BK;
+  } else if (GM == 0 && p.splits > 1) {
+    // Slice-major order: the first wave runs slice 0 of consecutive tiles, as without a split.
+    const int per = num_m * num_n;
+    t.slice = tile / per;
+    tile_coords(tile - t.slice * per, num_m, num_n, t.mb, t.nb);
+    const int kper = (num_kb + p.splits - 1) / p.splits;
+    t.kb0 = t.slice * kper;
+    t.nkb = min(kper, num_kb - t.kb0);
   } else {
     tile_coords(tile, num_m, num_n, t.mb, t.nb);
     t.group = GM == 1 ? group_of_row(p.offsets, p.groups, t.mb * BM) : 0;
@@ -253,7 +283,7 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM, num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n * (GM == 2 ? p.groups : 1);
+  const int num_tiles = num_m * num_n * (GM == 2 ? p.groups : (GM == 0 && p.splits > 1 ? p.splits : 1));
   const int num_kb = (p.K + BK - 1) / BK;
 
   if (threadIdx.x == 0) {
@@ -337,7 +367,8 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t acc_phase = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
-        const int tile_nkb = GM == 2 ? tile_info<GM>(p, tile, num_m, num_n, num_kb, BM, BK).nkb : num_kb;
+        const int tile_nkb =
+            (GM == 2 || (GM == 0 && p.splits > 1)) ? tile_info<GM>(p, tile, num_m, num_n, num_kb, BM, BK).nkb : num_kb;
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status, kStatusTimeoutMma)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
@@ -389,7 +420,8 @@ __global__ void __launch_bounds__(192, 1)
       tc_fence_after();
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
       if (GM != 2) {
-        epilogue_tile<BN>(t_row, stage, p, static_cast<long>(ti.mb) * BM + q * 32, ti.nb * BN, vec_ok, p.M);
+        epilogue_tile<BN>(t_row, stage, p, static_cast<long>(ti.mb) * BM + q * 32, ti.nb * BN, vec_ok, p.M,
+                          GM == 0 && p.splits > 1);
       } else if (ti.nkb > 0) {
         // Expert block: rows [group * M, group * M + M) of the stacked output; an expert without
         // rows contributes nothing (its accumulator was never written).
@@ -404,11 +436,232 @@ __global__ void __launch_bounds__(192, 1)
     }
   }
 
+  if (p.pub_n > 0 && warp >= 2) __threadfence();  // this thread's C stores, before the CTA's arrival
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (p.pub_n > 0 && threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(p.pub_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      // Every CTA has arrived: their fenced stores are ordered before this point.
+      __threadfence_system();
+      for (int d = 0; d < p.pub_n && d < 8; ++d) st_relaxed_sys_u64(p.pub_flag[d], p.pub_epoch);
+      *p.pub_ctr = 0u;  // at rest again for the next launch (kernel boundary orders it)
+    }
+  }
+}
+
+// ------------------------------------------------------------------ CTA-pair (2-SM) GEMM
+// Plain GEMM on 256 x 256 tiles computed by a cluster of two CTAs on two SMs. CTA r of the pair
+// loads rows [128 r, 128 r + 128) of the tile's A and columns [128 r, 128 r + 128) of its B into its
+// own shared memory (no multicast), both loads completing on CTA 0's `full` barrier; CTA 0's MMA
+// warp issues tcgen05.mma.cta_group::2 (M = 256, N = 256), which reads both CTAs' operands and
+// writes rows [128 r, 128 r + 128) of the accumulator into CTA r's TMEM, and commits to the
+// `empty` / `tfull` barriers of both CTAs. Each CTA's epilogue drains its own half and arrives on
+// CTA 0's `tempty`. Per SM and K block, the tile moves 32 KB from L2 instead of the 48 KB of a
+// 128 x 256 single-CTA tile, for the same tensor-core work, and the six-stage ring fits.
+// Same parameters (fp32 accumulate, K slices, publication) as gemm_bf16_kernel with GM = 0.
+struct PairCfg {
+  static constexpr int BM = 128;  // rows per CTA; the pair covers 256
+  static constexpr int BN = 256;  // columns of the pair tile; each CTA holds 128 of B
+  static constexpr int BK = 64;
+  static constexpr int STAGES = 6;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = (BN / 2) * BK * 2;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGE_BYTES = 4 * 8192;
+  static constexpr int SMEM_BYTES = 1024 + STAGES * (A_BYTES + B_BYTES) + STAGE_BYTES + 256;
+};
+
+template <bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(192, 1)
+    gemm_bf16_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                          GemmParams p) {
+  using Cfg = PairCfg;
+  constexpr int BM = Cfg::BM, BN = Cfg::BN, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  constexpr int A_BYTES = Cfg::A_BYTES, B_BYTES = Cfg::B_BYTES;
+  constexpr uint32_t IDESC = make_idesc_f16(2 * BM, BN, A_MN, B_MN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_BYTES;
+  uint8_t* stage_base = sB + STAGES * B_BYTES;
+  uint64_t* full = reinterpret_cast<uint64_t*>(stage_base + Cfg::STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* drain = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const int num_m = (p.M + 2 * BM - 1) / (2 * BM), num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n * (p.splits > 1 ? p.splits : 1);
+  const int num_kb = (p.K + BK - 1) / BK;
+  const int pair = static_cast<int>(blockIdx.x >> 1), npairs = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);
+      mbar_init(&tempty[b], 2 * 128);  // every epilogue thread of both CTAs
+    }
+    mbar_init(drain, 1);
+    mbar_fence_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // both CTAs' barriers exist before either CTA signals the other's
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t full0 = cluster_addr(full, 0);      // CTA 0's full[s] at full0 + 8 s
+  const uint32_t tempty0 = cluster_addr(tempty, 0);  // CTA 0's tempty[b] at tempty0 + 8 b
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      uint32_t filled_mask = 0;
+      uint32_t last_phase[STAGES];
+#pragma unroll
+      for (int s = 0; s < STAGES; ++s) last_phase[s] = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const TileInfo ti = tile_info<0>(p, tile, num_m, num_n, num_kb, 2 * BM, BK);
+        const int arow = ti.mb * 2 * BM + static_cast<int>(rank) * BM;
+        const int bcol = ti.nb * BN + static_cast<int>(rank) * (BN / 2);
+        for (int kq = 0; kq < ti.nkb; ++kq) {
+          const int kb = ti.kb0 + kq;
+          if (!mbar_wait(&empty[stage], phase ^ 1, p.status, kStatusTimeoutProducer)) {
+            ok = false;
+            break;
+          }
+          // CTA 0 expects the bytes of both CTAs' loads on its barrier.
+          if (rank == 0) mbar_expect_tx(&full[stage], 2 * (A_BYTES + B_BYTES));
+          const uint32_t bar = full0 + 8u * static_cast<uint32_t>(stage);
+          uint8_t* a_dst = sA + stage * A_BYTES;
+          uint8_t* b_dst = sB + stage * B_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d_pair(a_dst, &tmA, bar, kb * BK, arow);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / 64; ++j) tma_load_2d_pair(a_dst + j * 8192, &tmA, bar, arow + j * 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d_pair(b_dst, &tmB, bar, kb * BK, bcol);
+          } else {
+#pragma unroll
+            for (int j = 0; j < (BN / 2) / 64; ++j)
+              tma_load_2d_pair(b_dst + j * 8192, &tmB, bar, bcol + j * 64, kb * BK);
+          }
+          filled_mask |= 1u << stage;
+          last_phase[stage] = phase;
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+      // CTA 0's barriers count both CTAs' bytes: never leave with a TMA write still landing.
+      if (rank == 0)
+        for (int s = 0; s < STAGES; ++s)
+          if (filled_mask & (1u << s)) mbar_wait(&full[s], last_phase[s], nullptr, 0) || true;
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && rank == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int tile = pair; tile < num_tiles && ok; tile += npairs) {
+        const int tile_nkb = p.splits > 1 ? tile_info<0>(p, tile, num_m, num_n, num_kb, 2 * BM, BK).nkb : num_kb;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1, p.status, kStatusTimeoutMma)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < tile_nkb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, kStatusTimeoutMma)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * A_BYTES);
+          const uint32_t b_base = smem_u32(sB + stage * B_BYTES);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t adesc = A_MN ? make_smem_desc_sw128(a_base + k * 2048, 8192, 1024)
+                                        : make_smem_desc_sw128(a_base + k * 32, 16, 1024);
+            const uint64_t bdesc = B_MN ? make_smem_desc_sw128(b_base + k * 2048, 8192, 1024)
+                                        : make_smem_desc_sw128(b_base + k * 32, 16, 1024);
+            umma_f16_ss_pair(d_tmem, adesc, bdesc, IDESC, (kb | k) != 0 ? 1u : 0u);
+          }
+          umma_commit_pair(cluster_addr(&empty[stage], 0));
+          umma_commit_pair(cluster_addr(&empty[stage], 1));
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(cluster_addr(&tfull[acc], 0));
+        umma_commit_pair(cluster_addr(&tfull[acc], 1));
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1;
+      }
+      // Every MMA (which reads both CTAs' shared memory) retires before either CTA moves on.
+      umma_commit_pair(cluster_addr(drain, 0));
+      mbar_wait(drain, 0, nullptr, 0);
+    }
+  } else {
+    const int q = warp & 3;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    const bool vec_ok = ((p.ldc & 7) == 0) && ((reinterpret_cast<uintptr_t>(p.C) & 15) == 0);
+    float* stage = reinterpret_cast<float*>(stage_base + q * 8192);
+    for (int tile = pair; tile < num_tiles; tile += npairs) {
+      const TileInfo ti = tile_info<0>(p, tile, num_m, num_n, num_kb, 2 * BM, BK);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, kStatusTimeoutEpilogue)) break;
+      tc_fence_after();
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(q * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      epilogue_tile<BN>(t_row, stage, p, static_cast<long>(ti.mb) * 2 * BM + rank * BM + q * 32, ti.nb * BN,
+                        vec_ok, p.M, p.splits > 1);
+      tc_fence_before();
+      mbar_arrive_cluster(tempty0 + 8u * static_cast<uint32_t>(acc));
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1;
+    }
+  }
+
+  if (p.pub_n > 0 && warp >= 2) __threadfence();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync_all();  // CTA 0's MMAs have retired and every cross-CTA arrival has landed
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (p.pub_n > 0 && threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(p.pub_ctr, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      for (int d = 0; d < p.pub_n && d < 8; ++d) st_relaxed_sys_u64(p.pub_flag[d], p.pub_epoch);
+      *p.pub_ctr = 0u;
+    }
   }
 }
 
@@ -425,12 +678,113 @@ static void launch_gemm(const CUtensorMap* ta, const CUtensorMap* tb, GemmParams
     NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     attr_set[dev & 15] = true;
   }
-  const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN) * (GM == 2 ? p.groups : 1);
+  const int num_tiles = ((p.M + Cfg::BM - 1) / Cfg::BM) * ((p.N + BN - 1) / BN) *
+                        (GM == 2 ? p.groups : (GM == 0 && p.splits > 1 ? p.splits : 1));
   const int grid = std::min(num_tiles, num_sms(dev));
   void* args[3] = {const_cast<CUtensorMap*>(ta), const_cast<CUtensorMap*>(tb), &p};
   NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), dim3(grid), dim3(192), args,
                                   Cfg::SMEM_BYTES, stream));
   NTB_LAUNCH_CHECK(1);
+}
+
+template <bool A_MN, bool B_MN>
+static void launch_gemm_pair(const CUtensorMap* ta, const CUtensorMap* tb, GemmParams p, cudaStream_t stream) {
+  auto kern = gemm_bf16_pair_kernel<A_MN, B_MN>;
+  static bool attr_set[16] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 15]) {
+    NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, PairCfg::SMEM_BYTES));
+    attr_set[dev & 15] = true;
+  }
+  const int units = ((p.M + 2 * PairCfg::BM - 1) / (2 * PairCfg::BM)) * ((p.N + PairCfg::BN - 1) / PairCfg::BN) *
+                    (p.splits > 1 ? p.splits : 1);
+  const int pairs = std::max(1, std::min(units, num_sms(dev) / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs);
+  cfg.blockDim = dim3(192);
+  cfg.dynamicSmemBytes = PairCfg::SMEM_BYTES;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[3] = {const_cast<CUtensorMap*>(ta), const_cast<CUtensorMap*>(tb), &p};
+  NTB_CUDA_CHECK(cudaLaunchKernelExC(&cfg, reinterpret_cast<const void*>(kern), args));
+  NTB_LAUNCH_CHECK(1);
+}
+
+// Tile shape of a dense GEMM: the tile width (128 or 256) and, for an fp32 accumulated
+// C without bias (weight gradients into fp32 main grads), a split of K into 1-3 slices.
+// Every unit of the persistent kernel runs the same K loop, so the kernel's time is
+// (waves of units) x (time of one unit). Measured on B200 (bench/profile_kernels.py gemm):
+//   - a 128-wide tile runs at about 0.63 of the 256-wide tile's rate (4096^3: 155.6 us
+//     against 112.6 us for 7 waves of narrow against 4 waves of wide tiles), so it wins
+//     only where the wide tiles leave most SMs idle;
+//   - a K slice adds its partial to C with fire-and-forget vector reductions; fitted over
+//     768..6144 x 512..4096 x 4096 weight gradients, two slices cost 6.5 % and three 29 % on
+//     top of the wave count (1.07x faster at 4096^3 and 3584 x 4096 with two slices, 1.2x at
+//     768 x 4096 with three, 0.84x at 4096^3 with three), so a split is taken only where the
+//     model saves more than 5 %.
+// Tensor-parallel ranks gain most: an N = 512 weight gradient is 64 wide tiles on 148 SMs.
+// NTB_GEMM_BN=128|256 forces the width; NTB_GEMM_SPLITK=0 turns the split off, =2..4 forces it.
+struct TileChoice {
+  bool wide;
+  int splits;
+};
+
+static TileChoice pick_tiles(int64_t M, int64_t N, int64_t K, int nsm, bool can_split) {
+  static const int forced_bn = [] {
+    const char* e = std::getenv("NTB_GEMM_BN");
+    return e ? std::atoi(e) : 0;
+  }();
+  static const int forced_split = [] {  // -1: automatic, 0: off, 2..4: that many slices where allowed
+    const char* e = std::getenv("NTB_GEMM_SPLITK");
+    return e ? std::atoi(e) : -1;
+  }();
+  constexpr double kNarrowRate = 0.63;     // rate of a 128-wide tile relative to a 256-wide one
+  constexpr double kSliceCost[4] = {1.0, 1.0, 1.065, 1.29};  // time factor of a unit split into s slices
+  constexpr double kSplitMargin = 0.95;    // a split must beat the best unsplit shape by 5 %
+  constexpr int64_t kMinSliceBlocks = 16;  // K blocks of 64 per slice, so the pipeline stays full
+  const int64_t mt = (M + 127) / 128, kb = (K + 63) / 64;
+  auto cost = [&](bool wide, int sp) {
+    const int64_t units = mt * ((N + (wide ? 255 : 127)) / (wide ? 256 : 128)) * sp;
+    const double w = static_cast<double>((units + nsm - 1) / nsm);
+    return w / sp * (wide ? 1.0 : 0.5 / kNarrowRate) * kSliceCost[sp];
+  };
+  auto width_ok = [&](bool wide) {
+    if (wide && N <= 128) return false;
+    if (forced_bn == 128) return !wide;
+    if (forced_bn == 256) return wide || N <= 128;
+    return true;
+  };
+  TileChoice best{N > 128, 1};
+  double best_cost = 1e30;
+  for (int w = 1; w >= 0; --w)
+    if (width_ok(w == 1) && cost(w == 1, 1) < best_cost - 1e-9) {
+      best_cost = cost(w == 1, 1);
+      best = {w == 1, 1};
+    }
+  if (!can_split || forced_split == 0) return best;
+  if (forced_split >= 2) {
+    const int sp = static_cast<int>(std::min<int64_t>(forced_split, std::max<int64_t>(1, kb / kMinSliceBlocks)));
+    return {best.wide, std::min(sp, 4)};
+  }
+  const double bar = best_cost * kSplitMargin;
+  TileChoice split = best;
+  double split_cost = 1e30;
+  for (int w = 1; w >= 0; --w) {
+    if (!width_ok(w == 1)) continue;
+    for (int sp = 2; sp <= 3 && kb >= kMinSliceBlocks * sp; ++sp)
+      if (cost(w == 1, sp) < split_cost - 1e-9) {
+        split_cost = cost(w == 1, sp);
+        split = {w == 1, sp};
+      }
+  }
+  return split_cost < bar ? split : best;
 }
 
 // Builds the TMA descriptor of one operand. K-major operands are read as
@@ -446,8 +800,9 @@ static void operand_map(CUtensorMap* out, const at::Tensor& t, bool mn_major, in
 //   a: [M,K] (a_mn=false) or [K,M] (a_mn=true), bf16, unit inner stride
 //   b: [N,K] (b_mn=false) or [K,N] (b_mn=true), bf16, unit inner stride
 //   out: [M,N] bf16 or fp32 with unit inner stride
-void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const c10::optional<at::Tensor>& bias,
-               bool a_mn, bool b_mn, bool accumulate, double alpha) {
+static void gemm_bf16_impl(const at::Tensor& a, const at::Tensor& b, at::Tensor& out,
+                           const c10::optional<at::Tensor>& bias, bool a_mn, bool b_mn, bool accumulate, double alpha,
+                           const std::vector<int64_t>& pub_flags, int64_t pub_epoch, unsigned int* pub_ctr) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && out.is_cuda(), "gemm_bf16: CUDA tensors required");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm_bf16: bf16 operands");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && out.dim() == 2, "gemm_bf16: 2-D tensors");
@@ -462,13 +817,15 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   TORCH_CHECK((a.stride(0) * 2) % 16 == 0 && (b.stride(0) * 2) % 16 == 0, "gemm_bf16: row stride must be 16B aligned");
   TORCH_CHECK((reinterpret_cast<uintptr_t>(a.data_ptr()) & 15) == 0 && (reinterpret_cast<uintptr_t>(b.data_ptr()) & 15) == 0,
               "gemm_bf16: operands must be 16B aligned");
+  // A publishing launch must run (peers wait for its epoch).
+  TORCH_CHECK(pub_flags.empty() || (M > 0 && N > 0 && K > 0), "gemm_bf16_publish: empty problem");
   if (M == 0 || N == 0) return;
   if (K == 0) {
     if (!accumulate) out.zero_();
     if (bias.has_value()) out.add_(bias.value());
     return;
   }
-  GemmParams p;
+  GemmParams p{};
   p.M = static_cast<int>(M);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
@@ -484,13 +841,35 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
   p.groups = 1;
   p.b_group_rows = 0;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(a.get_device());
-  // Narrow problems waste half of a 256-wide tile: use 128.
-  const bool wide = N > 128;
+  const TileChoice tc = pick_tiles(M, N, K, num_sms(a.get_device()),
+                                   accumulate && p.c_f32 && !bias.has_value());
+  const bool wide = tc.wide;
+  p.splits = tc.splits;
+  if (!pub_flags.empty()) {
+    TORCH_CHECK(pub_flags.size() <= 8 && pub_ctr != nullptr && !accumulate, "gemm_bf16: publication to 1..8 flags");
+    for (size_t i = 0; i < pub_flags.size(); ++i) p.pub_flag[i] = reinterpret_cast<unsigned long long*>(pub_flags[i]);
+    p.pub_n = static_cast<int>(pub_flags.size());
+    p.pub_epoch = static_cast<unsigned long long>(pub_epoch);
+    p.pub_ctr = pub_ctr;
+    p.splits = 1;
+  }
+  static const bool pair_on = [] {
+    const char* e = std::getenv("NTB_GEMM_2SM");
+    return e && e[0] == '1';
+  }();
+  const bool pair = pair_on && wide && M >= 256;
   TmaSlots& slots = tls_tma_slots();
   CUtensorMap* ta = &slots.m[0];
   CUtensorMap* tb = &slots.m[1];
   operand_map(ta, a, a_mn, 128);
-  operand_map(tb, b, b_mn, wide ? 256 : 128);
+  operand_map(tb, b, b_mn, (wide && !pair) ? 256 : 128);
+  if (pair) {
+    if (!a_mn && !b_mn) launch_gemm_pair<false, false>(ta, tb, p, stream);
+    else if (!a_mn && b_mn) launch_gemm_pair<false, true>(ta, tb, p, stream);
+    else if (a_mn && !b_mn) launch_gemm_pair<true, false>(ta, tb, p, stream);
+    else launch_gemm_pair<true, true>(ta, tb, p, stream);
+    return;
+  }
 #define NTB_GEMM_CASE(BN_, AM, BM_)                     \
   if (a_mn == AM && b_mn == BM_) {                      \
     launch_gemm<BN_, AM, BM_>(ta, tb, p, stream);       \
@@ -504,6 +883,22 @@ void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const 
     NTB_GEMM_CASE(128, true, true)
   }
 #undef NTB_GEMM_CASE
+}
+
+void gemm_bf16(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+               bool a_mn, bool b_mn, bool accumulate, double alpha) {
+  gemm_bf16_impl(a, b, out, bias, a_mn, b_mn, accumulate, alpha, {}, 0, nullptr);
+}
+
+// out = a . op(b)^T, then the last CTA publishes `epoch` to every address of `flags` (device
+// u64 epoch words, typically the peers' copies of this rank's flag) after a system-scope fence,
+// so peers may read `out` over NVLink once they see the epoch. `ctr`: int32 device word, zero.
+void gemm_bf16_publish(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool b_mn,
+                       std::vector<int64_t> flags, int64_t epoch, at::Tensor& ctr) {
+  TORCH_CHECK(ctr.is_cuda() && ctr.scalar_type() == at::kInt && ctr.numel() >= 1, "gemm_bf16_publish: int32 ctr");
+  TORCH_CHECK(!flags.empty(), "gemm_bf16_publish: at least one flag");
+  gemm_bf16_impl(a, b, out, c10::nullopt, false, b_mn, false, 1.0, flags, epoch,
+                 reinterpret_cast<unsigned int*>(ctr.data_ptr()));
 }
 
 // Grouped GEMM for mixture-of-experts layers. `offsets` (int32 [G + 1], device) are the

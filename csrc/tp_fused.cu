@@ -766,9 +766,25 @@ struct RsPullParams {
   const bf16* bias;
   long rows, N, ld_part, ld_out;
   int n;
+  // Optional wait (flags != nullptr): before reading, every CTA waits (bounded) until each of the n
+  // epoch words flags[0..n) - written by the ranks' publishing GEMMs - reaches `epoch`.
+  const unsigned long long* flags;
+  unsigned long long epoch;
+  int* status;
 };
 
 __global__ void __launch_bounds__(256) rs_pull_kernel(const __grid_constant__ RsPullParams p) {
+  if (p.flags != nullptr) {
+    __shared__ int ok;
+    if (threadIdx.x == 0) {
+      bool good = true;
+      for (int s = 0; s < p.n && good; ++s)
+        good = spin_until([&] { return ld_acquire_sys_u64(p.flags + s) >= p.epoch; }, p.status, kStatusTimeoutPeer);
+      ok = good ? 1 : 0;
+    }
+    __syncthreads();  // the acquiring thread's view of the peers' partials, for the whole CTA
+    if (!ok) return;
+  }
   const long cpr = p.N / 8;  // 16-byte chunks per row
   const long total = p.rows * cpr;
   for (long i = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x; i < total;
@@ -799,7 +815,8 @@ __global__ void __launch_bounds__(256) rs_pull_kernel(const __grid_constant__ Rs
 }
 
 // parts: int64 [n] device addresses of every rank's partial [n * T_local, N] (row pitch N)
-void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank) {
+void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank,
+             int64_t flags_ptr, int64_t epoch) {
   const int n = static_cast<int>(parts.size());
   TORCH_CHECK(n >= 1 && n <= kMaxRanks && rank >= 0 && rank < n, "rs_pull: 1..8 ranks");
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kBFloat16 && out.dim() == 2 && out.is_contiguous(),
@@ -821,6 +838,9 @@ void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at
   p.ld_out = N;
   p.n = n;
   const int dev = out.get_device();
+  p.flags = reinterpret_cast<const unsigned long long*>(flags_ptr);
+  p.epoch = static_cast<unsigned long long>(epoch);
+  p.status = device_status(dev);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
   const long chunks = rows * (N / 8);
   const int grid = static_cast<int>(std::max<long>(1, std::min<long>((chunks + 255) / 256, num_sms(dev) * 8L)));

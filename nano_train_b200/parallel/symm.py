@@ -71,6 +71,7 @@ class TPCommunicator:
                 self._opened.append(p)
         # Local scratch of the fused kernels (tile/piece counters, per-chunk copy counts); zeroed per call.
         self.ctrs = torch.zeros(1 + self.n, dtype=torch.int64, device=self.device)
+        self.pub_ctr = torch.zeros(1, dtype=torch.int32, device=self.device)  # GEMM arrival count, zero at rest
         self.ag_epoch = 0
         self.rs_epoch = 0
         self.closed = False
@@ -126,10 +127,9 @@ class TPCommunicator:
         return y, full
 
     def gemm_reduce_scatter_pull(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False, bias=None):
-        """GEMM into this rank's symmetric slot, publish, then one pull kernel sums this rank's rows of
-        every rank's partial (peer loads, fixed rank order)."""
-        from ..ops.linear import gemm
-
+        """GEMM into this rank's symmetric slot whose last CTA publishes the epoch to every rank, then one
+        pull kernel that waits for every rank's epoch and sums this rank's rows of every partial (peer
+        loads, fixed rank order). Two launches; no separate signal or wait kernel."""
         T, K = x.shape
         N = weight.shape[1] if b_mn else weight.shape[0]
         T_local = T // self.n
@@ -140,11 +140,10 @@ class TPCommunicator:
         C = ext()
         dev = x.device.index
         part = C.symm_local_view(self.local_ptr, self.rs_offs[parity], [T, N], torch.bfloat16, dev)
-        gemm(x, weight, out=part, b_mn=b_mn)
-        C.ep_signal([p + 512 + self.rank * 8 for p in self.ptrs], self.rs_epoch, dev)
-        C.ep_wait(self.local_ptr + 512, self.n, self.rs_epoch, dev)
+        C.gemm_bf16_publish(x.contiguous(), weight, part, b_mn, [p + 512 + self.rank * 8 for p in self.ptrs],
+                            self.rs_epoch, self.pub_ctr)
         out = torch.empty(T_local, N, dtype=torch.bfloat16, device=x.device)
-        C.rs_pull(self._rs_recv_ptrs(parity), out, bias, self.rank)
+        C.rs_pull(self._rs_recv_ptrs(parity), out, bias, self.rank, self.local_ptr + 512, self.rs_epoch)
         return out
 
     def gemm_reduce_scatter(self, x: torch.Tensor, weight: torch.Tensor, b_mn: bool = False, bias=None):

@@ -53,6 +53,24 @@ def test_gemm_fp32_accumulate_bias(C):
     assert rel_err(out, ref) < 1e-5
 
 
+# Weight-gradient shapes of a tensor-parallel rank (Llama-8B, TP = 8, 4096 tokens) and of one GPU: the
+# tile picker splits K into slices for most of them (fp32 C accumulated with atomics) and picks the
+# 128-wide tile for some; ragged shapes check the edges of a split unit.
+@pytest.mark.parametrize("M,N,K", [(768, 4096, 4096), (4096, 512, 4096), (3584, 4096, 4096), (4096, 1792, 4096),
+                                   (6144, 4096, 4096), (1000, 520, 2056), (200, 136, 8192)])
+def test_gemm_weight_grad_split_k(C, M, N, K):
+    torch.manual_seed(M + N + K)
+    dy = torch.randn(K, M, device="cuda", dtype=torch.bfloat16)  # [tokens, out] (M-major A)
+    x = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)   # [tokens, in]  (N-major B)
+    out = torch.randn(M, N, device="cuda", dtype=torch.float32)
+    ref = out + dy.float().t() @ x.float()
+    C.gemm_bf16(dy, x, out, None, True, True, True, 1.0)
+    torch.cuda.synchronize()
+    from nano_train_b200.ops._ext import check_status
+    check_status(0)
+    assert rel_err(out, ref) < 1e-5, rel_err(out, ref)
+
+
 def test_linear_autograd_matches_reference():
     from nano_train_b200.ops.linear import linear
     torch.manual_seed(0)
