@@ -403,7 +403,8 @@ def run_ours(args, rank, local, world):
         a = get_communicator(dist.group.WORLD)
         if a is not None and hasattr(a, "choice"):
             fused_paths = {f"{k[0]} x{list(k[1])} w{list(k[2])}{' bmn' if k[3] else ''}":
-                           {"path": v, "ms": a.timings.get(k, {}), "rel_err": getattr(a, "rel_err", {}).get(k, {})}
+                           {"path": v, "ms": a.timings.get(k, {}), "rel_err": getattr(a, "rel_err", {}).get(k, {}),
+                            **({"rejected": a.rejected[k]} if k in getattr(a, "rejected", {}) else {})}
                            for k, v in a.choice.items()}
 
     e2e = None

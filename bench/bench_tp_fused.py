@@ -10,6 +10,8 @@ the launching stream, max over ranks, median of iterations:
   gemm_ms    the GEMM alone on local data (no communication)
   roof_ms    max(FLOPs / measured bf16 peak, NVLink bytes / 770 GB/s)
   frac       roof_ms / fused_ms (fraction of roofline)
+and for the reduce-scatter ops also the GEMM + pull kernel (pull_*) and the progressive-pull
+single kernel (overlap_*).
 """
 import argparse
 import datetime
@@ -133,6 +135,7 @@ def main():
                 torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
             fused = lambda: c.gemm_reduce_scatter(x, w, b_mn=b_mn)
             pull = lambda: c.gemm_reduce_scatter_pull(x, w, b_mn=b_mn)
+            ovl = lambda: c.gemm_reduce_scatter_overlap(x, w, b_mn=b_mn)
             nccl = lambda: comm.reduce_scatter_dim0(gemm(x, w, b_mn=b_mn), g)
             alone = lambda: gemm(x, w, b_mn=b_mn)
             flops = 2.0 * T * N * K
@@ -157,6 +160,10 @@ def main():
             rel = ((pull().float() - ref).norm() / ref.norm()).item()
             tp = timeit(pull, args.iters)
             row.update(pull_ms=tp, pull_frac=roof / tp, pull_speedup_vs_nccl=tn / tp, pull_rel_err_vs_nccl=rel)
+            rel_o = ((ovl().float() - ref).norm() / ref.norm()).item()
+            to = timeit(ovl, args.iters)
+            row.update(overlap_ms=to, overlap_frac=roof / to, overlap_speedup_vs_nccl=tn / to,
+                       overlap_rel_err_vs_nccl=rel_o)
         rows.append(row)
         if rank == 0:
             print(json.dumps(row), flush=True)

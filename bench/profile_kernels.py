@@ -14,6 +14,8 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   attn_bwd      flash attention bwd, same shape
   attn_fwd_tc   tcgen05 flash attention fwd, same shape
   attn_bwd_tc   tcgen05 flash attention bwd (the default backward for head dim 128), same shape
+  attn_{fwd,bwd}_{tc128,tc128_tp8,mla}  tcgen05 attention on the Llama shape, one TP = 8 rank of it
+                (4 q / 1 kv heads) and the DeepSeek-V2-Lite MLA shape (--time reports TFLOP/s)
   fp8_gemm      block-scaled e4m3 GEMM 8192 x 2048 x 7168 (DeepSeek-V3 recipe scales)
   fp4_gemm      NVFP4 GEMM 16384 x 8192 x 2048 (GPT-1.3B MLP fc1 shape, e2m1 with e4m3 1x16 scales)
   grouped_fwd   grouped expert GEMM, 64 experts, 49152 routed rows x 2816 x 2048 (DeepSeek-V2-Lite gate|up)
@@ -123,11 +125,14 @@ def main():
         o, lse = C.flash_attn_fwd_tc(q, k, v, 128 ** -0.5, True)
         do = torch.randn_like(o)
         fn = lambda: C.flash_attn_bwd(do, q, k, v, o, lse, 128 ** -0.5, True)  # noqa: E731
-    elif a.case in ("attn_fwd_mla", "attn_bwd_mla", "attn_fwd_tc128", "attn_bwd_tc128"):
-        # DeepSeek-V2-Lite MLA shape (2 x 4096 tokens, 16 heads, q/k 192, v 128) or the Llama shape
-        # (1 x 4096, 32 q / 8 kv heads, 128), causal; tcgen05 kernels
+    elif a.case in ("attn_fwd_mla", "attn_bwd_mla", "attn_fwd_tc128", "attn_bwd_tc128", "attn_fwd_tc128_tp8",
+                    "attn_bwd_tc128_tp8"):
+        # DeepSeek-V2-Lite MLA shape (2 x 4096 tokens, 16 heads, q/k 192, v 128), the Llama shape
+        # (1 x 4096, 32 q / 8 kv heads, 128) or its TP = 8 rank (4 q / 1 kv heads), causal; tcgen05 kernels
         mla = a.case.endswith("mla")
         Bq, Sq, hq, hkv, dqk, dvv = (2, 4096, 16, 16, 192, 128) if mla else (1, 4096, 32, 8, 128, 128)
+        if a.case.endswith("tp8"):
+            hq, hkv = 4, 1
         buf = torch.randn(Bq, Sq, hq * dqk + hkv * (dqk + dvv), **bf)
         q = buf[..., : hq * dqk].view(Bq, Sq, hq, dqk)
         k = buf[..., hq * dqk: (hq + hkv) * dqk].view(Bq, Sq, hkv, dqk)

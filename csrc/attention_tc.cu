@@ -468,14 +468,43 @@ struct AttnTcBwdParams {
   float* dq_acc;       // [B, Hq, S, D] fp32, unscaled dS K
   __nv_bfloat16* dk;   // strided [B, S, Hkv, D]
   __nv_bfloat16* dv;
-  float* dk_acc;       // GQA: fp32 [B, S, Hkv, D] accumulators (one CTA per query head adds into them)
+  float* dk_acc;       // GQA or split: fp32 [B, S, Hkv, D] accumulators (every contributing CTA adds into them)
   float* dv_acc;
   int64_t dk_sb, dk_ss, dk_sh, dv_sb, dv_ss, dv_sh;
   int B, S, Hq, Hkv;
   float scale, scale_log2;
   int causal;
   int* status;
+  // Serial kernel only: 0, or the most query blocks one CTA processes. With a split, blockIdx.x
+  // enumerates (key block, run of at most qsplit query blocks) pairs, heaviest key blocks first,
+  // and dK / dV always go through the fp32 accumulators.
+  int qsplit;
 };
+
+// Key block and query-block run of this CTA (see AttnTcBwdParams::qsplit).
+__device__ __forceinline__ void bwd_work_item(const AttnTcBwdParams& p, int nqb, int& kb, int& qb_first, int& iters) {
+  if (p.qsplit <= 0) {
+    kb = static_cast<int>(blockIdx.x);
+    qb_first = p.causal ? kb : 0;
+    iters = nqb - qb_first;
+    return;
+  }
+  int rem = static_cast<int>(blockIdx.x);
+  for (kb = 0; kb < nqb; ++kb) {
+    const int first = p.causal ? kb : 0;
+    const int cnt = nqb - first;
+    const int runs = (cnt + p.qsplit - 1) / p.qsplit;
+    if (rem < runs) {
+      qb_first = first + rem * p.qsplit;
+      iters = min(p.qsplit, cnt - rem * p.qsplit);
+      return;
+    }
+    rem -= runs;
+  }
+  kb = 0;  // past the last item (the host sizes the grid exactly): no work
+  qb_first = 0;
+  iters = 0;
+}
 
 template <int DQK, int DV, bool SERIAL>
 __global__ void __launch_bounds__(192, 1)
@@ -510,15 +539,13 @@ __global__ void __launch_bounds__(192, 1)
   float* s_delta_all = s_lse_all + 256;                        // [2][128]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int kb = blockIdx.x;  // heaviest (lowest) key blocks first
   const int hq = blockIdx.y, b = blockIdx.z;
   const int group = p.Hq / p.Hkv;
   const int hk = hq / group;
-  const int k0 = kb * BN;
   const int nqb = (p.S + BM - 1) / BM;
-  const int qb_first = p.causal ? kb : 0;
-  const int per_head = nqb - qb_first;
-  const int iters = per_head;
+  int kb, qb_first, iters;  // heaviest (lowest) key blocks first
+  bwd_work_item(p, nqb, kb, qb_first, iters);
+  const int k0 = kb * BN;
 
   if (threadIdx.x == 0) {
     mbar_init(kv_full, 1);
@@ -1193,7 +1220,13 @@ static void launch_bwd_tc(AttnTcBwdParams& p, const at::Tensor& q, const at::Ten
     NTB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
     attr_done[dev] = true;
   }
-  dim3 grid(static_cast<unsigned>((p.S + BN - 1) / BN), static_cast<unsigned>(p.Hq), static_cast<unsigned>(p.B));
+  const int nqb = (p.S + BN - 1) / BN;
+  int items = nqb;
+  if (!PIPE && p.qsplit > 0) {
+    items = 0;
+    for (int kb = 0; kb < nqb; ++kb) items += (nqb - (p.causal ? kb : 0) + p.qsplit - 1) / p.qsplit;
+  }
+  dim3 grid(static_cast<unsigned>(items), static_cast<unsigned>(p.Hq), static_cast<unsigned>(p.B));
   void* args[5] = {&ts.m[0], &ts.m[1], &ts.m[2], &ts.m[3], &p};
   NTB_CUDA_CHECK(cudaLaunchKernel(reinterpret_cast<const void*>(kern), grid, dim3(192), args,
                                   static_cast<size_t>(SMEM), stream));
@@ -1228,23 +1261,39 @@ void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at
   p.status = device_status(dev);
   at::Tensor dk_acc, dv_acc;
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
-  if (Hq != Hkv) {
+  // The pipelined variant (double-buffered Q, S of the next block issued under this block's
+  // softmax) measured 1009 us against 941 us for the serial chain on the Llama shape (B=1,
+  // S=4096, 32q/8kv heads, d=128, causal), so it runs only with NTB_ATTN_BWD_PIPE=1.
+  const char* pipe_env = std::getenv("NTB_ATTN_BWD_PIPE");
+  const bool pipe = pipe_env != nullptr && pipe_env[0] == '1' && DQK != 192;
+  // Query-run split of the serial kernel: one CTA per (key block, query head) gives few, very
+  // unequal CTAs when the heads per rank are few (tensor parallelism: 4 query heads at TP = 8 make
+  // 128 CTAs on 148 SMs, the first key block running 32 query blocks and the last one). Runs of
+  // at most qsplit query blocks, about two per SM, bound the longest CTA; dK / dV then add into
+  // the fp32 accumulators. NTB_ATTN_BWD_SPLIT=0 turns it off.
+  {
+    const int64_t nqb = (S + 127) / 128;
+    int64_t work = 0;
+    for (int64_t kb = 0; kb < nqb; ++kb) work += nqb - (causal ? kb : 0);
+    work *= Hq * B;
+    const int64_t target = 2LL * num_sms(dev);
+    const int64_t run = std::max<int64_t>(4, (work + target - 1) / target);
+    const char* split_env = std::getenv("NTB_ATTN_BWD_SPLIT");
+    const bool split_on = !(split_env != nullptr && split_env[0] == '0');
+    p.qsplit = (!pipe && split_on && run < nqb) ? static_cast<int>(run) : 0;
+  }
+  if (Hq != Hkv || p.qsplit > 0) {
     dk_acc = at::zeros({B, S, Hkv, DQK}, q.options().dtype(at::kFloat));
     dv_acc = at::zeros({B, S, Hkv, DV}, q.options().dtype(at::kFloat));
     p.dk_acc = dk_acc.data_ptr<float>();
     p.dv_acc = dv_acc.data_ptr<float>();
   }
-  // The pipelined variant (double-buffered Q, S of the next block issued under this block's
-  // softmax) measured 1009 us against 941 us for the serial chain on the Llama shape (B=1,
-  // S=4096, 32q/8kv heads, d=128, causal), so it runs only with NTB_ATTN_BWD_PIPE=1.
-  const char* pipe_env = std::getenv("NTB_ATTN_BWD_PIPE");
-  const bool pipe = pipe_env != nullptr && pipe_env[0] == '1';
   if (DQK == 192) launch_bwd_tc<192, 128, true>(p, q, k, v, dout, dev, stream);
   else if (DQK == 128 && pipe) launch_bwd_tc<128, 128, false, true>(p, q, k, v, dout, dev, stream);
   else if (DQK == 128) launch_bwd_tc<128, 128, false>(p, q, k, v, dout, dev, stream);
   else if (pipe) launch_bwd_tc<64, 64, false, true>(p, q, k, v, dout, dev, stream);
   else launch_bwd_tc<64, 64, false>(p, q, k, v, dout, dev, stream);
-  if (Hq != Hkv) {
+  if (Hq != Hkv || p.qsplit > 0) {
     TORCH_CHECK(dk.stride(3) == 1 && dv.stride(3) == 1 && dk.stride(2) % 4 == 0 && dk.stride(1) % 4 == 0 &&
                     dv.stride(2) % 4 == 0 && dv.stride(1) % 4 == 0,
                 "flash_attn_bwd_tc: dk/dv strides must keep 8-byte alignment");

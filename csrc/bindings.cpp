@@ -102,6 +102,10 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
 void wait_flag(const at::Tensor& flag, int64_t expect, int64_t limit_ns);
 void rs_pull(std::vector<int64_t> parts, at::Tensor& out, const c10::optional<at::Tensor>& bias, int64_t rank,
              int64_t flags_ptr, int64_t epoch);
+void gemm_rsp(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+              bool b_mn, std::vector<int64_t> parts, std::vector<int64_t> rdy, int64_t my_rdy, int64_t tpc_stride,
+              at::Tensor& acc, at::Tensor& acc_cnt, at::Tensor& ctrs, int64_t rank, int64_t epoch,
+              const c10::optional<at::Tensor>& trace);
 void gemm_bf16_publish(const at::Tensor& a, const at::Tensor& b, at::Tensor& out, bool b_mn,
                        std::vector<int64_t> flags, int64_t epoch, at::Tensor& ctr);
 // router.cu
@@ -208,6 +212,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("trace") = py::none());
   m.def("rs_pull", &ntb::rs_pull, py::arg("parts"), py::arg("out"), py::arg("bias"), py::arg("rank"),
         py::arg("flags_ptr") = 0, py::arg("epoch") = 0);
+  m.def("gemm_rsp", &ntb::gemm_rsp, "GEMM + reduce-scatter with progressive peer pulls", py::arg("x"),
+        py::arg("w"), py::arg("out"), py::arg("bias"), py::arg("b_mn"), py::arg("parts"), py::arg("rdy"),
+        py::arg("my_rdy"), py::arg("tpc_stride"), py::arg("acc"), py::arg("acc_cnt"), py::arg("ctrs"),
+        py::arg("rank"), py::arg("epoch"), py::arg("trace") = py::none());
   m.def("gemm_bf16_publish", &ntb::gemm_bf16_publish, "tcgen05 bf16 GEMM whose last CTA publishes an epoch",
         py::arg("a"), py::arg("b"), py::arg("out"), py::arg("b_mn"), py::arg("flags"), py::arg("epoch"),
         py::arg("ctr"));

@@ -179,10 +179,13 @@ struct FusedSmem {
 //   bias   optional, indexed from the tile's first column
 //   part0  optional: partial products to add, source s at part0 + s * part_stride
 //          (row stride part_ld), for s in [0, nparts) except `skip` (reduce-scatter epilogue)
+//   facc0  optional: an fp32 sum of partials to add (row stride facc_ld); each value read is
+//          set back to zero, so the buffer is zero at rest again after the tile
 template <int BN>
 __device__ __forceinline__ void warp_store_tile(uint32_t t_row, uint8_t* stage, bf16* dst0, long ld, int ncols,
                                                 const bf16* bias, const bf16* part0 = nullptr, long part_ld = 0,
-                                                long part_stride = 0, int nparts = 0, int skip = -1) {
+                                                long part_stride = 0, int nparts = 0, int skip = -1,
+                                                float* facc0 = nullptr, long facc_ld = 0) {
   const int lane = threadIdx.x & 31;
 #pragma unroll 1
   for (int g = 0; g < BN; g += 64) {
@@ -210,9 +213,17 @@ __device__ __forceinline__ void warp_store_tile(uint32_t t_row, uint8_t* stage, 
       const int c = g + chunk * 8;
       if (c >= ncols) continue;
       uint4 v = *reinterpret_cast<const uint4*>(stage + row * 128 + ((chunk ^ (row & 7)) * 16));
-      if (bias != nullptr || part0 != nullptr) {
+      if (bias != nullptr || part0 != nullptr || facc0 != nullptr) {
         float acc[8] = {bf16_lo(v.x), bf16_hi(v.x), bf16_lo(v.y), bf16_hi(v.y),
                         bf16_lo(v.z), bf16_hi(v.z), bf16_lo(v.w), bf16_hi(v.w)};
+        if (facc0 != nullptr) {
+          float4* f = reinterpret_cast<float4*>(facc0 + row * facc_ld + c);
+          const float4 f0 = f[0], f1 = f[1];
+          acc[0] += f0.x; acc[1] += f0.y; acc[2] += f0.z; acc[3] += f0.w;
+          acc[4] += f1.x; acc[5] += f1.y; acc[6] += f1.z; acc[7] += f1.w;
+          f[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+          f[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
         if (part0 != nullptr) {
           for (int s = 0; s < nparts; ++s) {
             if (s == skip) continue;
@@ -605,6 +616,163 @@ __global__ void __launch_bounds__(224, 1)
   if (threadIdx.x == 0) stamp(p.trace, 7);
 }
 
+// ================================================================== GEMM + RS, progressive pull
+// Same GEMM and tile order as gemm_rs (destination chunks rank-rotated, this rank's own chunk
+// last), but no remote stores: a tile for destination chunk c is stored as bf16 into THIS rank's
+// partial slot (local), and the publisher warp releases it with one 8-byte epoch store into the
+// destination's ready word for (source, tile). Two more warps per CTA pull: they claim
+// (source, tile) items of this rank's own chunk in the order the sources finish them (source
+// rank - s computes this rank's chunk at its step s), wait for the ready word, read the tile over
+// NVLink and add it into a local fp32 accumulator with red.global.add.v4.f32, then count the
+// tile. The own-chunk epilogue (the GEMM's last tiles) waits until every source was added, adds
+// the accumulator to its own bf16-rounded tile (+ bias), writes the output and zeroes the
+// accumulator tile for the next call. The pulls of early sources overlap the rest of the GEMM.
+// Numerics equal the pull reduce-scatter's: each rank's partial is rounded to bf16 once and the
+// partials are summed in fp32 (here in arrival order).
+constexpr int kRspPullWarps = 2;
+
+struct RspParams {
+  int M, N, K;  // M = n * T_local
+  int T_local, n, rank, tpc_stride;
+  unsigned long long epoch;
+  bf16* my_part;                                // this rank's partial slot [n][T_local][N] (local)
+  const bf16* peer_part[kMaxRanks];             // every rank's partial slot (peer mappings)
+  unsigned long long* peer_rdy[kMaxRanks];      // rank r's ready words for source = this rank [tpc]
+  const unsigned long long* my_rdy;             // this rank's ready words [n sources][tpc_stride]
+  float* acc;                                   // local fp32 [T_local, N], zero at rest
+  unsigned int* acc_cnt;                        // local [tpc]: sources added per tile, zero at rest
+  unsigned int* ctr;                            // local: [0] tile counter, [1] pull item counter (zeroed per call)
+  bf16* out;                                    // [T_local, N]
+  long ldo;
+  const bf16* bias;
+  int* status;
+  unsigned long long* trace;
+};
+
+template <int BN>
+__device__ __forceinline__ void rsp_pull_loop(const RspParams& p, int mt_chunk, int tpc) {
+  const int lane = threadIdx.x & 31;
+  const int items = (p.n - 1) * tpc;
+  constexpr int CPR = BN / 8;  // 16-byte chunks per tile row
+  while (true) {
+    int it = 0;
+    if (lane == 0) it = static_cast<int>(atomicAdd(p.ctr + 1, 1u));
+    it = __shfl_sync(0xffffffffu, it, 0);
+    if (it >= items) break;
+    const int s = 1 + it / tpc, idx = it - (it / tpc) * tpc;
+    const int src = (p.rank - s + p.n) % p.n;
+    const unsigned long long* rdy = p.my_rdy + static_cast<long>(src) * p.tpc_stride + idx;
+    int ok = 1;
+    if (lane == 0) ok = spin_until([&] { return ld_acquire_sys_u64(rdy) >= p.epoch; }, p.status, kStatusTimeoutPeer) ? 1 : 0;
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+    if (!ok) break;
+    (void)ld_acquire_sys_u64(rdy);  // every lane acquires before reading the source's tile
+    const int lm = idx % mt_chunk, nb = idx / mt_chunk;
+    const bf16* sp = p.peer_part[src] + (static_cast<long>(p.rank) * p.T_local + lm * 128) * p.N + nb * BN;
+    float* dp = p.acc + static_cast<long>(lm * 128) * p.N + nb * BN;
+#pragma unroll 1
+    for (int base = 0; base < 128 * CPR; base += 32 * 8) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * 32 + lane;
+        const int r = i / CPR, c = (i - r * CPR) * 8;
+        v[u] = *reinterpret_cast<const uint4*>(sp + static_cast<long>(r) * p.N + c);
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int i = base + u * 32 + lane;
+        const int r = i / CPR, c = (i - r * CPR) * 8;
+        float* d = dp + static_cast<long>(r) * p.N + c;
+        red_add_v4(d, bf16_lo(v[u].x), bf16_hi(v[u].x), bf16_lo(v[u].y), bf16_hi(v[u].y));
+        red_add_v4(d + 4, bf16_lo(v[u].z), bf16_hi(v[u].z), bf16_lo(v[u].w), bf16_hi(v[u].w));
+      }
+    }
+    __threadfence();  // this lane's reductions, before the tile's count
+    __syncwarp();
+    if (lane == 0) atomicAdd(p.acc_cnt + idx, 1u);
+  }
+}
+
+template <int BN, bool B_MN>
+__global__ void __launch_bounds__(224 + 32 * kRspPullWarps, 1)
+    gemm_rsp_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ RspParams p) {
+  using Cfg = FusedCfg<BN>;
+  constexpr int BM = Cfg::BM;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  FusedSmem<BN> sm(smem);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int mt_chunk = p.T_local / BM;
+  const int num_n = p.N / BN;
+  const int tpc = mt_chunk * num_n;
+
+  if (threadIdx.x == 0) sm.init(true);
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(sm.tmem_slot, Cfg::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *sm.tmem_slot;
+  if (threadIdx.x == 0) stamp(p.trace, 0);
+
+  if (warp >= 7) {
+    rsp_pull_loop<BN>(p, mt_chunk, tpc);
+  } else {
+    auto tile_of = [&](int t, int& mb, int& nb, int& chunk) {
+      rotated_tile(t, tpc, mt_chunk, p.n, p.rank, 1, mb, nb, chunk);
+    };
+    auto wait_chunk = [&](int) -> bool { return true; };
+    auto pre_epilogue = [&]() {};
+    auto store = [&](uint32_t t_row, int mb, int nb, int chunk) {
+      const int q = warp & 3;
+      const int lm = mb - chunk * mt_chunk;
+      const long m_loc = static_cast<long>(lm) * BM + q * 32;
+      const int n0 = nb * BN;
+      if (chunk != p.rank) {
+        bf16* dst0 = p.my_part + (static_cast<long>(chunk) * p.T_local + m_loc) * p.N + n0;
+        warp_store_tile<BN>(t_row, sm.stage + q * 4096, dst0, p.N, p.N - n0, nullptr);
+      } else {
+        const unsigned int* cnt = p.acc_cnt + nb * mt_chunk + lm;
+        const unsigned int want = static_cast<unsigned int>(p.n - 1);
+        int ok = 1;
+        if (lane == 0) ok = spin_until([&] { return ld_acquire_gpu_u32(cnt) >= want; }, p.status, kStatusTimeoutPeer) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) return;
+        (void)ld_acquire_gpu_u32(cnt);
+        warp_store_tile<BN>(t_row, sm.stage + q * 4096, p.out + m_loc * p.ldo + n0, p.ldo, p.N - n0,
+                            p.bias != nullptr ? p.bias + n0 : nullptr, nullptr, 0, 0, 0, -1,
+                            p.acc + m_loc * p.N + n0, p.N);
+      }
+    };
+    auto published = [&](int mb, int nb, int chunk) {
+      const int idx = nb * mt_chunk + (mb - chunk * mt_chunk);
+      if (chunk != p.rank) {
+        __threadfence_system();  // the tile's local stores, visible to the destination's loads
+        st_relaxed_sys_u64(p.peer_rdy[chunk] + idx, p.epoch);
+      } else {
+        p.acc_cnt[idx] = 0u;  // consumed: zero at rest for the next call
+      }
+    };
+    gemm_phase<BN, B_MN, true>(sm, tmem_base, &tmA, &tmB, p.K, tpc * p.n, p.ctr, p.status, tile_of, wait_chunk,
+                               pre_epilogue, store, published, p.trace, nullptr, p.rank, mt_chunk);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::TMEM_COLS);
+  }
+  if (threadIdx.x == 0) stamp(p.trace, 7);
+}
+
 // ================================================================== host launchers
 // Ordinary launch: no wait in these kernels depends on a CTA that may not be
 // resident yet - copy pieces and GEMM tiles are claimed dynamically by the CTAs
@@ -754,6 +922,78 @@ void gemm_rs(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c1
   }
 }
 
+
+// x: [n*T_local, K]; out: [T_local, N] with N a multiple of the tile width.
+// parts: int64 [n] every rank's partial slot base for this epoch parity ([n][T_local][N] bf16)
+// rdy: int64 [n] address of rank r's ready words for source = this rank; my_rdy: this rank's
+//      ready words [n][tpc_stride] (u64 epochs, monotonic)
+// acc: fp32 [>= T_local * N] zero at rest; acc_cnt: int32 [>= tiles per chunk] zero at rest
+void gemm_rsp(const at::Tensor& x, const at::Tensor& w, at::Tensor& out, const c10::optional<at::Tensor>& bias,
+              bool b_mn, std::vector<int64_t> parts, std::vector<int64_t> rdy, int64_t my_rdy, int64_t tpc_stride,
+              at::Tensor& acc, at::Tensor& acc_cnt, at::Tensor& ctrs, int64_t rank, int64_t epoch,
+              const c10::optional<at::Tensor>& trace) {
+  const int n = static_cast<int>(parts.size());
+  TORCH_CHECK(n >= 1 && n <= kMaxRanks && static_cast<int>(rdy.size()) == n, "gemm_rsp: 1..8 ranks");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_rsp: bf16");
+  TORCH_CHECK(x.is_contiguous() && w.stride(1) == 1 && out.is_contiguous(), "gemm_rsp: layouts");
+  const int64_t M = x.size(0), K = x.size(1);
+  TORCH_CHECK(M % n == 0 && (M / n) % 128 == 0, "gemm_rsp: rows per rank must be a multiple of 128");
+  const int64_t N = b_mn ? w.size(1) : w.size(0);
+  TORCH_CHECK((b_mn ? w.size(0) : w.size(1)) == K, "gemm_rsp: K mismatch");
+  TORCH_CHECK(out.size(0) == M / n && out.size(1) == N, "gemm_rsp: out");
+  TORCH_CHECK(K % 8 == 0, "gemm_rsp: K multiple of 8");
+  const bool wide = N % 256 == 0;
+  TORCH_CHECK(N % 128 == 0, "gemm_rsp: N must be a multiple of 128");
+  const int BN = wide ? 256 : 128;
+  const int64_t tpc = (M / n / 128) * (N / BN);
+  TORCH_CHECK(tpc <= tpc_stride, "gemm_rsp: tiles per chunk exceed the ready-word stride");
+  TORCH_CHECK(acc.scalar_type() == at::kFloat && acc.numel() >= (M / n) * N && acc.is_contiguous(), "gemm_rsp: acc");
+  TORCH_CHECK(acc_cnt.scalar_type() == at::kInt && acc_cnt.numel() >= tpc, "gemm_rsp: acc_cnt");
+  TORCH_CHECK(ctrs.scalar_type() == at::kLong && ctrs.numel() >= 1 && ctrs.is_contiguous(), "gemm_rsp: ctrs");
+  RspParams p{};
+  p.M = static_cast<int>(M);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.T_local = static_cast<int>(M / n);
+  p.n = n;
+  p.rank = static_cast<int>(rank);
+  p.tpc_stride = static_cast<int>(tpc_stride);
+  p.epoch = static_cast<unsigned long long>(epoch);
+  for (int i = 0; i < n; ++i) {
+    TORCH_CHECK(parts[i] % 16 == 0, "gemm_rsp: 16-byte aligned partial slots");
+    p.peer_part[i] = reinterpret_cast<const bf16*>(parts[i]);
+    p.peer_rdy[i] = reinterpret_cast<unsigned long long*>(rdy[i]);
+  }
+  p.my_part = reinterpret_cast<bf16*>(parts[rank]);
+  p.my_rdy = reinterpret_cast<const unsigned long long*>(my_rdy);
+  p.acc = acc.data_ptr<float>();
+  p.acc_cnt = reinterpret_cast<unsigned int*>(acc_cnt.data_ptr());
+  p.ctr = reinterpret_cast<unsigned int*>(ctrs.data_ptr());
+  p.out = reinterpret_cast<bf16*>(out.data_ptr());
+  p.ldo = out.stride(0);
+  p.bias = bias.has_value() ? reinterpret_cast<const bf16*>(bias->data_ptr()) : nullptr;
+  const int dev = x.get_device();
+  p.status = device_status(dev);
+  const int grid = num_sms(dev);
+  if (trace.has_value()) {
+    TORCH_CHECK(trace->numel() >= grid * 8 && trace->scalar_type() == at::kLong, "gemm_rsp: trace [grid, 8] int64");
+    p.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr());
+  }
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
+  TmaSlots& ts = tls_tma_slots();
+  make_tma_2d_bf16(&ts.m[0], x.data_ptr(), K, M, x.stride(0), 64, 128);
+  make_tma_2d_bf16(&ts.m[1], w.data_ptr(), w.size(1), w.size(0), w.stride(0), 64, b_mn ? 64 : BN);
+  NTB_CUDA_CHECK(cudaMemsetAsync(ctrs.data_ptr(), 0, sizeof(int64_t), stream));  // tile and pull-item counters
+  void* args[3] = {&ts.m[0], &ts.m[1], &p};
+  const int threads = 224 + 32 * kRspPullWarps;
+  if (wide) {
+    if (b_mn) fused_launch(gemm_rsp_kernel<256, true>, grid, FusedCfg<256>::SMEM_BYTES, args, stream, threads);
+    else fused_launch(gemm_rsp_kernel<256, false>, grid, FusedCfg<256>::SMEM_BYTES, args, stream, threads);
+  } else {
+    if (b_mn) fused_launch(gemm_rsp_kernel<128, true>, grid, FusedCfg<128>::SMEM_BYTES, args, stream, threads);
+    else fused_launch(gemm_rsp_kernel<128, false>, grid, FusedCfg<128>::SMEM_BYTES, args, stream, threads);
+  }
+}
 
 // ================================================================== pull reduce-scatter
 // out[T_local, N] = sum_r part_r[rank * T_local : (rank + 1) * T_local, :] (+ bias), part_r being rank r's

@@ -50,7 +50,8 @@ def test_flash_fwd_tc_large_scores_rescale_path():
 
 
 @pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 8, 2, False),
-                                               (1, 130, 2, 1, True), (1, 1024, 4, 1, True)])
+                                               (1, 130, 2, 1, True), (1, 1024, 4, 1, True),
+                                               (1, 1024, 2, 2, True), (1, 1024, 2, 2, False)])
 @pytest.mark.parametrize("pipe", ["0", "1"])  # serial chain (default) / pipelined variant
 def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, pipe, monkeypatch):
     from nano_train_b200.ops._ext import check_status, ext
@@ -79,7 +80,7 @@ def test_flash_bwd_tc_matches_reference(B, S, hq, hkv, causal, pipe, monkeypatch
 
 @pytest.mark.parametrize("dqk,dv", [(192, 128), (64, 64)])
 @pytest.mark.parametrize("B,S,hq,hkv,causal", [(1, 512, 4, 4, True), (2, 300, 4, 2, True), (1, 256, 2, 2, False),
-                                               (1, 130, 2, 1, True)])
+                                               (1, 130, 2, 1, True), (1, 1024, 2, 2, True)])
 def test_flash_tc_mla_and_hd64_match_reference(dqk, dv, B, S, hq, hkv, causal, monkeypatch):
     """MLA head dims (q/k 192 = [nope 128 | rope 64], v 128) and head dim 64 on the tcgen05 kernels,
     forward and backward, against fp32 PyTorch; q, k, v are strided views of one buffer."""

@@ -50,12 +50,14 @@ def _worker(rank, world, port, q):
             dist.reduce_scatter_tensor(ref, part)
             errs.append(("rs", _rel(out, ref)))
             errs.append(("rs_pull", _rel(c.gemm_reduce_scatter_pull(xr, wr), ref)))
+            errs.append(("rs_overlap", _rel(c.gemm_reduce_scatter_overlap(xr, wr), ref)))
             wrt = torch.randn(K, 512, device="cuda", dtype=torch.bfloat16, generator=torch.Generator(device="cuda").manual_seed(17 + it))
             out2 = c.gemm_reduce_scatter(xr, wrt, b_mn=True)
             part2 = (xr.float() @ wrt.float()).contiguous()
             ref2 = torch.empty(T_local, 512, device="cuda", dtype=torch.float32)
             dist.reduce_scatter_tensor(ref2, part2)
             errs.append(("rs_bmn", _rel(out2, ref2)))
+            errs.append(("rs_overlap_bmn", _rel(c.gemm_reduce_scatter_overlap(xr, wrt, b_mn=True), ref2)))
         torch.cuda.synchronize()
         check_status(rank)
         bad = c.check_canaries()
