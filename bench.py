@@ -195,7 +195,7 @@ def build_gpt_fp4(args, rank, world, *, device=None, dims=None):
     dp = dist.group.WORLD if world > 1 else None
     trainer = LMTrainer(model, lr=3e-4, weight_decay=0.1, max_grad_norm=1.0,
                         micro_batch_size=CONFIGS["gpt1.3b-fp4-dp"]["batch_per_rank"], dp_group=dp,
-                        strategy="optim" if world > 1 else "no_shard")
+                        strategy="optim" if world > 1 else "no_shard", bucket_mb=256 if world > 1 else None)
     return trainer, layers
 
 
@@ -299,7 +299,8 @@ def build_dsv2lite(args, rank, world, *, device=None, dims=None):
             self.ps = torch.nn.ParameterList(params)
 
     opts = [FlatAdamW(split_decay_groups(_Params(dense), 0.1), lr=3e-4, weight_decay=0.1, max_grad_norm=1.0,
-                      dp_group=dist.group.WORLD if world > 1 else None, strategy="optim" if world > 1 else "no_shard")]
+                      dp_group=dist.group.WORLD if world > 1 else None, strategy="optim" if world > 1 else "no_shard",
+                      bucket_mb=128 if world > 1 else None)]
     if experts:
         opts.append(FlatAdamW(split_decay_groups(_Params(experts), 0.1), lr=3e-4, weight_decay=0.1,
                               max_grad_norm=1.0))
@@ -326,6 +327,8 @@ class _MoETrainer:
         logits = self.model(ids)
         task = ops.cross_entropy(logits.view(-1, logits.shape[-1]), lab.reshape(-1), inplace_grad=True)
         aux = torch.stack([m.last_aux_loss.float().reshape(()) for m in self.moes]).sum() if self.moes else 0.0
+        for o in self.opts:
+            o.overlap_next_backward()  # buckets of the data-parallel ZeRO step reduce under the backward
         (task + 0.01 * aux).backward()
         for o in self.opts:
             o.step()

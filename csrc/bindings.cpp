@@ -141,7 +141,8 @@ void ep_combine_bwd(at::Tensor& dy, const at::Tensor& rows_used, const at::Tenso
 // zero_fused.cu
 void zero_reduce_scatter(std::vector<std::vector<int64_t>> grad_ptrs, const std::vector<at::Tensor>& red,
                          std::vector<int64_t> cls, at::Tensor& stats_acc, std::vector<int64_t> stats_slots,
-                         std::vector<int64_t> flag_stats, const at::Tensor& done, int64_t me, int64_t epoch);
+                         std::vector<int64_t> flag_stats, const at::Tensor& done, int64_t me, int64_t epoch,
+                         bool publish, int64_t grid);
 void zero_adam_allgather(std::vector<std::vector<int64_t>> param_ptrs, const std::vector<at::Tensor>& red,
                          const std::vector<at::Tensor>& master, const std::vector<at::Tensor>& m,
                          const std::vector<at::Tensor>& v, std::vector<double> lr, std::vector<double> wd,
@@ -228,7 +229,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_recv_layout", &ntb::ep_recv_layout);
   m.def("ep_wait", &ntb::ep_wait);
   m.def("router_fwd", &ntb::router_fwd);
-  m.def("zero_reduce_scatter", &ntb::zero_reduce_scatter);
+  m.def("zero_reduce_scatter", &ntb::zero_reduce_scatter, py::arg("grad_ptrs"), py::arg("red"), py::arg("cls"),
+        py::arg("stats_acc"), py::arg("stats_slots"), py::arg("flag_stats"), py::arg("done"), py::arg("me"),
+        py::arg("epoch"), py::arg("publish") = true, py::arg("grid") = 0);
   m.def("zero_adam_allgather", &ntb::zero_adam_allgather);
   m.def("router_bwd", &ntb::router_bwd);
   m.def("ep_signal", &ntb::ep_signal);

@@ -45,7 +45,7 @@ namespace {
 
 using bf16 = __nv_bfloat16;
 constexpr int kZMaxRanks = 8;
-constexpr int kZMaxBufs = 8;
+constexpr int kZMaxBufs = 32;
 
 struct ZeroBuf {
   const float* grad[kZMaxRanks];  // rank r's gradient buffer at this rank's shard offset
@@ -70,6 +70,7 @@ struct ZeroParams {
   const unsigned long long* my_stats_flags;    // local STATS flags [8]
   unsigned int* done;                          // local arrival counter (zero at rest)
   unsigned long long epoch;
+  int publish;  // reduce-scatter: 1 = the last CTA publishes the partial sums (the step's last bucket)
   // update
   float b1, b2, eps, bc1, sqrt_bc2, inv_dp, max_norm;
   float* grad_norm;  // out [1]
@@ -123,7 +124,9 @@ __global__ void __launch_bounds__(256) zero_rs_kernel(const __grid_constant__ Ze
     atomicAdd(p.stats_acc + 1, s1);
     __threadfence_system();
     const unsigned int prev = atomicAdd(p.done, 1u);
-    if (prev == gridDim.x - 1) {
+    if (prev == gridDim.x - 1 && !p.publish) {
+      *p.done = 0u;  // an earlier bucket of the step: the sums stay in stats_acc for the next launch
+    } else if (prev == gridDim.x - 1) {
       __threadfence_system();
       const float a0 = atomicAdd(p.stats_acc, 0.f), a1 = atomicAdd(p.stats_acc + 1, 0.f);
       for (int r = 0; r < p.n; ++r) {
@@ -275,9 +278,13 @@ int zero_grid(int dev) { return num_sms(dev) * 4; }
 }  // namespace
 
 // Reduce-scatter (pull) of this rank's gradient shards + the clipping partials.
+// publish = false: an earlier bucket of a step whose buffers are reduced one launch per bucket
+// (while the backward still runs); its sums of squares stay in stats_acc for the last launch.
+// grid = 0: the default (4 CTAs per SM); a bucket reduced under the backward uses a few CTAs.
 void zero_reduce_scatter(std::vector<std::vector<int64_t>> grad_ptrs, const std::vector<at::Tensor>& red,
                          std::vector<int64_t> cls, at::Tensor& stats_acc, std::vector<int64_t> stats_slots,
-                         std::vector<int64_t> flag_stats, const at::Tensor& done, int64_t me, int64_t epoch) {
+                         std::vector<int64_t> flag_stats, const at::Tensor& done, int64_t me, int64_t epoch,
+                         bool publish, int64_t grid) {
   TORCH_CHECK(!grad_ptrs.empty(), "zero_reduce_scatter: no buffers");
   std::vector<std::vector<int64_t>> param_ptrs(grad_ptrs.size(), std::vector<int64_t>(grad_ptrs[0].size(), 0));
   std::vector<double> z(red.size(), 0.0);
@@ -288,10 +295,11 @@ void zero_reduce_scatter(std::vector<std::vector<int64_t>> grad_ptrs, const std:
   fill8(p.flag_stats, flag_stats);
   p.done = reinterpret_cast<unsigned int*>(done.data_ptr());
   p.epoch = static_cast<unsigned long long>(epoch);
+  p.publish = publish ? 1 : 0;
   const int dev = red[0].get_device();
   p.status = device_status(dev);
   cudaStream_t stream = at::cuda::getCurrentCUDAStream(dev);
-  zero_rs_kernel<<<zero_grid(dev), 256, 0, stream>>>(p);
+  zero_rs_kernel<<<grid > 0 ? static_cast<int>(grid) : zero_grid(dev), 256, 0, stream>>>(p);
   NTB_LAUNCH_CHECK(1);
 }
 

@@ -30,6 +30,7 @@ buffer.
 """
 from __future__ import annotations
 
+import os
 from dataclasses import dataclass
 from typing import Iterable, Optional
 
@@ -110,7 +111,9 @@ class FlatParamBuffer:
         self.grad_data.zero_()
 
 
-def _install_grad_hooks(params: Iterable[torch.nn.Parameter]) -> list:
+def _install_grad_hooks(params: Iterable[torch.nn.Parameter], on_ready=None) -> list:
+    """``.grad`` -> ``main_grad`` after autograd accumulated it; ``on_ready(param)`` then runs, as it does
+    when a native kernel accumulated straight into ``main_grad`` (``param._ntb_grad_ready_hook``)."""
     handles = []
     for p in params:
         if not p.requires_grad:
@@ -120,9 +123,28 @@ def _install_grad_hooks(params: Iterable[torch.nn.Parameter]) -> list:
             if param.grad is not None:
                 param.main_grad.add_(param.grad.to(param.main_grad.dtype))
                 param.grad = None
+                if on_ready is not None:
+                    on_ready(param)
 
         handles.append(p.register_post_accumulate_grad_hook(hook))
+        if on_ready is not None:
+            p._ntb_grad_ready_hook = on_ready
     return handles
+
+
+def _buckets(params: list, bucket_elems: int) -> list[list]:
+    """Consecutive runs of ``params`` in reverse order (the backward produces the last parameters'
+    gradients first), each about ``bucket_elems`` elements; bucket 0 holds the last parameters."""
+    out, cur, n = [], [], 0
+    for p in reversed(params):
+        cur.append(p)
+        n += p.numel()
+        if n >= bucket_elems:
+            out.append(list(reversed(cur)))
+            cur, n = [], 0
+    if cur:
+        out.append(list(reversed(cur)))
+    return out
 
 
 class FlatAdamW:
@@ -131,9 +153,15 @@ class FlatAdamW:
     def __init__(self, param_groups: list[dict], *, lr: float = 1e-3, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.0, dp_group=None, strategy: str = "no_shard",
                  max_grad_norm: Optional[float] = None, grad_norm_group=None, tp_group=None,
-                 sequence_parallel: bool = False, fused_dp: Optional[bool] = None):
+                 sequence_parallel: bool = False, fused_dp: Optional[bool] = None,
+                 bucket_mb: Optional[float] = None):
         """``fused_dp``: run the sharded step as the peer-memory kernels of parallel/zero_fused.py
-        (None: whenever the group allows it; NTB_FUSED_ZERO=0 turns it off)."""
+        (None: whenever the group allows it; NTB_FUSED_ZERO=0 turns it off).
+
+        ``bucket_mb`` (default NTB_ZERO_BUCKET_MB, else one buffer per group): with the peer-memory
+        step, cut every group into buffers of about this many MB of fp32 gradient, last parameters
+        first, so that ``overlap_next_backward`` can reduce-scatter each bucket as soon as the
+        backward has produced it."""
         if strategy not in ("no_shard", "optim", "optim_grads"):
             raise ValueError(f"unknown sharding strategy {strategy}")
         self.lr = lr
@@ -159,17 +187,33 @@ class FlatAdamW:
         groups = [(i, g, [p for p in g["params"] if p.requires_grad]) for i, g in enumerate(param_groups)]
         groups = [(i, g, ps) for i, g, ps in groups if ps]
         self._zsym = None
+        fused = False
         if self.strategy != "no_shard" and fused_dp is not False and groups:
-            from .zero_fused import ZeroSymm, fused_zero_available
+            from .zero_fused import fused_zero_available
 
             dts = [p.dtype for _, _, ps in groups for p in ps]
-            if fused_zero_available(dp_group, dts, grad_norm_group=self.grad_norm_group) \
-                    and all(p.is_cuda for _, _, ps in groups for p in ps):
-                self._zsym = ZeroSymm(dp_group, [FlatParamBuffer.padded_numel(ps, dp_for_pad) for _, _, ps in groups],
-                                      groups[0][2][0].device)
+            fused = fused_zero_available(dp_group, dts, grad_norm_group=self.grad_norm_group) \
+                and all(p.is_cuda for _, _, ps in groups for p in ps)
+        if bucket_mb is None:
+            bucket_mb = float(os.environ.get("NTB_ZERO_BUCKET_MB", "0") or 0)
+        if fused and bucket_mb > 0:
+            from .zero_fused import MAX_BUFFERS
+
+            total = sum(p.numel() for _, _, ps in groups for p in ps)
+            elems = max(int(bucket_mb * 2 ** 20 / 4), -(-total // (MAX_BUFFERS - len(groups))))
+            pos = {id(p): k for k, p in enumerate(p for _, _, ps in groups for p in ps)}
+            groups = [(i, g, b) for i, g, ps in groups for b in _buckets(ps, elems)]
+            # bucket order = expected readiness order: the backward finishes the last layers first
+            groups.sort(key=lambda t: -max(pos[id(p)] for p in t[2]))
+        if fused:
+            from .zero_fused import ZeroSymm
+
+            self._zsym = ZeroSymm(dp_group, [FlatParamBuffer.padded_numel(ps, dp_for_pad) for _, _, ps in groups],
+                                  groups[0][2][0].device)
         for bi, (i, g, params) in enumerate(groups):
             storage = self._zsym.views(bi) if self._zsym is not None else None
-            buf = FlatParamBuffer(params, dp_size=dp_for_pad, name=g.get("name", f"group{i}"), storage=storage)
+            name = g.get("name", f"group{i}") + (f".b{bi}" if fused and bucket_mb > 0 else "")
+            buf = FlatParamBuffer(params, dp_size=dp_for_pad, name=name, storage=storage)
             self.buffers.append(buf)
             self.group_wd.append(g.get("weight_decay", weight_decay))
             self.group_replicated.append(bool(g.get("tp_replicated", False)))
@@ -182,7 +226,14 @@ class FlatAdamW:
             master = buf.param_data[lo:hi].float().clone()
             self.shards.append(dict(lo=lo, hi=hi, master=master, exp_avg=torch.zeros_like(master),
                                     exp_avg_sq=torch.zeros_like(master)))
-        self._hooks = _install_grad_hooks(all_params)
+        self._hooks = _install_grad_hooks(all_params, self._on_grad_ready if self._zsym is not None else None)
+        # Overlap of the peer-memory reduce-scatter with the backward (overlap_next_backward).
+        self._bucket_of = {id(p): bi for bi, buf in enumerate(self.buffers) for p in buf.params}
+        self._armed = False
+        self._calls: dict = {}        # notifications per parameter in the armed backward
+        self._expected: Optional[dict] = None  # the same, learned from the previous armed backward
+        self._bucket_done = [0] * len(self.buffers)
+        self._side: Optional[torch.cuda.Stream] = None
         # torch-optimizer-style groups (one per buffer): schedulers set "lr" here.
         self.param_groups = [dict(params=buf.params, lr=float(lr), weight_decay=float(wd), betas=tuple(betas),
                                   eps=float(eps), name=buf.name) for buf, wd in zip(self.buffers, self.group_wd)]
@@ -191,6 +242,60 @@ class FlatAdamW:
         self._stats_rep = torch.zeros(2, dtype=torch.float32, device=dev)
         self._scale = torch.ones(1, dtype=torch.float32, device=dev)
         self.last_grad_norm: Optional[torch.Tensor] = None
+
+    # ------------------------------------------------------------------ overlap with the backward
+    def overlap_next_backward(self) -> bool:
+        """Reduce-scatter each bucket while the next backward still runs (the last micro-batch's
+        backward before ``step``). A bucket is launched - in bucket order, on a side stream, after
+        the gradients enqueued so far - once each of its parameters has been notified as many times
+        as in the previous armed backward (so the first armed step only learns those counts and
+        reduces everything in ``step``, as without overlap). Returns whether overlap is possible
+        (the peer-memory step is in use)."""
+        if self._zsym is None or os.environ.get("NTB_ZERO_OVERLAP", "0") != "1":
+            return False
+        self._armed = True
+        self._calls = {}
+        self._bucket_done = [0] * len(self.buffers)
+        return True
+
+    def _on_grad_ready(self, param) -> None:
+        if not self._armed:
+            return
+        key = id(param)
+        c = self._calls.get(key, 0) + 1
+        self._calls[key] = c
+        if self._expected is None or c != self._expected.get(key, -1):
+            return
+        bi = self._bucket_of.get(key)
+        if bi is None:
+            return
+        self._bucket_done[bi] += 1
+        # launch every complete bucket from the next one on, in order
+        k = self._zsym.next_bucket
+        while k < len(self.buffers) and self._bucket_done[k] == len(self.buffers[k].params):
+            k += 1
+        if k > self._zsym.next_bucket:
+            if self._side is None:
+                self._side = torch.cuda.Stream(device=self.buffers[0].param_data.device)
+            self._side.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(self._side):
+                self._zsym.reduce_through(k - 1, self.shards, self.group_replicated, grid=32)
+
+    def _finish_overlap(self) -> None:
+        """Before the step: the side stream's reductions precede the update; learn or check counts."""
+        if not self._armed:
+            return
+        self._armed = False
+        if self._side is not None:
+            torch.cuda.current_stream().wait_stream(self._side)
+        if self._expected is None:
+            self._expected = dict(self._calls)
+            return
+        early = [k for k, c in self._calls.items() if c > self._expected.get(k, c)]
+        if early:
+            # a bucket may have been reduced before all of its gradient arrived
+            raise RuntimeError(f"{len(early)} parameters received more gradient contributions than in the "
+                               "previous overlapped backward; overlap_next_backward needs the same graph every step")
 
     # ------------------------------------------------------------------ API
     def zero_grad(self, set_to_none: bool = True) -> None:
@@ -226,6 +331,7 @@ class FlatAdamW:
     def step(self, lr: Optional[float] = None) -> None:
         """One update. ``lr`` overrides the groups' learning rates for this step."""
         self.step_count += 1
+        self._finish_overlap()
         if self._zsym is not None:
             for buf, rep in zip(self.buffers, self.group_replicated):
                 if rep and self.sequence_parallel:

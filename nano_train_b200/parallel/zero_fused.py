@@ -12,6 +12,11 @@ Reference parity: src/distributed/zero.py:392-499 (reduce-scatter or
 all-reduce, AdamW on the shard, all-gather, per parameter); here one pass per
 step over all buffers.
 
+The reduce-scatter runs one launch per buffer in index order, so the flat optimizer can cut its
+parameters into buckets (buffers, last layers first) and reduce each bucket while the backward
+still produces the earlier layers' gradients (``FlatAdamW.overlap_next_backward``); the clipping
+partials accumulate over the buckets and the last one publishes them.
+
 Layout of the region:
     [0, 256)        flags u64 [3 kinds][8 source ranks]: gradients ready, partial norm, parameters written
     [256, 320)      partial sums of squares fp32 [8 source ranks][2]
@@ -31,6 +36,7 @@ from .region import RegionLayout
 
 GRADS, STATS, PARAMS = range(3)
 MAX_RANKS = 8
+MAX_BUFFERS = 32  # buffers per launch of the step kernels (csrc/zero_fused.cu, kZMaxBufs)
 
 
 def _align(x: int, a: int = 256) -> int:
@@ -91,6 +97,8 @@ class ZeroSymm:
         self.grad_norm = torch.zeros(1, dtype=torch.float32, device=device)
         self.scale = torch.ones(1, dtype=torch.float32, device=device)
         self.epoch = 0
+        self._open = False  # a step's first bucket was reduced and its adam launch has not run yet
+        self._next = 0
         self.closed = False
         lay.fill(C, self.local, device.index)
         dist.barrier(group=dp_group)
@@ -105,30 +113,60 @@ class ZeroSymm:
     def _flags(self, kind: int):
         return [p + (kind * MAX_RANKS + self.rank) * 8 for p in self.ptrs]
 
+    def _open_step(self) -> int:
+        """Epoch of the step in progress (a step opens with its first bucket reduction)."""
+        if not self._open:
+            self.epoch += 1
+            self._open = True
+            self._next = 0
+        return self.epoch
+
+    @property
+    def next_bucket(self) -> int:
+        """Index of the next buffer to reduce in the step in progress (0 when none is open)."""
+        return self._next if self._open else 0
+
+    @torch.no_grad()
+    def reduce_through(self, k: int, shards: list[dict], classes, *, grid: int = 0) -> None:
+        """Reduce-scatter buffers next_bucket..k in index order, each once every rank has signalled it
+        (gradients-ready flag = epoch * nbuf + i + 1, monotonic over buckets and steps). Runs on the
+        current stream; the last buffer of the step publishes the clipping partials."""
+        C, n, me = self._C, self.n, self.rank
+        e = self._open_step()
+        dev = self.device.index
+        nb = len(self.numels)
+        for i in range(self._next, min(k, nb - 1) + 1):
+            value = e * nb + i + 1
+            C.ep_signal(self._flags(GRADS), value, dev)
+            C.ep_wait(self.local + GRADS * MAX_RANKS * 8, n, value, dev)
+            lo, hi = shards[i]["lo"], shards[i]["hi"]
+            C.zero_reduce_scatter([[p + self.goff[i] + lo * 4 for p in self.ptrs]], [self.views(i)[1][lo:hi]],
+                                  [int(classes[i])], self.stats_acc, [p + 256 + me * 8 for p in self.ptrs],
+                                  self._flags(STATS), self.done, me, e, publish=(i == nb - 1), grid=grid)
+            self._next = i + 1
+
     @torch.no_grad()
     def step(self, shards: list[dict], lrs, wds, classes, *, step: int, betas, eps: float, inv_dp: float,
              max_norm: float) -> None:
-        """One optimizer step over every buffer; ``shards[i]`` holds lo/hi/master/exp_avg/exp_avg_sq."""
+        """One optimizer step over every buffer; ``shards[i]`` holds lo/hi/master/exp_avg/exp_avg_sq.
+        Buffers already reduced during the backward (``reduce_through``) are not reduced again."""
         C, n, me = self._C, self.n, self.rank
-        self.epoch += 1
-        e = self.epoch
+        e = self._open_step()
         dev = self.device.index
-        C.ep_signal(self._flags(GRADS), e, dev)
-        C.ep_wait(self.local + GRADS * MAX_RANKS * 8, n, e, dev)
-        red, grad_ptrs, param_ptrs = [], [], []
+        self.reduce_through(len(self.numels) - 1, shards, classes)
+        red, param_ptrs = [], []
         for i, sh in enumerate(shards):
             lo, hi = sh["lo"], sh["hi"]
             red.append(self.views(i)[1][lo:hi])
-            grad_ptrs.append([p + self.goff[i] + lo * 4 for p in self.ptrs])
             param_ptrs.append([p + self.poff[i] + lo * 2 for p in self.ptrs])
-        C.zero_reduce_scatter(grad_ptrs, red, [int(c) for c in classes], self.stats_acc,
-                              [p + 256 + me * 8 for p in self.ptrs], self._flags(STATS), self.done, me, e)
         C.zero_adam_allgather(param_ptrs, red, [s["master"] for s in shards], [s["exp_avg"] for s in shards],
                               [s["exp_avg_sq"] for s in shards], [float(x) for x in lrs], [float(x) for x in wds],
                               self.local + 256, self.local + STATS * MAX_RANKS * 8, self._flags(PARAMS), self.done,
                               me, e, float(betas[0]), float(betas[1]), float(eps), int(step), float(inv_dp),
                               float(max_norm), self.grad_norm, self.scale)
         C.ep_wait(self.local + PARAMS * MAX_RANKS * 8, n, e, dev)
+        self._open = False
+        self._next = 0
 
     def check_canaries(self) -> list[str]:
         """Sections of this rank's region whose trailing canary was overwritten (synchronises)."""

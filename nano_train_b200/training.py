@@ -23,7 +23,8 @@ class LMTrainer:
     def __init__(self, model: torch.nn.Module, *, lr: float = 3e-4, weight_decay: float = 0.1,
                  betas=(0.9, 0.95), eps: float = 1e-8, max_grad_norm: Optional[float] = 1.0,
                  micro_batch_size: int = 1, dp_group=None, strategy: str = "no_shard", grad_norm_group=None,
-                 device: Optional[torch.device] = None):
+                 device: Optional[torch.device] = None, bucket_mb: Optional[float] = None,
+                 overlap_grad_reduce: bool = True):
         self.model = model
         self.micro_batch_size = micro_batch_size
         self.device = device or next(model.parameters()).device
@@ -34,7 +35,11 @@ class LMTrainer:
                                    strategy=strategy, max_grad_norm=max_grad_norm,
                                    grad_norm_group=grad_norm_group if grad_norm_group is not None else tp_group,
                                    tp_group=tp_group,
-                                   sequence_parallel=bool(getattr(model, "sequence_parallel", False)))
+                                   sequence_parallel=bool(getattr(model, "sequence_parallel", False)),
+                                   bucket_mb=bucket_mb)
+        # With the peer-memory ZeRO step, the last micro-batch's backward reduce-scatters every
+        # gradient bucket as soon as it is complete (FlatAdamW.overlap_next_backward).
+        self.overlap_grad_reduce = overlap_grad_reduce
 
     def train_step(self, input_ids: torch.Tensor, labels: torch.Tensor, lr: Optional[float] = None) -> torch.Tensor:
         with nvtx_range("h2d"):
@@ -48,6 +53,8 @@ class LMTrainer:
         for i in range(n_mb):
             with nvtx_range(f"forward mb{i}"):
                 loss = self.model.forward_loss(ids[i * mb:(i + 1) * mb], lab[i * mb:(i + 1) * mb])
+            if i == n_mb - 1 and self.overlap_grad_reduce:
+                self.optimizer.overlap_next_backward()
             with nvtx_range(f"backward mb{i}"):
                 (loss / n_mb).backward()
             total += loss.detach().float()

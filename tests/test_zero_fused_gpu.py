@@ -36,10 +36,15 @@ def _worker(rank, world, port, q):
         from nano_train_b200.parallel.flat_optimizer import FlatAdamW, split_decay_groups
 
         res = []
-        for strategy, clip in (("optim_grads", 1.0), ("optim", None)):
+        os.environ["NTB_ZERO_OVERLAP"] = "1"
+        # (strategy, clipping, bucket MB): the last case cuts the model into ~10 buckets and reduces
+        # them under the backward (overlap_next_backward; the first step learns the hook counts)
+        for strategy, clip, bucket in (("optim_grads", 1.0, None), ("optim", None, None), ("optim_grads", 1.0, 0.05)):
             ma, mb = _model(0), _model(0)
             oa = FlatAdamW(split_decay_groups(ma, 0.1), lr=3e-3, weight_decay=0.1, dp_group=dist.group.WORLD,
-                           strategy=strategy, max_grad_norm=clip, fused_dp=True)
+                           strategy=strategy, max_grad_norm=clip, fused_dp=True, bucket_mb=bucket)
+            if bucket:
+                assert len(oa.buffers) > 4, len(oa.buffers)
             ob = FlatAdamW(split_decay_groups(mb, 0.1), lr=3e-3, weight_decay=0.1, dp_group=dist.group.WORLD,
                            strategy=strategy, max_grad_norm=clip, fused_dp=False)
             assert oa.fused_dp and not ob.fused_dp
@@ -48,7 +53,10 @@ def _worker(rank, world, port, q):
                 x = torch.randn(64, 256, device="cuda", dtype=torch.bfloat16, generator=g)
                 for m, o in ((ma, oa), (mb, ob)):
                     o.zero_grad()
-                    (m(x).float().pow(2).mean() * 10).backward()
+                    loss = m(x).float().pow(2).mean() * 10
+                    if bucket:
+                        o.overlap_next_backward()
+                    loss.backward()
                     o.step()
                 pa = torch.cat([p.detach().float().flatten() for p in ma.parameters()])
                 pb = torch.cat([p.detach().float().flatten() for p in mb.parameters()])
