@@ -26,7 +26,7 @@ import json
 import logging
 import os
 from dataclasses import asdict, dataclass
-from typing import Dict, Literal, Set
+from typing import Dict, Literal, Optional, Set
 
 import torch
 import torch.distributed as dist
@@ -102,6 +102,16 @@ def _resolve_dtype_alias(alias: str) -> torch.dtype:
     return m[alias]
 
 
+def _copy_pieces(dsts: list, srcs: list) -> None:
+    """dst_i <- src_i for lists of 1-D slices; same-dtype pairs go through one batched copy."""
+    same = [(d, s) for d, s in zip(dsts, srcs) if d.dtype == s.dtype]
+    cast = [(d, s) for d, s in zip(dsts, srcs) if d.dtype != s.dtype]
+    if same:
+        torch._foreach_copy_([d for d, _ in same], [s for _, s in same])
+    for d, s in cast:
+        d.copy_(s)
+
+
 def _compute_shard(numel: int, rank: int, size: int) -> tuple[int, int, int]:
     chunk = -(-numel // size)
     start = min(rank * chunk, numel)
@@ -114,9 +124,12 @@ class _Domain:
 
     Rank-major layout of size g * S, S = sum_p chunk_p: the block of rank r
     holds [p0 chunk r | p1 chunk r | ...]; slot s of parameter p inside a block
-    starts at off_p. ``perm[i]`` is the natural flat index (into the padded
-    concatenation of all parameters) of rank-major element i, or -1 for
-    padding past the end of a parameter.
+    starts at off_p, and padding past the end of a parameter is zero. Moving
+    between this layout and the parameters (or their gradients) is one
+    contiguous slice copy per (parameter, rank) - batched into a few launches -
+    with no index tensors and no natural-order copy of the whole domain, so the
+    only domain-sized temporary of a step is the rank-major gradient buffer
+    (the parameter all-gather lands in the same storage).
     """
 
     def __init__(self, items, group, device, dtypes):
@@ -136,23 +149,21 @@ class _Domain:
             self.nat_offs.append(n)
             n += p.numel()
         self.N = n
-        perm = torch.full((self.g * S,), -1, dtype=torch.int64)
-        for (name, p, m), off, noff in zip(items, self.offs, self.nat_offs):
+        # (item, rank, start, end): the slice [start, end) of item's flat parameter that lives in
+        # rank `rank`'s block at offset offs[item]
+        self.pieces = []
+        for i, (_, _, m) in enumerate(items):
             for rr in range(self.g):
-                s, e, _ = _compute_shard(m.numel, rr, self.g)
-                if e > s:
-                    perm[rr * S + off: rr * S + off + (e - s)] = torch.arange(noff + s, noff + e)
-        self.valid = (perm >= 0).to(device)
-        self.perm = perm.clamp_min(0).to(device)
-        self.inv_index = perm[perm >= 0].to(device)           # natural positions
-        self.inv_src = torch.nonzero(perm >= 0).flatten().to(device)  # rank-major positions
+                s_, e_, _ = _compute_shard(m.numel, rr, self.g)
+                if e_ > s_:
+                    self.pieces.append((i, rr, s_, e_))
         mp_dt, ea_dt, es_dt = dtypes
         self.master = torch.zeros(S, dtype=mp_dt, device=device)
         self.exp_avg = torch.zeros(S, dtype=ea_dt, device=device)
         self.exp_avg_sq = torch.zeros(S, dtype=es_dt, device=device)
         with torch.no_grad():
-            nat = self.natural_params(device, mp_dt)
-            self.master.copy_(self.to_rank_major(nat)[self.r * S:(self.r + 1) * S])
+            self.master.copy_(self.gather_rank_major([p.detach() for _, p, _ in items], mp_dt, device)
+                              [self.r * S:(self.r + 1) * S])
 
     def natural_params(self, device, dtype) -> torch.Tensor:
         return torch.cat([p.detach().reshape(-1).to(device=device, dtype=dtype) for _, p, _ in self.items]) \
@@ -168,12 +179,44 @@ class _Domain:
                          else g.detach().reshape(-1).to(device=device, dtype=dtype))
         return torch.cat(parts) if parts else torch.zeros(0, dtype=dtype, device=device)
 
+    def gather_rank_major(self, tensors: list, dtype, device, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Rank-major buffer [g * S] of per-item tensors (parameters or gradients; None reads as zero)."""
+        if out is None:
+            out = torch.zeros(self.g * self.S, dtype=dtype, device=device)
+        else:
+            out.zero_()
+        dsts, srcs = [], []
+        for i, rr, s_, e_ in self.pieces:
+            t = tensors[i]
+            if t is None:
+                continue
+            base = rr * self.S + self.offs[i]
+            dsts.append(out[base: base + (e_ - s_)])
+            srcs.append(t.reshape(-1)[s_:e_])
+        _copy_pieces(dsts, srcs)
+        return out
+
+    def scatter_to(self, rank_major: torch.Tensor, tensors: list) -> None:
+        """Writes every item's slices from a rank-major buffer back into ``tensors`` (cast on copy)."""
+        dts = {t.dtype for t in tensors}
+        if len(dts) == 1 and rank_major.dtype not in dts:
+            rank_major = rank_major.to(next(iter(dts)))  # one cast, then batched same-dtype copies
+        dsts, srcs = [], []
+        for i, rr, s_, e_ in self.pieces:
+            base = rr * self.S + self.offs[i]
+            dsts.append(tensors[i].view(-1)[s_:e_])
+            srcs.append(rank_major[base: base + (e_ - s_)])
+        _copy_pieces(dsts, srcs)
+
     def to_rank_major(self, nat: torch.Tensor) -> torch.Tensor:
-        return torch.where(self.valid, nat[self.perm], torch.zeros((), dtype=nat.dtype, device=nat.device))
+        """Rank-major buffer of a natural-order concatenation (``nat_offs``) of the items."""
+        return self.gather_rank_major([nat[o: o + p.numel()] for o, (_, p, _) in zip(self.nat_offs, self.items)],
+                                      nat.dtype, nat.device)
 
     def scatter_natural(self, rank_major: torch.Tensor) -> torch.Tensor:
+        """Natural-order concatenation of the items from a rank-major buffer."""
         out = torch.empty(self.N, dtype=rank_major.dtype, device=rank_major.device)
-        out[self.inv_index] = rank_major[self.inv_src]
+        self.scatter_to(rank_major, [out[o: o + p.numel()] for o, (_, p, _) in zip(self.nat_offs, self.items)])
         return out
 
     def local_view(self, buf: torch.Tensor, idx: int) -> torch.Tensor:
@@ -297,8 +340,12 @@ class MegatronZeroOptimizer:
         self._global_step += 1
         for d in self._domains:
             dev = d.master.device
-            nat = d.natural_grads(dev, self._main_grads_dtype)
-            shard_g = self._reduce(d, d.to_rank_major(nat))
+            grads = []
+            for _, p, _ in d.items:
+                g_ = getattr(p, "main_grad", None)
+                grads.append(g_ if g_ is not None else p.grad)
+            rm = d.gather_rank_major(grads, self._main_grads_dtype, dev)
+            shard_g = self._reduce(d, rm)
             step = None
             for _, p, _ in d.items:
                 self.state[p]["step"] = int(self.state[p]["step"]) + 1
@@ -313,14 +360,16 @@ class MegatronZeroOptimizer:
                 d.master.copy_(w)
                 d.exp_avg.copy_(m)
                 d.exp_avg_sq.copy_(v)
-            full = torch.empty(d.g * d.S, dtype=d.master.dtype, device=dev)
+            # the rank-major gradient buffer is free again: the parameter all-gather lands in it
+            full = rm if (rm.dtype == d.master.dtype and rm.numel() == d.g * d.S) else \
+                torch.empty(d.g * d.S, dtype=d.master.dtype, device=dev)
+            shard_copy = d.master.contiguous()
             if d.g > 1:
-                dist.all_gather_into_tensor(full, d.master.contiguous(), group=d.group)
+                dist.all_gather_into_tensor(full, shard_copy, group=d.group)
             else:
-                full.copy_(d.master)
-            nat_p = d.scatter_natural(full)
-            for (_, p, _), noff in zip(d.items, d.nat_offs):
-                p.data.copy_(nat_p[noff: noff + p.numel()].view_as(p).to(p.dtype))
+                full.copy_(shard_copy)
+            d.scatter_to(full, [p.data for _, p, _ in d.items])
+            del rm, full
         if self.config.debug and self._debug_steps < self.config.debug_max_steps:
             self._debug_steps += 1
             LOGGER.info("[ZeRO Debug][rank=%d] step=%d strategy=%s rs_fallback=%s", _dist_rank(), self._global_step,

@@ -275,6 +275,33 @@ class GatedMLP(nn.Module):
         return self.mlp(x)
 
 
+class _RopeColumnsInPlace(torch.autograd.Function):
+    """RoPE of columns [off, off + R) of every head of x [B, S, h, D], in place (x is a projection's
+    output that nothing else keeps); the backward rotates the incoming gradient in place. The q of MLA
+    thus stays one [B, S, h, nope | rope] tensor for the attention kernel, with no concatenation in the
+    forward and none in the backward."""
+
+    @staticmethod
+    def forward(ctx, x, off, R, theta, mode):
+        from ..ops.rope import rope_rows_
+
+        B, S, h, D = x.shape
+        rope_rows_(x.view(B * S, h, D), off, R, S, theta, mode, False)
+        ctx.mark_dirty(x)
+        ctx.meta = (off, R, theta, mode)
+        return x
+
+    @staticmethod
+    def backward(ctx, dy):
+        from ..ops.rope import rope_rows_
+
+        off, R, theta, mode = ctx.meta
+        dy = dy.contiguous()
+        B, S, h, D = dy.shape
+        rope_rows_(dy.view(B * S, h, D), off, R, S, theta, mode, True)
+        return dy, None, None, None, None
+
+
 class MultiHeadLatentAttention(nn.Module):
     def __init__(self, config: DeepSeekModelConfig, parallel_context: Optional[DeepSeekParallelContext] = None, *,
                  module_prefix: str):
@@ -349,17 +376,18 @@ class MultiHeadLatentAttention(nn.Module):
         B, S, _ = x.shape
         h = self.local_num_heads
         q, k_nope, k_rope, v = self._qkv(x)
-        pos = torch.arange(S, device=x.device)
-        q_nope, q_rope = torch.split(q, [self.qk_nope_head_dim, self.qk_rope_head_dim], dim=-1)
         if x.is_cuda and attention_mask is None:
-            q_rope = ops.apply_rope(q_rope, self.rope_theta, "deepseek")
+            qf = q if q.is_contiguous() else q.contiguous()
+            qf = _RopeColumnsInPlace.apply(qf, self.qk_nope_head_dim, self.qk_rope_head_dim, float(self.rope_theta),
+                                           "deepseek")
             k_rope = ops.apply_rope(k_rope.unsqueeze(2), self.rope_theta, "deepseek")
-            qf = torch.cat([q_nope, q_rope], dim=-1)
             kf = torch.cat([k_nope, k_rope.expand(B, S, h, self.qk_rope_head_dim)], dim=-1)
             o = flash_attention(qf, kf, v, causal=True, softmax_scale=self.scale)
             o = self.dropout(o)
             return self.out_proj(o.reshape(B, S, h * self.v_head_dim))
         # Reference math path (CPU / explicit masks): materialised scores, fp32 softmax.
+        pos = torch.arange(S, device=x.device)
+        q_nope, q_rope = torch.split(q, [self.qk_nope_head_dim, self.qk_rope_head_dim], dim=-1)
         q_rope = rope_reference(q_rope, pos, self.rope_theta, "deepseek")
         k_rope = rope_reference(k_rope.unsqueeze(2), pos, self.rope_theta, "deepseek")
         qf = torch.cat([q_nope, q_rope], dim=-1).permute(0, 2, 1, 3)

@@ -115,3 +115,40 @@ def test_flash_tc_mla_and_hd64_match_reference(dqk, dv, B, S, hq, hkv, causal, m
         check_status(0)
         for name, g, r in (("dq", dq3, qf.grad), ("dk", dk3, kf.grad), ("dv", dv3, vf.grad)):
             assert _rel(g, r) < 2e-2, (name, "pipelined", _rel(g, r))
+
+
+def test_mla_module_fast_path_matches_reference_path():
+    """MultiHeadLatentAttention on the GPU: the fast path (q rotated in place, tcgen05 flash attention)
+    against the module's own reference path (materialised causal scores, fp32 softmax), forward and
+    backward (input and parameter gradients)."""
+    import argparse
+
+    from nano_train_b200.models.deepseek import DeepSeekModelConfig, MultiHeadLatentAttention
+    from nano_train_b200.precision.mixed_precision import build_module_precision_resolver, resolve_precision_config
+
+    dev = torch.device("cuda", 0)
+    resolver = build_module_precision_resolver(resolve_precision_config(argparse.Namespace(), dev))
+    cfg = DeepSeekModelConfig(precision_resolver=resolver, param_dtype=torch.bfloat16, param_device=dev,
+                              vocab_size=97, hidden_size=256, num_hidden_layers=1, num_attention_heads=2,
+                              num_key_value_heads=2, intermediate_size=256, q_lora_rank=64, kv_lora_rank=64,
+                              qk_nope_head_dim=128, qk_rope_head_dim=64, v_head_dim=128, moe_intermediate_size=64,
+                              n_routed_experts=4, num_experts_per_tok=2, n_group=1, topk_group=1,
+                              max_position_embeddings=512, first_k_dense_replace=1)
+    torch.manual_seed(0)
+    attn = MultiHeadLatentAttention(cfg, module_prefix="layers.0.attn")
+    x = torch.randn(2, 256, 256, device=dev, dtype=torch.bfloat16)
+    mask = torch.full((256, 256), float("-inf"), device=dev).triu(1)
+    outs, grads = [], []
+    for m in (None, mask):
+        attn.zero_grad(set_to_none=True)
+        xi = x.clone().requires_grad_(True)
+        y = attn(xi, m)
+        g = torch.Generator(device=dev).manual_seed(1)
+        (y.float() * torch.randn(y.shape, device=dev, generator=g)).sum().backward()
+        outs.append((y.detach(), xi.grad.detach()))
+        grads.append({n: (p.main_grad if getattr(p, "main_grad", None) is not None else p.grad).detach().clone()
+                      for n, p in attn.named_parameters()})
+    assert _rel(outs[0][0], outs[1][0]) < 2e-2, _rel(outs[0][0], outs[1][0])
+    assert _rel(outs[0][1], outs[1][1]) < 3e-2, _rel(outs[0][1], outs[1][1])
+    for n in grads[0]:
+        assert _rel(grads[0][n], grads[1][n]) < 3e-2, (n, _rel(grads[0][n], grads[1][n]))

@@ -37,14 +37,14 @@ def _worker(rank, world, port, q):
 
         res = []
         os.environ["NTB_ZERO_OVERLAP"] = "1"
-        # (strategy, clipping, bucket MB): the last case cuts the model into ~10 buckets and reduces
+        # (strategy, clipping, bucket MB): the last case cuts the model into 3 buckets and reduces
         # them under the backward (overlap_next_backward; the first step learns the hook counts)
         for strategy, clip, bucket in (("optim_grads", 1.0, None), ("optim", None, None), ("optim_grads", 1.0, 0.05)):
             ma, mb = _model(0), _model(0)
             oa = FlatAdamW(split_decay_groups(ma, 0.1), lr=3e-3, weight_decay=0.1, dp_group=dist.group.WORLD,
                            strategy=strategy, max_grad_norm=clip, fused_dp=True, bucket_mb=bucket)
             if bucket:
-                assert len(oa.buffers) > 4, len(oa.buffers)
+                assert len(oa.buffers) >= 3, len(oa.buffers)  # buckets hold whole parameters
             ob = FlatAdamW(split_decay_groups(mb, 0.1), lr=3e-3, weight_decay=0.1, dp_group=dist.group.WORLD,
                            strategy=strategy, max_grad_norm=clip, fused_dp=False)
             assert oa.fused_dp and not ob.fused_dp
