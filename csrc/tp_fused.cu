@@ -13,9 +13,10 @@
 // depends on a CTA that has not started.
 //
 // ag_gemm: tiles run chunk by chunk in rank-rotated order, own chunk first
-// (its A operand is read straight from the local shard). The epilogue warps
-// are idle until the first accumulator is ready, so before their first tile
-// they gather X: they claim 16 KB pieces from a second atomic counter - the
+// (its A operand is read straight from the local shard). Two copy warps per
+// CTA, next to the GEMM's six, gather X while the GEMM runs (the epilogue
+// warps stay free to drain accumulators): they claim 16 KB pieces from a
+// second atomic counter - the
 // own shard first (local -> gathered buffer + this rank's symmetric slot),
 // then every peer's shard from its symmetric slot (peer loads over NVLink ->
 // gathered buffer). The warp that completes the own shard publishes the epoch
@@ -416,8 +417,10 @@ __device__ __forceinline__ void gemm_phase(FusedSmem<BN>& sm, uint32_t tmem_base
 }
 
 // ================================================================== AG + GEMM
+constexpr int kAgCopyWarps = 2;
+
 template <int BN, bool B_MN>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(192 + 32 * kAgCopyWarps, 1)
     ag_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmA_local, AgParams p) {
   using Cfg = FusedCfg<BN>;
@@ -521,7 +524,7 @@ __global__ void __launch_bounds__(192, 1)
         }
       }
     }
-    if (warp == 2 && lane == 0) stamp(p.trace, 1);
+    if (warp == 6 && lane == 0) stamp(p.trace, 1);
   };
   auto store = [&](uint32_t t_row, int mb, int nb, int) {
     const int q = warp & 3;
@@ -531,8 +534,13 @@ __global__ void __launch_bounds__(192, 1)
                         p.bias != nullptr ? p.bias + n0 : nullptr);
   };
   auto published = [&](int, int, int) {};
-  gemm_phase<BN, B_MN, false>(sm, tmem_base, &tmA, &tmB, p.K, tpc * p.n, p.ctr, p.status, tile_of, wait_chunk,
-                              pre_epilogue, store, published, p.trace, &tmA_local, p.rank, mt_chunk);
+  auto nothing = [&]() {};
+  if (warp >= 6) {
+    pre_epilogue();  // the copy warps: the gather of X
+  } else {
+    gemm_phase<BN, B_MN, false>(sm, tmem_base, &tmA, &tmB, p.K, tpc * p.n, p.ctr, p.status, tile_of, wait_chunk,
+                                nothing, store, published, p.trace, &tmA_local, p.rank, mt_chunk);
+  }
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
@@ -853,12 +861,13 @@ void ag_gemm(const at::Tensor& x_local, at::Tensor& x_full_out, const at::Tensor
   make_tma_2d_bf16(&ts.m[2], x_local.data_ptr(), K, M / n, K, 64, 128);
   NTB_CUDA_CHECK(cudaMemsetAsync(ctrs.data_ptr(), 0, sizeof(int64_t) * (1 + n), stream));
   void* args[4] = {&ts.m[0], &ts.m[1], &ts.m[2], &p};
+  const int threads = 192 + 32 * kAgCopyWarps;
   if (wide) {
-    if (b_mn) fused_launch(ag_gemm_kernel<256, true>, grid, FusedCfg<256>::SMEM_BYTES, args, stream);
-    else fused_launch(ag_gemm_kernel<256, false>, grid, FusedCfg<256>::SMEM_BYTES, args, stream);
+    if (b_mn) fused_launch(ag_gemm_kernel<256, true>, grid, FusedCfg<256>::SMEM_BYTES, args, stream, threads);
+    else fused_launch(ag_gemm_kernel<256, false>, grid, FusedCfg<256>::SMEM_BYTES, args, stream, threads);
   } else {
-    if (b_mn) fused_launch(ag_gemm_kernel<128, true>, grid, FusedCfg<128>::SMEM_BYTES, args, stream);
-    else fused_launch(ag_gemm_kernel<128, false>, grid, FusedCfg<128>::SMEM_BYTES, args, stream);
+    if (b_mn) fused_launch(ag_gemm_kernel<128, true>, grid, FusedCfg<128>::SMEM_BYTES, args, stream, threads);
+    else fused_launch(ag_gemm_kernel<128, false>, grid, FusedCfg<128>::SMEM_BYTES, args, stream, threads);
   }
 }
 
