@@ -41,8 +41,39 @@ __device__ __forceinline__ float e4m3_sr(float y, float u) {
   return copysignf(fminf(r, 448.f), y);
 }
 
+// x / s rounded to nearest in fp32 from one reciprocal per scale: y = RN(1/s), q0 = RN(x y),
+// r = x - s q0 (exact with an FMA), q = RN(q0 + r y). This is the FMA division correction of
+// P. Markstein (IBM J. Res. Dev. 34(1), 1990; Muller et al., Handbook of Floating-Point Arithmetic,
+// Markstein's theorem): with y within half an ulp of 1/s and q0 within one ulp of x / s, q is the
+// correctly rounded quotient, provided no intermediate underflows. A quotient below 2^-126 may
+// differ in its last bit; it rounds to 0 in e4m3 either way (smallest e4m3 subnormal 2^-9). Scales
+// whose reciprocal is not a normal number take the IEEE division.
+struct ScaleDiv {
+  float s, y;
+  bool fast;
+};
+
+__device__ __forceinline__ ScaleDiv make_scale_div(float s) {
+  const float y = __frcp_rn(s);
+  const bool fast = s >= 1.17549435e-38f && s <= 8.50705917e37f && y >= 1.17549435e-38f;
+  return {s, y, fast};
+}
+
+__device__ __forceinline__ float div_scale(float x, const ScaleDiv& d) {
+  if (!d.fast) return __fdiv_rn(x, d.s);
+  const float q0 = __fmul_rn(x, d.y);
+  const float r = fmaf(-d.s, q0, x);
+  return fmaf(r, d.y, q0);
+}
+
 __device__ __forceinline__ uint8_t to_e4m3(float y) {
   return static_cast<uint8_t>(__nv_cvt_float_to_fp8(y, __NV_SATFINITE, __NV_E4M3));
+}
+
+// Two values to two e4m3 codes in one conversion (saturating, round to nearest even): a in the
+// low byte.
+__device__ __forceinline__ uint32_t to_e4m3x2(float a, float b) {
+  return static_cast<uint32_t>(__nv_cvt_float2_to_fp8x2(make_float2(a, b), __NV_SATFINITE, __NV_E4M3)) & 0xFFFFu;
 }
 
 __device__ __forceinline__ float from_e4m3(uint8_t q) {

@@ -84,9 +84,10 @@ __device__ __forceinline__ float half_warp_max(float v) {
 __device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, bool stochastic, uint64_t seed,
                                         uint64_t elem0) {
   uint32_t w[2] = {0u, 0u};
+  const ScaleDiv sd = make_scale_div(s);  // the correctly rounded v / s, as the tile quantiser
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    float y = fminf(fmaxf(v[j] / s, -448.f), 448.f);
+    float y = fminf(fmaxf(div_scale(v[j], sd), -448.f), 448.f);
     if (stochastic) y = e4m3_sr(y, uniform01(seed, elem0 + j));
     w[j >> 2] |= static_cast<uint32_t>(to_e4m3(y)) << (8 * (j & 3));
   }

@@ -43,26 +43,36 @@ __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
   *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
 }
 
-// Quantises 8 values with scale s (exact IEEE division, as the recipe states q = e4m3(x / s)),
-// optionally stochastically; returns the 8 codes packed little-endian, and the dequantised values.
+// Quantises 8 values with scale s (the correctly rounded quotient, as the recipe states
+// q = e4m3(x / s); div_scale), optionally stochastically; returns the 8 codes packed little-endian,
+// and with DQ the dequantised values.
+template <bool DQ = true>
 __device__ __forceinline__ uint2 quant8(const float (&v)[8], float s, bool stochastic, uint64_t seed, int64_t idx0,
                                         float (&dq)[8]) {
-  uint8_t b[8];
+  const ScaleDiv sd = make_scale_div(s);
+  float y[8];
 #pragma unroll
   for (int j = 0; j < 8; ++j) {
-    float y = fminf(fmaxf(__fdiv_rn(v[j], s), -448.f), 448.f);
-    if (stochastic) y = e4m3_sr(y, uniform01(seed, static_cast<uint64_t>(idx0 + j)));
-    b[j] = to_e4m3(y);
-    dq[j] = from_e4m3(b[j]) * s;
+    y[j] = div_scale(v[j], sd);
+    // nearest: the saturating conversion clamps to +-448 itself; stochastic rounding needs |y| <= 448
+    if (stochastic)
+      y[j] = e4m3_sr(fminf(fmaxf(y[j], -448.f), 448.f), uniform01(seed, static_cast<uint64_t>(idx0 + j)));
   }
-  return make_uint2(b[0] | (b[1] << 8) | (b[2] << 16) | (static_cast<uint32_t>(b[3]) << 24),
-                    b[4] | (b[5] << 8) | (b[6] << 16) | (static_cast<uint32_t>(b[7]) << 24));
+  uint32_t w[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h)
+    w[h] = to_e4m3x2(y[4 * h], y[4 * h + 1]) | (to_e4m3x2(y[4 * h + 2], y[4 * h + 3]) << 16);
+  if (DQ) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) dq[j] = from_e4m3(static_cast<uint8_t>(w[j >> 2] >> (8 * (j & 3)))) * s;
+  }
+  return make_uint2(w[0], w[1]);
 }
 
 // 1x128 tiles: a half-warp per (row, 128-column tile), 8 elements (one 16-byte load) per lane; the
 // tile's amax is reduced over the 16 lanes with shuffles. Writes the codes (8-byte stores), the
 // scale, and optionally the dequantised value. Grid-stride over tile pairs.
-template <typename T>
+template <typename T, bool DQ>
 __global__ void __launch_bounds__(256) quant_tile_kernel(const T* __restrict__ x, int64_t rows, int cols,
                                                          uint8_t* __restrict__ q, float* __restrict__ scales,
                                                          T* __restrict__ dq, int stochastic, uint64_t seed) {
@@ -98,9 +108,9 @@ __global__ void __launch_bounds__(256) quant_tile_kernel(const T* __restrict__ x
       if (hl == 0) scales[t[u]] = s;
       const int64_t idx0 = t[u] * 128 + hl * 8;
       float d[8];
-      const uint2 codes = quant8(v[u], s, stochastic != 0, seed, idx0, d);
+      const uint2 codes = quant8<DQ>(v[u], s, stochastic != 0, seed, idx0, d);
       if (q) *reinterpret_cast<uint2*>(q + idx0) = codes;
-      if (dq) store8(dq + idx0, d);
+      if (DQ) store8(dq + idx0, d);
     }
   }
 }
@@ -186,8 +196,11 @@ static void launch_quant(const at::Tensor& x, int block_rows, bool stochastic, i
     if (block_rows == 1) {
       const int64_t pairs = (rows * (cols / 128) + 1) / 2;
       const int grid = static_cast<int>(std::min<int64_t>((pairs + 7) / 8, 16L * num_sms(x.get_device())));
-      quant_tile_kernel<bf16><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<bf16*>(dq), stochastic,
-                                                        sd);
+      if (dq)
+        quant_tile_kernel<bf16, true><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<bf16*>(dq),
+                                                                stochastic, sd);
+      else
+        quant_tile_kernel<bf16, false><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, nullptr, stochastic, sd);
     } else {
       const int64_t blocks = ((rows + 127) / 128) * (cols / 128);
       quant_block_kernel<bf16><<<blocks, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<bf16*>(dq),
@@ -199,8 +212,11 @@ static void launch_quant(const at::Tensor& x, int block_rows, bool stochastic, i
     if (block_rows == 1) {
       const int64_t pairs = (rows * (cols / 128) + 1) / 2;
       const int grid = static_cast<int>(std::min<int64_t>((pairs + 7) / 8, 16L * num_sms(x.get_device())));
-      quant_tile_kernel<float><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<float*>(dq),
-                                                         stochastic, sd);
+      if (dq)
+        quant_tile_kernel<float, true><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<float*>(dq),
+                                                                 stochastic, sd);
+      else
+        quant_tile_kernel<float, false><<<grid, 256, 0, stream>>>(xp, rows, cols, q, s, nullptr, stochastic, sd);
     } else {
       const int64_t blocks = ((rows + 127) / 128) * (cols / 128);
       quant_block_kernel<float><<<blocks, 256, 0, stream>>>(xp, rows, cols, q, s, reinterpret_cast<float*>(dq),
