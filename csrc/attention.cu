@@ -338,6 +338,43 @@ __global__ void attn_bwd_delta_kernel(const bf16* __restrict__ dout, const bf16*
 }
 
 // dq[b,s,h,:] = bf16(acc[b,h,s,:] * scale) (dq strided)
+// delta with 16-byte loads: half a warp per (b, s, h) row, 8 elements per lane per step; rows are
+// grid-strided so each warp keeps two rows' loads in flight. Needs D % 8 == 0 and 16-byte aligned rows.
+__global__ void __launch_bounds__(256) attn_bwd_delta_vec_kernel(const bf16* __restrict__ dout,
+                                                                 const bf16* __restrict__ out,
+                                                                 float* __restrict__ delta, int B, int S, int H,
+                                                                 int D) {
+  const int lane = threadIdx.x & 31, half = lane >> 4, hl = lane & 15;
+  const int64_t rows = static_cast<int64_t>(B) * S * H;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+  for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); 2 * w < rows;
+       w += nwarps) {
+    const int64_t row = 2 * w + half;
+    const bool live = row < rows;
+    float acc = 0.f;
+    if (live) {
+      const bf16* a = dout + row * D;
+      const bf16* c = out + row * D;
+      for (int i = hl * 8; i < D; i += 128) {
+        const uint4 x = *reinterpret_cast<const uint4*>(a + i);
+        const uint4 y = *reinterpret_cast<const uint4*>(c + i);
+        acc += bf16_lo(x.x) * bf16_lo(y.x) + bf16_hi(x.x) * bf16_hi(y.x) + bf16_lo(x.y) * bf16_lo(y.y) +
+               bf16_hi(x.y) * bf16_hi(y.y) + bf16_lo(x.z) * bf16_lo(y.z) + bf16_hi(x.z) * bf16_hi(y.z) +
+               bf16_lo(x.w) * bf16_lo(y.w) + bf16_hi(x.w) * bf16_hi(y.w);
+      }
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    if (live && hl == 0) {
+      const int h = static_cast<int>(row % H);
+      const int64_t bs = row / H;
+      const int s = static_cast<int>(bs % S);
+      const int64_t bb = bs / S;
+      delta[(bb * H + h) * S + s] = acc;
+    }
+  }
+}
+
 __global__ void attn_bwd_dq_convert_kernel(const float* __restrict__ acc, bf16* __restrict__ dq, int B, int S, int H,
                                            int D, float scale, int64_t sb, int64_t ss, int64_t sh) {
   const int64_t total = static_cast<int64_t>(B) * S * H * D;
@@ -350,6 +387,34 @@ __global__ void attn_bwd_dq_convert_kernel(const float* __restrict__ acc, bf16* 
     const int s = bs % S;
     const int bb = bs / S;
     dq[bb * sb + s * ss + h * sh + d] = __float2bfloat16(acc[((static_cast<int64_t>(bb) * H + h) * S + s) * D + d] * scale);
+  }
+}
+
+// The same conversion, 8 head-dim elements per thread: two 16-byte loads of the fp32 accumulator,
+// one 16-byte bf16 store, threads ordered like the output rows (b, s, h) so the stores coalesce.
+// Needs D % 8 == 0 and 16-byte aligned output rows.
+__global__ void __launch_bounds__(256) attn_bwd_dq_convert_vec_kernel(const float* __restrict__ acc,
+                                                                      bf16* __restrict__ dq, int B, int S, int H,
+                                                                      int D, float scale, int64_t sb, int64_t ss,
+                                                                      int64_t sh) {
+  const int cpr = D / 8;  // chunks per (b, s, h) row
+  const int64_t total = static_cast<int64_t>(B) * S * H * cpr;
+  for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(i % cpr);
+    const int64_t r = i / cpr;
+    const int h = static_cast<int>(r % H);
+    const int64_t bs = r / H;
+    const int s = static_cast<int>(bs % S);
+    const int64_t bb = bs / S;
+    const float4* src = reinterpret_cast<const float4*>(acc + ((bb * H + h) * S + s) * D + c * 8);
+    const float4 a = src[0], b = src[1];
+    uint4 o;
+    o.x = pack_bf16x2(a.x * scale, a.y * scale);
+    o.y = pack_bf16x2(a.z * scale, a.w * scale);
+    o.z = pack_bf16x2(b.x * scale, b.y * scale);
+    o.w = pack_bf16x2(b.z * scale, b.w * scale);
+    *reinterpret_cast<uint4*>(dq + bb * sb + s * ss + h * sh + c * 8) = o;
   }
 }
 
@@ -708,9 +773,17 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
   auto stream = at::cuda::getCurrentCUDAStream();
   {
     const int64_t rows = static_cast<int64_t>(p.B) * p.S * p.Hq;
-    attn_bwd_delta_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(reinterpret_cast<const bf16*>(dout.data_ptr()),
-                                                               reinterpret_cast<const bf16*>(out.data_ptr()),
-                                                               delta.data_ptr<float>(), p.B, p.S, p.Hq, DV);
+    const bool vec = DV % 8 == 0 && out.is_contiguous() && dout.is_contiguous() &&
+                     (reinterpret_cast<uintptr_t>(out.data_ptr()) & 15) == 0 &&
+                     (reinterpret_cast<uintptr_t>(dout.data_ptr()) & 15) == 0;
+    if (vec)
+      attn_bwd_delta_vec_kernel<<<static_cast<int>(std::min<int64_t>((rows + 15) / 16, 148 * 8)), 256, 0, stream>>>(
+          reinterpret_cast<const bf16*>(dout.data_ptr()), reinterpret_cast<const bf16*>(out.data_ptr()),
+          delta.data_ptr<float>(), p.B, p.S, p.Hq, DV);
+    else
+      attn_bwd_delta_kernel<<<(rows + 7) / 8, 256, 0, stream>>>(reinterpret_cast<const bf16*>(dout.data_ptr()),
+                                                                 reinterpret_cast<const bf16*>(out.data_ptr()),
+                                                                 delta.data_ptr<float>(), p.B, p.S, p.Hq, DV);
   }
   p.dout = reinterpret_cast<const bf16*>(dout.data_ptr());
   p.lse = lse.data_ptr<float>();
@@ -738,9 +811,17 @@ std::vector<at::Tensor> flash_attn_bwd(const at::Tensor& dout, const at::Tensor&
 #undef NTB_BWD
   TORCH_CHECK(launched, "flash_attn_bwd: unsupported head dims ", DQK, "/", DV);
   const int64_t total = static_cast<int64_t>(p.B) * p.S * p.Hq * DQK;
-  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
-  attn_bwd_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc.data_ptr<float>(), p.dq, p.B, p.S, p.Hq, DQK, p.scale,
-                                                         p.dq_sb, p.dq_ss, p.dq_sh);
+  const bool vec = DQK % 8 == 0 && p.dq_sb % 8 == 0 && p.dq_ss % 8 == 0 && p.dq_sh % 8 == 0 &&
+                   (reinterpret_cast<uintptr_t>(p.dq) & 15) == 0;
+  if (vec) {
+    const int blocks = static_cast<int>(std::min<int64_t>((total / 8 + 255) / 256, 148 * 16));
+    attn_bwd_dq_convert_vec_kernel<<<blocks, 256, 0, stream>>>(dq_acc.data_ptr<float>(), p.dq, p.B, p.S, p.Hq, DQK,
+                                                               p.scale, p.dq_sb, p.dq_ss, p.dq_sh);
+  } else {
+    const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 148 * 16));
+    attn_bwd_dq_convert_kernel<<<blocks, 256, 0, stream>>>(dq_acc.data_ptr<float>(), p.dq, p.B, p.S, p.Hq, DQK,
+                                                           p.scale, p.dq_sb, p.dq_ss, p.dq_sh);
+  }
   NTB_LAUNCH_CHECK(1);
   return {dq, dk, dv};
 }
