@@ -200,11 +200,13 @@ class FlatAdamW:
             from .zero_fused import MAX_BUFFERS
 
             total = sum(p.numel() for _, _, ps in groups for p in ps)
-            elems = max(int(bucket_mb * 2 ** 20 / 4), -(-total // (MAX_BUFFERS - len(groups))))
+            elems = max(int(bucket_mb * 2 ** 20 / 4), -(-total // max(1, MAX_BUFFERS - 2 * len(groups)))))
             pos = {id(p): k for k, p in enumerate(p for _, _, ps in groups for p in ps)}
             groups = [(i, g, b) for i, g, ps in groups for b in _buckets(ps, elems)]
             # bucket order = expected readiness order: the backward finishes the last layers first
             groups.sort(key=lambda t: -max(pos[id(p)] for p in t[2]))
+        if fused and len(groups) > 32:
+            raise ValueError(f"the peer-memory ZeRO step takes at most 32 buffers, got {len(groups)} parameter groups")
         if fused:
             from .zero_fused import ZeroSymm
 
