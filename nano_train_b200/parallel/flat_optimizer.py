@@ -200,7 +200,7 @@ class FlatAdamW:
             from .zero_fused import MAX_BUFFERS
 
             total = sum(p.numel() for _, _, ps in groups for p in ps)
-            elems = max(int(bucket_mb * 2 ** 20 / 4), -(-total // max(1, MAX_BUFFERS - 2 * len(groups)))))
+            elems = max(int(bucket_mb * 2 ** 20 / 4), -(-total // max(1, MAX_BUFFERS - 2 * len(groups))))
             pos = {id(p): k for k, p in enumerate(p for _, _, ps in groups for p in ps)}
             groups = [(i, g, b) for i, g, ps in groups for b in _buckets(ps, elems)]
             # bucket order = expected readiness order: the backward finishes the last layers first
