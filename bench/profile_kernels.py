@@ -174,9 +174,15 @@ def main():
         pb = torch.empty(n, **bf)
         sc = torch.ones(1, device=dev)
         fn = lambda: C.adamw_flat_(p, m, v, g, pb, 1e-4, 0.9, 0.95, 1e-8, 0.1, 1, sc, None)  # noqa: E731
-    elif a.case == "swiglu":
+    elif a.case in ("swiglu", "swiglu_bwd"):
         gu = torch.randn(8192, 2 * 14336, **bf)
-        fn = lambda: C.swiglu_fwd(gu)  # noqa: E731
+        if a.case == "swiglu":
+            nbytes = gu.numel() * 2 + gu.numel()  # read gate|up, write the activation
+            fn = lambda: C.swiglu_fwd(gu)  # noqa: E731
+        else:
+            dy = torch.randn(8192, 14336, **bf)
+            nbytes = gu.numel() * 2 * 2 + dy.numel() * 2  # read gate|up and dY, write d(gate|up)
+            fn = lambda: C.swiglu_bwd(dy, gu)  # noqa: E731
     elif a.case == "ce":
         logits = torch.randn(4096, 32064, **bf)
         labels = torch.randint(0, 32064, (4096,), device=dev)

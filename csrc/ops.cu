@@ -927,39 +927,43 @@ __global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ out,
   }
 }
 
-template <typename T>
+// IDX: the index type (uint32_t when rows * I < 2^31: the row / column split is then a 32-bit
+// division per 8 elements instead of a 64-bit one). silu(g) = g * (1 / (1 + e^-g)) with the correctly
+// rounded reciprocal.
+template <typename T, typename IDX>
 __global__ void swiglu_fwd_vec_kernel(const T* __restrict__ gu, T* __restrict__ out, int64_t rows, int I) {
-  const int64_t total = rows * I / 8;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t e = idx * 8;
-    const int64_t r = e / I;
-    const int c = e % I;
+  const IDX total = static_cast<IDX>(rows * I / 8);
+  for (IDX idx = blockIdx.x * static_cast<IDX>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<IDX>(gridDim.x) * blockDim.x) {
+    const IDX e = idx * 8;
+    const IDX r = e / static_cast<IDX>(I);
+    const IDX c = e - r * static_cast<IDX>(I);
     float g[8], u[8], o[8];
-    ld8(gu + r * 2 * I + c, g);
-    ld8(gu + r * 2 * I + I + c, u);
+    ld8(gu + static_cast<int64_t>(r) * 2 * I + c, g);
+    ld8(gu + static_cast<int64_t>(r) * 2 * I + I + c, u);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = g[j] / (1.f + __expf(-g[j])) * u[j];
-    st8(out + e, o);
+    for (int j = 0; j < 8; ++j) o[j] = g[j] * __frcp_rn(1.f + __expf(-g[j])) * u[j];
+    st8(out + static_cast<int64_t>(e), o);
   }
 }
 
-template <typename T>
+template <typename T, typename IDX>
 __global__ void swiglu_bwd_vec_kernel(const T* __restrict__ dout, const T* __restrict__ gu, T* __restrict__ dgu,
                                       int64_t rows, int I) {
-  const int64_t total = rows * I / 8;
-  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
-       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t e = idx * 8;
-    const int64_t r = e / I;
-    const int c = e % I;
+  const IDX total = static_cast<IDX>(rows * I / 8);
+  for (IDX idx = blockIdx.x * static_cast<IDX>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<IDX>(gridDim.x) * blockDim.x) {
+    const int64_t e = static_cast<int64_t>(idx) * 8;
+    const IDX rr = static_cast<IDX>(idx * 8) / static_cast<IDX>(I);
+    const int64_t r = rr;
+    const int c = static_cast<int>(static_cast<IDX>(idx * 8) - rr * static_cast<IDX>(I));
     float g[8], u[8], d[8], dg[8], du[8];
     ld8(gu + r * 2 * I + c, g);
     ld8(gu + r * 2 * I + I + c, u);
     ld8(dout + e, d);
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
-      const float s = 1.f / (1.f + __expf(-g[j]));
+      const float s = __frcp_rn(1.f + __expf(-g[j]));
       const float sg = g[j] * s;
       du[j] = d[j] * sg;
       dg[j] = d[j] * u[j] * (s + sg * (1.f - s));
@@ -1000,7 +1004,12 @@ at::Tensor swiglu_fwd(const at::Tensor& gu) {
   const bool vec = I % 8 == 0;
   NTB_DISPATCH_FLOAT(gu.scalar_type(), "swiglu_fwd", [&] {
     if (vec)
-      swiglu_fwd_vec_kernel<scalar_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(P<scalar_t>(gu), P<scalar_t>(out), rows, I);
+      if (rows * I < (1LL << 31))
+        swiglu_fwd_vec_kernel<scalar_t, uint32_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(P<scalar_t>(gu),
+                                                                                             P<scalar_t>(out), rows, I);
+      else
+        swiglu_fwd_vec_kernel<scalar_t, int64_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(P<scalar_t>(gu),
+                                                                                            P<scalar_t>(out), rows, I);
     else
       swiglu_fwd_kernel<scalar_t><<<ew_blocks(rows * I), 256, 0, stream>>>(P<scalar_t>(gu), P<scalar_t>(out), rows, I);
   });
@@ -1018,8 +1027,12 @@ at::Tensor swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu) {
   const bool vec = I % 8 == 0;
   NTB_DISPATCH_FLOAT(gu.scalar_type(), "swiglu_bwd", [&] {
     if (vec)
-      swiglu_bwd_vec_kernel<scalar_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(gu),
-                                                                                P<scalar_t>(dgu), rows, I);
+      if (rows * I < (1LL << 31))
+        swiglu_bwd_vec_kernel<scalar_t, uint32_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(
+            P<scalar_t>(d), P<scalar_t>(gu), P<scalar_t>(dgu), rows, I);
+      else
+        swiglu_bwd_vec_kernel<scalar_t, int64_t><<<ew_blocks(rows * I / 8), 256, 0, stream>>>(
+            P<scalar_t>(d), P<scalar_t>(gu), P<scalar_t>(dgu), rows, I);
     else
       swiglu_bwd_kernel<scalar_t><<<ew_blocks(rows * I), 256, 0, stream>>>(P<scalar_t>(d), P<scalar_t>(gu),
                                                                           P<scalar_t>(dgu), rows, I);
