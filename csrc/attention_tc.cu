@@ -1167,22 +1167,31 @@ __global__ void __launch_bounds__(192, 1)
   }
 }
 
-// fp32 [B, S, H, D] accumulator -> bf16 strided [B, S, H, D] view.
+// fp32 [B, S, H, D] accumulator -> bf16 strided [B, S, H, D] view, 8 elements per thread (two
+// 16-byte loads, one 16-byte store; D % 8 == 0 and 16-byte aligned output rows, else 4 with an
+// 8-byte store).
+template <int V>
 __global__ void acc_to_bf16_kernel(const float* __restrict__ acc, __nv_bfloat16* __restrict__ out, int B, int S, int H,
                                    int D, int64_t sb, int64_t ss, int64_t sh) {
-  const int64_t total = static_cast<int64_t>(B) * S * H * D / 4;
+  const int64_t total = static_cast<int64_t>(B) * S * H * D / V;
   for (int64_t i = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; i < total;
        i += static_cast<int64_t>(gridDim.x) * blockDim.x) {
-    const int64_t e = i * 4;
+    const int64_t e = i * V;
     const int d = static_cast<int>(e % D);
     const int64_t r = e / D;
     const int h = static_cast<int>(r % H);
     const int64_t bs = r / H;
     const int s = static_cast<int>(bs % S);
     const int bb = static_cast<int>(bs / S);
-    const float4 v = *reinterpret_cast<const float4*>(acc + e);
     __nv_bfloat16* o = out + bb * sb + s * ss + h * sh + d;
-    *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    const float4 v = *reinterpret_cast<const float4*>(acc + e);
+    if constexpr (V == 8) {
+      const float4 w = *reinterpret_cast<const float4*>(acc + e + 4);
+      *reinterpret_cast<uint4*>(o) = make_uint4(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w), pack_bf16x2(w.x, w.y),
+                                                pack_bf16x2(w.z, w.w));
+    } else {
+      *reinterpret_cast<uint2*>(o) = make_uint2(pack_bf16x2(v.x, v.y), pack_bf16x2(v.z, v.w));
+    }
   }
 }
 
@@ -1297,13 +1306,20 @@ void flash_attn_bwd_tc_launch(const at::Tensor& q, const at::Tensor& k, const at
     TORCH_CHECK(dk.stride(3) == 1 && dv.stride(3) == 1 && dk.stride(2) % 4 == 0 && dk.stride(1) % 4 == 0 &&
                     dv.stride(2) % 4 == 0 && dv.stride(1) % 4 == 0,
                 "flash_attn_bwd_tc: dk/dv strides must keep 8-byte alignment");
-    const int64_t nk = B * S * Hkv * DQK / 4, nv = B * S * Hkv * DV / 4;
-    const int bk = static_cast<int>(std::min<int64_t>((nk + 255) / 256, 148 * 8));
-    const int bv = static_cast<int>(std::min<int64_t>((nv + 255) / 256, 148 * 8));
-    acc_to_bf16_kernel<<<bk, 256, 0, stream>>>(dk_acc.data_ptr<float>(), p.dk, p.B, p.S, p.Hkv,
-                                               static_cast<int>(DQK), p.dk_sb, p.dk_ss, p.dk_sh);
-    acc_to_bf16_kernel<<<bv, 256, 0, stream>>>(dv_acc.data_ptr<float>(), p.dv, p.B, p.S, p.Hkv, static_cast<int>(DV),
-                                               p.dv_sb, p.dv_ss, p.dv_sh);
+    auto convert = [&](const at::Tensor& acc, __nv_bfloat16* o, int64_t D, int64_t sb, int64_t ss, int64_t sh) {
+      const bool v8 = D % 8 == 0 && sb % 8 == 0 && ss % 8 == 0 && sh % 8 == 0 &&
+                      (reinterpret_cast<uintptr_t>(o) & 15) == 0;
+      const int64_t n = B * S * Hkv * D / (v8 ? 8 : 4);
+      const int blocks = static_cast<int>(std::min<int64_t>((n + 255) / 256, 148 * 8));
+      if (v8)
+        acc_to_bf16_kernel<8><<<blocks, 256, 0, stream>>>(acc.data_ptr<float>(), o, p.B, p.S, p.Hkv,
+                                                          static_cast<int>(D), sb, ss, sh);
+      else
+        acc_to_bf16_kernel<4><<<blocks, 256, 0, stream>>>(acc.data_ptr<float>(), o, p.B, p.S, p.Hkv,
+                                                          static_cast<int>(D), sb, ss, sh);
+    };
+    convert(dk_acc, p.dk, DQK, p.dk_sb, p.dk_ss, p.dk_sh);
+    convert(dv_acc, p.dv, DV, p.dv_sb, p.dv_ss, p.dv_sh);
     NTB_LAUNCH_CHECK(2);
   }
 }
