@@ -291,16 +291,26 @@ def test_adamw_flat_matches_torch():
     torch.testing.assert_close(pb.float(), ref.detach(), rtol=1e-2, atol=1e-2)
 
 
-def test_grad_stats():
+@pytest.mark.parametrize("n", [5000, 5003, 3, 1 << 22])
+def test_grad_stats(n):
+    """Sum of squares, optional in-place unscale and the non-finite flag: the fp32 vector kernel
+    (n % 4 tails included) and the scalar one."""
     from nano_train_b200.ops.optim import grad_stats_
-    g = torch.randn(5000, device="cuda")
+    gb = torch.randn(n, device="cuda", dtype=torch.bfloat16)
+    outb = torch.zeros(2, device="cuda")
+    grad_stats_(gb, outb)
+    refb = gb.float().pow(2).sum()
+    assert abs(outb[0].item() - refb.item()) / refb.item() < 1e-4
+    g = torch.randn(n, device="cuda")
+    g_half = g * 0.5
     out = torch.zeros(2, device="cuda")
     inv = torch.tensor([0.5], device="cuda")
     ref = (g * 0.5).pow(2).sum()
     grad_stats_(g, out, inv)
-    assert abs(out[0].item() - ref.item()) / ref.item() < 1e-5
+    assert abs(out[0].item() - ref.item()) / ref.item() < 1e-4
     assert out[1].item() == 0
-    g[7] = float("inf")
+    torch.testing.assert_close(g, g_half, rtol=0, atol=0)  # unscaled in place
+    g[n - 1] = float("inf")  # the last element: in the tail when n % 4 != 0
     grad_stats_(g, out)
     assert out[1].item() == 1
 
