@@ -43,6 +43,10 @@ void rope_(at::Tensor& x, const c10::optional<at::Tensor>& positions, int64_t of
            double theta, int64_t mode, bool inverse);
 void rope_table_(at::Tensor& x, const at::Tensor& table, int64_t off, int64_t R, int64_t seq_len, int64_t mode,
                  bool inverse);
+at::Tensor mla_k_assemble(const at::Tensor& kv, const at::Tensor& kr, const at::Tensor& table, int64_t Dn,
+                          int64_t seq_len);
+at::Tensor mla_k_assemble_bwd(const at::Tensor& dk, at::Tensor& dkv, const at::Tensor& table, int64_t Dn,
+                              int64_t seq_len);
 at::Tensor swiglu_fwd(const at::Tensor& gu);
 at::Tensor swiglu_bwd(const at::Tensor& dout, const at::Tensor& gu);
 at::Tensor gelu_fwd(const at::Tensor& x);
@@ -174,6 +178,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("layernorm_bwd", &ntb::layernorm_bwd);
   m.def("rope_", &ntb::rope_);
   m.def("rope_table_", &ntb::rope_table_);
+  m.def("mla_k_assemble", &ntb::mla_k_assemble, "MLA keys [nope | rope(kr)] per head in one launch");
+  m.def("mla_k_assemble_bwd", &ntb::mla_k_assemble_bwd, "dK nope part into dkv, rope part summed over heads");
   m.def("swiglu_fwd", &ntb::swiglu_fwd);
   m.def("swiglu_bwd", &ntb::swiglu_bwd);
   m.def("gelu_fwd", &ntb::gelu_fwd);

@@ -912,6 +912,149 @@ void rope_table_(at::Tensor& x, const at::Tensor& table, int64_t off, int64_t R,
   NTB_LAUNCH_CHECK(1);
 }
 
+// Key assembly of multi-head latent attention. Each head's key is [nope | rope]: the nope part is
+// columns [0, Dn) of that head's slice of the kv up-projection, the rope part one rotated vector per
+// token that every head shares. One launch writes kf[t, h, :] = [kv[t, h, 0:Dn] | rope(kr[t, :])] in
+// 16-byte chunks (interleaved-pair rotation from the (cos, sin) table, positions t % seq_len); it
+// stands for a rotation launch, the broadcast over heads and the concatenation.
+__global__ void __launch_bounds__(256) mla_k_assemble_kernel(const bf16* __restrict__ kv, int64_t kv_st,
+                                                             int64_t kv_sh, const bf16* __restrict__ kr,
+                                                             int64_t kr_st, const float2* __restrict__ cs,
+                                                             bf16* __restrict__ kf, int64_t T_, int heads, int Dn,
+                                                             int R, int seq_len) {
+  const int cn = Dn / 8, chunks = cn + R / 8, half = R / 2;
+  const int64_t total = T_ * heads * chunks;
+  for (int64_t idx = blockIdx.x * static_cast<int64_t>(blockDim.x) + threadIdx.x; idx < total;
+       idx += static_cast<int64_t>(gridDim.x) * blockDim.x) {
+    const int c = static_cast<int>(idx % chunks);
+    const int64_t th = idx / chunks;
+    const int hd = static_cast<int>(th % heads);
+    const int64_t t = th / heads;
+    bf16* dst = kf + th * (Dn + R) + c * 8;
+    if (c < cn) {
+      *reinterpret_cast<uint4*>(dst) = *reinterpret_cast<const uint4*>(kv + t * kv_st + hd * kv_sh + c * 8);
+      continue;
+    }
+    const int j0 = (c - cn) * 8;
+    const float2* row = cs + static_cast<int64_t>(t % seq_len) * half;
+    float v[8], o[8];
+    ld8(kr + t * kr_st + j0, v);
+#pragma unroll
+    for (int m = 0; m < 4; ++m) {
+      const float2 q0 = row[(j0 + 2 * m) % half], q1 = row[(j0 + 2 * m + 1) % half];
+      o[2 * m] = v[2 * m] * q0.x - v[2 * m + 1] * q0.y;
+      o[2 * m + 1] = v[2 * m + 1] * q1.x + v[2 * m] * q1.y;
+    }
+    st8(dst, o);
+  }
+}
+
+// Backward of the key assembly: dkv[t, h, 0:Dn] = dk[t, h, 0:Dn] for every head, and
+// dkr[t, :] = rope^T(sum over heads of dk[t, h, Dn:Dn+R]) with the head sum in fp32 and one rounding.
+// One warp per token: the lanes copy the nope chunks, then lane l adds rope chunk l % (R/8) of heads
+// l / (R/8), l / (R/8) + 32 / (R/8), ...; lanes holding the same chunk combine by xor shuffles (R/8
+// divides 32, checked by the binding), and lanes 0 .. R/8-1 rotate back and store.
+__global__ void __launch_bounds__(256) mla_k_assemble_bwd_kernel(const bf16* __restrict__ dk, int64_t dk_st,
+                                                                 int64_t dk_sh, bf16* __restrict__ dkv,
+                                                                 int64_t dkv_st, int64_t dkv_sh,
+                                                                 bf16* __restrict__ dkr, int64_t dkr_st,
+                                                                 const float2* __restrict__ cs, int64_t T_,
+                                                                 int heads, int Dn, int R, int seq_len) {
+  const int lane = threadIdx.x & 31;
+  const int cn = Dn / 8, cr = R / 8, half = R / 2;
+  const int64_t wpb = blockDim.x / 32;
+  const int64_t nwarps = static_cast<int64_t>(gridDim.x) * wpb;
+  for (int64_t t = blockIdx.x * wpb + threadIdx.x / 32; t < T_; t += nwarps) {
+    const bf16* src = dk + t * dk_st;
+    bf16* dst = dkv + t * dkv_st;
+    for (int i = lane; i < heads * cn; i += 32) {
+      const int hd = i / cn, c = i - hd * cn;
+      *reinterpret_cast<uint4*>(dst + hd * dkv_sh + c * 8) =
+          *reinterpret_cast<const uint4*>(src + hd * dk_sh + c * 8);
+    }
+    const int rc = lane % cr;
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int hd = lane / cr; hd < heads; hd += 32 / cr) {
+      float v[8];
+      ld8(src + hd * dk_sh + Dn + rc * 8, v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += v[j];
+    }
+    for (int off = cr; off < 32; off <<= 1) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], off);
+    }
+    if (lane < cr) {
+      const int j0 = lane * 8;
+      const float2* row = cs + static_cast<int64_t>(t % seq_len) * half;
+      float o[8];
+#pragma unroll
+      for (int m = 0; m < 4; ++m) {
+        const float2 q0 = row[(j0 + 2 * m) % half], q1 = row[(j0 + 2 * m + 1) % half];
+        o[2 * m] = acc[2 * m] * q0.x + acc[2 * m + 1] * q1.y;
+        o[2 * m + 1] = acc[2 * m + 1] * q1.x - acc[2 * m] * q0.y;
+      }
+      st8(dkr + t * dkr_st + j0, o);
+    }
+  }
+}
+
+static void check_mla_rows(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kBFloat16 && t.stride(-1) == 1, what, ": bf16 CUDA, last dim contiguous");
+  for (int d = 0; d + 1 < t.dim(); ++d) TORCH_CHECK(t.stride(d) % 8 == 0, what, ": strides must be 16-byte multiples");
+  TORCH_CHECK((reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0, what, ": 16-byte aligned start");
+}
+
+static void check_mla_table(const at::Tensor& table, int64_t seq_len, int64_t R) {
+  TORCH_CHECK(table.is_cuda() && table.scalar_type() == at::kFloat && table.is_contiguous() &&
+                  table.numel() == seq_len * R,
+              "mla_k_assemble: table must be contiguous fp32 [seq_len, R/2, 2]");
+  TORCH_CHECK(R % 8 == 0 && R > 0 && 32 % (R / 8) == 0, "mla_k_assemble: R / 8 must divide 32");
+}
+
+// kv [T, heads, >= Dn], kr [T, R] -> kf [T, heads, Dn + R] (contiguous).
+at::Tensor mla_k_assemble(const at::Tensor& kv, const at::Tensor& kr, const at::Tensor& table, int64_t Dn,
+                          int64_t seq_len) {
+  TORCH_CHECK(kv.dim() == 3 && kr.dim() == 2 && kv.size(0) == kr.size(0), "mla_k_assemble: kv [T, heads, D], kr [T, R]");
+  check_mla_rows(kv, "mla_k_assemble kv");
+  check_mla_rows(kr, "mla_k_assemble kr");
+  const int64_t R = kr.size(1), T_ = kv.size(0), heads = kv.size(1);
+  TORCH_CHECK(Dn % 8 == 0 && Dn > 0 && Dn <= kv.size(2), "mla_k_assemble: Dn");
+  check_mla_table(table, seq_len, R);
+  auto kf = at::empty({T_, heads, Dn + R}, kv.options());
+  if (T_ == 0 || heads == 0) return kf;
+  const int64_t total = T_ * heads * (Dn + R) / 8;
+  const int blocks = static_cast<int>(std::min<int64_t>((total + 255) / 256, 16L * num_sms(kv.get_device())));
+  mla_k_assemble_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      P<bf16>(kv), kv.stride(0), kv.stride(1), P<bf16>(kr), kr.stride(0),
+      reinterpret_cast<const float2*>(table.data_ptr<float>()), P<bf16>(kf), T_, static_cast<int>(heads),
+      static_cast<int>(Dn), static_cast<int>(R), static_cast<int>(seq_len));
+  NTB_LAUNCH_CHECK(1);
+  return kf;
+}
+
+// dk [T, heads, Dn + R]; writes dkv[:, :, 0:Dn] and returns dkr [T, R].
+at::Tensor mla_k_assemble_bwd(const at::Tensor& dk, at::Tensor& dkv, const at::Tensor& table, int64_t Dn,
+                              int64_t seq_len) {
+  TORCH_CHECK(dk.dim() == 3 && dkv.dim() == 3 && dk.size(0) == dkv.size(0) && dk.size(1) == dkv.size(1),
+              "mla_k_assemble_bwd: dk [T, heads, Dn + R], dkv [T, heads, >= Dn]");
+  check_mla_rows(dk, "mla_k_assemble_bwd dk");
+  check_mla_rows(dkv, "mla_k_assemble_bwd dkv");
+  const int64_t R = dk.size(2) - Dn, T_ = dk.size(0), heads = dk.size(1);
+  TORCH_CHECK(Dn % 8 == 0 && Dn > 0 && Dn <= dkv.size(2), "mla_k_assemble_bwd: Dn");
+  check_mla_table(table, seq_len, R);
+  auto dkr = at::empty({T_, R}, dk.options());
+  if (T_ == 0) return dkr;
+  if (heads == 0) return dkr.zero_();
+  const int blocks = static_cast<int>(std::min<int64_t>((T_ + 7) / 8, 16L * num_sms(dk.get_device())));
+  mla_k_assemble_bwd_kernel<<<blocks, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
+      P<bf16>(dk), dk.stride(0), dk.stride(1), P<bf16>(dkv), dkv.stride(0), dkv.stride(1), P<bf16>(dkr), dkr.stride(0),
+      reinterpret_cast<const float2*>(table.data_ptr<float>()), T_, static_cast<int>(heads), static_cast<int>(Dn),
+      static_cast<int>(R), static_cast<int>(seq_len));
+  NTB_LAUNCH_CHECK(1);
+  return dkr;
+}
+
 // =========================================================== activations
 // SwiGLU over a packed [rows, 2I] tensor: gate = cols [0, I), up = cols [I, 2I).
 template <typename T>

@@ -302,6 +302,67 @@ class _RopeColumnsInPlace(torch.autograd.Function):
         return dy, None, None, None, None
 
 
+class _MlaAttention(torch.autograd.Function):
+    """Causal MLA attention from the projection outputs, without materialising the broadcast rope key.
+
+    q [B, S, h, Dn + R] (rope columns already rotated), kv [B, S, h, Dn + Dv] (the kv up-projection: nope
+    keys, then values, per head), k_rope [B, S, R] (rope part of the kv down-projection, not rotated, one
+    vector per token shared by every head; reference: src/models/deepseek.py:681-738, where it is
+    expanded over heads and concatenated to k_nope). Forward: one kernel writes the keys
+    [k_nope | rope(k_rope)] per head, and the tcgen05 attention reads the values as a strided view of kv.
+    Backward: the attention backward stores dV straight into the value columns of dkv, and one kernel
+    copies dK's nope part into dkv and reduces its rope part over heads into dk_rope (rotated back)."""
+
+    @staticmethod
+    def forward(ctx, q, kv, k_rope, Dn, scale, theta):
+        from ..ops._ext import ext
+        from ..ops.attention import _fwd
+        from ..ops.rope import rope_table
+
+        B, S, h, Dkv = kv.shape
+        R = k_rope.shape[-1]
+        table = rope_table(S, R, theta, kv.device)
+        kf = ext().mla_k_assemble(kv.reshape(B * S, h, Dkv), k_rope.reshape(B * S, R), table, Dn, S)
+        kf = kf.view(B, S, h, Dn + R)
+        v = kv[..., Dn:]
+        o, lse = _fwd(q, kf, v, scale, True)
+        ctx.save_for_backward(q, kf, v, o, lse)
+        ctx.meta = (Dn, scale, theta)
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        from ..ops._ext import ext
+        from ..ops.rope import rope_table
+
+        q, kf, v, o, lse = ctx.saved_tensors
+        Dn, scale, theta = ctx.meta
+        B, S, h, Dk = kf.shape
+        Dv = v.shape[-1]
+        C = ext()
+        dkv = torch.empty(B, S, h, Dn + Dv, device=kf.device, dtype=kf.dtype)
+        dk = torch.empty_like(kf)
+        dq = C.flash_attn_bwd(do.contiguous(), q, kf, v, o, lse, float(scale), True, None, dk, dkv[..., Dn:])[0]
+        dkr = C.mla_k_assemble_bwd(dk.view(B * S, h, Dk), dkv.view(B * S, h, Dn + Dv),
+                                   rope_table(S, Dk - Dn, theta, kf.device), Dn, S)
+        return dq, dkv, dkr.view(B, S, Dk - Dn), None, None, None
+
+
+def _mla_fused_ok(q: torch.Tensor, kv: torch.Tensor, k_rope: torch.Tensor, Dn: int) -> bool:
+    """The fused key assembly applies: bf16 tensors whose rows start on 16-byte boundaries, head dims of
+    a tcgen05 attention kernel, rope width R with R / 8 dividing 32."""
+    from ..ops._ext import ext
+    from ..ops.attention import _KERNEL_HEAD_DIMS
+
+    R = k_rope.shape[-1]
+    if not (q.is_cuda and q.dtype == kv.dtype == k_rope.dtype == torch.bfloat16 and hasattr(ext(), "mla_k_assemble")):
+        return False
+    if (Dn + R, kv.shape[-1] - Dn) not in _KERNEL_HEAD_DIMS or R % 8 or 32 % (R // 8) or Dn % 8:
+        return False
+    return all(t.stride(-1) == 1 and all(st % 8 == 0 for st in t.stride()[:-1]) and t.data_ptr() % 16 == 0
+               for t in (kv, k_rope))
+
+
 class MultiHeadLatentAttention(nn.Module):
     def __init__(self, config: DeepSeekModelConfig, parallel_context: Optional[DeepSeekParallelContext] = None, *,
                  module_prefix: str):
@@ -362,6 +423,7 @@ class MultiHeadLatentAttention(nn.Module):
         self.dropout = Dropout(config.attention_dropout)
 
     def _qkv(self, x: torch.Tensor):
+        """q [B, S, h, Dn + R], kv [B, S, h, Dn + Dv] (nope keys | values per head), k_rope [B, S, R]."""
         B, S, _ = x.shape
         h = self.local_num_heads
         q = self.q_proj(x) if self.q_proj is not None else self.q_b_proj(self.q_a_norm(self.q_a_proj(x)))
@@ -369,17 +431,20 @@ class MultiHeadLatentAttention(nn.Module):
         kv_a = self.kv_a_proj(x)
         kv_latent, k_rope = torch.split(kv_a, [self.kv_a_norm.weight.shape[0], self.qk_rope_head_dim], dim=-1)
         kv = self.kv_b_proj(self.kv_a_norm(kv_latent)).view(B, S, h, self.qk_nope_head_dim + self.v_head_dim)
-        k_nope, v = torch.split(kv, [self.qk_nope_head_dim, self.v_head_dim], dim=-1)
-        return q, k_nope, k_rope, v
+        return q, kv, k_rope
 
     def forward(self, x: torch.Tensor, attention_mask: Optional[torch.Tensor] = None) -> torch.Tensor:
         B, S, _ = x.shape
         h = self.local_num_heads
-        q, k_nope, k_rope, v = self._qkv(x)
+        q, kv, k_rope = self._qkv(x)
+        k_nope, v = torch.split(kv, [self.qk_nope_head_dim, self.v_head_dim], dim=-1)
         if x.is_cuda and attention_mask is None:
             qf = q if q.is_contiguous() else q.contiguous()
             qf = _RopeColumnsInPlace.apply(qf, self.qk_nope_head_dim, self.qk_rope_head_dim, float(self.rope_theta),
                                            "deepseek")
+            if _mla_fused_ok(qf, kv, k_rope, self.qk_nope_head_dim):
+                o = _MlaAttention.apply(qf, kv, k_rope, self.qk_nope_head_dim, self.scale, float(self.rope_theta))
+                return self.out_proj(self.dropout(o).reshape(B, S, h * self.v_head_dim))
             k_rope = ops.apply_rope(k_rope.unsqueeze(2), self.rope_theta, "deepseek")
             kf = torch.cat([k_nope, k_rope.expand(B, S, h, self.qk_rope_head_dim)], dim=-1)
             o = flash_attention(qf, kf, v, causal=True, softmax_scale=self.scale)

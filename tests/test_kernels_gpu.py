@@ -224,6 +224,32 @@ def test_rope_table_rows(mode, dtype, dqk, R, inverse):
     torch.testing.assert_close(x[:, (nq + nkv) * dqk:], ref[:, (nq + nkv) * dqk:])  # v untouched
 
 
+@pytest.mark.parametrize("B,S,h,Dn,Dv,R,lat", [(2, 128, 16, 128, 128, 64, 512), (1, 100, 3, 128, 128, 64, 64),
+                                                (3, 37, 5, 64, 64, 16, 48)])
+def test_mla_k_assemble(C, B, S, h, Dn, Dv, R, lat):
+    """MLA key assembly [k_nope | rope(k_rope) broadcast over heads] and its backward (nope part of dK
+    copied into dkv, rope part summed over heads and rotated back) against the fp32 PyTorch statement."""
+    from nano_train_b200.ops.rope import rope_reference, rope_table
+    torch.manual_seed(0)
+    theta = 1e4
+    kv = torch.randn(B, S, h * (Dn + Dv), device="cuda", dtype=torch.bfloat16).view(B, S, h, Dn + Dv)
+    kv_a = torch.randn(B, S, lat + R, device="cuda", dtype=torch.bfloat16)
+    k_rope = kv_a[..., lat:]
+    table = rope_table(S, R, theta, kv.device)
+    kf = C.mla_k_assemble(kv.reshape(B * S, h, Dn + Dv), k_rope.reshape(B * S, R), table, Dn, S).view(B, S, h, Dn + R)
+    pos = torch.arange(S, device="cuda")
+    rot = rope_reference(k_rope.float().unsqueeze(2), pos, theta, "deepseek")
+    assert torch.equal(kf[..., :Dn], kv[..., :Dn])
+    assert rel_err(kf[..., Dn:], rot.expand(B, S, h, R)) < 8e-3
+    dk = torch.randn(B, S, h, Dn + R, device="cuda", dtype=torch.bfloat16)
+    dkv = torch.full((B, S, h, Dn + Dv), 7.0, device="cuda", dtype=torch.bfloat16)
+    dkr = C.mla_k_assemble_bwd(dk.view(B * S, h, Dn + R), dkv.view(B * S, h, Dn + Dv), table, Dn, S)
+    assert torch.equal(dkv[..., :Dn], dk[..., :Dn])
+    assert bool((dkv[..., Dn:] == 7).all())
+    exp = rope_reference(dk[..., Dn:].float().sum(2, keepdim=True), pos, theta, "deepseek", inverse=True)
+    assert rel_err(dkr.view(B, S, R), exp[:, :, 0]) < 8e-3
+
+
 def test_swiglu_gelu():
     from nano_train_b200.ops.activation import gelu, swiglu
     gu = torch.randn(40, 2 * 96, device="cuda", requires_grad=True)
