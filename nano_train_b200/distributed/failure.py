@@ -17,13 +17,18 @@ Three layers, none of which needs a GPU fault to be exercised:
   ``CommTimeoutError`` for communication waits.
 
 Plus ``assert_finite`` (fail fast on non-finite loss / norms, reference:
-src/trainer.py:1301-1304, 1371-1375).
+src/trainer.py:1301-1304, 1371-1375), and ``HostFaultInjector``: faults made on
+the host (a rank that exits like a crashed process, or raises) at named points
+of the training loop, for recovery tests. The reference has no fault injection.
 """
 from __future__ import annotations
 
 import math
+import os
+import sys
 import threading
 import time
+from dataclasses import dataclass
 from typing import Callable, Optional
 
 import torch
@@ -150,3 +155,79 @@ class HeartbeatMonitor:
         dead = self.dead_ranks()
         if dead:
             raise PeerFailureError(f"rank {self.rank}: no heartbeat from ranks {dead} for > {self.timeout_s}s")
+
+
+# --------------------------------------------------------------------------- host fault injection
+class InjectedFault(RuntimeError):
+    """Raised by a ``HostFaultInjector`` in mode ``"raise"``."""
+
+
+FAULT_POINTS = ("step_end", "checkpoint_save")
+
+
+@dataclass
+class HostFaultInjector:
+    """Host-side fault at a named point of the training loop; nothing on the GPU is touched.
+
+    Points: ``"step_end"`` - step ``step`` finished and its checkpoint hook ran, with no kernel or
+    collective in flight; ``"checkpoint_save"`` - this rank's files of the checkpoint taken after
+    ``step`` completed steps are written and the completion barrier is not yet reached (the directory
+    stays without its ``COMPLETE`` marker). At the point, rank ``rank`` either leaves the process the way a
+    crashed one does (``mode="exit"``: output flushed, then ``os._exit(exit_code)``, no teardown, so the
+    peers see a dead rank) or raises ``InjectedFault`` (``mode="raise"``)."""
+
+    point: str
+    step: int
+    rank: int = 0
+    mode: str = "exit"
+    exit_code: int = 17
+
+    def __post_init__(self) -> None:
+        if self.point not in FAULT_POINTS:
+            raise ValueError(f"fault point must be one of {FAULT_POINTS}, got {self.point!r}")
+        if self.mode not in ("exit", "raise"):
+            raise ValueError(f"fault mode must be 'exit' or 'raise', got {self.mode!r}")
+
+    @classmethod
+    def from_env(cls, env=None) -> Optional["HostFaultInjector"]:
+        """NTB_FAULT_STEP (required to enable), NTB_FAULT_POINT (default step_end), NTB_FAULT_RANK
+        (default 0), NTB_FAULT_MODE (default exit): an unmodified launch line can be failed from outside."""
+        env = os.environ if env is None else env
+        if not env.get("NTB_FAULT_STEP"):
+            return None
+        return cls(point=env.get("NTB_FAULT_POINT", "step_end"), step=int(env["NTB_FAULT_STEP"]),
+                   rank=int(env.get("NTB_FAULT_RANK", "0")), mode=env.get("NTB_FAULT_MODE", "exit"))
+
+    def maybe_fail(self, point: str, step: int, rank: int) -> None:
+        if (point, step, rank) != (self.point, self.step, self.rank):
+            return
+        msg = f"injected fault: rank {rank} at {point} of step {step}"
+        if self.mode == "raise":
+            raise InjectedFault(msg)
+        import logging
+
+        print(msg, file=sys.stderr)
+        for h in logging.getLogger().handlers:
+            h.flush()
+        sys.stdout.flush()
+        sys.stderr.flush()
+        os._exit(self.exit_code)
+
+
+_injector: Optional[HostFaultInjector] = None
+_injector_read = False
+
+
+def set_fault_injector(injector: Optional[HostFaultInjector]) -> None:
+    """Install (or with None remove) the process's injector; overrides the environment."""
+    global _injector, _injector_read
+    _injector, _injector_read = injector, True
+
+
+def fault_point(point: str, step: int, rank: int) -> None:
+    """Hook the runtime calls at each fault point; a no-op unless an injector names this point."""
+    global _injector, _injector_read
+    if not _injector_read:
+        _injector, _injector_read = HostFaultInjector.from_env(), True
+    if _injector is not None:
+        _injector.maybe_fail(point, step, rank)

@@ -15,6 +15,7 @@ from typing import Optional
 
 import torch
 
+from ..distributed.failure import fault_point
 from .context import RuntimeContext, TrainState
 from .contracts import OptimizerState, ResumeState
 
@@ -87,6 +88,7 @@ class DirectoryCheckpointManager:
             torch.save(opt.state_dict(), os.path.join(d, f"optimizer_rank{rank}.pt"))
         torch.save({"train_state": vars(state).copy(), "next_step": next_step, "rng": _rng_state()},
                    os.path.join(d, f"meta_rank{rank}.pt"))
+        fault_point("checkpoint_save", next_step, rank)
         if world > 1 and torch.distributed.is_initialized():
             torch.distributed.barrier()
         if rank == 0:

@@ -29,6 +29,7 @@ from typing import Iterator
 import torch
 import torch.distributed as dist
 
+from ..distributed.failure import fault_point
 from ..logging import get_logger
 from ..utils.nvtx import nvtx_range
 from .context import RuntimeContext, TrainState
@@ -221,6 +222,7 @@ class RuntimeEngine:
                                                       ctx=ctx)
             if parallel.rank == 0 and every > 0 and state.global_step % every == 0:
                 logger.info(STEP_LINE, state.global_step, *means)
+            fault_point("step_end", state.global_step, parallel.rank)
             state.global_step += 1
         if not source.reduce_each_step:
             close_epoch(state.epoch)  # an epoch cut short by max_steps still gets its summary

@@ -2,7 +2,8 @@
 
 Host side (gloo ranks on CPU): a rank that raises before a collective, a rank
 that never joins one (short process-group timeout), a rank that stops
-heartbeating, non-finite loss. Device side (GPU test): a bounded wait on a
+heartbeating, non-finite loss, the host fault injector's configuration
+(the kill-and-resume run is in test_train4d_cpu.py). Device side (GPU test): a bounded wait on a
 flag that nothing sets returns with a status the host turns into
 CommTimeoutError, and the context stays usable.
 """
@@ -119,6 +120,29 @@ def test_assert_finite():
         assert_finite("loss", torch.tensor(float("nan")))
     with pytest.raises(NonFiniteError):
         assert_finite("grad_norm", float("inf"))
+
+
+def test_host_fault_injector_configuration_and_raise_mode():
+    from nano_train_b200.distributed.failure import (HostFaultInjector, InjectedFault, fault_point,
+                                                     set_fault_injector)
+    assert HostFaultInjector.from_env({}) is None
+    inj = HostFaultInjector.from_env({"NTB_FAULT_STEP": "2", "NTB_FAULT_RANK": "1", "NTB_FAULT_MODE": "raise",
+                                      "NTB_FAULT_POINT": "checkpoint_save"})
+    assert (inj.point, inj.step, inj.rank, inj.mode) == ("checkpoint_save", 2, 1, "raise")
+    with pytest.raises(ValueError):
+        HostFaultInjector.from_env({"NTB_FAULT_STEP": "2", "NTB_FAULT_POINT": "forward"})
+    with pytest.raises(ValueError):
+        HostFaultInjector(point="step_end", step=1, mode="segfault")
+    set_fault_injector(HostFaultInjector(point="step_end", step=3, rank=0, mode="raise"))
+    try:
+        fault_point("step_end", 2, 0)        # other step
+        fault_point("step_end", 3, 1)        # other rank
+        fault_point("checkpoint_save", 3, 0)  # other point
+        with pytest.raises(InjectedFault, match="rank 0 at step_end of step 3"):
+            fault_point("step_end", 3, 0)
+    finally:
+        set_fault_injector(None)
+    fault_point("step_end", 3, 0)  # removed: no-op
 
 
 @pytest.mark.gpu
