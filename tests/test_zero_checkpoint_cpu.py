@@ -131,6 +131,16 @@ def test_nonparam_state_restores_hyperparameters():
 def _zero_worker(rank, world, port, path, strategy, q):
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60))
+    rs_calls = []
+    if strategy == "optim_grads_rs_fault":
+        # the reduce-scatter fails (host-side fault): the optimizer falls back to all-reduce + slice for good
+        strategy = "optim_grads"
+
+        def failing_reduce_scatter(*a, **k):
+            rs_calls.append(1)
+            raise RuntimeError("injected reduce-scatter failure")
+
+        dist.reduce_scatter_tensor = failing_reduce_scatter
     try:
         torch.manual_seed(3)
         model = _Tiny(hidden=7)  # odd sizes: the last shard of every parameter is ragged
@@ -150,6 +160,7 @@ def _zero_worker(rank, world, port, path, strategy, q):
             (sum(nn.functional.mse_loss(ref(x), y) for x, y in zip(xs, ys)) / world).backward()
             ref_opt.step()
         err = max(float((p - r).abs().max()) for p, r in zip(model.parameters(), ref.parameters()))
+        n_rs = len(rs_calls)  # reduce-scatter attempts of the first optimizer over its three steps
 
         opt.save_checkpoint_files(path)
         dist.barrier()
@@ -164,14 +175,14 @@ def _zero_worker(rank, world, port, path, strategy, q):
             nn.functional.mse_loss(m(x), y).backward()
             o.step_with_ready_grads()
         same_after = all(torch.equal(p, r) for p, r in zip(model.parameters(), model2.parameters()))
-        q.put((rank, ("ok", err, same_params, same_after, shard_sizes)))
+        q.put((rank, ("ok", err, same_params, same_after, shard_sizes, n_rs, opt._reduce_scatter_fallback)))
     except Exception as e:  # noqa: BLE001 - reported to the parent
         q.put((rank, ("error", repr(e))))
     finally:
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("strategy", ["optim", "optim_grads"])
+@pytest.mark.parametrize("strategy", ["optim", "optim_grads", "optim_grads_rs_fault"])
 def test_two_rank_zero_matches_adamw_and_resumes_from_files(tmp_path, strategy):
     world = 2
     ctx = mp.get_context("spawn")
@@ -186,9 +197,11 @@ def test_two_rank_zero_matches_adamw_and_resumes_from_files(tmp_path, strategy):
         p.join(timeout=30)
     for r in range(world):
         assert res[r][0] == "ok", res[r]
-        _, err, same_params, same_after, shards = res[r]
+        _, err, same_params, same_after, shards, rs_calls, fallback = res[r]
         assert err < 1e-5, err
         assert same_params and same_after
+        if strategy == "optim_grads_rs_fault":
+            assert fallback and rs_calls == 1, (fallback, rs_calls)  # sticky: never retried
     # the two ranks own disjoint halves (ceil-sized chunks, ragged last) of every parameter
     for name, (s0, e0) in res[0][4].items():
         s1, e1 = res[1][4][name]
