@@ -120,3 +120,15 @@ def test_loss_spike_alerts(tmp_path, caplog):
     assert r > tr.config.alerts.loss_spike_warn and "loss spike" in caplog.text
     with pytest.raises(RuntimeError, match="stop threshold"):
         tr._update_loss_ema(1e6)
+
+
+def test_fixed_probe_batch_change_is_detected(tmp_path):
+    """The fixed probe batch is hashed when captured; a later change of its contents raises instead of
+    silently evaluating another batch (reference: src/trainer.py:524-531)."""
+    tr = _trainer(tmp_path)
+    tr._run_fixed_probe(step=1)
+    assert ("Probe/loss", 1) in tr.writer.scalars
+    ids, _ = tr._probe
+    ids[0, 0] = (ids[0, 0] + 1) % 64
+    with pytest.raises(RuntimeError, match="hash mismatch"):
+        tr._run_fixed_probe(step=2)
