@@ -209,3 +209,24 @@ def test_two_rank_zero_matches_adamw_and_resumes_from_files(tmp_path, strategy):
     files = sorted(os.listdir(tmp_path))
     assert files == ["optimizer_manifest.json", "optimizer_manifest_rank1.json", "optimizer_nonparam.pt",
                      "optimizer_shard_rank0.pt", "optimizer_shard_rank1.pt"]
+
+
+def test_corrupted_shard_file_fails_the_load_and_leaves_the_state_alone(tmp_path):
+    """A truncated shard file (a host-side corruption) makes the load raise; the optimizer that tried to
+    load keeps its own state instead of a partly restored one."""
+    torch.manual_seed(5)
+    model = _Tiny()
+    opt = _opt(model)
+    _train(model, opt, 2, seed=3)
+    _save(opt, tmp_path)
+    shard = tmp_path / "optimizer_shard_rank0.pt"
+    data = shard.read_bytes()
+    shard.write_bytes(data[: len(data) // 2])
+    other = _opt(_Tiny())
+    before = other.get_parameter_state_dp_zero(include_tensors=True)
+    with pytest.raises(Exception):
+        other.load_parameter_state(str(tmp_path), rank=0, world_size=1)
+    after = other.get_parameter_state_dp_zero(include_tensors=True)
+    for name, rec in before["parameters"].items():
+        for k in ("master_param", "exp_avg", "exp_avg_sq"):
+            assert torch.equal(rec[k], after["parameters"][name][k]), (name, k)
