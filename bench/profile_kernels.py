@@ -22,6 +22,8 @@ L2 where the kernel is bandwidth-bound), runs 2 warm-up launches and then
   rmsnorm_bwd   RMSNorm backward 8192 x 4096 bf16
   adamw         fused flat AdamW over 64M fp32 elements
   swiglu        SwiGLU fwd 8192 x 14336
+  mla_k         MLA key assembly [k_nope | rope(k_rope)], DeepSeek-V2-Lite micro-batch (8192 tokens, 16 heads,
+                nope 128 / rope 64 / v 128, kv_lora 512); mla_k_bwd its backward
   ce            vocab cross-entropy stats+bwd 4096 x 32064
   router        fused top-k router fwd, 16384 tokens x 64 experts, top-6 softmax (bf16)
   router_bwd    its backward
@@ -183,6 +185,21 @@ def main():
             dy = torch.randn(8192, 14336, **bf)
             nbytes = gu.numel() * 2 * 2 + dy.numel() * 2  # read gate|up and dY, write d(gate|up)
             fn = lambda: C.swiglu_bwd(dy, gu)  # noqa: E731
+    elif a.case in ("mla_k", "mla_k_bwd"):
+        from nano_train_b200.ops.rope import rope_table
+
+        T, h, Dn, Dv, R, lat, S = 8192, 16, 128, 128, 64, 512, 4096
+        table = rope_table(S, R, 1e4, dev)
+        if a.case == "mla_k":
+            kv = torch.randn(T, h, Dn + Dv, **bf)
+            kr = torch.randn(T, lat + R, **bf)[:, lat:]
+            nbytes = T * h * Dn * 2 + T * R * 2 + T * h * (Dn + R) * 2  # read nope + rope part, write keys
+            fn = lambda: C.mla_k_assemble(kv, kr, table, Dn, S)  # noqa: E731
+        else:
+            dk = torch.randn(T, h, Dn + R, **bf)
+            dkv = torch.empty(T, h, Dn + Dv, **bf)
+            nbytes = T * h * (Dn + R) * 2 + T * h * Dn * 2 + T * R * 2  # read dK, write nope grads + dk_rope
+            fn = lambda: C.mla_k_assemble_bwd(dk, dkv, table, Dn, S)  # noqa: E731
     elif a.case == "ce":
         logits = torch.randn(4096, 32064, **bf)
         labels = torch.randint(0, 32064, (4096,), device=dev)
