@@ -76,6 +76,9 @@ def _default_store():
     return c10d._get_default_store()
 
 
+_active_monitor: Optional["HeartbeatMonitor"] = None
+
+
 class HeartbeatMonitor:
     """Store-based liveness of the ranks of the default process group.
 
@@ -120,22 +123,35 @@ class HeartbeatMonitor:
             self._stop.wait(self.interval_s)
 
     def start(self) -> "HeartbeatMonitor":
+        global _active_monitor
+        _active_monitor = self
         self.beat()
         self._thread = threading.Thread(target=self._run, name="ntb-heartbeat", daemon=True)
         self._thread.start()
         return self
 
-    def stop(self) -> None:
+    def stop(self, done: bool = False) -> None:
+        """Stop beating. ``done=True`` (a clean end of this rank's run) also records that in the store,
+        so peers still finishing do not take the silence for a failure."""
+        global _active_monitor
         self._stop.set()
         if self._thread is not None:
             self._thread.join(timeout=5 * self.interval_s + 1)
+        if done:
+            try:
+                self.store.set(self._key(self.rank), "done")
+            except Exception:  # the store may already be gone at teardown
+                pass
+        if _active_monitor is self:
+            _active_monitor = None
 
     def last_beat(self, r: int) -> Optional[float]:
         key = self._key(r)
         try:
             if not self.store.check([key]):
                 return None
-            return float(self.store.get(key).decode())
+            v = self.store.get(key).decode()
+            return math.inf if v == "done" else float(v)
         except Exception:
             return None
 
@@ -157,6 +173,26 @@ class HeartbeatMonitor:
             raise PeerFailureError(f"rank {self.rank}: no heartbeat from ranks {dead} for > {self.timeout_s}s")
 
 
+EXIT_PEER_DEAD = 43
+
+
+def fail_fast_monitor(timeout_s: float, *, interval_s: Optional[float] = None, exit_code: int = EXIT_PEER_DEAD,
+                      **kw) -> HeartbeatMonitor:
+    """A started ``HeartbeatMonitor`` that ends this process (``os._exit(exit_code)``, after a message on
+    stderr) as soon as a peer has been silent for ``timeout_s``. A rank blocked in a collective with a dead
+    or wedged peer then leaves after about ``timeout_s`` instead of the process-group timeout, and the
+    launcher ends the job with a named culprit."""
+
+    def _exit(dead: list[int]) -> None:
+        print(f"heartbeat: rank {mon.rank}: no heartbeat from ranks {dead} for > {timeout_s}s; ending this process",
+              file=sys.stderr, flush=True)
+        os._exit(exit_code)
+
+    mon = HeartbeatMonitor(interval_s=interval_s if interval_s is not None else max(0.05, min(1.0, timeout_s / 4)),
+                           timeout_s=timeout_s, on_failure=_exit, **kw)
+    return mon.start()
+
+
 # --------------------------------------------------------------------------- host fault injection
 class InjectedFault(RuntimeError):
     """Raised by a ``HostFaultInjector`` in mode ``"raise"``."""
@@ -174,29 +210,33 @@ class HostFaultInjector:
     ``step`` completed steps are written and the completion barrier is not yet reached (the directory
     stays without its ``COMPLETE`` marker). At the point, rank ``rank`` either leaves the process the way a
     crashed one does (``mode="exit"``: output flushed, then ``os._exit(exit_code)``, no teardown, so the
-    peers see a dead rank) or raises ``InjectedFault`` (``mode="raise"``)."""
+    peers see a dead rank), raises ``InjectedFault`` (``mode="raise"``), or wedges (``mode="stall"``: its
+    heartbeat stops and it sleeps for ``stall_s`` seconds, then exits like ``"exit"``)."""
 
     point: str
     step: int
     rank: int = 0
     mode: str = "exit"
     exit_code: int = 17
+    stall_s: float = 60.0
 
     def __post_init__(self) -> None:
         if self.point not in FAULT_POINTS:
             raise ValueError(f"fault point must be one of {FAULT_POINTS}, got {self.point!r}")
-        if self.mode not in ("exit", "raise"):
-            raise ValueError(f"fault mode must be 'exit' or 'raise', got {self.mode!r}")
+        if self.mode not in ("exit", "raise", "stall"):
+            raise ValueError(f"fault mode must be 'exit', 'raise' or 'stall', got {self.mode!r}")
 
     @classmethod
     def from_env(cls, env=None) -> Optional["HostFaultInjector"]:
         """NTB_FAULT_STEP (required to enable), NTB_FAULT_POINT (default step_end), NTB_FAULT_RANK
-        (default 0), NTB_FAULT_MODE (default exit): an unmodified launch line can be failed from outside."""
+        (default 0), NTB_FAULT_MODE (default exit), NTB_FAULT_STALL_S (default 60): an unmodified launch
+        line can be failed from outside."""
         env = os.environ if env is None else env
         if not env.get("NTB_FAULT_STEP"):
             return None
         return cls(point=env.get("NTB_FAULT_POINT", "step_end"), step=int(env["NTB_FAULT_STEP"]),
-                   rank=int(env.get("NTB_FAULT_RANK", "0")), mode=env.get("NTB_FAULT_MODE", "exit"))
+                   rank=int(env.get("NTB_FAULT_RANK", "0")), mode=env.get("NTB_FAULT_MODE", "exit"),
+                   stall_s=float(env.get("NTB_FAULT_STALL_S", "60")))
 
     def maybe_fail(self, point: str, step: int, rank: int) -> None:
         if (point, step, rank) != (self.point, self.step, self.rank):
@@ -207,6 +247,11 @@ class HostFaultInjector:
         import logging
 
         print(msg, file=sys.stderr)
+        if self.mode == "stall":
+            if _active_monitor is not None:
+                _active_monitor.stop()
+            sys.stderr.flush()
+            time.sleep(self.stall_s)
         for h in logging.getLogger().handlers:
             h.flush()
         sys.stdout.flush()

@@ -174,6 +174,7 @@ class RuntimeEngine:
         model.train()
         state = TrainState(global_step=resume.start_global_step, epoch=resume.start_epoch,
                            pipeline_epoch=resume.pipeline_epoch, data_seed=getattr(resume, "data_seed", None))
+        heartbeat = _start_heartbeat(args, ctx)
         try:
             source = _batch_source(model, train_data, args, state, ctx.parallel.pipeline_model_parallel_size > 1)
             self._drive(source, schedule=schedule, model=model, optimizer_state=optimizer_state, ctx=ctx,
@@ -182,7 +183,12 @@ class RuntimeEngine:
                                                      ctx=ctx)
             if ctx.parallel.rank == 0:
                 logger.info("Training completed")
+            if heartbeat is not None:
+                heartbeat.stop(done=True)
+                heartbeat = None
         finally:
+            if heartbeat is not None:
+                heartbeat.stop()
             _teardown()
 
     def _drive(self, source, *, schedule, model, optimizer_state, ctx: RuntimeContext, state: TrainState,
@@ -229,6 +235,18 @@ class RuntimeEngine:
 
 
 _DONE = object()
+
+
+def _start_heartbeat(args, ctx: RuntimeContext):
+    """``--heartbeat-timeout-s T`` (> 0, more than one rank): every rank beats into the process group's
+    store, and a rank whose peer has been silent for T seconds ends its process with a message naming
+    that peer, instead of waiting in a collective for the process-group timeout."""
+    t = float(getattr(args, "heartbeat_timeout_s", 0.0) or 0.0)
+    if t <= 0 or ctx.parallel.world_size <= 1 or not dist.is_initialized():
+        return None
+    from ..distributed.failure import fail_fast_monitor
+
+    return fail_fast_monitor(t)
 
 
 def _announce(ctx: RuntimeContext) -> None:

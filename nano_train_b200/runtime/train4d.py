@@ -10,6 +10,9 @@ spelling kept) plus B200-build options:
   --scoring-func {sigmoid,softmax}    router scoring (reference hard-codes sigmoid)
   --checkpoint-dir / --save-every     real save + resume (the reference's
                                       train_4d checkpoint manager is a no-op)
+  --dist-timeout-s / --heartbeat-timeout-s
+                                      process-group timeout; fail-fast on a peer
+                                      whose heartbeat stopped
 """
 from __future__ import annotations
 
@@ -101,6 +104,8 @@ def build_parser() -> argparse.ArgumentParser:
     a("--checkpoint-dir", type=str, default=None)
     a("--save-every", type=int, default=0)
     a("--dist-timeout-s", type=float, default=600.0, help="process-group timeout (failure detection)")
+    a("--heartbeat-timeout-s", type=float, default=0.0,
+      help="end a rank whose peer sent no heartbeat for this many seconds (0: off)")
     add_mixed_precision_args(p)
     return p
 

@@ -106,6 +106,34 @@ def test_train_4d_recovers_from_a_killed_rank(tmp_path):
     assert os.path.exists(os.path.join(ck, "step_00000006", "COMPLETE"))
 
 
+def test_train_4d_heartbeat_ends_the_job_when_a_rank_wedges():
+    """A rank that wedges between steps (host-side stall: its heartbeat stops, it sleeps) while its peers
+    wait for it in the next step's collectives: with --heartbeat-timeout-s the peers end within seconds,
+    naming the silent rank, long before the 120 s process-group timeout."""
+    import time
+
+    layout = ["--tensor-model-parallel-size", "1", "--pipeline-model-parallel-size", "1",
+              "--expert-model-parallel-size", "2"]
+    t0 = time.time()
+    out, seen = _run(layout + ["--max_steps", "6", "--heartbeat-timeout-s", "3"],
+                     env_extra={"NTB_FAULT_STEP": "1", "NTB_FAULT_RANK": "2", "NTB_FAULT_MODE": "stall",
+                                "NTB_FAULT_STALL_S": "90"}, expect_ok=False)
+    elapsed = time.time() - t0
+    assert "injected fault: rank 2 at step_end of step 1" in out, out[-3000:]
+    assert "no heartbeat from ranks [2]" in out, out[-3000:]
+    assert max(seen) <= 1 and elapsed < 75, (seen, elapsed)
+
+
+def test_train_4d_heartbeat_clean_run_completes():
+    """Ranks that finish at slightly different times record a clean end, so the heartbeat does not fail
+    a completed run."""
+    out, steps = _run(["--tensor-model-parallel-size", "2", "--pipeline-model-parallel-size", "2",
+                       "--expert-model-parallel-size", "1", "--num_microbatches", "2", "--max_steps", "3",
+                       "--heartbeat-timeout-s", "2"])
+    assert "Training completed" in out and sorted(steps) == [0, 1, 2]
+    assert "no heartbeat" not in out
+
+
 def test_train_4d_full_4d_layout_eight_ranks():
     """BASELINE config #4's layout at toy size: TP2 x PP2 x DP2 with EP2 folded inside DP, ZeRO-2, 1F1B
     with 8 microbatches, on 8 gloo ranks."""
