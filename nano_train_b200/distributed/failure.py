@@ -83,9 +83,9 @@ class HeartbeatMonitor:
     """Store-based liveness of the ranks of the default process group.
 
     ``start()`` launches a daemon thread that writes ``hb/<rank>`` every
-    ``interval_s``. ``dead_ranks()`` compares every peer's last beat against
-    ``timeout_s``. ``on_failure`` (optional) is called from the thread with the
-    list of dead ranks the first time one is seen.
+    ``interval_s``. ``dead_ranks()`` lists peers whose beat has not changed for
+    ``timeout_s`` seconds of this process's clock. ``on_failure`` (optional) is called from the
+    thread with the list of dead ranks the first time one is seen (once armed).
     """
 
     def __init__(self, *, interval_s: float = 1.0, timeout_s: float = 10.0, store=None, rank: Optional[int] = None,
@@ -99,9 +99,10 @@ class HeartbeatMonitor:
         self.prefix = prefix
         self.on_failure = on_failure
         self._stop = threading.Event()
+        self._armed = threading.Event()
         self._thread: Optional[threading.Thread] = None
         self._reported = False
-        self._start_time = time.time()
+        self._seen: dict[int, tuple[Optional[str], float]] = {}  # peer -> (last stored beat, local time seen)
 
     def _key(self, r: int) -> str:
         return f"{self.prefix}/{r}"
@@ -113,7 +114,7 @@ class HeartbeatMonitor:
         while not self._stop.is_set():
             try:
                 self.beat()
-                if self.on_failure is not None and not self._reported:
+                if self.on_failure is not None and not self._reported and self._armed.is_set():
                     dead = self.dead_ranks()
                     if dead:
                         self._reported = True
@@ -122,10 +123,14 @@ class HeartbeatMonitor:
                 return
             self._stop.wait(self.interval_s)
 
-    def start(self) -> "HeartbeatMonitor":
+    def start(self, arm: bool = True) -> "HeartbeatMonitor":
+        """Beat now and from a daemon thread. With ``arm=False`` the thread does not call ``on_failure``
+        until ``arm()`` (so ranks that start at different times can first meet at a barrier)."""
         global _active_monitor
         _active_monitor = self
         self.beat()
+        if arm:
+            self.arm()
         self._thread = threading.Thread(target=self._run, name="ntb-heartbeat", daemon=True)
         self._thread.start()
         return self
@@ -145,6 +150,18 @@ class HeartbeatMonitor:
         if _active_monitor is self:
             _active_monitor = None
 
+    def arm(self) -> None:
+        """Start judging peers from now on: each peer's silence is counted from this moment at the earliest."""
+        self._seen.clear()
+        self._armed.set()
+
+    def _raw(self, r: int) -> Optional[str]:
+        try:
+            key = self._key(r)
+            return self.store.get(key).decode() if self.store.check([key]) else None
+        except Exception:
+            return None
+
     def last_beat(self, r: int) -> Optional[float]:
         key = self._key(r)
         try:
@@ -156,14 +173,21 @@ class HeartbeatMonitor:
             return None
 
     def dead_ranks(self) -> list[int]:
-        now = time.time()
+        """Peers whose stored beat has not changed for more than ``timeout_s`` by this process's clock
+        (a peer's clock is never compared with ours, so hosts need not agree on the time); a peer that
+        recorded a clean end is never dead, and a peer is first judged one call after it was first seen."""
+        now = time.monotonic()
         dead = []
         for r in range(self.world_size):
             if r == self.rank:
                 continue
-            t = self.last_beat(r)
-            ref = t if t is not None else self._start_time
-            if now - ref > self.timeout_s:
+            v = self._raw(r)
+            if v == "done":
+                continue
+            seen = self._seen.get(r)
+            if seen is None or seen[0] != v:
+                self._seen[r] = (v, now)
+            elif now - seen[1] > self.timeout_s:
                 dead.append(r)
         return dead
 
@@ -190,7 +214,11 @@ def fail_fast_monitor(timeout_s: float, *, interval_s: Optional[float] = None, e
 
     mon = HeartbeatMonitor(interval_s=interval_s if interval_s is not None else max(0.05, min(1.0, timeout_s / 4)),
                            timeout_s=timeout_s, on_failure=_exit, **kw)
-    return mon.start()
+    mon.start(arm=False)
+    if dist.is_available() and dist.is_initialized():
+        dist.barrier()  # every rank has beaten once before any rank starts judging
+    mon.arm()
+    return mon
 
 
 # --------------------------------------------------------------------------- host fault injection

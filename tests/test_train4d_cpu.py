@@ -115,7 +115,7 @@ def test_train_4d_heartbeat_ends_the_job_when_a_rank_wedges():
     layout = ["--tensor-model-parallel-size", "1", "--pipeline-model-parallel-size", "1",
               "--expert-model-parallel-size", "2"]
     t0 = time.time()
-    out, seen = _run(layout + ["--max_steps", "6", "--heartbeat-timeout-s", "3"],
+    out, seen = _run(layout + ["--max_steps", "6", "--heartbeat-timeout-s", "5"],
                      env_extra={"NTB_FAULT_STEP": "1", "NTB_FAULT_RANK": "2", "NTB_FAULT_MODE": "stall",
                                 "NTB_FAULT_STALL_S": "90"}, expect_ok=False)
     elapsed = time.time() - t0
@@ -129,7 +129,7 @@ def test_train_4d_heartbeat_clean_run_completes():
     a completed run."""
     out, steps = _run(["--tensor-model-parallel-size", "2", "--pipeline-model-parallel-size", "2",
                        "--expert-model-parallel-size", "1", "--num_microbatches", "2", "--max_steps", "3",
-                       "--heartbeat-timeout-s", "2"])
+                       "--heartbeat-timeout-s", "10"])
     assert "Training completed" in out and sorted(steps) == [0, 1, 2]
     assert "no heartbeat" not in out
 
