@@ -174,8 +174,9 @@ class RuntimeEngine:
         model.train()
         state = TrainState(global_step=resume.start_global_step, epoch=resume.start_epoch,
                            pipeline_epoch=resume.pipeline_epoch, data_seed=getattr(resume, "data_seed", None))
-        heartbeat = _start_heartbeat(args, ctx)
+        heartbeat = None
         try:
+            heartbeat = _start_heartbeat(args, ctx)
             source = _batch_source(model, train_data, args, state, ctx.parallel.pipeline_model_parallel_size > 1)
             self._drive(source, schedule=schedule, model=model, optimizer_state=optimizer_state, ctx=ctx,
                         state=state, components=components, args=args)
