@@ -120,3 +120,14 @@ def test_stages_chained_by_hand_match_the_whole_model():
         assert h.shape == (2, 10, 64)
         logits = stages[1].forward_stage(None, h)
         torch.testing.assert_close(logits, whole(ids), atol=1e-5, rtol=1e-5)
+
+
+def test_mla_fused_path_gate():
+    """The fused MLA key assembly is taken only for CUDA bf16 tensors with 16-byte rows and the head
+    dims of a tcgen05 attention kernel; CPU tensors and other shapes keep the reference formulation."""
+    from nano_train_b200.models.deepseek import _mla_fused_ok
+
+    q = torch.zeros(1, 4, 2, 192, dtype=torch.bfloat16)
+    kv = torch.zeros(1, 4, 2, 256, dtype=torch.bfloat16)
+    k_rope = torch.zeros(1, 4, 576, dtype=torch.bfloat16)[..., 512:]
+    assert not _mla_fused_ok(q, kv, k_rope, 128)  # CPU tensors
